@@ -1,0 +1,370 @@
+#!/usr/bin/env python
+"""Synaptic-event throughput of the snn_b200 simulation step on B200.
+
+Workload ("resident recurrent pool"): 10M LIF neurons,
+fixed fanout 1,000 (10B synapses), weights U[-0.2, 0.5] mV, FULL policy;
+every step injects 0.5% of the neurons (seeded uniform indices) with 25.0.
+The network is generated on the device, bit-identical to the reference's
+snn_build_random_pool for the same seed (a host build would need ~120 GB and
+minutes). At N GPUs the pool is sharded by postsynaptic neuron (strong
+scaling: the total network is fixed) and the spike bitmap is all-gathered
+with NCCL every step.
+
+    python bench.py [--gpus N --steps K --warmup W]          # snn_b200 arm
+    python bench.py --impl reference [--steps K --warmup W]  # reference CPU arm
+    torchrun --nproc-per-node N bench.py --gpus N ...        # N > 1
+
+One JSON line is printed by rank 0. value = synaptic events (sum of the
+out-degrees of the spiking rows, benchmarks/step_throughput.c:121-126) of all
+ranks / device time of exactly K steps (CUDA events on the library's stream,
+max over ranks). e2e = the same metric through the reference-facing C ABI
+(snn_cuda_inject_current + snn_cuda_step with host index/value buffers and a
+host spike download every step).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+L2_NOTE = "inputs larger than L2 (FULL CSR of the shard read sparsely each step; target currents L2-resident by design)"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=500)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    ap.add_argument("--neurons", type=int, default=10_000_000)
+    ap.add_argument("--fanout", type=int, default=1000)
+    ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--inject-frac", type=float, default=0.005)
+    ap.add_argument("--inject-value", type=float, default=25.0)
+    ap.add_argument("--cpu-neurons", type=int, default=1_000_000,
+                    help="bounded CPU sample: the same pool scaled to this many neurons")
+    ap.add_argument("--cpu-seconds", type=float, default=15.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    return ap.parse_args()
+
+
+# --------------------------------------------------------------- clocks ----
+class ClockSampler:
+    """Samples SM clock and clock-event reasons with NVML during the timed region."""
+
+    REASONS = {0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap", 0x8: "hw_slowdown",
+               0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown",
+               0x100: "display_clock_setting"}
+
+    def __init__(self, device_index: int):
+        self.samples, self.reasons, self.ok = [], set(), False
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            self.h = pynvml.nvmlDeviceGetHandleByIndex(device_index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+            self.ok = True
+        except Exception:
+            self.max_mhz = None
+        self._stop = threading.Event()
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                self.samples.append(self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM))
+                mask = self.nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+                for bit, name in self.REASONS.items():
+                    if mask & bit:
+                        self.reasons.add(name)
+            except Exception:
+                pass
+            time.sleep(0.002)
+
+    def __enter__(self):
+        if self.ok:
+            self.t = threading.Thread(target=self._run, daemon=True)
+            self.t.start()
+        return self
+
+    def __exit__(self, *a):
+        self._stop.set()
+        if self.ok:
+            self.t.join()
+
+    def summary(self):
+        return {"sm_mhz": statistics.median(self.samples) if self.samples else None, "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(self.reasons - {"gpu_idle"}), "samples": len(self.samples)}
+
+
+def measured_peak_gbs():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def traffic_per_event():
+    """DRAM bytes per synaptic event of the push kernel from the committed ncu
+    summary (profiles/propagate_push_traffic.json), or None."""
+    try:
+        with open(os.path.join(ROOT, "profiles", "propagate_push_traffic.json")) as f:
+            d = json.load(f)
+        return float(d["dram_bytes_per_event"]), float(d["dram_bytes_per_spike"])
+    except Exception:
+        return None
+
+
+# ------------------------------------------------------------ CPU side ----
+def cpu_sample(args, kind_pref=("ref_omp", "port"), steps=None, warmup=None, seconds=None):
+    """Times the reference CPU step (OpenMP build when present) on a bounded
+    sample: the same pool scaled to --cpu-neurons neurons."""
+    import numpy as np
+
+    from oracle.oracle import Oracle, State, baseline_lif, ref_available, stream_indices_np
+    kind = next(k for k in kind_pref if k == "port" or ref_available(k))
+    orc = Oracle(kind)
+    n = args.cpu_neurons
+    net = orc.random_pool(n, args.fanout, -0.2, 0.5, args.seed, lif=baseline_lif())
+    st = State(net)
+    rp = net.row_ptr()
+    deg = (rp[1:] - rp[:-1]).astype(np.int64)
+    count = max(1, int(round(args.inject_frac * n)))
+    val = np.full(count, args.inject_value, np.float32)
+    warm = 10 if warmup is None else warmup
+    for t in range(warm):
+        st.inject(stream_indices_np(args.seed, t, count, n), val)
+        st.step()
+    events, elapsed, done = 0, 0.0, 0
+    idxs = {}
+    limit = steps if steps is not None else 10 ** 9
+    while done < limit and (seconds is None or elapsed < seconds):
+        t = warm + done
+        idx = idxs.pop(t, None)
+        if idx is None:
+            idx = stream_indices_np(args.seed, t, count, n)
+        t0 = time.perf_counter()
+        st.inject(idx, val)
+        s = st.step()
+        elapsed += time.perf_counter() - t0
+        events += int(deg[s.astype(bool)].sum())
+        done += 1
+    threads = int(os.environ.get("OMP_NUM_THREADS", os.cpu_count() or 1)) if kind == "ref_omp" else 1
+    return {"value": events / elapsed if elapsed > 0 else 0.0, "unit": "events/s", "cores": threads,
+            "kind": "reference" if kind.startswith("ref") else "port",
+            "sample": f"same pool scaled to {n} neurons x fanout {args.fanout}, {done} steps after {warm} warm-up "
+                      f"steps, {kind} build ({'OpenMP' if kind == 'ref_omp' else 'serial'})",
+            "steps": done, "seconds": elapsed}
+
+
+def reference_arm(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    if not os.path.exists(os.path.join(ROOT, "oracle", "liboracle.so")):
+        print(json.dumps({"impl": "reference", "unavailable": "oracle/liboracle.so not built"}))
+        return
+    warm = max(args.warmup, 0)
+    r = cpu_sample(args, steps=args.steps, warmup=warm, seconds=None)
+    cfg = workload_config(args, args.gpus)
+    line = {"impl": "reference", "metric": "synaptic_events_per_sec", "value": r["value"], "unit": "events/s",
+            "n_gpus": args.gpus, "steps": r["steps"], "warmup": warm,
+            "ms_per_step": 1000.0 * r["seconds"] / max(r["steps"], 1), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": cfg,
+            "cpu_baseline": {k: r[k] for k in ("value", "unit", "cores", "kind", "sample")},
+            "e2e": {"value": r["value"], "unit": "events/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def workload_config(args, world):
+    return {"workload": "config2_resident_random_pool", "neurons": args.neurons, "fanout": args.fanout,
+            "synapses": args.neurons * args.fanout, "weights": "U[-0.2,0.5] mV", "seed": args.seed,
+            "inject": f"{args.inject_frac * 100:g}% of neurons x {args.inject_value:g} per step",
+            "lif": "dt 1 ms, tau 20 ms, rest=reset -65 mV, thr -50 mV, refractory 2", "policy": "FULL",
+            "propagation": "push", "parallelism": f"postsynaptic shards x{world}", "l2": L2_NOTE}
+
+
+# ------------------------------------------------------------ GPU side ----
+def main():
+    args = parse()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        reference_arm(args)
+        return
+    run_b200(args)
+
+
+def run_b200(args):
+    import numpy as np
+    import torch
+
+    import snn_b200 as sb
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+    nccl_id = None
+    if world > 1:
+        obj = [sb.nccl_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(obj, src=0)
+        nccl_id = obj[0]
+    id_buf = None
+    opts = sb.default_options(device=local, world_size=world, rank=rank, timing=1)
+    if nccl_id is not None:
+        import ctypes
+        id_buf = ctypes.create_string_buffer(nccl_id, 128)
+        opts.nccl_id = ctypes.cast(id_buf, ctypes.c_void_p)
+    lif = sb.LifParams(1.0, 20.0, -65.0, -65.0, -50.0, 1.0, 2)
+    n, f = args.neurons, args.fanout
+    count = max(1, int(round(args.inject_frac * n)))
+    t0 = time.time()
+    ctx = sb.CudaContext.random_pool(n, f, -0.2, 0.5, args.seed, lif=lif, options=opts)
+    gen_s = time.time() - t0
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+
+    def max_over_ranks(x: float) -> float:
+        if dist is None:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def sum_over_ranks(x: float) -> float:
+        if dist is None:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.SUM)
+        return float(t.item())
+
+    # Warm-up (untimed) then exactly K timed steps.
+    ctx.run_stream_async(args.seed, 0, args.warmup, count, args.inject_value)
+    ctx.synchronize()
+    ctx.reset_stats()
+    stream = torch.cuda.ExternalStream(ctx.stream())
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clk:
+        ev0.record(stream)
+        ctx.run_stream_async(args.seed, args.warmup, args.steps, count, args.inject_value)
+        ev1.record(stream)
+        ctx.synchronize()
+        torch.cuda.synchronize()
+    barrier()
+    ms_local = ev0.elapsed_time(ev1)
+    ms = max_over_ranks(ms_local)
+    s = ctx.stats()
+    events_total = sum_over_ranks(float(s["events"]))
+    spikes_total = sum_over_ranks(float(s["spikes"]))
+    value = events_total / (ms / 1e3)
+    # Roofline of the dominant kernel (push propagation) on this rank:
+    # algorithmic bytes = 12 per event (8 B col_idx + 4 B weight, the
+    # reference's CSR format) + 16 per spiking row (row_ptr pair).
+    peak, peak_kind = measured_peak_gbs()
+    prop_bytes = 12.0 * s["events"] + 16.0 * spikes_total
+    prop_s = s["propagate_ms"] / 1e3
+    achieved = prop_bytes / prop_s / 1e9 if prop_s > 0 else 0.0
+    tpe = traffic_per_event()
+    traffic = None
+    if tpe is not None and s["steps"]:
+        traffic = (tpe[0] * s["events"] + tpe[1] * spikes_total) / s["steps"]
+    step_bytes = (12.0 * s["events"] + 16.0 * spikes_total + 25.0 * ctx.local_count * s["steps"]
+                  + 12.0 * count * s["steps"])
+    lay = ctx.layout
+    launches = int(s["kernel_launches"])
+
+    e2e = None
+    if not args.no_e2e:
+        pinned_idx = torch.empty((args.steps, count), dtype=torch.int64).pin_memory()
+        from_stream = _stream_indices(args.seed, args.warmup + args.steps, args.steps, count, n)
+        pinned_idx.numpy()[:] = from_stream.view(np.int64)
+        pinned_val = torch.full((count,), args.inject_value, dtype=torch.float32).pin_memory()
+        spikes_out = torch.empty((ctx.local_count,), dtype=torch.uint8).pin_memory()
+        idx_np, val_np, sp_np = pinned_idx.numpy().view(np.uint64), pinned_val.numpy(), spikes_out.numpy()
+        ctx.reset_stats()
+        barrier()
+        t0 = time.perf_counter()
+        for k in range(args.steps):
+            st = ctx.inject_current(idx_np[k], val_np)
+            if st != 0:
+                raise sb.SnnError(st, "snn_cuda_inject_current")
+            ctx.step(out=sp_np)
+        e2e_s = time.perf_counter() - t0
+        barrier()
+        e2e_s = max_over_ranks(e2e_s)
+        s2 = ctx.stats()
+        e2e_events = sum_over_ranks(float(s2["events"]))
+        e2e = {"value": e2e_events / e2e_s, "unit": "events/s", "h2d_bytes_per_step": count * 12,
+               "d2h_bytes_per_step": int(ctx.local_count), "ms_per_step": 1e3 * e2e_s / args.steps,
+               "api": "snn_cuda_inject_current + snn_cuda_step (host buffers, synchronous)"}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        try:
+            r = cpu_sample(args, seconds=args.cpu_seconds)
+            cpu = {k: r[k] for k in ("value", "unit", "cores", "kind", "sample")}
+        except Exception as exc:  # the baseline is reported, never required
+            cpu = {"value": None, "unavailable": repr(exc)}
+
+    if rank == 0:
+        line = {
+            "metric": "synaptic_events_per_sec", "value": value, "unit": "events/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic: seeded random pool generated on device (bit-identical to snn_build_random_pool), "
+                    "seeded injection stream",
+            "config": dict(workload_config(args, world), index_bits=int(lay["index_bits"])),
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "traffic": traffic, "peak_kind": peak_kind,
+                         "kernel": "propagate_push_kernel",
+                         "algorithmic_bytes_per_launch": prop_bytes / max(s["steps"], 1),
+                         "kernel_ms_per_launch": s["propagate_ms"] / max(s["steps"], 1)},
+            "step_roofline": {"achieved": step_bytes / (ms / 1e3) / 1e9 if world == 1 else None,
+                              "frac": (step_bytes / (ms / 1e3) / 1e9) / peak if world == 1 else None,
+                              "bytes_per_step": step_bytes / max(s["steps"], 1)},
+            "spike_rate": spikes_total / (args.steps * n), "events_per_step": events_total / args.steps,
+            "kernel_ms": {"lif": s["lif_ms"] / args.steps, "exchange": s["exchange_ms"] / args.steps,
+                          "propagate": s["propagate_ms"] / args.steps},
+            "gpu_launches": launches, "generate_s": gen_s, "clocks": clk.summary(), "e2e": e2e,
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    ctx.free()
+    if dist is not None:
+        dist.destroy_process_group()
+
+
+def _stream_indices(seed, first_step, steps, count, n):
+    """Host copy of the seeded injection stream (same formula as
+    snn_b200_inject_stream_async) for the host-buffer e2e run."""
+    import numpy as np
+    g = np.uint64(0x9E3779B97F4A7C15)
+    with np.errstate(over="ignore"):
+        d = np.arange(first_step * count + 1, (first_step + steps) * count + 1, dtype=np.uint64)
+        z = np.uint64(seed) + d * g
+        z = (z ^ (z >> np.uint64(30))) * np.uint64(0xBF58476D1CE4E5B9)
+        z = (z ^ (z >> np.uint64(27))) * np.uint64(0x94D049BB133111EB)
+        z = z ^ (z >> np.uint64(31))
+    return (z % np.uint64(n)).reshape(steps, count)
+
+
+if __name__ == "__main__":
+    main()

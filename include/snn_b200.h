@@ -1,0 +1,272 @@
+/*
+ * snn_b200 -- B200 (sm_100a) CUDA backend for the Ichigo-Labs/snn LIF simulator.
+ *
+ * Part 1 declares the reference's CUDA entry points with identical names,
+ * argument types, meaning and status codes, so the library links behind the
+ * reference's host code (src/snn.c) in place of src/snn_cuda.cu. When the
+ * reference header <snn/snn.h> is included first, its declarations are used;
+ * otherwise this header declares the same types itself (identical layouts).
+ *
+ * Part 2 declares the test hooks of include/snn/snn_test.h:19-25 that the
+ * reference's unit tests call (deterministic fault injection).
+ *
+ * Part 3 declares extensions with no counterpart in the reference's CUDA API:
+ * postsynaptic sharding over several GPUs (one process per GPU, NCCL spike
+ * all-gather), on-device network generation, device-resident input streams,
+ * state reset, ordered (CSR-order bit-exact) propagation and device timing.
+ *
+ * Every call is synchronous on return unless its name ends in _async.
+ */
+#ifndef SNN_B200_H
+#define SNN_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ===================== Part 1: reference CUDA API ====================== */
+#ifndef SNN_SNN_H
+/* Types of include/snn/snn.h, same names, values and layouts. */
+typedef uint64_t snn_size_t; /* include/snn/snn.h:15 */
+
+typedef enum snn_status { /* include/snn/snn.h:17-24 */
+    SNN_OK = 0,
+    SNN_ERR_INVALID_ARGUMENT = -1,
+    SNN_ERR_OUT_OF_MEMORY = -2,
+    SNN_ERR_OVERFLOW = -3,
+    SNN_ERR_CUDA = -4,
+    SNN_ERR_UNSUPPORTED = -5
+} snn_status_t;
+
+typedef enum snn_architecture { /* include/snn/snn.h:26-30 */
+    SNN_ARCH_CUSTOM_CSR = 0,
+    SNN_ARCH_FEED_FORWARD = 1,
+    SNN_ARCH_RANDOM_POOL = 2
+} snn_architecture_t;
+
+typedef struct snn_lif_params { /* include/snn/snn.h:32-40 */
+    float dt_ms;
+    float membrane_tau_ms;
+    float v_rest;
+    float v_reset;
+    float v_threshold;
+    float input_scale;
+    uint32_t refractory_steps;
+} snn_lif_params_t;
+
+typedef struct snn_random_pool_config { /* include/snn/snn.h:50-57 */
+    snn_size_t neuron_count;
+    snn_size_t fanout_per_neuron;
+    float weight_min;
+    float weight_max;
+    uint64_t seed;
+    int allow_self_connections;
+} snn_random_pool_config_t;
+
+typedef struct snn_network snn_network_t; /* include/snn/snn.h:87 */
+
+typedef enum snn_cuda_mode { /* include/snn/snn.h:90-94 */
+    SNN_CUDA_MODE_NONE = 0,
+    SNN_CUDA_MODE_FULL = 1,
+    SNN_CUDA_MODE_STREAMING = 2
+} snn_cuda_mode_t;
+
+typedef struct snn_cuda_config { /* include/snn/snn.h:96-108 */
+    uint64_t max_vram_bytes;
+    snn_size_t max_stream_synapses;
+    snn_size_t max_stream_rows;
+    int prefer_streaming;
+} snn_cuda_config_t;
+
+typedef struct snn_cuda_context snn_cuda_context_t; /* include/snn/snn.h:110 */
+
+/* Replaces include/snn/snn.h:182 (src/snn_cuda.cu:403-410): all-zero config. */
+snn_cuda_config_t snn_cuda_default_config(void);
+/* Replaces include/snn/snn.h:183 (src/snn_cuda.cu:412-418): 1 if a CUDA device is usable. */
+int snn_cuda_available(void);
+/* Replaces include/snn/snn.h:189-191 (src/snn_cuda.cu:420-483). Chooses FULL
+ * (topology resident) when the device layout fits the budget and streaming is
+ * not preferred, else STREAMING (topology copied in bounded chunks each step).
+ * The network must outlive the context. Propagation is the atomic push. */
+snn_status_t snn_cuda_create(const snn_network_t *network, const snn_cuda_config_t *config,
+                             snn_cuda_context_t **out_context);
+/* Replaces include/snn/snn.h:192 (src/snn_cuda.cu:485-503). NULL-safe. */
+void snn_cuda_free(snn_cuda_context_t *context);
+/* Replaces include/snn/snn.h:193 (src/snn_cuda.cu:505-508). */
+snn_cuda_mode_t snn_cuda_context_mode(const snn_cuda_context_t *context);
+/* Replaces include/snn/snn.h:197-200 (src/snn_cuda.cu:510-563). Adds
+ * values[k]*input_scale into the current the next step consumes; all indices
+ * are validated before anything is applied; duplicates accumulate. Unlike the
+ * reference, duplicate indices with unequal values fold in k order, matching
+ * snn_state_inject_current bit for bit. */
+snn_status_t snn_cuda_inject_current(snn_cuda_context_t *context, const snn_size_t *host_indices,
+                                     const float *host_values, snn_size_t count);
+/* Replaces include/snn/snn.h:204-206 (src/snn_cuda.cu:635-682). One LIF step
+ * plus propagation; host_external_current (n floats) and host_out_spikes
+ * (n bytes) are optional. On a sharded context both cover the rank's own
+ * neurons only (see snn_b200_get_layout). */
+snn_status_t snn_cuda_step(snn_cuda_context_t *context, const float *host_external_current,
+                           uint8_t *host_out_spikes);
+/* Replaces include/snn/snn.h:207-209 (src/snn_cuda.cu:684-691). count is a
+ * capacity; exactly n (or the rank's local count) voltages are written. */
+snn_status_t snn_cuda_download_voltage(const snn_cuda_context_t *context, float *host_voltage,
+                                       snn_size_t count);
+#endif /* SNN_SNN_H */
+
+/* ===================== Part 2: reference test hooks ===================== */
+#ifndef SNN_SNN_TEST_H
+/* include/snn/snn_test.h:19-25 (src/snn_cuda.cu:51-67,694-698). The fault
+ * seams are numbered exactly like the reference's: create #0 context calloc,
+ * #1-#6 device state, #7 init launch, then FULL #8-#10 topology allocations
+ * and #11-#13 uploads, or STREAMING #8 host chunk table and #9-#11 chunk
+ * buffers; step #0 external upload, #1 integrate launch, #2 propagate launch
+ * (STREAMING: per chunk row_ptr, col_idx, weights copy then launch), #3 spike
+ * download; inject #0-#1 staging growth, then uploads and the launch. */
+snn_cuda_context_t *snn_test_nonnull_cuda_context(void);
+void snn_test_cuda_set_fail_after(int64_t calls_before_failure);
+void snn_test_cuda_disable_failure(void);
+void snn_test_cuda_force_unavailable(int enable);
+void snn_test_cuda_force_meminfo_fail(int enable);
+#endif
+
+/* ===================== Part 3: snn_b200 extensions ====================== */
+
+typedef enum snn_b200_propagation {
+    /* Push from the compacted spike list with L2-resident fp32 red.add
+     * (the reference's accumulation semantics; order not deterministic). */
+    SNN_B200_PROPAGATE_PUSH = 0,
+    /* Per-target fold over a device CSC in CSR order (ascending presynaptic
+     * row, ascending edge): bit-identical to the reference's serial CPU step
+     * (src/snn.c:898-906) for any weights. FULL mode only. */
+    SNN_B200_PROPAGATE_ORDERED = 1
+} snn_b200_propagation_t;
+
+typedef struct snn_b200_options {
+    int propagation;        /* snn_b200_propagation_t */
+    int device;             /* CUDA device ordinal; -1 = the calling thread's current device */
+    int index_width;        /* device col_idx width: 0 auto (32 bits when n <= 2^32), 32 or 64 */
+    uint32_t rank;          /* shard index in [0, world_size) */
+    uint32_t world_size;    /* number of postsynaptic shards (1 = unsharded) */
+    const void *nccl_id;    /* 128-byte NCCL unique id (snn_b200_nccl_unique_id), world_size > 1 */
+    int timing;             /* 1: record per-step device timings (snn_b200_stats) */
+} snn_b200_options_t;
+
+typedef struct snn_b200_stats {
+    uint64_t steps;            /* steps completed since create / reset_stats */
+    uint64_t spikes;           /* spikes of this rank's neurons */
+    uint64_t events;           /* synaptic events delivered to this rank's targets */
+    uint64_t kernel_launches;  /* kernels launched by the library */
+    double step_ms;            /* device time of the whole steps (timing = 1) */
+    double propagate_ms;       /* device time of the propagation kernels (timing = 1) */
+    double lif_ms;             /* device time of the LIF kernels (timing = 1) */
+    double exchange_ms;        /* device time of the spike all-gather + compaction (timing = 1) */
+} snn_b200_stats_t;
+
+typedef struct snn_b200_layout {
+    snn_size_t neuron_count;        /* global n */
+    snn_size_t local_begin;         /* first neuron owned by this rank */
+    snn_size_t local_count;         /* neurons owned by this rank */
+    snn_size_t local_synapses;      /* edges targeting this rank's neurons */
+    uint32_t index_bits;            /* 32 or 64 */
+    int propagation;                /* snn_b200_propagation_t */
+    uint64_t device_state_bytes;    /* resident per-neuron state + spike workspace */
+    uint64_t device_topology_bytes; /* resident topology (FULL) or chunk buffers (STREAMING) */
+} snn_b200_layout_t;
+
+snn_b200_options_t snn_b200_default_options(void);
+
+/* snn_cuda_create with options: propagation mode, device, index width and
+ * postsynaptic sharding. With world_size > 1 every rank passes the same
+ * host network and the same NCCL id; rank r owns neurons
+ * [r*S, min((r+1)*S, n)) with S = ceil(n / world_size / 32) * 32. */
+snn_status_t snn_b200_create(const snn_network_t *network, const snn_cuda_config_t *config,
+                             const snn_b200_options_t *options, snn_cuda_context_t **out_context);
+
+/* Generates the network of snn_build_random_pool (src/snn.c:523-574) directly
+ * on the device, bit-identical to the host builder, without a host copy:
+ * edge e takes draws 2e+1 (target) and 2e+2 (weight) of the seeded splitmix64
+ * stream. Each shard generates only the edges that target its neurons.
+ * The context is FULL; config may be NULL. */
+snn_status_t snn_b200_create_random_pool(const snn_random_pool_config_t *pool, const snn_lif_params_t *lif,
+                                         const snn_cuda_config_t *config, const snn_b200_options_t *options,
+                                         snn_cuda_context_t **out_context);
+
+/* Deep layered net generated on the device: every neuron of layer l < L-1
+ * sends `fanout` edges to uniform targets (with replacement) in layer l+1,
+ * weights weight_min + (weight_max - weight_min) * u clamped to weight_max,
+ * draws as in snn_b200_create_random_pool. At most 16 layers. */
+snn_status_t snn_b200_create_layered_random(const snn_size_t *layer_sizes, size_t layer_count,
+                                            snn_size_t fanout, float weight_min, float weight_max,
+                                            uint64_t seed, const snn_lif_params_t *lif,
+                                            const snn_b200_options_t *options,
+                                            snn_cuda_context_t **out_context);
+
+/* Writes a fresh 128-byte NCCL unique id (rank 0 calls it and shares the bytes). */
+snn_status_t snn_b200_nccl_unique_id(void *out_id128);
+
+/* Voltages back to v_rest, currents, refractory counters and spikes to zero;
+ * the topology stays resident (no re-upload). */
+snn_status_t snn_b200_reset(snn_cuda_context_t *context);
+
+/* Device-resident input: the seeded injection stream. Step t injects `count`
+ * events of `value` at indices mix64(seed + (t*count + k + 1) * 0x9e3779b97f4a7c15) % n,
+ * k = 0..count-1, generated on the device (each shard applies its own). */
+snn_status_t snn_b200_inject_stream_async(snn_cuda_context_t *context, uint64_t seed, uint64_t step,
+                                          snn_size_t count, float value);
+
+/* `steps` steps, each after injecting step t of the seeded stream (t from
+ * first_step), with no host synchronisation between steps and no host
+ * copies. count = 0 runs without input. */
+snn_status_t snn_b200_run_stream_async(snn_cuda_context_t *context, uint64_t seed, uint64_t first_step,
+                                       uint64_t steps, snn_size_t count, float value);
+
+/* One step without host input or output and without a final synchronisation. */
+snn_status_t snn_b200_step_async(snn_cuda_context_t *context);
+
+/* Waits for all work of the context; folds pending timings into the stats. */
+snn_status_t snn_b200_synchronize(snn_cuda_context_t *context);
+
+snn_status_t snn_b200_get_stats(snn_cuda_context_t *context, snn_b200_stats_t *out_stats);
+snn_status_t snn_b200_reset_stats(snn_cuda_context_t *context);
+snn_status_t snn_b200_get_layout(const snn_cuda_context_t *context, snn_b200_layout_t *out_layout);
+
+/* The context's CUDA stream (a cudaStream_t), for callers that order their
+ * own work or events against the library's. */
+void *snn_b200_stream(const snn_cuda_context_t *context);
+
+/* Checkpoint / resume of this rank's neuron state: voltages, the current the
+ * next step consumes (propagated + injected so far) and refractory counters,
+ * `count` >= local neuron count (exactly the local count is read/written).
+ * Any pointer may be NULL to skip that array. */
+snn_status_t snn_b200_upload_state(snn_cuda_context_t *context, const float *voltage, const float *current,
+                                   const uint32_t *refractory, snn_size_t count);
+snn_status_t snn_b200_download_state(const snn_cuda_context_t *context, float *voltage, float *current,
+                                     uint32_t *refractory, snn_size_t count);
+
+/* Diagnostics for parity tests: copy this rank's spike bytes (last step),
+ * the current the next step will consume, or the device topology. */
+snn_status_t snn_b200_download_spikes(const snn_cuda_context_t *context, uint8_t *host_spikes, snn_size_t count);
+snn_status_t snn_b200_download_current(const snn_cuda_context_t *context, float *host_current, snn_size_t count);
+/* Device CSR of a FULL push context (row_ptr over all n presynaptic rows,
+ * col_idx as global neuron ids, weights); pass NULL to skip an array. */
+snn_status_t snn_b200_download_topology(const snn_cuda_context_t *context, snn_size_t *row_ptr,
+                                        snn_size_t row_capacity, snn_size_t *col_idx, float *weights,
+                                        snn_size_t edge_capacity);
+
+/* A network view over caller-owned CSR arrays (no copy; the arrays must
+ * outlive the view and every context made from it), for callers that do not
+ * link the reference's host library. Validates like snn_build_custom_csr
+ * (src/snn.c:158-180, 427-461). */
+snn_status_t snn_b200_network_wrap(snn_size_t neuron_count, snn_size_t synapse_count, const snn_size_t *row_ptr,
+                                   const snn_size_t *col_idx, const float *weights, const snn_lif_params_t *lif,
+                                   snn_network_t **out_network);
+void snn_b200_network_unwrap(snn_network_t *network);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SNN_B200_H */

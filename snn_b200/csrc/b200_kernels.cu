@@ -1,0 +1,791 @@
+// snn_b200 device kernels for sm_100a.
+//
+// The simulation step is HBM-bound integer/byte work plus fp32 adds, so the
+// kernels are SIMT with wide vector loads, warp ballots and warp/block
+// aggregated atomics; nothing here is a dense contraction, so there is no
+// tensor-core path. Floating point follows the reference's bit-exactness rules
+// (src/snn_cuda.cu:203-225, CMakeLists.txt:57-60): every LIF, injection and
+// weight-generation operation is an explicitly rounded __fadd_rn / __fmul_rn /
+// __fsub_rn, so no FMA contraction can change a bit, and the host's
+// decay = expf(-dt/tau) is used as given.
+#include "b200_kernels.h"
+
+#include <cub/device/device_scan.cuh>
+
+#include <mutex>
+#include <vector>
+
+namespace b200 {
+
+namespace {
+
+constexpr uint64_t kGamma = 0x9e3779b97f4a7c15ull;
+constexpr unsigned kFull = 0xffffffffu;
+
+__device__ __forceinline__ uint64_t mix64(uint64_t z) {
+    z = (z ^ (z >> 30)) * 0xbf58476d1ce4e5b9ull;
+    z = (z ^ (z >> 27)) * 0x94d049bb133111ebull;
+    return z ^ (z >> 31);
+}
+
+// Draw d (1-based) of the splitmix64 stream seeded `seed` (src/snn.c:94-99:
+// the state advances by gamma before every mix).
+__device__ __forceinline__ uint64_t draw_at(uint64_t seed, uint64_t d) { return mix64(seed + d * kGamma); }
+
+// src/snn.c:101-105: top 53 bits scaled to [0,1) in double, rounded to float.
+__device__ __forceinline__ float unit_float(uint64_t r) {
+    return __double2float_rn((double)(r >> 11) * (1.0 / 9007199254740992.0));
+}
+
+// src/snn.c:559-567: weight_min + span * u in float (no FMA), clamped.
+__device__ __forceinline__ float lerp_weight(float wmin, float wmax, float u) {
+    const float w = __fadd_rn(wmin, __fmul_rn(__fsub_rn(wmax, wmin), u));
+    return w < wmax ? w : wmax;
+}
+
+__device__ __forceinline__ unsigned lane_id() { return threadIdx.x & 31u; }
+
+// Fire-and-forget fp32 add into L2 (red.global.add.f32; note that the PTX
+// f32 atomic flushes subnormal inputs/results to zero, as the reference's
+// atomicAdd does).
+__device__ __forceinline__ void red_add(float *p, float v) { atomicAdd(p, v); }
+
+template <typename T>
+struct Vec16;
+template <>
+struct Vec16<uint32_t> {
+    using type = uint4;
+    static constexpr int n = 4;
+};
+template <>
+struct Vec16<uint64_t> {
+    using type = ulonglong2;
+    static constexpr int n = 2;
+};
+template <int N>
+struct FVec;
+template <>
+struct FVec<4> {
+    using type = float4;
+};
+template <>
+struct FVec<2> {
+    using type = float2;
+};
+
+template <typename T>
+__device__ __forceinline__ T vget(const uint4 &v, int i) {
+    return i == 0 ? v.x : i == 1 ? v.y : i == 2 ? v.z : v.w;
+}
+__device__ __forceinline__ uint64_t cget(const ulonglong2 &v, int i) { return i == 0 ? v.x : v.y; }
+__device__ __forceinline__ uint32_t cget(const uint4 &v, int i) {
+    return i == 0 ? v.x : i == 1 ? v.y : i == 2 ? v.z : v.w;
+}
+__device__ __forceinline__ float fget(const float4 &v, int i) {
+    return i == 0 ? v.x : i == 1 ? v.y : i == 2 ? v.z : v.w;
+}
+__device__ __forceinline__ float fget(const float2 &v, int i) { return i == 0 ? v.x : v.y; }
+
+// ---------------------------------------------------------------- init ----
+__global__ void init_state_kernel(uint64_t n, float v_rest, float *v, float *cur0, float *cur1, float *ext,
+                                  uint32_t *refr, uint8_t *spikes, uint64_t words, uint32_t *bitmap,
+                                  DevCounters *ctr) {
+    const uint64_t stride = (uint64_t)blockDim.x * gridDim.x;
+    const uint64_t t0 = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    for (uint64_t i = t0; i < n; i += stride) {
+        v[i] = v_rest;
+        cur0[i] = 0.0f;
+        cur1[i] = 0.0f;
+        if (ext != nullptr) ext[i] = 0.0f;
+        refr[i] = 0u;
+        spikes[i] = 0u;
+    }
+    for (uint64_t i = t0; i < words; i += stride) bitmap[i] = 0u;
+    if (t0 == 0 && ctr != nullptr) {
+        ctr->list_count[0] = 0u;
+        ctr->list_count[1] = 0u;
+        ctr->error = 0u;
+        ctr->spikes = 0ull;
+        ctr->events = 0ull;
+    }
+}
+
+// ----------------------------------------------------------------- LIF ----
+// One CTA owns a tile of ITERS*1024 consecutive neurons; each thread updates 4
+// consecutive neurons per iteration with 16-byte loads/stores. The 4 fired
+// flags of a lane form a nibble; 8 lanes OR their nibbles into one 32-bit
+// bitmap word. Spiking ids are ranked with a warp scan + a per-iteration block
+// scan, buffered ascending in shared memory, and appended to the global list
+// with ONE atomic per tile (the list is ascending inside a tile).
+constexpr int kLifThreads = 256;
+
+__device__ __forceinline__ uint32_t lif_one(float &v, float &c, float in, uint32_t &r, const LifArgs &p) {
+    // ((v_rest + (v - v_rest) * decay) + current) + in   (src/snn_cuda.cu:214)
+    const float v_int =
+        __fadd_rn(__fadd_rn(__fadd_rn(p.v_rest, __fmul_rn(__fsub_rn(v, p.v_rest), p.decay)), c), in);
+    const uint32_t active = r == 0u;
+    const uint32_t fired = active & (v_int >= p.v_threshold ? 1u : 0u);
+    c = 0.0f;
+    v = (active & (fired ^ 1u)) ? v_int : p.v_reset;
+    r = fired ? p.refractory_steps : r - (uint32_t)(r != 0u);
+    return fired;
+}
+
+template <bool HAS_EXT, bool WRITE_LIST, typename TIdx, int ITERS>
+__global__ void __launch_bounds__(kLifThreads) lif_kernel(uint64_t n, LifArgs p, float *__restrict__ v,
+                                                          float *__restrict__ cur,
+                                                          const float *__restrict__ ext,
+                                                          uint32_t *__restrict__ refr, uint8_t *__restrict__ spikes,
+                                                          uint32_t *__restrict__ bitmap, TIdx *__restrict__ list,
+                                                          uint64_t global_offset, DevCounters *ctr, int parity) {
+    constexpr uint64_t kTile = (uint64_t)ITERS * kLifThreads * 4u;
+    __shared__ TIdx sbuf[WRITE_LIST ? kTile : 1];
+    __shared__ uint32_t warp_tot[kLifThreads / 32];
+    __shared__ uint32_t s_base;
+    const unsigned lane = lane_id();
+    const unsigned warp = threadIdx.x >> 5;
+    const uint64_t tiles = (n + kTile - 1) / kTile;
+    for (uint64_t tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
+        uint32_t block_off = 0;
+        for (int it = 0; it < ITERS; ++it) {
+            const uint64_t i0 = tile * kTile + (uint64_t)it * (kLifThreads * 4u) + threadIdx.x * 4u;
+            uint32_t nib = 0;
+            if (i0 + 3 < n) {
+                float4 vv = *reinterpret_cast<const float4 *>(v + i0);
+                float4 cc = *reinterpret_cast<const float4 *>(cur + i0);
+                uint4 rr = *reinterpret_cast<const uint4 *>(refr + i0);
+                float4 ee = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                if (HAS_EXT) {
+                    ee = *reinterpret_cast<const float4 *>(ext + i0);
+                    ee.x = __fmul_rn(ee.x, p.input_scale);
+                    ee.y = __fmul_rn(ee.y, p.input_scale);
+                    ee.z = __fmul_rn(ee.z, p.input_scale);
+                    ee.w = __fmul_rn(ee.w, p.input_scale);
+                }
+                nib |= lif_one(vv.x, cc.x, ee.x, rr.x, p);
+                nib |= lif_one(vv.y, cc.y, ee.y, rr.y, p) << 1;
+                nib |= lif_one(vv.z, cc.z, ee.z, rr.z, p) << 2;
+                nib |= lif_one(vv.w, cc.w, ee.w, rr.w, p) << 3;
+                *reinterpret_cast<float4 *>(v + i0) = vv;
+                *reinterpret_cast<float4 *>(cur + i0) = cc;
+                *reinterpret_cast<uint4 *>(refr + i0) = rr;
+                *reinterpret_cast<uint32_t *>(spikes + i0) =
+                    (nib & 1u) | ((nib >> 1) & 1u) << 8 | ((nib >> 2) & 1u) << 16 | ((nib >> 3) & 1u) << 24;
+            } else if (i0 < n) {
+                for (int k = 0; k < 4; ++k) {
+                    const uint64_t i = i0 + k;
+                    if (i < n) {
+                        float vv = v[i], cc = cur[i];
+                        uint32_t rr = refr[i];
+                        const float in = HAS_EXT ? __fmul_rn(ext[i], p.input_scale) : 0.0f;
+                        const uint32_t f = lif_one(vv, cc, in, rr, p);
+                        v[i] = vv;
+                        cur[i] = cc;
+                        refr[i] = rr;
+                        spikes[i] = (uint8_t)f;
+                        nib |= f << k;
+                    }
+                }
+            }
+            // 8 lanes x 4 neurons = one 32-bit bitmap word.
+            uint32_t word = nib << (4u * (lane & 7u));
+            word |= __shfl_xor_sync(kFull, word, 1);
+            word |= __shfl_xor_sync(kFull, word, 2);
+            word |= __shfl_xor_sync(kFull, word, 4);
+            if ((lane & 7u) == 0u && i0 < n) bitmap[i0 >> 5] = word;
+            if (WRITE_LIST) {
+                const uint32_t cnt = __popc(nib);
+                uint32_t incl = cnt;
+#pragma unroll
+                for (int d = 1; d < 32; d <<= 1) {
+                    const uint32_t y = __shfl_up_sync(kFull, incl, d);
+                    if (lane >= (unsigned)d) incl += y;
+                }
+                if (lane == 31u) warp_tot[warp] = incl;
+                __syncthreads();
+                uint32_t wbase = block_off, total = 0;
+#pragma unroll
+                for (int w = 0; w < kLifThreads / 32; ++w) {
+                    const uint32_t t = warp_tot[w];
+                    wbase += (w < (int)warp) ? t : 0u;
+                    total += t;
+                }
+                uint32_t pos = wbase + incl - cnt;
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    if (nib & (1u << k)) sbuf[pos++] = (TIdx)(i0 + k);
+                }
+                __syncthreads();
+                block_off += total;
+            }
+        }
+        if (WRITE_LIST) {
+            if (threadIdx.x == 0) s_base = block_off ? atomicAdd(&ctr->list_count[parity], block_off) : 0u;
+            __syncthreads();
+            const uint32_t base = s_base;
+            for (uint32_t k = threadIdx.x; k < block_off; k += kLifThreads)
+                list[base + k] = (TIdx)(sbuf[k] + global_offset);
+            __syncthreads();
+        }
+    }
+}
+
+// ---------------------------------------------------------- compaction ----
+template <typename TIdx>
+__global__ void __launch_bounds__(256) compact_kernel(const uint32_t *__restrict__ bitmap, uint64_t words,
+                                                      TIdx *__restrict__ list, DevCounters *ctr, int parity,
+                                                      uint64_t own_begin, uint64_t own_end) {
+    const unsigned lane = lane_id();
+    const uint64_t stride = (uint64_t)blockDim.x * gridDim.x;
+    uint32_t own = 0;
+    for (uint64_t base = (uint64_t)blockIdx.x * blockDim.x; base < words; base += stride) {
+        const uint64_t wi = base + threadIdx.x;
+        const uint32_t word = wi < words ? bitmap[wi] : 0u;
+        const uint32_t cnt = __popc(word);
+        if (wi >= own_begin && wi < own_end) own += cnt;
+        uint32_t incl = cnt;
+#pragma unroll
+        for (int d = 1; d < 32; d <<= 1) {
+            const uint32_t y = __shfl_up_sync(kFull, incl, d);
+            if (lane >= (unsigned)d) incl += y;
+        }
+        const uint32_t total = __shfl_sync(kFull, incl, 31);
+        uint32_t off = 0;
+        if (lane == 31u && total) off = atomicAdd(&ctr->list_count[parity], total);
+        off = __shfl_sync(kFull, off, 31);
+        uint32_t pos = off + incl - cnt;
+        uint32_t m = word;
+        while (m) {
+            const int b = __ffs(m) - 1;
+            m &= m - 1u;
+            list[pos++] = (TIdx)(wi * 32u + (uint64_t)b);
+        }
+    }
+#pragma unroll
+    for (int d = 16; d > 0; d >>= 1) own += __shfl_xor_sync(kFull, own, d);
+    if (lane == 0 && own) atomicAdd(&ctr->spikes, (unsigned long long)own);
+}
+
+// Block-level sum of per-thread u64 values, added once into *dst.
+__device__ __forceinline__ void block_add_u64(unsigned long long v, unsigned long long *dst) {
+    __shared__ unsigned long long s_acc;
+    if (threadIdx.x == 0) s_acc = 0ull;
+    __syncthreads();
+#pragma unroll
+    for (int d = 16; d > 0; d >>= 1) v += __shfl_xor_sync(kFull, v, d);
+    if (lane_id() == 0 && v) atomicAdd(&s_acc, v);
+    __syncthreads();
+    if (threadIdx.x == 0 && s_acc) atomicAdd(dst, s_acc);
+}
+
+// Per step bookkeeping done by block 0 of the (last) propagation kernel:
+// zero the list slot the next step appends to, and count this step's spikes.
+__device__ __forceinline__ void step_epilogue(DevCounters *ctr, int parity, int count_spikes, uint32_t count) {
+    if (blockIdx.x == 0 && threadIdx.x == 0) {
+        ctr->list_count[parity ^ 1] = 0u;
+        if (count_spikes) ctr->spikes += count;
+    }
+}
+
+// ---------------------------------------------------------------- push ----
+// Warp per spiking row (grid-stride over the list). The row's col_idx and
+// weights are streamed with 16-byte evict-first loads (__ldcs: they are read
+// once per step and must not push the L2-resident target currents out),
+// software-pipelined one vector deep, and every edge issues a fire-and-forget
+// red.global.add.f32 into next_current, which stays L2-resident.
+template <typename TCol>
+__device__ __forceinline__ void push_row(uint64_t b, uint64_t e, const TCol *__restrict__ col,
+                                         const float *__restrict__ w, float *__restrict__ next, unsigned lane) {
+    using V = typename Vec16<TCol>::type;
+    constexpr int VN = Vec16<TCol>::n;
+    using FV = typename FVec<VN>::type;
+    uint64_t a = (b + (VN - 1)) & ~(uint64_t)(VN - 1);
+    if (a > e) a = e;
+    if (lane < a - b) red_add(next + col[b + lane], w[b + lane]);
+    const uint64_t nvec = (e - a) / VN;
+    const V *cv = reinterpret_cast<const V *>(col + a);
+    const FV *wv = reinterpret_cast<const FV *>(w + a);
+    uint64_t k = lane;
+    V c0;
+    FV x0;
+    if (k < nvec) {
+        c0 = __ldcs(cv + k);
+        x0 = __ldcs(wv + k);
+    }
+    while (k < nvec) {
+        const uint64_t k1 = k + 32u;
+        V c1;
+        FV x1;
+        if (k1 < nvec) {
+            c1 = __ldcs(cv + k1);
+            x1 = __ldcs(wv + k1);
+        }
+#pragma unroll
+        for (int j = 0; j < VN; ++j) red_add(next + cget(c0, j), fget(x0, j));
+        c0 = c1;
+        x0 = x1;
+        k = k1;
+    }
+    const uint64_t t0 = a + nvec * VN;
+    if (lane < e - t0) red_add(next + col[t0 + lane], w[t0 + lane]);
+}
+
+template <typename TIdx, typename TCol>
+__global__ void __launch_bounds__(256) propagate_push_kernel(const TIdx *__restrict__ list,
+                                                             const uint64_t *__restrict__ row_ptr,
+                                                             const TCol *__restrict__ col,
+                                                             const float *__restrict__ w, float *__restrict__ next,
+                                                             DevCounters *ctr, int parity, int count_spikes) {
+    const uint32_t count = *(volatile uint32_t *)&ctr->list_count[parity];
+    const unsigned lane = lane_id();
+    const uint64_t gwarp = ((uint64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const uint64_t nwarps = ((uint64_t)gridDim.x * blockDim.x) >> 5;
+    unsigned long long events = 0;
+    for (uint64_t s = gwarp; s < count; s += nwarps) {
+        const uint64_t row = (uint64_t)list[s];
+        const uint64_t b = row_ptr[row];
+        const uint64_t e = row_ptr[row + 1];
+        events += e - b;
+        push_row<TCol>(b, e, col, w, next, lane);
+    }
+    block_add_u64(lane == 0 ? events : 0ull, &ctr->events);
+    step_epilogue(ctr, parity, count_spikes, count);
+}
+
+// ----------------------------------------------------------- ordered pull ----
+// Warp per local target. The target's incoming (pre, w) pairs are stored in
+// CSR order (ascending pre, ascending edge). 32 pairs are tested per
+// iteration against the spike bitmap; the spiking ones are folded in lane
+// order, so acc follows exactly the serial CPU fold starting from +0.0f
+// (src/snn.c:898-906). The fold runs redundantly in every lane from warp
+// shuffles; lane 0 stores the sum, overwriting the whole target buffer.
+template <typename TPre, typename TIdx>
+__global__ void __launch_bounds__(256) propagate_pull_kernel(uint64_t n_local, const uint64_t *__restrict__ col_ptr,
+                                                             const TPre *__restrict__ pre,
+                                                             const float *__restrict__ w,
+                                                             const uint32_t *__restrict__ bitmap,
+                                                             float *__restrict__ next, const TIdx *__restrict__ list,
+                                                             const uint32_t *__restrict__ out_degree,
+                                                             DevCounters *ctr, int parity, int count_spikes) {
+    const unsigned lane = lane_id();
+    const uint64_t gwarp = ((uint64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const uint64_t nwarps = ((uint64_t)gridDim.x * blockDim.x) >> 5;
+    for (uint64_t t = gwarp; t < n_local; t += nwarps) {
+        const uint64_t b = col_ptr[t];
+        const uint64_t e = col_ptr[t + 1];
+        float acc = 0.0f;
+        for (uint64_t k0 = b; k0 < e; k0 += 32u) {
+            const uint64_t k = k0 + lane;
+            uint32_t bit = 0;
+            float wv = 0.0f;
+            if (k < e) {
+                const uint64_t p = (uint64_t)pre[k];
+                bit = (__ldg(bitmap + (p >> 5)) >> (p & 31u)) & 1u;
+                if (bit) wv = w[k];
+            }
+            uint32_t m = __ballot_sync(kFull, bit);
+            while (m) {
+                const int j = __ffs(m) - 1;
+                m &= m - 1u;
+                acc = __fadd_rn(acc, __shfl_sync(kFull, wv, j));
+            }
+        }
+        if (lane == 0) next[t] = acc;
+    }
+    // Event statistics: out-degree (towards this rank) of every spiking row.
+    const uint32_t count = *(volatile uint32_t *)&ctr->list_count[parity];
+    const uint64_t gthread = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const uint64_t nthreads = (uint64_t)gridDim.x * blockDim.x;
+    unsigned long long events = 0;
+    for (uint64_t s = gthread; s < count; s += nthreads) events += out_degree[(uint64_t)list[s]];
+    block_add_u64(events, &ctr->events);
+    step_epilogue(ctr, parity, count_spikes, count);
+}
+
+// ----------------------------------------------------------- streaming ----
+// One chunk of rows whose CSR slice was just copied in: warp per 32 rows,
+// ballot over the rows' spike bits, then the warp strides each spiking row.
+__global__ void __launch_bounds__(256) propagate_chunk_kernel(uint64_t row0, uint64_t rows, uint64_t edge_base,
+                                                              const uint32_t *__restrict__ bitmap,
+                                                              const uint64_t *__restrict__ row_ptr,
+                                                              const uint64_t *__restrict__ col,
+                                                              const float *__restrict__ w, float *__restrict__ next,
+                                                              DevCounters *ctr, int parity, int first_chunk) {
+    const unsigned lane = lane_id();
+    const uint64_t gwarp = ((uint64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const uint64_t nwarps = ((uint64_t)gridDim.x * blockDim.x) >> 5;
+    unsigned long long events = 0;
+    for (uint64_t base = gwarp * 32u; base < rows; base += nwarps * 32u) {
+        const uint64_t r = base + lane;
+        uint32_t bit = 0;
+        if (r < rows) {
+            const uint64_t g = row0 + r;
+            bit = (bitmap[g >> 5] >> (g & 31u)) & 1u;
+        }
+        uint32_t m = __ballot_sync(kFull, bit);
+        while (m) {
+            const int j = __ffs(m) - 1;
+            m &= m - 1u;
+            const uint64_t lr = base + (uint64_t)j;
+            const uint64_t b = row_ptr[lr] - edge_base;
+            const uint64_t e = row_ptr[lr + 1] - edge_base;
+            events += e - b;
+            push_row<uint64_t>(b, e, col, w, next, lane);
+        }
+    }
+    block_add_u64(lane == 0 ? events : 0ull, &ctr->events);
+    if (first_chunk) {
+        const uint32_t count = *(volatile uint32_t *)&ctr->list_count[parity];
+        step_epilogue(ctr, parity, 1, count);
+    }
+}
+
+__global__ void step_epilogue_kernel(DevCounters *ctr, int parity, int count_spikes) {
+    const uint32_t count = ctr->list_count[parity];
+    step_epilogue(ctr, parity, count_spikes, count);
+}
+
+// ------------------------------------------------------------- inject ----
+__global__ void inject_atomic_kernel(uint64_t count, const uint64_t *__restrict__ idx,
+                                     const float *__restrict__ val, float scale, float *__restrict__ cur,
+                                     uint64_t lo, uint64_t hi) {
+    const uint64_t stride = (uint64_t)blockDim.x * gridDim.x;
+    for (uint64_t k = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; k < count; k += stride) {
+        const uint64_t i = idx[k];
+        if (i >= lo && i < hi) red_add(cur + (i - lo), __fmul_rn(val[k], scale));
+    }
+}
+
+// The thread at the head of each run of equal (stably sorted) indices folds
+// the run sequentially: c = (c + v0*s) + v1*s ... exactly as the CPU's
+// in-order loop does (src/snn.c:737-739).
+__global__ void inject_ordered_kernel(uint64_t count, const uint64_t *__restrict__ idx,
+                                      const float *__restrict__ val, float scale, float *__restrict__ cur,
+                                      uint64_t lo, uint64_t hi) {
+    const uint64_t stride = (uint64_t)blockDim.x * gridDim.x;
+    for (uint64_t k = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; k < count; k += stride) {
+        const uint64_t i = idx[k];
+        if ((k != 0 && idx[k - 1] == i) || i < lo || i >= hi) continue;
+        float c = cur[i - lo];
+        for (uint64_t q = k; q < count && idx[q] == i; ++q) c = __fadd_rn(c, __fmul_rn(val[q], scale));
+        cur[i - lo] = c;
+    }
+}
+
+__global__ void inject_stream_kernel(uint64_t seed, uint64_t first_draw, uint64_t count, uint64_t n, float addend,
+                                     float *__restrict__ cur, uint64_t lo, uint64_t hi) {
+    const uint64_t stride = (uint64_t)blockDim.x * gridDim.x;
+    for (uint64_t k = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; k < count; k += stride) {
+        const uint64_t i = draw_at(seed, first_draw + k + 1u) % n;
+        if (i >= lo && i < hi) red_add(cur + (i - lo), addend);
+    }
+}
+
+// ------------------------------------------------------------ topology ----
+template <typename TCol>
+__global__ void convert_cols_kernel(const uint64_t *__restrict__ src, TCol *__restrict__ dst, uint64_t count,
+                                    uint64_t lo) {
+    const uint64_t stride = (uint64_t)blockDim.x * gridDim.x;
+    for (uint64_t k = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; k < count; k += stride)
+        dst[k] = (TCol)(src[k] - lo);
+}
+
+__global__ void row_degrees_kernel(const uint64_t *__restrict__ row_ptr, uint64_t rows, uint32_t *__restrict__ deg) {
+    const uint64_t stride = (uint64_t)blockDim.x * gridDim.x;
+    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < rows; i += stride)
+        deg[i] = (uint32_t)(row_ptr[i + 1] - row_ptr[i]);
+}
+
+// Target range of presynaptic row `pre`: random pool -> all n neurons;
+// layered -> the next layer (the last layer has no edges).
+struct TargetRange {
+    uint64_t base;
+    uint64_t count;
+    bool has_edges;
+};
+
+__device__ __forceinline__ TargetRange target_range(const GenParams &g, uint64_t pre) {
+    TargetRange t{0, g.n, true};
+    if (!g.recurrent) {
+        int l = 0;
+        while (l + 1 < g.layers && pre >= g.off[l + 1]) ++l;
+        if (l + 1 >= g.layers) {
+            t.has_edges = false;
+            t.count = 0;
+        } else {
+            t.base = g.off[l + 1];
+            t.count = g.off[l + 2] - g.off[l + 1];
+        }
+    }
+    return t;
+}
+
+// Edges of rows in non-last layers: row `pre` owns edges [pre*F, pre*F+F).
+__device__ __forceinline__ uint64_t gen_target(const GenParams &g, uint64_t pre, uint64_t e, const TargetRange &t) {
+    uint64_t post = t.base + draw_at(g.seed, 2u * e + 1u) % t.count;
+    if (g.recurrent && !g.allow_self && post == pre) post = (post + 1u) % g.n;  // src/snn.c:563-565
+    return post;
+}
+
+__device__ __forceinline__ float gen_weight(const GenParams &g, uint64_t e) {
+    return lerp_weight(g.wmin, g.wmax, unit_float(draw_at(g.seed, 2u * e + 2u)));
+}
+
+__device__ __forceinline__ uint64_t rows_with_edges(const GenParams &g) {
+    return g.recurrent ? g.n : g.off[g.layers - 1];
+}
+
+__global__ void gen_row_ptr_dense_kernel(GenParams g, uint64_t *__restrict__ row_ptr) {
+    const uint64_t stride = (uint64_t)blockDim.x * gridDim.x;
+    const uint64_t r = rows_with_edges(g);
+    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i <= g.n; i += stride)
+        row_ptr[i] = (i < r ? i : r) * g.fanout;
+}
+
+template <typename TCol>
+__global__ void __launch_bounds__(256) gen_edges_dense_kernel(GenParams g, uint64_t e0, uint64_t e1,
+                                                              TCol *__restrict__ col, float *__restrict__ w) {
+    const uint64_t stride = (uint64_t)blockDim.x * gridDim.x;
+    for (uint64_t e = e0 + (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; e < e1; e += stride) {
+        const uint64_t pre = e / g.fanout;
+        const TargetRange t = target_range(g, pre);
+        col[e] = (TCol)gen_target(g, pre, e, t);
+        w[e] = gen_weight(g, e);
+    }
+}
+
+// Warp per row: count the row's edges that target [lo, hi).
+__global__ void __launch_bounds__(256) gen_count_shard_kernel(GenParams g, uint64_t lo, uint64_t hi,
+                                                              uint64_t *__restrict__ counts) {
+    const unsigned lane = lane_id();
+    const uint64_t gwarp = ((uint64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const uint64_t nwarps = ((uint64_t)gridDim.x * blockDim.x) >> 5;
+    for (uint64_t pre = gwarp; pre < g.n; pre += nwarps) {
+        const TargetRange t = target_range(g, pre);
+        uint32_t c = 0;
+        if (t.has_edges) {
+            for (uint64_t j = lane; j < g.fanout; j += 32u) {
+                const uint64_t post = gen_target(g, pre, pre * g.fanout + j, t);
+                c += (post >= lo && post < hi);
+            }
+        }
+#pragma unroll
+        for (int d = 16; d > 0; d >>= 1) c += __shfl_xor_sync(kFull, c, d);
+        if (lane == 0) counts[pre] = c;
+    }
+}
+
+// Warp per row: write the kept edges in edge order (ballot compaction).
+template <typename TCol>
+__global__ void __launch_bounds__(256) gen_fill_shard_kernel(GenParams g, uint64_t lo, uint64_t hi,
+                                                             const uint64_t *__restrict__ row_ptr,
+                                                             TCol *__restrict__ col, float *__restrict__ w) {
+    const unsigned lane = lane_id();
+    const uint64_t gwarp = ((uint64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const uint64_t nwarps = ((uint64_t)gridDim.x * blockDim.x) >> 5;
+    for (uint64_t pre = gwarp; pre < g.n; pre += nwarps) {
+        const TargetRange t = target_range(g, pre);
+        if (!t.has_edges) continue;
+        uint64_t pos = row_ptr[pre];
+        for (uint64_t j0 = 0; j0 < g.fanout; j0 += 32u) {
+            const uint64_t j = j0 + lane;
+            bool keep = false;
+            uint64_t post = 0;
+            const uint64_t e = pre * g.fanout + j;
+            if (j < g.fanout) {
+                post = gen_target(g, pre, e, t);
+                keep = post >= lo && post < hi;
+            }
+            const uint32_t m = __ballot_sync(kFull, keep);
+            if (keep) {
+                const uint64_t q = pos + __popc(m & ((1u << lane) - 1u));
+                col[q] = (TCol)(post - lo);
+                w[q] = gen_weight(g, e);
+            }
+            pos += __popc(m);
+        }
+    }
+}
+
+int grid_for(int device, int blocks_per_sm, uint64_t work, uint64_t per_block) {
+    const uint64_t need = (work + per_block - 1) / per_block;
+    const uint64_t cap = (uint64_t)sm_count(device) * (uint64_t)blocks_per_sm;
+    uint64_t g = need < cap ? need : cap;
+    return g == 0 ? 1 : (int)g;
+}
+
+}  // namespace
+
+int sm_count(int device) {
+    static std::mutex mu;
+    static std::vector<int> cache;
+    std::lock_guard<std::mutex> lock(mu);
+    if (device < 0) device = 0;
+    if ((int)cache.size() <= device) cache.resize(device + 1, 0);
+    if (cache[device] == 0) {
+        int v = 0;
+        if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, device) != cudaSuccess || v <= 0) v = 148;
+        cache[device] = v;
+    }
+    return cache[device];
+}
+
+void launch_init_state(cudaStream_t s, uint64_t n, float v_rest, float *v, float *cur0, float *cur1, float *ext,
+                       uint32_t *refr, uint8_t *spikes, uint64_t words, uint32_t *bitmap, DevCounters *ctr) {
+    const uint64_t work = n > words ? n : words;
+    uint64_t blocks = (work + 255) / 256;
+    if (blocks > 65535) blocks = 65535;
+    if (blocks == 0) blocks = 1;
+    init_state_kernel<<<(unsigned)blocks, 256, 0, s>>>(n, v_rest, v, cur0, cur1, ext, refr, spikes, words, bitmap, ctr);
+}
+
+template <bool EXT, typename TIdx, int ITERS>
+static void lif_dispatch(cudaStream_t s, int device, uint64_t n, const LifArgs &p, float *v, float *cur,
+                         const float *ext, uint32_t *refr, uint8_t *spikes, uint32_t *bitmap, void *list,
+                         uint64_t off, DevCounters *ctr, int parity) {
+    constexpr uint64_t tile = (uint64_t)ITERS * kLifThreads * 4u;
+    const int grid = grid_for(device, 6, n, tile);
+    if (list != nullptr)
+        lif_kernel<EXT, true, TIdx, ITERS><<<grid, kLifThreads, 0, s>>>(n, p, v, cur, ext, refr, spikes, bitmap,
+                                                                        (TIdx *)list, off, ctr, parity);
+    else
+        lif_kernel<EXT, false, TIdx, ITERS><<<grid, kLifThreads, 0, s>>>(n, p, v, cur, ext, refr, spikes, bitmap,
+                                                                         (TIdx *)list, off, ctr, parity);
+}
+
+void launch_lif(cudaStream_t s, int device, uint64_t n, const LifArgs &p, float *v, float *cur, const float *ext,
+                uint32_t *refr, uint8_t *spikes, uint32_t *bitmap, void *list, int idx_bits, uint64_t off,
+                DevCounters *ctr, int parity) {
+    if (n == 0) return;
+    if (idx_bits == 32) {
+        if (ext) lif_dispatch<true, uint32_t, 8>(s, device, n, p, v, cur, ext, refr, spikes, bitmap, list, off, ctr, parity);
+        else lif_dispatch<false, uint32_t, 8>(s, device, n, p, v, cur, ext, refr, spikes, bitmap, list, off, ctr, parity);
+    } else {
+        if (ext) lif_dispatch<true, uint64_t, 4>(s, device, n, p, v, cur, ext, refr, spikes, bitmap, list, off, ctr, parity);
+        else lif_dispatch<false, uint64_t, 4>(s, device, n, p, v, cur, ext, refr, spikes, bitmap, list, off, ctr, parity);
+    }
+}
+
+void launch_compact(cudaStream_t s, int device, const uint32_t *bitmap, uint64_t words, void *list, int idx_bits,
+                    DevCounters *ctr, int parity, uint64_t own_begin, uint64_t own_end) {
+    const int grid = grid_for(device, 8, words, 256);
+    if (idx_bits == 32)
+        compact_kernel<uint32_t><<<grid, 256, 0, s>>>(bitmap, words, (uint32_t *)list, ctr, parity, own_begin, own_end);
+    else
+        compact_kernel<uint64_t><<<grid, 256, 0, s>>>(bitmap, words, (uint64_t *)list, ctr, parity, own_begin, own_end);
+}
+
+template <typename TIdx, typename TCol>
+static int push_grid(int device) {
+    static int blocks_per_sm[2] = {0, 0};
+    int &b = blocks_per_sm[sizeof(TCol) == 8];
+    if (b == 0) {
+        int v = 0;
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&v, propagate_push_kernel<TIdx, TCol>, 256, 0) !=
+                cudaSuccess ||
+            v <= 0)
+            v = 4;
+        b = v;
+    }
+    return sm_count(device) * b;
+}
+
+void launch_propagate_push(cudaStream_t s, int device, const void *list, int idx_bits, const uint64_t *row_ptr,
+                           const void *col, int col_bits, const float *w, float *next, DevCounters *ctr, int parity,
+                           int count_spikes) {
+#define B200_PUSH(TI, TC)                                                                                      \
+    propagate_push_kernel<TI, TC><<<push_grid<TI, TC>(device), 256, 0, s>>>((const TI *)list, row_ptr,         \
+                                                                            (const TC *)col, w, next, ctr,     \
+                                                                            parity, count_spikes)
+    if (idx_bits == 32 && col_bits == 32) B200_PUSH(uint32_t, uint32_t);
+    else if (idx_bits == 32) B200_PUSH(uint32_t, uint64_t);
+    else if (col_bits == 32) B200_PUSH(uint64_t, uint32_t);
+    else B200_PUSH(uint64_t, uint64_t);
+#undef B200_PUSH
+}
+
+void launch_propagate_pull(cudaStream_t s, int device, uint64_t n_local, const uint64_t *col_ptr, const void *pre,
+                           int pre_bits, const float *w, const uint32_t *bitmap, float *next, const void *list,
+                           int idx_bits, const uint32_t *out_degree, DevCounters *ctr, int parity, int count_spikes) {
+    const int grid = sm_count(device) * 8;
+#define B200_PULL(TP, TI)                                                                                   \
+    propagate_pull_kernel<TP, TI><<<grid, 256, 0, s>>>(n_local, col_ptr, (const TP *)pre, w, bitmap, next,   \
+                                                       (const TI *)list, out_degree, ctr, parity, count_spikes)
+    if (pre_bits == 32 && idx_bits == 32) B200_PULL(uint32_t, uint32_t);
+    else if (pre_bits == 32) B200_PULL(uint32_t, uint64_t);
+    else if (idx_bits == 32) B200_PULL(uint64_t, uint32_t);
+    else B200_PULL(uint64_t, uint64_t);
+#undef B200_PULL
+}
+
+void launch_propagate_chunk(cudaStream_t s, int device, uint64_t row0, uint64_t rows, uint64_t edge_base,
+                            const uint32_t *bitmap, const uint64_t *row_ptr, const uint64_t *col, const float *w,
+                            float *next, DevCounters *ctr, int parity, int first_chunk) {
+    const int grid = grid_for(device, 8, rows, 256);
+    propagate_chunk_kernel<<<grid, 256, 0, s>>>(row0, rows, edge_base, bitmap, row_ptr, col, w, next, ctr, parity,
+                                                first_chunk);
+}
+
+void launch_step_epilogue(cudaStream_t s, DevCounters *ctr, int parity, int count_spikes) {
+    step_epilogue_kernel<<<1, 32, 0, s>>>(ctr, parity, count_spikes);
+}
+
+void launch_inject_atomic(cudaStream_t s, int device, uint64_t count, const uint64_t *idx, const float *val,
+                          float scale, float *cur, uint64_t lo, uint64_t hi) {
+    inject_atomic_kernel<<<grid_for(device, 8, count, 256), 256, 0, s>>>(count, idx, val, scale, cur, lo, hi);
+}
+
+void launch_inject_ordered(cudaStream_t s, int device, uint64_t count, const uint64_t *idx, const float *val,
+                           float scale, float *cur, uint64_t lo, uint64_t hi) {
+    inject_ordered_kernel<<<grid_for(device, 8, count, 256), 256, 0, s>>>(count, idx, val, scale, cur, lo, hi);
+}
+
+void launch_inject_stream(cudaStream_t s, int device, uint64_t seed, uint64_t step, uint64_t count, uint64_t n,
+                          float addend, float *cur, uint64_t lo, uint64_t hi) {
+    inject_stream_kernel<<<grid_for(device, 8, count, 256), 256, 0, s>>>(seed, step * count, count, n, addend, cur,
+                                                                        lo, hi);
+}
+
+void launch_convert_cols(cudaStream_t s, int device, const uint64_t *src, void *dst, int col_bits, uint64_t count,
+                         uint64_t lo) {
+    const int grid = grid_for(device, 8, count, 256);
+    if (col_bits == 32) convert_cols_kernel<uint32_t><<<grid, 256, 0, s>>>(src, (uint32_t *)dst, count, lo);
+    else convert_cols_kernel<uint64_t><<<grid, 256, 0, s>>>(src, (uint64_t *)dst, count, lo);
+}
+
+void launch_gen_row_ptr_dense(cudaStream_t s, int device, const GenParams &g, uint64_t *row_ptr) {
+    gen_row_ptr_dense_kernel<<<grid_for(device, 8, g.n + 1, 256), 256, 0, s>>>(g, row_ptr);
+}
+
+void launch_gen_edges_dense(cudaStream_t s, int device, const GenParams &g, uint64_t e0, uint64_t e1, void *col,
+                            int col_bits, float *w) {
+    if (e1 <= e0) return;
+    const int grid = grid_for(device, 8, e1 - e0, 256);
+    if (col_bits == 32) gen_edges_dense_kernel<uint32_t><<<grid, 256, 0, s>>>(g, e0, e1, (uint32_t *)col, w);
+    else gen_edges_dense_kernel<uint64_t><<<grid, 256, 0, s>>>(g, e0, e1, (uint64_t *)col, w);
+}
+
+void launch_gen_count_shard(cudaStream_t s, int device, const GenParams &g, uint64_t lo, uint64_t hi,
+                            uint64_t *counts) {
+    gen_count_shard_kernel<<<grid_for(device, 8, g.n * 32u, 256), 256, 0, s>>>(g, lo, hi, counts);
+}
+
+void launch_gen_fill_shard(cudaStream_t s, int device, const GenParams &g, uint64_t lo, uint64_t hi,
+                           const uint64_t *row_ptr, void *col, int col_bits, float *w) {
+    const int grid = grid_for(device, 8, g.n * 32u, 256);
+    if (col_bits == 32)
+        gen_fill_shard_kernel<uint32_t><<<grid, 256, 0, s>>>(g, lo, hi, row_ptr, (uint32_t *)col, w);
+    else
+        gen_fill_shard_kernel<uint64_t><<<grid, 256, 0, s>>>(g, lo, hi, row_ptr, (uint64_t *)col, w);
+}
+
+cudaError_t exclusive_scan_u64(cudaStream_t s, const uint64_t *in, uint64_t *out, uint64_t n, void *temp,
+                               size_t *temp_bytes) {
+    return cub::DeviceScan::ExclusiveSum(temp, *temp_bytes, in, out, (int64_t)n, s);
+}
+
+void launch_row_degrees(cudaStream_t s, int device, const uint64_t *row_ptr, uint64_t rows, uint32_t *deg) {
+    row_degrees_kernel<<<grid_for(device, 8, rows, 256), 256, 0, s>>>(row_ptr, rows, deg);
+}
+
+}  // namespace b200

@@ -1,0 +1,126 @@
+// Host-side launch interface of the snn_b200 kernels (b200_kernels.cu).
+// Everything here is C++ with no torch types; the C ABI lives in snn_cuda_b200.cu.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace b200 {
+
+// LIF constants captured at create time (src/snn_cuda.cu:456-460): the host's
+// decay = expf(-dt/tau) is used as is, never recomputed on the device.
+struct LifArgs {
+    float decay;
+    float v_rest;
+    float v_reset;
+    float v_threshold;
+    float input_scale;
+    uint32_t refractory_steps;
+};
+
+// Small device-side bookkeeping block, one per context.
+//  list_count[p]  number of entries of the spike list of a step with parity p
+//                 (ping-pong: the propagation of step t zeroes slot (t+1)&1).
+//  spikes/events  cumulative statistics (this rank's neurons / targets).
+//  error          first error code raised by a bounded device wait (0 = none).
+struct DevCounters {
+    uint32_t list_count[2];
+    uint32_t error;
+    uint32_t pad;
+    unsigned long long spikes;
+    unsigned long long events;
+};
+
+// Network generator description shared by the random-pool and the layered
+// generators. Edge e (CSR order) uses draws 2e+1 (target) and 2e+2 (weight)
+// of the splitmix64 stream seeded `seed` (src/snn.c:94-105, 553-568).
+struct GenParams {
+    uint64_t n;           // global neuron count
+    uint64_t fanout;      // edges per non-last-layer neuron
+    uint64_t seed;
+    float wmin;
+    float wmax;
+    int allow_self;       // recurrent pool only
+    int recurrent;        // 1: random pool (targets in [0,n)), 0: layered
+    int layers;           // layered: number of layers (<= 16)
+    uint64_t off[17];     // layered: prefix offsets of the layers
+};
+
+// Number of SMs of the current device (cached per device).
+int sm_count(int device);
+
+void launch_init_state(cudaStream_t s, uint64_t n, float v_rest, float *v, float *cur0, float *cur1, float *ext,
+                       uint32_t *refr, uint8_t *spikes, uint64_t bitmap_words, uint32_t *bitmap,
+                       DevCounters *ctr);
+
+// LIF update of n local neurons; writes spikes (u8), the local bitmap words
+// and, when list != nullptr, appends the spiking ids (+ global_offset) to the
+// spike list of parity `parity`. idx_bits selects a 32- or 64-bit list.
+void launch_lif(cudaStream_t s, int device, uint64_t n, const LifArgs &p, float *v, float *cur, const float *ext,
+                uint32_t *refr, uint8_t *spikes, uint32_t *bitmap, void *list, int idx_bits, uint64_t global_offset,
+                DevCounters *ctr, int parity);
+
+// Global bitmap -> spike list (sharded contexts, after the all-gather).
+// Also adds the popcount of words [own_begin, own_end) to ctr->spikes.
+void launch_compact(cudaStream_t s, int device, const uint32_t *bitmap, uint64_t words, void *list, int idx_bits,
+                    DevCounters *ctr, int parity, uint64_t own_begin, uint64_t own_end);
+
+// Push propagation from the spike list over a resident CSR.
+// col_bits = 32 or 64 (local target ids), idx_bits = spike list width.
+void launch_propagate_push(cudaStream_t s, int device, const void *list, int idx_bits, const uint64_t *row_ptr,
+                           const void *col, int col_bits, const float *w, float *next, DevCounters *ctr,
+                           int parity, int count_spikes);
+
+// Ordered pull over a CSC: for every local target, folds the weights of its
+// spiking presynaptic rows in (row, edge) order starting from 0.0f.
+void launch_propagate_pull(cudaStream_t s, int device, uint64_t n_local, const uint64_t *col_ptr,
+                           const void *pre, int pre_bits, const float *w, const uint32_t *bitmap, float *next,
+                           const void *list, int idx_bits, const uint32_t *out_degree, DevCounters *ctr,
+                           int parity, int count_spikes);
+
+// STREAMING: one chunk of `rows` rows starting at row0, with the chunk's raw
+// row_ptr slice (rows+1 entries, absolute edge offsets) and its edges starting
+// at edge_base; col holds 64-bit global target ids.
+void launch_propagate_chunk(cudaStream_t s, int device, uint64_t row0, uint64_t rows, uint64_t edge_base,
+                            const uint32_t *bitmap, const uint64_t *row_ptr, const uint64_t *col, const float *w,
+                            float *next, DevCounters *ctr, int parity, int first_chunk);
+
+// Step epilogue for STREAMING contexts with no chunk (never happens) or for
+// steps without a propagation launch: zeroes the next list slot, adds stats.
+void launch_step_epilogue(cudaStream_t s, DevCounters *ctr, int parity, int count_spikes);
+
+// Sparse injection. Indices outside [lo, hi) are skipped (other shards).
+void launch_inject_atomic(cudaStream_t s, int device, uint64_t count, const uint64_t *idx, const float *val,
+                          float scale, float *cur, uint64_t lo, uint64_t hi);
+// Indices sorted ascending with a stable sort: every run of equal indices is
+// folded sequentially in its (original k) order.
+void launch_inject_ordered(cudaStream_t s, int device, uint64_t count, const uint64_t *idx, const float *val,
+                           float scale, float *cur, uint64_t lo, uint64_t hi);
+// The seeded injection stream (see snn_b200_inject_stream_async).
+void launch_inject_stream(cudaStream_t s, int device, uint64_t seed, uint64_t step, uint64_t count, uint64_t n,
+                          float addend, float *cur, uint64_t lo, uint64_t hi);
+
+// u64 global column ids -> local ids of the chosen width (subtracting lo).
+void launch_convert_cols(cudaStream_t s, int device, const uint64_t *src, void *dst, int col_bits, uint64_t count,
+                         uint64_t lo);
+
+// Device network generation.
+// Unsharded: row_ptr[i] = edges before row i, col/w of every edge.
+void launch_gen_row_ptr_dense(cudaStream_t s, int device, const GenParams &g, uint64_t *row_ptr);
+void launch_gen_edges_dense(cudaStream_t s, int device, const GenParams &g, uint64_t edge_begin, uint64_t edge_end,
+                            void *col, int col_bits, float *w);
+// Sharded: per-row counts of edges targeting [lo, hi), then the fill.
+void launch_gen_count_shard(cudaStream_t s, int device, const GenParams &g, uint64_t lo, uint64_t hi,
+                            uint64_t *counts);
+void launch_gen_fill_shard(cudaStream_t s, int device, const GenParams &g, uint64_t lo, uint64_t hi,
+                           const uint64_t *row_ptr, void *col, int col_bits, float *w);
+
+// Exclusive prefix sum of n u64 values (temp storage allocated by the caller
+// through the returned size when temp == nullptr).
+cudaError_t exclusive_scan_u64(cudaStream_t s, const uint64_t *in, uint64_t *out, uint64_t n, void *temp,
+                               size_t *temp_bytes);
+
+// Per-row out-degrees (u32) from a row_ptr, for event statistics in ordered mode.
+void launch_row_degrees(cudaStream_t s, int device, const uint64_t *row_ptr, uint64_t rows, uint32_t *deg);
+
+}  // namespace b200

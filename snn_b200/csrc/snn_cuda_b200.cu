@@ -1,0 +1,1193 @@
+// snn_b200: the C ABI (include/snn_b200.h) over the sm_100a kernels.
+//
+// Drop-in replacement for the reference's src/snn_cuda.cu: same eight
+// snn_cuda_* entry points, same status codes, same fault-seam numbering
+// (so the reference's own tests/test_snn.c links and passes against it),
+// plus the snn_b200_* extensions. Differences in how the work is done:
+//  * each context owns a non-blocking stream (and a copy stream for
+//    STREAMING); every public reference call is still synchronous on return;
+//  * the LIF kernel emits a spike bitmap and a compacted spike list, and
+//    propagation is driven by the list instead of a scan of all n rows;
+//  * device col_idx is 32-bit when the target ids fit (the host CSR stays 64-bit);
+//  * STREAMING double-buffers the CSR chunks on a copy stream so the copy of
+//    chunk i+1 overlaps the propagation of chunk i;
+//  * ORDERED propagation (extension) folds in CSR order over a device CSC and
+//    is bit-identical to the reference's serial CPU step for any weights;
+//  * sharded contexts (extension) own a contiguous range of postsynaptic
+//    neurons and all-gather the spike bitmap with NCCL every step.
+#include "snn_b200.h"
+#include "b200_kernels.h"
+
+#include <cuda_runtime.h>
+#include <nccl.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdlib>
+#include <cstring>
+#include <new>
+#include <numeric>
+#include <vector>
+
+// Same field layout as the reference's struct snn_network (src/snn_internal.h:15-24):
+// the backend reads a network built by the reference's host library directly.
+struct snn_network {
+    snn_size_t neuron_count;
+    snn_size_t synapse_count;
+    snn_architecture_t architecture;
+    snn_lif_params_t lif;
+    float decay;
+    snn_size_t *row_ptr;
+    snn_size_t *col_idx;
+    float *weights;
+};
+
+namespace {
+
+// ------------------------------------------------------------------ seams --
+// Deterministic fault injection with the reference's semantics
+// (src/snn_cuda.cu:46-125): the k-th seam call after set_fail_after(k) fails.
+int64_t g_fail_after = -1;
+int g_force_unavailable = 0;
+int g_force_meminfo_fail = 0;
+
+int seam_fail() {
+    if (g_fail_after < 0) return 0;
+    if (g_fail_after == 0) return 1;
+    --g_fail_after;
+    return 0;
+}
+
+snn_status_t cuda_status(cudaError_t e) { return e == cudaSuccess ? SNN_OK : SNN_ERR_CUDA; }
+
+struct StreamChunk {
+    uint64_t row_begin;
+    uint64_t rows;
+    uint64_t edge_begin;
+    uint64_t edge_count;
+};
+
+struct TimingGroup {
+    cudaEvent_t ev[4];  // start, after LIF, after exchange, after propagation
+};
+
+}  // namespace
+
+struct snn_cuda_context {
+    const snn_network_t *network = nullptr;
+    snn_cuda_mode_t mode = SNN_CUDA_MODE_NONE;
+    int device = 0;
+    cudaStream_t stream = nullptr;
+    cudaStream_t copy_stream = nullptr;
+    int propagation = SNN_B200_PROPAGATE_PUSH;
+    int col_bits = 32;
+    int idx_bits = 32;
+    uint32_t rank = 0;
+    uint32_t world = 1;
+    uint64_t n_global = 0;
+    uint64_t slot = 0;  // neurons per shard slot (multiple of 32)
+    uint64_t lo = 0, hi = 0, n_local = 0;
+    uint64_t e_local = 0;
+    snn_lif_params_t lif{};
+    b200::LifArgs args{};
+
+    float *d_v = nullptr;
+    float *d_cur_pair = nullptr;
+    float *d_cur[2] = {nullptr, nullptr};
+    int cur = 0;
+    float *d_ext = nullptr;
+    uint32_t *d_refr = nullptr;
+    uint8_t *d_spikes = nullptr;
+    void *d_ws = nullptr;
+    uint32_t *d_bitmap = nullptr;  // global (padded) bitmap
+    uint64_t bitmap_words = 0;
+    void *d_list = nullptr;
+    b200::DevCounters *d_ctr = nullptr;
+
+    uint64_t *d_row_ptr = nullptr;
+    void *d_col = nullptr;
+    float *d_w = nullptr;
+
+    uint64_t *d_col_ptr = nullptr;
+    void *d_pre = nullptr;
+    float *d_cw = nullptr;
+    uint32_t *d_deg = nullptr;
+
+    std::vector<StreamChunk> chunks;
+    uint64_t slot_rows = 0, slot_edges = 0, slot_stride = 0;
+    uint64_t *d_chunk_row = nullptr;
+    uint64_t *d_chunk_col = nullptr;
+    float *d_chunk_w = nullptr;
+    cudaEvent_t ev_copied[2] = {nullptr, nullptr};
+    cudaEvent_t ev_free[2] = {nullptr, nullptr};
+    const void *registered[3] = {nullptr, nullptr, nullptr};
+
+    uint64_t *d_inj_idx = nullptr;
+    float *d_inj_val = nullptr;
+    uint64_t inj_cap = 0;
+    uint64_t *h_inj_idx = nullptr;
+    float *h_inj_val = nullptr;
+    uint64_t h_inj_cap = 0;
+    cudaEvent_t ev_inj = nullptr;
+
+    ncclComm_t comm = nullptr;
+
+    uint64_t step = 0;
+    uint64_t launches = 0;
+    int timing = 0;
+    std::vector<TimingGroup> pending, pool;
+    double t_step = 0, t_lif = 0, t_exchange = 0, t_prop = 0;
+};
+
+namespace {
+
+snn_status_t dmalloc(void **ptr, uint64_t count, uint64_t elem) {
+    *ptr = nullptr;
+    if (count == 0) return SNN_OK;
+    if (seam_fail()) return SNN_ERR_CUDA;
+    return cuda_status(cudaMalloc(ptr, (size_t)(count * elem)));
+}
+
+snn_status_t h2d(snn_cuda_context_t *c, void *dst, const void *src, uint64_t bytes) {
+    if (bytes == 0) return SNN_OK;
+    if (seam_fail()) return SNN_ERR_CUDA;
+    return cuda_status(cudaMemcpyAsync(dst, src, (size_t)bytes, cudaMemcpyHostToDevice, c->stream));
+}
+
+snn_status_t check_launch(snn_cuda_context_t *c) {
+    c->launches++;
+    if (seam_fail()) return SNN_ERR_CUDA;
+    return cuda_status(cudaGetLastError());
+}
+
+snn_status_t set_device(const snn_cuda_context_t *c) { return cuda_status(cudaSetDevice(c->device)); }
+
+uint64_t ceil_div(uint64_t a, uint64_t b) { return (a + b - 1) / b; }
+
+// src/snn.c:308-316
+bool lif_valid(const snn_lif_params_t *p) {
+    return p && std::isfinite(p->dt_ms) && std::isfinite(p->membrane_tau_ms) && std::isfinite(p->v_rest) &&
+           std::isfinite(p->v_reset) && std::isfinite(p->v_threshold) && std::isfinite(p->input_scale) &&
+           p->dt_ms > 0.0f && p->membrane_tau_ms > 0.0f && p->v_threshold > p->v_reset;
+}
+
+void free_context(snn_cuda_context_t *c) {
+    if (c == nullptr) return;
+    if (c->device >= 0) cudaSetDevice(c->device);
+    if (c->stream) cudaStreamSynchronize(c->stream);
+    if (c->copy_stream) cudaStreamSynchronize(c->copy_stream);
+    if (c->comm) ncclCommDestroy(c->comm);
+    void *dev[] = {c->d_v, c->d_cur_pair, c->d_ext, c->d_refr, c->d_spikes, c->d_ws, c->d_row_ptr, c->d_col,
+                   c->d_w, c->d_col_ptr, c->d_pre, c->d_cw, c->d_deg, c->d_chunk_row, c->d_chunk_col,
+                   c->d_chunk_w, c->d_inj_idx, c->d_inj_val};
+    for (void *p : dev)
+        if (p) cudaFree(p);
+    if (c->h_inj_idx) cudaFreeHost(c->h_inj_idx);
+    if (c->h_inj_val) cudaFreeHost(c->h_inj_val);
+    for (const void *p : c->registered)
+        if (p) cudaHostUnregister(const_cast<void *>(p));
+    for (int i = 0; i < 2; ++i) {
+        if (c->ev_copied[i]) cudaEventDestroy(c->ev_copied[i]);
+        if (c->ev_free[i]) cudaEventDestroy(c->ev_free[i]);
+    }
+    if (c->ev_inj) cudaEventDestroy(c->ev_inj);
+    for (auto *v : {&c->pending, &c->pool})
+        for (auto &g : *v)
+            for (auto e : g.ev) cudaEventDestroy(e);
+    if (c->copy_stream) cudaStreamDestroy(c->copy_stream);
+    if (c->stream) cudaStreamDestroy(c->stream);
+    delete c;
+}
+
+// Resolves options, validates them and fills the shard geometry.
+snn_status_t apply_options(snn_cuda_context_t *c, uint64_t n, const snn_b200_options_t &o) {
+    if (o.world_size == 0 || o.rank >= o.world_size) return SNN_ERR_INVALID_ARGUMENT;
+    if (o.propagation != SNN_B200_PROPAGATE_PUSH && o.propagation != SNN_B200_PROPAGATE_ORDERED)
+        return SNN_ERR_INVALID_ARGUMENT;
+    if (o.index_width != 0 && o.index_width != 32 && o.index_width != 64) return SNN_ERR_INVALID_ARGUMENT;
+    if (o.world_size > 1 && o.nccl_id == nullptr) return SNN_ERR_INVALID_ARGUMENT;
+    c->propagation = o.propagation;
+    c->world = o.world_size;
+    c->rank = o.rank;
+    c->timing = o.timing;
+    c->n_global = n;
+    c->slot = ceil_div(ceil_div(n, o.world_size), 32) * 32;
+    c->lo = std::min<uint64_t>(n, (uint64_t)o.rank * c->slot);
+    c->hi = std::min<uint64_t>(n, c->lo + c->slot);
+    c->n_local = c->hi - c->lo;
+    c->bitmap_words = c->slot / 32 * o.world_size;
+    const bool fits32 = n <= 0xffffffffull;
+    c->idx_bits = fits32 ? 32 : 64;
+    c->col_bits = (o.index_width == 64 || !fits32) ? 64 : 32;
+    if (o.index_width == 32 && !fits32) return SNN_ERR_INVALID_ARGUMENT;
+    if (c->n_local >= 0xffffffffull) return SNN_ERR_UNSUPPORTED;
+    return SNN_OK;
+}
+
+uint64_t state_bytes(const snn_cuda_context_t *c) {
+    return c->n_local * (4u + 8u + 4u + 4u + 1u) + c->bitmap_words * 4u + c->n_global * (c->idx_bits / 8) + 256u;
+}
+
+// Device state: seams #1-#6 (six allocations) and #7 (init launch), matching
+// the reference's allocate_device_state (src/snn_cuda.cu:264-289).
+snn_status_t allocate_state(snn_cuda_context_t *c) {
+    snn_status_t st;
+    const uint64_t n = c->n_local;
+    if ((st = dmalloc((void **)&c->d_v, n, 4)) != SNN_OK) return st;
+    if ((st = dmalloc((void **)&c->d_cur_pair, 2 * n, 4)) != SNN_OK) return st;
+    if ((st = dmalloc((void **)&c->d_ext, n, 4)) != SNN_OK) return st;
+    if ((st = dmalloc((void **)&c->d_refr, n, 4)) != SNN_OK) return st;
+    if ((st = dmalloc((void **)&c->d_spikes, n, 1)) != SNN_OK) return st;
+    // Workspace: [counters | bitmap (global, padded) | spike list (global)].
+    const uint64_t list_bytes = c->n_global * (c->idx_bits / 8);
+    const uint64_t ws = 256 + ((c->bitmap_words * 4 + 255) / 256) * 256 + list_bytes;
+    if ((st = dmalloc(&c->d_ws, ws, 1)) != SNN_OK) return st;
+    c->d_ctr = (b200::DevCounters *)c->d_ws;
+    c->d_bitmap = (uint32_t *)((char *)c->d_ws + 256);
+    c->d_list = (char *)c->d_ws + 256 + ((c->bitmap_words * 4 + 255) / 256) * 256;
+    c->d_cur[0] = c->d_cur_pair;
+    c->d_cur[1] = c->d_cur_pair ? c->d_cur_pair + n : nullptr;
+    b200::launch_init_state(c->stream, n, c->lif.v_rest, c->d_v, c->d_cur[0], c->d_cur[1], c->d_ext, c->d_refr,
+                            c->d_spikes, c->bitmap_words, c->d_bitmap, c->d_ctr);
+    return check_launch(c);
+}
+
+snn_status_t create_streams(snn_cuda_context_t *c) {
+    if (cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) != cudaSuccess) return SNN_ERR_CUDA;
+    if (cudaEventCreateWithFlags(&c->ev_inj, cudaEventDisableTiming) != cudaSuccess) return SNN_ERR_CUDA;
+    return SNN_OK;
+}
+
+snn_status_t init_nccl(snn_cuda_context_t *c, const void *id) {
+    if (c->world <= 1) return SNN_OK;
+    ncclUniqueId uid;
+    std::memcpy(&uid, id, sizeof(uid));
+    if (ncclCommInitRank(&c->comm, (int)c->world, uid, (int)c->rank) != ncclSuccess) return SNN_ERR_CUDA;
+    return SNN_OK;
+}
+
+// Uploads a host u64 column array as local ids of c->col_bits, through a
+// bounded device staging buffer when narrowing. One fault seam.
+snn_status_t upload_cols(snn_cuda_context_t *c, void *dst, const uint64_t *src, uint64_t count, uint64_t lo,
+                         int bits) {
+    if (count == 0) return SNN_OK;
+    if (seam_fail()) return SNN_ERR_CUDA;
+    if (bits == 64 && lo == 0)
+        return cuda_status(cudaMemcpyAsync(dst, src, count * 8, cudaMemcpyHostToDevice, c->stream));
+    const uint64_t chunk = std::min<uint64_t>(count, 1ull << 26);
+    uint64_t *tmp = nullptr;
+    if (cudaMalloc(&tmp, chunk * 8) != cudaSuccess) return SNN_ERR_CUDA;
+    snn_status_t st = SNN_OK;
+    for (uint64_t k = 0; k < count && st == SNN_OK; k += chunk) {
+        const uint64_t m = std::min(chunk, count - k);
+        st = cuda_status(cudaMemcpyAsync(tmp, src + k, m * 8, cudaMemcpyHostToDevice, c->stream));
+        if (st == SNN_OK) {
+            b200::launch_convert_cols(c->stream, c->device, tmp, (char *)dst + k * (bits / 8), bits, m, lo);
+            st = cuda_status(cudaGetLastError());
+        }
+        if (st == SNN_OK) st = cuda_status(cudaStreamSynchronize(c->stream));
+    }
+    cudaFree(tmp);
+    return st;
+}
+
+// FULL push topology from a host network: seams #8-#10 allocations, #11-#13
+// uploads (src/snn_cuda.cu:291-314). Sharded contexts first slice the CSR to
+// the edges that target their neurons (all presynaptic rows kept).
+snn_status_t upload_full_push(snn_cuda_context_t *c, const snn_network_t *net) {
+    const uint64_t n = net->neuron_count;
+    std::vector<uint64_t> rp, cl;
+    std::vector<float> wl;
+    const uint64_t *row_ptr = net->row_ptr, *col = net->col_idx;
+    const float *w = net->weights;
+    uint64_t e = net->synapse_count;
+    if (c->world > 1) {
+        try {
+            rp.assign(n + 1, 0);
+            for (uint64_t i = 0; i < n; ++i) {
+                uint64_t k = 0;
+                for (uint64_t q = net->row_ptr[i]; q < net->row_ptr[i + 1]; ++q)
+                    k += (net->col_idx[q] >= c->lo && net->col_idx[q] < c->hi);
+                rp[i + 1] = rp[i] + k;
+            }
+            cl.resize(rp[n]);
+            wl.resize(rp[n]);
+            uint64_t pos = 0;
+            for (uint64_t q = 0; q < net->synapse_count; ++q) {
+                if (net->col_idx[q] >= c->lo && net->col_idx[q] < c->hi) {
+                    cl[pos] = net->col_idx[q];
+                    wl[pos] = net->weights[q];
+                    ++pos;
+                }
+            }
+        } catch (const std::bad_alloc &) {
+            return SNN_ERR_OUT_OF_MEMORY;
+        }
+        row_ptr = rp.data();
+        col = cl.data();
+        w = wl.data();
+        e = rp[n];
+    }
+    c->e_local = e;
+    snn_status_t st;
+    if ((st = dmalloc((void **)&c->d_row_ptr, n + 1, 8)) != SNN_OK) return st;
+    // +16 bytes of tail so no vector load can run past the allocation.
+    if ((st = dmalloc(&c->d_col, e ? e + 16 / (c->col_bits / 8) : 0, c->col_bits / 8)) != SNN_OK) return st;
+    if ((st = dmalloc((void **)&c->d_w, e ? e + 4 : 0, 4)) != SNN_OK) return st;
+    if ((st = h2d(c, c->d_row_ptr, row_ptr, (n + 1) * 8)) != SNN_OK) return st;
+    if ((st = upload_cols(c, c->d_col, col, e, c->lo, c->col_bits)) != SNN_OK) return st;
+    if ((st = h2d(c, c->d_w, w, e * 4)) != SNN_OK) return st;
+    return cuda_status(cudaStreamSynchronize(c->stream));
+}
+
+// FULL ordered topology: a CSC of the rank's targets built on the host with a
+// stable counting sort, so every target's incoming edges keep CSR order
+// (ascending presynaptic row, ascending edge index). Seams #8-#10 / #11-#13
+// as for push; the out-degree table for statistics follows.
+snn_status_t upload_full_ordered(snn_cuda_context_t *c, const snn_network_t *net) {
+    const uint64_t n = net->neuron_count;
+    const uint64_t nl = c->n_local;
+    std::vector<uint64_t> col_ptr, pre;
+    std::vector<float> w;
+    std::vector<uint32_t> deg;
+    try {
+        col_ptr.assign(nl + 1, 0);
+        deg.assign(n, 0);
+        for (uint64_t i = 0; i < n; ++i) {
+            for (uint64_t q = net->row_ptr[i]; q < net->row_ptr[i + 1]; ++q) {
+                const uint64_t t = net->col_idx[q];
+                if (t >= c->lo && t < c->hi) {
+                    col_ptr[t - c->lo + 1]++;
+                    deg[i]++;
+                }
+            }
+        }
+        for (uint64_t t = 0; t < nl; ++t) col_ptr[t + 1] += col_ptr[t];
+        pre.resize(col_ptr[nl]);
+        w.resize(col_ptr[nl]);
+        std::vector<uint64_t> cursor(col_ptr.begin(), col_ptr.end() - 1);
+        for (uint64_t i = 0; i < n; ++i) {
+            for (uint64_t q = net->row_ptr[i]; q < net->row_ptr[i + 1]; ++q) {
+                const uint64_t t = net->col_idx[q];
+                if (t >= c->lo && t < c->hi) {
+                    const uint64_t k = cursor[t - c->lo]++;
+                    pre[k] = i;
+                    w[k] = net->weights[q];
+                }
+            }
+        }
+    } catch (const std::bad_alloc &) {
+        return SNN_ERR_OUT_OF_MEMORY;
+    }
+    const uint64_t e = col_ptr[nl];
+    c->e_local = e;
+    snn_status_t st;
+    const int pre_bits = c->idx_bits;
+    if ((st = dmalloc((void **)&c->d_col_ptr, nl + 1, 8)) != SNN_OK) return st;
+    if ((st = dmalloc(&c->d_pre, e, pre_bits / 8)) != SNN_OK) return st;
+    if ((st = dmalloc((void **)&c->d_cw, e, 4)) != SNN_OK) return st;
+    if ((st = h2d(c, c->d_col_ptr, col_ptr.data(), (nl + 1) * 8)) != SNN_OK) return st;
+    if ((st = upload_cols(c, c->d_pre, pre.data(), e, 0, pre_bits)) != SNN_OK) return st;
+    if ((st = h2d(c, c->d_cw, w.data(), e * 4)) != SNN_OK) return st;
+    if ((st = dmalloc((void **)&c->d_deg, n, 4)) != SNN_OK) return st;
+    if ((st = h2d(c, c->d_deg, deg.data(), n * 4)) != SNN_OK) return st;
+    return cuda_status(cudaStreamSynchronize(c->stream));
+}
+
+uint64_t max_degree(const snn_network_t *net) {
+    uint64_t m = 0;
+    for (uint64_t i = 0; i < net->neuron_count; ++i) m = std::max<uint64_t>(m, net->row_ptr[i + 1] - net->row_ptr[i]);
+    return m;
+}
+
+// STREAMING: chunk sizing follows the reference's rules
+// (src/snn_cuda.cu:327-401): rows <= 65536 and <= n; auto rows take at most
+// half of the budget left after the resident state; an explicit synapse cap
+// below the densest row is INVALID_ARGUMENT; auto synapses fill the rest,
+// clamped up to the densest row and down to the synapse count, minimum 1.
+// Two copy slots are allocated (double buffering), so auto sizes are halved.
+// Seams: #8 host chunk table (OUT_OF_MEMORY), #9-#11 chunk buffers.
+snn_status_t allocate_streaming(snn_cuda_context_t *c, const snn_cuda_config_t &cfg, uint64_t budget) {
+    const snn_network_t *net = c->network;
+    const uint64_t n = net->neuron_count, e = net->synapse_count;
+    const uint64_t maxdeg = max_degree(net);
+    const uint64_t sb = state_bytes(c);
+    const uint64_t avail = budget > sb ? budget - sb : 0;
+    uint64_t rows = cfg.max_stream_rows ? cfg.max_stream_rows : n;
+    rows = std::min<uint64_t>(std::min<uint64_t>(rows, 65536), n);
+    if (cfg.max_stream_rows == 0) {
+        const uint64_t max_rows = avail / 2 / 2 / 8;
+        if (rows + 1 > max_rows) rows = max_rows > 1 ? max_rows - 1 : 1;
+    }
+    const uint64_t row_bytes = (rows + 1) * 8;
+    uint64_t syn;
+    if (cfg.max_stream_synapses != 0) {
+        if (cfg.max_stream_synapses < maxdeg) return SNN_ERR_INVALID_ARGUMENT;
+        syn = cfg.max_stream_synapses;
+    } else {
+        syn = avail > 2 * (row_bytes + 12) ? (avail - 2 * row_bytes) / (2 * 12) : 0;
+        if (syn < maxdeg) syn = maxdeg;
+    }
+    if (syn > e) syn = e;
+    if (syn == 0) syn = 1;
+    if (seam_fail()) return SNN_ERR_OUT_OF_MEMORY;
+    try {
+        // Greedy row admission, as the reference's per-step loop does
+        // (src/snn_cuda.cu:586-601); the schedule is fixed, so it is built once.
+        uint64_t r = 0;
+        while (r < n) {
+            StreamChunk ch{r, 0, net->row_ptr[r], 0};
+            uint64_t end = r;
+            while (end < n && ch.rows < rows) {
+                const uint64_t d = net->row_ptr[end + 1] - net->row_ptr[end];
+                if (ch.rows != 0 && ch.edge_count + d > syn) break;
+                ch.edge_count += d;
+                ++end;
+                ++ch.rows;
+                if (ch.edge_count == syn) break;
+            }
+            c->chunks.push_back(ch);
+            r = end;
+        }
+    } catch (const std::bad_alloc &) {
+        return SNN_ERR_OUT_OF_MEMORY;
+    }
+    c->slot_rows = rows;
+    c->slot_edges = syn;
+    // Slot strides are multiples of 4 elements so every slot base keeps the
+    // 16-byte alignment the vectorised edge loads rely on.
+    c->slot_stride = (syn + 3) / 4 * 4;
+    snn_status_t st;
+    if ((st = dmalloc((void **)&c->d_chunk_row, 2 * (rows + 1), 8)) != SNN_OK) return st;
+    if ((st = dmalloc((void **)&c->d_chunk_col, 2 * c->slot_stride + 4, 8)) != SNN_OK) return st;
+    if ((st = dmalloc((void **)&c->d_chunk_w, 2 * c->slot_stride + 4, 4)) != SNN_OK) return st;
+    if (cudaStreamCreateWithFlags(&c->copy_stream, cudaStreamNonBlocking) != cudaSuccess) return SNN_ERR_CUDA;
+    for (int i = 0; i < 2; ++i) {
+        if (cudaEventCreateWithFlags(&c->ev_copied[i], cudaEventDisableTiming) != cudaSuccess ||
+            cudaEventCreateWithFlags(&c->ev_free[i], cudaEventDisableTiming) != cudaSuccess)
+            return SNN_ERR_CUDA;
+        cudaEventRecord(c->ev_free[i], c->stream);
+    }
+    // Page-lock the borrowed host CSR in place (best effort) so chunk copies
+    // run asynchronously at full host-link speed; unregistered on free.
+    const void *arrays[3] = {net->row_ptr, net->col_idx, net->weights};
+    const uint64_t sizes[3] = {(n + 1) * 8, e * 8, e * 4};
+    for (int i = 0; i < 3; ++i) {
+        if (arrays[i] == nullptr || sizes[i] == 0) continue;
+        if (cudaHostRegister(const_cast<void *>(arrays[i]), sizes[i], cudaHostRegisterDefault) == cudaSuccess)
+            c->registered[i] = arrays[i];
+        else
+            cudaGetLastError();
+    }
+    return SNN_OK;
+}
+
+uint64_t full_push_bytes(const snn_cuda_context_t *c, uint64_t e) {
+    return state_bytes(c) + (c->n_global + 1) * 8 + e * (c->col_bits / 8 + 4);
+}
+
+struct CreateEnv {
+    uint64_t budget = 0;
+};
+
+// Shared prologue: availability, device, memory info, context allocation
+// (seam #0), streams, NCCL, device state (seams #1-#7).
+snn_status_t begin_create(uint64_t n, const snn_lif_params_t &lif, float decay, const snn_cuda_config_t *config,
+                          const snn_b200_options_t *options, snn_cuda_context_t **out, CreateEnv *env) {
+    if (!snn_cuda_available()) return SNN_ERR_CUDA;
+    const snn_b200_options_t o = options ? *options : snn_b200_default_options();
+    const snn_cuda_config_t cfg = config ? *config : snn_cuda_default_config();
+    int dev = o.device;
+    if (dev < 0 && cudaGetDevice(&dev) != cudaSuccess) return SNN_ERR_CUDA;
+    if (cudaSetDevice(dev) != cudaSuccess) return SNN_ERR_CUDA;
+    size_t free_b = 0, total_b = 0;
+    if (g_force_meminfo_fail || cudaMemGetInfo(&free_b, &total_b) != cudaSuccess) return SNN_ERR_CUDA;
+    env->budget = (cfg.max_vram_bytes == 0 || cfg.max_vram_bytes > free_b) ? (uint64_t)free_b : cfg.max_vram_bytes;
+    if (seam_fail()) return SNN_ERR_OUT_OF_MEMORY;
+    snn_cuda_context_t *c = new (std::nothrow) snn_cuda_context();
+    if (c == nullptr) return SNN_ERR_OUT_OF_MEMORY;
+    c->device = dev;
+    c->lif = lif;
+    c->args = b200::LifArgs{decay, lif.v_rest, lif.v_reset, lif.v_threshold, lif.input_scale, lif.refractory_steps};
+    snn_status_t st = apply_options(c, n, o);
+    if (st == SNN_OK) st = create_streams(c);
+    if (st == SNN_OK) st = init_nccl(c, o.nccl_id);
+    if (st == SNN_OK) st = allocate_state(c);
+    if (st != SNN_OK) {
+        free_context(c);
+        return st;
+    }
+    *out = c;
+    return SNN_OK;
+}
+
+// --------------------------------------------------------------- timing --
+TimingGroup *timing_begin(snn_cuda_context_t *c) {
+    if (!c->timing) return nullptr;
+    if (c->pool.empty()) {
+        TimingGroup g;
+        for (auto &e : g.ev) cudaEventCreate(&e);
+        c->pool.push_back(g);
+    }
+    c->pending.push_back(c->pool.back());
+    c->pool.pop_back();
+    TimingGroup *g = &c->pending.back();
+    cudaEventRecord(g->ev[0], c->stream);
+    return g;
+}
+
+void timing_mark(snn_cuda_context_t *c, TimingGroup *g, int k) {
+    if (g) cudaEventRecord(g->ev[k], c->stream);
+}
+
+void timing_fold(snn_cuda_context_t *c) {
+    for (auto &g : c->pending) {
+        float a = 0, b = 0, d = 0, t = 0;
+        if (cudaEventElapsedTime(&a, g.ev[0], g.ev[1]) == cudaSuccess &&
+            cudaEventElapsedTime(&b, g.ev[1], g.ev[2]) == cudaSuccess &&
+            cudaEventElapsedTime(&d, g.ev[2], g.ev[3]) == cudaSuccess &&
+            cudaEventElapsedTime(&t, g.ev[0], g.ev[3]) == cudaSuccess) {
+            c->t_lif += a;
+            c->t_exchange += b;
+            c->t_prop += d;
+            c->t_step += t;
+        }
+        c->pool.push_back(g);
+    }
+    c->pending.clear();
+    cudaGetLastError();
+}
+
+// --------------------------------------------------------------- step ----
+// The device part of one step: LIF (+ exchange) + propagation, then the
+// current-buffer swap. Seams: #1 integrate launch, #2 propagate launch (or
+// the per-chunk copies and launches in STREAMING). Enqueued on c->stream.
+snn_status_t enqueue_step(snn_cuda_context_t *c, bool has_ext) {
+    const int parity = (int)(c->step & 1u);
+    float *cur = c->d_cur[c->cur];
+    float *next = c->d_cur[c->cur ^ 1];
+    TimingGroup *tg = timing_begin(c);
+    const bool sharded = c->world > 1;
+    uint32_t *own_bitmap = c->d_bitmap + (uint64_t)c->rank * (c->slot / 32);
+    b200::launch_lif(c->stream, c->device, c->n_local, c->args, c->d_v, cur, has_ext ? c->d_ext : nullptr, c->d_refr,
+                     c->d_spikes, own_bitmap, sharded ? nullptr : c->d_list, c->idx_bits, c->lo, c->d_ctr, parity);
+    snn_status_t st = check_launch(c);
+    if (st != SNN_OK) return st;
+    timing_mark(c, tg, 1);
+    if (sharded) {
+        const size_t words = c->slot / 32;
+        if (ncclAllGather(own_bitmap, c->d_bitmap, words, ncclUint32, c->comm, c->stream) != ncclSuccess)
+            return SNN_ERR_CUDA;
+        b200::launch_compact(c->stream, c->device, c->d_bitmap, c->bitmap_words, c->d_list, c->idx_bits, c->d_ctr,
+                             parity, c->lo / 32, ceil_div(c->hi, 32));
+        c->launches++;
+        if ((st = cuda_status(cudaGetLastError())) != SNN_OK) return st;
+    }
+    timing_mark(c, tg, 2);
+    if (c->mode == SNN_CUDA_MODE_FULL) {
+        if (c->propagation == SNN_B200_PROPAGATE_ORDERED)
+            b200::launch_propagate_pull(c->stream, c->device, c->n_local, c->d_col_ptr, c->d_pre, c->idx_bits,
+                                        c->d_cw, c->d_bitmap, next, c->d_list, c->idx_bits, c->d_deg, c->d_ctr,
+                                        parity, !sharded);
+        else
+            b200::launch_propagate_push(c->stream, c->device, c->d_list, c->idx_bits, c->d_row_ptr, c->d_col,
+                                        c->col_bits, c->d_w, next, c->d_ctr, parity, !sharded);
+        if ((st = check_launch(c)) != SNN_OK) return st;
+    } else {
+        // STREAMING: chunk i uses copy slot i&1; its copies wait until the
+        // propagation that last used the slot is done, and its propagation
+        // waits for its copies, so copy i+1 overlaps propagation i.
+        const snn_network_t *net = c->network;
+        for (size_t i = 0; i < c->chunks.size(); ++i) {
+            const StreamChunk &ch = c->chunks[i];
+            const int s = (int)(i & 1u);
+            uint64_t *drow = c->d_chunk_row + (uint64_t)s * (c->slot_rows + 1);
+            uint64_t *dcol = c->d_chunk_col + (uint64_t)s * c->slot_stride;
+            float *dw = c->d_chunk_w + (uint64_t)s * c->slot_stride;
+            cudaStreamWaitEvent(c->copy_stream, c->ev_free[s], 0);
+            if (seam_fail()) return SNN_ERR_CUDA;
+            if (cudaMemcpyAsync(drow, net->row_ptr + ch.row_begin, (ch.rows + 1) * 8, cudaMemcpyHostToDevice,
+                                c->copy_stream) != cudaSuccess)
+                return SNN_ERR_CUDA;
+            if (ch.edge_count) {
+                if (seam_fail()) return SNN_ERR_CUDA;
+                if (cudaMemcpyAsync(dcol, net->col_idx + ch.edge_begin, ch.edge_count * 8, cudaMemcpyHostToDevice,
+                                    c->copy_stream) != cudaSuccess)
+                    return SNN_ERR_CUDA;
+                if (seam_fail()) return SNN_ERR_CUDA;
+                if (cudaMemcpyAsync(dw, net->weights + ch.edge_begin, ch.edge_count * 4, cudaMemcpyHostToDevice,
+                                    c->copy_stream) != cudaSuccess)
+                    return SNN_ERR_CUDA;
+            }
+            cudaEventRecord(c->ev_copied[s], c->copy_stream);
+            cudaStreamWaitEvent(c->stream, c->ev_copied[s], 0);
+            b200::launch_propagate_chunk(c->stream, c->device, ch.row_begin, ch.rows, ch.edge_begin, c->d_bitmap,
+                                         drow, dcol, dw, next, c->d_ctr, parity, i == 0);
+            if ((st = check_launch(c)) != SNN_OK) return st;
+            cudaEventRecord(c->ev_free[s], c->stream);
+        }
+    }
+    timing_mark(c, tg, 3);
+    c->cur ^= 1;
+    c->step++;
+    return SNN_OK;
+}
+
+snn_status_t ensure_inject_capacity(snn_cuda_context_t *c, uint64_t count) {
+    if (count > c->inj_cap) {
+        cudaStreamSynchronize(c->stream);
+        cudaFree(c->d_inj_idx);
+        cudaFree(c->d_inj_val);
+        c->d_inj_idx = nullptr;
+        c->d_inj_val = nullptr;
+        c->inj_cap = 0;
+        snn_status_t st;
+        if ((st = dmalloc((void **)&c->d_inj_idx, count, 8)) != SNN_OK) return st;
+        if ((st = dmalloc((void **)&c->d_inj_val, count, 4)) != SNN_OK) return st;
+        c->inj_cap = count;
+    }
+    if (count > c->h_inj_cap) {
+        cudaEventSynchronize(c->ev_inj);
+        if (c->h_inj_idx) cudaFreeHost(c->h_inj_idx);
+        if (c->h_inj_val) cudaFreeHost(c->h_inj_val);
+        c->h_inj_idx = nullptr;
+        c->h_inj_val = nullptr;
+        c->h_inj_cap = 0;
+        if (cudaMallocHost(&c->h_inj_idx, count * 8) != cudaSuccess ||
+            cudaMallocHost(&c->h_inj_val, count * 4) != cudaSuccess)
+            return SNN_ERR_OUT_OF_MEMORY;
+        c->h_inj_cap = count;
+    }
+    return SNN_OK;
+}
+
+snn_status_t validate_csr(uint64_t n, uint64_t e, const uint64_t *row_ptr, const uint64_t *col, const float *w) {
+    // src/snn.c:158-180
+    if (n == 0 || row_ptr == nullptr || (e != 0 && (col == nullptr || w == nullptr))) return SNN_ERR_INVALID_ARGUMENT;
+    if (row_ptr[0] != 0 || row_ptr[n] != e) return SNN_ERR_INVALID_ARGUMENT;
+    for (uint64_t i = 0; i < n; ++i)
+        if (row_ptr[i] > row_ptr[i + 1] || row_ptr[i + 1] > e) return SNN_ERR_INVALID_ARGUMENT;
+    for (uint64_t i = 0; i < e; ++i)
+        if (col[i] >= n || !std::isfinite(w[i])) return SNN_ERR_INVALID_ARGUMENT;
+    return SNN_OK;
+}
+
+// Device generation of a random pool / layered net into a FULL push context.
+snn_status_t generate_full(snn_cuda_context_t *c, const b200::GenParams &g, uint64_t e_total) {
+    snn_status_t st;
+    const uint64_t n = g.n;
+    if ((st = dmalloc((void **)&c->d_row_ptr, n + 1, 8)) != SNN_OK) return st;
+    uint64_t e = e_total;
+    if (c->world > 1) {
+        uint64_t *counts = nullptr;
+        if (cudaMalloc(&counts, (n + 1) * 8) != cudaSuccess) return SNN_ERR_CUDA;
+        cudaMemsetAsync(counts, 0, (n + 1) * 8, c->stream);
+        b200::launch_gen_count_shard(c->stream, c->device, g, c->lo, c->hi, counts);
+        size_t tb = 0;
+        b200::exclusive_scan_u64(c->stream, counts, c->d_row_ptr, n + 1, nullptr, &tb);
+        void *tmp = nullptr;
+        if (cudaMalloc(&tmp, tb ? tb : 1) != cudaSuccess) {
+            cudaFree(counts);
+            return SNN_ERR_CUDA;
+        }
+        st = cuda_status(b200::exclusive_scan_u64(c->stream, counts, c->d_row_ptr, n + 1, tmp, &tb));
+        if (st == SNN_OK)
+            st = cuda_status(cudaMemcpyAsync(&e, c->d_row_ptr + n, 8, cudaMemcpyDeviceToHost, c->stream));
+        if (st == SNN_OK) st = cuda_status(cudaStreamSynchronize(c->stream));
+        cudaFree(tmp);
+        cudaFree(counts);
+        if (st != SNN_OK) return st;
+    } else {
+        b200::launch_gen_row_ptr_dense(c->stream, c->device, g, c->d_row_ptr);
+    }
+    c->e_local = e;
+    if ((st = dmalloc(&c->d_col, e ? e + 16 / (c->col_bits / 8) : 0, c->col_bits / 8)) != SNN_OK) return st;
+    if ((st = dmalloc((void **)&c->d_w, e ? e + 4 : 0, 4)) != SNN_OK) return st;
+    if (c->world > 1) {
+        b200::launch_gen_fill_shard(c->stream, c->device, g, c->lo, c->hi, c->d_row_ptr, c->d_col, c->col_bits,
+                                    c->d_w);
+        if ((st = cuda_status(cudaGetLastError())) != SNN_OK) return st;
+    } else {
+        // Bounded launches (<= 2^30 edges each) keep every kernel short.
+        const uint64_t step = 1ull << 30;
+        for (uint64_t e0 = 0; e0 < e; e0 += step) {
+            b200::launch_gen_edges_dense(c->stream, c->device, g, e0, std::min(e, e0 + step), c->d_col, c->col_bits,
+                                         c->d_w);
+            if ((st = cuda_status(cudaGetLastError())) != SNN_OK) return st;
+        }
+    }
+    return cuda_status(cudaStreamSynchronize(c->stream));
+}
+
+snn_status_t finish_generated(snn_cuda_context_t *c, const b200::GenParams &g, uint64_t e_total,
+                              snn_cuda_context_t **out) {
+    snn_status_t st = SNN_OK;
+    if (c->propagation != SNN_B200_PROPAGATE_PUSH) st = SNN_ERR_UNSUPPORTED;
+    if (st == SNN_OK) {
+        c->mode = SNN_CUDA_MODE_FULL;
+        st = generate_full(c, g, e_total);
+    }
+    if (st != SNN_OK) {
+        free_context(c);
+        return st;
+    }
+    *out = c;
+    return SNN_OK;
+}
+
+}  // namespace
+
+// ======================================================================
+//                              C ABI
+// ======================================================================
+extern "C" {
+
+snn_cuda_config_t snn_cuda_default_config(void) {
+    snn_cuda_config_t c;
+    c.max_vram_bytes = 0;
+    c.max_stream_synapses = 0;
+    c.max_stream_rows = 0;
+    c.prefer_streaming = 0;
+    return c;
+}
+
+int snn_cuda_available(void) {
+    if (g_force_unavailable) return 0;
+    int count = 0;
+    return cudaGetDeviceCount(&count) == cudaSuccess && count > 0;
+}
+
+snn_b200_options_t snn_b200_default_options(void) {
+    snn_b200_options_t o;
+    o.propagation = SNN_B200_PROPAGATE_PUSH;
+    o.device = -1;
+    o.index_width = 0;
+    o.rank = 0;
+    o.world_size = 1;
+    o.nccl_id = nullptr;
+    o.timing = 0;
+    return o;
+}
+
+snn_status_t snn_b200_create(const snn_network_t *network, const snn_cuda_config_t *config,
+                             const snn_b200_options_t *options, snn_cuda_context_t **out_context) {
+    if (out_context == nullptr) return SNN_ERR_INVALID_ARGUMENT;
+    *out_context = nullptr;
+    if (network == nullptr) return SNN_ERR_INVALID_ARGUMENT;
+    const snn_cuda_config_t cfg = config ? *config : snn_cuda_default_config();
+    const snn_b200_options_t o = options ? *options : snn_b200_default_options();
+    if ((o.world_size > 1 || o.propagation == SNN_B200_PROPAGATE_ORDERED) && cfg.prefer_streaming)
+        return SNN_ERR_UNSUPPORTED;
+    snn_cuda_context_t *c = nullptr;
+    CreateEnv env;
+    snn_status_t st = begin_create(network->neuron_count, network->lif, network->decay, &cfg, &o, &c, &env);
+    if (st != SNN_OK) return st;
+    c->network = network;
+    const bool full_only = c->world > 1 || c->propagation == SNN_B200_PROPAGATE_ORDERED;
+    if (full_only || (!cfg.prefer_streaming && full_push_bytes(c, network->synapse_count) <= env.budget)) {
+        c->mode = SNN_CUDA_MODE_FULL;
+        st = c->propagation == SNN_B200_PROPAGATE_ORDERED ? upload_full_ordered(c, network)
+                                                          : upload_full_push(c, network);
+    } else {
+        c->mode = SNN_CUDA_MODE_STREAMING;
+        c->e_local = network->synapse_count;
+        st = allocate_streaming(c, cfg, env.budget);
+    }
+    if (st != SNN_OK) {
+        free_context(c);
+        return st;
+    }
+    *out_context = c;
+    return SNN_OK;
+}
+
+snn_status_t snn_cuda_create(const snn_network_t *network, const snn_cuda_config_t *config,
+                             snn_cuda_context_t **out_context) {
+    return snn_b200_create(network, config, nullptr, out_context);
+}
+
+void snn_cuda_free(snn_cuda_context_t *context) { free_context(context); }
+
+snn_cuda_mode_t snn_cuda_context_mode(const snn_cuda_context_t *context) {
+    return context == nullptr ? SNN_CUDA_MODE_NONE : context->mode;
+}
+
+snn_status_t snn_cuda_inject_current(snn_cuda_context_t *c, const snn_size_t *host_indices,
+                                     const float *host_values, snn_size_t count) {
+    if (c == nullptr || (count != 0 && (host_indices == nullptr || host_values == nullptr)))
+        return SNN_ERR_INVALID_ARGUMENT;
+    if (count == 0) return SNN_OK;
+    if (count > UINT64_MAX / sizeof(snn_size_t)) return SNN_ERR_INVALID_ARGUMENT;
+    for (uint64_t k = 0; k < count; ++k)
+        if (host_indices[k] >= c->n_global) return SNN_ERR_INVALID_ARGUMENT;
+    bool uniform = true;
+    uint32_t v0;
+    std::memcpy(&v0, host_values, 4);
+    for (uint64_t k = 1; k < count && uniform; ++k) {
+        uint32_t vk;
+        std::memcpy(&vk, host_values + k, 4);
+        uniform = vk == v0;
+    }
+    snn_status_t st = set_device(c);
+    if (st != SNN_OK) return st;
+    if ((st = ensure_inject_capacity(c, count)) != SNN_OK) return st;
+    // The pinned staging is reused: wait until the previous batch's copy is done.
+    if (cudaEventSynchronize(c->ev_inj) != cudaSuccess) return SNN_ERR_CUDA;
+    if (uniform) {
+        // Equal values: any accumulation order gives the same bits, so a
+        // plain atomic scatter is exact.
+        std::memcpy(c->h_inj_idx, host_indices, count * 8);
+        std::memcpy(c->h_inj_val, host_values, count * 4);
+    } else {
+        // Unequal values: stable sort by index so each index's values fold
+        // in their original order (src/snn.c:737-739).
+        std::vector<uint64_t> perm(count);
+        std::iota(perm.begin(), perm.end(), 0ull);
+        std::stable_sort(perm.begin(), perm.end(),
+                         [&](uint64_t a, uint64_t b) { return host_indices[a] < host_indices[b]; });
+        for (uint64_t k = 0; k < count; ++k) {
+            c->h_inj_idx[k] = host_indices[perm[k]];
+            c->h_inj_val[k] = host_values[perm[k]];
+        }
+    }
+    if ((st = h2d(c, c->d_inj_idx, c->h_inj_idx, count * 8)) != SNN_OK) return st;
+    if ((st = h2d(c, c->d_inj_val, c->h_inj_val, count * 4)) != SNN_OK) return st;
+    cudaEventRecord(c->ev_inj, c->stream);
+    float *cur = c->d_cur[c->cur];
+    if (uniform)
+        b200::launch_inject_atomic(c->stream, c->device, count, c->d_inj_idx, c->d_inj_val, c->lif.input_scale, cur,
+                                   c->lo, c->hi);
+    else
+        b200::launch_inject_ordered(c->stream, c->device, count, c->d_inj_idx, c->d_inj_val, c->lif.input_scale, cur,
+                                    c->lo, c->hi);
+    return check_launch(c);
+}
+
+snn_status_t snn_cuda_step(snn_cuda_context_t *c, const float *host_external_current, uint8_t *host_out_spikes) {
+    if (c == nullptr) return SNN_ERR_INVALID_ARGUMENT;
+    snn_status_t st = set_device(c);
+    if (st != SNN_OK) return st;
+    if (host_external_current != nullptr) {
+        if (seam_fail()) return SNN_ERR_CUDA;
+        if (cudaMemcpyAsync(c->d_ext, host_external_current, c->n_local * 4, cudaMemcpyHostToDevice, c->stream) !=
+            cudaSuccess)
+            return SNN_ERR_CUDA;
+    }
+    if ((st = enqueue_step(c, host_external_current != nullptr)) != SNN_OK) return st;
+    if (host_out_spikes != nullptr && c->n_local != 0) {
+        if (seam_fail()) return SNN_ERR_CUDA;
+        if (cudaMemcpyAsync(host_out_spikes, c->d_spikes, c->n_local, cudaMemcpyDeviceToHost, c->stream) !=
+            cudaSuccess)
+            return SNN_ERR_CUDA;
+    }
+    return cuda_status(cudaStreamSynchronize(c->stream));
+}
+
+snn_status_t snn_cuda_download_voltage(const snn_cuda_context_t *c, float *host_voltage, snn_size_t count) {
+    if (c == nullptr || host_voltage == nullptr || count < c->n_local) return SNN_ERR_INVALID_ARGUMENT;
+    if (c->n_local == 0) return SNN_OK;
+    if (set_device(c) != SNN_OK) return SNN_ERR_CUDA;
+    if (seam_fail()) return SNN_ERR_CUDA;
+    if (cudaMemcpyAsync(host_voltage, c->d_v, c->n_local * 4, cudaMemcpyDeviceToHost, c->stream) != cudaSuccess)
+        return SNN_ERR_CUDA;
+    return cuda_status(cudaStreamSynchronize(c->stream));
+}
+
+// ----------------------------------------------------------- test hooks --
+snn_cuda_context_t *snn_test_nonnull_cuda_context(void) { return (snn_cuda_context_t *)(uintptr_t)1u; }
+void snn_test_cuda_set_fail_after(int64_t calls_before_failure) { g_fail_after = calls_before_failure; }
+void snn_test_cuda_disable_failure(void) {
+    g_fail_after = -1;
+    g_force_unavailable = 0;
+    g_force_meminfo_fail = 0;
+}
+void snn_test_cuda_force_unavailable(int enable) { g_force_unavailable = enable; }
+void snn_test_cuda_force_meminfo_fail(int enable) { g_force_meminfo_fail = enable; }
+
+// ----------------------------------------------------------- extensions --
+snn_status_t snn_b200_create_random_pool(const snn_random_pool_config_t *pool, const snn_lif_params_t *lif,
+                                         const snn_cuda_config_t *config, const snn_b200_options_t *options,
+                                         snn_cuda_context_t **out_context) {
+    if (out_context == nullptr) return SNN_ERR_INVALID_ARGUMENT;
+    *out_context = nullptr;
+    // src/snn.c:536-548
+    if (pool == nullptr || pool->neuron_count == 0 ||
+        (!pool->allow_self_connections && pool->neuron_count == 1u && pool->fanout_per_neuron != 0u) ||
+        !std::isfinite(pool->weight_min) || !std::isfinite(pool->weight_max) || pool->weight_max < pool->weight_min ||
+        !std::isfinite(pool->weight_max - pool->weight_min))
+        return SNN_ERR_INVALID_ARGUMENT;
+    const snn_lif_params_t p = lif ? *lif : snn_lif_params_t{1.0f, 20.0f, 0.0f, 0.0f, 1.0f, 1.0f, 1u};
+    if (!lif_valid(&p)) return SNN_ERR_INVALID_ARGUMENT;
+    const uint64_t n = pool->neuron_count, f = pool->fanout_per_neuron;
+    if (f != 0 && n > UINT64_MAX / f) return SNN_ERR_OVERFLOW;
+    b200::GenParams g{};
+    g.n = n;
+    g.fanout = f;
+    g.seed = pool->seed;
+    g.wmin = pool->weight_min;
+    g.wmax = pool->weight_max;
+    g.allow_self = pool->allow_self_connections;
+    g.recurrent = 1;
+    snn_cuda_context_t *c = nullptr;
+    CreateEnv env;
+    snn_status_t st = begin_create(n, p, expf(-p.dt_ms / p.membrane_tau_ms), config, options, &c, &env);
+    if (st != SNN_OK) return st;
+    return finish_generated(c, g, n * f, out_context);
+}
+
+snn_status_t snn_b200_create_layered_random(const snn_size_t *layer_sizes, size_t layer_count, snn_size_t fanout,
+                                            float weight_min, float weight_max, uint64_t seed,
+                                            const snn_lif_params_t *lif, const snn_b200_options_t *options,
+                                            snn_cuda_context_t **out_context) {
+    if (out_context == nullptr) return SNN_ERR_INVALID_ARGUMENT;
+    *out_context = nullptr;
+    if (layer_sizes == nullptr || layer_count < 2 || layer_count > 16 || fanout == 0 || !std::isfinite(weight_min) ||
+        !std::isfinite(weight_max) || weight_max < weight_min || !std::isfinite(weight_max - weight_min))
+        return SNN_ERR_INVALID_ARGUMENT;
+    const snn_lif_params_t p = lif ? *lif : snn_lif_params_t{1.0f, 20.0f, 0.0f, 0.0f, 1.0f, 1.0f, 1u};
+    if (!lif_valid(&p)) return SNN_ERR_INVALID_ARGUMENT;
+    b200::GenParams g{};
+    g.off[0] = 0;
+    for (size_t l = 0; l < layer_count; ++l) {
+        if (layer_sizes[l] == 0 || g.off[l] > UINT64_MAX - layer_sizes[l]) return SNN_ERR_INVALID_ARGUMENT;
+        g.off[l + 1] = g.off[l] + layer_sizes[l];
+    }
+    g.n = g.off[layer_count];
+    g.fanout = fanout;
+    g.seed = seed;
+    g.wmin = weight_min;
+    g.wmax = weight_max;
+    g.recurrent = 0;
+    g.layers = (int)layer_count;
+    const uint64_t rows = g.off[layer_count - 1];
+    if (rows > UINT64_MAX / fanout) return SNN_ERR_OVERFLOW;
+    snn_cuda_context_t *c = nullptr;
+    CreateEnv env;
+    snn_status_t st = begin_create(g.n, p, expf(-p.dt_ms / p.membrane_tau_ms), nullptr, options, &c, &env);
+    if (st != SNN_OK) return st;
+    return finish_generated(c, g, rows * fanout, out_context);
+}
+
+snn_status_t snn_b200_nccl_unique_id(void *out_id128) {
+    if (out_id128 == nullptr) return SNN_ERR_INVALID_ARGUMENT;
+    ncclUniqueId id;
+    if (ncclGetUniqueId(&id) != ncclSuccess) return SNN_ERR_CUDA;
+    std::memcpy(out_id128, &id, sizeof(id));
+    return SNN_OK;
+}
+
+snn_status_t snn_b200_reset(snn_cuda_context_t *c) {
+    if (c == nullptr) return SNN_ERR_INVALID_ARGUMENT;
+    snn_status_t st = set_device(c);
+    if (st != SNN_OK) return st;
+    cudaStreamSynchronize(c->stream);
+    // Keep the cumulative statistics across the reset.
+    b200::DevCounters saved{};
+    if (cudaMemcpy(&saved, c->d_ctr, sizeof(saved), cudaMemcpyDeviceToHost) != cudaSuccess) return SNN_ERR_CUDA;
+    b200::launch_init_state(c->stream, c->n_local, c->lif.v_rest, c->d_v, c->d_cur[0], c->d_cur[1], c->d_ext,
+                            c->d_refr, c->d_spikes, c->bitmap_words, c->d_bitmap, c->d_ctr);
+    c->launches++;
+    if ((st = cuda_status(cudaGetLastError())) != SNN_OK) return st;
+    saved.list_count[0] = saved.list_count[1] = 0;
+    if (cudaMemcpyAsync(c->d_ctr, &saved, sizeof(saved), cudaMemcpyHostToDevice, c->stream) != cudaSuccess)
+        return SNN_ERR_CUDA;
+    c->cur = 0;
+    c->step = 0;
+    return cuda_status(cudaStreamSynchronize(c->stream));
+}
+
+snn_status_t snn_b200_inject_stream_async(snn_cuda_context_t *c, uint64_t seed, uint64_t step, snn_size_t count,
+                                          float value) {
+    if (c == nullptr) return SNN_ERR_INVALID_ARGUMENT;
+    if (count == 0) return SNN_OK;
+    snn_status_t st = set_device(c);
+    if (st != SNN_OK) return st;
+    // Uniform value: the atomic scatter is order-exact (see inject_current).
+    b200::launch_inject_stream(c->stream, c->device, seed, step, count, c->n_global,
+                               value * c->lif.input_scale, c->d_cur[c->cur], c->lo, c->hi);
+    c->launches++;
+    return cuda_status(cudaGetLastError());
+}
+
+snn_status_t snn_b200_step_async(snn_cuda_context_t *c) {
+    if (c == nullptr) return SNN_ERR_INVALID_ARGUMENT;
+    snn_status_t st = set_device(c);
+    if (st != SNN_OK) return st;
+    return enqueue_step(c, false);
+}
+
+snn_status_t snn_b200_run_stream_async(snn_cuda_context_t *c, uint64_t seed, uint64_t first_step, uint64_t steps,
+                                       snn_size_t count, float value) {
+    if (c == nullptr) return SNN_ERR_INVALID_ARGUMENT;
+    snn_status_t st = set_device(c);
+    if (st != SNN_OK) return st;
+    for (uint64_t t = 0; t < steps; ++t) {
+        if (count) {
+            b200::launch_inject_stream(c->stream, c->device, seed, first_step + t, count, c->n_global,
+                                       value * c->lif.input_scale, c->d_cur[c->cur], c->lo, c->hi);
+            c->launches++;
+        }
+        if ((st = enqueue_step(c, false)) != SNN_OK) return st;
+    }
+    return cuda_status(cudaGetLastError());
+}
+
+snn_status_t snn_b200_synchronize(snn_cuda_context_t *c) {
+    if (c == nullptr) return SNN_ERR_INVALID_ARGUMENT;
+    snn_status_t st = set_device(c);
+    if (st != SNN_OK) return st;
+    st = cuda_status(cudaStreamSynchronize(c->stream));
+    timing_fold(c);
+    return st;
+}
+
+snn_status_t snn_b200_get_stats(snn_cuda_context_t *c, snn_b200_stats_t *out) {
+    if (c == nullptr || out == nullptr) return SNN_ERR_INVALID_ARGUMENT;
+    snn_status_t st = snn_b200_synchronize(c);
+    if (st != SNN_OK) return st;
+    b200::DevCounters d{};
+    if (cudaMemcpy(&d, c->d_ctr, sizeof(d), cudaMemcpyDeviceToHost) != cudaSuccess) return SNN_ERR_CUDA;
+    out->steps = c->step;
+    out->spikes = d.spikes;
+    out->events = d.events;
+    out->kernel_launches = c->launches;
+    out->step_ms = c->t_step;
+    out->propagate_ms = c->t_prop;
+    out->lif_ms = c->t_lif;
+    out->exchange_ms = c->t_exchange;
+    return SNN_OK;
+}
+
+snn_status_t snn_b200_reset_stats(snn_cuda_context_t *c) {
+    if (c == nullptr) return SNN_ERR_INVALID_ARGUMENT;
+    snn_status_t st = snn_b200_synchronize(c);
+    if (st != SNN_OK) return st;
+    b200::DevCounters d{};
+    if (cudaMemcpy(&d, c->d_ctr, sizeof(d), cudaMemcpyDeviceToHost) != cudaSuccess) return SNN_ERR_CUDA;
+    d.spikes = 0;
+    d.events = 0;
+    if (cudaMemcpy(c->d_ctr, &d, sizeof(d), cudaMemcpyHostToDevice) != cudaSuccess) return SNN_ERR_CUDA;
+    c->launches = 0;
+    c->t_step = c->t_lif = c->t_exchange = c->t_prop = 0;
+    return SNN_OK;
+}
+
+snn_status_t snn_b200_get_layout(const snn_cuda_context_t *c, snn_b200_layout_t *out) {
+    if (c == nullptr || out == nullptr) return SNN_ERR_INVALID_ARGUMENT;
+    out->neuron_count = c->n_global;
+    out->local_begin = c->lo;
+    out->local_count = c->n_local;
+    out->local_synapses = c->e_local;
+    out->index_bits = (uint32_t)c->col_bits;
+    out->propagation = c->propagation;
+    out->device_state_bytes = state_bytes(c);
+    if (c->mode == SNN_CUDA_MODE_STREAMING)
+        out->device_topology_bytes = 2 * ((c->slot_rows + 1) * 8 + c->slot_edges * 12);
+    else if (c->propagation == SNN_B200_PROPAGATE_ORDERED)
+        out->device_topology_bytes = (c->n_local + 1) * 8 + c->e_local * (c->idx_bits / 8 + 4) + c->n_global * 4;
+    else
+        out->device_topology_bytes = (c->n_global + 1) * 8 + c->e_local * (c->col_bits / 8 + 4);
+    return SNN_OK;
+}
+
+void *snn_b200_stream(const snn_cuda_context_t *c) { return c ? (void *)c->stream : nullptr; }
+
+snn_status_t snn_b200_download_spikes(const snn_cuda_context_t *c, uint8_t *host, snn_size_t count) {
+    if (c == nullptr || host == nullptr || count < c->n_local) return SNN_ERR_INVALID_ARGUMENT;
+    if (c->n_local == 0) return SNN_OK;
+    if (set_device(c) != SNN_OK) return SNN_ERR_CUDA;
+    if (cudaMemcpyAsync(host, c->d_spikes, c->n_local, cudaMemcpyDeviceToHost, c->stream) != cudaSuccess)
+        return SNN_ERR_CUDA;
+    return cuda_status(cudaStreamSynchronize(c->stream));
+}
+
+snn_status_t snn_b200_download_current(const snn_cuda_context_t *c, float *host, snn_size_t count) {
+    if (c == nullptr || host == nullptr || count < c->n_local) return SNN_ERR_INVALID_ARGUMENT;
+    if (c->n_local == 0) return SNN_OK;
+    if (set_device(c) != SNN_OK) return SNN_ERR_CUDA;
+    if (cudaMemcpyAsync(host, c->d_cur[c->cur], c->n_local * 4, cudaMemcpyDeviceToHost, c->stream) != cudaSuccess)
+        return SNN_ERR_CUDA;
+    return cuda_status(cudaStreamSynchronize(c->stream));
+}
+
+snn_status_t snn_b200_upload_state(snn_cuda_context_t *c, const float *v, const float *cur, const uint32_t *refr,
+                                   snn_size_t count) {
+    if (c == nullptr || count < c->n_local) return SNN_ERR_INVALID_ARGUMENT;
+    if (c->n_local == 0) return SNN_OK;
+    if (set_device(c) != SNN_OK) return SNN_ERR_CUDA;
+    const uint64_t n = c->n_local;
+    if (v && cudaMemcpyAsync(c->d_v, v, n * 4, cudaMemcpyHostToDevice, c->stream) != cudaSuccess) return SNN_ERR_CUDA;
+    if (cur && cudaMemcpyAsync(c->d_cur[c->cur], cur, n * 4, cudaMemcpyHostToDevice, c->stream) != cudaSuccess)
+        return SNN_ERR_CUDA;
+    if (refr && cudaMemcpyAsync(c->d_refr, refr, n * 4, cudaMemcpyHostToDevice, c->stream) != cudaSuccess)
+        return SNN_ERR_CUDA;
+    return cuda_status(cudaStreamSynchronize(c->stream));
+}
+
+snn_status_t snn_b200_download_state(const snn_cuda_context_t *c, float *v, float *cur, uint32_t *refr,
+                                     snn_size_t count) {
+    if (c == nullptr || count < c->n_local) return SNN_ERR_INVALID_ARGUMENT;
+    if (c->n_local == 0) return SNN_OK;
+    if (set_device(c) != SNN_OK) return SNN_ERR_CUDA;
+    const uint64_t n = c->n_local;
+    if (v && cudaMemcpyAsync(v, c->d_v, n * 4, cudaMemcpyDeviceToHost, c->stream) != cudaSuccess) return SNN_ERR_CUDA;
+    if (cur && cudaMemcpyAsync(cur, c->d_cur[c->cur], n * 4, cudaMemcpyDeviceToHost, c->stream) != cudaSuccess)
+        return SNN_ERR_CUDA;
+    if (refr && cudaMemcpyAsync(refr, c->d_refr, n * 4, cudaMemcpyDeviceToHost, c->stream) != cudaSuccess)
+        return SNN_ERR_CUDA;
+    return cuda_status(cudaStreamSynchronize(c->stream));
+}
+
+snn_status_t snn_b200_download_topology(const snn_cuda_context_t *c, snn_size_t *row_ptr, snn_size_t row_capacity,
+                                        snn_size_t *col_idx, float *weights, snn_size_t edge_capacity) {
+    if (c == nullptr || c->mode != SNN_CUDA_MODE_FULL || c->propagation != SNN_B200_PROPAGATE_PUSH)
+        return SNN_ERR_INVALID_ARGUMENT;
+    if ((row_ptr && row_capacity < c->n_global + 1) || ((col_idx || weights) && edge_capacity < c->e_local))
+        return SNN_ERR_INVALID_ARGUMENT;
+    if (set_device(c) != SNN_OK) return SNN_ERR_CUDA;
+    if (cudaStreamSynchronize(c->stream) != cudaSuccess) return SNN_ERR_CUDA;
+    if (row_ptr && cudaMemcpy(row_ptr, c->d_row_ptr, (c->n_global + 1) * 8, cudaMemcpyDeviceToHost) != cudaSuccess)
+        return SNN_ERR_CUDA;
+    if (weights && c->e_local &&
+        cudaMemcpy(weights, c->d_w, c->e_local * 4, cudaMemcpyDeviceToHost) != cudaSuccess)
+        return SNN_ERR_CUDA;
+    if (col_idx && c->e_local) {
+        if (c->col_bits == 64) {
+            if (cudaMemcpy(col_idx, c->d_col, c->e_local * 8, cudaMemcpyDeviceToHost) != cudaSuccess)
+                return SNN_ERR_CUDA;
+        } else {
+            std::vector<uint32_t> tmp(c->e_local);
+            if (cudaMemcpy(tmp.data(), c->d_col, c->e_local * 4, cudaMemcpyDeviceToHost) != cudaSuccess)
+                return SNN_ERR_CUDA;
+            for (uint64_t k = 0; k < c->e_local; ++k) col_idx[k] = tmp[k];
+        }
+        for (uint64_t k = 0; k < c->e_local; ++k) col_idx[k] += c->lo;
+    }
+    return SNN_OK;
+}
+
+snn_status_t snn_b200_network_wrap(snn_size_t n, snn_size_t e, const snn_size_t *row_ptr, const snn_size_t *col_idx,
+                                   const float *weights, const snn_lif_params_t *lif, snn_network_t **out) {
+    if (out == nullptr) return SNN_ERR_INVALID_ARGUMENT;
+    *out = nullptr;
+    snn_status_t st = validate_csr(n, e, row_ptr, col_idx, weights);
+    if (st != SNN_OK) return st;
+    const snn_lif_params_t p = lif ? *lif : snn_lif_params_t{1.0f, 20.0f, 0.0f, 0.0f, 1.0f, 1.0f, 1u};
+    if (!lif_valid(&p)) return SNN_ERR_INVALID_ARGUMENT;
+    snn_network_t *net = new (std::nothrow) snn_network_t();
+    if (net == nullptr) return SNN_ERR_OUT_OF_MEMORY;
+    net->neuron_count = n;
+    net->synapse_count = e;
+    net->architecture = SNN_ARCH_CUSTOM_CSR;
+    net->lif = p;
+    net->decay = expf(-p.dt_ms / p.membrane_tau_ms);  // src/snn.c:111-113
+    net->row_ptr = const_cast<snn_size_t *>(row_ptr);
+    net->col_idx = const_cast<snn_size_t *>(col_idx);
+    net->weights = const_cast<float *>(weights);
+    *out = net;
+    return SNN_OK;
+}
+
+void snn_b200_network_unwrap(snn_network_t *network) { delete network; }
+
+}  // extern "C"
