@@ -204,6 +204,12 @@ snn_status_t snn_b200_create_layered_random(const snn_size_t *layer_sizes, size_
                                             const snn_b200_options_t *options,
                                             snn_cuda_context_t **out_context);
 
+/* Postsynaptic shard geometry (pure host computation, no device needed):
+ * rank r of world_size owns neurons [*out_begin, *out_begin + *out_count),
+ * slots of S = ceil(n / world_size / 32) * 32 neurons. */
+snn_status_t snn_b200_shard_range(snn_size_t neuron_count, uint32_t world_size, uint32_t rank,
+                                  snn_size_t *out_begin, snn_size_t *out_count);
+
 /* Writes a fresh 128-byte NCCL unique id (rank 0 calls it and shares the bytes). */
 snn_status_t snn_b200_nccl_unique_id(void *out_id128);
 

@@ -117,6 +117,7 @@ ENTRY_POINTS = [
     ("snn_b200_create_random_pool", C.c_int, [P, P, P, P, P]),
     ("snn_b200_create_layered_random", C.c_int, [P, C.c_size_t, u64, f32, f32, u64, P, P, P]),
     ("snn_b200_nccl_unique_id", C.c_int, [P]),
+    ("snn_b200_shard_range", C.c_int, [u64, C.c_uint32, C.c_uint32, P, P]),
     ("snn_b200_reset", C.c_int, [P]),
     ("snn_b200_inject_stream_async", C.c_int, [P, u64, u64, u64, f32]),
     ("snn_b200_run_stream_async", C.c_int, [P, u64, u64, u64, u64, f32]),
@@ -178,6 +179,13 @@ def default_options(**kw) -> Options:
 
 def cuda_available() -> bool:
     return bool(lib().snn_cuda_available())
+
+
+def shard_range(n: int, world: int, rank: int) -> tuple[int, int]:
+    """(first neuron, neuron count) owned by `rank` of `world` postsynaptic shards."""
+    b, c = u64(), u64()
+    _check(lib().snn_b200_shard_range(n, world, rank, C.byref(b), C.byref(c)), "snn_b200_shard_range")
+    return int(b.value), int(c.value)
 
 
 def nccl_unique_id() -> bytes:

@@ -199,6 +199,15 @@ void free_context(snn_cuda_context_t *c) {
     delete c;
 }
 
+// Rank r owns [r*S, min((r+1)*S, n)) with S = ceil(n / world / 32) * 32: equal
+// 32-aligned slots keep every rank's bitmap slice whole words of equal size
+// (the in-place all-gather needs equal counts).
+void shard_geometry(uint64_t n, uint32_t world, uint32_t rank, uint64_t *slot, uint64_t *lo, uint64_t *hi) {
+    *slot = ceil_div(ceil_div(n, world), 32) * 32;
+    *lo = std::min<uint64_t>(n, (uint64_t)rank * *slot);
+    *hi = std::min<uint64_t>(n, *lo + *slot);
+}
+
 // Resolves options, validates them and fills the shard geometry.
 snn_status_t apply_options(snn_cuda_context_t *c, uint64_t n, const snn_b200_options_t &o) {
     if (o.world_size == 0 || o.rank >= o.world_size) return SNN_ERR_INVALID_ARGUMENT;
@@ -211,9 +220,7 @@ snn_status_t apply_options(snn_cuda_context_t *c, uint64_t n, const snn_b200_opt
     c->rank = o.rank;
     c->timing = o.timing;
     c->n_global = n;
-    c->slot = ceil_div(ceil_div(n, o.world_size), 32) * 32;
-    c->lo = std::min<uint64_t>(n, (uint64_t)o.rank * c->slot);
-    c->hi = std::min<uint64_t>(n, c->lo + c->slot);
+    shard_geometry(n, o.world_size, o.rank, &c->slot, &c->lo, &c->hi);
     c->n_local = c->hi - c->lo;
     c->bitmap_words = c->slot / 32 * o.world_size;
     const bool fits32 = n <= 0xffffffffull;
@@ -234,7 +241,9 @@ snn_status_t allocate_state(snn_cuda_context_t *c) {
     snn_status_t st;
     const uint64_t n = c->n_local;
     if ((st = dmalloc((void **)&c->d_v, n, 4)) != SNN_OK) return st;
-    if ((st = dmalloc((void **)&c->d_cur_pair, 2 * n, 4)) != SNN_OK) return st;
+    // Both current buffers start on a 256-byte boundary (16-byte vector loads).
+    const uint64_t cur_stride = (n + 63) / 64 * 64;
+    if ((st = dmalloc((void **)&c->d_cur_pair, 2 * cur_stride, 4)) != SNN_OK) return st;
     if ((st = dmalloc((void **)&c->d_ext, n, 4)) != SNN_OK) return st;
     if ((st = dmalloc((void **)&c->d_refr, n, 4)) != SNN_OK) return st;
     if ((st = dmalloc((void **)&c->d_spikes, n, 1)) != SNN_OK) return st;
@@ -246,7 +255,7 @@ snn_status_t allocate_state(snn_cuda_context_t *c) {
     c->d_bitmap = (uint32_t *)((char *)c->d_ws + 256);
     c->d_list = (char *)c->d_ws + 256 + ((c->bitmap_words * 4 + 255) / 256) * 256;
     c->d_cur[0] = c->d_cur_pair;
-    c->d_cur[1] = c->d_cur_pair ? c->d_cur_pair + n : nullptr;
+    c->d_cur[1] = c->d_cur_pair ? c->d_cur_pair + cur_stride : nullptr;
     b200::launch_init_state(c->stream, n, c->lif.v_rest, c->d_v, c->d_cur[0], c->d_cur[1], c->d_ext, c->d_refr,
                             c->d_spikes, c->bitmap_words, c->d_bitmap, c->d_ctr);
     return check_launch(c);
@@ -966,6 +975,17 @@ snn_status_t snn_b200_create_layered_random(const snn_size_t *layer_sizes, size_
     snn_status_t st = begin_create(g.n, p, expf(-p.dt_ms / p.membrane_tau_ms), nullptr, options, &c, &env);
     if (st != SNN_OK) return st;
     return finish_generated(c, g, rows * fanout, out_context);
+}
+
+snn_status_t snn_b200_shard_range(snn_size_t n, uint32_t world, uint32_t rank, snn_size_t *out_begin,
+                                  snn_size_t *out_count) {
+    if (out_begin == nullptr || out_count == nullptr || world == 0 || rank >= world || n == 0)
+        return SNN_ERR_INVALID_ARGUMENT;
+    uint64_t slot, lo, hi;
+    shard_geometry(n, world, rank, &slot, &lo, &hi);
+    *out_begin = lo;
+    *out_count = hi - lo;
+    return SNN_OK;
 }
 
 snn_status_t snn_b200_nccl_unique_id(void *out_id128) {

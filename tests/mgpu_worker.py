@@ -1,0 +1,98 @@
+"""Worker for the sharded (multi-GPU) parity test, one process per GPU under
+torch.distributed.run. Every rank builds the same seeded network with the CPU
+oracle, creates a postsynaptic shard of it on its own GPU (NCCL spike
+all-gather inside the library), steps it with the seeded injection stream,
+and rank 0 compares the concatenated spike slices and voltages with the
+oracle's single-process run. Exit code 0 = parity holds.
+
+    python -m torch.distributed.run --nproc-per-node 2 --master-addr 127.0.0.1 \
+        --master-port 29511 tests/mgpu_worker.py
+"""
+import ctypes
+import os
+import sys
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+sys.path.insert(0, ROOT)
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+import torch.distributed as dist  # noqa: E402
+
+import snn_b200 as sb  # noqa: E402
+from oracle.oracle import Oracle, State, baseline_lif, stream_indices_np  # noqa: E402
+
+
+def main():
+    rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
+    local = int(os.environ.get("LOCAL_RANK", rank))
+    torch.cuda.set_device(local)
+    dist.init_process_group("gloo")
+    obj = [sb.nccl_unique_id() if rank == 0 else None]
+    dist.broadcast_object_list(obj, src=0)
+    idbuf = ctypes.create_string_buffer(obj[0], 128)
+
+    def options(prop):
+        o = sb.default_options(device=local, rank=rank, world_size=world, propagation=prop)
+        o.nccl_id = ctypes.cast(idbuf, ctypes.c_void_p)
+        return o
+
+    orc = Oracle("port")
+    failures = []
+    n, steps, count = 30011, 40, 300
+    lif = baseline_lif()
+    net = orc.random_pool(n, 120, -0.2, 0.5, 5, lif=lif)
+    for prop in (sb.PROPAGATE_ORDERED, sb.PROPAGATE_PUSH):
+        ctx = sb.CudaContext.create(net, None, options(prop))
+        lo, cnt = ctx.local_begin, ctx.local_count
+        raster = np.zeros((steps, cnt), np.uint8)
+        for t in range(steps):
+            idx = stream_indices_np(9, t, count, n)
+            assert ctx.inject_current(idx, np.full(count, 20.0, np.float32)) == 0
+            raster[t] = ctx.step()
+        v = ctx.download_voltage()
+        stats = ctx.stats()
+        parts = [None] * world
+        dist.all_gather_object(parts, (lo, raster, v, stats["events"], stats["spikes"]))
+        if rank == 0:
+            st = State(net)
+            sc, ev, hs, ras = orc.run_inject_stream(net, st, 9, 0, steps, count, 20.0, raster=True)
+            parts.sort(key=lambda p: p[0])
+            g_r = np.concatenate([p[1] for p in parts], axis=1)
+            g_v = np.concatenate([p[2] for p in parts])
+            exact = prop == sb.PROPAGATE_ORDERED
+            if exact:
+                if not np.array_equal(g_r, ras):
+                    failures.append(f"ordered raster mismatch at step {np.nonzero((g_r != ras).any(1))[0][:3]}")
+                if not np.array_equal(g_v.view(np.uint32), st.voltage().view(np.uint32)):
+                    failures.append("ordered voltage mismatch")
+                if sum(p[3] for p in parts) != int(ev.sum()) or sum(p[4] for p in parts) != int(sc.sum()):
+                    failures.append("ordered stats mismatch")
+            else:
+                if not np.array_equal(g_r[0], ras[0]):
+                    failures.append("push first-step raster mismatch")
+        ctx.free()
+    # Device-generated shards tile the host network exactly.
+    ctx = sb.CudaContext.random_pool(n, 120, -0.2, 0.5, 5, lif=None, options=options(sb.PROPAGATE_PUSH))
+    rp, ci, w = ctx.download_topology()
+    parts = [None] * world
+    dist.all_gather_object(parts, (ctx.local_begin, ctx.local_count, rp, ci, w))
+    if rank == 0:
+        hrp, hci, hw = net.row_ptr(), net.col_idx(), net.weights()
+        for lo, cnt, rp, ci, w in parts:
+            keep = (hci >= lo) & (hci < lo + cnt)
+            deg = np.add.reduceat(keep.astype(np.int64), hrp[:-1].astype(np.int64)) if hci.size else None
+            exp_rp = np.concatenate([[0], np.cumsum(deg)]).astype(np.uint64)
+            if not (np.array_equal(rp, exp_rp) and np.array_equal(ci, hci[keep]) and
+                    np.array_equal(w.view(np.uint32), hw[keep].view(np.uint32))):
+                failures.append(f"device shard {lo} topology mismatch")
+    ctx.free()
+    dist.barrier()
+    if rank == 0:
+        print("FAILURES:" if failures else "MGPU PARITY OK", failures)
+    dist.destroy_process_group()
+    sys.exit(1 if failures else 0)
+
+
+if __name__ == "__main__":
+    main()
