@@ -204,6 +204,10 @@ snn_status_t snn_b200_create_layered_random(const snn_size_t *layer_sizes, size_
                                             const snn_b200_options_t *options,
                                             snn_cuda_context_t **out_context);
 
+/* Human-readable detail of the calling thread's most recent CUDA/NCCL
+ * failure inside the library ("" if none); valid until the next failure. */
+const char *snn_b200_last_error(void);
+
 /* Postsynaptic shard geometry (pure host computation, no device needed):
  * rank r of world_size owns neurons [*out_begin, *out_begin + *out_count),
  * slots of S = ceil(n / world_size / 32) * 32 neurons. */

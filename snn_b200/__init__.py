@@ -118,6 +118,7 @@ ENTRY_POINTS = [
     ("snn_b200_create_layered_random", C.c_int, [P, C.c_size_t, u64, f32, f32, u64, P, P, P]),
     ("snn_b200_nccl_unique_id", C.c_int, [P]),
     ("snn_b200_shard_range", C.c_int, [u64, C.c_uint32, C.c_uint32, P, P]),
+    ("snn_b200_last_error", C.c_char_p, []),
     ("snn_b200_reset", C.c_int, [P]),
     ("snn_b200_inject_stream_async", C.c_int, [P, u64, u64, u64, f32]),
     ("snn_b200_run_stream_async", C.c_int, [P, u64, u64, u64, u64, f32]),
@@ -154,9 +155,15 @@ def lib() -> C.CDLL:
     return _LIB
 
 
+def last_error() -> str:
+    """Detail of this thread's most recent CUDA/NCCL failure in the library."""
+    return (lib().snn_b200_last_error() or b"").decode(errors="replace")
+
+
 def _check(st: int, what: str):
     if st != SNN_OK:
-        raise SnnError(st, what)
+        detail = last_error() if st == SNN_ERR_CUDA else ""
+        raise SnnError(st, f"{what} [{detail}]" if detail else what)
 
 
 def _ptr(a):

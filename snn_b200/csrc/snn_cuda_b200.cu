@@ -23,6 +23,7 @@
 
 #include <algorithm>
 #include <cmath>
+#include <cstdio>
 #include <cstdlib>
 #include <cstring>
 #include <new>
@@ -58,7 +59,19 @@ int seam_fail() {
     return 0;
 }
 
-snn_status_t cuda_status(cudaError_t e) { return e == cudaSuccess ? SNN_OK : SNN_ERR_CUDA; }
+thread_local char g_last_error[512] = "";
+
+void set_error(const char *what, const char *detail) {
+    std::snprintf(g_last_error, sizeof(g_last_error), "%s: %s", what, detail ? detail : "");
+}
+
+snn_status_t cuda_status_at(cudaError_t e, const char *where) {
+    if (e == cudaSuccess) return SNN_OK;
+    set_error(where, cudaGetErrorString(e));
+    return SNN_ERR_CUDA;
+}
+
+#define cuda_status(e) cuda_status_at((e), __func__)
 
 struct StreamChunk {
     uint64_t row_begin;
@@ -144,7 +157,10 @@ namespace {
 snn_status_t dmalloc(void **ptr, uint64_t count, uint64_t elem) {
     *ptr = nullptr;
     if (count == 0) return SNN_OK;
-    if (seam_fail()) return SNN_ERR_CUDA;
+    if (seam_fail()) {
+        set_error("cudaMalloc", "fault injected by snn_test_cuda_set_fail_after");
+        return SNN_ERR_CUDA;
+    }
     return cuda_status(cudaMalloc(ptr, (size_t)(count * elem)));
 }
 
@@ -271,7 +287,12 @@ snn_status_t init_nccl(snn_cuda_context_t *c, const void *id) {
     if (c->world <= 1) return SNN_OK;
     ncclUniqueId uid;
     std::memcpy(&uid, id, sizeof(uid));
-    if (ncclCommInitRank(&c->comm, (int)c->world, uid, (int)c->rank) != ncclSuccess) return SNN_ERR_CUDA;
+    const ncclResult_t r = ncclCommInitRank(&c->comm, (int)c->world, uid, (int)c->rank);
+    if (r != ncclSuccess) {
+        set_error("ncclCommInitRank", ncclGetErrorString(r));
+        c->comm = nullptr;
+        return SNN_ERR_CUDA;
+    }
     return SNN_OK;
 }
 
@@ -585,8 +606,11 @@ snn_status_t enqueue_step(snn_cuda_context_t *c, bool has_ext) {
     timing_mark(c, tg, 1);
     if (sharded) {
         const size_t words = c->slot / 32;
-        if (ncclAllGather(own_bitmap, c->d_bitmap, words, ncclUint32, c->comm, c->stream) != ncclSuccess)
+        const ncclResult_t r = ncclAllGather(own_bitmap, c->d_bitmap, words, ncclUint32, c->comm, c->stream);
+        if (r != ncclSuccess) {
+            set_error("ncclAllGather", ncclGetErrorString(r));
             return SNN_ERR_CUDA;
+        }
         b200::launch_compact(c->stream, c->device, c->d_bitmap, c->bitmap_words, c->d_list, c->idx_bits, c->d_ctr,
                              parity, c->lo / 32, ceil_div(c->hi, 32));
         c->launches++;
@@ -976,6 +1000,8 @@ snn_status_t snn_b200_create_layered_random(const snn_size_t *layer_sizes, size_
     if (st != SNN_OK) return st;
     return finish_generated(c, g, rows * fanout, out_context);
 }
+
+const char *snn_b200_last_error(void) { return g_last_error; }
 
 snn_status_t snn_b200_shard_range(snn_size_t n, uint32_t world, uint32_t rank, snn_size_t *out_begin,
                                   snn_size_t *out_count) {

@@ -28,11 +28,14 @@ def main():
     local = int(os.environ.get("LOCAL_RANK", rank))
     torch.cuda.set_device(local)
     dist.init_process_group("gloo")
-    obj = [sb.nccl_unique_id() if rank == 0 else None]
-    dist.broadcast_object_list(obj, src=0)
-    idbuf = ctypes.create_string_buffer(obj[0], 128)
+    keep = []
 
     def options(prop):
+        # A fresh NCCL unique id per context (one communicator each).
+        obj = [sb.nccl_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(obj, src=0)
+        idbuf = ctypes.create_string_buffer(obj[0], 128)
+        keep.append(idbuf)
         o = sb.default_options(device=local, rank=rank, world_size=world, propagation=prop)
         o.nccl_id = ctypes.cast(idbuf, ctypes.c_void_p)
         return o
