@@ -275,6 +275,36 @@ snn_status_t snn_b200_network_wrap(snn_size_t neuron_count, snn_size_t synapse_c
                                    snn_network_t **out_network);
 void snn_b200_network_unwrap(snn_network_t *network);
 
+/* Largest network snn_b200_step_noalloc accepts: its scratch is a fixed
+ * array of this many spike-list entries (plus bitmap and counters, ~4.2 MB)
+ * compiled into the library and resident on every GPU that loads it. */
+#define SNN_B200_NOALLOC_MAX_NEURONS 1048576u
+
+/* No counterpart in the reference: it has no allocation-free call.
+ *
+ * One push-mode step (LIF update, spike compaction, propagation) over device
+ * arrays the caller owns, for callers that cannot allocate device memory
+ * while they run -- memory owned by an outer framework's pool or arena, or
+ * loops where allocation after start-up is forbidden. It calls no cudaMalloc,
+ * cudaFree or other allocating routine; its only scratch is the fixed
+ * library array above. Same arithmetic as snn_cuda_step on a FULL push
+ * context: `current` (the input this step consumes) is zeroed, `next_current`
+ * must be all zero on entry and receives the propagated input; swap the two
+ * before the next call. `external` may be NULL; row_ptr holds n+1 edge
+ * offsets, col_idx 32-bit target ids. Neuron, external, col_idx and weight
+ * arrays must be 16-byte aligned, spikes 4-byte aligned.
+ *
+ * Work is enqueued on `stream` (a cudaStream_t, NULL = legacy default) of
+ * `device`; the call does not synchronise. neuron_count of 0 or above
+ * SNN_B200_NOALLOC_MAX_NEURONS, NULL or misaligned arrays return
+ * SNN_ERR_INVALID_ARGUMENT. The first call on a device looks up the scratch
+ * array's device address (make it before any stream capture). All calls on a
+ * device share the scratch: calls that overlap on the GPU race. */
+snn_status_t snn_b200_step_noalloc(int device, void *stream, snn_size_t neuron_count, const snn_lif_params_t *lif,
+                                   float decay, float *voltage, float *current, const float *external,
+                                   uint32_t *refractory, uint8_t *spikes, const snn_size_t *row_ptr,
+                                   const uint32_t *col_idx, const float *weights, float *next_current);
+
 #ifdef __cplusplus
 }
 #endif

@@ -38,6 +38,7 @@ STATUS_NAMES = {0: "ok", -1: "invalid argument", -2: "out of memory", -3: "integ
                 -4: "cuda error", -5: "unsupported"}
 
 MODE_NONE, MODE_FULL, MODE_STREAMING = 0, 1, 2
+NOALLOC_MAX_NEURONS = 1048576  # SNN_B200_NOALLOC_MAX_NEURONS
 PROPAGATE_PUSH, PROPAGATE_ORDERED = 0, 1
 
 
@@ -119,6 +120,7 @@ ENTRY_POINTS = [
     ("snn_b200_nccl_unique_id", C.c_int, [P]),
     ("snn_b200_shard_range", C.c_int, [u64, C.c_uint32, C.c_uint32, P, P]),
     ("snn_b200_last_error", C.c_char_p, []),
+    ("snn_b200_step_noalloc", C.c_int, [C.c_int, P, u64, P, f32, P, P, P, P, P, P, P, P, P]),
     ("snn_b200_reset", C.c_int, [P]),
     ("snn_b200_inject_stream_async", C.c_int, [P, u64, u64, u64, f32]),
     ("snn_b200_run_stream_async", C.c_int, [P, u64, u64, u64, u64, f32]),
