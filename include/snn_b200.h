@@ -141,7 +141,12 @@ typedef enum snn_b200_propagation {
     /* Per-target fold over a device CSC in CSR order (ascending presynaptic
      * row, ascending edge): bit-identical to the reference's serial CPU step
      * (src/snn.c:898-906) for any weights. FULL mode only. */
-    SNN_B200_PROPAGATE_ORDERED = 1
+    SNN_B200_PROPAGATE_ORDERED = 1,
+    /* The plain push kernel (one red.global.add per event), never binned.
+     * SNN_B200_PROPAGATE_PUSH selects the binned shared-memory variant when
+     * the device and the network allow it (32-bit columns, < 2^24 targets
+     * per GPU), else this one. Same results up to fp32 reassociation. */
+    SNN_B200_PROPAGATE_PUSH_ATOMIC = 2
 } snn_b200_propagation_t;
 
 typedef struct snn_b200_options {

@@ -1,0 +1,40 @@
+// Device helpers shared by the snn_b200 kernel translation units.
+#pragma once
+
+#include "b200_kernels.h"
+
+namespace b200 {
+namespace dev {
+
+constexpr unsigned kFull = 0xffffffffu;
+
+__device__ __forceinline__ unsigned lane_id() { return threadIdx.x & 31u; }
+
+// Fire-and-forget fp32 add into L2 (red.global.add.f32). The PTX f32 atomic
+// flushes subnormal inputs/results to zero, as the reference's atomicAdd does.
+__device__ __forceinline__ void red_add(float *p, float v) { atomicAdd(p, v); }
+
+// Block-level sum of per-thread u64 values, added once into *dst. Every
+// thread of the block must call it.
+__device__ __forceinline__ void block_add_u64(unsigned long long v, unsigned long long *dst) {
+    __shared__ unsigned long long s_acc;
+    if (threadIdx.x == 0) s_acc = 0ull;
+    __syncthreads();
+#pragma unroll
+    for (int d = 16; d > 0; d >>= 1) v += __shfl_xor_sync(kFull, v, d);
+    if (lane_id() == 0 && v) atomicAdd(&s_acc, v);
+    __syncthreads();
+    if (threadIdx.x == 0 && s_acc) atomicAdd(dst, s_acc);
+}
+
+// Per step bookkeeping done by block 0 of the (last) propagation kernel:
+// zero the list slot the next step appends to, and count this step's spikes.
+__device__ __forceinline__ void step_epilogue(DevCounters *ctr, int parity, int count_spikes, uint32_t count) {
+    if (blockIdx.x == 0 && threadIdx.x == 0) {
+        ctr->list_count[parity ^ 1] = 0u;
+        if (count_spikes) ctr->spikes += count;
+    }
+}
+
+}  // namespace dev
+}  // namespace b200

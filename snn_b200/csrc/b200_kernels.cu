@@ -9,6 +9,7 @@
 // __fsub_rn, so no FMA contraction can change a bit, and the host's
 // decay = expf(-dt/tau) is used as given.
 #include "b200_kernels.h"
+#include "b200_device.cuh"
 
 #include <cub/device/device_scan.cuh>
 
@@ -19,8 +20,9 @@ namespace b200 {
 
 namespace {
 
+using namespace dev;
+
 constexpr uint64_t kGamma = 0x9e3779b97f4a7c15ull;
-constexpr unsigned kFull = 0xffffffffu;
 
 __device__ __forceinline__ uint64_t mix64(uint64_t z) {
     z = (z ^ (z >> 30)) * 0xbf58476d1ce4e5b9ull;
@@ -43,12 +45,6 @@ __device__ __forceinline__ float lerp_weight(float wmin, float wmax, float u) {
     return w < wmax ? w : wmax;
 }
 
-__device__ __forceinline__ unsigned lane_id() { return threadIdx.x & 31u; }
-
-// Fire-and-forget fp32 add into L2 (red.global.add.f32; note that the PTX
-// f32 atomic flushes subnormal inputs/results to zero, as the reference's
-// atomicAdd does).
-__device__ __forceinline__ void red_add(float *p, float v) { atomicAdd(p, v); }
 
 template <typename T>
 struct Vec16;
@@ -264,27 +260,6 @@ __global__ void __launch_bounds__(256) compact_kernel(const uint32_t *__restrict
 #pragma unroll
     for (int d = 16; d > 0; d >>= 1) own += __shfl_xor_sync(kFull, own, d);
     if (lane == 0 && own) atomicAdd(&ctr->spikes, (unsigned long long)own);
-}
-
-// Block-level sum of per-thread u64 values, added once into *dst.
-__device__ __forceinline__ void block_add_u64(unsigned long long v, unsigned long long *dst) {
-    __shared__ unsigned long long s_acc;
-    if (threadIdx.x == 0) s_acc = 0ull;
-    __syncthreads();
-#pragma unroll
-    for (int d = 16; d > 0; d >>= 1) v += __shfl_xor_sync(kFull, v, d);
-    if (lane_id() == 0 && v) atomicAdd(&s_acc, v);
-    __syncthreads();
-    if (threadIdx.x == 0 && s_acc) atomicAdd(dst, s_acc);
-}
-
-// Per step bookkeeping done by block 0 of the (last) propagation kernel:
-// zero the list slot the next step appends to, and count this step's spikes.
-__device__ __forceinline__ void step_epilogue(DevCounters *ctr, int parity, int count_spikes, uint32_t count) {
-    if (blockIdx.x == 0 && threadIdx.x == 0) {
-        ctr->list_count[parity ^ 1] = 0u;
-        if (count_spikes) ctr->spikes += count;
-    }
 }
 
 // ---------------------------------------------------------------- push ----

@@ -121,6 +121,11 @@ struct snn_cuda_context {
     void *d_col = nullptr;
     float *d_w = nullptr;
 
+    bool binned = false;
+    b200::BinLayout bin{};
+    void *d_bin_mem = nullptr;
+    uint32_t *h_err = nullptr;  // pinned copy of DevCounters::error
+
     uint64_t *d_col_ptr = nullptr;
     void *d_pre = nullptr;
     float *d_cw = nullptr;
@@ -195,9 +200,10 @@ void free_context(snn_cuda_context_t *c) {
     if (c->comm) ncclCommDestroy(c->comm);
     void *dev[] = {c->d_v, c->d_cur_pair, c->d_ext, c->d_refr, c->d_spikes, c->d_ws, c->d_row_ptr, c->d_col,
                    c->d_w, c->d_col_ptr, c->d_pre, c->d_cw, c->d_deg, c->d_chunk_row, c->d_chunk_col,
-                   c->d_chunk_w, c->d_inj_idx, c->d_inj_val};
+                   c->d_chunk_w, c->d_inj_idx, c->d_inj_val, c->d_bin_mem};
     for (void *p : dev)
         if (p) cudaFree(p);
+    if (c->h_err) cudaFreeHost(c->h_err);
     if (c->h_inj_idx) cudaFreeHost(c->h_inj_idx);
     if (c->h_inj_val) cudaFreeHost(c->h_inj_val);
     for (const void *p : c->registered)
@@ -227,7 +233,8 @@ void shard_geometry(uint64_t n, uint32_t world, uint32_t rank, uint64_t *slot, u
 // Resolves options, validates them and fills the shard geometry.
 snn_status_t apply_options(snn_cuda_context_t *c, uint64_t n, const snn_b200_options_t &o) {
     if (o.world_size == 0 || o.rank >= o.world_size) return SNN_ERR_INVALID_ARGUMENT;
-    if (o.propagation != SNN_B200_PROPAGATE_PUSH && o.propagation != SNN_B200_PROPAGATE_ORDERED)
+    if (o.propagation != SNN_B200_PROPAGATE_PUSH && o.propagation != SNN_B200_PROPAGATE_ORDERED &&
+        o.propagation != SNN_B200_PROPAGATE_PUSH_ATOMIC)
         return SNN_ERR_INVALID_ARGUMENT;
     if (o.index_width != 0 && o.index_width != 32 && o.index_width != 64) return SNN_ERR_INVALID_ARGUMENT;
     if (o.world_size > 1 && o.nccl_id == nullptr) return SNN_ERR_INVALID_ARGUMENT;
@@ -280,7 +287,32 @@ snn_status_t allocate_state(snn_cuda_context_t *c) {
 snn_status_t create_streams(snn_cuda_context_t *c) {
     if (cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) != cudaSuccess) return SNN_ERR_CUDA;
     if (cudaEventCreateWithFlags(&c->ev_inj, cudaEventDisableTiming) != cudaSuccess) return SNN_ERR_CUDA;
+    if (cudaMallocHost(&c->h_err, sizeof(uint32_t)) != cudaSuccess) return SNN_ERR_OUT_OF_MEMORY;
+    *c->h_err = 0;
     return SNN_OK;
+}
+
+// Binned push (b200_binned.cu) for FULL push contexts with 32-bit columns:
+// allocates the L2 bins and the round counters. SNN_B200_OWNED_FRACTION
+// (environment, default 1) caps the share of targets accumulated in shared
+// memory; the rest use direct L2 atomics.
+snn_status_t setup_binned(snn_cuda_context_t *c) {
+    if (c->propagation != SNN_B200_PROPAGATE_PUSH || c->mode != SNN_CUDA_MODE_FULL || c->col_bits != 32)
+        return SNN_OK;
+    double frac = 1.0;
+    if (const char *env = std::getenv("SNN_B200_OWNED_FRACTION")) frac = std::atof(env);
+    if (!(frac > 0.0)) return SNN_OK;
+    if (!b200::binned_layout(c->device, c->n_local, c->e_local, c->n_global, frac, &c->bin)) return SNN_OK;
+    const uint64_t nbins = (uint64_t)c->bin.nb * c->bin.grid;
+    const uint64_t bytes = 256 + ((nbins * 4 + 255) / 256) * 256 + nbins * c->bin.cap * 8ull;
+    snn_status_t st = dmalloc(&c->d_bin_mem, bytes, 1);
+    if (st != SNN_OK) return st;
+    c->bin.sync = (unsigned long long *)c->d_bin_mem;
+    c->bin.bin_count = (uint32_t *)((char *)c->d_bin_mem + 256);
+    c->bin.bins = (uint2 *)((char *)c->d_bin_mem + 256 + ((nbins * 4 + 255) / 256) * 256);
+    if ((st = cuda_status(cudaMemsetAsync(c->d_bin_mem, 0, 256 + nbins * 4, c->stream))) != SNN_OK) return st;
+    c->binned = true;
+    return cuda_status(cudaStreamSynchronize(c->stream));
 }
 
 snn_status_t init_nccl(snn_cuda_context_t *c, const void *id) {
@@ -551,6 +583,20 @@ snn_status_t begin_create(uint64_t n, const snn_lif_params_t &lif, float decay, 
     return SNN_OK;
 }
 
+// Queues a copy of the device error word (raised by a bounded device wait
+// that expired) behind the work already on the stream.
+void queue_error_check(snn_cuda_context_t *c) {
+    cudaMemcpyAsync(c->h_err, &c->d_ctr->error, sizeof(uint32_t), cudaMemcpyDeviceToHost, c->stream);
+}
+
+snn_status_t error_after_sync(snn_cuda_context_t *c, snn_status_t st) {
+    if (st == SNN_OK && c->h_err && *c->h_err) {
+        set_error("device", "a bounded cross-CTA wait expired (propagation aborted)");
+        return SNN_ERR_CUDA;
+    }
+    return st;
+}
+
 // --------------------------------------------------------------- timing --
 TimingGroup *timing_begin(snn_cuda_context_t *c) {
     if (!c->timing) return nullptr;
@@ -622,7 +668,12 @@ snn_status_t enqueue_step(snn_cuda_context_t *c, bool has_ext) {
             b200::launch_propagate_pull(c->stream, c->device, c->n_local, c->d_col_ptr, c->d_pre, c->idx_bits,
                                         c->d_cw, c->d_bitmap, next, c->d_list, c->idx_bits, c->d_deg, c->d_ctr,
                                         parity, !sharded);
-        else
+        else if (c->binned) {
+            const cudaError_t e = b200::launch_propagate_binned(c->stream, c->d_list, c->idx_bits, c->d_row_ptr,
+                                                                (const uint32_t *)c->d_col, c->d_w, next, c->d_ctr,
+                                                                parity, !sharded, c->bin);
+            if (e != cudaSuccess) return cuda_status(e);
+        } else
             b200::launch_propagate_push(c->stream, c->device, c->d_list, c->idx_bits, c->d_row_ptr, c->d_col,
                                         c->col_bits, c->d_w, next, c->d_ctr, parity, !sharded);
         if ((st = check_launch(c)) != SNN_OK) return st;
@@ -755,11 +806,12 @@ snn_status_t generate_full(snn_cuda_context_t *c, const b200::GenParams &g, uint
 snn_status_t finish_generated(snn_cuda_context_t *c, const b200::GenParams &g, uint64_t e_total,
                               snn_cuda_context_t **out) {
     snn_status_t st = SNN_OK;
-    if (c->propagation != SNN_B200_PROPAGATE_PUSH) st = SNN_ERR_UNSUPPORTED;
+    if (c->propagation == SNN_B200_PROPAGATE_ORDERED) st = SNN_ERR_UNSUPPORTED;
     if (st == SNN_OK) {
         c->mode = SNN_CUDA_MODE_FULL;
         st = generate_full(c, g, e_total);
     }
+    if (st == SNN_OK) st = setup_binned(c);
     if (st != SNN_OK) {
         free_context(c);
         return st;
@@ -821,6 +873,7 @@ snn_status_t snn_b200_create(const snn_network_t *network, const snn_cuda_config
         c->mode = SNN_CUDA_MODE_FULL;
         st = c->propagation == SNN_B200_PROPAGATE_ORDERED ? upload_full_ordered(c, network)
                                                           : upload_full_push(c, network);
+        if (st == SNN_OK) st = setup_binned(c);
     } else {
         c->mode = SNN_CUDA_MODE_STREAMING;
         c->e_local = network->synapse_count;
@@ -907,13 +960,14 @@ snn_status_t snn_cuda_step(snn_cuda_context_t *c, const float *host_external_cur
             return SNN_ERR_CUDA;
     }
     if ((st = enqueue_step(c, host_external_current != nullptr)) != SNN_OK) return st;
+    if (c->binned) queue_error_check(c);
     if (host_out_spikes != nullptr && c->n_local != 0) {
         if (seam_fail()) return SNN_ERR_CUDA;
         if (cudaMemcpyAsync(host_out_spikes, c->d_spikes, c->n_local, cudaMemcpyDeviceToHost, c->stream) !=
             cudaSuccess)
             return SNN_ERR_CUDA;
     }
-    return cuda_status(cudaStreamSynchronize(c->stream));
+    return error_after_sync(c, cuda_status(cudaStreamSynchronize(c->stream)));
 }
 
 snn_status_t snn_cuda_download_voltage(const snn_cuda_context_t *c, float *host_voltage, snn_size_t count) {
@@ -1082,7 +1136,8 @@ snn_status_t snn_b200_synchronize(snn_cuda_context_t *c) {
     if (c == nullptr) return SNN_ERR_INVALID_ARGUMENT;
     snn_status_t st = set_device(c);
     if (st != SNN_OK) return st;
-    st = cuda_status(cudaStreamSynchronize(c->stream));
+    queue_error_check(c);
+    st = error_after_sync(c, cuda_status(cudaStreamSynchronize(c->stream)));
     timing_fold(c);
     return st;
 }
@@ -1186,7 +1241,7 @@ snn_status_t snn_b200_download_state(const snn_cuda_context_t *c, float *v, floa
 
 snn_status_t snn_b200_download_topology(const snn_cuda_context_t *c, snn_size_t *row_ptr, snn_size_t row_capacity,
                                         snn_size_t *col_idx, float *weights, snn_size_t edge_capacity) {
-    if (c == nullptr || c->mode != SNN_CUDA_MODE_FULL || c->propagation != SNN_B200_PROPAGATE_PUSH)
+    if (c == nullptr || c->mode != SNN_CUDA_MODE_FULL || c->propagation == SNN_B200_PROPAGATE_ORDERED)
         return SNN_ERR_INVALID_ARGUMENT;
     if ((row_ptr && row_capacity < c->n_global + 1) || ((col_idx || weights) && edge_capacity < c->e_local))
         return SNN_ERR_INVALID_ARGUMENT;

@@ -74,25 +74,28 @@ def test_ordered_negative_weights_dense_external():
     np.testing.assert_array_equal(bits(cv), bits(gv))
 
 
-def test_push_dyadic_bit_exact():
+@pytest.mark.parametrize("prop", [sb.PROPAGATE_PUSH, sb.PROPAGATE_PUSH_ATOMIC])
+def test_push_dyadic_bit_exact(prop):
     lif = baseline_lif()
     net = ORC.random_pool(20000, 48, 0.046875, 0.046875, 4242, lif=lif)
-    ctx = sb.CudaContext.create(net)
+    ctx = sb.CudaContext.create(net, None, opts(propagation=prop))
     assert ctx.mode == sb.MODE_FULL
     cr, gr, cv, gv = run_pair(net, ctx, 40, inject=stream_inject(3, 400, 20.0, 20000))
     assert first_divergence(cr, gr) is None
     np.testing.assert_array_equal(bits(cv), bits(gv))
 
 
-@pytest.mark.parametrize("width", [32, 64])
-def test_push_general_weights_tolerance(width):
+@pytest.mark.parametrize("width,prop,owned", [(32, sb.PROPAGATE_PUSH, "1"), (32, sb.PROPAGATE_PUSH, "0.4"),
+                                               (32, sb.PROPAGATE_PUSH_ATOMIC, "1"), (64, sb.PROPAGATE_PUSH, "1")])
+def test_push_general_weights_tolerance(width, prop, owned, monkeypatch):
     """Push with fp32 atomics: from the SAME state each step (teacher forcing
     through snn_b200_upload_state), voltages agree within 1e-5 relative and
     the divergent spikes (threshold ties) are counted and must be rare."""
     lif = baseline_lif()
     n = 20000
     net = ORC.random_pool(n, 100, 0.0, 0.6, 0, lif=lif)
-    ctx = sb.CudaContext.create(net, None, opts(index_width=width))
+    monkeypatch.setenv("SNN_B200_OWNED_FRACTION", owned)  # share of targets accumulated in smem tiles
+    ctx = sb.CudaContext.create(net, None, opts(index_width=width, propagation=prop))
     st = State(net)
     inj = stream_inject(1, 200, 20.0, n)
     divergent = 0
@@ -301,3 +304,24 @@ def test_dense_gaussian_config1_samples_with_reset():
         np.testing.assert_array_equal(bits(st.voltage()), bits(ctx.download_voltage()))
         st.reset()
         ctx.reset()
+
+
+def test_binned_push_overflow_fallback_exact():
+    """A hub row whose 70k edges hit 7 targets overflows the shared-memory
+    staging and the L2 bin capacity of one tile; the overflow falls back to
+    direct L2 atomics. Dyadic weights keep every sum exact, so the binned
+    push must equal the ordered CPU fold bit for bit."""
+    n = 70001
+    rp = np.zeros(n + 1, np.uint64)
+    rp[1:] = 70000
+    col = (np.arange(70000, dtype=np.uint64) % 7) + 1
+    w = np.full(70000, 0.0625, np.float32)
+    net = ORC.custom_csr(rp, col, w, lif=default_lif(v_threshold=1e6))
+    ext = np.zeros(n, np.float32)
+    ext[0] = 2e6
+    for prop in (sb.PROPAGATE_PUSH, sb.PROPAGATE_PUSH_ATOMIC):
+        ctx = sb.CudaContext.create(net, None, opts(propagation=prop))
+        cr, gr, cv, gv = run_pair(net, ctx, 3, ext=lambda t: ext if t == 0 else None)
+        assert first_divergence(cr, gr) is None
+        np.testing.assert_array_equal(bits(cv), bits(gv))
+        ctx.free()
