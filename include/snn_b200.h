@@ -144,8 +144,9 @@ typedef enum snn_b200_propagation {
     SNN_B200_PROPAGATE_ORDERED = 1,
     /* The plain push kernel (one red.global.add per event), never binned.
      * SNN_B200_PROPAGATE_PUSH selects the binned shared-memory variant when
-     * the device and the network allow it (32-bit columns, < 2^24 targets
-     * per GPU), else this one. Same results up to fp32 reassociation. */
+     * the device and the network allow it (32-bit columns, at most 4 target
+     * passes of < 2^24 targets each), else this one. Same results up to fp32
+     * reassociation. */
     SNN_B200_PROPAGATE_PUSH_ATOMIC = 2
 } snn_b200_propagation_t;
 
@@ -179,6 +180,8 @@ typedef struct snn_b200_layout {
     int propagation;                /* snn_b200_propagation_t */
     uint64_t device_state_bytes;    /* resident per-neuron state + spike workspace */
     uint64_t device_topology_bytes; /* resident topology (FULL) or chunk buffers (STREAMING) */
+    uint32_t binned;                /* 1: push runs the binned shared-memory kernel */
+    uint32_t binned_passes;         /* binned: target passes (each with its own CSR slice) */
 } snn_b200_layout_t;
 
 snn_b200_options_t snn_b200_default_options(void);

@@ -92,7 +92,7 @@ class Stats(C.Structure):
 class Layout(C.Structure):
     _fields_ = [("neuron_count", u64), ("local_begin", u64), ("local_count", u64), ("local_synapses", u64),
                 ("index_bits", C.c_uint32), ("propagation", C.c_int), ("device_state_bytes", u64),
-                ("device_topology_bytes", u64)]
+                ("device_topology_bytes", u64), ("binned", C.c_uint32), ("binned_passes", C.c_uint32)]
 
     def as_dict(self):
         return {k: getattr(self, k) for k, _ in self._fields_}

@@ -47,29 +47,36 @@ struct GenParams {
 };
 
 // Geometry and buffers of the binned push propagation (b200_binned.cu).
+constexpr uint32_t kMaxBinPasses = 4;
 struct BinLayout {
-    uint2 *bins;              // [nb][grid][cap] (offset in tile, weight bits)
-    uint32_t *bin_count;      // [nb][grid], zero between rounds
+    uint2 *bins;              // [nb][grid dest][grid src][cap] (offset in tile, weight bits)
+    uint32_t *counts;         // [nb][grid dest][grid src] entries per sub-bin, published per round
     unsigned long long *sync; // [0] router rounds finished, [1] drain rounds finished (x grid)
+    const uint64_t *row_ptr[kMaxBinPasses];  // per pass: CSR over all rows, edges into the pass only
+    const uint32_t *col[kMaxBinPasses];      // per pass: target ids relative to pass_lo
+    const float *w[kMaxBinPasses];
+    uint64_t pass_lo[kMaxBinPasses];         // first local target of each pass
+    uint64_t pass_len[kMaxBinPasses];        // targets of each pass
+    uint32_t passes;
     uint32_t grid;            // persistent CTAs = target tiles (one per SM)
     uint32_t nb;              // bin buffers (routers run up to nb-1 rounds ahead)
-    uint32_t stage;           // staged entries per tile in a router CTA's shared memory
     uint32_t tile;            // targets per tile
-    uint32_t owned;           // targets [0, owned) accumulate in shared memory
     uint64_t div_magic;       // ceil(2^40 / tile): t / tile == (t * div_magic) >> 40 for t < 2^24
     uint32_t rows_per_cta;    // spiking rows each CTA routes per round
-    uint32_t cap;             // bin capacity per (buffer, tile); overflow falls back to red.global
+    uint32_t cap;             // capacity of one sub-bin; overflow falls back to red.global
     uint32_t smem_bytes;      // dynamic shared memory per CTA
     uint32_t spin_limit;      // polls before a cross-CTA wait is declared failed
 };
 
-// Fills the geometry for n_local targets (bins/bin_count/sync left unset);
-// false when the device cannot run it (no cooperative launch, too large).
-bool binned_layout(int device, uint64_t n_local, uint64_t e_local, uint64_t n_rows, double owned_fraction,
+// Fills the geometry for n_local targets (buffers and CSR pointers left
+// unset); false when the device cannot run it. force_passes > 0 asks for at
+// least that many passes.
+bool binned_layout(int device, uint64_t n_local, uint64_t e_local, uint64_t n_rows, uint32_t force_passes,
                    BinLayout *layout);
-cudaError_t launch_propagate_binned(cudaStream_t s, const void *list, int idx_bits, const uint64_t *row_ptr,
-                                    const uint32_t *col, const float *w, float *next, DevCounters *ctr, int parity,
-                                    int count_spikes, const BinLayout &layout);
+// True when the cooperative grid of this layout is resident on the device.
+bool binned_fits(int device, const BinLayout &layout);
+cudaError_t launch_propagate_binned(cudaStream_t s, const void *list, int idx_bits, float *next, DevCounters *ctr,
+                                    int parity, int count_spikes, const BinLayout &layout);
 
 // Number of SMs of the current device (cached per device).
 int sm_count(int device);

@@ -124,6 +124,12 @@ struct snn_cuda_context {
     bool binned = false;
     b200::BinLayout bin{};
     void *d_bin_mem = nullptr;
+    // Binned push with more than one target pass keeps one CSR slice per
+    // pass (edges into the pass only, columns relative to the pass start).
+    uint32_t passes = 1;
+    uint64_t *d_prow[b200::kMaxBinPasses] = {};
+    void *d_pcol[b200::kMaxBinPasses] = {};
+    float *d_pw[b200::kMaxBinPasses] = {};
     uint32_t *h_err = nullptr;  // pinned copy of DevCounters::error
 
     uint64_t *d_col_ptr = nullptr;
@@ -203,6 +209,11 @@ void free_context(snn_cuda_context_t *c) {
                    c->d_chunk_w, c->d_inj_idx, c->d_inj_val, c->d_bin_mem};
     for (void *p : dev)
         if (p) cudaFree(p);
+    for (uint32_t p = 1; p < b200::kMaxBinPasses; ++p) {
+        if (c->d_prow[p]) cudaFree(c->d_prow[p]);
+        if (c->d_pcol[p]) cudaFree(c->d_pcol[p]);
+        if (c->d_pw[p]) cudaFree(c->d_pw[p]);
+    }
     if (c->h_err) cudaFreeHost(c->h_err);
     if (c->h_inj_idx) cudaFreeHost(c->h_inj_idx);
     if (c->h_inj_val) cudaFreeHost(c->h_inj_val);
@@ -292,26 +303,41 @@ snn_status_t create_streams(snn_cuda_context_t *c) {
     return SNN_OK;
 }
 
-// Binned push (b200_binned.cu) for FULL push contexts with 32-bit columns:
-// allocates the L2 bins and the round counters. SNN_B200_OWNED_FRACTION
-// (environment, default 1) caps the share of targets accumulated in shared
-// memory; the rest use direct L2 atomics.
-snn_status_t setup_binned(snn_cuda_context_t *c) {
-    if (c->propagation != SNN_B200_PROPAGATE_PUSH || c->mode != SNN_CUDA_MODE_FULL || c->col_bits != 32)
-        return SNN_OK;
-    double frac = 1.0;
-    if (const char *env = std::getenv("SNN_B200_OWNED_FRACTION")) frac = std::atof(env);
-    if (!(frac > 0.0)) return SNN_OK;
-    if (!b200::binned_layout(c->device, c->n_local, c->e_local, c->n_global, frac, &c->bin)) return SNN_OK;
-    const uint64_t nbins = (uint64_t)c->bin.nb * c->bin.grid;
-    const uint64_t bytes = 256 + ((nbins * 4 + 255) / 256) * 256 + nbins * c->bin.cap * 8ull;
+// Binned push (b200_binned.cu) for FULL push contexts with 32-bit columns.
+// plan_binned decides, before the topology is built, whether the binned
+// kernel runs and with how many target passes (each pass then gets its own
+// CSR slice); finish_binned allocates the bins once the slices exist.
+// SNN_B200_BINNED_PASSES (environment) forces a minimum pass count, for tests.
+void plan_binned(snn_cuda_context_t *c, uint64_t e_estimate) {
+    c->binned = false;
+    c->passes = 1;
+    if (c->propagation != SNN_B200_PROPAGATE_PUSH || c->mode != SNN_CUDA_MODE_FULL || c->col_bits != 32) return;
+    uint32_t force = 0;
+    if (const char *env = std::getenv("SNN_B200_BINNED_PASSES")) force = (uint32_t)std::atoi(env);
+    if (!b200::binned_layout(c->device, c->n_local, e_estimate, c->n_global, force, &c->bin) ||
+        !b200::binned_fits(c->device, c->bin))
+        return;
+    c->binned = true;
+    c->passes = c->bin.passes;
+}
+
+snn_status_t finish_binned(snn_cuda_context_t *c) {
+    if (!c->binned) return SNN_OK;
+    b200::BinLayout &L = c->bin;
+    for (uint32_t p = 0; p < L.passes; ++p) {
+        L.row_ptr[p] = p == 0 ? c->d_row_ptr : c->d_prow[p];
+        L.col[p] = (const uint32_t *)(p == 0 ? c->d_col : c->d_pcol[p]);
+        L.w[p] = p == 0 ? c->d_w : c->d_pw[p];
+    }
+    const uint64_t subs = (uint64_t)L.nb * L.grid * L.grid;
+    const uint64_t counts_bytes = ((subs * 4 + 255) / 256) * 256;
+    const uint64_t bytes = 256 + counts_bytes + subs * L.cap * 8ull;
     snn_status_t st = dmalloc(&c->d_bin_mem, bytes, 1);
     if (st != SNN_OK) return st;
-    c->bin.sync = (unsigned long long *)c->d_bin_mem;
-    c->bin.bin_count = (uint32_t *)((char *)c->d_bin_mem + 256);
-    c->bin.bins = (uint2 *)((char *)c->d_bin_mem + 256 + ((nbins * 4 + 255) / 256) * 256);
-    if ((st = cuda_status(cudaMemsetAsync(c->d_bin_mem, 0, 256 + nbins * 4, c->stream))) != SNN_OK) return st;
-    c->binned = true;
+    L.sync = (unsigned long long *)c->d_bin_mem;
+    L.counts = (uint32_t *)((char *)c->d_bin_mem + 256);
+    L.bins = (uint2 *)((char *)c->d_bin_mem + 256 + counts_bytes);
+    if ((st = cuda_status(cudaMemsetAsync(c->d_bin_mem, 0, 256 + counts_bytes, c->stream))) != SNN_OK) return st;
     return cuda_status(cudaStreamSynchronize(c->stream));
 }
 
@@ -353,30 +379,32 @@ snn_status_t upload_cols(snn_cuda_context_t *c, void *dst, const uint64_t *src, 
     return st;
 }
 
-// FULL push topology from a host network: seams #8-#10 allocations, #11-#13
-// uploads (src/snn_cuda.cu:291-314). Sharded contexts first slice the CSR to
-// the edges that target their neurons (all presynaptic rows kept).
-snn_status_t upload_full_push(snn_cuda_context_t *c, const snn_network_t *net) {
+// Push CSR of the edges that target [rlo, rhi) (global ids), columns stored
+// relative to rlo; all presynaptic rows kept. The whole-network case uploads
+// the host arrays directly. Seams: three allocations then three uploads, as
+// the reference's allocate_full_topology (src/snn_cuda.cu:291-314).
+snn_status_t upload_push_range(snn_cuda_context_t *c, const snn_network_t *net, uint64_t rlo, uint64_t rhi,
+                               uint64_t **d_row, void **d_col, float **d_w, uint64_t *edges) {
     const uint64_t n = net->neuron_count;
     std::vector<uint64_t> rp, cl;
     std::vector<float> wl;
     const uint64_t *row_ptr = net->row_ptr, *col = net->col_idx;
     const float *w = net->weights;
     uint64_t e = net->synapse_count;
-    if (c->world > 1) {
+    if (rlo != 0 || rhi != n) {
         try {
             rp.assign(n + 1, 0);
             for (uint64_t i = 0; i < n; ++i) {
                 uint64_t k = 0;
                 for (uint64_t q = net->row_ptr[i]; q < net->row_ptr[i + 1]; ++q)
-                    k += (net->col_idx[q] >= c->lo && net->col_idx[q] < c->hi);
+                    k += (net->col_idx[q] >= rlo && net->col_idx[q] < rhi);
                 rp[i + 1] = rp[i] + k;
             }
             cl.resize(rp[n]);
             wl.resize(rp[n]);
             uint64_t pos = 0;
             for (uint64_t q = 0; q < net->synapse_count; ++q) {
-                if (net->col_idx[q] >= c->lo && net->col_idx[q] < c->hi) {
+                if (net->col_idx[q] >= rlo && net->col_idx[q] < rhi) {
                     cl[pos] = net->col_idx[q];
                     wl[pos] = net->weights[q];
                     ++pos;
@@ -390,16 +418,35 @@ snn_status_t upload_full_push(snn_cuda_context_t *c, const snn_network_t *net) {
         w = wl.data();
         e = rp[n];
     }
-    c->e_local = e;
+    *edges = e;
     snn_status_t st;
-    if ((st = dmalloc((void **)&c->d_row_ptr, n + 1, 8)) != SNN_OK) return st;
+    if ((st = dmalloc((void **)d_row, n + 1, 8)) != SNN_OK) return st;
     // +16 bytes of tail so no vector load can run past the allocation.
-    if ((st = dmalloc(&c->d_col, e ? e + 16 / (c->col_bits / 8) : 0, c->col_bits / 8)) != SNN_OK) return st;
-    if ((st = dmalloc((void **)&c->d_w, e ? e + 4 : 0, 4)) != SNN_OK) return st;
-    if ((st = h2d(c, c->d_row_ptr, row_ptr, (n + 1) * 8)) != SNN_OK) return st;
-    if ((st = upload_cols(c, c->d_col, col, e, c->lo, c->col_bits)) != SNN_OK) return st;
-    if ((st = h2d(c, c->d_w, w, e * 4)) != SNN_OK) return st;
+    if ((st = dmalloc(d_col, e ? e + 16 / (c->col_bits / 8) : 0, c->col_bits / 8)) != SNN_OK) return st;
+    if ((st = dmalloc((void **)d_w, e ? e + 4 : 0, 4)) != SNN_OK) return st;
+    if ((st = h2d(c, *d_row, row_ptr, (n + 1) * 8)) != SNN_OK) return st;
+    if ((st = upload_cols(c, *d_col, col, e, rlo, c->col_bits)) != SNN_OK) return st;
+    if ((st = h2d(c, *d_w, w, e * 4)) != SNN_OK) return st;
     return cuda_status(cudaStreamSynchronize(c->stream));
+}
+
+// FULL push topology from a host network: the rank's range, or one slice per
+// binned target pass.
+snn_status_t upload_full_push(snn_cuda_context_t *c, const snn_network_t *net) {
+    const uint64_t e_est = (uint64_t)((double)net->synapse_count * ((double)c->n_local / (double)c->n_global));
+    plan_binned(c, e_est);
+    snn_status_t st = SNN_OK;
+    c->e_local = 0;
+    for (uint32_t p = 0; p < c->passes && st == SNN_OK; ++p) {
+        const uint64_t rlo = c->passes > 1 ? c->lo + c->bin.pass_lo[p] : c->lo;
+        const uint64_t rhi = c->passes > 1 ? rlo + c->bin.pass_len[p] : c->hi;
+        uint64_t e = 0;
+        st = p == 0 ? upload_push_range(c, net, rlo, rhi, &c->d_row_ptr, &c->d_col, &c->d_w, &e)
+                    : upload_push_range(c, net, rlo, rhi, &c->d_prow[p], &c->d_pcol[p], &c->d_pw[p], &e);
+        c->e_local += e;
+    }
+    if (st == SNN_OK) st = finish_binned(c);
+    return st;
 }
 
 // FULL ordered topology: a CSC of the rank's targets built on the host with a
@@ -669,8 +716,7 @@ snn_status_t enqueue_step(snn_cuda_context_t *c, bool has_ext) {
                                         c->d_cw, c->d_bitmap, next, c->d_list, c->idx_bits, c->d_deg, c->d_ctr,
                                         parity, !sharded);
         else if (c->binned) {
-            const cudaError_t e = b200::launch_propagate_binned(c->stream, c->d_list, c->idx_bits, c->d_row_ptr,
-                                                                (const uint32_t *)c->d_col, c->d_w, next, c->d_ctr,
+            const cudaError_t e = b200::launch_propagate_binned(c->stream, c->d_list, c->idx_bits, next, c->d_ctr,
                                                                 parity, !sharded, c->bin);
             if (e != cudaSuccess) return cuda_status(e);
         } else
@@ -756,51 +802,69 @@ snn_status_t validate_csr(uint64_t n, uint64_t e, const uint64_t *row_ptr, const
     return SNN_OK;
 }
 
-// Device generation of a random pool / layered net into a FULL push context.
-snn_status_t generate_full(snn_cuda_context_t *c, const b200::GenParams &g, uint64_t e_total) {
+// Device generation of the edges that target [rlo, rhi) (global ids) into a
+// push CSR with columns relative to rlo. The whole network takes the dense
+// path (row_ptr is i * fanout); a sub-range counts per row, scans, and fills.
+snn_status_t generate_range(snn_cuda_context_t *c, const b200::GenParams &g, uint64_t e_total, uint64_t rlo,
+                            uint64_t rhi, uint64_t **d_row, void **d_col, float **d_w, uint64_t *edges) {
     snn_status_t st;
     const uint64_t n = g.n;
-    if ((st = dmalloc((void **)&c->d_row_ptr, n + 1, 8)) != SNN_OK) return st;
+    if ((st = dmalloc((void **)d_row, n + 1, 8)) != SNN_OK) return st;
     uint64_t e = e_total;
-    if (c->world > 1) {
+    const bool whole = rlo == 0 && rhi == n;
+    if (!whole) {
         uint64_t *counts = nullptr;
         if (cudaMalloc(&counts, (n + 1) * 8) != cudaSuccess) return SNN_ERR_CUDA;
         cudaMemsetAsync(counts, 0, (n + 1) * 8, c->stream);
-        b200::launch_gen_count_shard(c->stream, c->device, g, c->lo, c->hi, counts);
+        b200::launch_gen_count_shard(c->stream, c->device, g, rlo, rhi, counts);
         size_t tb = 0;
-        b200::exclusive_scan_u64(c->stream, counts, c->d_row_ptr, n + 1, nullptr, &tb);
+        b200::exclusive_scan_u64(c->stream, counts, *d_row, n + 1, nullptr, &tb);
         void *tmp = nullptr;
         if (cudaMalloc(&tmp, tb ? tb : 1) != cudaSuccess) {
             cudaFree(counts);
             return SNN_ERR_CUDA;
         }
-        st = cuda_status(b200::exclusive_scan_u64(c->stream, counts, c->d_row_ptr, n + 1, tmp, &tb));
-        if (st == SNN_OK)
-            st = cuda_status(cudaMemcpyAsync(&e, c->d_row_ptr + n, 8, cudaMemcpyDeviceToHost, c->stream));
+        st = cuda_status(b200::exclusive_scan_u64(c->stream, counts, *d_row, n + 1, tmp, &tb));
+        if (st == SNN_OK) st = cuda_status(cudaMemcpyAsync(&e, *d_row + n, 8, cudaMemcpyDeviceToHost, c->stream));
         if (st == SNN_OK) st = cuda_status(cudaStreamSynchronize(c->stream));
         cudaFree(tmp);
         cudaFree(counts);
         if (st != SNN_OK) return st;
     } else {
-        b200::launch_gen_row_ptr_dense(c->stream, c->device, g, c->d_row_ptr);
+        b200::launch_gen_row_ptr_dense(c->stream, c->device, g, *d_row);
     }
-    c->e_local = e;
-    if ((st = dmalloc(&c->d_col, e ? e + 16 / (c->col_bits / 8) : 0, c->col_bits / 8)) != SNN_OK) return st;
-    if ((st = dmalloc((void **)&c->d_w, e ? e + 4 : 0, 4)) != SNN_OK) return st;
-    if (c->world > 1) {
-        b200::launch_gen_fill_shard(c->stream, c->device, g, c->lo, c->hi, c->d_row_ptr, c->d_col, c->col_bits,
-                                    c->d_w);
+    *edges = e;
+    if ((st = dmalloc(d_col, e ? e + 16 / (c->col_bits / 8) : 0, c->col_bits / 8)) != SNN_OK) return st;
+    if ((st = dmalloc((void **)d_w, e ? e + 4 : 0, 4)) != SNN_OK) return st;
+    if (!whole) {
+        b200::launch_gen_fill_shard(c->stream, c->device, g, rlo, rhi, *d_row, *d_col, c->col_bits, *d_w);
         if ((st = cuda_status(cudaGetLastError())) != SNN_OK) return st;
     } else {
         // Bounded launches (<= 2^30 edges each) keep every kernel short.
         const uint64_t step = 1ull << 30;
         for (uint64_t e0 = 0; e0 < e; e0 += step) {
-            b200::launch_gen_edges_dense(c->stream, c->device, g, e0, std::min(e, e0 + step), c->d_col, c->col_bits,
-                                         c->d_w);
+            b200::launch_gen_edges_dense(c->stream, c->device, g, e0, std::min(e, e0 + step), *d_col, c->col_bits,
+                                         *d_w);
             if ((st = cuda_status(cudaGetLastError())) != SNN_OK) return st;
         }
     }
     return cuda_status(cudaStreamSynchronize(c->stream));
+}
+
+snn_status_t generate_full(snn_cuda_context_t *c, const b200::GenParams &g, uint64_t e_total) {
+    plan_binned(c, (uint64_t)((double)e_total * ((double)c->n_local / (double)c->n_global)));
+    snn_status_t st = SNN_OK;
+    c->e_local = 0;
+    for (uint32_t p = 0; p < c->passes && st == SNN_OK; ++p) {
+        const uint64_t rlo = c->passes > 1 ? c->lo + c->bin.pass_lo[p] : c->lo;
+        const uint64_t rhi = c->passes > 1 ? rlo + c->bin.pass_len[p] : c->hi;
+        uint64_t e = 0;
+        st = p == 0 ? generate_range(c, g, e_total, rlo, rhi, &c->d_row_ptr, &c->d_col, &c->d_w, &e)
+                    : generate_range(c, g, e_total, rlo, rhi, &c->d_prow[p], &c->d_pcol[p], &c->d_pw[p], &e);
+        c->e_local += e;
+    }
+    if (st == SNN_OK) st = finish_binned(c);
+    return st;
 }
 
 snn_status_t finish_generated(snn_cuda_context_t *c, const b200::GenParams &g, uint64_t e_total,
@@ -811,7 +875,6 @@ snn_status_t finish_generated(snn_cuda_context_t *c, const b200::GenParams &g, u
         c->mode = SNN_CUDA_MODE_FULL;
         st = generate_full(c, g, e_total);
     }
-    if (st == SNN_OK) st = setup_binned(c);
     if (st != SNN_OK) {
         free_context(c);
         return st;
@@ -873,7 +936,6 @@ snn_status_t snn_b200_create(const snn_network_t *network, const snn_cuda_config
         c->mode = SNN_CUDA_MODE_FULL;
         st = c->propagation == SNN_B200_PROPAGATE_ORDERED ? upload_full_ordered(c, network)
                                                           : upload_full_push(c, network);
-        if (st == SNN_OK) st = setup_binned(c);
     } else {
         c->mode = SNN_CUDA_MODE_STREAMING;
         c->e_local = network->synapse_count;
@@ -1188,6 +1250,8 @@ snn_status_t snn_b200_get_layout(const snn_cuda_context_t *c, snn_b200_layout_t 
         out->device_topology_bytes = (c->n_local + 1) * 8 + c->e_local * (c->idx_bits / 8 + 4) + c->n_global * 4;
     else
         out->device_topology_bytes = (c->n_global + 1) * 8 + c->e_local * (c->col_bits / 8 + 4);
+    out->binned = c->binned ? 1u : 0u;
+    out->binned_passes = c->binned ? c->bin.passes : 0u;
     return SNN_OK;
 }
 
@@ -1243,6 +1307,7 @@ snn_status_t snn_b200_download_topology(const snn_cuda_context_t *c, snn_size_t 
                                         snn_size_t *col_idx, float *weights, snn_size_t edge_capacity) {
     if (c == nullptr || c->mode != SNN_CUDA_MODE_FULL || c->propagation == SNN_B200_PROPAGATE_ORDERED)
         return SNN_ERR_INVALID_ARGUMENT;
+    if (c->passes > 1) return SNN_ERR_UNSUPPORTED;  // topology split into target-pass slices
     if ((row_ptr && row_capacity < c->n_global + 1) || ((col_idx || weights) && edge_capacity < c->e_local))
         return SNN_ERR_INVALID_ARGUMENT;
     if (set_device(c) != SNN_OK) return SNN_ERR_CUDA;

@@ -80,22 +80,25 @@ def test_push_dyadic_bit_exact(prop):
     net = ORC.random_pool(20000, 48, 0.046875, 0.046875, 4242, lif=lif)
     ctx = sb.CudaContext.create(net, None, opts(propagation=prop))
     assert ctx.mode == sb.MODE_FULL
+    assert ctx.layout["binned"] == (1 if prop == sb.PROPAGATE_PUSH else 0)
     cr, gr, cv, gv = run_pair(net, ctx, 40, inject=stream_inject(3, 400, 20.0, 20000))
     assert first_divergence(cr, gr) is None
     np.testing.assert_array_equal(bits(cv), bits(gv))
 
 
-@pytest.mark.parametrize("width,prop,owned", [(32, sb.PROPAGATE_PUSH, "1"), (32, sb.PROPAGATE_PUSH, "0.4"),
-                                               (32, sb.PROPAGATE_PUSH_ATOMIC, "1"), (64, sb.PROPAGATE_PUSH, "1")])
-def test_push_general_weights_tolerance(width, prop, owned, monkeypatch):
+@pytest.mark.parametrize("width,prop,passes", [(32, sb.PROPAGATE_PUSH, "0"), (32, sb.PROPAGATE_PUSH, "3"),
+                                                (32, sb.PROPAGATE_PUSH_ATOMIC, "0"), (64, sb.PROPAGATE_PUSH, "0")])
+def test_push_general_weights_tolerance(width, prop, passes, monkeypatch):
     """Push with fp32 atomics: from the SAME state each step (teacher forcing
     through snn_b200_upload_state), voltages agree within 1e-5 relative and
     the divergent spikes (threshold ties) are counted and must be rare."""
     lif = baseline_lif()
     n = 20000
     net = ORC.random_pool(n, 100, 0.0, 0.6, 0, lif=lif)
-    monkeypatch.setenv("SNN_B200_OWNED_FRACTION", owned)  # share of targets accumulated in smem tiles
+    monkeypatch.setenv("SNN_B200_BINNED_PASSES", passes)  # force several target passes (CSR slices)
     ctx = sb.CudaContext.create(net, None, opts(index_width=width, propagation=prop))
+    if prop == sb.PROPAGATE_PUSH and width == 32:
+        assert ctx.layout["binned"] == 1 and ctx.layout["binned_passes"] == max(1, int(passes))
     st = State(net)
     inj = stream_inject(1, 200, 20.0, n)
     divergent = 0
@@ -325,3 +328,22 @@ def test_binned_push_overflow_fallback_exact():
         assert first_divergence(cr, gr) is None
         np.testing.assert_array_equal(bits(cv), bits(gv))
         ctx.free()
+
+
+@pytest.mark.parametrize("passes", ["0", "2"])
+def test_generated_pool_binned_passes_exact(passes, monkeypatch):
+    """Device-generated pool on the binned push path, with one and with two
+    target passes (per-pass CSR slices generated on the device): dyadic weights
+    make every sum exact, so spikes, events and voltages equal the oracle's."""
+    monkeypatch.setenv("SNN_B200_BINNED_PASSES", passes)
+    lif = baseline_lif()
+    n, f = 30011, 64
+    net = ORC.random_pool(n, f, 0.25, 0.25, 21, lif=lif)
+    st = State(net)
+    sc, ev, hs, _ = ORC.run_inject_stream(net, st, 5, 0, 30, 600, 20.0)
+    ctx = sb.CudaContext.random_pool(n, f, 0.25, 0.25, 21, lif=lif_to_sb(lif))
+    assert ctx.layout["binned"] == 1 and ctx.layout["binned_passes"] == max(1, int(passes))
+    ctx.run_stream_async(5, 0, 30, 600, 20.0)
+    s = ctx.stats()
+    assert s["spikes"] == int(sc.sum()) and s["events"] == int(ev.sum())
+    np.testing.assert_array_equal(bits(st.voltage()), bits(ctx.download_voltage()))
