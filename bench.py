@@ -53,6 +53,8 @@ def parse():
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--propagation", choices=["auto", "binned", "atomic"], default="auto",
+                    help="push kernel: auto (library default), binned (shared-memory tiles), atomic (L2 red)")
     return ap.parse_args()
 
 
@@ -190,7 +192,7 @@ def workload_config(args, world):
             "synapses": args.neurons * args.fanout, "weights": "U[-0.2,0.5] mV", "seed": args.seed,
             "inject": f"{args.inject_frac * 100:g}% of neurons x {args.inject_value:g} per step",
             "lif": "dt 1 ms, tau 20 ms, rest=reset -65 mV, thr -50 mV, refractory 2", "policy": "FULL",
-            "propagation": "push", "parallelism": f"postsynaptic shards x{world}", "l2": L2_NOTE}
+            "propagation": f"push ({args.propagation})", "parallelism": f"postsynaptic shards x{world}", "l2": L2_NOTE}
 
 
 # ------------------------------------------------------------ GPU side ----
@@ -224,7 +226,9 @@ def run_b200(args):
         dist.broadcast_object_list(obj, src=0)
         nccl_id = obj[0]
     id_buf = None
-    opts = sb.default_options(device=local, world_size=world, rank=rank, timing=1)
+    prop = {"auto": sb.PROPAGATE_PUSH, "binned": sb.PROPAGATE_PUSH_BINNED, "atomic": sb.PROPAGATE_PUSH_ATOMIC}
+    opts = sb.default_options(device=local, world_size=world, rank=rank, timing=1,
+                              propagation=prop[args.propagation])
     if nccl_id is not None:
         import ctypes
         id_buf = ctypes.create_string_buffer(nccl_id, 128)

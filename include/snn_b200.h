@@ -142,12 +142,15 @@ typedef enum snn_b200_propagation {
      * row, ascending edge): bit-identical to the reference's serial CPU step
      * (src/snn.c:898-906) for any weights. FULL mode only. */
     SNN_B200_PROPAGATE_ORDERED = 1,
-    /* The plain push kernel (one red.global.add per event), never binned.
-     * SNN_B200_PROPAGATE_PUSH selects the binned shared-memory variant when
-     * the device and the network allow it (32-bit columns, at most 4 target
-     * passes of < 2^24 targets each), else this one. Same results up to fp32
+    /* The plain push kernel: one red.global.add.f32 per event. */
+    SNN_B200_PROPAGATE_PUSH_ATOMIC = 2,
+    /* The binned push kernel: target tiles in shared memory, events routed
+     * through L2 bins by TMA-fed producer/consumer warps (at most 4 target
+     * passes of < 2^24 targets each, 32-bit columns; falls back to the
+     * atomic kernel otherwise). SNN_B200_PROPAGATE_PUSH picks whichever of
+     * the two is faster on this device. Both equal ORDERED up to fp32
      * reassociation. */
-    SNN_B200_PROPAGATE_PUSH_ATOMIC = 2
+    SNN_B200_PROPAGATE_PUSH_BINNED = 3
 } snn_b200_propagation_t;
 
 typedef struct snn_b200_options {

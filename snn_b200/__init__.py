@@ -39,7 +39,7 @@ STATUS_NAMES = {0: "ok", -1: "invalid argument", -2: "out of memory", -3: "integ
 
 MODE_NONE, MODE_FULL, MODE_STREAMING = 0, 1, 2
 NOALLOC_MAX_NEURONS = 1048576  # SNN_B200_NOALLOC_MAX_NEURONS
-PROPAGATE_PUSH, PROPAGATE_ORDERED, PROPAGATE_PUSH_ATOMIC = 0, 1, 2
+PROPAGATE_PUSH, PROPAGATE_ORDERED, PROPAGATE_PUSH_ATOMIC, PROPAGATE_PUSH_BINNED = 0, 1, 2, 3
 
 
 class SnnError(RuntimeError):

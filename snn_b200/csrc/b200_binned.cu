@@ -42,28 +42,11 @@ namespace {
 
 using namespace dev;
 
-constexpr int kRouterWarps = 12;
-constexpr int kDrainWarps = 4;
-constexpr int kThreads = 32 * (kRouterWarps + kDrainWarps);
-constexpr int kRouterThreads = 32 * kRouterWarps;
-constexpr int kDrainThreads = 32 * kDrainWarps;
-constexpr int kChunkEdges = 256;  // edges a router warp handles between staging flushes
-constexpr uint32_t kStage = 24;   // staged entries per destination tile
+constexpr int kThreads = 512;
+constexpr uint32_t kStage = 24;  // staged entries per destination tile
 
 __device__ __forceinline__ void named_sync(int id, int n) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
-}
-
-// Named barrier that also ANDs a per-thread predicate over the participants.
-__device__ __forceinline__ bool named_sync_and(int id, int n, bool pred) {
-    uint32_t r;
-    asm volatile(
-        "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 p, %1, 0;\n\tbar.red.and.pred q, %2, %3, p;\n\t"
-        "selp.u32 %0, 1, 0, q;\n\t}"
-        : "=r"(r)
-        : "r"((uint32_t)pred), "r"(id), "r"(n)
-        : "memory");
-    return r != 0u;
 }
 
 __device__ __forceinline__ unsigned long long ld_acquire(const unsigned long long *p) {
@@ -91,31 +74,145 @@ __device__ bool wait_geq(const unsigned long long *p, unsigned long long target,
     return true;
 }
 
+// ---------------------------------------------------------------------------
+// Warp roles (16 warps, one CTA per SM):
+//   warp 0        router producer: streams spiking-row segments with TMA bulk
+//                 copies (cp.async.bulk) into the router ring;
+//   warps 1-11    router consumers: route the ring's edges into staging and
+//                 flush staging into this CTA's sub-bins;
+//   warp 12       drain producer: streams this CTA's sub-bins of a finished
+//                 round into the drain ring (cp.async.bulk);
+//   warps 13-15   drain consumers: fold drain-ring entries into the tile.
+// Rings are flow-controlled by mbarriers (full: TMA bytes landed; empty:
+// consumers done), so no warp waits on memory latency.
+constexpr int kRConsThreads = 32 * 11;
+constexpr int kDConsThreads = 32 * 3;
+constexpr uint32_t kRSlots = 2;
+constexpr uint32_t kRSlotEdges = 1536;                         // edges per router slot (one staging flush)
+constexpr uint32_t kRMaxPieces = 32;                           // row segments per router slot
+constexpr uint32_t kRSlotCap = kRSlotEdges + 8 * kRMaxPieces;  // + alignment slack of the copies
+constexpr uint32_t kDSlots = 2;
+constexpr uint32_t kDSlotEntries = 1536;  // sub-bin entries per drain slot
+constexpr uint32_t kDMaxPieces = 64;      // sub-bins per drain slot
+constexpr uint32_t kDSlotCap = kDSlotEntries + 2 * kDMaxPieces;
+constexpr uint32_t kRoundEnd = 1u;
+
+template <uint32_t MAXP>
+struct SlotHdr {
+    uint32_t npieces;
+    uint32_t total;  // valid elements in the slot
+    uint32_t flags;  // kRoundEnd: last slot of a round
+    uint32_t pad;
+    uint32_t start[MAXP];       // data index of each piece's first valid element
+    uint32_t prefix[MAXP + 1];  // valid elements before each piece
+};
+
 struct Smem {
     float *tile;       // [tile]          the pass's targets owned by this CTA
     uint2 *stage;      // [grid][kStage]  staged events per destination
     uint32_t *scount;  // [grid]          staged entries per destination
     uint32_t *wcount;  // [grid]          entries written this round into my sub-bin of each destination
     uint32_t *sbase;   // [grid]          flush base per destination
-    uint32_t *dcount;  // [grid]          drain: entries in each source's sub-bin
+    uint32_t *dcount;  // [grid]          drain producer: entries in each source's sub-bin
+    uint32_t *rcol;    // [kRSlots][kRSlotCap]
+    float *rw;         // [kRSlots][kRSlotCap]
+    uint2 *dbuf;       // [kDSlots][kDSlotCap]
+    SlotHdr<kRMaxPieces> *rhdr;  // [kRSlots]
+    SlotHdr<kDMaxPieces> *dhdr;  // [kDSlots]
+    uint64_t *bar;               // rfull[2], rempty[2], dfull[2], dempty[2]
 };
+
+__host__ __device__ constexpr size_t align16(size_t x) { return (x + 15) & ~(size_t)15; }
+
+__host__ __device__ inline size_t smem_fixed_bytes(uint32_t grid) {
+    return align16((size_t)grid * kStage * 8) + 4 * align16((size_t)grid * 4) +
+           2 * align16((size_t)kRSlots * kRSlotCap * 4) + align16((size_t)kDSlots * kDSlotCap * 8) +
+           align16(kRSlots * sizeof(SlotHdr<kRMaxPieces>)) + align16(kDSlots * sizeof(SlotHdr<kDMaxPieces>)) + 8 * 8;
+}
 
 __device__ __forceinline__ Smem smem_layout(const BinLayout &L) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     Smem s;
     size_t o = 0;
     s.tile = reinterpret_cast<float *>(smem_raw + o);
-    o += (size_t)L.tile * 4u;
+    o += align16((size_t)L.tile * 4u);
     s.stage = reinterpret_cast<uint2 *>(smem_raw + o);
-    o += (size_t)L.grid * kStage * 8u;
+    o += align16((size_t)L.grid * kStage * 8u);
     s.scount = reinterpret_cast<uint32_t *>(smem_raw + o);
-    o += (size_t)L.grid * 4u;
+    o += align16((size_t)L.grid * 4u);
     s.wcount = reinterpret_cast<uint32_t *>(smem_raw + o);
-    o += (size_t)L.grid * 4u;
+    o += align16((size_t)L.grid * 4u);
     s.sbase = reinterpret_cast<uint32_t *>(smem_raw + o);
-    o += (size_t)L.grid * 4u;
+    o += align16((size_t)L.grid * 4u);
     s.dcount = reinterpret_cast<uint32_t *>(smem_raw + o);
+    o += align16((size_t)L.grid * 4u);
+    s.rcol = reinterpret_cast<uint32_t *>(smem_raw + o);
+    o += align16((size_t)kRSlots * kRSlotCap * 4);
+    s.rw = reinterpret_cast<float *>(smem_raw + o);
+    o += align16((size_t)kRSlots * kRSlotCap * 4);
+    s.dbuf = reinterpret_cast<uint2 *>(smem_raw + o);
+    o += align16((size_t)kDSlots * kDSlotCap * 8);
+    s.rhdr = reinterpret_cast<SlotHdr<kRMaxPieces> *>(smem_raw + o);
+    o += align16(kRSlots * sizeof(SlotHdr<kRMaxPieces>));
+    s.dhdr = reinterpret_cast<SlotHdr<kDMaxPieces> *>(smem_raw + o);
+    o += align16(kDSlots * sizeof(SlotHdr<kDMaxPieces>));
+    s.bar = reinterpret_cast<uint64_t *>(smem_raw + o);
     return s;
+}
+
+// ------------------------------------------------------------ mbarrier ----
+__device__ __forceinline__ uint32_t saddr(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ void mbar_init(uint64_t *b, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(saddr(b)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t *b, uint32_t bytes) {
+    asm volatile("mbarrier.expect_tx.relaxed.cta.shared::cta.b64 [%0], %1;" ::"r"(saddr(b)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t *b) {
+    asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.release.cta.shared::cta.b64 st, [%0];\n\t}" ::"r"(saddr(b))
+                 : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *b, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(saddr(b)), "r"(parity)
+        : "memory");
+    return ok != 0u;
+}
+// Bounded wait for the phase with `parity` to complete; raises the error
+// word on expiry and gives up at once if another CTA raised it.
+__device__ bool mbar_wait(uint64_t *b, uint32_t parity, uint32_t limit, uint32_t *err) {
+    for (uint32_t it = 0; !mbar_try_wait(b, parity); ++it) {
+        if (*(volatile uint32_t *)err != 0u) return false;
+        if (it >= limit) {
+            atomicExch(err, 2u);
+            return false;
+        }
+    }
+    return true;
+}
+// 1-D TMA bulk copy global -> this CTA's shared memory (no multicast),
+// completing `bytes` on the mbarrier. Addresses 16-byte aligned, bytes % 16 == 0.
+__device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(saddr(dst)),
+        "l"(src), "r"(bytes), "r"(saddr(bar))
+        : "memory");
+}
+
+template <uint32_t MAXP>
+__device__ __forceinline__ uint32_t find_piece(const SlotHdr<MAXP> &h, uint32_t j) {
+    uint32_t lo = 0, hi = h.npieces;  // largest p with prefix[p] <= j
+    while (hi - lo > 1) {
+        const uint32_t mid = (lo + hi) >> 1;
+        if (h.prefix[mid] <= j) lo = mid;
+        else hi = mid;
+    }
+    return lo;
 }
 
 struct RouteCtx {
@@ -139,45 +236,6 @@ __device__ __forceinline__ void route(uint32_t t, float wv, const BinLayout &L, 
     }
 }
 
-// Route edges [p, p + n) with the whole warp: 16-byte loads for the 4-aligned
-// body (both vectors of a lane issued before any routing), scalar head/tail.
-__device__ __forceinline__ void route_range(uint64_t p, uint64_t n, const uint32_t *__restrict__ col,
-                                            const float *__restrict__ w, const BinLayout &L, const Smem &S,
-                                            const RouteCtx &R, unsigned lane) {
-    const uint64_t e = p + n;
-    uint64_t a = (p + 3) & ~(uint64_t)3;
-    if (a > e) a = e;
-    if (lane < a - p) route(col[p + lane], w[p + lane], L, S, R);
-    const uint64_t nvec = (e - a) / 4;
-    const uint4 *cv = reinterpret_cast<const uint4 *>(col + a);
-    const float4 *wv = reinterpret_cast<const float4 *>(w + a);
-    uint4 c0 = make_uint4(0, 0, 0, 0), c1 = c0;
-    float4 x0 = make_float4(0, 0, 0, 0), x1 = x0;
-    const bool h0 = lane < nvec, h1 = lane + 32 < nvec;
-    if (h0) {
-        c0 = __ldcs(cv + lane);
-        x0 = __ldcs(wv + lane);
-    }
-    if (h1) {
-        c1 = __ldcs(cv + lane + 32);
-        x1 = __ldcs(wv + lane + 32);
-    }
-    if (h0) {
-        route(c0.x, x0.x, L, S, R);
-        route(c0.y, x0.y, L, S, R);
-        route(c0.z, x0.z, L, S, R);
-        route(c0.w, x0.w, L, S, R);
-    }
-    if (h1) {
-        route(c1.x, x1.x, L, S, R);
-        route(c1.y, x1.y, L, S, R);
-        route(c1.z, x1.z, L, S, R);
-        route(c1.w, x1.w, L, S, R);
-    }
-    const uint64_t t0 = a + nvec * 4;
-    if (lane < e - t0) route(col[t0 + lane], w[t0 + lane], L, S, R);
-}
-
 template <typename TIdx>
 __global__ void __launch_bounds__(kThreads, 1)
     propagate_binned_kernel(const TIdx *__restrict__ list, float *__restrict__ next, DevCounters *ctr, int parity,
@@ -195,10 +253,23 @@ __global__ void __launch_bounds__(kThreads, 1)
     unsigned long long *drained = L.sync + 1;
     const size_t q_stride = (size_t)G * L.cap;       // one destination's sub-bins (all sources)
     const size_t buf_stride = (size_t)G * q_stride;  // one bin buffer
+    uint64_t *rfull = S.bar, *rempty = S.bar + 2, *dfull = S.bar + 4, *dempty = S.bar + 6;
+    uint32_t *err = &ctr->error;
+    const uint32_t lim = L.spin_limit;
 
-    if (threadIdx.x == 0) s_abort = 0u;
+    if (threadIdx.x == 0) {
+        s_abort = 0u;
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(rfull + i, 1);
+            mbar_init(rempty + i, 1);
+            mbar_init(dfull + i, 1);
+            mbar_init(dempty + i, 1);
+        }
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
     for (uint32_t j = threadIdx.x; j < G; j += kThreads) S.scount[j] = 0u;
     unsigned long long events = 0;
+    uint32_t rfill = 0, dfill = 0;  // ring fills so far (slot = fill % 2, use = fill / 2)
 
     for (uint32_t pass = 0; pass < L.passes; ++pass) {
         const uint64_t *__restrict__ row_ptr = L.row_ptr[pass];
@@ -207,59 +278,115 @@ __global__ void __launch_bounds__(kThreads, 1)
         float *next_pass = next + L.pass_lo[pass];
         for (uint32_t j = threadIdx.x; j < L.tile; j += kThreads) S.tile[j] = 0.0f;
         __syncthreads();
-        if (warp < (unsigned)kRouterWarps) {
-            // --------------------------------------------------- routers --
-            const unsigned rw = warp;
+        if (warp == 0) {
+            // ------------------------------------------- router producer --
+            for (uint32_t k = 0; k < rounds && !s_abort; ++k) {
+                const uint32_t r0 = k * rows_round + c * L.rows_per_cta;
+                const uint32_t r1 = min(r0 + L.rows_per_cta, S_rows);
+                uint32_t s = rfill & 1u, np = 0, total = 0, used = 0;
+                bool ok = true;
+                if (lane == 0 && rfill >= 2) ok = mbar_wait(rempty + s, ((rfill >> 1) - 1) & 1u, lim, err);
+                for (uint32_t rb = r0; rb < r1 && __shfl_sync(kFull, ok, 0); rb += 32) {
+                    uint64_t b = 0, e = 0;
+                    if (rb + lane < r1) {
+                        const uint64_t row = (uint64_t)list[rb + lane];
+                        b = row_ptr[row];
+                        e = row_ptr[row + 1];
+                        events += e - b;
+                    }
+                    const uint32_t nrow = min(32u, r1 - rb);
+                    for (uint32_t jr = 0; jr < nrow; ++jr) {
+                        const uint64_t bj = __shfl_sync(kFull, b, jr), ej = __shfl_sync(kFull, e, jr);
+                        if (lane == 0) {
+                            uint64_t pos = bj;
+                            while (ok && pos < ej) {
+                                if (np == kRMaxPieces || total == kRSlotEdges) {
+                                    SlotHdr<kRMaxPieces> &h = S.rhdr[s];
+                                    h.npieces = np;
+                                    h.total = total;
+                                    h.prefix[np] = total;
+                                    h.flags = 0u;
+                                    mbar_arrive(rfull + s);
+                                    ++rfill;
+                                    s = rfill & 1u;
+                                    np = total = used = 0;
+                                    if (rfill >= 2) ok = mbar_wait(rempty + s, ((rfill >> 1) - 1) & 1u, lim, err);
+                                    if (!ok) break;
+                                }
+                                const uint64_t take = min(ej - pos, (uint64_t)(kRSlotEdges - total));
+                                const uint64_t ab = pos & ~(uint64_t)3;
+                                const uint64_t ae = (pos + take + 3) & ~(uint64_t)3;
+                                const uint32_t nal = (uint32_t)(ae - ab);
+                                SlotHdr<kRMaxPieces> &h = S.rhdr[s];
+                                h.start[np] = used + (uint32_t)(pos - ab);
+                                h.prefix[np] = total;
+                                ++np;
+                                total += (uint32_t)take;
+                                mbar_expect_tx(rfull + s, nal * 8u);
+                                bulk_g2s(S.rcol + s * kRSlotCap + used, col + ab, nal * 4u, rfull + s);
+                                bulk_g2s(S.rw + s * kRSlotCap + used, w + ab, nal * 4u, rfull + s);
+                                used += nal;
+                                pos += take;
+                            }
+                        }
+                        ok = __shfl_sync(kFull, ok, 0);
+                    }
+                }
+                if (lane == 0) {
+                    if (ok) {
+                        SlotHdr<kRMaxPieces> &h = S.rhdr[s];
+                        h.npieces = np;
+                        h.total = total;
+                        h.prefix[np] = total;
+                        h.flags = kRoundEnd;
+                        mbar_arrive(rfull + s);
+                        ++rfill;
+                    } else {
+                        s_abort = 1u;
+                    }
+                }
+                if (!__shfl_sync(kFull, ok, 0)) break;
+            }
+        } else if (warp <= 11) {
+            // ------------------------------------------ router consumers --
+            const unsigned rt = threadIdx.x - 32;
+            const unsigned rw = warp - 1;
             for (uint32_t k = 0; k < rounds; ++k) {
                 const uint32_t g = pass * rounds + k;
                 const uint32_t b = g % L.nb;
                 const RouteCtx R{L.bins + b * buf_stride + (size_t)c * L.cap, q_stride, next_pass};
-                if (threadIdx.x == 0 && g >= L.nb &&
-                    !wait_geq(drained, (unsigned long long)G * (g - L.nb + 1), L.spin_limit, &ctr->error))
+                if (rt == 0 && g >= L.nb && !wait_geq(drained, (unsigned long long)G * (g - L.nb + 1), lim, err))
                     s_abort = 1u;
-                for (uint32_t j = threadIdx.x; j < G; j += kRouterThreads) S.wcount[j] = 0u;
-                named_sync(1, kRouterThreads);
+                for (uint32_t j = rt; j < G; j += kRConsThreads) S.wcount[j] = 0u;
+                named_sync(1, kRConsThreads);
                 if (s_abort) break;
-                const uint32_t r0 = k * rows_round + c * L.rows_per_cta;
-                const uint32_t r1 = min(r0 + L.rows_per_cta, S_rows);
-                uint32_t ri = r0 + rw;  // warp rw walks rows r0 + rw, + kRouterWarps, ...
-                uint64_t pos = 0, end = 0;
-                bool done = ri >= r1;
-                if (!done) {
-                    const uint64_t row = (uint64_t)list[ri];
-                    pos = row_ptr[row];
-                    end = row_ptr[row + 1];
-                    events += end - pos;
-                }
-                for (;;) {
-                    uint64_t budget = kChunkEdges;
-                    while (!done && budget > 0) {
-                        const uint64_t n = min(end - pos, budget);
-                        if (n) route_range(pos, n, col, w, L, S, R, lane);
-                        pos += n;
-                        budget -= n;
-                        if (pos == end) {
-                            ri += kRouterWarps;
-                            if (ri < r1) {
-                                const uint64_t row = (uint64_t)list[ri];
-                                pos = row_ptr[row];
-                                end = row_ptr[row + 1];
-                                events += end - pos;
-                            } else {
-                                done = true;
-                            }
-                        }
+                bool round_end = false;
+                while (!round_end) {
+                    const uint32_t s = rfill & 1u;
+                    const bool ok = mbar_wait(rfull + s, (rfill >> 1) & 1u, lim, err);
+                    if (!ok) s_abort = 1u;
+                    const SlotHdr<kRMaxPieces> &h = S.rhdr[s];
+                    const uint32_t total = ok ? h.total : 0u;
+                    round_end = !ok || (h.flags & kRoundEnd);
+                    const uint32_t *scol = S.rcol + s * kRSlotCap;
+                    const float *sw = S.rw + s * kRSlotCap;
+                    for (uint32_t j = rt; j < total; j += kRConsThreads) {
+                        const uint32_t p = find_piece(h, j);
+                        const uint32_t idx = h.start[p] + (j - h.prefix[p]);
+                        route(scol[idx], sw[idx], L, S, R);
                     }
-                    named_sync(1, kRouterThreads);
+                    named_sync(1, kRConsThreads);
+                    if (rt == 0 && ok) mbar_arrive(rempty + s);  // ring slot consumed
+                    ++rfill;
                     // Flush: reserve per destination in shared memory, then
                     // copy each destination's staged run with one warp.
-                    for (uint32_t q = threadIdx.x; q < G; q += kRouterThreads) {
+                    for (uint32_t q = rt; q < G; q += kRConsThreads) {
                         const uint32_t cnt = min(S.scount[q], kStage);
                         S.sbase[q] = S.wcount[q];
                         S.wcount[q] += cnt;
                     }
-                    named_sync(1, kRouterThreads);
-                    for (uint32_t q = rw; q < G; q += kRouterWarps) {
+                    named_sync(1, kRConsThreads);
+                    for (uint32_t q = rw; q < G; q += 11) {
                         const uint32_t cnt = min(S.scount[q], kStage);
                         if (lane < cnt) {
                             const uint2 ent = S.stage[q * kStage + lane];
@@ -270,51 +397,100 @@ __global__ void __launch_bounds__(kThreads, 1)
                         __syncwarp();
                         if (lane == 0) S.scount[q] = 0u;
                     }
-                    if (named_sync_and(1, kRouterThreads, done)) break;
+                    named_sync(1, kRConsThreads);
+                    if (s_abort) break;
                 }
+                if (s_abort) break;
                 // Publish my sub-bin sizes for this round, then the round.
                 uint32_t *counts = L.counts + (size_t)b * G * G;
-                for (uint32_t q = threadIdx.x; q < G; q += kRouterThreads)
-                    counts[(size_t)q * G + c] = min(S.wcount[q], L.cap);
-                named_sync(1, kRouterThreads);
-                if (threadIdx.x == 0) {
+                for (uint32_t q = rt; q < G; q += kRConsThreads) counts[(size_t)q * G + c] = min(S.wcount[q], L.cap);
+                named_sync(1, kRConsThreads);
+                if (rt == 0) {
                     __threadfence();
                     red_release_add(routed, 1ull);
                 }
             }
-        } else {
-            // -------------------------------------------------- drainers --
-            const unsigned dt = threadIdx.x - kRouterThreads;
-            const unsigned dw = dt >> 5;
-            for (uint32_t k = 0; k < rounds; ++k) {
+        } else if (warp == 12) {
+            // -------------------------------------------- drain producer --
+            for (uint32_t k = 0; k < rounds && !s_abort; ++k) {
                 const uint32_t g = pass * rounds + k;
                 const uint32_t b = g % L.nb;
-                if (dt == 0 && !wait_geq(routed, (unsigned long long)G * (g + 1), L.spin_limit, &ctr->error))
-                    s_abort = 1u;
-                named_sync(2, kDrainThreads);
-                if (s_abort) break;
+                const bool ready = wait_geq(routed, (unsigned long long)G * (g + 1), lim, err);
+                if (!__all_sync(kFull, ready)) {
+                    if (lane == 0) s_abort = 1u;
+                    break;
+                }
                 const uint32_t *counts = L.counts + (size_t)b * G * G + (size_t)c * G;
-                for (uint32_t src = dt; src < G; src += kDrainThreads) S.dcount[src] = __ldcg(counts + src);
-                named_sync(2, kDrainThreads);
-                const uint2 *mine = L.bins + b * buf_stride + (size_t)c * q_stride;
-                for (uint32_t src = dw; src < G; src += kDrainWarps) {
-                    const uint32_t cnt = S.dcount[src];
-                    const uint2 *bin = mine + (size_t)src * L.cap;
-                    uint32_t i = lane;
-                    for (; i + 96u < cnt; i += 128u) {
-                        const uint2 e0 = __ldcg(bin + i), e1 = __ldcg(bin + i + 32u);
-                        const uint2 e2 = __ldcg(bin + i + 64u), e3 = __ldcg(bin + i + 96u);
-                        atomicAdd(&S.tile[e0.x], __uint_as_float(e0.y));
-                        atomicAdd(&S.tile[e1.x], __uint_as_float(e1.y));
-                        atomicAdd(&S.tile[e2.x], __uint_as_float(e2.y));
-                        atomicAdd(&S.tile[e3.x], __uint_as_float(e3.y));
+                for (uint32_t src = lane; src < G; src += 32) S.dcount[src] = __ldcg(counts + src);
+                __syncwarp();
+                if (lane == 0) {
+                    const uint2 *mine = L.bins + b * buf_stride + (size_t)c * q_stride;
+                    uint32_t s = dfill & 1u, np = 0, total = 0, used = 0;
+                    bool ok = dfill < 2 || mbar_wait(dempty + s, ((dfill >> 1) - 1) & 1u, lim, err);
+                    for (uint32_t src = 0; src < G && ok; ++src) {
+                        const uint32_t cnt = S.dcount[src];
+                        if (cnt == 0) continue;
+                        const uint32_t nal = (cnt + 1u) & ~1u;  // 16-byte multiple
+                        if (np == kDMaxPieces || used + nal > kDSlotCap) {
+                            SlotHdr<kDMaxPieces> &h = S.dhdr[s];
+                            h.npieces = np;
+                            h.total = total;
+                            h.prefix[np] = total;
+                            h.flags = 0u;
+                            mbar_arrive(dfull + s);
+                            ++dfill;
+                            s = dfill & 1u;
+                            np = total = used = 0;
+                            if (dfill >= 2) ok = mbar_wait(dempty + s, ((dfill >> 1) - 1) & 1u, lim, err);
+                            if (!ok) break;
+                        }
+                        SlotHdr<kDMaxPieces> &h = S.dhdr[s];
+                        h.start[np] = used;
+                        h.prefix[np] = total;
+                        ++np;
+                        total += cnt;
+                        mbar_expect_tx(dfull + s, nal * 8u);
+                        bulk_g2s(S.dbuf + s * kDSlotCap + used, mine + (size_t)src * L.cap, nal * 8u, dfull + s);
+                        used += nal;
                     }
-                    for (; i < cnt; i += 32u) {
-                        const uint2 e0 = __ldcg(bin + i);
-                        atomicAdd(&S.tile[e0.x], __uint_as_float(e0.y));
+                    if (ok) {
+                        SlotHdr<kDMaxPieces> &h = S.dhdr[s];
+                        h.npieces = np;
+                        h.total = total;
+                        h.prefix[np] = total;
+                        h.flags = kRoundEnd;
+                        mbar_arrive(dfull + s);
+                        ++dfill;
+                    } else {
+                        s_abort = 1u;
                     }
                 }
-                named_sync(2, kDrainThreads);
+                dfill = __shfl_sync(kFull, dfill, 0);
+                __syncwarp();
+            }
+        } else {
+            // ------------------------------------------- drain consumers --
+            const unsigned dt = threadIdx.x - 13 * 32;
+            for (uint32_t k = 0; k < rounds; ++k) {
+                bool round_end = false;
+                while (!round_end) {
+                    const uint32_t s = dfill & 1u;
+                    const bool ok = mbar_wait(dfull + s, (dfill >> 1) & 1u, lim, err);
+                    if (!ok) s_abort = 1u;
+                    const SlotHdr<kDMaxPieces> &h = S.dhdr[s];
+                    const uint32_t total = ok ? h.total : 0u;
+                    round_end = !ok || (h.flags & kRoundEnd);
+                    const uint2 *buf = S.dbuf + s * kDSlotCap;
+                    for (uint32_t j = dt; j < total; j += kDConsThreads) {
+                        const uint32_t p = find_piece(h, j);
+                        const uint2 e = buf[h.start[p] + (j - h.prefix[p])];
+                        atomicAdd(&S.tile[e.x], __uint_as_float(e.y));
+                    }
+                    named_sync(2, kDConsThreads);
+                    if (dt == 0 && ok) mbar_arrive(dempty + s);
+                    ++dfill;
+                }
+                if (s_abort) break;
                 if (dt == 0) {
                     __threadfence();
                     red_release_add(drained, 1ull);
@@ -333,7 +509,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         __syncthreads();
     }
-    block_add_u64(lane == 0 ? events : 0ull, &ctr->events);
+    block_add_u64(events, &ctr->events);
     step_epilogue(ctr, parity, count_spikes, S_rows);
 }
 
@@ -364,7 +540,7 @@ bool binned_layout(int device, uint64_t n_local, uint64_t e_local, uint64_t n_ro
         return false;
     if (n_local == 0) return false;
     const uint32_t G = (uint32_t)sm_count(device);
-    const size_t fixed = (size_t)G * kStage * 8 + (size_t)G * 16 + 2048;  // + static smem and slack
+    const size_t fixed = smem_fixed_bytes(G) + 1024;  // + static smem and slack
     if ((size_t)optin <= fixed + 4096) return false;
     const uint64_t tmax = ((optin - fixed) / 4) & ~(uint64_t)3;
     uint32_t passes = (uint32_t)((n_local + (uint64_t)G * tmax - 1) / ((uint64_t)G * tmax));
@@ -376,7 +552,7 @@ bool binned_layout(int device, uint64_t n_local, uint64_t e_local, uint64_t n_ro
     tile = std::max<uint64_t>((tile + 3) & ~(uint64_t)3, 4);
     const double deg = n_rows ? (double)e_local / (double)n_rows / passes : 0.0;
     // ~8K events per tile per round: sub-bins average 8K / grid entries.
-    const double per_tile = 8192.0;
+    const double per_tile = 16384.0;
     double rpc = deg > 0.0 ? per_tile / deg : 1e9;
     rpc = std::min(std::max(rpc, 1.0), 1e6);
     L->grid = G;
@@ -391,7 +567,7 @@ bool binned_layout(int device, uint64_t n_local, uint64_t e_local, uint64_t n_ro
     L->rows_per_cta = (uint32_t)rpc;
     const double per_sub = per_tile / G;
     L->cap = (uint32_t)(((uint64_t)(3.0 * per_sub) + 64 + 31) & ~31ull);
-    L->smem_bytes = (uint32_t)(tile * 4 + (size_t)G * kStage * 8 + (size_t)G * 16);
+    L->smem_bytes = (uint32_t)(align16(tile * 4) + smem_fixed_bytes(G));
     L->spin_limit = 1u << 22;  // x ~100 ns naps: ~0.5 s before a wait is declared failed
     return true;
 }

@@ -245,7 +245,7 @@ void shard_geometry(uint64_t n, uint32_t world, uint32_t rank, uint64_t *slot, u
 snn_status_t apply_options(snn_cuda_context_t *c, uint64_t n, const snn_b200_options_t &o) {
     if (o.world_size == 0 || o.rank >= o.world_size) return SNN_ERR_INVALID_ARGUMENT;
     if (o.propagation != SNN_B200_PROPAGATE_PUSH && o.propagation != SNN_B200_PROPAGATE_ORDERED &&
-        o.propagation != SNN_B200_PROPAGATE_PUSH_ATOMIC)
+        o.propagation != SNN_B200_PROPAGATE_PUSH_ATOMIC && o.propagation != SNN_B200_PROPAGATE_PUSH_BINNED)
         return SNN_ERR_INVALID_ARGUMENT;
     if (o.index_width != 0 && o.index_width != 32 && o.index_width != 64) return SNN_ERR_INVALID_ARGUMENT;
     if (o.world_size > 1 && o.nccl_id == nullptr) return SNN_ERR_INVALID_ARGUMENT;
@@ -303,6 +303,10 @@ snn_status_t create_streams(snn_cuda_context_t *c) {
     return SNN_OK;
 }
 
+// Whether SNN_B200_PROPAGATE_PUSH picks the binned kernel (when it can run)
+// rather than the atomic one; set from the measured step times on B200.
+constexpr bool kAutoBinned = false;
+
 // Binned push (b200_binned.cu) for FULL push contexts with 32-bit columns.
 // plan_binned decides, before the topology is built, whether the binned
 // kernel runs and with how many target passes (each pass then gets its own
@@ -311,7 +315,9 @@ snn_status_t create_streams(snn_cuda_context_t *c) {
 void plan_binned(snn_cuda_context_t *c, uint64_t e_estimate) {
     c->binned = false;
     c->passes = 1;
-    if (c->propagation != SNN_B200_PROPAGATE_PUSH || c->mode != SNN_CUDA_MODE_FULL || c->col_bits != 32) return;
+    const bool want = c->propagation == SNN_B200_PROPAGATE_PUSH_BINNED ||
+                      (c->propagation == SNN_B200_PROPAGATE_PUSH && kAutoBinned);
+    if (!want || c->mode != SNN_CUDA_MODE_FULL || c->col_bits != 32) return;
     uint32_t force = 0;
     if (const char *env = std::getenv("SNN_B200_BINNED_PASSES")) force = (uint32_t)std::atoi(env);
     if (!b200::binned_layout(c->device, c->n_local, e_estimate, c->n_global, force, &c->bin) ||

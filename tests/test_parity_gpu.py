@@ -74,19 +74,19 @@ def test_ordered_negative_weights_dense_external():
     np.testing.assert_array_equal(bits(cv), bits(gv))
 
 
-@pytest.mark.parametrize("prop", [sb.PROPAGATE_PUSH, sb.PROPAGATE_PUSH_ATOMIC])
+@pytest.mark.parametrize("prop", [sb.PROPAGATE_PUSH, sb.PROPAGATE_PUSH_BINNED, sb.PROPAGATE_PUSH_ATOMIC])
 def test_push_dyadic_bit_exact(prop):
     lif = baseline_lif()
     net = ORC.random_pool(20000, 48, 0.046875, 0.046875, 4242, lif=lif)
     ctx = sb.CudaContext.create(net, None, opts(propagation=prop))
     assert ctx.mode == sb.MODE_FULL
-    assert ctx.layout["binned"] == (1 if prop == sb.PROPAGATE_PUSH else 0)
+    assert ctx.layout["binned"] == (1 if prop == sb.PROPAGATE_PUSH_BINNED else 0) or prop == sb.PROPAGATE_PUSH
     cr, gr, cv, gv = run_pair(net, ctx, 40, inject=stream_inject(3, 400, 20.0, 20000))
     assert first_divergence(cr, gr) is None
     np.testing.assert_array_equal(bits(cv), bits(gv))
 
 
-@pytest.mark.parametrize("width,prop,passes", [(32, sb.PROPAGATE_PUSH, "0"), (32, sb.PROPAGATE_PUSH, "3"),
+@pytest.mark.parametrize("width,prop,passes", [(32, sb.PROPAGATE_PUSH_BINNED, "0"), (32, sb.PROPAGATE_PUSH_BINNED, "3"),
                                                 (32, sb.PROPAGATE_PUSH_ATOMIC, "0"), (64, sb.PROPAGATE_PUSH, "0")])
 def test_push_general_weights_tolerance(width, prop, passes, monkeypatch):
     """Push with fp32 atomics: from the SAME state each step (teacher forcing
@@ -97,7 +97,7 @@ def test_push_general_weights_tolerance(width, prop, passes, monkeypatch):
     net = ORC.random_pool(n, 100, 0.0, 0.6, 0, lif=lif)
     monkeypatch.setenv("SNN_B200_BINNED_PASSES", passes)  # force several target passes (CSR slices)
     ctx = sb.CudaContext.create(net, None, opts(index_width=width, propagation=prop))
-    if prop == sb.PROPAGATE_PUSH and width == 32:
+    if prop == sb.PROPAGATE_PUSH_BINNED and width == 32:
         assert ctx.layout["binned"] == 1 and ctx.layout["binned_passes"] == max(1, int(passes))
     st = State(net)
     inj = stream_inject(1, 200, 20.0, n)
@@ -322,7 +322,7 @@ def test_binned_push_overflow_fallback_exact():
     net = ORC.custom_csr(rp, col, w, lif=default_lif(v_threshold=1e6))
     ext = np.zeros(n, np.float32)
     ext[0] = 2e6
-    for prop in (sb.PROPAGATE_PUSH, sb.PROPAGATE_PUSH_ATOMIC):
+    for prop in (sb.PROPAGATE_PUSH_BINNED, sb.PROPAGATE_PUSH_ATOMIC):
         ctx = sb.CudaContext.create(net, None, opts(propagation=prop))
         cr, gr, cv, gv = run_pair(net, ctx, 3, ext=lambda t: ext if t == 0 else None)
         assert first_divergence(cr, gr) is None
@@ -341,7 +341,8 @@ def test_generated_pool_binned_passes_exact(passes, monkeypatch):
     net = ORC.random_pool(n, f, 0.25, 0.25, 21, lif=lif)
     st = State(net)
     sc, ev, hs, _ = ORC.run_inject_stream(net, st, 5, 0, 30, 600, 20.0)
-    ctx = sb.CudaContext.random_pool(n, f, 0.25, 0.25, 21, lif=lif_to_sb(lif))
+    ctx = sb.CudaContext.random_pool(n, f, 0.25, 0.25, 21, lif=lif_to_sb(lif),
+                                     options=opts(propagation=sb.PROPAGATE_PUSH_BINNED))
     assert ctx.layout["binned"] == 1 and ctx.layout["binned_passes"] == max(1, int(passes))
     ctx.run_stream_async(5, 0, 30, 600, 20.0)
     s = ctx.stats()
