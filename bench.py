@@ -115,15 +115,10 @@ def measured_peak_gbs():
         return 6650.0, "fallback"
 
 
-def traffic_per_event():
-    """DRAM bytes per synaptic event of the push kernel from the committed ncu
-    summary (profiles/propagate_push_traffic.json), or None."""
-    try:
-        with open(os.path.join(ROOT, "profiles", "propagate_push_traffic.json")) as f:
-            d = json.load(f)
-        return float(d["dram_bytes_per_event"]), float(d["dram_bytes_per_spike"])
-    except Exception:
-        return None
+# DRAM bytes per synaptic event of propagate_push_kernel (32-bit columns),
+# dram__bytes_read.sum + dram__bytes_write.sum / events of one ncu capture
+# (profiles/propagate_push_config2.md); scaled by this run's events.
+NCU_DRAM_BYTES_PER_EVENT = 8.68
 
 
 # ------------------------------------------------------------ CPU side ----
@@ -286,13 +281,12 @@ def run_b200(args):
     prop_bytes = 12.0 * s["events"] + 16.0 * spikes_total
     prop_s = s["propagate_ms"] / 1e3
     achieved = prop_bytes / prop_s / 1e9 if prop_s > 0 else 0.0
-    tpe = traffic_per_event()
+    lay = ctx.layout
     traffic = None
-    if tpe is not None and s["steps"]:
-        traffic = (tpe[0] * s["events"] + tpe[1] * spikes_total) / s["steps"]
+    if args.propagation != "binned" and int(lay["index_bits"]) == 32 and s["steps"]:
+        traffic = NCU_DRAM_BYTES_PER_EVENT * s["events"] / s["steps"]
     step_bytes = (12.0 * s["events"] + 16.0 * spikes_total + 25.0 * ctx.local_count * s["steps"]
                   + 12.0 * count * s["steps"])
-    lay = ctx.layout
     launches = int(s["kernel_launches"])
 
     e2e = None
