@@ -78,15 +78,22 @@ __device__ bool wait_geq(const unsigned long long *p, unsigned long long target,
 // Warp roles (16 warps, one CTA per SM):
 //   warp 0        router producer: streams spiking-row segments with TMA bulk
 //                 copies (cp.async.bulk) into the router ring;
-//   warps 1-11    router consumers: route the ring's edges into staging and
-//                 flush staging into this CTA's sub-bins;
-//   warp 12       drain producer: streams this CTA's sub-bins of a finished
+//   warps 1-7     router consumers: route the ring's edges into staging (a
+//                 warp per row piece of <= 256 edges) and flush staging into
+//                 this CTA's sub-bins;
+//   warp 8        drain producer: streams this CTA's sub-bins of a finished
 //                 round into the drain ring (cp.async.bulk);
-//   warps 13-15   drain consumers: fold drain-ring entries into the tile.
+//   warps 9-15    drain consumers: fold drain-ring entries into the tile.
+// Sub-bins are padded to an even length with (0, +0.0f) entries, so the drain
+// ring holds whole 16-byte entry pairs with no gaps.
 // Rings are flow-controlled by mbarriers (full: TMA bytes landed; empty:
 // consumers done), so no warp waits on memory latency.
-constexpr int kRConsThreads = 32 * 11;
-constexpr int kDConsThreads = 32 * 3;
+constexpr int kRConsWarps = 7;  // warps 1..7
+constexpr int kDConsWarps = 7;  // warps 9..15
+constexpr int kRConsThreads = 32 * kRConsWarps;
+constexpr int kDConsThreads = 32 * kDConsWarps;
+constexpr int kDProdWarp = 1 + kRConsWarps;
+constexpr uint32_t kPieceEdges = 256;  // longest row piece (one consumer warp routes a piece)
 constexpr uint32_t kRSlots = 2;
 constexpr uint32_t kRSlotEdges = 1536;                         // edges per router slot (one staging flush)
 constexpr uint32_t kRMaxPieces = 32;                           // row segments per router slot
@@ -204,15 +211,12 @@ __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t by
         : "memory");
 }
 
-template <uint32_t MAXP>
-__device__ __forceinline__ uint32_t find_piece(const SlotHdr<MAXP> &h, uint32_t j) {
-    uint32_t lo = 0, hi = h.npieces;  // largest p with prefix[p] <= j
-    while (hi - lo > 1) {
-        const uint32_t mid = (lo + hi) >> 1;
-        if (h.prefix[mid] <= j) lo = mid;
-        else hi = mid;
-    }
-    return lo;
+// Optional per-CTA cycle accounting (BinLayout::prof), for diagnosing where
+// a round's time goes. Slots: 0 rprod wait-empty, 1 rprod total, 2 rcons
+// wait-drained, 3 rcons wait-full, 4 rcons route, 5 rcons flush, 6 dprod
+// wait-routed, 7 dprod issue, 8 dcons wait-full, 9 dcons fold, 10 kernel.
+__device__ __forceinline__ void prof_add(const BinLayout &L, int slot, long long dt) {
+    if (L.prof) atomicAdd(L.prof + blockIdx.x * 16 + slot, (unsigned long long)dt);
 }
 
 struct RouteCtx {
@@ -269,7 +273,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (uint32_t j = threadIdx.x; j < G; j += kThreads) S.scount[j] = 0u;
     unsigned long long events = 0;
-    uint32_t rfill = 0, dfill = 0;  // ring fills so far (slot = fill % 2, use = fill / 2)
+    uint32_t rfill = 0, dfill = 0;
+    const long long t_kernel = clock64();  // ring fills so far (slot = fill % 2, use = fill / 2)
 
     for (uint32_t pass = 0; pass < L.passes; ++pass) {
         const uint64_t *__restrict__ row_ptr = L.row_ptr[pass];
@@ -280,6 +285,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         __syncthreads();
         if (warp == 0) {
             // ------------------------------------------- router producer --
+            const long long t_rp = clock64();
             for (uint32_t k = 0; k < rounds && !s_abort; ++k) {
                 const uint32_t r0 = k * rows_round + c * L.rows_per_cta;
                 const uint32_t r1 = min(r0 + L.rows_per_cta, S_rows);
@@ -310,10 +316,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                                     ++rfill;
                                     s = rfill & 1u;
                                     np = total = used = 0;
+                                    const long long tw = clock64();
                                     if (rfill >= 2) ok = mbar_wait(rempty + s, ((rfill >> 1) - 1) & 1u, lim, err);
+                                    prof_add(L, 0, clock64() - tw);
                                     if (!ok) break;
                                 }
-                                const uint64_t take = min(ej - pos, (uint64_t)(kRSlotEdges - total));
+                                const uint64_t take =
+                                    min(min(ej - pos, (uint64_t)(kRSlotEdges - total)), (uint64_t)kPieceEdges);
                                 const uint64_t ab = pos & ~(uint64_t)3;
                                 const uint64_t ae = (pos + take + 3) & ~(uint64_t)3;
                                 const uint32_t nal = (uint32_t)(ae - ab);
@@ -347,7 +356,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 if (!__shfl_sync(kFull, ok, 0)) break;
             }
-        } else if (warp <= 11) {
+            if (lane == 0) prof_add(L, 1, clock64() - t_rp);
+        } else if (warp <= (unsigned)kRConsWarps) {
             // ------------------------------------------ router consumers --
             const unsigned rt = threadIdx.x - 32;
             const unsigned rw = warp - 1;
@@ -355,27 +365,36 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const uint32_t g = pass * rounds + k;
                 const uint32_t b = g % L.nb;
                 const RouteCtx R{L.bins + b * buf_stride + (size_t)c * L.cap, q_stride, next_pass};
+                const long long t_wd = clock64();
                 if (rt == 0 && g >= L.nb && !wait_geq(drained, (unsigned long long)G * (g - L.nb + 1), lim, err))
                     s_abort = 1u;
+                if (rt == 0) prof_add(L, 2, clock64() - t_wd);
                 for (uint32_t j = rt; j < G; j += kRConsThreads) S.wcount[j] = 0u;
                 named_sync(1, kRConsThreads);
                 if (s_abort) break;
                 bool round_end = false;
                 while (!round_end) {
                     const uint32_t s = rfill & 1u;
+                    const long long t_wf = clock64();
                     const bool ok = mbar_wait(rfull + s, (rfill >> 1) & 1u, lim, err);
+                    const long long t_rt = clock64();
+                    if (rt == 0) prof_add(L, 3, t_rt - t_wf);
                     if (!ok) s_abort = 1u;
                     const SlotHdr<kRMaxPieces> &h = S.rhdr[s];
                     const uint32_t total = ok ? h.total : 0u;
                     round_end = !ok || (h.flags & kRoundEnd);
                     const uint32_t *scol = S.rcol + s * kRSlotCap;
                     const float *sw = S.rw + s * kRSlotCap;
-                    for (uint32_t j = rt; j < total; j += kRConsThreads) {
-                        const uint32_t p = find_piece(h, j);
-                        const uint32_t idx = h.start[p] + (j - h.prefix[p]);
-                        route(scol[idx], sw[idx], L, S, R);
+                    const uint32_t np = ok ? h.npieces : 0u;
+                    for (uint32_t p = rw; p < np; p += kRConsWarps) {
+                        const uint32_t n = h.prefix[p + 1] - h.prefix[p];
+                        const uint32_t base = h.start[p];
+                        for (uint32_t j = lane; j < n; j += 32) route(scol[base + j], sw[base + j], L, S, R);
                     }
+                    (void)total;
                     named_sync(1, kRConsThreads);
+                    const long long t_fl = clock64();
+                    if (rt == 0) prof_add(L, 4, t_fl - t_rt);
                     if (rt == 0 && ok) mbar_arrive(rempty + s);  // ring slot consumed
                     ++rfill;
                     // Flush: reserve per destination in shared memory, then
@@ -386,36 +405,46 @@ __global__ void __launch_bounds__(kThreads, 1)
                         S.wcount[q] += cnt;
                     }
                     named_sync(1, kRConsThreads);
-                    for (uint32_t q = rw; q < G; q += 11) {
-                        const uint32_t cnt = min(S.scount[q], kStage);
-                        if (lane < cnt) {
-                            const uint2 ent = S.stage[q * kStage + lane];
-                            const uint32_t p = S.sbase[q] + lane;
+                    // Copy: one thread per staging slot (destination-major), so a
+                    // destination's run is stored by consecutive threads.
+                    for (uint32_t i = rt; i < G * kStage; i += kRConsThreads) {
+                        const uint32_t q = i / kStage, k = i - q * kStage;
+                        if (k < min(S.scount[q], kStage)) {
+                            const uint2 ent = S.stage[i];
+                            const uint32_t p = S.sbase[q] + k;
                             if (p < L.cap) R.sub[q * q_stride + p] = ent;
                             else red_add(next_pass + (size_t)q * L.tile + ent.x, __uint_as_float(ent.y));
                         }
-                        __syncwarp();
-                        if (lane == 0) S.scount[q] = 0u;
                     }
                     named_sync(1, kRConsThreads);
+                    for (uint32_t q = rt; q < G; q += kRConsThreads) S.scount[q] = 0u;
+                    named_sync(1, kRConsThreads);
+                    if (rt == 0) prof_add(L, 5, clock64() - t_fl);
                     if (s_abort) break;
                 }
                 if (s_abort) break;
                 // Publish my sub-bin sizes for this round, then the round.
                 uint32_t *counts = L.counts + (size_t)b * G * G;
-                for (uint32_t q = rt; q < G; q += kRConsThreads) counts[(size_t)q * G + c] = min(S.wcount[q], L.cap);
+                for (uint32_t q = rt; q < G; q += kRConsThreads) {
+                    uint32_t cnt = min(S.wcount[q], L.cap);
+                    if (cnt & 1u) R.sub[q * q_stride + cnt++] = make_uint2(0u, 0u);  // pad: adds +0.0f to entry 0
+                    counts[(size_t)q * G + c] = cnt;
+                }
                 named_sync(1, kRConsThreads);
                 if (rt == 0) {
                     __threadfence();
                     red_release_add(routed, 1ull);
                 }
             }
-        } else if (warp == 12) {
+        } else if (warp == (unsigned)kDProdWarp) {
             // -------------------------------------------- drain producer --
             for (uint32_t k = 0; k < rounds && !s_abort; ++k) {
                 const uint32_t g = pass * rounds + k;
                 const uint32_t b = g % L.nb;
+                const long long t_wr = clock64();
                 const bool ready = wait_geq(routed, (unsigned long long)G * (g + 1), lim, err);
+                if (lane == 0) prof_add(L, 6, clock64() - t_wr);
+                const long long t_is = clock64();
                 if (!__all_sync(kFull, ready)) {
                     if (lane == 0) s_abort = 1u;
                     break;
@@ -430,7 +459,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     for (uint32_t src = 0; src < G && ok; ++src) {
                         const uint32_t cnt = S.dcount[src];
                         if (cnt == 0) continue;
-                        const uint32_t nal = (cnt + 1u) & ~1u;  // 16-byte multiple
+                        const uint32_t nal = cnt;  // even: sub-bins are padded to entry pairs
                         if (np == kDMaxPieces || used + nal > kDSlotCap) {
                             SlotHdr<kDMaxPieces> &h = S.dhdr[s];
                             h.npieces = np;
@@ -467,26 +496,32 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 dfill = __shfl_sync(kFull, dfill, 0);
                 __syncwarp();
+                if (lane == 0) prof_add(L, 7, clock64() - t_is);
             }
         } else {
             // ------------------------------------------- drain consumers --
-            const unsigned dt = threadIdx.x - 13 * 32;
+            const unsigned dt = threadIdx.x - (kDProdWarp + 1) * 32;
             for (uint32_t k = 0; k < rounds; ++k) {
                 bool round_end = false;
                 while (!round_end) {
                     const uint32_t s = dfill & 1u;
+                    const long long t_df = clock64();
                     const bool ok = mbar_wait(dfull + s, (dfill >> 1) & 1u, lim, err);
+                    const long long t_fo = clock64();
+                    if (dt == 0) prof_add(L, 8, t_fo - t_df);
                     if (!ok) s_abort = 1u;
                     const SlotHdr<kDMaxPieces> &h = S.dhdr[s];
                     const uint32_t total = ok ? h.total : 0u;
                     round_end = !ok || (h.flags & kRoundEnd);
-                    const uint2 *buf = S.dbuf + s * kDSlotCap;
-                    for (uint32_t j = dt; j < total; j += kDConsThreads) {
-                        const uint32_t p = find_piece(h, j);
-                        const uint2 e = buf[h.start[p] + (j - h.prefix[p])];
+                    // Dense entry pairs: one 16-byte load per thread and pair.
+                    const uint4 *buf = reinterpret_cast<const uint4 *>(S.dbuf + s * kDSlotCap);
+                    for (uint32_t j = dt; 2 * j < total; j += kDConsThreads) {
+                        const uint4 e = buf[j];
                         atomicAdd(&S.tile[e.x], __uint_as_float(e.y));
+                        atomicAdd(&S.tile[e.z], __uint_as_float(e.w));
                     }
                     named_sync(2, kDConsThreads);
+                    if (dt == 0) prof_add(L, 9, clock64() - t_fo);
                     if (dt == 0 && ok) mbar_arrive(dempty + s);
                     ++dfill;
                 }
@@ -509,6 +544,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         __syncthreads();
     }
+    if (threadIdx.x == 0) prof_add(L, 10, clock64() - t_kernel);
     block_add_u64(events, &ctr->events);
     step_epilogue(ctr, parity, count_spikes, S_rows);
 }

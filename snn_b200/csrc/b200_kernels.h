@@ -66,6 +66,7 @@ struct BinLayout {
     uint32_t cap;             // capacity of one sub-bin; overflow falls back to red.global
     uint32_t smem_bytes;      // dynamic shared memory per CTA
     uint32_t spin_limit;      // polls before a cross-CTA wait is declared failed
+    unsigned long long *prof; // optional [grid][16] clock64 totals per role/section (diagnostics)
 };
 
 // Fills the geometry for n_local targets (buffers and CSR pointers left

@@ -198,11 +198,34 @@ bool lif_valid(const snn_lif_params_t *p) {
            p->dt_ms > 0.0f && p->membrane_tau_ms > 0.0f && p->v_threshold > p->v_reset;
 }
 
+// SNN_B200_BINNED_PROFILE: print the binned kernel's per-role cycle totals
+// (summed over CTAs, in ms at the current SM clock) when a context is freed.
+void report_binned_profile(snn_cuda_context_t *c) {
+    if (!c->bin.prof) return;
+    std::vector<unsigned long long> h((size_t)c->bin.grid * 16);
+    cudaStreamSynchronize(c->stream);
+    if (cudaMemcpy(h.data(), c->bin.prof, h.size() * 8, cudaMemcpyDeviceToHost) != cudaSuccess) return;
+    int khz = 0;
+    cudaDeviceGetAttribute(&khz, cudaDevAttrClockRate, c->device);
+    const char *names[11] = {"rprod_wait_empty", "rprod_total", "rcons_wait_drained", "rcons_wait_full",
+                             "rcons_route", "rcons_flush", "dprod_wait_routed", "dprod_issue",
+                             "dcons_wait_full", "dcons_fold", "kernel"};
+    std::fprintf(stderr, "[snn_b200 binned profile] mean per CTA over %llu steps (ms):", (unsigned long long)c->step);
+    for (int k = 0; k < 11; ++k) {
+        double sum = 0;
+        for (uint32_t b = 0; b < c->bin.grid; ++b) sum += (double)h[(size_t)b * 16 + k];
+        std::fprintf(stderr, " %s=%.3f", names[k], khz ? sum / c->bin.grid / khz : 0.0);
+    }
+    std::fprintf(stderr, "\n");
+    cudaFree(c->bin.prof);
+}
+
 void free_context(snn_cuda_context_t *c) {
     if (c == nullptr) return;
     if (c->device >= 0) cudaSetDevice(c->device);
     if (c->stream) cudaStreamSynchronize(c->stream);
     if (c->copy_stream) cudaStreamSynchronize(c->copy_stream);
+    report_binned_profile(c);
     if (c->comm) ncclCommDestroy(c->comm);
     void *dev[] = {c->d_v, c->d_cur_pair, c->d_ext, c->d_refr, c->d_spikes, c->d_ws, c->d_row_ptr, c->d_col,
                    c->d_w, c->d_col_ptr, c->d_pre, c->d_cw, c->d_deg, c->d_chunk_row, c->d_chunk_col,
@@ -344,6 +367,10 @@ snn_status_t finish_binned(snn_cuda_context_t *c) {
     L.counts = (uint32_t *)((char *)c->d_bin_mem + 256);
     L.bins = (uint2 *)((char *)c->d_bin_mem + 256 + counts_bytes);
     if ((st = cuda_status(cudaMemsetAsync(c->d_bin_mem, 0, 256 + counts_bytes, c->stream))) != SNN_OK) return st;
+    if (std::getenv("SNN_B200_BINNED_PROFILE")) {
+        if (cudaMalloc(&L.prof, (size_t)L.grid * 16 * 8) != cudaSuccess) return SNN_ERR_CUDA;
+        cudaMemsetAsync(L.prof, 0, (size_t)L.grid * 16 * 8, c->stream);
+    }
     return cuda_status(cudaStreamSynchronize(c->stream));
 }
 
