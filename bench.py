@@ -53,6 +53,8 @@ def parse():
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--exchange", choices=["nccl", "peer"], default="peer",
+                    help="N>1: spike exchange by ncclAllGather or fused into the LIF kernel over NVLink")
     ap.add_argument("--propagation", choices=["auto", "binned", "atomic"], default="auto",
                     help="push kernel: auto (library default), binned (shared-memory tiles), atomic (L2 red)")
     return ap.parse_args()
@@ -187,7 +189,7 @@ def workload_config(args, world):
             "synapses": args.neurons * args.fanout, "weights": "U[-0.2,0.5] mV", "seed": args.seed,
             "inject": f"{args.inject_frac * 100:g}% of neurons x {args.inject_value:g} per step",
             "lif": "dt 1 ms, tau 20 ms, rest=reset -65 mV, thr -50 mV, refractory 2", "policy": "FULL",
-            "propagation": f"push ({args.propagation})", "parallelism": f"postsynaptic shards x{world}", "l2": L2_NOTE}
+            "propagation": f"push ({args.propagation})", "parallelism": f"postsynaptic shards x{world}" + (f", {args.exchange} spike exchange" if world > 1 else ""), "l2": L2_NOTE}
 
 
 # ------------------------------------------------------------ GPU side ----
@@ -216,14 +218,15 @@ def run_b200(args):
         import torch.distributed as dist
         dist.init_process_group("nccl", device_id=torch.device("cuda", local))
     nccl_id = None
-    if world > 1:
+    if world > 1 and args.exchange == "nccl":
         obj = [sb.nccl_unique_id() if rank == 0 else None]
         dist.broadcast_object_list(obj, src=0)
         nccl_id = obj[0]
     id_buf = None
     prop = {"auto": sb.PROPAGATE_PUSH, "binned": sb.PROPAGATE_PUSH_BINNED, "atomic": sb.PROPAGATE_PUSH_ATOMIC}
     opts = sb.default_options(device=local, world_size=world, rank=rank, timing=1,
-                              propagation=prop[args.propagation])
+                              propagation=prop[args.propagation],
+                              exchange=sb.EXCHANGE_PEER if args.exchange == "peer" else sb.EXCHANGE_NCCL)
     if nccl_id is not None:
         import ctypes
         id_buf = ctypes.create_string_buffer(nccl_id, 128)
@@ -234,6 +237,10 @@ def run_b200(args):
     t0 = time.time()
     ctx = sb.CudaContext.random_pool(n, f, -0.2, 0.5, args.seed, lif=lif, options=opts)
     gen_s = time.time() - t0
+    if world > 1 and args.exchange == "peer":
+        handles = [None] * world
+        dist.all_gather_object(handles, ctx.ipc_handle())
+        ctx.ipc_connect(handles)
 
     def barrier():
         if dist is not None:

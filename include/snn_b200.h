@@ -153,6 +153,16 @@ typedef enum snn_b200_propagation {
     SNN_B200_PROPAGATE_PUSH_BINNED = 3
 } snn_b200_propagation_t;
 
+typedef enum snn_b200_exchange {
+    /* ncclAllGather of the spike bitmap after the LIF kernel (needs nccl_id). */
+    SNN_B200_EXCHANGE_NCCL = 0,
+    /* The LIF kernel itself stores its bitmap words into every rank's buffer
+     * over NVLink (CUDA IPC mappings, one node) and raises a per-step flag
+     * that the other ranks wait on (bounded) before compacting. Needs
+     * snn_b200_ipc_handle / snn_b200_ipc_connect after create; <= 8 ranks. */
+    SNN_B200_EXCHANGE_PEER = 1
+} snn_b200_exchange_t;
+
 typedef struct snn_b200_options {
     int propagation;        /* snn_b200_propagation_t */
     int device;             /* CUDA device ordinal; -1 = the calling thread's current device */
@@ -161,6 +171,7 @@ typedef struct snn_b200_options {
     uint32_t world_size;    /* number of postsynaptic shards (1 = unsharded) */
     const void *nccl_id;    /* 128-byte NCCL unique id (snn_b200_nccl_unique_id), world_size > 1 */
     int timing;             /* 1: record per-step device timings (snn_b200_stats) */
+    int exchange;           /* snn_b200_exchange_t: how sharded ranks share spikes */
 } snn_b200_options_t;
 
 typedef struct snn_b200_stats {
@@ -224,6 +235,12 @@ const char *snn_b200_last_error(void);
  * slots of S = ceil(n / world_size / 32) * 32 neurons. */
 snn_status_t snn_b200_shard_range(snn_size_t neuron_count, uint32_t world_size, uint32_t rank,
                                   snn_size_t *out_begin, snn_size_t *out_count);
+
+/* Peer exchange set-up: every rank exports the 64-byte CUDA IPC handle of its
+ * exchange buffer, the caller gathers all ranks' handles in rank order
+ * (world_size * 64 bytes) and hands them to every rank's context. */
+snn_status_t snn_b200_ipc_handle(const snn_cuda_context_t *context, void *out_handle64);
+snn_status_t snn_b200_ipc_connect(snn_cuda_context_t *context, const void *handles);
 
 /* Writes a fresh 128-byte NCCL unique id (rank 0 calls it and shares the bytes). */
 snn_status_t snn_b200_nccl_unique_id(void *out_id128);

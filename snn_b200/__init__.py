@@ -40,6 +40,7 @@ STATUS_NAMES = {0: "ok", -1: "invalid argument", -2: "out of memory", -3: "integ
 MODE_NONE, MODE_FULL, MODE_STREAMING = 0, 1, 2
 NOALLOC_MAX_NEURONS = 1048576  # SNN_B200_NOALLOC_MAX_NEURONS
 PROPAGATE_PUSH, PROPAGATE_ORDERED, PROPAGATE_PUSH_ATOMIC, PROPAGATE_PUSH_BINNED = 0, 1, 2, 3
+EXCHANGE_NCCL, EXCHANGE_PEER = 0, 1
 
 
 class SnnError(RuntimeError):
@@ -77,7 +78,8 @@ class RandomPoolConfig(C.Structure):
 class Options(C.Structure):
     """snn_b200_options_t (include/snn_b200.h)."""
     _fields_ = [("propagation", C.c_int), ("device", C.c_int), ("index_width", C.c_int),
-                ("rank", C.c_uint32), ("world_size", C.c_uint32), ("nccl_id", P), ("timing", C.c_int)]
+                ("rank", C.c_uint32), ("world_size", C.c_uint32), ("nccl_id", P), ("timing", C.c_int),
+                ("exchange", C.c_int)]
 
 
 class Stats(C.Structure):
@@ -118,6 +120,8 @@ ENTRY_POINTS = [
     ("snn_b200_create_random_pool", C.c_int, [P, P, P, P, P]),
     ("snn_b200_create_layered_random", C.c_int, [P, C.c_size_t, u64, f32, f32, u64, P, P, P]),
     ("snn_b200_nccl_unique_id", C.c_int, [P]),
+    ("snn_b200_ipc_handle", C.c_int, [P, P]),
+    ("snn_b200_ipc_connect", C.c_int, [P, P]),
     ("snn_b200_shard_range", C.c_int, [u64, C.c_uint32, C.c_uint32, P, P]),
     ("snn_b200_last_error", C.c_char_p, []),
     ("snn_b200_step_noalloc", C.c_int, [C.c_int, P, u64, P, f32, P, P, P, P, P, P, P, P, P]),
@@ -354,6 +358,16 @@ class CudaContext:
         _check(lib().snn_b200_download_state(self.handle, _ptr(v), _ptr(c), _ptr(r), self.local_count),
                "snn_b200_download_state")
         return v, c, r
+
+    def ipc_handle(self) -> bytes:
+        buf = C.create_string_buffer(64)
+        _check(lib().snn_b200_ipc_handle(self.handle, buf), "snn_b200_ipc_handle")
+        return buf.raw
+
+    def ipc_connect(self, handles: list):
+        """handles: every rank's ipc_handle() bytes, in rank order."""
+        blob = C.create_string_buffer(b"".join(handles), 64 * len(handles))
+        _check(lib().snn_b200_ipc_connect(self.handle, blob), "snn_b200_ipc_connect")
 
     def download_topology(self):
         e = int(self.layout["local_synapses"])

@@ -133,7 +133,8 @@ __global__ void __launch_bounds__(kLifThreads) lif_kernel(uint64_t n, LifArgs p,
                                                           const float *__restrict__ ext,
                                                           uint32_t *__restrict__ refr, uint8_t *__restrict__ spikes,
                                                           uint32_t *__restrict__ bitmap, TIdx *__restrict__ list,
-                                                          uint64_t global_offset, DevCounters *ctr, int parity) {
+                                                          uint64_t global_offset, DevCounters *ctr, int parity,
+                                                          PeerArgs peer) {
     constexpr uint64_t kTile = (uint64_t)ITERS * kLifThreads * 4u;
     __shared__ TIdx sbuf[WRITE_LIST ? kTile : 1];
     __shared__ uint32_t warp_tot[kLifThreads / 32];
@@ -188,7 +189,12 @@ __global__ void __launch_bounds__(kLifThreads) lif_kernel(uint64_t n, LifArgs p,
             word |= __shfl_xor_sync(kFull, word, 1);
             word |= __shfl_xor_sync(kFull, word, 2);
             word |= __shfl_xor_sync(kFull, word, 4);
-            if ((lane & 7u) == 0u && i0 < n) bitmap[i0 >> 5] = word;
+            if ((lane & 7u) == 0u && i0 < n) {
+                bitmap[i0 >> 5] = word;
+                // Fused all-gather: the same word goes to every rank's
+                // exchange buffer over NVLink (plain peer stores).
+                for (uint32_t q = 0; q < peer.npeers; ++q) peer.dst[q][peer.word_offset + (i0 >> 5)] = word;
+            }
             if (WRITE_LIST) {
                 const uint32_t cnt = __popc(nib);
                 uint32_t incl = cnt;
@@ -224,19 +230,57 @@ __global__ void __launch_bounds__(kLifThreads) lif_kernel(uint64_t n, LifArgs p,
             __syncthreads();
         }
     }
+    if (peer.npeers) {
+        // Publish: every CTA's peer stores become visible system-wide before
+        // its ticket; the last CTA then raises this rank's flag everywhere.
+        __threadfence_system();
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            const uint32_t t = atomicAdd(peer.ticket, 1u);
+            if (t == gridDim.x - 1) {
+                __threadfence_system();
+                for (uint32_t q = 0; q < peer.npeers; ++q)
+                    asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(peer.flag[q]), "l"(peer.tag) : "memory");
+                *peer.ticket = 0u;
+            }
+        }
+    }
 }
 
 // ---------------------------------------------------------- compaction ----
 template <typename TIdx>
 __global__ void __launch_bounds__(256) compact_kernel(const uint32_t *__restrict__ bitmap, uint64_t words,
                                                       TIdx *__restrict__ list, DevCounters *ctr, int parity,
-                                                      uint64_t own_begin, uint64_t own_end) {
+                                                      uint64_t own_begin, uint64_t own_end, PeerWait pw) {
     const unsigned lane = lane_id();
+    if (pw.nflags) {
+        // Wait (bounded) until every rank has published this step's slice.
+        __shared__ uint32_t s_ok;
+        if (threadIdx.x == 0) {
+            uint32_t ok = 1u;
+            for (uint32_t r = 0; r < pw.nflags && ok; ++r) {
+                for (uint32_t it = 0;; ++it) {
+                    unsigned long long v;
+                    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(pw.flags + r) : "memory");
+                    if (v >= pw.tag) break;
+                    if (*(volatile uint32_t *)&ctr->error != 0u || it >= pw.spin_limit) {
+                        atomicExch(&ctr->error, 3u);
+                        ok = 0u;
+                        break;
+                    }
+                    __nanosleep(64);
+                }
+            }
+            s_ok = ok;
+        }
+        __syncthreads();
+        if (!s_ok) return;
+    }
     const uint64_t stride = (uint64_t)blockDim.x * gridDim.x;
     uint32_t own = 0;
     for (uint64_t base = (uint64_t)blockIdx.x * blockDim.x; base < words; base += stride) {
         const uint64_t wi = base + threadIdx.x;
-        const uint32_t word = wi < words ? bitmap[wi] : 0u;
+        const uint32_t word = wi < words ? __ldcg(bitmap + wi) : 0u;
         const uint32_t cnt = __popc(word);
         if (wi >= own_begin && wi < own_end) own += cnt;
         uint32_t incl = cnt;
@@ -617,37 +661,41 @@ void launch_init_state(cudaStream_t s, uint64_t n, float v_rest, float *v, float
 template <bool EXT, typename TIdx, int ITERS>
 static void lif_dispatch(cudaStream_t s, int device, uint64_t n, const LifArgs &p, float *v, float *cur,
                          const float *ext, uint32_t *refr, uint8_t *spikes, uint32_t *bitmap, void *list,
-                         uint64_t off, DevCounters *ctr, int parity) {
+                         uint64_t off, DevCounters *ctr, int parity, const PeerArgs &peer) {
     constexpr uint64_t tile = (uint64_t)ITERS * kLifThreads * 4u;
     const int grid = grid_for(device, 6, n, tile);
     if (list != nullptr)
         lif_kernel<EXT, true, TIdx, ITERS><<<grid, kLifThreads, 0, s>>>(n, p, v, cur, ext, refr, spikes, bitmap,
-                                                                        (TIdx *)list, off, ctr, parity);
+                                                                        (TIdx *)list, off, ctr, parity, peer);
     else
         lif_kernel<EXT, false, TIdx, ITERS><<<grid, kLifThreads, 0, s>>>(n, p, v, cur, ext, refr, spikes, bitmap,
-                                                                         (TIdx *)list, off, ctr, parity);
+                                                                         (TIdx *)list, off, ctr, parity, peer);
 }
 
 void launch_lif(cudaStream_t s, int device, uint64_t n, const LifArgs &p, float *v, float *cur, const float *ext,
                 uint32_t *refr, uint8_t *spikes, uint32_t *bitmap, void *list, int idx_bits, uint64_t off,
-                DevCounters *ctr, int parity) {
-    if (n == 0) return;
+                DevCounters *ctr, int parity, const PeerArgs *peer_in) {
+    PeerArgs peer{};
+    if (peer_in) peer = *peer_in;
+    if (n == 0 && peer.npeers == 0) return;
     if (idx_bits == 32) {
-        if (ext) lif_dispatch<true, uint32_t, 8>(s, device, n, p, v, cur, ext, refr, spikes, bitmap, list, off, ctr, parity);
-        else lif_dispatch<false, uint32_t, 8>(s, device, n, p, v, cur, ext, refr, spikes, bitmap, list, off, ctr, parity);
+        if (ext) lif_dispatch<true, uint32_t, 8>(s, device, n, p, v, cur, ext, refr, spikes, bitmap, list, off, ctr, parity, peer);
+        else lif_dispatch<false, uint32_t, 8>(s, device, n, p, v, cur, ext, refr, spikes, bitmap, list, off, ctr, parity, peer);
     } else {
-        if (ext) lif_dispatch<true, uint64_t, 4>(s, device, n, p, v, cur, ext, refr, spikes, bitmap, list, off, ctr, parity);
-        else lif_dispatch<false, uint64_t, 4>(s, device, n, p, v, cur, ext, refr, spikes, bitmap, list, off, ctr, parity);
+        if (ext) lif_dispatch<true, uint64_t, 4>(s, device, n, p, v, cur, ext, refr, spikes, bitmap, list, off, ctr, parity, peer);
+        else lif_dispatch<false, uint64_t, 4>(s, device, n, p, v, cur, ext, refr, spikes, bitmap, list, off, ctr, parity, peer);
     }
 }
 
 void launch_compact(cudaStream_t s, int device, const uint32_t *bitmap, uint64_t words, void *list, int idx_bits,
-                    DevCounters *ctr, int parity, uint64_t own_begin, uint64_t own_end) {
+                    DevCounters *ctr, int parity, uint64_t own_begin, uint64_t own_end, const PeerWait *wait) {
+    PeerWait pw{};
+    if (wait) pw = *wait;
     const int grid = grid_for(device, 8, words, 256);
     if (idx_bits == 32)
-        compact_kernel<uint32_t><<<grid, 256, 0, s>>>(bitmap, words, (uint32_t *)list, ctr, parity, own_begin, own_end);
+        compact_kernel<uint32_t><<<grid, 256, 0, s>>>(bitmap, words, (uint32_t *)list, ctr, parity, own_begin, own_end, pw);
     else
-        compact_kernel<uint64_t><<<grid, 256, 0, s>>>(bitmap, words, (uint64_t *)list, ctr, parity, own_begin, own_end);
+        compact_kernel<uint64_t><<<grid, 256, 0, s>>>(bitmap, words, (uint64_t *)list, ctr, parity, own_begin, own_end, pw);
 }
 
 template <typename TIdx, typename TCol>

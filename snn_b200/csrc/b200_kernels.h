@@ -31,6 +31,28 @@ struct DevCounters {
     unsigned long long events;
 };
 
+// Peer (NVLink, CUDA IPC) spike-bitmap exchange fused into the LIF kernel:
+// every bitmap word a rank computes is also stored into each rank's exchange
+// buffer; the LIF grid's last CTA then publishes `tag` into every rank's
+// flag slot for this rank. npeers == 0 disables it.
+constexpr uint32_t kMaxPeers = 8;
+struct PeerArgs {
+    uint32_t *dst[kMaxPeers];             // exchange bitmap (this step's parity) of each rank
+    unsigned long long *flag[kMaxPeers];  // this rank's flag slot in each rank's exchange buffer
+    uint32_t *ticket;                     // local CTA-completion counter (returns to 0)
+    uint64_t word_offset;                 // first word of this rank's slice
+    unsigned long long tag;               // monotonic exchange step, published when done
+    uint32_t npeers;
+};
+// Wait side of the exchange, done by the compaction kernel before it reads
+// the assembled bitmap: all `nflags` flags must reach `tag` (bounded wait).
+struct PeerWait {
+    const unsigned long long *flags;
+    unsigned long long tag;
+    uint32_t nflags;
+    uint32_t spin_limit;
+};
+
 // Network generator description shared by the random-pool and the layered
 // generators. Edge e (CSR order) uses draws 2e+1 (target) and 2e+2 (weight)
 // of the splitmix64 stream seeded `seed` (src/snn.c:94-105, 553-568).
@@ -91,12 +113,12 @@ void launch_init_state(cudaStream_t s, uint64_t n, float v_rest, float *v, float
 // spike list of parity `parity`. idx_bits selects a 32- or 64-bit list.
 void launch_lif(cudaStream_t s, int device, uint64_t n, const LifArgs &p, float *v, float *cur, const float *ext,
                 uint32_t *refr, uint8_t *spikes, uint32_t *bitmap, void *list, int idx_bits, uint64_t global_offset,
-                DevCounters *ctr, int parity);
+                DevCounters *ctr, int parity, const PeerArgs *peer = nullptr);
 
 // Global bitmap -> spike list (sharded contexts, after the all-gather).
 // Also adds the popcount of words [own_begin, own_end) to ctr->spikes.
 void launch_compact(cudaStream_t s, int device, const uint32_t *bitmap, uint64_t words, void *list, int idx_bits,
-                    DevCounters *ctr, int parity, uint64_t own_begin, uint64_t own_end);
+                    DevCounters *ctr, int parity, uint64_t own_begin, uint64_t own_end, const PeerWait *wait = nullptr);
 
 // Push propagation from the spike list over a resident CSR.
 // col_bits = 32 or 64 (local target ids), idx_bits = spike list width.

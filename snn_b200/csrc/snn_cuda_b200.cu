@@ -155,6 +155,13 @@ struct snn_cuda_context {
     cudaEvent_t ev_inj = nullptr;
 
     ncclComm_t comm = nullptr;
+    // Peer exchange (SNN_B200_EXCHANGE_PEER): [2 parities][bitmap_words] u32,
+    // then world u64 flags, then a u32 ticket; peers' buffers mapped by IPC.
+    int exchange = SNN_B200_EXCHANGE_NCCL;
+    void *d_xbuf = nullptr;
+    uint32_t *peer_x[b200::kMaxPeers] = {};
+    bool peers_connected = false;
+    unsigned long long xstep = 0;  // monotonic exchange counter (never reset)
 
     uint64_t step = 0;
     uint64_t launches = 0;
@@ -227,6 +234,9 @@ void free_context(snn_cuda_context_t *c) {
     if (c->copy_stream) cudaStreamSynchronize(c->copy_stream);
     report_binned_profile(c);
     if (c->comm) ncclCommDestroy(c->comm);
+    for (uint32_t r = 0; r < b200::kMaxPeers; ++r)
+        if (c->peer_x[r] && r != c->rank) cudaIpcCloseMemHandle(c->peer_x[r]);
+    if (c->d_xbuf) cudaFree(c->d_xbuf);
     void *dev[] = {c->d_v, c->d_cur_pair, c->d_ext, c->d_refr, c->d_spikes, c->d_ws, c->d_row_ptr, c->d_col,
                    c->d_w, c->d_col_ptr, c->d_pre, c->d_cw, c->d_deg, c->d_chunk_row, c->d_chunk_col,
                    c->d_chunk_w, c->d_inj_idx, c->d_inj_val, c->d_bin_mem};
@@ -271,7 +281,11 @@ snn_status_t apply_options(snn_cuda_context_t *c, uint64_t n, const snn_b200_opt
         o.propagation != SNN_B200_PROPAGATE_PUSH_ATOMIC && o.propagation != SNN_B200_PROPAGATE_PUSH_BINNED)
         return SNN_ERR_INVALID_ARGUMENT;
     if (o.index_width != 0 && o.index_width != 32 && o.index_width != 64) return SNN_ERR_INVALID_ARGUMENT;
-    if (o.world_size > 1 && o.nccl_id == nullptr) return SNN_ERR_INVALID_ARGUMENT;
+    if (o.exchange != SNN_B200_EXCHANGE_NCCL && o.exchange != SNN_B200_EXCHANGE_PEER) return SNN_ERR_INVALID_ARGUMENT;
+    if (o.world_size > 1 && o.exchange == SNN_B200_EXCHANGE_NCCL && o.nccl_id == nullptr)
+        return SNN_ERR_INVALID_ARGUMENT;
+    if (o.exchange == SNN_B200_EXCHANGE_PEER && o.world_size > b200::kMaxPeers) return SNN_ERR_UNSUPPORTED;
+    c->exchange = o.exchange;
     c->propagation = o.propagation;
     c->world = o.world_size;
     c->rank = o.rank;
@@ -374,8 +388,19 @@ snn_status_t finish_binned(snn_cuda_context_t *c) {
     return cuda_status(cudaStreamSynchronize(c->stream));
 }
 
+// Offsets inside the peer exchange buffer.
+uint64_t xflags_offset(const snn_cuda_context_t *c) { return ((2 * c->bitmap_words * 4 + 255) / 256) * 256; }
+
+snn_status_t init_peer_exchange(snn_cuda_context_t *c) {
+    if (c->world <= 1 || c->exchange != SNN_B200_EXCHANGE_PEER) return SNN_OK;
+    const uint64_t bytes = xflags_offset(c) + c->world * 8 + 256;
+    // Plain cudaMalloc (not the seam wrapper): IPC export needs its own allocation.
+    if (cudaMalloc(&c->d_xbuf, bytes) != cudaSuccess) return SNN_ERR_CUDA;
+    return cuda_status(cudaMemset(c->d_xbuf, 0, bytes));
+}
+
 snn_status_t init_nccl(snn_cuda_context_t *c, const void *id) {
-    if (c->world <= 1) return SNN_OK;
+    if (c->world <= 1 || c->exchange != SNN_B200_EXCHANGE_NCCL) return SNN_OK;
     ncclUniqueId uid;
     std::memcpy(&uid, id, sizeof(uid));
     const ncclResult_t r = ncclCommInitRank(&c->comm, (int)c->world, uid, (int)c->rank);
@@ -654,6 +679,7 @@ snn_status_t begin_create(uint64_t n, const snn_lif_params_t &lif, float decay, 
     snn_status_t st = apply_options(c, n, o);
     if (st == SNN_OK) st = create_streams(c);
     if (st == SNN_OK) st = init_nccl(c, o.nccl_id);
+    if (st == SNN_OK) st = init_peer_exchange(c);
     if (st == SNN_OK) st = allocate_state(c);
     if (st != SNN_OK) {
         free_context(c);
@@ -725,12 +751,42 @@ snn_status_t enqueue_step(snn_cuda_context_t *c, bool has_ext) {
     TimingGroup *tg = timing_begin(c);
     const bool sharded = c->world > 1;
     uint32_t *own_bitmap = c->d_bitmap + (uint64_t)c->rank * (c->slot / 32);
+    const bool peer = sharded && c->exchange == SNN_B200_EXCHANGE_PEER;
+    if (peer && !c->peers_connected) {
+        set_error("snn_b200", "peer exchange used before snn_b200_ipc_connect");
+        return SNN_ERR_INVALID_ARGUMENT;
+    }
+    b200::PeerArgs pa{};
+    uint32_t *xbitmap = nullptr;  // this step's assembled global bitmap (peer exchange)
+    if (peer) {
+        ++c->xstep;
+        const uint64_t par = c->xstep & 1u;
+        for (uint32_t r = 0; r < c->world; ++r) {
+            pa.dst[r] = c->peer_x[r] + par * c->bitmap_words;
+            pa.flag[r] = (unsigned long long *)((char *)c->peer_x[r] + xflags_offset(c)) + c->rank;
+        }
+        pa.npeers = c->world;
+        pa.word_offset = (uint64_t)c->rank * (c->slot / 32);
+        pa.tag = c->xstep;
+        pa.ticket = (uint32_t *)((char *)c->d_xbuf + xflags_offset(c) + c->world * 8);
+        xbitmap = (uint32_t *)c->d_xbuf + par * c->bitmap_words;
+    }
     b200::launch_lif(c->stream, c->device, c->n_local, c->args, c->d_v, cur, has_ext ? c->d_ext : nullptr, c->d_refr,
-                     c->d_spikes, own_bitmap, sharded ? nullptr : c->d_list, c->idx_bits, c->lo, c->d_ctr, parity);
+                     c->d_spikes, own_bitmap, sharded ? nullptr : c->d_list, c->idx_bits, c->lo, c->d_ctr, parity,
+                     peer ? &pa : nullptr);
     snn_status_t st = check_launch(c);
     if (st != SNN_OK) return st;
     timing_mark(c, tg, 1);
-    if (sharded) {
+    if (peer) {
+        // LIF already stored this rank's words into every rank's buffer and
+        // raised its flag; the compaction waits for all flags of this step.
+        const b200::PeerWait pw{(const unsigned long long *)((char *)c->d_xbuf + xflags_offset(c)), c->xstep,
+                                c->world, 1u << 24};
+        b200::launch_compact(c->stream, c->device, xbitmap, c->bitmap_words, c->d_list, c->idx_bits, c->d_ctr,
+                             parity, c->lo / 32, ceil_div(c->hi, 32), &pw);
+        c->launches++;
+        if ((st = cuda_status(cudaGetLastError())) != SNN_OK) return st;
+    } else if (sharded) {
         const size_t words = c->slot / 32;
         const ncclResult_t r = ncclAllGather(own_bitmap, c->d_bitmap, words, ncclUint32, c->comm, c->stream);
         if (r != ncclSuccess) {
@@ -746,7 +802,7 @@ snn_status_t enqueue_step(snn_cuda_context_t *c, bool has_ext) {
     if (c->mode == SNN_CUDA_MODE_FULL) {
         if (c->propagation == SNN_B200_PROPAGATE_ORDERED)
             b200::launch_propagate_pull(c->stream, c->device, c->n_local, c->d_col_ptr, c->d_pre, c->idx_bits,
-                                        c->d_cw, c->d_bitmap, next, c->d_list, c->idx_bits, c->d_deg, c->d_ctr,
+                                        c->d_cw, peer ? xbitmap : c->d_bitmap, next, c->d_list, c->idx_bits, c->d_deg, c->d_ctr,
                                         parity, !sharded);
         else if (c->binned) {
             const cudaError_t e = b200::launch_propagate_binned(c->stream, c->d_list, c->idx_bits, next, c->d_ctr,
@@ -947,6 +1003,7 @@ snn_b200_options_t snn_b200_default_options(void) {
     o.world_size = 1;
     o.nccl_id = nullptr;
     o.timing = 0;
+    o.exchange = SNN_B200_EXCHANGE_NCCL;
     return o;
 }
 
@@ -1055,7 +1112,7 @@ snn_status_t snn_cuda_step(snn_cuda_context_t *c, const float *host_external_cur
             return SNN_ERR_CUDA;
     }
     if ((st = enqueue_step(c, host_external_current != nullptr)) != SNN_OK) return st;
-    if (c->binned) queue_error_check(c);
+    if (c->binned || c->exchange == SNN_B200_EXCHANGE_PEER) queue_error_check(c);
     if (host_out_spikes != nullptr && c->n_local != 0) {
         if (seam_fail()) return SNN_ERR_CUDA;
         if (cudaMemcpyAsync(host_out_spikes, c->d_spikes, c->n_local, cudaMemcpyDeviceToHost, c->stream) !=
@@ -1151,6 +1208,35 @@ snn_status_t snn_b200_create_layered_random(const snn_size_t *layer_sizes, size_
 }
 
 const char *snn_b200_last_error(void) { return g_last_error; }
+
+snn_status_t snn_b200_ipc_handle(const snn_cuda_context_t *c, void *out_handle64) {
+    if (c == nullptr || out_handle64 == nullptr || c->d_xbuf == nullptr) return SNN_ERR_INVALID_ARGUMENT;
+    if (set_device(c) != SNN_OK) return SNN_ERR_CUDA;
+    cudaIpcMemHandle_t h;
+    const snn_status_t st = cuda_status(cudaIpcGetMemHandle(&h, c->d_xbuf));
+    if (st == SNN_OK) std::memcpy(out_handle64, &h, sizeof(h));
+    return st;
+}
+
+snn_status_t snn_b200_ipc_connect(snn_cuda_context_t *c, const void *handles) {
+    if (c == nullptr || handles == nullptr || c->d_xbuf == nullptr || c->peers_connected)
+        return SNN_ERR_INVALID_ARGUMENT;
+    if (set_device(c) != SNN_OK) return SNN_ERR_CUDA;
+    for (uint32_t r = 0; r < c->world; ++r) {
+        if (r == c->rank) {
+            c->peer_x[r] = (uint32_t *)c->d_xbuf;
+            continue;
+        }
+        cudaIpcMemHandle_t h;
+        std::memcpy(&h, (const char *)handles + (size_t)r * sizeof(h), sizeof(h));
+        void *p = nullptr;
+        const snn_status_t st = cuda_status(cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess));
+        if (st != SNN_OK) return st;
+        c->peer_x[r] = (uint32_t *)p;
+    }
+    c->peers_connected = true;
+    return SNN_OK;
+}
 
 snn_status_t snn_b200_shard_range(snn_size_t n, uint32_t world, uint32_t rank, snn_size_t *out_begin,
                                   snn_size_t *out_count) {

@@ -30,23 +30,33 @@ def main():
     dist.init_process_group("gloo")
     keep = []
 
-    def options(prop):
-        # A fresh NCCL unique id per context (one communicator each).
-        obj = [sb.nccl_unique_id() if rank == 0 else None]
-        dist.broadcast_object_list(obj, src=0)
-        idbuf = ctypes.create_string_buffer(obj[0], 128)
-        keep.append(idbuf)
-        o = sb.default_options(device=local, rank=rank, world_size=world, propagation=prop)
-        o.nccl_id = ctypes.cast(idbuf, ctypes.c_void_p)
+    def options(prop, exchange=sb.EXCHANGE_NCCL):
+        o = sb.default_options(device=local, rank=rank, world_size=world, propagation=prop, exchange=exchange)
+        if exchange == sb.EXCHANGE_NCCL:
+            # A fresh NCCL unique id per context (one communicator each).
+            obj = [sb.nccl_unique_id() if rank == 0 else None]
+            dist.broadcast_object_list(obj, src=0)
+            idbuf = ctypes.create_string_buffer(obj[0], 128)
+            keep.append(idbuf)
+            o.nccl_id = ctypes.cast(idbuf, ctypes.c_void_p)
         return o
+
+    def connect(ctx, exchange):
+        # Peer exchange: gather every rank's IPC handle, map the peers.
+        if exchange == sb.EXCHANGE_PEER:
+            handles = [None] * world
+            dist.all_gather_object(handles, ctx.ipc_handle())
+            ctx.ipc_connect(handles)
 
     orc = Oracle("port")
     failures = []
     n, steps, count = 30011, 40, 300
     lif = baseline_lif()
     net = orc.random_pool(n, 120, -0.2, 0.5, 5, lif=lif)
-    for prop in (sb.PROPAGATE_ORDERED, sb.PROPAGATE_PUSH):
-        ctx = sb.CudaContext.create(net, None, options(prop))
+    for prop, exchange in ((sb.PROPAGATE_ORDERED, sb.EXCHANGE_NCCL), (sb.PROPAGATE_PUSH, sb.EXCHANGE_NCCL),
+                           (sb.PROPAGATE_ORDERED, sb.EXCHANGE_PEER), (sb.PROPAGATE_PUSH, sb.EXCHANGE_PEER)):
+        ctx = sb.CudaContext.create(net, None, options(prop, exchange))
+        connect(ctx, exchange)
         lo, cnt = ctx.local_begin, ctx.local_count
         raster = np.zeros((steps, cnt), np.uint8)
         for t in range(steps):
@@ -66,15 +76,28 @@ def main():
             exact = prop == sb.PROPAGATE_ORDERED
             if exact:
                 if not np.array_equal(g_r, ras):
-                    failures.append(f"ordered raster mismatch at step {np.nonzero((g_r != ras).any(1))[0][:3]}")
+                    failures.append(f"ordered/{exchange} raster mismatch at step "
+                                    f"{np.nonzero((g_r != ras).any(1))[0][:3]}")
                 if not np.array_equal(g_v.view(np.uint32), st.voltage().view(np.uint32)):
-                    failures.append("ordered voltage mismatch")
+                    failures.append(f"ordered/{exchange} voltage mismatch")
                 if sum(p[3] for p in parts) != int(ev.sum()) or sum(p[4] for p in parts) != int(sc.sum()):
-                    failures.append("ordered stats mismatch")
+                    failures.append(f"ordered/{exchange} stats mismatch")
             else:
                 if not np.array_equal(g_r[0], ras[0]):
-                    failures.append("push first-step raster mismatch")
+                    failures.append(f"push/{exchange} first-step raster mismatch")
         ctx.free()
+    # Async multi-step run on the peer exchange equals the NCCL one (ordered: exact).
+    finals = []
+    for exchange in (sb.EXCHANGE_NCCL, sb.EXCHANGE_PEER):
+        ctx = sb.CudaContext.create(net, None, options(sb.PROPAGATE_ORDERED, exchange))
+        connect(ctx, exchange)
+        ctx.run_stream_async(9, 0, 30, count, 20.0)
+        ctx.synchronize()
+        finals.append((ctx.download_voltage(), ctx.stats()["spikes"]))
+        ctx.free()
+    if not (np.array_equal(finals[0][0].view(np.uint32), finals[1][0].view(np.uint32)) and
+            finals[0][1] == finals[1][1]):
+        failures.append(f"rank {rank}: async peer run differs from NCCL run")
     # Device-generated shards tile the host network exactly.
     ctx = sb.CudaContext.random_pool(n, 120, -0.2, 0.5, 5, lif=None, options=options(sb.PROPAGATE_PUSH))
     rp, ci, w = ctx.download_topology()
