@@ -139,6 +139,7 @@ __global__ void __launch_bounds__(kLifThreads) lif_kernel(uint64_t n, LifArgs p,
     __shared__ TIdx sbuf[WRITE_LIST ? kTile : 1];
     __shared__ uint32_t warp_tot[kLifThreads / 32];
     __shared__ uint32_t s_base;
+    __shared__ uint32_t s_words[kTile / 32];  // this tile's bitmap words, for the peer stores
     const unsigned lane = lane_id();
     const unsigned warp = threadIdx.x >> 5;
     const uint64_t tiles = (n + kTile - 1) / kTile;
@@ -191,9 +192,7 @@ __global__ void __launch_bounds__(kLifThreads) lif_kernel(uint64_t n, LifArgs p,
             word |= __shfl_xor_sync(kFull, word, 4);
             if ((lane & 7u) == 0u && i0 < n) {
                 bitmap[i0 >> 5] = word;
-                // Fused all-gather: the same word goes to every rank's
-                // exchange buffer over NVLink (plain peer stores).
-                for (uint32_t q = 0; q < peer.npeers; ++q) peer.dst[q][peer.word_offset + (i0 >> 5)] = word;
+                if (peer.npeers) s_words[it * (kLifThreads / 8) + (threadIdx.x >> 3)] = word;
             }
             if (WRITE_LIST) {
                 const uint32_t cnt = __popc(nib);
@@ -221,6 +220,17 @@ __global__ void __launch_bounds__(kLifThreads) lif_kernel(uint64_t n, LifArgs p,
                 block_off += total;
             }
         }
+        if (peer.npeers) {
+            // Fused all-gather: the tile's words go to every rank's exchange
+            // buffer over NVLink as coalesced runs of plain peer stores.
+            __syncthreads();
+            const uint64_t w0 = tile * (kTile / 32);
+            const uint64_t nw = min((uint64_t)(kTile / 32), (n + 31) / 32 - w0);
+            for (uint32_t q = 0; q < peer.npeers; ++q)
+                for (uint32_t k = threadIdx.x; k < nw; k += kLifThreads)
+                    peer.dst[q][peer.word_offset + w0 + k] = s_words[k];
+            __syncthreads();
+        }
         if (WRITE_LIST) {
             if (threadIdx.x == 0) s_base = block_off ? atomicAdd(&ctr->list_count[parity], block_off) : 0u;
             __syncthreads();
@@ -233,9 +243,9 @@ __global__ void __launch_bounds__(kLifThreads) lif_kernel(uint64_t n, LifArgs p,
     if (peer.npeers) {
         // Publish: every CTA's peer stores become visible system-wide before
         // its ticket; the last CTA then raises this rank's flag everywhere.
-        __threadfence_system();
         __syncthreads();
         if (threadIdx.x == 0) {
+            __threadfence_system();
             const uint32_t t = atomicAdd(peer.ticket, 1u);
             if (t == gridDim.x - 1) {
                 __threadfence_system();
