@@ -242,6 +242,13 @@ snn_status_t snn_b200_shard_range(snn_size_t neuron_count, uint32_t world_size, 
 snn_status_t snn_b200_ipc_handle(const snn_cuda_context_t *context, void *out_handle64);
 snn_status_t snn_b200_ipc_connect(snn_cuda_context_t *context, const void *handles);
 
+/* Test hook for failure detection: maps every peer of a sharded
+ * SNN_B200_EXCHANGE_PEER context onto its own exchange buffer and sets the
+ * poll budget of the exchange wait, so the other ranks' step flags never
+ * arrive: the next step's bounded wait expires and the step returns
+ * SNN_ERR_CUDA (no device fault, the GPU stays usable). */
+snn_status_t snn_test_b200_peer_loopback(snn_cuda_context_t *context, uint32_t spin_limit);
+
 /* Writes a fresh 128-byte NCCL unique id (rank 0 calls it and shares the bytes). */
 snn_status_t snn_b200_nccl_unique_id(void *out_id128);
 

@@ -122,6 +122,7 @@ ENTRY_POINTS = [
     ("snn_b200_nccl_unique_id", C.c_int, [P]),
     ("snn_b200_ipc_handle", C.c_int, [P, P]),
     ("snn_b200_ipc_connect", C.c_int, [P, P]),
+    ("snn_test_b200_peer_loopback", C.c_int, [P, C.c_uint32]),
     ("snn_b200_shard_range", C.c_int, [u64, C.c_uint32, C.c_uint32, P, P]),
     ("snn_b200_last_error", C.c_char_p, []),
     ("snn_b200_step_noalloc", C.c_int, [C.c_int, P, u64, P, f32, P, P, P, P, P, P, P, P, P]),

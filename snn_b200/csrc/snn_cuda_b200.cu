@@ -162,6 +162,7 @@ struct snn_cuda_context {
     uint32_t *peer_x[b200::kMaxPeers] = {};
     bool peers_connected = false;
     unsigned long long xstep = 0;  // monotonic exchange counter (never reset)
+    uint32_t peer_spin_limit = 1u << 24;
 
     uint64_t step = 0;
     uint64_t launches = 0;
@@ -697,7 +698,8 @@ void queue_error_check(snn_cuda_context_t *c) {
 
 snn_status_t error_after_sync(snn_cuda_context_t *c, snn_status_t st) {
     if (st == SNN_OK && c->h_err && *c->h_err) {
-        set_error("device", "a bounded cross-CTA wait expired (propagation aborted)");
+        set_error("device", *c->h_err == 3u ? "a peer's spike exchange flag did not arrive in time (bounded wait expired)"
+                                            : "a bounded cross-CTA wait expired (propagation aborted)");
         return SNN_ERR_CUDA;
     }
     return st;
@@ -781,7 +783,7 @@ snn_status_t enqueue_step(snn_cuda_context_t *c, bool has_ext) {
         // LIF already stored this rank's words into every rank's buffer and
         // raised its flag; the compaction waits for all flags of this step.
         const b200::PeerWait pw{(const unsigned long long *)((char *)c->d_xbuf + xflags_offset(c)), c->xstep,
-                                c->world, 1u << 24};
+                                c->world, c->peer_spin_limit};
         b200::launch_compact(c->stream, c->device, xbitmap, c->bitmap_words, c->d_list, c->idx_bits, c->d_ctr,
                              parity, c->lo / 32, ceil_div(c->hi, 32), &pw);
         c->launches++;
@@ -1208,6 +1210,14 @@ snn_status_t snn_b200_create_layered_random(const snn_size_t *layer_sizes, size_
 }
 
 const char *snn_b200_last_error(void) { return g_last_error; }
+
+snn_status_t snn_test_b200_peer_loopback(snn_cuda_context_t *c, uint32_t spin_limit) {
+    if (c == nullptr || c->d_xbuf == nullptr || c->peers_connected) return SNN_ERR_INVALID_ARGUMENT;
+    for (uint32_t r = 0; r < c->world; ++r) c->peer_x[r] = (uint32_t *)c->d_xbuf;
+    c->peer_spin_limit = spin_limit;
+    c->peers_connected = true;
+    return SNN_OK;
+}
 
 snn_status_t snn_b200_ipc_handle(const snn_cuda_context_t *c, void *out_handle64) {
     if (c == nullptr || out_handle64 == nullptr || c->d_xbuf == nullptr) return SNN_ERR_INVALID_ARGUMENT;

@@ -348,3 +348,25 @@ def test_generated_pool_binned_passes_exact(passes, monkeypatch):
     s = ctx.stats()
     assert s["spikes"] == int(sc.sum()) and s["events"] == int(ev.sum())
     np.testing.assert_array_equal(bits(st.voltage()), bits(ctx.download_voltage()))
+
+
+def test_peer_exchange_wait_expires_without_fault():
+    """Failure detection without a GPU fault: a 2-rank peer-exchange context
+    whose peer mappings loop back to itself never receives rank 1's step
+    flag. The compaction's bounded wait runs out, the step reports
+    SNN_ERR_CUDA with a message, and the device stays usable."""
+    import ctypes
+    n = 4096
+    net = ORC.random_pool(n, 16, 0.1, 0.2, 1)
+    o = opts(world_size=2, rank=0, exchange=sb.EXCHANGE_PEER)
+    ctx = sb.CudaContext.create(net, None, o)
+    assert sb.lib().snn_test_b200_peer_loopback(ctx.handle, 2000) == sb.SNN_OK
+    st = sb.lib().snn_cuda_step(ctx.handle, None, None)
+    assert st == sb.SNN_ERR_CUDA
+    assert "did not arrive" in sb.last_error()
+    ctx.free()
+    # The GPU and the library remain usable.
+    ok = sb.CudaContext.create(net)
+    ok.step(np.full(n, 2.0, np.float32))
+    ok.free()
+    del ctypes
