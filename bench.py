@@ -59,6 +59,7 @@ def parse():
                     help="streaming: STREAMING VRAM policy on a host-resident pool (--stream-neurons), "
                          "measured against the host-link roofline")
     ap.add_argument("--stream-neurons", type=int, default=1_000_000)
+    ap.add_argument("--stream-mode", choices=["chunked", "sparse"], default="sparse")
     ap.add_argument("--stream-budget-frac", type=float, default=0.25,
                     help="VRAM budget as a fraction of the host CSR bytes (config 3 streams ~15x its budget)")
     ap.add_argument("--propagation", choices=["auto", "binned", "atomic"], default="auto",
@@ -232,7 +233,9 @@ def run_streaming(args):
     net = sb.Network.from_csr(row_ptr, col, w, lif)
     csr_bytes = 12 * e + 8 * (n + 1)
     cfg = sb.default_config(prefer_streaming=1, max_vram_bytes=int(args.stream_budget_frac * csr_bytes))
-    ctx = sb.CudaContext.create(net, cfg, sb.default_options(device=0, timing=1))
+    sparse = args.stream_mode == "sparse"
+    ctx = sb.CudaContext.create(net, cfg, sb.default_options(
+        device=0, timing=1, streaming=sb.STREAMING_SPARSE if sparse else sb.STREAMING_CHUNKED))
     assert ctx.mode == sb.MODE_STREAMING
     count = max(1, int(round(args.inject_frac * n)))
     # Host-link roofline: pinned host -> device copy of 1 GiB, best of 5.
@@ -260,7 +263,9 @@ def run_streaming(args):
         ctx.synchronize()
     ms = ev0.elapsed_time(ev1)
     s = ctx.stats()
-    streamed = csr_bytes * args.steps
+    # Bytes that cross the host link: the whole CSR every step (chunked), or
+    # the spiking rows' edges (12 B/event + 16 B/row, sparse).
+    streamed = csr_bytes * args.steps if not sparse else 12 * s["events"] + 16 * s["spikes"]
     gbs = streamed / (ms / 1e3) / 1e9
     print(json.dumps({
         "metric": "synaptic_events_per_sec", "value": s["events"] / (ms / 1e3), "unit": "events/s", "n_gpus": 1,
@@ -269,10 +274,10 @@ def run_streaming(args):
         "data": "synthetic: numpy-seeded uniform pool in host memory",
         "config": {"workload": "config3_streaming_scaled", "neurons": n, "fanout": f, "synapses": e,
                    "host_csr_bytes": csr_bytes, "vram_budget_bytes": int(args.stream_budget_frac * csr_bytes),
-                   "policy": "STREAMING", "layout": ctx.layout},
+                   "policy": f"STREAMING ({args.stream_mode})", "layout": ctx.layout},
         "roofline": {"bound": "host_link", "achieved": gbs, "peak": best, "unit": "GB/s", "frac": gbs / best,
                      "peak_kind": "measured pinned H2D (1 GiB, best of 5)",
-                     "algorithmic_bytes_per_step": csr_bytes},
+                     "algorithmic_bytes_per_step": streamed / args.steps},
         "spike_rate": s["spikes"] / (args.steps * n), "clocks": clk.summary(),
     }), flush=True)
     ctx.free()

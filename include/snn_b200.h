@@ -163,6 +163,16 @@ typedef enum snn_b200_exchange {
     SNN_B200_EXCHANGE_PEER = 1
 } snn_b200_exchange_t;
 
+typedef enum snn_b200_streaming {
+    /* The reference's scheme: every step copies the whole host CSR to the
+     * device in bounded chunks (double-buffered: copy overlaps propagation). */
+    SNN_B200_STREAMING_CHUNKED = 0,
+    /* The host col_idx/weights are page-locked and mapped; each step the push
+     * kernel reads only the spiking rows' edges over the host link (row_ptr
+     * resident). Arrays must be 16-byte aligned; otherwise CHUNKED is used. */
+    SNN_B200_STREAMING_SPARSE = 1
+} snn_b200_streaming_t;
+
 typedef struct snn_b200_options {
     int propagation;        /* snn_b200_propagation_t */
     int device;             /* CUDA device ordinal; -1 = the calling thread's current device */
@@ -172,6 +182,7 @@ typedef struct snn_b200_options {
     const void *nccl_id;    /* 128-byte NCCL unique id (snn_b200_nccl_unique_id), world_size > 1 */
     int timing;             /* 1: record per-step device timings (snn_b200_stats) */
     int exchange;           /* snn_b200_exchange_t: how sharded ranks share spikes */
+    int streaming;          /* snn_b200_streaming_t: how a STREAMING context reads the host CSR */
 } snn_b200_options_t;
 
 typedef struct snn_b200_stats {

@@ -41,6 +41,7 @@ MODE_NONE, MODE_FULL, MODE_STREAMING = 0, 1, 2
 NOALLOC_MAX_NEURONS = 1048576  # SNN_B200_NOALLOC_MAX_NEURONS
 PROPAGATE_PUSH, PROPAGATE_ORDERED, PROPAGATE_PUSH_ATOMIC, PROPAGATE_PUSH_BINNED = 0, 1, 2, 3
 EXCHANGE_NCCL, EXCHANGE_PEER = 0, 1
+STREAMING_CHUNKED, STREAMING_SPARSE = 0, 1
 
 
 class SnnError(RuntimeError):
@@ -79,7 +80,7 @@ class Options(C.Structure):
     """snn_b200_options_t (include/snn_b200.h)."""
     _fields_ = [("propagation", C.c_int), ("device", C.c_int), ("index_width", C.c_int),
                 ("rank", C.c_uint32), ("world_size", C.c_uint32), ("nccl_id", P), ("timing", C.c_int),
-                ("exchange", C.c_int)]
+                ("exchange", C.c_int), ("streaming", C.c_int)]
 
 
 class Stats(C.Structure):

@@ -158,8 +158,13 @@ struct snn_cuda_context {
     // Peer exchange (SNN_B200_EXCHANGE_PEER): [2 parities][bitmap_words] u32,
     // then world u64 flags, then a u32 ticket; peers' buffers mapped by IPC.
     int exchange = SNN_B200_EXCHANGE_NCCL;
+    int streaming = SNN_B200_STREAMING_CHUNKED;
+    // Sparse streaming: device pointers of the page-locked, mapped host CSR.
+    const uint64_t *h_col_dev = nullptr;
+    const float *h_w_dev = nullptr;
     void *d_xbuf = nullptr;
     uint32_t *peer_x[b200::kMaxPeers] = {};
+    bool peer_ipc[b200::kMaxPeers] = {};  // mapping opened with cudaIpcOpenMemHandle
     bool peers_connected = false;
     unsigned long long xstep = 0;  // monotonic exchange counter (never reset)
     uint32_t peer_spin_limit = 1u << 24;
@@ -236,7 +241,7 @@ void free_context(snn_cuda_context_t *c) {
     report_binned_profile(c);
     if (c->comm) ncclCommDestroy(c->comm);
     for (uint32_t r = 0; r < b200::kMaxPeers; ++r)
-        if (c->peer_x[r] && r != c->rank) cudaIpcCloseMemHandle(c->peer_x[r]);
+        if (c->peer_ipc[r]) cudaIpcCloseMemHandle(c->peer_x[r]);
     if (c->d_xbuf) cudaFree(c->d_xbuf);
     void *dev[] = {c->d_v, c->d_cur_pair, c->d_ext, c->d_refr, c->d_spikes, c->d_ws, c->d_row_ptr, c->d_col,
                    c->d_w, c->d_col_ptr, c->d_pre, c->d_cw, c->d_deg, c->d_chunk_row, c->d_chunk_col,
@@ -264,6 +269,7 @@ void free_context(snn_cuda_context_t *c) {
     if (c->copy_stream) cudaStreamDestroy(c->copy_stream);
     if (c->stream) cudaStreamDestroy(c->stream);
     delete c;
+    cudaGetLastError();  // leave no non-sticky error behind for the next launch check
 }
 
 // Rank r owns [r*S, min((r+1)*S, n)) with S = ceil(n / world / 32) * 32: equal
@@ -287,6 +293,9 @@ snn_status_t apply_options(snn_cuda_context_t *c, uint64_t n, const snn_b200_opt
         return SNN_ERR_INVALID_ARGUMENT;
     if (o.exchange == SNN_B200_EXCHANGE_PEER && o.world_size > b200::kMaxPeers) return SNN_ERR_UNSUPPORTED;
     c->exchange = o.exchange;
+    if (o.streaming != SNN_B200_STREAMING_CHUNKED && o.streaming != SNN_B200_STREAMING_SPARSE)
+        return SNN_ERR_INVALID_ARGUMENT;
+    c->streaming = o.streaming;
     c->propagation = o.propagation;
     c->world = o.world_size;
     c->rank = o.rank;
@@ -650,6 +659,42 @@ snn_status_t allocate_streaming(snn_cuda_context_t *c, const snn_cuda_config_t &
     return SNN_OK;
 }
 
+// Sparse STREAMING: the host CSR's col_idx and weights are page-locked in
+// place and mapped into the device address space; only row_ptr is resident.
+// Each step the push kernel reads the spiking rows' edges straight from host
+// memory over the host link (no chunk copies, no per-step work for silent
+// rows). Falls back to chunked streaming if the arrays cannot be mapped.
+snn_status_t allocate_sparse_streaming(snn_cuda_context_t *c, bool *fallback) {
+    const snn_network_t *net = c->network;
+    const uint64_t n = net->neuron_count, e = net->synapse_count;
+    *fallback = false;
+    const void *arrays[2] = {net->col_idx, net->weights};
+    const uint64_t sizes[2] = {e * 8, e * 4};
+    void *dev[2] = {nullptr, nullptr};
+    for (int i = 0; i < 2 && e; ++i) {
+        if ((uintptr_t)arrays[i] % 16 != 0 ||
+            cudaHostRegister(const_cast<void *>(arrays[i]), sizes[i], cudaHostRegisterMapped | cudaHostRegisterPortable) !=
+                cudaSuccess ||
+            cudaHostGetDevicePointer(&dev[i], const_cast<void *>(arrays[i]), 0) != cudaSuccess) {
+            cudaGetLastError();
+            for (int k = 0; k < 2; ++k)
+                if (c->registered[k + 1]) {
+                    cudaHostUnregister(const_cast<void *>(c->registered[k + 1]));
+                    c->registered[k + 1] = nullptr;
+                }
+            *fallback = true;
+            return SNN_OK;
+        }
+        c->registered[i + 1] = arrays[i];
+    }
+    c->h_col_dev = (const uint64_t *)dev[0];
+    c->h_w_dev = (const float *)dev[1];
+    snn_status_t st;
+    if ((st = dmalloc((void **)&c->d_row_ptr, n + 1, 8)) != SNN_OK) return st;
+    if ((st = h2d(c, c->d_row_ptr, net->row_ptr, (n + 1) * 8)) != SNN_OK) return st;
+    return cuda_status(cudaStreamSynchronize(c->stream));
+}
+
 uint64_t full_push_bytes(const snn_cuda_context_t *c, uint64_t e) {
     return state_bytes(c) + (c->n_global + 1) * 8 + e * (c->col_bits / 8 + 4);
 }
@@ -813,6 +858,11 @@ snn_status_t enqueue_step(snn_cuda_context_t *c, bool has_ext) {
         } else
             b200::launch_propagate_push(c->stream, c->device, c->d_list, c->idx_bits, c->d_row_ptr, c->d_col,
                                         c->col_bits, c->d_w, next, c->d_ctr, parity, !sharded);
+        if ((st = check_launch(c)) != SNN_OK) return st;
+    } else if (c->streaming == SNN_B200_STREAMING_SPARSE) {
+        // Sparse STREAMING: spiking rows read straight from mapped host memory.
+        b200::launch_propagate_push(c->stream, c->device, c->d_list, c->idx_bits, c->d_row_ptr, c->h_col_dev, 64,
+                                    c->h_w_dev, next, c->d_ctr, parity, 1);
         if ((st = check_launch(c)) != SNN_OK) return st;
     } else {
         // STREAMING: chunk i uses copy slot i&1; its copies wait until the
@@ -1006,6 +1056,7 @@ snn_b200_options_t snn_b200_default_options(void) {
     o.nccl_id = nullptr;
     o.timing = 0;
     o.exchange = SNN_B200_EXCHANGE_NCCL;
+    o.streaming = SNN_B200_STREAMING_CHUNKED;
     return o;
 }
 
@@ -1031,7 +1082,12 @@ snn_status_t snn_b200_create(const snn_network_t *network, const snn_cuda_config
     } else {
         c->mode = SNN_CUDA_MODE_STREAMING;
         c->e_local = network->synapse_count;
-        st = allocate_streaming(c, cfg, env.budget);
+        bool fallback = true;
+        if (c->streaming == SNN_B200_STREAMING_SPARSE) st = allocate_sparse_streaming(c, &fallback);
+        if (st == SNN_OK && fallback) {
+            c->streaming = SNN_B200_STREAMING_CHUNKED;
+            st = allocate_streaming(c, cfg, env.budget);
+        }
     }
     if (st != SNN_OK) {
         free_context(c);
@@ -1243,6 +1299,7 @@ snn_status_t snn_b200_ipc_connect(snn_cuda_context_t *c, const void *handles) {
         const snn_status_t st = cuda_status(cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess));
         if (st != SNN_OK) return st;
         c->peer_x[r] = (uint32_t *)p;
+        c->peer_ipc[r] = true;
     }
     c->peers_connected = true;
     return SNN_OK;
@@ -1373,7 +1430,9 @@ snn_status_t snn_b200_get_layout(const snn_cuda_context_t *c, snn_b200_layout_t 
     out->index_bits = (uint32_t)c->col_bits;
     out->propagation = c->propagation;
     out->device_state_bytes = state_bytes(c);
-    if (c->mode == SNN_CUDA_MODE_STREAMING)
+    if (c->mode == SNN_CUDA_MODE_STREAMING && c->streaming == SNN_B200_STREAMING_SPARSE)
+        out->device_topology_bytes = (c->n_global + 1) * 8;
+    else if (c->mode == SNN_CUDA_MODE_STREAMING)
         out->device_topology_bytes = 2 * ((c->slot_rows + 1) * 8 + c->slot_edges * 12);
     else if (c->propagation == SNN_B200_PROPAGATE_ORDERED)
         out->device_topology_bytes = (c->n_local + 1) * 8 + c->e_local * (c->idx_bits / 8 + 4) + c->n_global * 4;

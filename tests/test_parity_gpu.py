@@ -370,3 +370,22 @@ def test_peer_exchange_wait_expires_without_fault():
     ok.step(np.full(n, 2.0, np.float32))
     ok.free()
     del ctypes
+
+
+def test_sparse_streaming_dyadic_bit_exact():
+    """STREAMING with SNN_B200_STREAMING_SPARSE: only row_ptr is resident and
+    the push kernel reads the spiking rows' edges from the page-locked host
+    CSR. Dyadic weights: bit-exact with the CPU step."""
+    lif = default_lif(refractory_steps=2)
+    net = ORC.random_pool(20000, 48, 0.046875, 0.046875, 4242, lif=lif)
+    cfg = sb.default_config(prefer_streaming=1)
+    ctx = sb.CudaContext.create(net, cfg, opts(streaming=sb.STREAMING_SPARSE))
+    assert ctx.mode == sb.MODE_STREAMING
+    assert ctx.layout["device_topology_bytes"] == (20000 + 1) * 8  # row_ptr only
+    rng = np.random.default_rng(11)
+    frames = [(rng.random(20000) < 0.08).astype(np.float32) * np.float32(1.5) for _ in range(8)]
+    cr, gr, cv, gv = run_pair(net, ctx, 8, ext=lambda t: frames[t])
+    assert first_divergence(cr, gr) is None
+    np.testing.assert_array_equal(bits(cv), bits(gv))
+    s = ctx.stats()
+    assert s["events"] == int(cr.sum()) * 48
