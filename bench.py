@@ -62,8 +62,9 @@ def parse():
     ap.add_argument("--stream-mode", choices=["chunked", "sparse"], default="sparse")
     ap.add_argument("--stream-budget-frac", type=float, default=0.25,
                     help="VRAM budget as a fraction of the host CSR bytes (config 3 streams ~15x its budget)")
-    ap.add_argument("--propagation", choices=["auto", "binned", "atomic"], default="auto",
-                    help="push kernel: auto (library default), binned (shared-memory tiles), atomic (L2 red)")
+    ap.add_argument("--propagation", choices=["auto", "binned", "atomic", "ordered"], default="auto",
+                    help="push kernel: auto (library default), binned (shared-memory tiles), atomic (L2 red); "
+                         "ordered: the bit-exact pull over a device-built CSC")
     return ap.parse_args()
 
 
@@ -196,7 +197,7 @@ def workload_config(args, world):
             "synapses": args.neurons * args.fanout, "weights": "U[-0.2,0.5] mV", "seed": args.seed,
             "inject": f"{args.inject_frac * 100:g}% of neurons x {args.inject_value:g} per step",
             "lif": "dt 1 ms, tau 20 ms, rest=reset -65 mV, thr -50 mV, refractory 2", "policy": "FULL",
-            "propagation": f"push ({args.propagation})", "parallelism": f"postsynaptic shards x{world}" + (f", {args.exchange} spike exchange" if world > 1 else ""), "l2": L2_NOTE}
+            "propagation": "ordered (bit-exact pull)" if args.propagation == "ordered" else f"push ({args.propagation})", "parallelism": f"postsynaptic shards x{world}" + (f", {args.exchange} spike exchange" if world > 1 else ""), "l2": L2_NOTE}
 
 
 # ------------------------------------------------------------ GPU side ----
@@ -303,7 +304,8 @@ def run_b200(args):
         dist.broadcast_object_list(obj, src=0)
         nccl_id = obj[0]
     id_buf = None
-    prop = {"auto": sb.PROPAGATE_PUSH, "binned": sb.PROPAGATE_PUSH_BINNED, "atomic": sb.PROPAGATE_PUSH_ATOMIC}
+    prop = {"auto": sb.PROPAGATE_PUSH, "binned": sb.PROPAGATE_PUSH_BINNED, "atomic": sb.PROPAGATE_PUSH_ATOMIC,
+            "ordered": sb.PROPAGATE_ORDERED}
     opts = sb.default_options(device=local, world_size=world, rank=rank, timing=1,
                               propagation=prop[args.propagation],
                               exchange=sb.EXCHANGE_PEER if args.exchange == "peer" else sb.EXCHANGE_NCCL)
@@ -366,13 +368,20 @@ def run_b200(args):
     # reference's CSR format) + 16 per spiking row (row_ptr pair).
     peak, peak_kind = measured_peak_gbs()
     prop_bytes = 12.0 * s["events"] + 16.0 * spikes_total
+    kernel_name = "propagate_push_kernel"
+    lay = ctx.layout
+    if args.propagation == "ordered":
+        # Pull over the CSC: every step reads each in-edge's presynaptic id
+        # (4 B), the weight of each event (4 B) and the col_ptr pair (8 B
+        # per local target).
+        kernel_name = "propagate_pull_kernel"
+        prop_bytes = (4.0 * int(lay["local_synapses"]) + 8.0 * (ctx.local_count + 1)) * s["steps"] + 4.0 * s["events"]
     prop_s = s["propagate_ms"] / 1e3
     achieved = prop_bytes / prop_s / 1e9 if prop_s > 0 else 0.0
-    lay = ctx.layout
     traffic = None
-    if args.propagation != "binned" and int(lay["index_bits"]) == 32 and s["steps"]:
+    if args.propagation not in ("binned", "ordered") and int(lay["index_bits"]) == 32 and s["steps"]:
         traffic = NCU_DRAM_BYTES_PER_EVENT * s["events"] / s["steps"]
-    step_bytes = (12.0 * s["events"] + 16.0 * spikes_total + 25.0 * ctx.local_count * s["steps"]
+    step_bytes = (prop_bytes + 25.0 * ctx.local_count * s["steps"]
                   + 12.0 * count * s["steps"])
     launches = int(s["kernel_launches"])
 
@@ -419,7 +428,7 @@ def run_b200(args):
             "config": dict(workload_config(args, world), index_bits=int(lay["index_bits"])),
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": traffic, "peak_kind": peak_kind,
-                         "kernel": "propagate_push_kernel",
+                         "kernel": kernel_name,
                          "algorithmic_bytes_per_launch": prop_bytes / max(s["steps"], 1),
                          "kernel_ms_per_launch": s["propagate_ms"] / max(s["steps"], 1)},
             "step_roofline": {"achieved": step_bytes / (ms / 1e3) / 1e9 if world == 1 else None,

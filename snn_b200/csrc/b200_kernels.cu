@@ -11,6 +11,7 @@
 #include "b200_kernels.h"
 #include "b200_device.cuh"
 
+#include <cub/device/device_radix_sort.cuh>
 #include <cub/device/device_scan.cuh>
 
 #include <mutex>
@@ -584,8 +585,9 @@ __global__ void __launch_bounds__(256) gen_edges_dense_kernel(GenParams g, uint6
 }
 
 // Warp per row: count the row's edges that target [lo, hi).
+template <typename TCount>
 __global__ void __launch_bounds__(256) gen_count_shard_kernel(GenParams g, uint64_t lo, uint64_t hi,
-                                                              uint64_t *__restrict__ counts) {
+                                                              TCount *__restrict__ counts) {
     const unsigned lane = lane_id();
     const uint64_t gwarp = ((uint64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const uint64_t nwarps = ((uint64_t)gridDim.x * blockDim.x) >> 5;
@@ -633,6 +635,63 @@ __global__ void __launch_bounds__(256) gen_fill_shard_kernel(GenParams g, uint64
             }
             pos += __popc(m);
         }
+    }
+}
+
+// --------------------------------------------------------- device CSC ----
+// In-degree of the targets in [lo, hi): one relaxed atomic per kept edge.
+__global__ void __launch_bounds__(256) gen_indegree_kernel(GenParams g, uint64_t lo, uint64_t hi,
+                                                           unsigned long long *__restrict__ indeg) {
+    const uint64_t total = rows_with_edges(g) * g.fanout;
+    const uint64_t stride = (uint64_t)blockDim.x * gridDim.x;
+    for (uint64_t e = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += stride) {
+        const uint64_t pre = e / g.fanout;
+        const uint64_t post = gen_target(g, pre, e, target_range(g, pre));
+        if (post >= lo && post < hi) atomicAdd(indeg + (post - lo), 1ull);
+    }
+}
+
+// Warp per row: (post - lo, global edge id) of the row's edges into
+// [lo, hi), in edge order, at row_off[pre] (ballot compaction).
+__global__ void __launch_bounds__(256) gen_fill_keys_kernel(GenParams g, uint64_t lo, uint64_t hi,
+                                                            const uint64_t *__restrict__ row_off,
+                                                            uint32_t *__restrict__ keys,
+                                                            uint64_t *__restrict__ eids) {
+    const unsigned lane = lane_id();
+    const uint64_t gwarp = ((uint64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const uint64_t nwarps = ((uint64_t)gridDim.x * blockDim.x) >> 5;
+    for (uint64_t pre = gwarp; pre < g.n; pre += nwarps) {
+        const TargetRange t = target_range(g, pre);
+        if (!t.has_edges) continue;
+        uint64_t pos = row_off[pre];
+        for (uint64_t j0 = 0; j0 < g.fanout; j0 += 32u) {
+            const uint64_t j = j0 + lane;
+            const uint64_t e = pre * g.fanout + j;
+            uint64_t post = 0;
+            bool keep = false;
+            if (j < g.fanout) {
+                post = gen_target(g, pre, e, t);
+                keep = post >= lo && post < hi;
+            }
+            const uint32_t m = __ballot_sync(kFull, keep);
+            if (keep) {
+                const uint64_t q = pos + __popc(m & ((1u << lane) - 1u));
+                keys[q] = (uint32_t)(post - lo);
+                eids[q] = e;
+            }
+            pos += __popc(m);
+        }
+    }
+}
+
+template <typename TPre>
+__global__ void gather_generated_csc_kernel(GenParams g, const uint64_t *__restrict__ eids, uint64_t e,
+                                            TPre *__restrict__ pre, float *__restrict__ w_out) {
+    const uint64_t stride = (uint64_t)blockDim.x * gridDim.x;
+    for (uint64_t k = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; k < e; k += stride) {
+        const uint64_t ed = eids[k];
+        pre[k] = (TPre)(ed / g.fanout);
+        w_out[k] = gen_weight(g, ed);
     }
 }
 
@@ -800,7 +859,7 @@ void launch_gen_edges_dense(cudaStream_t s, int device, const GenParams &g, uint
 
 void launch_gen_count_shard(cudaStream_t s, int device, const GenParams &g, uint64_t lo, uint64_t hi,
                             uint64_t *counts) {
-    gen_count_shard_kernel<<<grid_for(device, 8, g.n * 32u, 256), 256, 0, s>>>(g, lo, hi, counts);
+    gen_count_shard_kernel<uint64_t><<<grid_for(device, 8, g.n * 32u, 256), 256, 0, s>>>(g, lo, hi, counts);
 }
 
 void launch_gen_fill_shard(cudaStream_t s, int device, const GenParams &g, uint64_t lo, uint64_t hi,
@@ -815,6 +874,38 @@ void launch_gen_fill_shard(cudaStream_t s, int device, const GenParams &g, uint6
 cudaError_t exclusive_scan_u64(cudaStream_t s, const uint64_t *in, uint64_t *out, uint64_t n, void *temp,
                                size_t *temp_bytes) {
     return cub::DeviceScan::ExclusiveSum(temp, *temp_bytes, in, out, (int64_t)n, s);
+}
+
+void launch_gen_indegree(cudaStream_t s, int device, const GenParams &g, uint64_t lo, uint64_t hi,
+                         unsigned long long *indeg) {
+    gen_indegree_kernel<<<grid_for(device, 8, g.n * g.fanout, 256), 256, 0, s>>>(g, lo, hi, indeg);
+}
+
+void launch_gen_count_shard_u32(cudaStream_t s, int device, const GenParams &g, uint64_t lo, uint64_t hi,
+                                uint32_t *counts) {
+    gen_count_shard_kernel<uint32_t><<<grid_for(device, 8, g.n * 32u, 256), 256, 0, s>>>(g, lo, hi, counts);
+}
+
+void launch_gen_fill_keys(cudaStream_t s, int device, const GenParams &g, uint64_t lo, uint64_t hi,
+                          const uint64_t *row_off, uint32_t *keys, uint64_t *eids) {
+    gen_fill_keys_kernel<<<grid_for(device, 8, g.n * 32u, 256), 256, 0, s>>>(g, lo, hi, row_off, keys, eids);
+}
+
+cudaError_t sort_pairs_u32_u64(cudaStream_t s, uint32_t *keys, uint32_t *keys_alt, uint64_t *vals,
+                               uint64_t *vals_alt, uint64_t n, int end_bit, void *temp, size_t *temp_bytes,
+                               bool *result_in_alt) {
+    cub::DoubleBuffer<uint32_t> k(keys, keys_alt);
+    cub::DoubleBuffer<uint64_t> v(vals, vals_alt);
+    const cudaError_t e = cub::DeviceRadixSort::SortPairs(temp, *temp_bytes, k, v, (int64_t)n, 0, end_bit, s);
+    if (temp != nullptr) *result_in_alt = k.Current() != keys;
+    return e;
+}
+
+void launch_gather_generated_csc(cudaStream_t s, int device, const GenParams &g, const uint64_t *eids, uint64_t e,
+                                 void *pre, int pre_bits, float *w_out) {
+    const int grid = grid_for(device, 8, e, 256);
+    if (pre_bits == 32) gather_generated_csc_kernel<uint32_t><<<grid, 256, 0, s>>>(g, eids, e, (uint32_t *)pre, w_out);
+    else gather_generated_csc_kernel<uint64_t><<<grid, 256, 0, s>>>(g, eids, e, (uint64_t *)pre, w_out);
 }
 
 void launch_row_degrees(cudaStream_t s, int device, const uint64_t *row_ptr, uint64_t rows, uint32_t *deg) {

@@ -175,6 +175,27 @@ void launch_gen_fill_shard(cudaStream_t s, int device, const GenParams &g, uint6
 cudaError_t exclusive_scan_u64(cudaStream_t s, const uint64_t *in, uint64_t *out, uint64_t n, void *temp,
                                size_t *temp_bytes);
 
+// Device CSC construction (ORDERED propagation of generated networks), one
+// pass per local target range [a, b) (global [lo+a, lo+b)):
+//  * gen_indegree: in-degree of every local target (col_ptr = its scan);
+//  * gen_count_shard (u32 variant): per-row edge counts into a range;
+//  * gen_fill_keys: (target - range_lo, global edge id) pairs in CSR order;
+//  * sort_pairs_u32_u64: stable radix sort by target, so each target's
+//    in-edges stay in ascending edge id = CSR order;
+//  * gather_generated_csc: presynaptic row = id / fanout (every row with
+//    edges owns [row*F, row*F+F)) and the weight recomputed from the id.
+void launch_gen_indegree(cudaStream_t s, int device, const GenParams &g, uint64_t lo, uint64_t hi,
+                         unsigned long long *indeg);
+void launch_gen_count_shard_u32(cudaStream_t s, int device, const GenParams &g, uint64_t lo, uint64_t hi,
+                                uint32_t *counts);
+void launch_gen_fill_keys(cudaStream_t s, int device, const GenParams &g, uint64_t lo, uint64_t hi,
+                          const uint64_t *row_off, uint32_t *keys, uint64_t *eids);
+cudaError_t sort_pairs_u32_u64(cudaStream_t s, uint32_t *keys, uint32_t *keys_alt, uint64_t *vals,
+                               uint64_t *vals_alt, uint64_t n, int end_bit, void *temp, size_t *temp_bytes,
+                               bool *result_in_alt);
+void launch_gather_generated_csc(cudaStream_t s, int device, const GenParams &g, const uint64_t *eids, uint64_t e,
+                                 void *pre, int pre_bits, float *w_out);
+
 // Per-row out-degrees (u32) from a row_ptr, for event statistics in ordered mode.
 void launch_row_degrees(cudaStream_t s, int device, const uint64_t *row_ptr, uint64_t rows, uint32_t *deg);
 

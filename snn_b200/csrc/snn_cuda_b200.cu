@@ -22,6 +22,7 @@
 #include <nccl.h>
 
 #include <algorithm>
+#include <utility>
 #include <cmath>
 #include <cstdio>
 #include <cstdlib>
@@ -1008,14 +1009,142 @@ snn_status_t generate_full(snn_cuda_context_t *c, const b200::GenParams &g, uint
     return st;
 }
 
+// ORDERED for a device-generated network: build the CSC the ordered pull
+// kernel folds over directly on the device, never materialising the CSR.
+// col_ptr is the scan of the local targets' in-degrees. The edges are then
+// produced in passes over local target ranges sized to the free memory: each
+// pass generates (target - range start, global edge id) pairs in CSR order
+// and stable-radix-sorts them by target, so every target's in-edges keep
+// ascending edge id = CSR order = the serial CPU fold order
+// (src/snn.c:898-906). The presynaptic row is id / fanout and the weight is
+// recomputed from the id, bit-identical to snn_build_random_pool.
+snn_status_t build_generated_csc(snn_cuda_context_t *c, const b200::GenParams &g) {
+    const uint64_t n = g.n, nl = c->n_local, lo = c->lo;
+    const int pre_bytes = c->idx_bits / 8;
+    snn_status_t st;
+    c->binned = false;
+    c->passes = 1;
+    if ((st = dmalloc((void **)&c->d_col_ptr, nl + 1, 8)) != SNN_OK) return st;
+    if ((st = dmalloc((void **)&c->d_deg, n, 4)) != SNN_OK) return st;
+    {
+        unsigned long long *indeg = nullptr;
+        void *tmp = nullptr;
+        size_t tb = 0;
+        if (cudaMalloc(&indeg, (nl + 1) * 8) != cudaSuccess) return SNN_ERR_OUT_OF_MEMORY;
+        cudaMemsetAsync(indeg, 0, (nl + 1) * 8, c->stream);
+        b200::launch_gen_indegree(c->stream, c->device, g, lo, lo + nl, indeg);
+        b200::exclusive_scan_u64(c->stream, (const uint64_t *)indeg, c->d_col_ptr, nl + 1, nullptr, &tb);
+        if (cudaMalloc(&tmp, tb ? tb : 1) != cudaSuccess) {
+            cudaFree(indeg);
+            return SNN_ERR_OUT_OF_MEMORY;
+        }
+        st = cuda_status(b200::exclusive_scan_u64(c->stream, (const uint64_t *)indeg, c->d_col_ptr, nl + 1, tmp, &tb));
+        cudaStreamSynchronize(c->stream);
+        cudaFree(tmp);
+        cudaFree(indeg);
+        if (st != SNN_OK) return st;
+    }
+    b200::launch_gen_count_shard_u32(c->stream, c->device, g, lo, lo + nl, c->d_deg);
+    std::vector<uint64_t> col_ptr;
+    try {
+        col_ptr.resize(nl + 1);
+    } catch (const std::bad_alloc &) {
+        return SNN_ERR_OUT_OF_MEMORY;
+    }
+    if ((st = cuda_status(cudaMemcpy(col_ptr.data(), c->d_col_ptr, (nl + 1) * 8, cudaMemcpyDeviceToHost))) != SNN_OK)
+        return st;
+    const uint64_t e = col_ptr[nl];
+    c->e_local = e;
+    if ((st = dmalloc(&c->d_pre, e, pre_bytes)) != SNN_OK) return st;
+    if ((st = dmalloc((void **)&c->d_cw, e, 4)) != SNN_OK) return st;
+    if (e == 0) return cuda_status(cudaStreamSynchronize(c->stream));
+
+    // Pass size: what fits in the free memory at 24 B per edge (keys and ids,
+    // double-buffered) plus the per-pass row offsets and sort workspace.
+    size_t free_b = 0, total_b = 0;
+    if ((st = cuda_status(cudaMemGetInfo(&free_b, &total_b))) != SNN_OK) return st;
+    const uint64_t fixed = 2 * (n + 1) * 8 + (512ull << 20);
+    if (free_b <= fixed) {
+        set_error("ordered CSC build", "no device memory left for the sort passes");
+        return SNN_ERR_OUT_OF_MEMORY;
+    }
+    uint64_t cap = (free_b - fixed) / 26;
+    // SNN_B200_CSC_PASS_EDGES (environment) caps the pass size, for tests.
+    if (const char *env = std::getenv("SNN_B200_CSC_PASS_EDGES")) {
+        const uint64_t v = std::strtoull(env, nullptr, 10);
+        if (v) cap = std::min(cap, v);
+    }
+    uint64_t max_in = 0;
+    for (uint64_t t = 0; t < nl; ++t) max_in = std::max(max_in, col_ptr[t + 1] - col_ptr[t]);
+    if (cap < max_in) {
+        set_error("ordered CSC build", "one target's in-edges exceed the sort pass memory");
+        return SNN_ERR_OUT_OF_MEMORY;
+    }
+    std::vector<uint64_t> cuts{0};  // pass boundaries in local targets
+    uint64_t pass_max = 0;
+    while (cuts.back() < nl) {
+        const uint64_t a = cuts.back();
+        // Largest b with col_ptr[b] - col_ptr[a] <= cap.
+        const uint64_t b = (uint64_t)(std::upper_bound(col_ptr.begin() + a, col_ptr.end(), col_ptr[a] + cap) -
+                                      col_ptr.begin()) - 1;
+        cuts.push_back(std::max(b, a + 1));
+        pass_max = std::max(pass_max, col_ptr[cuts.back()] - col_ptr[a]);
+    }
+    uint32_t *keys = nullptr, *keys_alt = nullptr;
+    uint64_t *ids = nullptr, *ids_alt = nullptr, *counts = nullptr, *row_off = nullptr;
+    void *temp = nullptr;
+    size_t temp_bytes = 0, scan_bytes = 0;
+    bool alt = false;
+    b200::sort_pairs_u32_u64(c->stream, nullptr, nullptr, nullptr, nullptr, pass_max, 32, nullptr, &temp_bytes,
+                             &alt);
+    b200::exclusive_scan_u64(c->stream, nullptr, nullptr, n + 1, nullptr, &scan_bytes);
+    temp_bytes = std::max(temp_bytes, scan_bytes);
+    if (cudaMalloc(&keys, pass_max * 4) != cudaSuccess || cudaMalloc(&keys_alt, pass_max * 4) != cudaSuccess ||
+        cudaMalloc(&ids, pass_max * 8) != cudaSuccess || cudaMalloc(&ids_alt, pass_max * 8) != cudaSuccess ||
+        cudaMalloc(&counts, (n + 1) * 8) != cudaSuccess || cudaMalloc(&row_off, (n + 1) * 8) != cudaSuccess ||
+        cudaMalloc(&temp, temp_bytes ? temp_bytes : 1) != cudaSuccess) {
+        set_error("ordered CSC build", "out of device memory for the sort passes");
+        st = SNN_ERR_OUT_OF_MEMORY;
+    }
+    for (size_t p = 0; p + 1 < cuts.size() && st == SNN_OK; ++p) {
+        const uint64_t a = cuts[p], b = cuts[p + 1];
+        const uint64_t ep = col_ptr[b] - col_ptr[a];
+        if (ep == 0) continue;
+        cudaMemsetAsync(counts, 0, (n + 1) * 8, c->stream);
+        b200::launch_gen_count_shard(c->stream, c->device, g, lo + a, lo + b, counts);
+        size_t tb = temp_bytes;
+        if ((st = cuda_status(b200::exclusive_scan_u64(c->stream, counts, row_off, n + 1, temp, &tb))) != SNN_OK)
+            break;
+        b200::launch_gen_fill_keys(c->stream, c->device, g, lo + a, lo + b, row_off, keys, ids);
+        int end_bit = 1;
+        while (end_bit < 32 && (1ull << end_bit) < b - a) ++end_bit;
+        tb = temp_bytes;
+        if ((st = cuda_status(b200::sort_pairs_u32_u64(c->stream, keys, keys_alt, ids, ids_alt, ep, end_bit, temp,
+                                                       &tb, &alt))) != SNN_OK)
+            break;
+        b200::launch_gather_generated_csc(c->stream, c->device, g, alt ? ids_alt : ids, ep,
+                                          (char *)c->d_pre + col_ptr[a] * pre_bytes, c->idx_bits,
+                                          c->d_cw + col_ptr[a]);
+        st = cuda_status(cudaGetLastError());
+    }
+    if (st == SNN_OK) st = cuda_status(cudaStreamSynchronize(c->stream));
+    cudaFree(keys);
+    cudaFree(keys_alt);
+    cudaFree(ids);
+    cudaFree(ids_alt);
+    cudaFree(counts);
+    cudaFree(row_off);
+    cudaFree(temp);
+    return st;
+}
+
 snn_status_t finish_generated(snn_cuda_context_t *c, const b200::GenParams &g, uint64_t e_total,
                               snn_cuda_context_t **out) {
     snn_status_t st = SNN_OK;
-    if (c->propagation == SNN_B200_PROPAGATE_ORDERED) st = SNN_ERR_UNSUPPORTED;
-    if (st == SNN_OK) {
-        c->mode = SNN_CUDA_MODE_FULL;
-        st = generate_full(c, g, e_total);
-    }
+    c->mode = SNN_CUDA_MODE_FULL;
+    if (c->propagation != SNN_B200_PROPAGATE_ORDERED) st = generate_full(c, g, e_total);
+    else if (c->n_local > 0xffffffffull) st = SNN_ERR_UNSUPPORTED;  // 32-bit sort keys
+    else st = build_generated_csc(c, g);
     if (st != SNN_OK) {
         free_context(c);
         return st;

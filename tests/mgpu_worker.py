@@ -21,6 +21,7 @@ import torch.distributed as dist  # noqa: E402
 
 import snn_b200 as sb  # noqa: E402
 from oracle.oracle import Oracle, State, baseline_lif, stream_indices_np  # noqa: E402
+from tests._helpers import lif_to_sb  # noqa: E402
 
 
 def main():
@@ -95,9 +96,18 @@ def main():
         ctx.synchronize()
         finals.append((ctx.download_voltage(), ctx.stats()["spikes"]))
         ctx.free()
-    if not (np.array_equal(finals[0][0].view(np.uint32), finals[1][0].view(np.uint32)) and
-            finals[0][1] == finals[1][1]):
-        failures.append(f"rank {rank}: async peer run differs from NCCL run")
+    # Device-generated ORDERED shard (CSC built on the device), peer exchange.
+    ctx = sb.CudaContext.random_pool(n, 120, -0.2, 0.5, 5, lif=lif_to_sb(lif),
+                                     options=options(sb.PROPAGATE_ORDERED, sb.EXCHANGE_PEER))
+    connect(ctx, sb.EXCHANGE_PEER)
+    ctx.run_stream_async(9, 0, 30, count, 20.0)
+    ctx.synchronize()
+    finals.append((ctx.download_voltage(), ctx.stats()["spikes"]))
+    ctx.free()
+    for i, what in ((1, "async peer run differs from NCCL run"), (2, "generated ordered shard differs")):
+        if not (np.array_equal(finals[0][0].view(np.uint32), finals[i][0].view(np.uint32)) and
+                finals[0][1] == finals[i][1]):
+            failures.append(f"rank {rank}: {what}")
     # Device-generated shards tile the host network exactly.
     ctx = sb.CudaContext.random_pool(n, 120, -0.2, 0.5, 5, lif=None, options=options(sb.PROPAGATE_PUSH))
     rp, ci, w = ctx.download_topology()

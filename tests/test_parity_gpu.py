@@ -389,3 +389,44 @@ def test_sparse_streaming_dyadic_bit_exact():
     np.testing.assert_array_equal(bits(cv), bits(gv))
     s = ctx.stats()
     assert s["events"] == int(cr.sum()) * 48
+
+
+@pytest.mark.parametrize("allow_self,pass_edges", [(0, None), (1, "150000")])
+def test_generated_pool_ordered_bit_exact(allow_self, pass_edges, monkeypatch):
+    """snn_b200_create_random_pool with ORDERED propagation: the CSC is built
+    on the device (in-degree scan, stable sort of (target, edge id) pairs, in
+    one pass or several memory-capped passes). General weights: spikes,
+    events and voltages bit-identical to the serial CPU step."""
+    if pass_edges:
+        monkeypatch.setenv("SNN_B200_CSC_PASS_EDGES", pass_edges)
+    lif = baseline_lif()
+    n, f = 20011, 100
+    net = ORC.random_pool(n, f, 0.0, 0.6, 31, allow_self=bool(allow_self), lif=lif)
+    st = State(net)
+    sc, ev, hs, _ = ORC.run_inject_stream(net, st, 7, 0, 50, 200, 20.0)
+    ctx = sb.CudaContext.random_pool(n, f, 0.0, 0.6, 31, allow_self=bool(allow_self), lif=lif_to_sb(lif),
+                                     options=ordered())
+    lay = ctx.layout
+    assert lay["propagation"] == sb.PROPAGATE_ORDERED and lay["local_synapses"] == n * f
+    ctx.run_stream_async(7, 0, 50, 200, 20.0)
+    s = ctx.stats()
+    assert int(sc.sum()) > 1000
+    assert s["spikes"] == int(sc.sum()) and s["events"] == int(ev.sum())
+    np.testing.assert_array_equal(bits(st.voltage()), bits(ctx.download_voltage()))
+
+
+def test_generated_layered_ordered_bit_exact():
+    """snn_b200_create_layered_random with ORDERED propagation (the last
+    layer owns no edges), stepped against the oracle with injection."""
+    lif = baseline_lif()
+    layers = [1500, 1200, 900, 64]
+    net = ORC.layered_random(layers, 300, 0.0, 1.0, 8, lif=lif)
+    ctx = sb.CudaContext.layered_random(layers, 300, 0.0, 1.0, 8, lif=lif_to_sb(lif), options=ordered())
+
+    def inj(t):
+        return stream_indices_np(9, t, 75, 1500), np.full(75, 30.0, np.float32)
+
+    cr, gr, cv, gv = run_pair(net, ctx, 30, inject=inj)
+    assert first_divergence(cr, gr) is None
+    assert cr[:, 1500:].sum() > 0
+    np.testing.assert_array_equal(bits(cv), bits(gv))
