@@ -197,7 +197,7 @@ def workload_config(args, world):
             "synapses": args.neurons * args.fanout, "weights": "U[-0.2,0.5] mV", "seed": args.seed,
             "inject": f"{args.inject_frac * 100:g}% of neurons x {args.inject_value:g} per step",
             "lif": "dt 1 ms, tau 20 ms, rest=reset -65 mV, thr -50 mV, refractory 2", "policy": "FULL",
-            "propagation": "ordered (bit-exact pull)" if args.propagation == "ordered" else f"push ({args.propagation})", "parallelism": f"postsynaptic shards x{world}" + (f", {args.exchange} spike exchange" if world > 1 else ""), "l2": L2_NOTE}
+            "propagation": "ordered (bit-exact push)" if args.propagation == "ordered" else f"push ({args.propagation})", "parallelism": f"postsynaptic shards x{world}" + (f", {args.exchange} spike exchange" if world > 1 else ""), "l2": L2_NOTE}
 
 
 # ------------------------------------------------------------ GPU side ----
@@ -367,22 +367,23 @@ def run_b200(args):
     # algorithmic bytes = 12 per event (8 B col_idx + 4 B weight, the
     # reference's CSR format) + 16 per spiking row (row_ptr pair).
     peak, peak_kind = measured_peak_gbs()
+    # Stats count steps since creation; the timed region ran args.steps.
+    timed = args.steps
     prop_bytes = 12.0 * s["events"] + 16.0 * spikes_total
     kernel_name = "propagate_push_kernel"
     lay = ctx.layout
     if args.propagation == "ordered":
-        # Pull over the CSC: every step reads each in-edge's presynaptic id
-        # (4 B), the weight of each event (4 B) and the col_ptr pair (8 B
-        # per local target).
-        kernel_name = "propagate_pull_kernel"
-        prop_bytes = (4.0 * int(lay["local_synapses"]) + 8.0 * (ctx.local_count + 1)) * s["steps"] + 4.0 * s["events"]
+        # Ordered push: the same algorithmic bytes as the push (the spiking
+        # rows' CSR slices); its kernels (histogram, placement, segmented
+        # sort, fold) are timed together as the propagation.
+        kernel_name = "ordered push (hist + scatter + segmented sort + fold)"
     prop_s = s["propagate_ms"] / 1e3
     achieved = prop_bytes / prop_s / 1e9 if prop_s > 0 else 0.0
     traffic = None
-    if args.propagation not in ("binned", "ordered") and int(lay["index_bits"]) == 32 and s["steps"]:
-        traffic = NCU_DRAM_BYTES_PER_EVENT * s["events"] / s["steps"]
-    step_bytes = (prop_bytes + 25.0 * ctx.local_count * s["steps"]
-                  + 12.0 * count * s["steps"])
+    if args.propagation not in ("binned", "ordered") and int(lay["index_bits"]) == 32 and timed:
+        traffic = NCU_DRAM_BYTES_PER_EVENT * s["events"] / timed
+    step_bytes = (prop_bytes + 25.0 * ctx.local_count * timed
+                  + 12.0 * count * timed)
     launches = int(s["kernel_launches"])
 
     e2e = None
@@ -429,11 +430,11 @@ def run_b200(args):
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": traffic, "peak_kind": peak_kind,
                          "kernel": kernel_name,
-                         "algorithmic_bytes_per_launch": prop_bytes / max(s["steps"], 1),
-                         "kernel_ms_per_launch": s["propagate_ms"] / max(s["steps"], 1)},
+                         "algorithmic_bytes_per_launch": prop_bytes / timed,
+                         "kernel_ms_per_launch": s["propagate_ms"] / timed},
             "step_roofline": {"achieved": step_bytes / (ms / 1e3) / 1e9 if world == 1 else None,
                               "frac": (step_bytes / (ms / 1e3) / 1e9) / peak if world == 1 else None,
-                              "bytes_per_step": step_bytes / max(s["steps"], 1)},
+                              "bytes_per_step": step_bytes / timed},
             "spike_rate": spikes_total / (args.steps * n), "events_per_step": events_total / args.steps,
             "kernel_ms": {"lif": s["lif_ms"] / args.steps, "exchange": s["exchange_ms"] / args.steps,
                           "propagate": s["propagate_ms"] / args.steps},

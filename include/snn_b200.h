@@ -138,9 +138,12 @@ typedef enum snn_b200_propagation {
     /* Push from the compacted spike list with L2-resident fp32 red.add
      * (the reference's accumulation semantics; order not deterministic). */
     SNN_B200_PROPAGATE_PUSH = 0,
-    /* Per-target fold over a device CSC in CSR order (ascending presynaptic
-     * row, ascending edge): bit-identical to the reference's serial CPU step
-     * (src/snn.c:898-906) for any weights. FULL mode only. */
+    /* Every target folds its contributions in CSR order (ascending
+     * presynaptic row, ascending edge): bit-identical to the reference's
+     * serial CPU step (src/snn.c:898-906) for any weights. FULL mode only.
+     * Each step either sorts its events by target (stable radix sort of the
+     * spiking rows' CSR slices; cost ~ events) or, on dense steps when a CSC
+     * fits beside the CSR, pulls over the CSC (cost ~ synapses). */
     SNN_B200_PROPAGATE_ORDERED = 1,
     /* The plain push kernel: one red.global.add.f32 per event. */
     SNN_B200_PROPAGATE_PUSH_ATOMIC = 2,
@@ -194,6 +197,7 @@ typedef struct snn_b200_stats {
     double propagate_ms;       /* device time of the propagation kernels (timing = 1) */
     double lif_ms;             /* device time of the LIF kernels (timing = 1) */
     double exchange_ms;        /* device time of the spike all-gather + compaction (timing = 1) */
+    uint64_t pull_steps;       /* ORDERED: steps that took the pull over the CSC (dense steps) */
 } snn_b200_stats_t;
 
 typedef struct snn_b200_layout {
@@ -207,6 +211,8 @@ typedef struct snn_b200_layout {
     uint64_t device_topology_bytes; /* resident topology (FULL) or chunk buffers (STREAMING) */
     uint32_t binned;                /* 1: push runs the binned shared-memory kernel */
     uint32_t binned_passes;         /* binned: target passes (each with its own CSR slice) */
+    uint32_t ordered_csc;           /* ORDERED: 1 when a CSC is resident (pull for dense steps) */
+    uint32_t reserved;
 } snn_b200_layout_t;
 
 snn_b200_options_t snn_b200_default_options(void);

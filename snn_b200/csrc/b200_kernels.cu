@@ -13,6 +13,7 @@
 
 #include <cub/device/device_radix_sort.cuh>
 #include <cub/device/device_scan.cuh>
+#include <thrust/iterator/transform_iterator.h>
 
 #include <mutex>
 #include <vector>
@@ -382,13 +383,149 @@ __global__ void __launch_bounds__(256) propagate_push_kernel(const TIdx *__restr
     step_epilogue(ctr, parity, count_spikes, count);
 }
 
+// --------------------------------------------------------- ordered push ----
+// Bit-exact propagation driven by the spike list (cost ~ events, not
+// synapses). Every target must fold its contributions in CSR order, i.e. in
+// ascending edge index (src/snn.c:898-906). Each step:
+//  1. ordered_sdeg: sdeg[row] = out-degree of every spiking row;
+//  2. exclusive scan of sdeg over all rows -> eoff[row]: the step's events
+//     numbered densely in CSR order;
+//  3. ordered_gen: every spiking row writes its (target, weight) pairs at
+//     eoff[row] (coalesced runs), so the event array is in CSR order;
+//  4. a stable LSD radix sort by target groups the events per target and
+//     keeps each group in CSR order;
+//  5. ordered_fold: the first event of every target's run folds the run
+//     sequentially onto next[t].
+// A step whose events exceed the buffer capacity runs 3-5 per row range.
+template <typename TIdx>
+__global__ void __launch_bounds__(256) ordered_sdeg_kernel(const TIdx *__restrict__ list, DevCounters *ctr,
+                                                           int parity, const uint64_t *__restrict__ row_ptr,
+                                                           uint32_t *__restrict__ sdeg, int clear) {
+    const uint32_t count = *(volatile uint32_t *)&ctr->list_count[parity];
+    const uint64_t stride = (uint64_t)blockDim.x * gridDim.x;
+    for (uint64_t s = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; s < count; s += stride) {
+        const uint64_t row = (uint64_t)list[s];
+        sdeg[row] = clear ? 0u : (uint32_t)(row_ptr[row + 1] - row_ptr[row]);
+    }
+}
+
+// Warp per spiking row of [row_lo, row_hi): copy the row's (target, weight)
+// pairs to event slots eoff[row] - id_base onwards and clear its sdeg entry.
+// Block 0 adds the step's events (eoff[rows]) and runs the step epilogue when
+// asked.
+template <typename TIdx, typename TCol>
+__global__ void __launch_bounds__(256) ordered_gen_kernel(const TIdx *__restrict__ list, DevCounters *ctr, int parity,
+                                                          uint64_t row_lo, uint64_t row_hi,
+                                                          const uint64_t *__restrict__ row_ptr,
+                                                          const TCol *__restrict__ col, const float *__restrict__ w,
+                                                          const unsigned long long *__restrict__ eoff, uint64_t rows,
+                                                          uint64_t id_base, uint32_t *__restrict__ sdeg,
+                                                          uint32_t *__restrict__ keys, float *__restrict__ vals,
+                                                          int epilogue, int count_spikes) {
+    const uint32_t count = *(volatile uint32_t *)&ctr->list_count[parity];
+    const unsigned lane = lane_id();
+    const uint64_t gwarp = ((uint64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const uint64_t nwarps = ((uint64_t)gridDim.x * blockDim.x) >> 5;
+    for (uint64_t s = gwarp; s < count; s += nwarps) {
+        const uint64_t row = (uint64_t)list[s];
+        if (row < row_lo || row >= row_hi) continue;
+        const uint64_t b = row_ptr[row], e = row_ptr[row + 1];
+        const uint64_t d = eoff[row] - id_base - b;
+        for (uint64_t k = b + lane; k < e; k += 32u) {
+            keys[d + k] = (uint32_t)col[k];
+            vals[d + k] = __ldcs(w + k);
+        }
+        if (lane == 0) sdeg[row] = 0u;
+    }
+    if (epilogue) {
+        if (blockIdx.x == 0 && threadIdx.x == 0) ctr->events += eoff[rows];
+        step_epilogue(ctr, parity, count_spikes, count);
+    }
+}
+
+// Warp per 32-event chunk of the target-sorted array; every run (one
+// target's events) is folded in order onto next[target] by the chunk where
+// it starts. A run shorter than 32 events is walked by the lane at its start
+// (four events per round of loads); a longer run is walked by the whole warp,
+// 32 events per coalesced load, folded through lane shuffles.
+__global__ void __launch_bounds__(256) ordered_fold_kernel(uint64_t events, const uint32_t *__restrict__ keys,
+                                                           const float *__restrict__ vals, float *__restrict__ next) {
+    const unsigned lane = lane_id();
+    const uint64_t gwarp = ((uint64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const uint64_t nwarps = ((uint64_t)gridDim.x * blockDim.x) >> 5;
+    for (uint64_t c0 = gwarp * 32u; c0 < events; c0 += nwarps * 32u) {
+        const uint64_t k = c0 + lane;
+        const uint32_t key = k < events ? keys[k] : 0xffffffffu;
+        const bool start = k < events && (k == 0 || keys[k - 1] != key);
+        const bool longrun = start && k + 31 < events && keys[k + 31] == key;
+        if (start && !longrun) {
+            float acc = next[key];
+            uint64_t j = k;
+            bool more = true;
+            while (more) {
+                uint32_t kk[4];
+                float vv[4];
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    const uint64_t q = j + u;
+                    kk[u] = q < events ? keys[q] : ~key;
+                    vv[u] = q < events ? vals[q] : 0.0f;
+                }
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    if (more && kk[u] == key) acc = __fadd_rn(acc, vv[u]);
+                    else more = false;
+                }
+                j += 4;
+            }
+            next[key] = acc;
+        }
+        uint32_t longs = __ballot_sync(kFull, longrun);
+        while (longs) {
+            const int src = __ffs(longs) - 1;
+            longs &= longs - 1u;
+            const uint32_t t = __shfl_sync(kFull, key, src);
+            float acc = next[t];
+            for (uint64_t j = c0 + (uint64_t)src;; j += 32u) {
+                const uint64_t q = j + lane;
+                const bool in = q < events && keys[q] == t;
+                const float v = in ? vals[q] : 0.0f;
+                const uint32_t m = __ballot_sync(kFull, in);  // a prefix: runs are contiguous
+                const int len = __popc(m);
+                for (int i = 0; i < len; ++i) acc = __fadd_rn(acc, __shfl_sync(kFull, v, i));
+                if (len < 32) break;
+            }
+            if (lane == 0) next[t] = acc;
+        }
+    }
+}
+
 // ----------------------------------------------------------- ordered pull ----
-// Warp per local target. The target's incoming (pre, w) pairs are stored in
-// CSR order (ascending pre, ascending edge). 32 pairs are tested per
-// iteration against the spike bitmap; the spiking ones are folded in lane
-// order, so acc follows exactly the serial CPU fold starting from +0.0f
-// (src/snn.c:898-906). The fold runs redundantly in every lane from warp
-// shuffles; lane 0 stores the sum, overwriting the whole target buffer.
+// Thread per local target. The target's incoming (pre, w) pairs are stored in
+// CSR order (ascending pre, ascending edge); the thread folds the spiking
+// ones in that order, so acc follows exactly the serial CPU fold starting
+// from +0.0f (src/snn.c:898-906), and stores it over the whole target buffer.
+// Each thread streams its own contiguous range four pairs at a time (16-byte
+// loads once aligned), so every lane of every instruction does useful work
+// even when most rows spike. Cost ~ local synapses, whatever the spike
+// count: the ordered push is cheaper unless many rows spike.
+template <typename TPre>
+__device__ __forceinline__ uint32_t spike_bit(const uint32_t *__restrict__ bitmap, TPre p) {
+    return (__ldg(bitmap + ((uint64_t)p >> 5)) >> ((uint32_t)p & 31u)) & 1u;
+}
+
+template <typename TPre>
+__device__ __forceinline__ void load_pre4(const TPre *__restrict__ pre, uint64_t k, uint64_t (&p)[4]) {
+    if constexpr (sizeof(TPre) == 4) {
+        const uint4 v = __ldcs(reinterpret_cast<const uint4 *>(pre + k));
+        p[0] = v.x, p[1] = v.y, p[2] = v.z, p[3] = v.w;
+    } else {
+        const ulonglong2 a = __ldcs(reinterpret_cast<const ulonglong2 *>(pre + k));
+        const ulonglong2 b = __ldcs(reinterpret_cast<const ulonglong2 *>(pre + k + 2));
+        p[0] = a.x, p[1] = a.y, p[2] = b.x, p[3] = b.y;
+    }
+}
+
 template <typename TPre, typename TIdx>
 __global__ void __launch_bounds__(256) propagate_pull_kernel(uint64_t n_local, const uint64_t *__restrict__ col_ptr,
                                                              const TPre *__restrict__ pre,
@@ -397,30 +534,29 @@ __global__ void __launch_bounds__(256) propagate_pull_kernel(uint64_t n_local, c
                                                              float *__restrict__ next, const TIdx *__restrict__ list,
                                                              const uint32_t *__restrict__ out_degree,
                                                              DevCounters *ctr, int parity, int count_spikes) {
-    const unsigned lane = lane_id();
-    const uint64_t gwarp = ((uint64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-    const uint64_t nwarps = ((uint64_t)gridDim.x * blockDim.x) >> 5;
-    for (uint64_t t = gwarp; t < n_local; t += nwarps) {
-        const uint64_t b = col_ptr[t];
+    const uint64_t stride = (uint64_t)blockDim.x * gridDim.x;
+    for (uint64_t t = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; t < n_local; t += stride) {
+        uint64_t k = col_ptr[t];
         const uint64_t e = col_ptr[t + 1];
         float acc = 0.0f;
-        for (uint64_t k0 = b; k0 < e; k0 += 32u) {
-            const uint64_t k = k0 + lane;
-            uint32_t bit = 0;
-            float wv = 0.0f;
-            if (k < e) {
-                const uint64_t p = (uint64_t)pre[k];
-                bit = (__ldg(bitmap + (p >> 5)) >> (p & 31u)) & 1u;
-                if (bit) wv = w[k];
-            }
-            uint32_t m = __ballot_sync(kFull, bit);
-            while (m) {
-                const int j = __ffs(m) - 1;
-                m &= m - 1u;
-                acc = __fadd_rn(acc, __shfl_sync(kFull, wv, j));
+        for (; k < e && (k & 3u); ++k)
+            if (spike_bit(bitmap, pre[k])) acc = __fadd_rn(acc, w[k]);
+        for (; k + 4 <= e; k += 4) {
+            uint64_t p[4];
+            load_pre4(pre, k, p);
+            const uint32_t m = spike_bit(bitmap, p[0]) | spike_bit(bitmap, p[1]) << 1 |
+                               spike_bit(bitmap, p[2]) << 2 | spike_bit(bitmap, p[3]) << 3;
+            if (m) {
+                const float4 wv = __ldcs(reinterpret_cast<const float4 *>(w + k));
+                if (m & 1u) acc = __fadd_rn(acc, wv.x);
+                if (m & 2u) acc = __fadd_rn(acc, wv.y);
+                if (m & 4u) acc = __fadd_rn(acc, wv.z);
+                if (m & 8u) acc = __fadd_rn(acc, wv.w);
             }
         }
-        if (lane == 0) next[t] = acc;
+        for (; k < e; ++k)
+            if (spike_bit(bitmap, pre[k])) acc = __fadd_rn(acc, w[k]);
+        next[t] = acc;
     }
     // Event statistics: out-degree (towards this rank) of every spiking row.
     const uint32_t count = *(volatile uint32_t *)&ctr->list_count[parity];
@@ -695,6 +831,10 @@ __global__ void gather_generated_csc_kernel(GenParams g, const uint64_t *__restr
     }
 }
 
+struct WidenU32 {
+    __host__ __device__ unsigned long long operator()(uint32_t x) const { return x; }
+};
+
 int grid_for(int device, int blocks_per_sm, uint64_t work, uint64_t per_block) {
     const uint64_t need = (work + per_block - 1) / per_block;
     const uint64_t cap = (uint64_t)sm_count(device) * (uint64_t)blocks_per_sm;
@@ -906,6 +1046,52 @@ void launch_gather_generated_csc(cudaStream_t s, int device, const GenParams &g,
     const int grid = grid_for(device, 8, e, 256);
     if (pre_bits == 32) gather_generated_csc_kernel<uint32_t><<<grid, 256, 0, s>>>(g, eids, e, (uint32_t *)pre, w_out);
     else gather_generated_csc_kernel<uint64_t><<<grid, 256, 0, s>>>(g, eids, e, (uint64_t *)pre, w_out);
+}
+
+void launch_ordered_sdeg(cudaStream_t s, int device, const void *list, int idx_bits, DevCounters *ctr, int parity,
+                         uint64_t max_rows, const uint64_t *row_ptr, uint32_t *sdeg, int clear) {
+    const int grid = grid_for(device, 4, max_rows, 256);
+    if (idx_bits == 32)
+        ordered_sdeg_kernel<uint32_t><<<grid, 256, 0, s>>>((const uint32_t *)list, ctr, parity, row_ptr, sdeg, clear);
+    else
+        ordered_sdeg_kernel<uint64_t><<<grid, 256, 0, s>>>((const uint64_t *)list, ctr, parity, row_ptr, sdeg, clear);
+}
+
+void launch_ordered_gen(cudaStream_t s, int device, const void *list, int idx_bits, DevCounters *ctr, int parity,
+                        uint64_t row_lo, uint64_t row_hi, const uint64_t *row_ptr, const void *col, int col_bits,
+                        const float *w, const unsigned long long *eoff, uint64_t rows, uint64_t id_base,
+                        uint32_t *sdeg, uint32_t *keys, float *vals, int epilogue, int count_spikes) {
+    const int grid = sm_count(device) * 8;
+#define B200_OG(TI, TC)                                                                                        \
+    ordered_gen_kernel<TI, TC><<<grid, 256, 0, s>>>((const TI *)list, ctr, parity, row_lo, row_hi, row_ptr,     \
+                                                    (const TC *)col, w, eoff, rows, id_base, sdeg, keys, vals,  \
+                                                    epilogue, count_spikes)
+    if (idx_bits == 32 && col_bits == 32) B200_OG(uint32_t, uint32_t);
+    else if (idx_bits == 32) B200_OG(uint32_t, uint64_t);
+    else if (col_bits == 32) B200_OG(uint64_t, uint32_t);
+    else B200_OG(uint64_t, uint64_t);
+#undef B200_OG
+}
+
+cudaError_t sort_pairs_u32_f32(cudaStream_t s, uint32_t *keys, uint32_t *keys_alt, float *vals, float *vals_alt,
+                               uint64_t n, int end_bit, void *temp, size_t *temp_bytes, bool *result_in_alt) {
+    cub::DoubleBuffer<uint32_t> k(keys, keys_alt);
+    cub::DoubleBuffer<float> v(vals, vals_alt);
+    const cudaError_t e = cub::DeviceRadixSort::SortPairs(temp, *temp_bytes, k, v, (int64_t)n, 0, end_bit, s);
+    if (temp != nullptr) *result_in_alt = k.Current() != keys;
+    return e;
+}
+
+void launch_ordered_fold(cudaStream_t s, int device, uint64_t events, const uint32_t *keys, const float *vals,
+                         float *next) {
+    ordered_fold_kernel<<<grid_for(device, 8, events, 256), 256, 0, s>>>(events, keys, vals, next);
+}
+
+cudaError_t scan_degrees_u64(cudaStream_t s, const uint32_t *in, unsigned long long *out, uint64_t n, void *temp,
+                             size_t *temp_bytes) {
+    // u32 degrees summed in 64 bits.
+    thrust::transform_iterator<WidenU32, const uint32_t *, unsigned long long> it(in, WidenU32());
+    return cub::DeviceScan::ExclusiveSum(temp, *temp_bytes, it, out, (int64_t)n, s);
 }
 
 void launch_row_degrees(cudaStream_t s, int device, const uint64_t *row_ptr, uint64_t rows, uint32_t *deg) {

@@ -196,6 +196,23 @@ cudaError_t sort_pairs_u32_u64(cudaStream_t s, uint32_t *keys, uint32_t *keys_al
 void launch_gather_generated_csc(cudaStream_t s, int device, const GenParams &g, const uint64_t *eids, uint64_t e,
                                  void *pre, int pre_bits, float *w_out);
 
+// Ordered push (bit-exact, event-driven), in step order: sdeg of the
+// spiking rows -> scan_degrees_u64 (eoff, rows+1 entries) -> per row range:
+// gen (events in CSR order) -> sort_pairs_u32_f32 (stable, by target) ->
+// fold.
+void launch_ordered_sdeg(cudaStream_t s, int device, const void *list, int idx_bits, DevCounters *ctr, int parity,
+                         uint64_t max_rows, const uint64_t *row_ptr, uint32_t *sdeg, int clear);
+cudaError_t scan_degrees_u64(cudaStream_t s, const uint32_t *in, unsigned long long *out, uint64_t n, void *temp,
+                             size_t *temp_bytes);
+void launch_ordered_gen(cudaStream_t s, int device, const void *list, int idx_bits, DevCounters *ctr, int parity,
+                        uint64_t row_lo, uint64_t row_hi, const uint64_t *row_ptr, const void *col, int col_bits,
+                        const float *w, const unsigned long long *eoff, uint64_t rows, uint64_t id_base,
+                        uint32_t *sdeg, uint32_t *keys, float *vals, int epilogue, int count_spikes);
+cudaError_t sort_pairs_u32_f32(cudaStream_t s, uint32_t *keys, uint32_t *keys_alt, float *vals, float *vals_alt,
+                               uint64_t n, int end_bit, void *temp, size_t *temp_bytes, bool *result_in_alt);
+void launch_ordered_fold(cudaStream_t s, int device, uint64_t events, const uint32_t *keys, const float *vals,
+                         float *next);
+
 // Per-row out-degrees (u32) from a row_ptr, for event statistics in ordered mode.
 void launch_row_degrees(cudaStream_t s, int device, const uint64_t *row_ptr, uint64_t rows, uint32_t *deg);
 

@@ -22,6 +22,7 @@
 #include <nccl.h>
 
 #include <algorithm>
+#include <array>
 #include <utility>
 #include <cmath>
 #include <cstdio>
@@ -137,6 +138,21 @@ struct snn_cuda_context {
     void *d_pre = nullptr;
     float *d_cw = nullptr;
     uint32_t *d_deg = nullptr;
+    // Ordered push (bit-exact, event-driven; the default ORDERED kernel):
+    // per-row spiking degrees and event offsets over all rows, and the
+    // double-buffered (target, weight) event arrays of ocap entries.
+    bool opull = false;    // SNN_B200_ORDERED_PULL: always the pull over a CSC (no CSR)
+    bool has_csc = false;  // ordered push with the CSC as well: dense steps pull
+    uint64_t pull_div = 10;  // pull when a step's events exceed local synapses / pull_div
+    uint64_t pull_steps = 0;
+    uint32_t *d_sdeg = nullptr;
+    unsigned long long *d_eoff = nullptr;
+    uint32_t *d_okeys[2] = {nullptr, nullptr};
+    float *d_ovals[2] = {nullptr, nullptr};
+    uint64_t ocap = 0;
+    void *d_otemp = nullptr;
+    size_t otemp_bytes = 0;
+    unsigned long long *h_ototal = nullptr;
 
     std::vector<StreamChunk> chunks;
     uint64_t slot_rows = 0, slot_edges = 0, slot_stride = 0;
@@ -154,6 +170,11 @@ struct snn_cuda_context {
     float *h_inj_val = nullptr;
     uint64_t h_inj_cap = 0;
     cudaEvent_t ev_inj = nullptr;
+    // snn_cuda_step on FULL contexts: the spike download runs on its own
+    // stream as soon as the LIF kernel is done, overlapping propagation.
+    cudaStream_t spk_stream = nullptr;
+    cudaEvent_t ev_lif = nullptr, ev_spk = nullptr;
+    uint8_t *spk_dst = nullptr;  // set for the duration of one snn_cuda_step
 
     ncclComm_t comm = nullptr;
     // Peer exchange (SNN_B200_EXCHANGE_PEER): [2 parities][bitmap_words] u32,
@@ -239,13 +260,15 @@ void free_context(snn_cuda_context_t *c) {
     if (c->device >= 0) cudaSetDevice(c->device);
     if (c->stream) cudaStreamSynchronize(c->stream);
     if (c->copy_stream) cudaStreamSynchronize(c->copy_stream);
+    if (c->spk_stream) cudaStreamSynchronize(c->spk_stream);
     report_binned_profile(c);
     if (c->comm) ncclCommDestroy(c->comm);
     for (uint32_t r = 0; r < b200::kMaxPeers; ++r)
         if (c->peer_ipc[r]) cudaIpcCloseMemHandle(c->peer_x[r]);
     if (c->d_xbuf) cudaFree(c->d_xbuf);
     void *dev[] = {c->d_v, c->d_cur_pair, c->d_ext, c->d_refr, c->d_spikes, c->d_ws, c->d_row_ptr, c->d_col,
-                   c->d_w, c->d_col_ptr, c->d_pre, c->d_cw, c->d_deg, c->d_chunk_row, c->d_chunk_col,
+                   c->d_w, c->d_col_ptr, c->d_pre, c->d_cw, c->d_deg, c->d_sdeg, c->d_eoff, c->d_okeys[0], c->d_okeys[1], c->d_ovals[0], c->d_ovals[1], c->d_otemp,
+                   c->d_chunk_row, c->d_chunk_col,
                    c->d_chunk_w, c->d_inj_idx, c->d_inj_val, c->d_bin_mem};
     for (void *p : dev)
         if (p) cudaFree(p);
@@ -255,6 +278,7 @@ void free_context(snn_cuda_context_t *c) {
         if (c->d_pw[p]) cudaFree(c->d_pw[p]);
     }
     if (c->h_err) cudaFreeHost(c->h_err);
+    if (c->h_ototal) cudaFreeHost(c->h_ototal);
     if (c->h_inj_idx) cudaFreeHost(c->h_inj_idx);
     if (c->h_inj_val) cudaFreeHost(c->h_inj_val);
     for (const void *p : c->registered)
@@ -264,6 +288,9 @@ void free_context(snn_cuda_context_t *c) {
         if (c->ev_free[i]) cudaEventDestroy(c->ev_free[i]);
     }
     if (c->ev_inj) cudaEventDestroy(c->ev_inj);
+    if (c->ev_lif) cudaEventDestroy(c->ev_lif);
+    if (c->ev_spk) cudaEventDestroy(c->ev_spk);
+    if (c->spk_stream) cudaStreamDestroy(c->spk_stream);
     for (auto *v : {&c->pending, &c->pool})
         for (auto &g : *v)
             for (auto e : g.ev) cudaEventDestroy(e);
@@ -298,6 +325,7 @@ snn_status_t apply_options(snn_cuda_context_t *c, uint64_t n, const snn_b200_opt
         return SNN_ERR_INVALID_ARGUMENT;
     c->streaming = o.streaming;
     c->propagation = o.propagation;
+    c->opull = o.propagation == SNN_B200_PROPAGATE_ORDERED && std::getenv("SNN_B200_ORDERED_PULL") != nullptr;
     c->world = o.world_size;
     c->rank = o.rank;
     c->timing = o.timing;
@@ -516,6 +544,127 @@ snn_status_t upload_full_push(snn_cuda_context_t *c, const snn_network_t *net) {
     }
     if (st == SNN_OK) st = finish_binned(c);
     return st;
+}
+
+// Radix bits that cover the local target ids.
+int target_bits(const snn_cuda_context_t *c) {
+    int bits = 1;
+    while (bits < 32 && (1ull << bits) < c->n_local) ++bits;
+    return bits;
+}
+
+// Ordered push buffers, after the push CSR exists. The event capacity (events
+// per sort) is bounded by half of the free device memory at 16 B per event
+// (keys and weights, double-buffered) and by the local synapse count.
+snn_status_t setup_ordered_push(snn_cuda_context_t *c) {
+    const uint64_t n = c->n_global, nl = c->n_local;
+    auto fail = [&](const char *what) {
+        set_error("ordered push setup", what);
+        return SNN_ERR_OUT_OF_MEMORY;
+    };
+    if (nl > 0xffffffffull) return SNN_ERR_UNSUPPORTED;  // 32-bit sort keys
+    if (cudaMalloc(&c->d_sdeg, (n + 1) * 4) != cudaSuccess || cudaMalloc(&c->d_eoff, (n + 1) * 8) != cudaSuccess)
+        return fail("out of device memory for the per-row arrays");
+    if (cudaMallocHost(&c->h_ototal, 8) != cudaSuccess) return fail("out of pinned memory");
+    cudaMemsetAsync(c->d_sdeg, 0, (n + 1) * 4, c->stream);
+    // Largest row: one row's events must fit one sort.
+    std::vector<uint64_t> rp;
+    try {
+        rp.resize(n + 1);
+    } catch (const std::bad_alloc &) {
+        return SNN_ERR_OUT_OF_MEMORY;
+    }
+    if (cudaMemcpy(rp.data(), c->d_row_ptr, (n + 1) * 8, cudaMemcpyDeviceToHost) != cudaSuccess) return SNN_ERR_CUDA;
+    uint64_t max_deg = 0;
+    for (uint64_t i = 0; i < n; ++i) max_deg = std::max(max_deg, rp[i + 1] - rp[i]);
+    size_t free_b = 0, total_b = 0;
+    if (cudaMemGetInfo(&free_b, &total_b) != cudaSuccess) return SNN_ERR_CUDA;
+    uint64_t cap = std::min<uint64_t>(c->e_local, (uint64_t)(free_b / 2) / 16);
+    if (const char *env = std::getenv("SNN_B200_ORDERED_CAP")) {  // tests: force the multi-range path
+        const uint64_t v = std::strtoull(env, nullptr, 10);
+        if (v) cap = std::min(cap, v);
+    }
+    if (c->e_local && cap < std::max<uint64_t>(max_deg, 1)) return fail("a row's events exceed the event capacity");
+    c->ocap = c->e_local ? cap : 0;
+    if (c->ocap) {
+        for (int i = 0; i < 2; ++i)
+            if (cudaMalloc(&c->d_okeys[i], c->ocap * 4) != cudaSuccess ||
+                cudaMalloc(&c->d_ovals[i], c->ocap * 4) != cudaSuccess)
+                return fail("out of device memory for the event arrays");
+    }
+    size_t a = 0, b = 0;
+    bool alt = false;
+    b200::scan_degrees_u64(c->stream, nullptr, nullptr, n + 1, nullptr, &a);
+    if (c->ocap)
+        b200::sort_pairs_u32_f32(c->stream, nullptr, nullptr, nullptr, nullptr, c->ocap, target_bits(c), nullptr, &b,
+                                 &alt);
+    c->otemp_bytes = std::max({a, b, (size_t)256});
+    if (cudaMalloc(&c->d_otemp, c->otemp_bytes) != cudaSuccess) return fail("out of device memory for sort scratch");
+    return cuda_status(cudaStreamSynchronize(c->stream));
+}
+
+// One ordered push propagation (b200_kernels.cu describes the steps); one
+// host round trip reads the step's event count to size the sort.
+snn_status_t ordered_push_step(snn_cuda_context_t *c, int parity, float *next, bool sharded,
+                               const uint32_t *bitmap) {
+    const uint64_t n = c->n_global;
+    snn_status_t st;
+    b200::launch_ordered_sdeg(c->stream, c->device, c->d_list, c->idx_bits, c->d_ctr, parity, n, c->d_row_ptr,
+                              c->d_sdeg, 0);
+    size_t tb = c->otemp_bytes;
+    if ((st = cuda_status(b200::scan_degrees_u64(c->stream, c->d_sdeg, c->d_eoff, n + 1, c->d_otemp, &tb))) != SNN_OK)
+        return st;
+    if ((st = cuda_status(cudaMemcpyAsync(c->h_ototal, c->d_eoff + n, 8, cudaMemcpyDeviceToHost, c->stream))) !=
+        SNN_OK)
+        return st;
+    if ((st = cuda_status(cudaStreamSynchronize(c->stream))) != SNN_OK) return st;
+    const uint64_t total = *c->h_ototal;
+    if (c->has_csc && c->pull_div && total > c->e_local / c->pull_div) {
+        // Most rows spike: the pull over the CSC reads every synapse once,
+        // cheaper than sorting this many events.
+        b200::launch_ordered_sdeg(c->stream, c->device, c->d_list, c->idx_bits, c->d_ctr, parity, n, c->d_row_ptr,
+                                  c->d_sdeg, 1);
+        b200::launch_propagate_pull(c->stream, c->device, c->n_local, c->d_col_ptr, c->d_pre, c->idx_bits, c->d_cw,
+                                    bitmap, next, c->d_list, c->idx_bits, c->d_deg, c->d_ctr, parity, !sharded);
+        c->launches += 2;
+        c->pull_steps++;
+        return SNN_OK;
+    }
+    // Row ranges of at most ocap events each (one range unless the step is huge).
+    std::vector<std::array<uint64_t, 3>> ranges;  // row_lo, row_hi, first event id
+    if (total <= c->ocap) {
+        ranges.push_back({0, n, 0});
+    } else {
+        std::vector<unsigned long long> eo(n + 1);
+        if ((st = cuda_status(cudaMemcpy(eo.data(), c->d_eoff, (n + 1) * 8, cudaMemcpyDeviceToHost))) != SNN_OK)
+            return st;
+        uint64_t r0 = 0;
+        while (r0 < n) {
+            uint64_t r1 = (uint64_t)(std::upper_bound(eo.begin() + r0, eo.end(), eo[r0] + c->ocap) - eo.begin()) - 1;
+            if (r1 <= r0) r1 = r0 + 1;  // cannot happen: ocap >= the largest row
+            ranges.push_back({r0, r1, eo[r0]});
+            r0 = r1;
+        }
+    }
+    for (size_t i = 0; i < ranges.size(); ++i) {
+        const uint64_t r0 = ranges[i][0], r1 = ranges[i][1], base = ranges[i][2];
+        const uint64_t events = (i + 1 < ranges.size() ? ranges[i + 1][2] : total) - base;
+        b200::launch_ordered_gen(c->stream, c->device, c->d_list, c->idx_bits, c->d_ctr, parity, r0, r1, c->d_row_ptr,
+                                 c->d_col, c->col_bits, c->d_w, c->d_eoff, n, base, c->d_sdeg, c->d_okeys[0],
+                                 c->d_ovals[0], i + 1 == ranges.size(), !sharded);
+        c->launches++;
+        if (!events) continue;
+        tb = c->otemp_bytes;
+        bool alt = false;
+        if ((st = cuda_status(b200::sort_pairs_u32_f32(c->stream, c->d_okeys[0], c->d_okeys[1], c->d_ovals[0],
+                                                       c->d_ovals[1], events, target_bits(c), c->d_otemp, &tb,
+                                                       &alt))) != SNN_OK)
+            return st;
+        b200::launch_ordered_fold(c->stream, c->device, events, c->d_okeys[alt ? 1 : 0], c->d_ovals[alt ? 1 : 0],
+                                  next);
+        c->launches++;
+    }
+    return SNN_OK;
 }
 
 // FULL ordered topology: a CSC of the rank's targets built on the host with a
@@ -825,6 +974,17 @@ snn_status_t enqueue_step(snn_cuda_context_t *c, bool has_ext) {
     snn_status_t st = check_launch(c);
     if (st != SNN_OK) return st;
     timing_mark(c, tg, 1);
+    if (c->spk_dst != nullptr) {
+        // The spikes are final once LIF is done; download them while the
+        // propagation runs. The main stream waits for the copy at the end of
+        // the step (the next LIF overwrites d_spikes).
+        cudaEventRecord(c->ev_lif, c->stream);
+        cudaStreamWaitEvent(c->spk_stream, c->ev_lif, 0);
+        if (cudaMemcpyAsync(c->spk_dst, c->d_spikes, c->n_local, cudaMemcpyDeviceToHost, c->spk_stream) !=
+            cudaSuccess)
+            return SNN_ERR_CUDA;
+        cudaEventRecord(c->ev_spk, c->spk_stream);
+    }
     if (peer) {
         // LIF already stored this rank's words into every rank's buffer and
         // raised its flag; the compaction waits for all flags of this step.
@@ -848,10 +1008,12 @@ snn_status_t enqueue_step(snn_cuda_context_t *c, bool has_ext) {
     }
     timing_mark(c, tg, 2);
     if (c->mode == SNN_CUDA_MODE_FULL) {
-        if (c->propagation == SNN_B200_PROPAGATE_ORDERED)
+        if (c->propagation == SNN_B200_PROPAGATE_ORDERED && !c->opull) {
+            if ((st = ordered_push_step(c, parity, next, sharded, peer ? xbitmap : c->d_bitmap)) != SNN_OK) return st;
+        } else if (c->propagation == SNN_B200_PROPAGATE_ORDERED)
             b200::launch_propagate_pull(c->stream, c->device, c->n_local, c->d_col_ptr, c->d_pre, c->idx_bits,
-                                        c->d_cw, peer ? xbitmap : c->d_bitmap, next, c->d_list, c->idx_bits, c->d_deg, c->d_ctr,
-                                        parity, !sharded);
+                                        c->d_cw, peer ? xbitmap : c->d_bitmap, next, c->d_list, c->idx_bits,
+                                        c->d_deg, c->d_ctr, parity, !sharded);
         else if (c->binned) {
             const cudaError_t e = b200::launch_propagate_binned(c->stream, c->d_list, c->idx_bits, next, c->d_ctr,
                                                                 parity, !sharded, c->bin);
@@ -899,6 +1061,7 @@ snn_status_t enqueue_step(snn_cuda_context_t *c, bool has_ext) {
             cudaEventRecord(c->ev_free[s], c->stream);
         }
     }
+    if (c->spk_dst != nullptr) cudaStreamWaitEvent(c->stream, c->ev_spk, 0);
     timing_mark(c, tg, 3);
     c->cur ^= 1;
     c->step++;
@@ -1138,12 +1301,38 @@ snn_status_t build_generated_csc(snn_cuda_context_t *c, const b200::GenParams &g
     return st;
 }
 
+// ORDERED contexts keep a CSC beside the push CSR when the device has room for
+// it (and for a usable event buffer): dense steps then take the pull.
+// SNN_B200_ORDERED_PULL_DIV (environment) sets the density threshold
+// (events > local synapses / div; 0 keeps every step on the ordered push).
+snn_status_t add_ordered_csc(snn_cuda_context_t *c, const snn_network_t *net, const b200::GenParams *g) {
+    if (const char *env = std::getenv("SNN_B200_ORDERED_PULL_DIV")) c->pull_div = std::strtoull(env, nullptr, 10);
+    if (c->pull_div == 0 || c->e_local == 0) return SNN_OK;
+    size_t free_b = 0, total_b = 0;
+    if (cudaMemGetInfo(&free_b, &total_b) != cudaSuccess) return SNN_ERR_CUDA;
+    const uint64_t csc = (c->n_local + 1) * 8 + c->e_local * (c->idx_bits / 8 + 4) + c->n_global * 4;
+    const uint64_t reserve = (2 * (c->n_global + 1) * 8) + (4ull << 30);  // build scratch + event buffers
+    if (csc + reserve > free_b) return SNN_OK;  // no room: every step takes the ordered push
+    const uint64_t e_push = c->e_local;
+    snn_status_t st = net ? upload_full_ordered(c, net) : build_generated_csc(c, *g);
+    if (st != SNN_OK) return st;
+    if (c->e_local != e_push) {
+        set_error("ordered setup", "CSC and CSR synapse counts differ");
+        return SNN_ERR_CUDA;
+    }
+    c->has_csc = true;
+    return SNN_OK;
+}
+
 snn_status_t finish_generated(snn_cuda_context_t *c, const b200::GenParams &g, uint64_t e_total,
                               snn_cuda_context_t **out) {
     snn_status_t st = SNN_OK;
     c->mode = SNN_CUDA_MODE_FULL;
     if (c->propagation != SNN_B200_PROPAGATE_ORDERED) st = generate_full(c, g, e_total);
-    else if (c->n_local > 0xffffffffull) st = SNN_ERR_UNSUPPORTED;  // 32-bit sort keys
+    else if (!c->opull) {
+        if ((st = generate_full(c, g, e_total)) == SNN_OK && (st = add_ordered_csc(c, nullptr, &g)) == SNN_OK)
+            st = setup_ordered_push(c);
+    } else if (c->n_local > 0xffffffffull) st = SNN_ERR_UNSUPPORTED;  // 32-bit sort keys
     else st = build_generated_csc(c, g);
     if (st != SNN_OK) {
         free_context(c);
@@ -1206,8 +1395,10 @@ snn_status_t snn_b200_create(const snn_network_t *network, const snn_cuda_config
     const bool full_only = c->world > 1 || c->propagation == SNN_B200_PROPAGATE_ORDERED;
     if (full_only || (!cfg.prefer_streaming && full_push_bytes(c, network->synapse_count) <= env.budget)) {
         c->mode = SNN_CUDA_MODE_FULL;
-        st = c->propagation == SNN_B200_PROPAGATE_ORDERED ? upload_full_ordered(c, network)
-                                                          : upload_full_push(c, network);
+        if (c->propagation != SNN_B200_PROPAGATE_ORDERED) st = upload_full_push(c, network);
+        else if (c->opull) st = upload_full_ordered(c, network);
+        else if ((st = upload_full_push(c, network)) == SNN_OK && (st = add_ordered_csc(c, network, nullptr)) == SNN_OK)
+            st = setup_ordered_push(c);
     } else {
         c->mode = SNN_CUDA_MODE_STREAMING;
         c->e_local = network->synapse_count;
@@ -1298,12 +1489,30 @@ snn_status_t snn_cuda_step(snn_cuda_context_t *c, const float *host_external_cur
             cudaSuccess)
             return SNN_ERR_CUDA;
     }
-    if ((st = enqueue_step(c, host_external_current != nullptr)) != SNN_OK) return st;
+    // FULL contexts download the spikes inside the step (overlapping the
+    // propagation); the fault seam of that copy keeps its place below.
+    const bool early = host_out_spikes != nullptr && c->n_local != 0 && c->mode == SNN_CUDA_MODE_FULL;
+    if (early && c->spk_stream == nullptr) {
+        if (cudaStreamCreateWithFlags(&c->spk_stream, cudaStreamNonBlocking) != cudaSuccess ||
+            cudaEventCreateWithFlags(&c->ev_lif, cudaEventDisableTiming) != cudaSuccess ||
+            cudaEventCreateWithFlags(&c->ev_spk, cudaEventDisableTiming) != cudaSuccess)
+            return SNN_ERR_CUDA;
+    }
+    c->spk_dst = early ? host_out_spikes : nullptr;
+    st = enqueue_step(c, host_external_current != nullptr);
+    c->spk_dst = nullptr;
+    if (st != SNN_OK) {
+        if (early) cudaStreamSynchronize(c->spk_stream);  // no copy lands after the return
+        return st;
+    }
     if (c->binned || c->exchange == SNN_B200_EXCHANGE_PEER) queue_error_check(c);
     if (host_out_spikes != nullptr && c->n_local != 0) {
-        if (seam_fail()) return SNN_ERR_CUDA;
-        if (cudaMemcpyAsync(host_out_spikes, c->d_spikes, c->n_local, cudaMemcpyDeviceToHost, c->stream) !=
-            cudaSuccess)
+        if (seam_fail()) {
+            cudaStreamSynchronize(c->stream);
+            return SNN_ERR_CUDA;
+        }
+        if (!early && cudaMemcpyAsync(host_out_spikes, c->d_spikes, c->n_local, cudaMemcpyDeviceToHost,
+                                      c->stream) != cudaSuccess)
             return SNN_ERR_CUDA;
     }
     return error_after_sync(c, cuda_status(cudaStreamSynchronize(c->stream)));
@@ -1533,6 +1742,7 @@ snn_status_t snn_b200_get_stats(snn_cuda_context_t *c, snn_b200_stats_t *out) {
     out->propagate_ms = c->t_prop;
     out->lif_ms = c->t_lif;
     out->exchange_ms = c->t_exchange;
+    out->pull_steps = c->pull_steps;
     return SNN_OK;
 }
 
@@ -1546,6 +1756,7 @@ snn_status_t snn_b200_reset_stats(snn_cuda_context_t *c) {
     d.events = 0;
     if (cudaMemcpy(c->d_ctr, &d, sizeof(d), cudaMemcpyHostToDevice) != cudaSuccess) return SNN_ERR_CUDA;
     c->launches = 0;
+    c->pull_steps = 0;
     c->t_step = c->t_lif = c->t_exchange = c->t_prop = 0;
     return SNN_OK;
 }
@@ -1563,12 +1774,15 @@ snn_status_t snn_b200_get_layout(const snn_cuda_context_t *c, snn_b200_layout_t 
         out->device_topology_bytes = (c->n_global + 1) * 8;
     else if (c->mode == SNN_CUDA_MODE_STREAMING)
         out->device_topology_bytes = 2 * ((c->slot_rows + 1) * 8 + c->slot_edges * 12);
-    else if (c->propagation == SNN_B200_PROPAGATE_ORDERED)
-        out->device_topology_bytes = (c->n_local + 1) * 8 + c->e_local * (c->idx_bits / 8 + 4) + c->n_global * 4;
+    else if (c->opull || c->has_csc)
+        out->device_topology_bytes = (c->has_csc ? (c->n_global + 1) * 8 + c->e_local * (c->col_bits / 8 + 4) : 0) +
+                                     (c->n_local + 1) * 8 + c->e_local * (c->idx_bits / 8 + 4) + c->n_global * 4;
     else
         out->device_topology_bytes = (c->n_global + 1) * 8 + c->e_local * (c->col_bits / 8 + 4);
     out->binned = c->binned ? 1u : 0u;
     out->binned_passes = c->binned ? c->bin.passes : 0u;
+    out->ordered_csc = (c->opull || c->has_csc) ? 1u : 0u;
+    out->reserved = 0u;
     return SNN_OK;
 }
 

@@ -391,14 +391,20 @@ def test_sparse_streaming_dyadic_bit_exact():
     assert s["events"] == int(cr.sum()) * 48
 
 
-@pytest.mark.parametrize("allow_self,pass_edges", [(0, None), (1, "150000")])
-def test_generated_pool_ordered_bit_exact(allow_self, pass_edges, monkeypatch):
-    """snn_b200_create_random_pool with ORDERED propagation: the CSC is built
-    on the device (in-degree scan, stable sort of (target, edge id) pairs, in
-    one pass or several memory-capped passes). General weights: spikes,
-    events and voltages bit-identical to the serial CPU step."""
-    if pass_edges:
-        monkeypatch.setenv("SNN_B200_CSC_PASS_EDGES", pass_edges)
+@pytest.mark.parametrize("allow_self,env", [
+    (0, {}),                                   # ordered push, one bucket pass per step
+    (1, {"SNN_B200_ORDERED_CAP": "3000"}),     # ordered push, several row ranges per step
+    (0, {"SNN_B200_ORDERED_PULL": "1"}),       # pull over a device-built CSC
+    (1, {"SNN_B200_ORDERED_PULL": "1", "SNN_B200_CSC_PASS_EDGES": "150000"}),  # CSC built in several passes
+])
+def test_generated_pool_ordered_bit_exact(allow_self, env, monkeypatch):
+    """snn_b200_create_random_pool with ORDERED propagation, through both
+    bit-exact kernels: the event-driven ordered push (bucket by target, sort
+    by edge index, sequential fold) and the pull over a CSC built on the
+    device. General weights: spikes, events and voltages bit-identical to the
+    serial CPU step."""
+    for k, v in env.items():
+        monkeypatch.setenv(k, v)
     lif = baseline_lif()
     n, f = 20011, 100
     net = ORC.random_pool(n, f, 0.0, 0.6, 31, allow_self=bool(allow_self), lif=lif)
@@ -430,3 +436,29 @@ def test_generated_layered_ordered_bit_exact():
     assert first_divergence(cr, gr) is None
     assert cr[:, 1500:].sum() > 0
     np.testing.assert_array_equal(bits(cv), bits(gv))
+
+
+@pytest.mark.parametrize("cap,pull_div", [(None, "0"), ("20000", "0"), (None, None)])
+def test_ordered_dense_bursts_bit_exact(cap, pull_div, monkeypatch):
+    """Dense recurrent pool (in-degree ~1500) with strong drive: most rows
+    spike together, so every target's run of events is hundreds long (the
+    warp-cooperative fold); with a small event capacity a step is split into
+    many row ranges; with the default density threshold the dense steps take
+    the pull over the CSC. Bit-identical to the serial CPU step."""
+    if cap:
+        monkeypatch.setenv("SNN_B200_ORDERED_CAP", cap)
+    if pull_div:
+        monkeypatch.setenv("SNN_B200_ORDERED_PULL_DIV", pull_div)
+    lif = default_lif(v_rest=0.0, v_reset=0.0, v_threshold=1.0, input_scale=1.0, refractory_steps=1)
+    n = 3001
+    net = ORC.random_pool(n, 1500, -0.05, 0.1, 12, allow_self=True, lif=lif)
+    ctx = sb.CudaContext.create(net, None, ordered())
+    rng = np.random.default_rng(8)
+    frames = [(rng.random(n) < 0.6).astype(np.float32) * np.float32(1.5) for _ in range(3)]
+    cr, gr, cv, gv = run_pair(net, ctx, 12, ext=lambda t: frames[t % 3])
+    assert first_divergence(cr, gr) is None
+    assert cr.sum(axis=1).max() > n // 2
+    np.testing.assert_array_equal(bits(cv), bits(gv))
+    assert ctx.layout["ordered_csc"] == (0 if pull_div == "0" else 1)
+    pulls = ctx.stats()["pull_steps"]
+    assert (pulls > 0) if pull_div is None else (pulls == 0)
