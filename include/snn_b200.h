@@ -186,6 +186,11 @@ typedef struct snn_b200_options {
     int timing;             /* 1: record per-step device timings (snn_b200_stats) */
     int exchange;           /* snn_b200_exchange_t: how sharded ranks share spikes */
     int streaming;          /* snn_b200_streaming_t: how a STREAMING context reads the host CSR */
+    uint32_t batch;         /* independent network states sharing the topology (0 or 1 = one).
+                             * With batch B every per-neuron argument covers B x n neurons,
+                             * sample b owning [b*n, (b+1)*n): inject indices, external
+                             * current, spikes and voltages. FULL, world_size 1, PUSH /
+                             * PUSH_ATOMIC / ORDERED (event-driven) only. */
 } snn_b200_options_t;
 
 typedef struct snn_b200_stats {
@@ -212,7 +217,8 @@ typedef struct snn_b200_layout {
     uint32_t binned;                /* 1: push runs the binned shared-memory kernel */
     uint32_t binned_passes;         /* binned: target passes (each with its own CSR slice) */
     uint32_t ordered_csc;           /* ORDERED: 1 when a CSC is resident (pull for dense steps) */
-    uint32_t reserved;
+    uint32_t batch;                 /* states sharing the topology (neuron_count = batch x rows) */
+    snn_size_t topology_rows;       /* rows of the shared topology (n of the network) */
 } snn_b200_layout_t;
 
 snn_b200_options_t snn_b200_default_options(void);

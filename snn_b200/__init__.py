@@ -80,7 +80,7 @@ class Options(C.Structure):
     """snn_b200_options_t (include/snn_b200.h)."""
     _fields_ = [("propagation", C.c_int), ("device", C.c_int), ("index_width", C.c_int),
                 ("rank", C.c_uint32), ("world_size", C.c_uint32), ("nccl_id", P), ("timing", C.c_int),
-                ("exchange", C.c_int), ("streaming", C.c_int)]
+                ("exchange", C.c_int), ("streaming", C.c_int), ("batch", C.c_uint32)]
 
 
 class Stats(C.Structure):
@@ -96,7 +96,7 @@ class Layout(C.Structure):
     _fields_ = [("neuron_count", u64), ("local_begin", u64), ("local_count", u64), ("local_synapses", u64),
                 ("index_bits", C.c_uint32), ("propagation", C.c_int), ("device_state_bytes", u64),
                 ("device_topology_bytes", u64), ("binned", C.c_uint32), ("binned_passes", C.c_uint32),
-                ("ordered_csc", C.c_uint32), ("reserved", C.c_uint32)]
+                ("ordered_csc", C.c_uint32), ("batch", C.c_uint32), ("topology_rows", u64)]
 
     def as_dict(self):
         return {k: getattr(self, k) for k, _ in self._fields_}

@@ -366,18 +366,25 @@ __global__ void __launch_bounds__(256) propagate_push_kernel(const TIdx *__restr
                                                              const uint64_t *__restrict__ row_ptr,
                                                              const TCol *__restrict__ col,
                                                              const float *__restrict__ w, float *__restrict__ next,
-                                                             DevCounters *ctr, int parity, int count_spikes) {
+                                                             DevCounters *ctr, int parity, int count_spikes,
+                                                             uint64_t batch_rows) {
     const uint32_t count = *(volatile uint32_t *)&ctr->list_count[parity];
     const unsigned lane = lane_id();
     const uint64_t gwarp = ((uint64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const uint64_t nwarps = ((uint64_t)gridDim.x * blockDim.x) >> 5;
     unsigned long long events = 0;
     for (uint64_t s = gwarp; s < count; s += nwarps) {
-        const uint64_t row = (uint64_t)list[s];
+        uint64_t row = (uint64_t)list[s];
+        float *dst = next;
+        if (batch_rows) {  // batched states: sample (id / rows) adds into its own current slice
+            const uint64_t r = row % batch_rows;
+            dst = next + (row - r);
+            row = r;
+        }
         const uint64_t b = row_ptr[row];
         const uint64_t e = row_ptr[row + 1];
         events += e - b;
-        push_row<TCol>(b, e, col, w, next, lane);
+        push_row<TCol>(b, e, col, w, dst, lane);
     }
     block_add_u64(lane == 0 ? events : 0ull, &ctr->events);
     step_epilogue(ctr, parity, count_spikes, count);
@@ -400,12 +407,14 @@ __global__ void __launch_bounds__(256) propagate_push_kernel(const TIdx *__restr
 template <typename TIdx>
 __global__ void __launch_bounds__(256) ordered_sdeg_kernel(const TIdx *__restrict__ list, DevCounters *ctr,
                                                            int parity, const uint64_t *__restrict__ row_ptr,
-                                                           uint32_t *__restrict__ sdeg, int clear) {
+                                                           uint32_t *__restrict__ sdeg, int clear,
+                                                           uint64_t batch_rows) {
     const uint32_t count = *(volatile uint32_t *)&ctr->list_count[parity];
     const uint64_t stride = (uint64_t)blockDim.x * gridDim.x;
     for (uint64_t s = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; s < count; s += stride) {
-        const uint64_t row = (uint64_t)list[s];
-        sdeg[row] = clear ? 0u : (uint32_t)(row_ptr[row + 1] - row_ptr[row]);
+        const uint64_t id = (uint64_t)list[s];
+        const uint64_t row = batch_rows ? id % batch_rows : id;
+        sdeg[id] = clear ? 0u : (uint32_t)(row_ptr[row + 1] - row_ptr[row]);
     }
 }
 
@@ -421,21 +430,23 @@ __global__ void __launch_bounds__(256) ordered_gen_kernel(const TIdx *__restrict
                                                           const unsigned long long *__restrict__ eoff, uint64_t rows,
                                                           uint64_t id_base, uint32_t *__restrict__ sdeg,
                                                           uint32_t *__restrict__ keys, float *__restrict__ vals,
-                                                          int epilogue, int count_spikes) {
+                                                          int epilogue, int count_spikes, uint64_t batch_rows) {
     const uint32_t count = *(volatile uint32_t *)&ctr->list_count[parity];
     const unsigned lane = lane_id();
     const uint64_t gwarp = ((uint64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const uint64_t nwarps = ((uint64_t)gridDim.x * blockDim.x) >> 5;
     for (uint64_t s = gwarp; s < count; s += nwarps) {
-        const uint64_t row = (uint64_t)list[s];
-        if (row < row_lo || row >= row_hi) continue;
+        const uint64_t id = (uint64_t)list[s];
+        if (id < row_lo || id >= row_hi) continue;
+        const uint64_t row = batch_rows ? id % batch_rows : id;
+        const uint32_t base = (uint32_t)(id - row);  // batched: the sample's first neuron
         const uint64_t b = row_ptr[row], e = row_ptr[row + 1];
-        const uint64_t d = eoff[row] - id_base - b;
+        const uint64_t d = eoff[id] - id_base - b;
         for (uint64_t k = b + lane; k < e; k += 32u) {
-            keys[d + k] = (uint32_t)col[k];
+            keys[d + k] = base + (uint32_t)col[k];
             vals[d + k] = __ldcs(w + k);
         }
-        if (lane == 0) sdeg[row] = 0u;
+        if (lane == 0) sdeg[id] = 0u;
     }
     if (epilogue) {
         if (blockIdx.x == 0 && threadIdx.x == 0) ctr->events += eoff[rows];
@@ -924,11 +935,11 @@ static int push_grid(int device) {
 
 void launch_propagate_push(cudaStream_t s, int device, const void *list, int idx_bits, const uint64_t *row_ptr,
                            const void *col, int col_bits, const float *w, float *next, DevCounters *ctr, int parity,
-                           int count_spikes) {
+                           int count_spikes, uint64_t batch_rows) {
 #define B200_PUSH(TI, TC)                                                                                      \
     propagate_push_kernel<TI, TC><<<push_grid<TI, TC>(device), 256, 0, s>>>((const TI *)list, row_ptr,         \
                                                                             (const TC *)col, w, next, ctr,     \
-                                                                            parity, count_spikes)
+                                                                            parity, count_spikes, batch_rows)
     if (idx_bits == 32 && col_bits == 32) B200_PUSH(uint32_t, uint32_t);
     else if (idx_bits == 32) B200_PUSH(uint32_t, uint64_t);
     else if (col_bits == 32) B200_PUSH(uint64_t, uint32_t);
@@ -1049,23 +1060,27 @@ void launch_gather_generated_csc(cudaStream_t s, int device, const GenParams &g,
 }
 
 void launch_ordered_sdeg(cudaStream_t s, int device, const void *list, int idx_bits, DevCounters *ctr, int parity,
-                         uint64_t max_rows, const uint64_t *row_ptr, uint32_t *sdeg, int clear) {
+                         uint64_t max_rows, const uint64_t *row_ptr, uint32_t *sdeg, int clear,
+                         uint64_t batch_rows) {
     const int grid = grid_for(device, 4, max_rows, 256);
     if (idx_bits == 32)
-        ordered_sdeg_kernel<uint32_t><<<grid, 256, 0, s>>>((const uint32_t *)list, ctr, parity, row_ptr, sdeg, clear);
+        ordered_sdeg_kernel<uint32_t><<<grid, 256, 0, s>>>((const uint32_t *)list, ctr, parity, row_ptr, sdeg, clear,
+                                                           batch_rows);
     else
-        ordered_sdeg_kernel<uint64_t><<<grid, 256, 0, s>>>((const uint64_t *)list, ctr, parity, row_ptr, sdeg, clear);
+        ordered_sdeg_kernel<uint64_t><<<grid, 256, 0, s>>>((const uint64_t *)list, ctr, parity, row_ptr, sdeg, clear,
+                                                           batch_rows);
 }
 
 void launch_ordered_gen(cudaStream_t s, int device, const void *list, int idx_bits, DevCounters *ctr, int parity,
                         uint64_t row_lo, uint64_t row_hi, const uint64_t *row_ptr, const void *col, int col_bits,
                         const float *w, const unsigned long long *eoff, uint64_t rows, uint64_t id_base,
-                        uint32_t *sdeg, uint32_t *keys, float *vals, int epilogue, int count_spikes) {
+                        uint32_t *sdeg, uint32_t *keys, float *vals, int epilogue, int count_spikes,
+                        uint64_t batch_rows) {
     const int grid = sm_count(device) * 8;
 #define B200_OG(TI, TC)                                                                                        \
     ordered_gen_kernel<TI, TC><<<grid, 256, 0, s>>>((const TI *)list, ctr, parity, row_lo, row_hi, row_ptr,     \
                                                     (const TC *)col, w, eoff, rows, id_base, sdeg, keys, vals,  \
-                                                    epilogue, count_spikes)
+                                                    epilogue, count_spikes, batch_rows)
     if (idx_bits == 32 && col_bits == 32) B200_OG(uint32_t, uint32_t);
     else if (idx_bits == 32) B200_OG(uint32_t, uint64_t);
     else if (col_bits == 32) B200_OG(uint64_t, uint32_t);

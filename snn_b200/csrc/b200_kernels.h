@@ -122,9 +122,11 @@ void launch_compact(cudaStream_t s, int device, const uint32_t *bitmap, uint64_t
 
 // Push propagation from the spike list over a resident CSR.
 // col_bits = 32 or 64 (local target ids), idx_bits = spike list width.
+// batch_rows != 0: batched states; list id g is row g % batch_rows of the
+// topology adding into the current slice starting at g - g % batch_rows.
 void launch_propagate_push(cudaStream_t s, int device, const void *list, int idx_bits, const uint64_t *row_ptr,
                            const void *col, int col_bits, const float *w, float *next, DevCounters *ctr,
-                           int parity, int count_spikes);
+                           int parity, int count_spikes, uint64_t batch_rows = 0);
 
 // Ordered pull over a CSC: for every local target, folds the weights of its
 // spiking presynaptic rows in (row, edge) order starting from 0.0f.
@@ -201,13 +203,15 @@ void launch_gather_generated_csc(cudaStream_t s, int device, const GenParams &g,
 // gen (events in CSR order) -> sort_pairs_u32_f32 (stable, by target) ->
 // fold.
 void launch_ordered_sdeg(cudaStream_t s, int device, const void *list, int idx_bits, DevCounters *ctr, int parity,
-                         uint64_t max_rows, const uint64_t *row_ptr, uint32_t *sdeg, int clear);
+                         uint64_t max_rows, const uint64_t *row_ptr, uint32_t *sdeg, int clear,
+                         uint64_t batch_rows);
 cudaError_t scan_degrees_u64(cudaStream_t s, const uint32_t *in, unsigned long long *out, uint64_t n, void *temp,
                              size_t *temp_bytes);
 void launch_ordered_gen(cudaStream_t s, int device, const void *list, int idx_bits, DevCounters *ctr, int parity,
                         uint64_t row_lo, uint64_t row_hi, const uint64_t *row_ptr, const void *col, int col_bits,
                         const float *w, const unsigned long long *eoff, uint64_t rows, uint64_t id_base,
-                        uint32_t *sdeg, uint32_t *keys, float *vals, int epilogue, int count_spikes);
+                        uint32_t *sdeg, uint32_t *keys, float *vals, int epilogue, int count_spikes,
+                        uint64_t batch_rows);
 cudaError_t sort_pairs_u32_f32(cudaStream_t s, uint32_t *keys, uint32_t *keys_alt, float *vals, float *vals_alt,
                                uint64_t n, int end_bit, void *temp, size_t *temp_bytes, bool *result_in_alt);
 void launch_ordered_fold(cudaStream_t s, int device, uint64_t events, const uint32_t *keys, const float *vals,

@@ -99,7 +99,9 @@ struct snn_cuda_context {
     int idx_bits = 32;
     uint32_t rank = 0;
     uint32_t world = 1;
-    uint64_t n_global = 0;
+    uint64_t n_global = 0;  // neurons of the state: batch x n_rows
+    uint64_t n_rows = 0;    // rows of the topology (the network's n)
+    uint64_t batch = 1;     // independent states sharing the topology
     uint64_t slot = 0;  // neurons per shard slot (multiple of 32)
     uint64_t lo = 0, hi = 0, n_local = 0;
     uint64_t e_local = 0;
@@ -329,12 +331,27 @@ snn_status_t apply_options(snn_cuda_context_t *c, uint64_t n, const snn_b200_opt
     c->world = o.world_size;
     c->rank = o.rank;
     c->timing = o.timing;
-    c->n_global = n;
-    shard_geometry(n, o.world_size, o.rank, &c->slot, &c->lo, &c->hi);
+    // Batched states: B copies of the n-neuron state over one topology, seen
+    // by every per-neuron kernel as one B*n-neuron network whose spike list
+    // ids g map to topology row g % n and target offset g - g % n.
+    const uint64_t batch = o.batch ? o.batch : 1;
+    if (batch > 1) {
+        if (o.world_size != 1 || o.streaming != SNN_B200_STREAMING_CHUNKED ||
+            (o.propagation != SNN_B200_PROPAGATE_PUSH && o.propagation != SNN_B200_PROPAGATE_PUSH_ATOMIC &&
+             o.propagation != SNN_B200_PROPAGATE_ORDERED) ||
+            (o.propagation == SNN_B200_PROPAGATE_ORDERED && c->opull))
+            return SNN_ERR_UNSUPPORTED;
+        if (n > UINT64_MAX / batch) return SNN_ERR_OVERFLOW;
+    }
+    c->batch = batch;
+    c->n_rows = n;
+    const uint64_t ns = n * batch;
+    c->n_global = ns;
+    shard_geometry(ns, o.world_size, o.rank, &c->slot, &c->lo, &c->hi);
     c->n_local = c->hi - c->lo;
     c->bitmap_words = c->slot / 32 * o.world_size;
     const bool fits32 = n <= 0xffffffffull;
-    c->idx_bits = fits32 ? 32 : 64;
+    c->idx_bits = ns <= 0xffffffffull ? 32 : 64;
     c->col_bits = (o.index_width == 64 || !fits32) ? 64 : 32;
     if (o.index_width == 32 && !fits32) return SNN_ERR_INVALID_ARGUMENT;
     if (c->n_local >= 0xffffffffull) return SNN_ERR_UNSUPPORTED;
@@ -536,7 +553,7 @@ snn_status_t upload_full_push(snn_cuda_context_t *c, const snn_network_t *net) {
     c->e_local = 0;
     for (uint32_t p = 0; p < c->passes && st == SNN_OK; ++p) {
         const uint64_t rlo = c->passes > 1 ? c->lo + c->bin.pass_lo[p] : c->lo;
-        const uint64_t rhi = c->passes > 1 ? rlo + c->bin.pass_len[p] : c->hi;
+        const uint64_t rhi = c->passes > 1 ? rlo + c->bin.pass_len[p] : std::min(c->hi, c->n_rows);
         uint64_t e = 0;
         st = p == 0 ? upload_push_range(c, net, rlo, rhi, &c->d_row_ptr, &c->d_col, &c->d_w, &e)
                     : upload_push_range(c, net, rlo, rhi, &c->d_prow[p], &c->d_pcol[p], &c->d_pw[p], &e);
@@ -568,18 +585,20 @@ snn_status_t setup_ordered_push(snn_cuda_context_t *c) {
     if (cudaMallocHost(&c->h_ototal, 8) != cudaSuccess) return fail("out of pinned memory");
     cudaMemsetAsync(c->d_sdeg, 0, (n + 1) * 4, c->stream);
     // Largest row: one row's events must fit one sort.
+    const uint64_t rows = c->n_rows;
     std::vector<uint64_t> rp;
     try {
-        rp.resize(n + 1);
+        rp.resize(rows + 1);
     } catch (const std::bad_alloc &) {
         return SNN_ERR_OUT_OF_MEMORY;
     }
-    if (cudaMemcpy(rp.data(), c->d_row_ptr, (n + 1) * 8, cudaMemcpyDeviceToHost) != cudaSuccess) return SNN_ERR_CUDA;
+    if (cudaMemcpy(rp.data(), c->d_row_ptr, (rows + 1) * 8, cudaMemcpyDeviceToHost) != cudaSuccess)
+        return SNN_ERR_CUDA;
     uint64_t max_deg = 0;
-    for (uint64_t i = 0; i < n; ++i) max_deg = std::max(max_deg, rp[i + 1] - rp[i]);
+    for (uint64_t i = 0; i < rows; ++i) max_deg = std::max(max_deg, rp[i + 1] - rp[i]);
     size_t free_b = 0, total_b = 0;
     if (cudaMemGetInfo(&free_b, &total_b) != cudaSuccess) return SNN_ERR_CUDA;
-    uint64_t cap = std::min<uint64_t>(c->e_local, (uint64_t)(free_b / 2) / 16);
+    uint64_t cap = std::min<uint64_t>(c->e_local * c->batch, (uint64_t)(free_b / 2) / 16);
     if (const char *env = std::getenv("SNN_B200_ORDERED_CAP")) {  // tests: force the multi-range path
         const uint64_t v = std::strtoull(env, nullptr, 10);
         if (v) cap = std::min(cap, v);
@@ -609,8 +628,9 @@ snn_status_t ordered_push_step(snn_cuda_context_t *c, int parity, float *next, b
                                const uint32_t *bitmap) {
     const uint64_t n = c->n_global;
     snn_status_t st;
+    const uint64_t brows = c->batch > 1 ? c->n_rows : 0;
     b200::launch_ordered_sdeg(c->stream, c->device, c->d_list, c->idx_bits, c->d_ctr, parity, n, c->d_row_ptr,
-                              c->d_sdeg, 0);
+                              c->d_sdeg, 0, brows);
     size_t tb = c->otemp_bytes;
     if ((st = cuda_status(b200::scan_degrees_u64(c->stream, c->d_sdeg, c->d_eoff, n + 1, c->d_otemp, &tb))) != SNN_OK)
         return st;
@@ -623,7 +643,7 @@ snn_status_t ordered_push_step(snn_cuda_context_t *c, int parity, float *next, b
         // Most rows spike: the pull over the CSC reads every synapse once,
         // cheaper than sorting this many events.
         b200::launch_ordered_sdeg(c->stream, c->device, c->d_list, c->idx_bits, c->d_ctr, parity, n, c->d_row_ptr,
-                                  c->d_sdeg, 1);
+                                  c->d_sdeg, 1, brows);
         b200::launch_propagate_pull(c->stream, c->device, c->n_local, c->d_col_ptr, c->d_pre, c->idx_bits, c->d_cw,
                                     bitmap, next, c->d_list, c->idx_bits, c->d_deg, c->d_ctr, parity, !sharded);
         c->launches += 2;
@@ -651,7 +671,7 @@ snn_status_t ordered_push_step(snn_cuda_context_t *c, int parity, float *next, b
         const uint64_t events = (i + 1 < ranges.size() ? ranges[i + 1][2] : total) - base;
         b200::launch_ordered_gen(c->stream, c->device, c->d_list, c->idx_bits, c->d_ctr, parity, r0, r1, c->d_row_ptr,
                                  c->d_col, c->col_bits, c->d_w, c->d_eoff, n, base, c->d_sdeg, c->d_okeys[0],
-                                 c->d_ovals[0], i + 1 == ranges.size(), !sharded);
+                                 c->d_ovals[0], i + 1 == ranges.size(), !sharded, brows);
         c->launches++;
         if (!events) continue;
         tb = c->otemp_bytes;
@@ -846,7 +866,7 @@ snn_status_t allocate_sparse_streaming(snn_cuda_context_t *c, bool *fallback) {
 }
 
 uint64_t full_push_bytes(const snn_cuda_context_t *c, uint64_t e) {
-    return state_bytes(c) + (c->n_global + 1) * 8 + e * (c->col_bits / 8 + 4);
+    return state_bytes(c) + (c->n_rows + 1) * 8 + e * (c->col_bits / 8 + 4);
 }
 
 struct CreateEnv {
@@ -1020,7 +1040,8 @@ snn_status_t enqueue_step(snn_cuda_context_t *c, bool has_ext) {
             if (e != cudaSuccess) return cuda_status(e);
         } else
             b200::launch_propagate_push(c->stream, c->device, c->d_list, c->idx_bits, c->d_row_ptr, c->d_col,
-                                        c->col_bits, c->d_w, next, c->d_ctr, parity, !sharded);
+                                        c->col_bits, c->d_w, next, c->d_ctr, parity, !sharded,
+                                        c->batch > 1 ? c->n_rows : 0);
         if ((st = check_launch(c)) != SNN_OK) return st;
     } else if (c->streaming == SNN_B200_STREAMING_SPARSE) {
         // Sparse STREAMING: spiking rows read straight from mapped host memory.
@@ -1162,7 +1183,7 @@ snn_status_t generate_full(snn_cuda_context_t *c, const b200::GenParams &g, uint
     c->e_local = 0;
     for (uint32_t p = 0; p < c->passes && st == SNN_OK; ++p) {
         const uint64_t rlo = c->passes > 1 ? c->lo + c->bin.pass_lo[p] : c->lo;
-        const uint64_t rhi = c->passes > 1 ? rlo + c->bin.pass_len[p] : c->hi;
+        const uint64_t rhi = c->passes > 1 ? rlo + c->bin.pass_len[p] : std::min(c->hi, c->n_rows);
         uint64_t e = 0;
         st = p == 0 ? generate_range(c, g, e_total, rlo, rhi, &c->d_row_ptr, &c->d_col, &c->d_w, &e)
                     : generate_range(c, g, e_total, rlo, rhi, &c->d_prow[p], &c->d_pcol[p], &c->d_pw[p], &e);
@@ -1307,7 +1328,7 @@ snn_status_t build_generated_csc(snn_cuda_context_t *c, const b200::GenParams &g
 // (events > local synapses / div; 0 keeps every step on the ordered push).
 snn_status_t add_ordered_csc(snn_cuda_context_t *c, const snn_network_t *net, const b200::GenParams *g) {
     if (const char *env = std::getenv("SNN_B200_ORDERED_PULL_DIV")) c->pull_div = std::strtoull(env, nullptr, 10);
-    if (c->pull_div == 0 || c->e_local == 0) return SNN_OK;
+    if (c->pull_div == 0 || c->e_local == 0 || c->batch > 1) return SNN_OK;
     size_t free_b = 0, total_b = 0;
     if (cudaMemGetInfo(&free_b, &total_b) != cudaSuccess) return SNN_ERR_CUDA;
     const uint64_t csc = (c->n_local + 1) * 8 + c->e_local * (c->idx_bits / 8 + 4) + c->n_global * 4;
@@ -1375,6 +1396,7 @@ snn_b200_options_t snn_b200_default_options(void) {
     o.timing = 0;
     o.exchange = SNN_B200_EXCHANGE_NCCL;
     o.streaming = SNN_B200_STREAMING_CHUNKED;
+    o.batch = 1;
     return o;
 }
 
@@ -1385,14 +1407,14 @@ snn_status_t snn_b200_create(const snn_network_t *network, const snn_cuda_config
     if (network == nullptr) return SNN_ERR_INVALID_ARGUMENT;
     const snn_cuda_config_t cfg = config ? *config : snn_cuda_default_config();
     const snn_b200_options_t o = options ? *options : snn_b200_default_options();
-    if ((o.world_size > 1 || o.propagation == SNN_B200_PROPAGATE_ORDERED) && cfg.prefer_streaming)
+    if ((o.world_size > 1 || o.propagation == SNN_B200_PROPAGATE_ORDERED || o.batch > 1) && cfg.prefer_streaming)
         return SNN_ERR_UNSUPPORTED;
     snn_cuda_context_t *c = nullptr;
     CreateEnv env;
     snn_status_t st = begin_create(network->neuron_count, network->lif, network->decay, &cfg, &o, &c, &env);
     if (st != SNN_OK) return st;
     c->network = network;
-    const bool full_only = c->world > 1 || c->propagation == SNN_B200_PROPAGATE_ORDERED;
+    const bool full_only = c->world > 1 || c->propagation == SNN_B200_PROPAGATE_ORDERED || c->batch > 1;
     if (full_only || (!cfg.prefer_streaming && full_push_bytes(c, network->synapse_count) <= env.budget)) {
         c->mode = SNN_CUDA_MODE_FULL;
         if (c->propagation != SNN_B200_PROPAGATE_ORDERED) st = upload_full_push(c, network);
@@ -1771,18 +1793,19 @@ snn_status_t snn_b200_get_layout(const snn_cuda_context_t *c, snn_b200_layout_t 
     out->propagation = c->propagation;
     out->device_state_bytes = state_bytes(c);
     if (c->mode == SNN_CUDA_MODE_STREAMING && c->streaming == SNN_B200_STREAMING_SPARSE)
-        out->device_topology_bytes = (c->n_global + 1) * 8;
+        out->device_topology_bytes = (c->n_rows + 1) * 8;
     else if (c->mode == SNN_CUDA_MODE_STREAMING)
         out->device_topology_bytes = 2 * ((c->slot_rows + 1) * 8 + c->slot_edges * 12);
     else if (c->opull || c->has_csc)
-        out->device_topology_bytes = (c->has_csc ? (c->n_global + 1) * 8 + c->e_local * (c->col_bits / 8 + 4) : 0) +
+        out->device_topology_bytes = (c->has_csc ? (c->n_rows + 1) * 8 + c->e_local * (c->col_bits / 8 + 4) : 0) +
                                      (c->n_local + 1) * 8 + c->e_local * (c->idx_bits / 8 + 4) + c->n_global * 4;
     else
-        out->device_topology_bytes = (c->n_global + 1) * 8 + c->e_local * (c->col_bits / 8 + 4);
+        out->device_topology_bytes = (c->n_rows + 1) * 8 + c->e_local * (c->col_bits / 8 + 4);
     out->binned = c->binned ? 1u : 0u;
     out->binned_passes = c->binned ? c->bin.passes : 0u;
     out->ordered_csc = (c->opull || c->has_csc) ? 1u : 0u;
-    out->reserved = 0u;
+    out->batch = (uint32_t)c->batch;
+    out->topology_rows = c->n_rows;
     return SNN_OK;
 }
 
@@ -1839,11 +1862,11 @@ snn_status_t snn_b200_download_topology(const snn_cuda_context_t *c, snn_size_t 
     if (c == nullptr || c->mode != SNN_CUDA_MODE_FULL || c->propagation == SNN_B200_PROPAGATE_ORDERED)
         return SNN_ERR_INVALID_ARGUMENT;
     if (c->passes > 1) return SNN_ERR_UNSUPPORTED;  // topology split into target-pass slices
-    if ((row_ptr && row_capacity < c->n_global + 1) || ((col_idx || weights) && edge_capacity < c->e_local))
+    if ((row_ptr && row_capacity < c->n_rows + 1) || ((col_idx || weights) && edge_capacity < c->e_local))
         return SNN_ERR_INVALID_ARGUMENT;
     if (set_device(c) != SNN_OK) return SNN_ERR_CUDA;
     if (cudaStreamSynchronize(c->stream) != cudaSuccess) return SNN_ERR_CUDA;
-    if (row_ptr && cudaMemcpy(row_ptr, c->d_row_ptr, (c->n_global + 1) * 8, cudaMemcpyDeviceToHost) != cudaSuccess)
+    if (row_ptr && cudaMemcpy(row_ptr, c->d_row_ptr, (c->n_rows + 1) * 8, cudaMemcpyDeviceToHost) != cudaSuccess)
         return SNN_ERR_CUDA;
     if (weights && c->e_local &&
         cudaMemcpy(weights, c->d_w, c->e_local * 4, cudaMemcpyDeviceToHost) != cudaSuccess)

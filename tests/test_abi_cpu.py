@@ -47,7 +47,7 @@ def test_defaults_and_null_arguments():
     cfg = L.snn_cuda_default_config()
     assert (cfg.max_vram_bytes, cfg.max_stream_synapses, cfg.max_stream_rows, cfg.prefer_streaming) == (0, 0, 0, 0)
     o = L.snn_b200_default_options()
-    assert (o.propagation, o.device, o.index_width, o.rank, o.world_size, o.timing) == (0, -1, 0, 0, 1, 0)
+    assert (o.propagation, o.device, o.index_width, o.rank, o.world_size, o.timing, o.batch) == (0, -1, 0, 0, 1, 0, 1)
     assert L.snn_cuda_context_mode(None) == sb.MODE_NONE
     assert L.snn_cuda_step(None, None, None) == sb.SNN_ERR_INVALID_ARGUMENT
     assert L.snn_cuda_inject_current(None, None, None, 0) == sb.SNN_ERR_INVALID_ARGUMENT

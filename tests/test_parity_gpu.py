@@ -462,3 +462,43 @@ def test_ordered_dense_bursts_bit_exact(cap, pull_div, monkeypatch):
     assert ctx.layout["ordered_csc"] == (0 if pull_div == "0" else 1)
     pulls = ctx.stats()["pull_steps"]
     assert (pulls > 0) if pull_div is None else (pulls == 0)
+
+
+@pytest.mark.parametrize("prop,weights", [(sb.PROPAGATE_ORDERED, "general"), (sb.PROPAGATE_PUSH, "dyadic")])
+def test_batched_states_equal_independent_runs(prop, weights):
+    """options.batch = B: B independent states over one shared topology.
+    Sample b owns neurons [b*n, (b+1)*n) of every per-neuron argument. Each
+    sample, driven by its own injection stream and external frames, must equal
+    a separate serial CPU run of the network bit for bit (ORDERED for general
+    weights; PUSH with one dyadic weight, where every sum is exact)."""
+    lif = default_lif(v_rest=0.25, v_reset=-0.5, v_threshold=1.0, input_scale=0.7, refractory_steps=2)
+    n, B, steps = 3001, 5, 25
+    wmin, wmax = (-0.2, 0.5) if weights == "general" else (0.125, 0.125)
+    net = ORC.random_pool(n, 64, wmin, wmax, 41, lif=lif)
+    ctx = sb.CudaContext.create(net, None, sb.default_options(propagation=prop, batch=B))
+    lay = ctx.layout
+    assert (lay["batch"], lay["topology_rows"], lay["neuron_count"]) == (B, n, B * n)
+    assert ctx.local_count == B * n
+    rng = np.random.default_rng(2)
+    inj = [[(rng.integers(0, n, 40).astype(np.uint64), np.full(40, 2.0, np.float32)) for _ in range(steps)]
+           for _ in range(B)]
+    ext = [[(rng.random(n) < 0.02 * (b + 1)).astype(np.float32) * np.float32(1.4) for _ in range(steps)]
+           for b in range(B)]
+    states = [State(net) for _ in range(B)]
+    for t in range(steps):
+        idx = np.concatenate([inj[b][t][0] + np.uint64(b * n) for b in range(B)])
+        val = np.concatenate([inj[b][t][1] for b in range(B)])
+        assert ctx.inject_current(idx, val) == 0
+        got = ctx.step(np.concatenate([ext[b][t] for b in range(B)]))
+        for b in range(B):
+            assert states[b].inject(*inj[b][t]) == 0
+            want = states[b].step(ext[b][t])
+            assert np.array_equal(got[b * n:(b + 1) * n], want), (b, t)
+    v = ctx.download_voltage()
+    for b in range(B):
+        np.testing.assert_array_equal(bits(v[b * n:(b + 1) * n]), bits(states[b].voltage()))
+    assert sum(int(st.voltage().size) for st in states) == B * n
+    assert ctx.stats()["spikes"] > 100
+    # Batched contexts are FULL, unsharded, and not for the CSC pull / binned push.
+    with pytest.raises(sb.SnnError):
+        sb.CudaContext.create(net, None, sb.default_options(propagation=sb.PROPAGATE_PUSH_BINNED, batch=B))
