@@ -294,6 +294,14 @@ snn_status_t snn_b200_run_stream_async(snn_cuda_context_t *context, uint64_t see
 /* One step without host input or output and without a final synchronisation. */
 snn_status_t snn_b200_step_async(snn_cuda_context_t *context);
 
+/* Holds an external current frame on the device (local-count floats, scaled
+ * by input_scale like snn_cuda_step's): every later step that does not pass
+ * its own external current adds it (snn_cuda_step with NULL, step_async,
+ * run_stream_async), across snn_b200_reset, until NULL clears it or a
+ * snn_cuda_step call passes its own frame (which replaces it for that step
+ * and ends the hold). For static per-sample inputs (one upload, many steps). */
+snn_status_t snn_b200_set_external(snn_cuda_context_t *context, const float *host_external_current);
+
 /* Waits for all work of the context; folds pending timings into the stats. */
 snn_status_t snn_b200_synchronize(snn_cuda_context_t *context);
 

@@ -132,6 +132,7 @@ ENTRY_POINTS = [
     ("snn_b200_inject_stream_async", C.c_int, [P, u64, u64, u64, f32]),
     ("snn_b200_run_stream_async", C.c_int, [P, u64, u64, u64, u64, f32]),
     ("snn_b200_step_async", C.c_int, [P]),
+    ("snn_b200_set_external", C.c_int, [P, P]),
     ("snn_b200_synchronize", C.c_int, [P]),
     ("snn_b200_get_stats", C.c_int, [P, P]),
     ("snn_b200_reset_stats", C.c_int, [P]),
@@ -322,6 +323,13 @@ class CudaContext:
 
     def step_async(self):
         _check(lib().snn_b200_step_async(self.handle), "snn_b200_step_async")
+
+    def set_external(self, external):
+        """Holds an external frame on the device for every later step without its own (None clears)."""
+        ext = None if external is None else np.ascontiguousarray(external, np.float32)
+        if ext is not None and ext.size < self.local_count:
+            raise ValueError("external frame shorter than the local neuron count")
+        _check(lib().snn_b200_set_external(self.handle, _ptr(ext)), "snn_b200_set_external")
 
     def synchronize(self):
         _check(lib().snn_b200_synchronize(self.handle), "snn_b200_synchronize")

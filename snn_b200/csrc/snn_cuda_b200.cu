@@ -113,6 +113,7 @@ struct snn_cuda_context {
     float *d_cur[2] = {nullptr, nullptr};
     int cur = 0;
     float *d_ext = nullptr;
+    bool ext_held = false;  // snn_b200_set_external: d_ext applies to every step without its own
     uint32_t *d_refr = nullptr;
     uint8_t *d_spikes = nullptr;
     void *d_ws = nullptr;
@@ -1521,7 +1522,8 @@ snn_status_t snn_cuda_step(snn_cuda_context_t *c, const float *host_external_cur
             return SNN_ERR_CUDA;
     }
     c->spk_dst = early ? host_out_spikes : nullptr;
-    st = enqueue_step(c, host_external_current != nullptr);
+    if (host_external_current != nullptr) c->ext_held = false;  // the held frame was overwritten
+    st = enqueue_step(c, host_external_current != nullptr || c->ext_held);
     c->spk_dst = nullptr;
     if (st != SNN_OK) {
         if (early) cudaStreamSynchronize(c->spk_stream);  // no copy lands after the return
@@ -1692,8 +1694,9 @@ snn_status_t snn_b200_reset(snn_cuda_context_t *c) {
     // Keep the cumulative statistics across the reset.
     b200::DevCounters saved{};
     if (cudaMemcpy(&saved, c->d_ctr, sizeof(saved), cudaMemcpyDeviceToHost) != cudaSuccess) return SNN_ERR_CUDA;
-    b200::launch_init_state(c->stream, c->n_local, c->lif.v_rest, c->d_v, c->d_cur[0], c->d_cur[1], c->d_ext,
-                            c->d_refr, c->d_spikes, c->bitmap_words, c->d_bitmap, c->d_ctr);
+    b200::launch_init_state(c->stream, c->n_local, c->lif.v_rest, c->d_v, c->d_cur[0], c->d_cur[1],
+                            c->ext_held ? nullptr : c->d_ext, c->d_refr, c->d_spikes, c->bitmap_words, c->d_bitmap,
+                            c->d_ctr);
     c->launches++;
     if ((st = cuda_status(cudaGetLastError())) != SNN_OK) return st;
     saved.list_count[0] = saved.list_count[1] = 0;
@@ -1721,7 +1724,24 @@ snn_status_t snn_b200_step_async(snn_cuda_context_t *c) {
     if (c == nullptr) return SNN_ERR_INVALID_ARGUMENT;
     snn_status_t st = set_device(c);
     if (st != SNN_OK) return st;
-    return enqueue_step(c, false);
+    return enqueue_step(c, c->ext_held);
+}
+
+snn_status_t snn_b200_set_external(snn_cuda_context_t *c, const float *host_external_current) {
+    if (c == nullptr) return SNN_ERR_INVALID_ARGUMENT;
+    snn_status_t st = set_device(c);
+    if (st != SNN_OK) return st;
+    if (host_external_current == nullptr) {
+        c->ext_held = false;
+        return SNN_OK;
+    }
+    if (c->n_local &&
+        (st = cuda_status(cudaMemcpyAsync(c->d_ext, host_external_current, c->n_local * 4, cudaMemcpyHostToDevice,
+                                          c->stream))) != SNN_OK)
+        return st;
+    if ((st = cuda_status(cudaStreamSynchronize(c->stream))) != SNN_OK) return st;
+    c->ext_held = true;
+    return SNN_OK;
 }
 
 snn_status_t snn_b200_run_stream_async(snn_cuda_context_t *c, uint64_t seed, uint64_t first_step, uint64_t steps,
@@ -1735,7 +1755,7 @@ snn_status_t snn_b200_run_stream_async(snn_cuda_context_t *c, uint64_t seed, uin
                                        value * c->lif.input_scale, c->d_cur[c->cur], c->lo, c->hi);
             c->launches++;
         }
-        if ((st = enqueue_step(c, false)) != SNN_OK) return st;
+        if ((st = enqueue_step(c, c->ext_held)) != SNN_OK) return st;
     }
     return cuda_status(cudaGetLastError());
 }

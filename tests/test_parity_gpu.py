@@ -502,3 +502,40 @@ def test_batched_states_equal_independent_runs(prop, weights):
     # Batched contexts are FULL, unsharded, and not for the CSC pull / binned push.
     with pytest.raises(sb.SnnError):
         sb.CudaContext.create(net, None, sb.default_options(propagation=sb.PROPAGATE_PUSH_BINNED, batch=B))
+
+
+def test_batched_config1_samples_with_held_frames():
+    """BASELINE config 1 as batched samples: 784-1000-10 dense gaussian, B
+    samples at once, each with its own static sparse frame held on the device
+    (snn_b200_set_external, one upload for 25 steps), two rounds of samples
+    with snn_b200_reset between them. Steps alternate between snn_cuda_step
+    without an external (spikes checked) and snn_b200_step_async. Every sample
+    equals its own serial CPU run bit for bit (ORDERED)."""
+    lif = baseline_lif()
+    net = ORC.dense_gaussian([784, 1000, 10], 21, lif=lif)
+    n, B = net.neuron_count, 24
+    ctx = sb.CudaContext.create(net, None, sb.default_options(propagation=sb.PROPAGATE_ORDERED, batch=B))
+    for rnd in range(2):
+        frames = [ORC.sparse_frame(99, rnd * B + b, 784, 0.8, n) * np.float32(40.0) for b in range(B)]
+        ctx.set_external(np.concatenate(frames))
+        ctx.reset()  # keeps the held frames
+        states = [State(net) for _ in range(B)]
+        for t in range(25):
+            want = [states[b].step(frames[b]) for b in range(B)]
+            if t % 2 == 0:
+                got = ctx.step()
+                for b in range(B):
+                    assert np.array_equal(got[b * n:(b + 1) * n], want[b]), (rnd, t, b)
+            else:
+                ctx.step_async()
+        ctx.synchronize()
+        v = ctx.download_voltage()
+        for b in range(B):
+            np.testing.assert_array_equal(bits(v[b * n:(b + 1) * n]), bits(states[b].voltage()))
+    # An explicit external replaces the held frame for that step and ends the hold.
+    ctx.set_external(None)
+    ctx.reset()
+    st0 = State(net)
+    zero_ext = np.zeros(B * n, np.float32)
+    got = ctx.step(zero_ext)
+    assert np.array_equal(got[:n], st0.step(np.zeros(n, np.float32)))
