@@ -62,6 +62,10 @@ def parse():
     ap.add_argument("--stream-mode", choices=["chunked", "sparse"], default="sparse")
     ap.add_argument("--stream-budget-frac", type=float, default=0.25,
                     help="VRAM budget as a fraction of the host CSR bytes (config 3 streams ~15x its budget)")
+    ap.add_argument("--workload", choices=["config2", "config1"], default="config2",
+                    help="config1: BASELINE config 1 (784-1000-10 dense, 25 steps per static frame) run as "
+                         "--batch samples at once over one shared topology")
+    ap.add_argument("--batch", type=int, default=2000, help="config1: samples per batched context")
     ap.add_argument("--propagation", choices=["auto", "binned", "atomic", "ordered"], default="auto",
                     help="push kernel: auto (library default), binned (shared-memory tiles), atomic (L2 red); "
                          "ordered: the bit-exact pull over a device-built CSC")
@@ -211,7 +215,141 @@ def main():
     if args.policy == "streaming":
         run_streaming(args)
         return
+    if args.workload == "config1":
+        run_config1(args)
+        return
     run_b200(args)
+
+
+def config1_network(seed):
+    """784-1000-10 dense, weights N(0, 1/sqrt(fan_in)) (numpy-seeded synthetic stand-in)."""
+    import numpy as np
+    layers = [784, 1000, 10]
+    rng = np.random.default_rng(seed)
+    n = sum(layers)
+    rows, cols, ws = [np.zeros(1, np.uint64)], [], []
+    off = np.cumsum([0] + layers)
+    row_ptr = np.zeros(n + 1, np.uint64)
+    for l in range(len(layers) - 1):
+        pre, post = layers[l], layers[l + 1]
+        w = (rng.standard_normal((pre, post)) / np.sqrt(pre)).astype(np.float32)
+        cols.append(np.tile(np.arange(off[l + 1], off[l + 2], dtype=np.uint64), pre))
+        ws.append(w.reshape(-1))
+        row_ptr[off[l] + 1:off[l + 1] + 1] = np.uint64(post)
+    row_ptr = np.cumsum(row_ptr).astype(np.uint64)
+    return row_ptr, np.concatenate(cols), np.concatenate(ws), layers
+
+
+def config1_frames(seed, first, count, n):
+    """Static per-sample frames: 784 pixels U[0,1), each zeroed with p = 0.8."""
+    import numpy as np
+    out = np.zeros((count, n), np.float32)
+    for k in range(count):
+        rng = np.random.default_rng((seed, first + k))
+        px = rng.random(784, dtype=np.float32)
+        px[rng.random(784) < 0.8] = 0.0
+        out[k, :784] = px
+    return out
+
+
+def run_config1(args):
+    """BASELINE config 1 (784-1000-10 dense, 25 steps per static frame, state
+    reset between samples) with --batch samples per context sharing one
+    topology: per round, one upload of the batch's frames (held on the device),
+    a reset, 25 steps. value = events / device time of the timed rounds
+    (uploads included); samples/s alongside. ORDERED: bit-exact with the
+    reference's serial CPU step sample by sample."""
+    import numpy as np
+    import torch
+
+    import snn_b200 as sb
+
+    row_ptr, col, w, layers = config1_network(args.seed)
+    n, B, T = int(row_ptr.size - 1), args.batch, 25
+    lif = sb.LifParams(1.0, 20.0, -65.0, -65.0, -50.0, 20.0, 2)
+    net = sb.Network.from_csr(row_ptr, col, w, lif)
+    prop = sb.PROPAGATE_ORDERED if args.propagation == "ordered" else sb.PROPAGATE_PUSH
+    ctx = sb.CudaContext.create(net, None, sb.default_options(device=0, timing=1, propagation=prop, batch=B))
+    rounds = max(1, args.steps // T)
+    warm_rounds = max(1, args.warmup // T)
+    frames = [np.ascontiguousarray(config1_frames(args.seed, r * B, B, n).reshape(-1))
+              for r in range(warm_rounds + rounds)]
+    pinned = [torch.from_numpy(f).pin_memory().numpy() for f in frames]
+
+    def round_(r):
+        ctx.set_external(pinned[r])
+        ctx.reset()
+        for _ in range(T):
+            ctx.step_async()
+
+    for r in range(warm_rounds):
+        round_(r)
+    ctx.synchronize()
+    ctx.reset_stats()
+    stream = torch.cuda.ExternalStream(ctx.stream())
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    with ClockSampler(0) as clk:
+        ev0.record(stream)
+        for r in range(rounds):
+            round_(warm_rounds + r)
+        ev1.record(stream)
+        ctx.synchronize()
+    wall = time.perf_counter() - t0
+    ms = ev0.elapsed_time(ev1)
+    s = ctx.stats()
+    samples = rounds * B
+    cpu = None
+    if not args.no_cpu_baseline:
+        try:
+            cpu = config1_cpu(row_ptr, col, w, frames[warm_rounds], lif, seconds=min(args.cpu_seconds, 10.0))
+        except Exception as exc:  # reported, never required
+            cpu = {"value": None, "unavailable": repr(exc)}
+    print(json.dumps({
+        "metric": "synaptic_events_per_sec", "value": s["events"] / (ms / 1e3), "unit": "events/s", "n_gpus": 1,
+        "steps": rounds * T, "warmup": warm_rounds * T, "ms_per_step": ms / (rounds * T), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic: numpy-seeded 784-1000-10 gaussian weights and sparse U[0,1) frames",
+        "config": {"workload": "config1_batched_samples", "layers": layers, "synapses": int(col.size),
+                   "batch": B, "steps_per_sample": T, "propagation": "ordered" if prop == sb.PROPAGATE_ORDERED
+                   else "push", "input_scale": 20.0, "l2": "topology (9.5 MB) L2-resident by design"},
+        "samples_per_sec": samples / (ms / 1e3), "e2e": {"value": s["events"] / wall, "unit": "events/s",
+                                                          "h2d_bytes_per_step": B * n * 4 // T,
+                                                          "d2h_bytes_per_step": 0,
+                                                          "samples_per_sec": samples / wall},
+        "spike_rate": s["spikes"] / (rounds * T * B * n), "events_per_sample": s["events"] / samples,
+        "gpu_launches": int(s["kernel_launches"]), "clocks": clk.summary(), "cpu_baseline": cpu,
+    }), flush=True)
+    ctx.free()
+
+
+def config1_cpu(row_ptr, col, w, frames, lif, seconds):
+    """The reference's serial CPU step (oracle/_ref, else the port) on the same
+    network and frames, sample after sample, for a bounded time."""
+    import numpy as np
+
+    from oracle.oracle import LifParams, Oracle, State, ref_available
+    kind = "ref" if ref_available("ref") else "port"
+    orc = Oracle(kind)
+    net = orc.custom_csr(row_ptr, col, w, lif=LifParams(lif.dt_ms, lif.membrane_tau_ms, lif.v_rest, lif.v_reset,
+                                                        lif.v_threshold, lif.input_scale, lif.refractory_steps))
+    n = int(row_ptr.size - 1)
+    deg = (row_ptr[1:] - row_ptr[:-1]).astype(np.int64)
+    st = State(net)
+    events, done, elapsed = 0, 0, 0.0
+    frames = frames.reshape(-1, n)
+    while elapsed < seconds and done < frames.shape[0]:
+        t0 = time.perf_counter()
+        st.reset()
+        for _ in range(25):
+            sp = st.step(frames[done])
+            events += int(deg[sp.astype(bool)].sum())
+        elapsed += time.perf_counter() - t0
+        done += 1
+    return {"value": events / elapsed, "unit": "events/s", "cores": 1,
+            "kind": "reference" if kind == "ref" else "port",
+            "sample": f"{done} samples x 25 steps, serial build", "samples_per_sec": done / elapsed}
 
 
 def run_streaming(args):
