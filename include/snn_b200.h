@@ -341,6 +341,20 @@ snn_status_t snn_b200_network_wrap(snn_size_t neuron_count, snn_size_t synapse_c
                                    snn_network_t **out_network);
 void snn_b200_network_unwrap(snn_network_t *network);
 
+/* The snn_b200 CSR file: header (4096 bytes: magic "SNNCSR01", version 1,
+ * n, e, architecture, LIF parameters, decay, section offsets, file size),
+ * then u64 row_ptr[n+1], u64 col_idx[e], f32 weights[e], each section
+ * 4096-byte aligned. snn_b200_network_save writes any network (written under
+ * "<path>.partial", then renamed). snn_b200_network_map maps a file read-only
+ * (no copy), validates it like snn_build_custom_csr and returns a network
+ * view that works with every create call; release it with
+ * snn_b200_network_unwrap (which unmaps it) after its contexts are freed.
+ * STREAMING contexts over a mapped network copy their chunks straight from
+ * the page cache (the library tries to lock the mapping read-only; where the
+ * OS refuses to lock file pages, SPARSE streaming falls back to chunks). */
+snn_status_t snn_b200_network_save(const snn_network_t *network, const char *path);
+snn_status_t snn_b200_network_map(const char *path, snn_network_t **out_network);
+
 /* Largest network snn_b200_step_noalloc accepts: its scratch is a fixed
  * array of this many spike-list entries (plus bitmap and counters, ~4.2 MB)
  * compiled into the library and resident on every GPU that loads it. */

@@ -145,6 +145,8 @@ ENTRY_POINTS = [
     ("snn_b200_download_state", C.c_int, [P, P, P, P, u64]),
     ("snn_b200_network_wrap", C.c_int, [u64, u64, P, P, P, P, P]),
     ("snn_b200_network_unwrap", None, [P]),
+    ("snn_b200_network_save", C.c_int, [P, C.c_char_p]),
+    ("snn_b200_network_map", C.c_int, [C.c_char_p, P]),
 ]
 
 _LIB = None
@@ -232,6 +234,13 @@ class Network:
         _check(st, "snn_b200_network_wrap")
         return cls(h, owner="wrap", keep=(rp, ci, w))
 
+    @classmethod
+    def map(cls, path: str) -> "Network":
+        """Maps an snn_b200 CSR file read-only (snn_b200_network_map); free() unmaps it."""
+        h = P()
+        _check(lib().snn_b200_network_map(os.fsencode(path), C.byref(h)), "snn_b200_network_map")
+        return cls(h, owner="wrap")
+
     def free(self):
         if self._owner == "wrap" and self.handle:
             lib().snn_b200_network_unwrap(self.handle)
@@ -242,6 +251,11 @@ class Network:
             self.free()
         except Exception:
             pass
+
+
+def save_network(net, path: str) -> None:
+    """Writes a network (anything with a .handle: sb.Network or the oracle's) as an snn_b200 CSR file."""
+    _check(lib().snn_b200_network_save(net.handle, os.fsencode(path)), "snn_b200_network_save")
 
 
 class CudaContext:

@@ -11,12 +11,15 @@
 //  * device col_idx is 32-bit when the target ids fit (the host CSR stays 64-bit);
 //  * STREAMING double-buffers the CSR chunks on a copy stream so the copy of
 //    chunk i+1 overlaps the propagation of chunk i;
-//  * ORDERED propagation (extension) folds in CSR order over a device CSC and
-//    is bit-identical to the reference's serial CPU step for any weights;
+//  * ORDERED propagation (extension) folds every target's events in CSR
+//    order (a stable sort of each step's events by target, or a pull over a
+//    CSC on dense steps) and is bit-identical to the reference's serial CPU
+//    step for any weights;
 //  * sharded contexts (extension) own a contiguous range of postsynaptic
 //    neurons and all-gather the spike bitmap with NCCL every step.
 #include "snn_b200.h"
 #include "b200_kernels.h"
+#include "b200_network.h"
 
 #include <cuda_runtime.h>
 #include <nccl.h>
@@ -31,19 +34,6 @@
 #include <new>
 #include <numeric>
 #include <vector>
-
-// Same field layout as the reference's struct snn_network (src/snn_internal.h:15-24):
-// the backend reads a network built by the reference's host library directly.
-struct snn_network {
-    snn_size_t neuron_count;
-    snn_size_t synapse_count;
-    snn_architecture_t architecture;
-    snn_lif_params_t lif;
-    float decay;
-    snn_size_t *row_ptr;
-    snn_size_t *col_idx;
-    float *weights;
-};
 
 namespace {
 
@@ -229,12 +219,8 @@ snn_status_t set_device(const snn_cuda_context_t *c) { return cuda_status(cudaSe
 
 uint64_t ceil_div(uint64_t a, uint64_t b) { return (a + b - 1) / b; }
 
-// src/snn.c:308-316
-bool lif_valid(const snn_lif_params_t *p) {
-    return p && std::isfinite(p->dt_ms) && std::isfinite(p->membrane_tau_ms) && std::isfinite(p->v_rest) &&
-           std::isfinite(p->v_reset) && std::isfinite(p->v_threshold) && std::isfinite(p->input_scale) &&
-           p->dt_ms > 0.0f && p->membrane_tau_ms > 0.0f && p->v_threshold > p->v_reset;
-}
+using b200host::lif_valid;
+using b200host::validate_csr;
 
 // SNN_B200_BINNED_PROFILE: print the binned kernel's per-role cycle totals
 // (summed over CTAs, in ms at the current SM clock) when a context is freed.
@@ -822,7 +808,11 @@ snn_status_t allocate_streaming(snn_cuda_context_t *c, const snn_cuda_config_t &
     const uint64_t sizes[3] = {(n + 1) * 8, e * 8, e * 4};
     for (int i = 0; i < 3; ++i) {
         if (arrays[i] == nullptr || sizes[i] == 0) continue;
-        if (cudaHostRegister(const_cast<void *>(arrays[i]), sizes[i], cudaHostRegisterDefault) == cudaSuccess)
+        // Read-only first: the device only reads the CSR, and a read-only
+        // file mapping (snn_b200_network_map) can only be locked that way.
+        if (cudaHostRegister(const_cast<void *>(arrays[i]), sizes[i], cudaHostRegisterReadOnly) == cudaSuccess ||
+            (cudaGetLastError(),
+             cudaHostRegister(const_cast<void *>(arrays[i]), sizes[i], cudaHostRegisterDefault) == cudaSuccess))
             c->registered[i] = arrays[i];
         else
             cudaGetLastError();
@@ -844,8 +834,12 @@ snn_status_t allocate_sparse_streaming(snn_cuda_context_t *c, bool *fallback) {
     void *dev[2] = {nullptr, nullptr};
     for (int i = 0; i < 2 && e; ++i) {
         if ((uintptr_t)arrays[i] % 16 != 0 ||
-            cudaHostRegister(const_cast<void *>(arrays[i]), sizes[i], cudaHostRegisterMapped | cudaHostRegisterPortable) !=
-                cudaSuccess ||
+            (cudaHostRegister(const_cast<void *>(arrays[i]), sizes[i],
+                              cudaHostRegisterMapped | cudaHostRegisterPortable | cudaHostRegisterReadOnly) !=
+                 cudaSuccess &&
+             (cudaGetLastError(), cudaHostRegister(const_cast<void *>(arrays[i]), sizes[i],
+                                                   cudaHostRegisterMapped | cudaHostRegisterPortable) !=
+                                      cudaSuccess)) ||
             cudaHostGetDevicePointer(&dev[i], const_cast<void *>(arrays[i]), 0) != cudaSuccess) {
             cudaGetLastError();
             for (int k = 0; k < 2; ++k)
@@ -1115,17 +1109,6 @@ snn_status_t ensure_inject_capacity(snn_cuda_context_t *c, uint64_t count) {
             return SNN_ERR_OUT_OF_MEMORY;
         c->h_inj_cap = count;
     }
-    return SNN_OK;
-}
-
-snn_status_t validate_csr(uint64_t n, uint64_t e, const uint64_t *row_ptr, const uint64_t *col, const float *w) {
-    // src/snn.c:158-180
-    if (n == 0 || row_ptr == nullptr || (e != 0 && (col == nullptr || w == nullptr))) return SNN_ERR_INVALID_ARGUMENT;
-    if (row_ptr[0] != 0 || row_ptr[n] != e) return SNN_ERR_INVALID_ARGUMENT;
-    for (uint64_t i = 0; i < n; ++i)
-        if (row_ptr[i] > row_ptr[i + 1] || row_ptr[i + 1] > e) return SNN_ERR_INVALID_ARGUMENT;
-    for (uint64_t i = 0; i < e; ++i)
-        if (col[i] >= n || !std::isfinite(w[i])) return SNN_ERR_INVALID_ARGUMENT;
     return SNN_OK;
 }
 
@@ -1928,6 +1911,8 @@ snn_status_t snn_b200_network_wrap(snn_size_t n, snn_size_t e, const snn_size_t 
     return SNN_OK;
 }
 
-void snn_b200_network_unwrap(snn_network_t *network) { delete network; }
+void snn_b200_network_unwrap(snn_network_t *network) {
+    if (network != nullptr && !b200host::release_mapping(network)) delete network;
+}
 
 }  // extern "C"

@@ -539,3 +539,34 @@ def test_batched_config1_samples_with_held_frames():
     zero_ext = np.zeros(B * n, np.float32)
     got = ctx.step(zero_ext)
     assert np.array_equal(got[:n], st0.step(np.zeros(n, np.float32)))
+
+
+@pytest.mark.parametrize("mode", ["full", "chunked", "sparse", "ordered"])
+def test_mapped_csr_file_contexts(mode, tmp_path):
+    """A network saved as an snn_b200 CSR file and mapped back read-only
+    (snn_b200_network_map, no copy) drives every policy: FULL push, STREAMING
+    chunked and sparse-requested, and ORDERED. Bit-exact with the CPU step of
+    the original."""
+    lif = default_lif(refractory_steps=2)
+    w = (0.046875, 0.046875) if mode != "ordered" else (-0.2, 0.5)
+    net = ORC.random_pool(20000, 48, *w, 4242, lif=lif)
+    path = str(tmp_path / "net.snncsr")
+    sb.save_network(net, path)
+    mapped = sb.Network.map(path)
+    if mode == "full":
+        ctx = sb.CudaContext.create(mapped, None)
+    elif mode == "ordered":
+        ctx = sb.CudaContext.create(mapped, None, ordered())
+    else:
+        ctx = sb.CudaContext.create(mapped, sb.default_config(prefer_streaming=1),
+                                    opts(streaming=sb.STREAMING_SPARSE if mode == "sparse" else sb.STREAMING_CHUNKED))
+        # Sparse streaming needs the mapping's pages locked; where the OS
+        # refuses to lock file pages the context streams chunks instead.
+        assert ctx.mode == sb.MODE_STREAMING
+    rng = np.random.default_rng(11)
+    frames = [(rng.random(20000) < 0.08).astype(np.float32) * np.float32(1.5) for _ in range(8)]
+    cr, gr, cv, gv = run_pair(net, ctx, 8, ext=lambda t: frames[t])
+    assert first_divergence(cr, gr) is None
+    np.testing.assert_array_equal(bits(cv), bits(gv))
+    ctx.free()
+    mapped.free()
