@@ -515,10 +515,16 @@ def run_b200(args):
         # rows' CSR slices); its kernels (histogram, placement, segmented
         # sort, fold) are timed together as the propagation.
         kernel_name = "ordered push (hist + scatter + segmented sort + fold)"
+    gated = int(lay.get("ordered_csc", 0)) == 1 and args.propagation == "auto"
+    if gated:
+        # A sliced-ELL CSC sits beside the CSR: steps where more than half the
+        # rows fire take propagate_pull_kernel (device-side gate), the rest
+        # propagate_push_kernel; both are timed as the propagation.
+        kernel_name = "propagate_push_kernel + propagate_pull_kernel (dense steps)"
     prop_s = s["propagate_ms"] / 1e3
     achieved = prop_bytes / prop_s / 1e9 if prop_s > 0 else 0.0
     traffic = None
-    if args.propagation not in ("binned", "ordered") and int(lay["index_bits"]) == 32 and timed:
+    if args.propagation not in ("binned", "ordered") and not gated and int(lay["index_bits"]) == 32 and timed:
         traffic = NCU_DRAM_BYTES_PER_EVENT * s["events"] / timed
     step_bytes = (prop_bytes + 25.0 * ctx.local_count * timed
                   + 12.0 * count * timed)

@@ -367,8 +367,9 @@ __global__ void __launch_bounds__(256) propagate_push_kernel(const TIdx *__restr
                                                              const TCol *__restrict__ col,
                                                              const float *__restrict__ w, float *__restrict__ next,
                                                              DevCounters *ctr, int parity, int count_spikes,
-                                                             uint64_t batch_rows) {
+                                                             uint64_t batch_rows, uint32_t pull_above) {
     const uint32_t count = *(volatile uint32_t *)&ctr->list_count[parity];
+    if (pull_above && count > pull_above) return;  // dense step: the pull kernel runs
     const unsigned lane = lane_id();
     const uint64_t gwarp = ((uint64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const uint64_t nwarps = ((uint64_t)gridDim.x * blockDim.x) >> 5;
@@ -512,65 +513,66 @@ __global__ void __launch_bounds__(256) ordered_fold_kernel(uint64_t events, cons
 }
 
 // ----------------------------------------------------------- ordered pull ----
-// Thread per local target. The target's incoming (pre, w) pairs are stored in
-// CSR order (ascending pre, ascending edge); the thread folds the spiking
-// ones in that order, so acc follows exactly the serial CPU fold starting
-// from +0.0f (src/snn.c:898-906), and stores it over the whole target buffer.
-// Each thread streams its own contiguous range four pairs at a time (16-byte
-// loads once aligned), so every lane of every instruction does useful work
-// even when most rows spike. Cost ~ local synapses, whatever the spike
-// count: the ordered push is cheaper unless many rows spike.
-template <typename TPre>
-__device__ __forceinline__ uint32_t spike_bit(const uint32_t *__restrict__ bitmap, TPre p) {
-    return (__ldg(bitmap + ((uint64_t)p >> 5)) >> ((uint32_t)p & 31u)) & 1u;
-}
-
-template <typename TPre>
-__device__ __forceinline__ void load_pre4(const TPre *__restrict__ pre, uint64_t k, uint64_t (&p)[4]) {
-    if constexpr (sizeof(TPre) == 4) {
-        const uint4 v = __ldcs(reinterpret_cast<const uint4 *>(pre + k));
-        p[0] = v.x, p[1] = v.y, p[2] = v.z, p[3] = v.w;
-    } else {
-        const ulonglong2 a = __ldcs(reinterpret_cast<const ulonglong2 *>(pre + k));
-        const ulonglong2 b = __ldcs(reinterpret_cast<const ulonglong2 *>(pre + k + 2));
-        p[0] = a.x, p[1] = a.y, p[2] = b.x, p[3] = b.y;
-    }
-}
+// The pull reads a sliced-ELL (SELL-32) CSC: local targets in blocks of 32;
+// block b holds width_b = max in-degree of its targets slots per target,
+// slot k of target t at sell_off[b] + k*32 + (t % 32), so a warp (one lane
+// per target) loads 32 consecutive entries per slot: every load is coalesced
+// and every lane folds its own target. Each target's in-edges keep CSR order
+// (ascending presynaptic row, ascending edge), and the lane folds the spiking
+// ones in that order from +0.0f, exactly the serial CPU fold
+// (src/snn.c:898-906); padding slots hold an all-ones id and are skipped.
+// Cost ~ local synapses whatever the firing, so it is taken on dense steps:
+// when pull_above != 0 the kernel runs only if the step's spike count
+// exceeds it (the push kernel, launched with the same gate, runs otherwise).
+constexpr int kPullUnroll = 4;
 
 template <typename TPre, typename TIdx>
-__global__ void __launch_bounds__(256) propagate_pull_kernel(uint64_t n_local, const uint64_t *__restrict__ col_ptr,
+__global__ void __launch_bounds__(256) propagate_pull_kernel(uint64_t n_local, const uint64_t *__restrict__ sell_off,
                                                              const TPre *__restrict__ pre,
                                                              const float *__restrict__ w,
                                                              const uint32_t *__restrict__ bitmap,
                                                              float *__restrict__ next, const TIdx *__restrict__ list,
                                                              const uint32_t *__restrict__ out_degree,
-                                                             DevCounters *ctr, int parity, int count_spikes) {
-    const uint64_t stride = (uint64_t)blockDim.x * gridDim.x;
-    for (uint64_t t = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; t < n_local; t += stride) {
-        uint64_t k = col_ptr[t];
-        const uint64_t e = col_ptr[t + 1];
+                                                             DevCounters *ctr, int parity, int count_spikes,
+                                                             uint32_t pull_above) {
+    const uint32_t count = *(volatile uint32_t *)&ctr->list_count[parity];
+    if (pull_above && count <= pull_above) return;  // sparse step: the push kernel runs
+    const unsigned lane = lane_id();
+    const uint64_t gwarp = ((uint64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const uint64_t nwarps = ((uint64_t)gridDim.x * blockDim.x) >> 5;
+    const uint64_t blocks = (n_local + 31) / 32;
+    const TPre pad = (TPre)~(TPre)0;
+    for (uint64_t blk = gwarp; blk < blocks; blk += nwarps) {
+        const uint64_t base = sell_off[blk];
+        const uint64_t width = (sell_off[blk + 1] - base) / 32;
+        const TPre *pp = pre + base + lane;
+        const float *wp = w + base + lane;
         float acc = 0.0f;
-        for (; k < e && (k & 3u); ++k)
-            if (spike_bit(bitmap, pre[k])) acc = __fadd_rn(acc, w[k]);
-        for (; k + 4 <= e; k += 4) {
-            uint64_t p[4];
-            load_pre4(pre, k, p);
-            const uint32_t m = spike_bit(bitmap, p[0]) | spike_bit(bitmap, p[1]) << 1 |
-                               spike_bit(bitmap, p[2]) << 2 | spike_bit(bitmap, p[3]) << 3;
-            if (m) {
-                const float4 wv = __ldcs(reinterpret_cast<const float4 *>(w + k));
-                if (m & 1u) acc = __fadd_rn(acc, wv.x);
-                if (m & 2u) acc = __fadd_rn(acc, wv.y);
-                if (m & 4u) acc = __fadd_rn(acc, wv.z);
-                if (m & 8u) acc = __fadd_rn(acc, wv.w);
-            }
+        uint64_t k = 0;
+        for (; k + kPullUnroll <= width; k += kPullUnroll) {
+            TPre p[kPullUnroll];
+#pragma unroll
+            for (int j = 0; j < kPullUnroll; ++j) p[j] = __ldcs(pp + (k + j) * 32u);
+            uint32_t bit[kPullUnroll];
+#pragma unroll
+            for (int j = 0; j < kPullUnroll; ++j)
+                bit[j] = p[j] != pad ? (__ldg(bitmap + ((uint64_t)p[j] >> 5)) >> ((uint32_t)p[j] & 31u)) & 1u : 0u;
+            float wv[kPullUnroll];
+#pragma unroll
+            for (int j = 0; j < kPullUnroll; ++j) wv[j] = bit[j] ? __ldcs(wp + (k + j) * 32u) : 0.0f;
+#pragma unroll
+            for (int j = 0; j < kPullUnroll; ++j)
+                if (bit[j]) acc = __fadd_rn(acc, wv[j]);
         }
-        for (; k < e; ++k)
-            if (spike_bit(bitmap, pre[k])) acc = __fadd_rn(acc, w[k]);
-        next[t] = acc;
+        for (; k < width; ++k) {
+            const TPre q = pp[k * 32u];
+            if (q != pad && ((__ldg(bitmap + ((uint64_t)q >> 5)) >> ((uint32_t)q & 31u)) & 1u))
+                acc = __fadd_rn(acc, wp[k * 32u]);
+        }
+        const uint64_t t = blk * 32u + lane;
+        if (t < n_local) next[t] = acc;
     }
     // Event statistics: out-degree (towards this rank) of every spiking row.
-    const uint32_t count = *(volatile uint32_t *)&ctr->list_count[parity];
     const uint64_t gthread = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
     const uint64_t nthreads = (uint64_t)gridDim.x * blockDim.x;
     unsigned long long events = 0;
@@ -831,14 +833,23 @@ __global__ void __launch_bounds__(256) gen_fill_keys_kernel(GenParams g, uint64_
     }
 }
 
+// Sorted pass position q holds the pass-local target keys[q] and the global
+// edge id eids[q]; its slot in the target's CSR-ordered in-edge list is
+// k = q0 + q - col_ptr[t], stored at the SELL position of (t, k).
 template <typename TPre>
-__global__ void gather_generated_csc_kernel(GenParams g, const uint64_t *__restrict__ eids, uint64_t e,
-                                            TPre *__restrict__ pre, float *__restrict__ w_out) {
+__global__ void gather_generated_sell_kernel(GenParams g, const uint32_t *__restrict__ keys,
+                                             const uint64_t *__restrict__ eids, uint64_t e, uint64_t t0, uint64_t q0,
+                                             const uint64_t *__restrict__ col_ptr,
+                                             const uint64_t *__restrict__ sell_off, TPre *__restrict__ pre,
+                                             float *__restrict__ w_out) {
     const uint64_t stride = (uint64_t)blockDim.x * gridDim.x;
-    for (uint64_t k = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; k < e; k += stride) {
-        const uint64_t ed = eids[k];
-        pre[k] = (TPre)(ed / g.fanout);
-        w_out[k] = gen_weight(g, ed);
+    for (uint64_t q = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; q < e; q += stride) {
+        const uint64_t ed = eids[q];
+        const uint64_t t = t0 + keys[q];
+        const uint64_t k = q0 + q - col_ptr[t];
+        const uint64_t dst = sell_off[t >> 5] + k * 32u + (t & 31u);
+        pre[dst] = (TPre)(ed / g.fanout);
+        w_out[dst] = gen_weight(g, ed);
     }
 }
 
@@ -935,11 +946,12 @@ static int push_grid(int device) {
 
 void launch_propagate_push(cudaStream_t s, int device, const void *list, int idx_bits, const uint64_t *row_ptr,
                            const void *col, int col_bits, const float *w, float *next, DevCounters *ctr, int parity,
-                           int count_spikes, uint64_t batch_rows) {
+                           int count_spikes, uint64_t batch_rows, uint32_t pull_above) {
 #define B200_PUSH(TI, TC)                                                                                      \
     propagate_push_kernel<TI, TC><<<push_grid<TI, TC>(device), 256, 0, s>>>((const TI *)list, row_ptr,         \
                                                                             (const TC *)col, w, next, ctr,     \
-                                                                            parity, count_spikes, batch_rows)
+                                                                            parity, count_spikes, batch_rows,  \
+                                                                            pull_above)
     if (idx_bits == 32 && col_bits == 32) B200_PUSH(uint32_t, uint32_t);
     else if (idx_bits == 32) B200_PUSH(uint32_t, uint64_t);
     else if (col_bits == 32) B200_PUSH(uint64_t, uint32_t);
@@ -947,13 +959,15 @@ void launch_propagate_push(cudaStream_t s, int device, const void *list, int idx
 #undef B200_PUSH
 }
 
-void launch_propagate_pull(cudaStream_t s, int device, uint64_t n_local, const uint64_t *col_ptr, const void *pre,
+void launch_propagate_pull(cudaStream_t s, int device, uint64_t n_local, const uint64_t *sell_off, const void *pre,
                            int pre_bits, const float *w, const uint32_t *bitmap, float *next, const void *list,
-                           int idx_bits, const uint32_t *out_degree, DevCounters *ctr, int parity, int count_spikes) {
+                           int idx_bits, const uint32_t *out_degree, DevCounters *ctr, int parity, int count_spikes,
+                           uint32_t pull_above) {
     const int grid = sm_count(device) * 8;
-#define B200_PULL(TP, TI)                                                                                   \
-    propagate_pull_kernel<TP, TI><<<grid, 256, 0, s>>>(n_local, col_ptr, (const TP *)pre, w, bitmap, next,   \
-                                                       (const TI *)list, out_degree, ctr, parity, count_spikes)
+#define B200_PULL(TP, TI)                                                                                    \
+    propagate_pull_kernel<TP, TI><<<grid, 256, 0, s>>>(n_local, sell_off, (const TP *)pre, w, bitmap, next,   \
+                                                       (const TI *)list, out_degree, ctr, parity, count_spikes, \
+                                                       pull_above)
     if (pre_bits == 32 && idx_bits == 32) B200_PULL(uint32_t, uint32_t);
     else if (pre_bits == 32) B200_PULL(uint32_t, uint64_t);
     else if (idx_bits == 32) B200_PULL(uint64_t, uint32_t);
@@ -1052,11 +1066,16 @@ cudaError_t sort_pairs_u32_u64(cudaStream_t s, uint32_t *keys, uint32_t *keys_al
     return e;
 }
 
-void launch_gather_generated_csc(cudaStream_t s, int device, const GenParams &g, const uint64_t *eids, uint64_t e,
-                                 void *pre, int pre_bits, float *w_out) {
+void launch_gather_generated_sell(cudaStream_t s, int device, const GenParams &g, const uint32_t *keys,
+                                  const uint64_t *eids, uint64_t e, uint64_t t0, uint64_t q0, const uint64_t *col_ptr,
+                                  const uint64_t *sell_off, void *pre, int pre_bits, float *w_out) {
     const int grid = grid_for(device, 8, e, 256);
-    if (pre_bits == 32) gather_generated_csc_kernel<uint32_t><<<grid, 256, 0, s>>>(g, eids, e, (uint32_t *)pre, w_out);
-    else gather_generated_csc_kernel<uint64_t><<<grid, 256, 0, s>>>(g, eids, e, (uint64_t *)pre, w_out);
+    if (pre_bits == 32)
+        gather_generated_sell_kernel<uint32_t><<<grid, 256, 0, s>>>(g, keys, eids, e, t0, q0, col_ptr, sell_off,
+                                                                     (uint32_t *)pre, w_out);
+    else
+        gather_generated_sell_kernel<uint64_t><<<grid, 256, 0, s>>>(g, keys, eids, e, t0, q0, col_ptr, sell_off,
+                                                                     (uint64_t *)pre, w_out);
 }
 
 void launch_ordered_sdeg(cudaStream_t s, int device, const void *list, int idx_bits, DevCounters *ctr, int parity,

@@ -126,14 +126,18 @@ void launch_compact(cudaStream_t s, int device, const uint32_t *bitmap, uint64_t
 // topology adding into the current slice starting at g - g % batch_rows.
 void launch_propagate_push(cudaStream_t s, int device, const void *list, int idx_bits, const uint64_t *row_ptr,
                            const void *col, int col_bits, const float *w, float *next, DevCounters *ctr,
-                           int parity, int count_spikes, uint64_t batch_rows = 0);
+                           int parity, int count_spikes, uint64_t batch_rows = 0, uint32_t pull_above = 0);
 
-// Ordered pull over a CSC: for every local target, folds the weights of its
-// spiking presynaptic rows in (row, edge) order starting from 0.0f.
-void launch_propagate_pull(cudaStream_t s, int device, uint64_t n_local, const uint64_t *col_ptr,
+// Ordered pull over a sliced-ELL CSC (blocks of 32 local targets, slot k of
+// target t at sell_off[t/32] + 32k + t%32, padding ids all ones): for every
+// local target, folds the weights of its spiking presynaptic rows in (row,
+// edge) order starting from 0.0f. pull_above != 0: a push kernel launched
+// with the same gate handles steps of at most pull_above spikes; the pull
+// runs only above it.
+void launch_propagate_pull(cudaStream_t s, int device, uint64_t n_local, const uint64_t *sell_off,
                            const void *pre, int pre_bits, const float *w, const uint32_t *bitmap, float *next,
                            const void *list, int idx_bits, const uint32_t *out_degree, DevCounters *ctr,
-                           int parity, int count_spikes);
+                           int parity, int count_spikes, uint32_t pull_above = 0);
 
 // STREAMING: one chunk of `rows` rows starting at row0, with the chunk's raw
 // row_ptr slice (rows+1 entries, absolute edge offsets) and its edges starting
@@ -184,7 +188,7 @@ cudaError_t exclusive_scan_u64(cudaStream_t s, const uint64_t *in, uint64_t *out
 //  * gen_fill_keys: (target - range_lo, global edge id) pairs in CSR order;
 //  * sort_pairs_u32_u64: stable radix sort by target, so each target's
 //    in-edges stay in ascending edge id = CSR order;
-//  * gather_generated_csc: presynaptic row = id / fanout (every row with
+//  * gather_generated_sell: presynaptic row = id / fanout (every row with
 //    edges owns [row*F, row*F+F)) and the weight recomputed from the id.
 void launch_gen_indegree(cudaStream_t s, int device, const GenParams &g, uint64_t lo, uint64_t hi,
                          unsigned long long *indeg);
@@ -195,8 +199,9 @@ void launch_gen_fill_keys(cudaStream_t s, int device, const GenParams &g, uint64
 cudaError_t sort_pairs_u32_u64(cudaStream_t s, uint32_t *keys, uint32_t *keys_alt, uint64_t *vals,
                                uint64_t *vals_alt, uint64_t n, int end_bit, void *temp, size_t *temp_bytes,
                                bool *result_in_alt);
-void launch_gather_generated_csc(cudaStream_t s, int device, const GenParams &g, const uint64_t *eids, uint64_t e,
-                                 void *pre, int pre_bits, float *w_out);
+void launch_gather_generated_sell(cudaStream_t s, int device, const GenParams &g, const uint32_t *keys,
+                                  const uint64_t *eids, uint64_t e, uint64_t t0, uint64_t q0, const uint64_t *col_ptr,
+                                  const uint64_t *sell_off, void *pre, int pre_bits, float *w_out);
 
 // Ordered push (bit-exact, event-driven), in step order: sdeg of the
 // spiking rows -> scan_degrees_u64 (eoff, rows+1 entries) -> per row range:

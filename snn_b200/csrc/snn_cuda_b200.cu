@@ -135,7 +135,10 @@ struct snn_cuda_context {
     // per-row spiking degrees and event offsets over all rows, and the
     // double-buffered (target, weight) event arrays of ocap entries.
     bool opull = false;    // SNN_B200_ORDERED_PULL: always the pull over a CSC (no CSR)
-    bool has_csc = false;  // ordered push with the CSC as well: dense steps pull
+    bool has_csc = false;  // a SELL CSC beside the CSR: dense steps pull
+    uint64_t *d_sell_off = nullptr;  // SELL-32 block offsets (blocks + 1); d_pre / d_cw are the slot arrays
+    uint64_t sell_slots = 0;
+    uint32_t pull_above = 0;  // PUSH with a SELL CSC: steps with more spikes than this pull
     uint64_t pull_div = 10;  // pull when a step's events exceed local synapses / pull_div
     uint64_t pull_steps = 0;
     uint32_t *d_sdeg = nullptr;
@@ -256,7 +259,7 @@ void free_context(snn_cuda_context_t *c) {
         if (c->peer_ipc[r]) cudaIpcCloseMemHandle(c->peer_x[r]);
     if (c->d_xbuf) cudaFree(c->d_xbuf);
     void *dev[] = {c->d_v, c->d_cur_pair, c->d_ext, c->d_refr, c->d_spikes, c->d_ws, c->d_row_ptr, c->d_col,
-                   c->d_w, c->d_col_ptr, c->d_pre, c->d_cw, c->d_deg, c->d_sdeg, c->d_eoff, c->d_okeys[0], c->d_okeys[1], c->d_ovals[0], c->d_ovals[1], c->d_otemp,
+                   c->d_w, c->d_col_ptr, c->d_pre, c->d_cw, c->d_deg, c->d_sell_off, c->d_sdeg, c->d_eoff, c->d_okeys[0], c->d_okeys[1], c->d_ovals[0], c->d_ovals[1], c->d_otemp,
                    c->d_chunk_row, c->d_chunk_col,
                    c->d_chunk_w, c->d_inj_idx, c->d_inj_val, c->d_bin_mem};
     for (void *p : dev)
@@ -631,7 +634,7 @@ snn_status_t ordered_push_step(snn_cuda_context_t *c, int parity, float *next, b
         // cheaper than sorting this many events.
         b200::launch_ordered_sdeg(c->stream, c->device, c->d_list, c->idx_bits, c->d_ctr, parity, n, c->d_row_ptr,
                                   c->d_sdeg, 1, brows);
-        b200::launch_propagate_pull(c->stream, c->device, c->n_local, c->d_col_ptr, c->d_pre, c->idx_bits, c->d_cw,
+        b200::launch_propagate_pull(c->stream, c->device, c->n_local, c->d_sell_off, c->d_pre, c->idx_bits, c->d_cw,
                                     bitmap, next, c->d_list, c->idx_bits, c->d_deg, c->d_ctr, parity, !sharded);
         c->launches += 2;
         c->pull_steps++;
@@ -674,14 +677,60 @@ snn_status_t ordered_push_step(snn_cuda_context_t *c, int parity, float *next, b
     return SNN_OK;
 }
 
-// FULL ordered topology: a CSC of the rank's targets built on the host with a
-// stable counting sort, so every target's incoming edges keep CSR order
-// (ascending presynaptic row, ascending edge index). Seams #8-#10 / #11-#13
-// as for push; the out-degree table for statistics follows.
+// Sliced-ELL layout of a CSC given its column pointers: blocks of 32 local
+// targets, each as wide as its largest in-degree.
+std::vector<uint64_t> sell_offsets(const std::vector<uint64_t> &col_ptr, uint64_t nl) {
+    const uint64_t blocks = (nl + 31) / 32;
+    std::vector<uint64_t> off(blocks + 1, 0);
+    for (uint64_t b = 0; b < blocks; ++b) {
+        uint64_t wmax = 0;
+        for (uint64_t t = b * 32; t < std::min(nl, b * 32 + 32); ++t) wmax = std::max(wmax, col_ptr[t + 1] - col_ptr[t]);
+        off[b + 1] = off[b] + 32 * wmax;
+    }
+    return off;
+}
+
+// Allocates the SELL slot arrays (padding: all-ones ids, zero weights) and
+// uploads the block offsets.
+snn_status_t alloc_sell(snn_cuda_context_t *c, const std::vector<uint64_t> &off) {
+    const uint64_t slots = off.back();
+    const int pre_bytes = c->idx_bits / 8;
+    c->sell_slots = slots;
+    if (cudaMalloc(&c->d_sell_off, off.size() * 8) != cudaSuccess ||
+        (slots && (cudaMalloc(&c->d_pre, slots * pre_bytes) != cudaSuccess ||
+                   cudaMalloc((void **)&c->d_cw, slots * 4) != cudaSuccess))) {
+        cudaGetLastError();
+        set_error("pull topology", "out of device memory for the sliced-ELL CSC");
+        return SNN_ERR_OUT_OF_MEMORY;
+    }
+    snn_status_t st = cuda_status(cudaMemcpyAsync(c->d_sell_off, off.data(), off.size() * 8, cudaMemcpyHostToDevice,
+                                                  c->stream));
+    if (st == SNN_OK && slots) st = cuda_status(cudaMemsetAsync(c->d_pre, 0xff, slots * pre_bytes, c->stream));
+    if (st == SNN_OK && slots) st = cuda_status(cudaMemsetAsync(c->d_cw, 0, slots * 4, c->stream));
+    if (st == SNN_OK) st = cuda_status(cudaStreamSynchronize(c->stream));
+    return st;
+}
+
+// Releases a pull topology (a hybrid context that could not finish one goes on without it).
+void free_sell(snn_cuda_context_t *c) {
+    cudaStreamSynchronize(c->stream);
+    for (void **p : {(void **)&c->d_sell_off, &c->d_pre, (void **)&c->d_cw, (void **)&c->d_col_ptr,
+                     (void **)&c->d_deg}) {
+        if (*p) cudaFree(*p);
+        *p = nullptr;
+    }
+    cudaGetLastError();
+    c->sell_slots = 0;
+}
+
+// FULL pull topology from a host network: the CSC of the rank's targets built
+// with a stable counting sort (every target's in-edges keep CSR order:
+// ascending presynaptic row, ascending edge index), stored sliced-ELL; plus
+// the out-degree table for event statistics.
 snn_status_t upload_full_ordered(snn_cuda_context_t *c, const snn_network_t *net) {
     const uint64_t n = net->neuron_count;
     const uint64_t nl = c->n_local;
-    std::vector<uint64_t> col_ptr, pre;
+    std::vector<uint64_t> col_ptr, off, pre;
     std::vector<float> w;
     std::vector<uint32_t> deg;
     try {
@@ -697,32 +746,29 @@ snn_status_t upload_full_ordered(snn_cuda_context_t *c, const snn_network_t *net
             }
         }
         for (uint64_t t = 0; t < nl; ++t) col_ptr[t + 1] += col_ptr[t];
-        pre.resize(col_ptr[nl]);
-        w.resize(col_ptr[nl]);
-        std::vector<uint64_t> cursor(col_ptr.begin(), col_ptr.end() - 1);
+        off = sell_offsets(col_ptr, nl);
+        pre.assign(off.back(), ~0ull);
+        w.assign(off.back(), 0.0f);
+        std::vector<uint64_t> fill(nl, 0);
         for (uint64_t i = 0; i < n; ++i) {
             for (uint64_t q = net->row_ptr[i]; q < net->row_ptr[i + 1]; ++q) {
                 const uint64_t t = net->col_idx[q];
                 if (t >= c->lo && t < c->hi) {
-                    const uint64_t k = cursor[t - c->lo]++;
-                    pre[k] = i;
-                    w[k] = net->weights[q];
+                    const uint64_t tl = t - c->lo;
+                    const uint64_t dst = off[tl >> 5] + fill[tl]++ * 32 + (tl & 31);
+                    pre[dst] = i;
+                    w[dst] = net->weights[q];
                 }
             }
         }
     } catch (const std::bad_alloc &) {
         return SNN_ERR_OUT_OF_MEMORY;
     }
-    const uint64_t e = col_ptr[nl];
-    c->e_local = e;
+    c->e_local = col_ptr[nl];
     snn_status_t st;
-    const int pre_bits = c->idx_bits;
-    if ((st = dmalloc((void **)&c->d_col_ptr, nl + 1, 8)) != SNN_OK) return st;
-    if ((st = dmalloc(&c->d_pre, e, pre_bits / 8)) != SNN_OK) return st;
-    if ((st = dmalloc((void **)&c->d_cw, e, 4)) != SNN_OK) return st;
-    if ((st = h2d(c, c->d_col_ptr, col_ptr.data(), (nl + 1) * 8)) != SNN_OK) return st;
-    if ((st = upload_cols(c, c->d_pre, pre.data(), e, 0, pre_bits)) != SNN_OK) return st;
-    if ((st = h2d(c, c->d_cw, w.data(), e * 4)) != SNN_OK) return st;
+    if ((st = alloc_sell(c, off)) != SNN_OK) return st;
+    if ((st = upload_cols(c, c->d_pre, pre.data(), off.back(), 0, c->idx_bits)) != SNN_OK) return st;
+    if ((st = h2d(c, c->d_cw, w.data(), off.back() * 4)) != SNN_OK) return st;
     if ((st = dmalloc((void **)&c->d_deg, n, 4)) != SNN_OK) return st;
     if ((st = h2d(c, c->d_deg, deg.data(), n * 4)) != SNN_OK) return st;
     return cuda_status(cudaStreamSynchronize(c->stream));
@@ -1026,17 +1072,26 @@ snn_status_t enqueue_step(snn_cuda_context_t *c, bool has_ext) {
         if (c->propagation == SNN_B200_PROPAGATE_ORDERED && !c->opull) {
             if ((st = ordered_push_step(c, parity, next, sharded, peer ? xbitmap : c->d_bitmap)) != SNN_OK) return st;
         } else if (c->propagation == SNN_B200_PROPAGATE_ORDERED)
-            b200::launch_propagate_pull(c->stream, c->device, c->n_local, c->d_col_ptr, c->d_pre, c->idx_bits,
+            b200::launch_propagate_pull(c->stream, c->device, c->n_local, c->d_sell_off, c->d_pre, c->idx_bits,
                                         c->d_cw, peer ? xbitmap : c->d_bitmap, next, c->d_list, c->idx_bits,
                                         c->d_deg, c->d_ctr, parity, !sharded);
         else if (c->binned) {
             const cudaError_t e = b200::launch_propagate_binned(c->stream, c->d_list, c->idx_bits, next, c->d_ctr,
                                                                 parity, !sharded, c->bin);
             if (e != cudaSuccess) return cuda_status(e);
-        } else
+        } else {
+            // With a SELL CSC both kernels are launched behind the same
+            // device-side gate on this step's spike count: one of them runs.
             b200::launch_propagate_push(c->stream, c->device, c->d_list, c->idx_bits, c->d_row_ptr, c->d_col,
                                         c->col_bits, c->d_w, next, c->d_ctr, parity, !sharded,
-                                        c->batch > 1 ? c->n_rows : 0);
+                                        c->batch > 1 ? c->n_rows : 0, c->has_csc ? c->pull_above : 0);
+            if (c->has_csc) {
+                b200::launch_propagate_pull(c->stream, c->device, c->n_local, c->d_sell_off, c->d_pre, c->idx_bits,
+                                            c->d_cw, peer ? xbitmap : c->d_bitmap, next, c->d_list, c->idx_bits,
+                                            c->d_deg, c->d_ctr, parity, !sharded, c->pull_above);
+                c->launches++;
+            }
+        }
         if ((st = check_launch(c)) != SNN_OK) return st;
     } else if (c->streaming == SNN_B200_STREAMING_SPARSE) {
         // Sparse STREAMING: spiking rows read straight from mapped host memory.
@@ -1188,10 +1243,7 @@ snn_status_t generate_full(snn_cuda_context_t *c, const b200::GenParams &g, uint
 // recomputed from the id, bit-identical to snn_build_random_pool.
 snn_status_t build_generated_csc(snn_cuda_context_t *c, const b200::GenParams &g) {
     const uint64_t n = g.n, nl = c->n_local, lo = c->lo;
-    const int pre_bytes = c->idx_bits / 8;
     snn_status_t st;
-    c->binned = false;
-    c->passes = 1;
     if ((st = dmalloc((void **)&c->d_col_ptr, nl + 1, 8)) != SNN_OK) return st;
     if ((st = dmalloc((void **)&c->d_deg, n, 4)) != SNN_OK) return st;
     {
@@ -1223,8 +1275,15 @@ snn_status_t build_generated_csc(snn_cuda_context_t *c, const b200::GenParams &g
         return st;
     const uint64_t e = col_ptr[nl];
     c->e_local = e;
-    if ((st = dmalloc(&c->d_pre, e, pre_bytes)) != SNN_OK) return st;
-    if ((st = dmalloc((void **)&c->d_cw, e, 4)) != SNN_OK) return st;
+    {
+        std::vector<uint64_t> off;
+        try {
+            off = sell_offsets(col_ptr, nl);
+        } catch (const std::bad_alloc &) {
+            return SNN_ERR_OUT_OF_MEMORY;
+        }
+        if ((st = alloc_sell(c, off)) != SNN_OK) return st;
+    }
     if (e == 0) return cuda_status(cudaStreamSynchronize(c->stream));
 
     // Pass size: what fits in the free memory at 24 B per edge (keys and ids,
@@ -1290,9 +1349,9 @@ snn_status_t build_generated_csc(snn_cuda_context_t *c, const b200::GenParams &g
         if ((st = cuda_status(b200::sort_pairs_u32_u64(c->stream, keys, keys_alt, ids, ids_alt, ep, end_bit, temp,
                                                        &tb, &alt))) != SNN_OK)
             break;
-        b200::launch_gather_generated_csc(c->stream, c->device, g, alt ? ids_alt : ids, ep,
-                                          (char *)c->d_pre + col_ptr[a] * pre_bytes, c->idx_bits,
-                                          c->d_cw + col_ptr[a]);
+        b200::launch_gather_generated_sell(c->stream, c->device, g, alt ? keys_alt : keys, alt ? ids_alt : ids, ep,
+                                           a, col_ptr[a], c->d_col_ptr, c->d_sell_off, c->d_pre, c->idx_bits,
+                                           c->d_cw);
         st = cuda_status(cudaGetLastError());
     }
     if (st == SNN_OK) st = cuda_status(cudaStreamSynchronize(c->stream));
@@ -1306,26 +1365,52 @@ snn_status_t build_generated_csc(snn_cuda_context_t *c, const b200::GenParams &g
     return st;
 }
 
-// ORDERED contexts keep a CSC beside the push CSR when the device has room for
-// it (and for a usable event buffer): dense steps then take the pull.
-// SNN_B200_ORDERED_PULL_DIV (environment) sets the density threshold
-// (events > local synapses / div; 0 keeps every step on the ordered push).
-snn_status_t add_ordered_csc(snn_cuda_context_t *c, const snn_network_t *net, const b200::GenParams *g) {
-    if (const char *env = std::getenv("SNN_B200_ORDERED_PULL_DIV")) c->pull_div = std::strtoull(env, nullptr, 10);
-    if (c->pull_div == 0 || c->e_local == 0 || c->batch > 1) return SNN_OK;
+// FULL contexts keep a sliced-ELL CSC beside the push CSR when the device
+// has room for it (and for a working margin): dense steps then take the pull,
+// which reads every local synapse once instead of one atomic (PUSH) or one
+// sorted event (ORDERED) per event. ORDERED decides per step from the exact
+// event count (events > local synapses / SNN_B200_ORDERED_PULL_DIV, default
+// 10); PUSH decides on the device from the spike count (spikes > rows /
+// SNN_B200_PUSH_PULL_DIV, default 2), launching both kernels behind the same
+// gate so no host round trip is added. A divisor of 0 disables the pull.
+snn_status_t add_pull_topology(snn_cuda_context_t *c, const snn_network_t *net, const b200::GenParams *g) {
+    const bool ordered = c->propagation == SNN_B200_PROPAGATE_ORDERED;
+    if (!ordered && (c->propagation != SNN_B200_PROPAGATE_PUSH || c->binned || c->mode != SNN_CUDA_MODE_FULL))
+        return SNN_OK;
+    // Measured at config 2 on B200: the pull takes ~33 ms whatever the
+    // firing; the ordered push costs about as much at ~1.5e9 events, the
+    // atomic push at ~5.6e9 (56% firing at fanout 1000).
+    uint64_t div = ordered ? 10 : 2;
+    if (const char *env = std::getenv(ordered ? "SNN_B200_ORDERED_PULL_DIV" : "SNN_B200_PUSH_PULL_DIV"))
+        div = std::strtoull(env, nullptr, 10);
+    c->pull_div = div;
+    if (div == 0 || c->e_local == 0 || c->batch > 1) return SNN_OK;
+    if (!ordered && c->n_rows / div > 0xffffffffull) return SNN_OK;
     size_t free_b = 0, total_b = 0;
     if (cudaMemGetInfo(&free_b, &total_b) != cudaSuccess) return SNN_ERR_CUDA;
-    const uint64_t csc = (c->n_local + 1) * 8 + c->e_local * (c->idx_bits / 8 + 4) + c->n_global * 4;
-    const uint64_t reserve = (2 * (c->n_global + 1) * 8) + (4ull << 30);  // build scratch + event buffers
-    if (csc + reserve > free_b) return SNN_OK;  // no room: every step takes the ordered push
+    // Padding of the sliced ELL: about 1.07x at fan-in 1000; budget 1.15x.
+    const uint64_t sell = (uint64_t)((double)c->e_local * 1.15) * (c->idx_bits / 8 + 4) + (c->n_local + 1) * 8 +
+                          c->n_global * 4;
+    const uint64_t reserve = (2 * (c->n_rows + 1) * 8) + (4ull << 30);  // build scratch + working margin
+    if (sell + reserve > free_b) return SNN_OK;  // no room: every step takes the push
     const uint64_t e_push = c->e_local;
     snn_status_t st = net ? upload_full_ordered(c, net) : build_generated_csc(c, *g);
+    if (st == SNN_ERR_OUT_OF_MEMORY) {  // the estimate was short: go on without the pull
+        free_sell(c);
+        c->e_local = e_push;
+        return SNN_OK;
+    }
     if (st != SNN_OK) return st;
     if (c->e_local != e_push) {
-        set_error("ordered setup", "CSC and CSR synapse counts differ");
+        set_error("pull topology", "CSC and CSR synapse counts differ");
         return SNN_ERR_CUDA;
     }
+    if (c->d_col_ptr) {  // only the build needs the column pointers
+        cudaFree(c->d_col_ptr);
+        c->d_col_ptr = nullptr;
+    }
     c->has_csc = true;
+    if (!ordered) c->pull_above = (uint32_t)std::max<uint64_t>(1, c->n_rows / div);
     return SNN_OK;
 }
 
@@ -1333,9 +1418,11 @@ snn_status_t finish_generated(snn_cuda_context_t *c, const b200::GenParams &g, u
                               snn_cuda_context_t **out) {
     snn_status_t st = SNN_OK;
     c->mode = SNN_CUDA_MODE_FULL;
-    if (c->propagation != SNN_B200_PROPAGATE_ORDERED) st = generate_full(c, g, e_total);
+    if (c->propagation != SNN_B200_PROPAGATE_ORDERED) {
+        if ((st = generate_full(c, g, e_total)) == SNN_OK) st = add_pull_topology(c, nullptr, &g);
+    }
     else if (!c->opull) {
-        if ((st = generate_full(c, g, e_total)) == SNN_OK && (st = add_ordered_csc(c, nullptr, &g)) == SNN_OK)
+        if ((st = generate_full(c, g, e_total)) == SNN_OK && (st = add_pull_topology(c, nullptr, &g)) == SNN_OK)
             st = setup_ordered_push(c);
     } else if (c->n_local > 0xffffffffull) st = SNN_ERR_UNSUPPORTED;  // 32-bit sort keys
     else st = build_generated_csc(c, g);
@@ -1401,9 +1488,14 @@ snn_status_t snn_b200_create(const snn_network_t *network, const snn_cuda_config
     const bool full_only = c->world > 1 || c->propagation == SNN_B200_PROPAGATE_ORDERED || c->batch > 1;
     if (full_only || (!cfg.prefer_streaming && full_push_bytes(c, network->synapse_count) <= env.budget)) {
         c->mode = SNN_CUDA_MODE_FULL;
-        if (c->propagation != SNN_B200_PROPAGATE_ORDERED) st = upload_full_push(c, network);
-        else if (c->opull) st = upload_full_ordered(c, network);
-        else if ((st = upload_full_push(c, network)) == SNN_OK && (st = add_ordered_csc(c, network, nullptr)) == SNN_OK)
+        if (c->propagation != SNN_B200_PROPAGATE_ORDERED) {
+            st = upload_full_push(c, network);
+            // The reference entry point (no options) and explicit VRAM budgets
+            // keep the plain push topology.
+            if (st == SNN_OK && options != nullptr && cfg.max_vram_bytes == 0)
+                st = add_pull_topology(c, network, nullptr);
+        } else if (c->opull) st = upload_full_ordered(c, network);
+        else if ((st = upload_full_push(c, network)) == SNN_OK && (st = add_pull_topology(c, network, nullptr)) == SNN_OK)
             st = setup_ordered_push(c);
     } else {
         c->mode = SNN_CUDA_MODE_STREAMING;
@@ -1801,7 +1893,8 @@ snn_status_t snn_b200_get_layout(const snn_cuda_context_t *c, snn_b200_layout_t 
         out->device_topology_bytes = 2 * ((c->slot_rows + 1) * 8 + c->slot_edges * 12);
     else if (c->opull || c->has_csc)
         out->device_topology_bytes = (c->has_csc ? (c->n_rows + 1) * 8 + c->e_local * (c->col_bits / 8 + 4) : 0) +
-                                     (c->n_local + 1) * 8 + c->e_local * (c->idx_bits / 8 + 4) + c->n_global * 4;
+                                     ((c->n_local + 31) / 32 + 1) * 8 + c->sell_slots * (c->idx_bits / 8 + 4) +
+                                     c->n_rows * 4;
     else
         out->device_topology_bytes = (c->n_rows + 1) * 8 + c->e_local * (c->col_bits / 8 + 4);
     out->binned = c->binned ? 1u : 0u;

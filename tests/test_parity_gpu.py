@@ -570,3 +570,39 @@ def test_mapped_csr_file_contexts(mode, tmp_path):
     np.testing.assert_array_equal(bits(cv), bits(gv))
     ctx.free()
     mapped.free()
+
+
+@pytest.mark.parametrize("generated", [False, True])
+def test_push_with_pull_gate_dyadic_bit_exact(generated, monkeypatch):
+    """PUSH contexts keep a sliced-ELL CSC beside the CSR when memory allows:
+    steps with more spikes than rows / SNN_B200_PUSH_PULL_DIV take the pull
+    kernel, the others the atomic push, chosen on the device. Frames alternate
+    between sparse and dense drive so both kernels run; one shared dyadic
+    weight makes every sum exact, so both equal the CPU step bit for bit."""
+    monkeypatch.setenv("SNN_B200_PUSH_PULL_DIV", "4")
+    lif = default_lif(v_rest=0.0, v_reset=0.0, v_threshold=1.0, input_scale=1.0, refractory_steps=1)
+    n, f = 3001, 700
+    net = ORC.random_pool(n, f, 0.0009765625, 0.0009765625, 12, lif=lif)
+    if generated:
+        ctx = sb.CudaContext.random_pool(n, f, 0.0009765625, 0.0009765625, 12, lif=lif, options=opts())
+    else:
+        ctx = sb.CudaContext.create(net, None, opts())
+    assert ctx.layout["ordered_csc"] == 1
+    rng = np.random.default_rng(8)
+    frames = [(rng.random(n) < (0.6 if t % 3 == 0 else 0.02)).astype(np.float32) * np.float32(1.5)
+              for t in range(12)]
+    cr, gr, cv, gv = run_pair(net, ctx, 12, ext=lambda t: frames[t])
+    assert first_divergence(cr, gr) is None
+    dense = (cr.sum(axis=1) > n // 4).sum()
+    assert 0 < dense < 12
+    np.testing.assert_array_equal(bits(cv), bits(gv))
+    assert ctx.stats()["events"] == int(cr.sum()) * f
+
+
+def test_push_pull_gate_disabled_keeps_plain_push(monkeypatch):
+    monkeypatch.setenv("SNN_B200_PUSH_PULL_DIV", "0")
+    net = ORC.random_pool(2000, 50, 0.1, 0.2, 3)
+    ctx = sb.CudaContext.create(net, None, opts())
+    assert ctx.layout["ordered_csc"] == 0
+    ref = sb.CudaContext.create(net, None)  # the reference entry point never adds it
+    assert ref.layout["ordered_csc"] == 0
