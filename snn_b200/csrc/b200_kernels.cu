@@ -15,6 +15,8 @@
 #include <cub/device/device_scan.cuh>
 #include <thrust/iterator/transform_iterator.h>
 
+#include <algorithm>
+#include <cstdlib>
 #include <mutex>
 #include <vector>
 
@@ -581,6 +583,127 @@ __global__ void __launch_bounds__(256) propagate_pull_kernel(uint64_t n_local, c
     step_epilogue(ctr, parity, count_spikes, count);
 }
 
+// Chunked variant (the default when the layout was built chunked): the
+// presynaptic ids are cut into chunks of kPullChunkWords bitmap words
+// (1.8M neurons) and every (block, chunk) has its own slot run, so a CTA can
+// stage one chunk of the bitmap in shared memory and serve every spike-bit
+// lookup from there instead of from L1/L2 (one sector per lookup). A CTA
+// takes sweeps of 32 warps x 4 blocks; each lane keeps its 4 targets' sums
+// in registers across the chunks, which are visited in ascending order, so
+// the fold order is still ascending presynaptic row, ascending edge.
+constexpr uint32_t kPullChunkWords = 56320;  // 220 KB of shared memory
+constexpr int kPullSmemThreads = 1024;
+constexpr int kPullBlocksPerWarp = 4;
+constexpr int kPullSmemUnroll = 8;  // slot loads in flight per lane
+
+template <typename TPre, typename TIdx>
+__global__ void __launch_bounds__(kPullSmemThreads, 1)
+    propagate_pull_smem_kernel(uint64_t n_local, uint32_t chunks, uint64_t chunk_words,
+                               const uint64_t *__restrict__ sell_off,
+                               const TPre *__restrict__ pre, const float *__restrict__ w,
+                               const uint32_t *__restrict__ bitmap, uint64_t words, float *__restrict__ next,
+                               const TIdx *__restrict__ list, const uint32_t *__restrict__ out_degree,
+                               DevCounters *ctr, int parity, int count_spikes, uint32_t pull_above) {
+    extern __shared__ __align__(16) uint32_t s_bits[];
+    const uint32_t count = *(volatile uint32_t *)&ctr->list_count[parity];
+    if (pull_above && count <= pull_above) return;  // sparse step: the push kernel runs
+    const unsigned lane = lane_id();
+    const unsigned warp = threadIdx.x >> 5;
+    const uint64_t blocks = (n_local + 31) / 32;
+    constexpr uint64_t kSweep = (kPullSmemThreads / 32) * kPullBlocksPerWarp;
+    const uint64_t sweeps = (blocks + kSweep - 1) / kSweep;
+    const TPre pad = (TPre)~(TPre)0;
+    for (uint64_t sw = blockIdx.x; sw < sweeps; sw += gridDim.x) {
+        const uint64_t b0 = sw * kSweep + (uint64_t)warp * kPullBlocksPerWarp;
+        float acc[kPullBlocksPerWarp];
+#pragma unroll
+        for (int j = 0; j < kPullBlocksPerWarp; ++j) acc[j] = 0.0f;
+        for (uint32_t c = 0; c < chunks; ++c) {
+            const uint64_t w0 = (uint64_t)c * chunk_words;
+            const uint64_t cw = words - w0 < chunk_words ? words - w0 : chunk_words;
+            __syncthreads();  // every warp is done with the previous chunk
+            const uint32_t *src = bitmap + w0;
+            if ((((uintptr_t)src) & 15u) == 0) {
+                const uint64_t cw4 = cw / 4;
+                for (uint64_t i = threadIdx.x; i < cw4; i += blockDim.x)
+                    reinterpret_cast<uint4 *>(s_bits)[i] = __ldcg(reinterpret_cast<const uint4 *>(src) + i);
+                for (uint64_t i = cw4 * 4 + threadIdx.x; i < cw; i += blockDim.x) s_bits[i] = __ldcg(src + i);
+            } else {
+                for (uint64_t i = threadIdx.x; i < cw; i += blockDim.x) s_bits[i] = __ldcg(src + i);
+            }
+            __syncthreads();
+            const uint64_t id0 = w0 * 32u;
+#pragma unroll
+            for (int j = 0; j < kPullBlocksPerWarp; ++j) {
+                const uint64_t b = b0 + j;
+                if (b >= blocks) break;
+                const uint64_t base = sell_off[b * chunks + c];
+                const uint64_t width = (sell_off[b * chunks + c + 1] - base) / 32;
+                const TPre *pp = pre + base + lane;
+                const float *wp = w + base + lane;
+                float a = acc[j];
+                uint64_t k = 0;
+                // Software-pipelined: the next group's ids are in flight
+                // while this group's bits are looked up and weights folded.
+                TPre q[kPullSmemUnroll];
+                bool have = kPullSmemUnroll <= width;
+                if (have) {
+#pragma unroll
+                    for (int u = 0; u < kPullSmemUnroll; ++u) q[u] = __ldcs(pp + (uint64_t)u * 32u);
+                }
+                while (have) {
+                    const uint64_t kn = k + kPullSmemUnroll;
+                    const bool more = kn + kPullSmemUnroll <= width;
+                    TPre qn[kPullSmemUnroll];
+                    if (more) {
+#pragma unroll
+                        for (int u = 0; u < kPullSmemUnroll; ++u) qn[u] = __ldcs(pp + (kn + u) * 32u);
+                    }
+                    uint32_t bits = 0;
+#pragma unroll
+                    for (int u = 0; u < kPullSmemUnroll; ++u) {
+                        const uint64_t r = (uint64_t)q[u] - id0;
+                        bits |= (q[u] != pad ? (s_bits[r >> 5] >> (r & 31u)) & 1u : 0u) << u;
+                    }
+                    float wv[kPullSmemUnroll];
+#pragma unroll
+                    for (int u = 0; u < kPullSmemUnroll; ++u)
+                        wv[u] = (bits >> u) & 1u ? __ldcs(wp + (k + u) * 32u) : 0.0f;
+#pragma unroll
+                    for (int u = 0; u < kPullSmemUnroll; ++u)
+                        if ((bits >> u) & 1u) a = __fadd_rn(a, wv[u]);
+                    if (more) {
+#pragma unroll
+                        for (int u = 0; u < kPullSmemUnroll; ++u) q[u] = qn[u];
+                    }
+                    k = kn;
+                    have = more;
+                }
+                for (; k < width; ++k) {
+                    const TPre q = pp[k * 32u];
+                    if (q != pad) {
+                        const uint64_t r = (uint64_t)q - id0;
+                        if ((s_bits[r >> 5] >> (r & 31u)) & 1u) a = __fadd_rn(a, wp[k * 32u]);
+                    }
+                }
+                acc[j] = a;
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < kPullBlocksPerWarp; ++j) {
+            const uint64_t t = (b0 + j) * 32u + lane;
+            if (b0 + j < blocks && t < n_local) next[t] = acc[j];
+        }
+    }
+    // Event statistics: out-degree (towards this rank) of every spiking row.
+    const uint64_t gthread = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const uint64_t nthreads = (uint64_t)gridDim.x * blockDim.x;
+    unsigned long long events = 0;
+    for (uint64_t s = gthread; s < count; s += nthreads) events += out_degree[(uint64_t)list[s]];
+    block_add_u64(events, &ctr->events);
+    step_epilogue(ctr, parity, count_spikes, count);
+}
+
 // ----------------------------------------------------------- streaming ----
 // One chunk of rows whose CSR slice was just copied in: warp per 32 rows,
 // ballot over the rows' spike bits, then the warp strides each spiking row.
@@ -800,6 +923,32 @@ __global__ void __launch_bounds__(256) gen_indegree_kernel(GenParams g, uint64_t
     }
 }
 
+// Per local target and presynaptic chunk (pre / chunk_neurons): how many of
+// the target's in-edges come from that chunk (chunked sliced-ELL layout).
+__global__ void __launch_bounds__(256) gen_chunk_counts_kernel(GenParams g, uint64_t lo, uint64_t hi, uint32_t chunks,
+                                                               uint64_t chunk_neurons, uint32_t *__restrict__ cnt) {
+    const uint64_t total = rows_with_edges(g) * g.fanout;
+    const uint64_t stride = (uint64_t)blockDim.x * gridDim.x;
+    for (uint64_t e = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += stride) {
+        const uint64_t pre = e / g.fanout;
+        const uint64_t post = gen_target(g, pre, e, target_range(g, pre));
+        if (post >= lo && post < hi) atomicAdd(cnt + (post - lo) * chunks + pre / chunk_neurons, 1u);
+    }
+}
+
+// slots[b * chunks + c] = 32 x the largest count of block b's targets in chunk c.
+__global__ void sell_slots_kernel(const uint32_t *__restrict__ cnt, uint64_t n_local, uint32_t chunks,
+                                  uint64_t *__restrict__ slots) {
+    const uint64_t blocks = (n_local + 31) / 32;
+    const uint64_t stride = (uint64_t)blockDim.x * gridDim.x;
+    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < blocks * chunks; i += stride) {
+        const uint64_t b = i / chunks, c = i % chunks;
+        uint32_t m = 0;
+        for (uint64_t t = b * 32; t < b * 32 + 32 && t < n_local; ++t) m = max(m, cnt[t * chunks + c]);
+        slots[i] = 32ull * m;
+    }
+}
+
 // Warp per row: (post - lo, global edge id) of the row's edges into
 // [lo, hi), in edge order, at row_off[pre] (ballot compaction).
 __global__ void __launch_bounds__(256) gen_fill_keys_kernel(GenParams g, uint64_t lo, uint64_t hi,
@@ -834,21 +983,27 @@ __global__ void __launch_bounds__(256) gen_fill_keys_kernel(GenParams g, uint64_
 }
 
 // Sorted pass position q holds the pass-local target keys[q] and the global
-// edge id eids[q]; its slot in the target's CSR-ordered in-edge list is
-// k = q0 + q - col_ptr[t], stored at the SELL position of (t, k).
+// edge id eids[q]; its rank in the target's CSR-ordered in-edge list is
+// k = q0 + q - col_ptr[t]. In the chunked sliced-ELL layout it goes to the
+// slots of (block t / 32, chunk c = pre / chunk_neurons) at rank k minus the
+// target's in-edges from earlier chunks.
 template <typename TPre>
 __global__ void gather_generated_sell_kernel(GenParams g, const uint32_t *__restrict__ keys,
                                              const uint64_t *__restrict__ eids, uint64_t e, uint64_t t0, uint64_t q0,
-                                             const uint64_t *__restrict__ col_ptr,
+                                             const uint64_t *__restrict__ col_ptr, const uint32_t *__restrict__ cnt,
+                                             uint32_t chunks, uint64_t chunk_neurons,
                                              const uint64_t *__restrict__ sell_off, TPre *__restrict__ pre,
                                              float *__restrict__ w_out) {
     const uint64_t stride = (uint64_t)blockDim.x * gridDim.x;
     for (uint64_t q = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; q < e; q += stride) {
         const uint64_t ed = eids[q];
         const uint64_t t = t0 + keys[q];
-        const uint64_t k = q0 + q - col_ptr[t];
-        const uint64_t dst = sell_off[t >> 5] + k * 32u + (t & 31u);
-        pre[dst] = (TPre)(ed / g.fanout);
+        const uint64_t p = ed / g.fanout;
+        const uint32_t c = (uint32_t)(p / chunk_neurons);
+        uint64_t k = q0 + q - col_ptr[t];
+        for (uint32_t c2 = 0; c2 < c; ++c2) k -= cnt[t * chunks + c2];
+        const uint64_t dst = sell_off[(t >> 5) * chunks + c] + k * 32u + (t & 31u);
+        pre[dst] = (TPre)p;
         w_out[dst] = gen_weight(g, ed);
     }
 }
@@ -959,10 +1114,50 @@ void launch_propagate_push(cudaStream_t s, int device, const void *list, int idx
 #undef B200_PUSH
 }
 
-void launch_propagate_pull(cudaStream_t s, int device, uint64_t n_local, const uint64_t *sell_off, const void *pre,
-                           int pre_bits, const float *w, const uint32_t *bitmap, float *next, const void *list,
-                           int idx_bits, const uint32_t *out_degree, DevCounters *ctr, int parity, int count_spikes,
+// SNN_B200_PULL_CHUNK_WORDS (environment, read when a layout is built)
+// shrinks the chunks, so tests reach several chunks with small networks.
+uint64_t pull_chunk_words() {
+    const char *env = std::getenv("SNN_B200_PULL_CHUNK_WORDS");
+    const uint64_t v = env ? std::strtoull(env, nullptr, 10) : 0;
+    return v ? std::min<uint64_t>(v, kPullChunkWords) : (uint64_t)kPullChunkWords;
+}
+
+uint32_t pull_chunks(uint64_t words) { return (uint32_t)((words + pull_chunk_words() - 1) / pull_chunk_words()); }
+
+uint64_t pull_chunk_neurons() { return pull_chunk_words() * 32u; }
+
+void launch_propagate_pull(cudaStream_t s, int device, uint64_t n_local, uint32_t chunks, uint64_t chunk_words,
+                           const uint64_t *sell_off, const void *pre, int pre_bits, const float *w,
+                           const uint32_t *bitmap, uint64_t words, float *next, const void *list, int idx_bits,
+                           const uint32_t *out_degree, DevCounters *ctr, int parity, int count_spikes,
                            uint32_t pull_above) {
+    if ((uint64_t)chunks * chunk_words >= words) {
+        // Chunked layout: shared-memory spike bits.
+        const uint64_t blocks = (n_local + 31) / 32;
+        const uint64_t sweeps = (blocks + (kPullSmemThreads / 32) * kPullBlocksPerWarp - 1) /
+                                ((kPullSmemThreads / 32) * kPullBlocksPerWarp);
+        const int grid = (int)std::max<uint64_t>(1, std::min<uint64_t>(sweeps, (uint64_t)sm_count(device)));
+        const size_t smem = (size_t)std::min<uint64_t>(std::max<uint64_t>(words, 1), chunk_words) * 4;
+#define B200_PULLS(TP, TI)                                                                                        \
+    do {                                                                                                          \
+        static bool attr[64] = {};                                                                                \
+        if (device >= 0 && device < 64 && !attr[device]) {                                                        \
+            cudaFuncSetAttribute(propagate_pull_smem_kernel<TP, TI>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
+                                 (int)(kPullChunkWords * 4));                                                     \
+            attr[device] = true;                                                                                  \
+        }                                                                                                         \
+        propagate_pull_smem_kernel<TP, TI><<<grid, kPullSmemThreads, smem, s>>>(                                  \
+            n_local, chunks, chunk_words, sell_off, (const TP *)pre, w, bitmap, words, next, (const TI *)list, out_degree,     \
+            ctr, parity, count_spikes, pull_above);                                                               \
+    } while (0)
+        if (pre_bits == 32 && idx_bits == 32) B200_PULLS(uint32_t, uint32_t);
+        else if (pre_bits == 32) B200_PULLS(uint32_t, uint64_t);
+        else if (idx_bits == 32) B200_PULLS(uint64_t, uint32_t);
+        else B200_PULLS(uint64_t, uint64_t);
+#undef B200_PULLS
+        return;
+    }
+    // One chunk over a bitmap larger than shared memory: lookups through L1/L2.
     const int grid = sm_count(device) * 8;
 #define B200_PULL(TP, TI)                                                                                    \
     propagate_pull_kernel<TP, TI><<<grid, 256, 0, s>>>(n_local, sell_off, (const TP *)pre, w, bitmap, next,   \
@@ -1068,14 +1263,27 @@ cudaError_t sort_pairs_u32_u64(cudaStream_t s, uint32_t *keys, uint32_t *keys_al
 
 void launch_gather_generated_sell(cudaStream_t s, int device, const GenParams &g, const uint32_t *keys,
                                   const uint64_t *eids, uint64_t e, uint64_t t0, uint64_t q0, const uint64_t *col_ptr,
+                                  const uint32_t *cnt, uint32_t chunks, uint64_t chunk_neurons,
                                   const uint64_t *sell_off, void *pre, int pre_bits, float *w_out) {
     const int grid = grid_for(device, 8, e, 256);
     if (pre_bits == 32)
-        gather_generated_sell_kernel<uint32_t><<<grid, 256, 0, s>>>(g, keys, eids, e, t0, q0, col_ptr, sell_off,
-                                                                     (uint32_t *)pre, w_out);
+        gather_generated_sell_kernel<uint32_t><<<grid, 256, 0, s>>>(g, keys, eids, e, t0, q0, col_ptr, cnt, chunks,
+                                                                     chunk_neurons, sell_off, (uint32_t *)pre, w_out);
     else
-        gather_generated_sell_kernel<uint64_t><<<grid, 256, 0, s>>>(g, keys, eids, e, t0, q0, col_ptr, sell_off,
-                                                                     (uint64_t *)pre, w_out);
+        gather_generated_sell_kernel<uint64_t><<<grid, 256, 0, s>>>(g, keys, eids, e, t0, q0, col_ptr, cnt, chunks,
+                                                                     chunk_neurons, sell_off, (uint64_t *)pre, w_out);
+}
+
+void launch_gen_chunk_counts(cudaStream_t s, int device, const GenParams &g, uint64_t lo, uint64_t hi,
+                             uint32_t chunks, uint64_t chunk_neurons, uint32_t *cnt) {
+    gen_chunk_counts_kernel<<<grid_for(device, 8, g.n * g.fanout, 256), 256, 0, s>>>(g, lo, hi, chunks,
+                                                                                      chunk_neurons, cnt);
+}
+
+void launch_sell_slots(cudaStream_t s, int device, const uint32_t *cnt, uint64_t n_local, uint32_t chunks,
+                       uint64_t *slots) {
+    const uint64_t items = (n_local + 31) / 32 * chunks;
+    sell_slots_kernel<<<grid_for(device, 8, items, 256), 256, 0, s>>>(cnt, n_local, chunks, slots);
 }
 
 void launch_ordered_sdeg(cudaStream_t s, int device, const void *list, int idx_bits, DevCounters *ctr, int parity,

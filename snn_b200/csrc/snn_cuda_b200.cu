@@ -138,6 +138,8 @@ struct snn_cuda_context {
     bool has_csc = false;  // a SELL CSC beside the CSR: dense steps pull
     uint64_t *d_sell_off = nullptr;  // SELL-32 block offsets (blocks + 1); d_pre / d_cw are the slot arrays
     uint64_t sell_slots = 0;
+    uint32_t sell_chunks = 1;  // presynaptic chunks of the SELL layout (b200::pull_chunks: shared-memory bits)
+    uint64_t sell_chunk_words = 0;  // bitmap words per chunk, fixed when the layout is built
     uint32_t pull_above = 0;  // PUSH with a SELL CSC: steps with more spikes than this pull
     uint64_t pull_div = 10;  // pull when a step's events exceed local synapses / pull_div
     uint64_t pull_steps = 0;
@@ -634,8 +636,10 @@ snn_status_t ordered_push_step(snn_cuda_context_t *c, int parity, float *next, b
         // cheaper than sorting this many events.
         b200::launch_ordered_sdeg(c->stream, c->device, c->d_list, c->idx_bits, c->d_ctr, parity, n, c->d_row_ptr,
                                   c->d_sdeg, 1, brows);
-        b200::launch_propagate_pull(c->stream, c->device, c->n_local, c->d_sell_off, c->d_pre, c->idx_bits, c->d_cw,
-                                    bitmap, next, c->d_list, c->idx_bits, c->d_deg, c->d_ctr, parity, !sharded);
+        b200::launch_propagate_pull(c->stream, c->device, c->n_local, c->sell_chunks, c->sell_chunk_words,
+                                    c->d_sell_off, c->d_pre, c->idx_bits, c->d_cw,
+                                    bitmap, c->bitmap_words, next, c->d_list, c->idx_bits, c->d_deg, c->d_ctr, parity,
+                                    !sharded);
         c->launches += 2;
         c->pull_steps++;
         return SNN_OK;
@@ -677,37 +681,55 @@ snn_status_t ordered_push_step(snn_cuda_context_t *c, int parity, float *next, b
     return SNN_OK;
 }
 
-// Sliced-ELL layout of a CSC given its column pointers: blocks of 32 local
-// targets, each as wide as its largest in-degree.
-std::vector<uint64_t> sell_offsets(const std::vector<uint64_t> &col_ptr, uint64_t nl) {
+// Chunked sliced-ELL layout from per-(target, chunk) counts cnt[t * C + c]:
+// the slots of (block b, chunk c) start at off[b * C + c], 32 x the block's
+// largest count in that chunk.
+std::vector<uint64_t> sell_offsets(const std::vector<uint32_t> &cnt, uint64_t nl, uint32_t chunks) {
     const uint64_t blocks = (nl + 31) / 32;
-    std::vector<uint64_t> off(blocks + 1, 0);
-    for (uint64_t b = 0; b < blocks; ++b) {
-        uint64_t wmax = 0;
-        for (uint64_t t = b * 32; t < std::min(nl, b * 32 + 32); ++t) wmax = std::max(wmax, col_ptr[t + 1] - col_ptr[t]);
-        off[b + 1] = off[b] + 32 * wmax;
-    }
+    std::vector<uint64_t> off(blocks * chunks + 1, 0);
+    for (uint64_t b = 0; b < blocks; ++b)
+        for (uint32_t c = 0; c < chunks; ++c) {
+            uint32_t m = 0;
+            for (uint64_t t = b * 32; t < std::min(nl, b * 32 + 32); ++t) m = std::max(m, cnt[t * chunks + c]);
+            off[b * chunks + c + 1] = off[b * chunks + c] + 32ull * m;
+        }
     return off;
+}
+
+// Presynaptic chunks for the shared-memory pull (the builders fall back to
+// one chunk when that layout's padding would not fit the free memory).
+uint32_t choose_chunks(snn_cuda_context_t *c) {
+    c->sell_chunk_words = b200::pull_chunk_words();
+    return b200::pull_chunks(c->bitmap_words);
 }
 
 // Allocates the SELL slot arrays (padding: all-ones ids, zero weights) and
 // uploads the block offsets.
-snn_status_t alloc_sell(snn_cuda_context_t *c, const std::vector<uint64_t> &off) {
-    const uint64_t slots = off.back();
+snn_status_t alloc_sell_slots(snn_cuda_context_t *c, uint64_t slots) {
     const int pre_bytes = c->idx_bits / 8;
     c->sell_slots = slots;
-    if (cudaMalloc(&c->d_sell_off, off.size() * 8) != cudaSuccess ||
-        (slots && (cudaMalloc(&c->d_pre, slots * pre_bytes) != cudaSuccess ||
-                   cudaMalloc((void **)&c->d_cw, slots * 4) != cudaSuccess))) {
+    if (slots && (cudaMalloc(&c->d_pre, slots * pre_bytes) != cudaSuccess ||
+                  cudaMalloc((void **)&c->d_cw, slots * 4) != cudaSuccess)) {
+        cudaGetLastError();
+        set_error("pull topology", "out of device memory for the sliced-ELL CSC");
+        return SNN_ERR_OUT_OF_MEMORY;
+    }
+    snn_status_t st = SNN_OK;
+    if (slots) st = cuda_status(cudaMemsetAsync(c->d_pre, 0xff, slots * pre_bytes, c->stream));
+    if (st == SNN_OK && slots) st = cuda_status(cudaMemsetAsync(c->d_cw, 0, slots * 4, c->stream));
+    if (st == SNN_OK) st = cuda_status(cudaStreamSynchronize(c->stream));
+    return st;
+}
+
+snn_status_t alloc_sell(snn_cuda_context_t *c, const std::vector<uint64_t> &off) {
+    if (cudaMalloc(&c->d_sell_off, off.size() * 8) != cudaSuccess) {
         cudaGetLastError();
         set_error("pull topology", "out of device memory for the sliced-ELL CSC");
         return SNN_ERR_OUT_OF_MEMORY;
     }
     snn_status_t st = cuda_status(cudaMemcpyAsync(c->d_sell_off, off.data(), off.size() * 8, cudaMemcpyHostToDevice,
                                                   c->stream));
-    if (st == SNN_OK && slots) st = cuda_status(cudaMemsetAsync(c->d_pre, 0xff, slots * pre_bytes, c->stream));
-    if (st == SNN_OK && slots) st = cuda_status(cudaMemsetAsync(c->d_cw, 0, slots * 4, c->stream));
-    if (st == SNN_OK) st = cuda_status(cudaStreamSynchronize(c->stream));
+    if (st == SNN_OK) st = alloc_sell_slots(c, off.back());
     return st;
 }
 
@@ -730,32 +752,46 @@ void free_sell(snn_cuda_context_t *c) {
 snn_status_t upload_full_ordered(snn_cuda_context_t *c, const snn_network_t *net) {
     const uint64_t n = net->neuron_count;
     const uint64_t nl = c->n_local;
-    std::vector<uint64_t> col_ptr, off, pre;
+    const uint32_t first_choice = choose_chunks(c);
+    const uint64_t chunk_neurons = c->sell_chunk_words * 32u;
+    std::vector<uint64_t> off, pre;
     std::vector<float> w;
-    std::vector<uint32_t> deg;
+    std::vector<uint32_t> deg, cnt;
+    uint64_t e = 0;
+    size_t free_b = 0, total_b = 0;
+    if (cudaMemGetInfo(&free_b, &total_b) != cudaSuccess) return SNN_ERR_CUDA;
     try {
-        col_ptr.assign(nl + 1, 0);
         deg.assign(n, 0);
-        for (uint64_t i = 0; i < n; ++i) {
-            for (uint64_t q = net->row_ptr[i]; q < net->row_ptr[i + 1]; ++q) {
-                const uint64_t t = net->col_idx[q];
-                if (t >= c->lo && t < c->hi) {
-                    col_ptr[t - c->lo + 1]++;
-                    deg[i]++;
+        for (uint32_t chunks : {first_choice, 1u}) {
+            c->sell_chunks = chunks;
+            cnt.assign(nl * chunks, 0);
+            e = 0;
+            for (uint64_t i = 0; i < n; ++i) {
+                for (uint64_t q = net->row_ptr[i]; q < net->row_ptr[i + 1]; ++q) {
+                    const uint64_t t = net->col_idx[q];
+                    if (t >= c->lo && t < c->hi) {
+                        cnt[(t - c->lo) * chunks + (chunks > 1 ? i / chunk_neurons : 0)]++;
+                        ++e;
+                    }
                 }
             }
+            off = sell_offsets(cnt, nl, chunks);
+            if (chunks == 1 || off.back() * (c->idx_bits / 8 + 4) + (1ull << 30) < free_b) break;
         }
-        for (uint64_t t = 0; t < nl; ++t) col_ptr[t + 1] += col_ptr[t];
-        off = sell_offsets(col_ptr, nl);
+        for (uint64_t i = 0; i < n; ++i)
+            for (uint64_t q = net->row_ptr[i]; q < net->row_ptr[i + 1]; ++q)
+                deg[i] += (net->col_idx[q] >= c->lo && net->col_idx[q] < c->hi);
         pre.assign(off.back(), ~0ull);
         w.assign(off.back(), 0.0f);
-        std::vector<uint64_t> fill(nl, 0);
+        const uint32_t chunks = c->sell_chunks;
+        std::vector<uint32_t> fill(nl * chunks, 0);
         for (uint64_t i = 0; i < n; ++i) {
+            const uint32_t ch = chunks > 1 ? (uint32_t)(i / chunk_neurons) : 0u;
             for (uint64_t q = net->row_ptr[i]; q < net->row_ptr[i + 1]; ++q) {
                 const uint64_t t = net->col_idx[q];
                 if (t >= c->lo && t < c->hi) {
                     const uint64_t tl = t - c->lo;
-                    const uint64_t dst = off[tl >> 5] + fill[tl]++ * 32 + (tl & 31);
+                    const uint64_t dst = off[(tl >> 5) * chunks + ch] + (uint64_t)fill[tl * chunks + ch]++ * 32 + (tl & 31);
                     pre[dst] = i;
                     w[dst] = net->weights[q];
                 }
@@ -764,7 +800,7 @@ snn_status_t upload_full_ordered(snn_cuda_context_t *c, const snn_network_t *net
     } catch (const std::bad_alloc &) {
         return SNN_ERR_OUT_OF_MEMORY;
     }
-    c->e_local = col_ptr[nl];
+    c->e_local = e;
     snn_status_t st;
     if ((st = alloc_sell(c, off)) != SNN_OK) return st;
     if ((st = upload_cols(c, c->d_pre, pre.data(), off.back(), 0, c->idx_bits)) != SNN_OK) return st;
@@ -1072,8 +1108,9 @@ snn_status_t enqueue_step(snn_cuda_context_t *c, bool has_ext) {
         if (c->propagation == SNN_B200_PROPAGATE_ORDERED && !c->opull) {
             if ((st = ordered_push_step(c, parity, next, sharded, peer ? xbitmap : c->d_bitmap)) != SNN_OK) return st;
         } else if (c->propagation == SNN_B200_PROPAGATE_ORDERED)
-            b200::launch_propagate_pull(c->stream, c->device, c->n_local, c->d_sell_off, c->d_pre, c->idx_bits,
-                                        c->d_cw, peer ? xbitmap : c->d_bitmap, next, c->d_list, c->idx_bits,
+            b200::launch_propagate_pull(c->stream, c->device, c->n_local, c->sell_chunks, c->sell_chunk_words,
+                                    c->d_sell_off, c->d_pre, c->idx_bits,
+                                        c->d_cw, peer ? xbitmap : c->d_bitmap, c->bitmap_words, next, c->d_list, c->idx_bits,
                                         c->d_deg, c->d_ctr, parity, !sharded);
         else if (c->binned) {
             const cudaError_t e = b200::launch_propagate_binned(c->stream, c->d_list, c->idx_bits, next, c->d_ctr,
@@ -1086,8 +1123,9 @@ snn_status_t enqueue_step(snn_cuda_context_t *c, bool has_ext) {
                                         c->col_bits, c->d_w, next, c->d_ctr, parity, !sharded,
                                         c->batch > 1 ? c->n_rows : 0, c->has_csc ? c->pull_above : 0);
             if (c->has_csc) {
-                b200::launch_propagate_pull(c->stream, c->device, c->n_local, c->d_sell_off, c->d_pre, c->idx_bits,
-                                            c->d_cw, peer ? xbitmap : c->d_bitmap, next, c->d_list, c->idx_bits,
+                b200::launch_propagate_pull(c->stream, c->device, c->n_local, c->sell_chunks, c->sell_chunk_words,
+                                    c->d_sell_off, c->d_pre, c->idx_bits,
+                                            c->d_cw, peer ? xbitmap : c->d_bitmap, c->bitmap_words, next, c->d_list, c->idx_bits,
                                             c->d_deg, c->d_ctr, parity, !sharded, c->pull_above);
                 c->launches++;
             }
@@ -1275,16 +1313,57 @@ snn_status_t build_generated_csc(snn_cuda_context_t *c, const b200::GenParams &g
         return st;
     const uint64_t e = col_ptr[nl];
     c->e_local = e;
-    {
-        std::vector<uint64_t> off;
-        try {
-            off = sell_offsets(col_ptr, nl);
-        } catch (const std::bad_alloc &) {
+    // Chunked layout when it fits with room left for fast build passes, else
+    // one chunk (lookups through L1/L2).
+    uint32_t *cnt = nullptr;
+    const uint64_t blocks = (nl + 31) / 32;
+    for (uint32_t chunks : {choose_chunks(c), 1u}) {
+        c->sell_chunks = chunks;
+        const uint64_t chunk_neurons = chunks > 1 ? c->sell_chunk_words * 32u : UINT64_MAX;
+        uint64_t *slots = nullptr;
+        void *tmp = nullptr;
+        size_t tb = 0;
+        if (cudaMalloc(&cnt, (nl ? nl : 1) * chunks * 4) != cudaSuccess ||
+            cudaMalloc(&slots, (blocks * chunks + 1) * 8) != cudaSuccess ||
+            cudaMalloc(&c->d_sell_off, (blocks * chunks + 1) * 8) != cudaSuccess) {
+            cudaGetLastError();
+            cudaFree(cnt);
+            cudaFree(slots);
             return SNN_ERR_OUT_OF_MEMORY;
         }
-        if ((st = alloc_sell(c, off)) != SNN_OK) return st;
+        cudaMemsetAsync(cnt, 0, (nl ? nl : 1) * chunks * 4, c->stream);
+        cudaMemsetAsync(slots, 0, (blocks * chunks + 1) * 8, c->stream);
+        b200::launch_gen_chunk_counts(c->stream, c->device, g, lo, lo + nl, chunks, chunk_neurons, cnt);
+        b200::launch_sell_slots(c->stream, c->device, cnt, nl, chunks, slots);
+        b200::exclusive_scan_u64(c->stream, slots, c->d_sell_off, blocks * chunks + 1, nullptr, &tb);
+        if (cudaMalloc(&tmp, tb ? tb : 1) == cudaSuccess)
+            st = cuda_status(b200::exclusive_scan_u64(c->stream, slots, c->d_sell_off, blocks * chunks + 1, tmp, &tb));
+        else
+            st = SNN_ERR_OUT_OF_MEMORY;
+        uint64_t total = 0;
+        if (st == SNN_OK)
+            st = cuda_status(cudaMemcpyAsync(&total, c->d_sell_off + blocks * chunks, 8, cudaMemcpyDeviceToHost,
+                                             c->stream));
+        if (st == SNN_OK) st = cuda_status(cudaStreamSynchronize(c->stream));
+        cudaFree(tmp);
+        cudaFree(slots);
+        size_t free_b = 0, total_b = 0;
+        if (st == SNN_OK) st = cuda_status(cudaMemGetInfo(&free_b, &total_b));
+        const bool fits = total * (c->idx_bits / 8 + 4) + (8ull << 30) < free_b;
+        if (st == SNN_OK && (fits || chunks == 1)) {
+            st = alloc_sell_slots(c, total);
+            break;
+        }
+        cudaFree(cnt);
+        cudaFree(c->d_sell_off);
+        cnt = nullptr;
+        c->d_sell_off = nullptr;
+        if (st != SNN_OK) return st;
     }
-    if (e == 0) return cuda_status(cudaStreamSynchronize(c->stream));
+    if (st != SNN_OK || e == 0) {
+        cudaFree(cnt);
+        return st != SNN_OK ? st : cuda_status(cudaStreamSynchronize(c->stream));
+    }
 
     // Pass size: what fits in the free memory at 24 B per edge (keys and ids,
     // double-buffered) plus the per-pass row offsets and sort workspace.
@@ -1350,8 +1429,9 @@ snn_status_t build_generated_csc(snn_cuda_context_t *c, const b200::GenParams &g
                                                        &tb, &alt))) != SNN_OK)
             break;
         b200::launch_gather_generated_sell(c->stream, c->device, g, alt ? keys_alt : keys, alt ? ids_alt : ids, ep,
-                                           a, col_ptr[a], c->d_col_ptr, c->d_sell_off, c->d_pre, c->idx_bits,
-                                           c->d_cw);
+                                           a, col_ptr[a], c->d_col_ptr, cnt, c->sell_chunks,
+                                           c->sell_chunks > 1 ? c->sell_chunk_words * 32u : UINT64_MAX,
+                                           c->d_sell_off, c->d_pre, c->idx_bits, c->d_cw);
         st = cuda_status(cudaGetLastError());
     }
     if (st == SNN_OK) st = cuda_status(cudaStreamSynchronize(c->stream));
@@ -1362,6 +1442,7 @@ snn_status_t build_generated_csc(snn_cuda_context_t *c, const b200::GenParams &g
     cudaFree(counts);
     cudaFree(row_off);
     cudaFree(temp);
+    cudaFree(cnt);
     return st;
 }
 

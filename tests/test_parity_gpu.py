@@ -396,6 +396,7 @@ def test_sparse_streaming_dyadic_bit_exact():
     (1, {"SNN_B200_ORDERED_CAP": "3000"}),     # ordered push, several row ranges per step
     (0, {"SNN_B200_ORDERED_PULL": "1"}),       # pull over a device-built CSC
     (1, {"SNN_B200_ORDERED_PULL": "1", "SNN_B200_CSC_PASS_EDGES": "150000"}),  # CSC built in several passes
+    (0, {"SNN_B200_ORDERED_PULL": "1", "SNN_B200_PULL_CHUNK_WORDS": "100"}),  # 7 presynaptic chunks
 ])
 def test_generated_pool_ordered_bit_exact(allow_self, env, monkeypatch):
     """snn_b200_create_random_pool with ORDERED propagation, through both
@@ -438,8 +439,9 @@ def test_generated_layered_ordered_bit_exact():
     np.testing.assert_array_equal(bits(cv), bits(gv))
 
 
-@pytest.mark.parametrize("cap,pull_div", [(None, "0"), ("20000", "0"), (None, None)])
-def test_ordered_dense_bursts_bit_exact(cap, pull_div, monkeypatch):
+@pytest.mark.parametrize("cap,pull_div,chunk_words", [(None, "0", None), ("20000", "0", None), (None, None, None),
+                                                      (None, None, "40")])
+def test_ordered_dense_bursts_bit_exact(cap, pull_div, chunk_words, monkeypatch):
     """Dense recurrent pool (in-degree ~1500) with strong drive: most rows
     spike together, so every target's run of events is hundreds long (the
     warp-cooperative fold); with a small event capacity a step is split into
@@ -449,6 +451,8 @@ def test_ordered_dense_bursts_bit_exact(cap, pull_div, monkeypatch):
         monkeypatch.setenv("SNN_B200_ORDERED_CAP", cap)
     if pull_div:
         monkeypatch.setenv("SNN_B200_ORDERED_PULL_DIV", pull_div)
+    if chunk_words:  # general weights over a 3-chunk pull layout
+        monkeypatch.setenv("SNN_B200_PULL_CHUNK_WORDS", chunk_words)
     lif = default_lif(v_rest=0.0, v_reset=0.0, v_threshold=1.0, input_scale=1.0, refractory_steps=1)
     n = 3001
     net = ORC.random_pool(n, 1500, -0.05, 0.1, 12, allow_self=True, lif=lif)
@@ -572,14 +576,18 @@ def test_mapped_csr_file_contexts(mode, tmp_path):
     mapped.free()
 
 
-@pytest.mark.parametrize("generated", [False, True])
-def test_push_with_pull_gate_dyadic_bit_exact(generated, monkeypatch):
+@pytest.mark.parametrize("generated,chunk_words", [(False, None), (True, None), (False, "32"), (True, "32")])
+def test_push_with_pull_gate_dyadic_bit_exact(generated, chunk_words, monkeypatch):
     """PUSH contexts keep a sliced-ELL CSC beside the CSR when memory allows:
     steps with more spikes than rows / SNN_B200_PUSH_PULL_DIV take the pull
     kernel, the others the atomic push, chosen on the device. Frames alternate
     between sparse and dense drive so both kernels run; one shared dyadic
-    weight makes every sum exact, so both equal the CPU step bit for bit."""
+    weight makes every sum exact, so both equal the CPU step bit for bit.
+    With SNN_B200_PULL_CHUNK_WORDS=32 the pull's layout is cut into 3
+    presynaptic chunks (shared-memory spike bits staged chunk by chunk)."""
     monkeypatch.setenv("SNN_B200_PUSH_PULL_DIV", "4")
+    if chunk_words:
+        monkeypatch.setenv("SNN_B200_PULL_CHUNK_WORDS", chunk_words)
     lif = default_lif(v_rest=0.0, v_reset=0.0, v_threshold=1.0, input_scale=1.0, refractory_steps=1)
     n, f = 3001, 700
     net = ORC.random_pool(n, f, 0.0009765625, 0.0009765625, 12, lif=lif)
