@@ -517,21 +517,23 @@ __global__ void __launch_bounds__(256) ordered_fold_kernel(uint64_t events, cons
 // ----------------------------------------------------------- ordered pull ----
 // The pull reads a sliced-ELL (SELL-32) CSC: local targets in blocks of 32;
 // block b holds width_b = max in-degree of its targets slots per target,
-// slot k of target t at sell_off[b] + k*32 + (t % 32), so a warp (one lane
-// per target) loads 32 consecutive entries per slot: every load is coalesced
-// and every lane folds its own target. Each target's in-edges keep CSR order
+// slot k of target t at sell_off[b] + k*32 + (t % 32), each slot an 8-byte
+// (presynaptic id, weight bits) pair, so a warp (one lane per target) loads
+// 256 contiguous bytes per slot row: every load is coalesced and every lane
+// folds its own target. Each target's in-edges keep CSR order
 // (ascending presynaptic row, ascending edge), and the lane folds the spiking
 // ones in that order from +0.0f, exactly the serial CPU fold
 // (src/snn.c:898-906); padding slots hold an all-ones id and are skipped.
+// (The chunked variant below stores chunk-relative ids; its padding id
+// points at a shared-memory word that is always zero.)
 // Cost ~ local synapses whatever the firing, so it is taken on dense steps:
 // when pull_above != 0 the kernel runs only if the step's spike count
 // exceeds it (the push kernel, launched with the same gate, runs otherwise).
 constexpr int kPullUnroll = 4;
 
-template <typename TPre, typename TIdx>
+template <typename TIdx>
 __global__ void __launch_bounds__(256) propagate_pull_kernel(uint64_t n_local, const uint64_t *__restrict__ sell_off,
-                                                             const TPre *__restrict__ pre,
-                                                             const float *__restrict__ w,
+                                                             const uint2 *__restrict__ slots,
                                                              const uint32_t *__restrict__ bitmap,
                                                              float *__restrict__ next, const TIdx *__restrict__ list,
                                                              const uint32_t *__restrict__ out_degree,
@@ -543,33 +545,25 @@ __global__ void __launch_bounds__(256) propagate_pull_kernel(uint64_t n_local, c
     const uint64_t gwarp = ((uint64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const uint64_t nwarps = ((uint64_t)gridDim.x * blockDim.x) >> 5;
     const uint64_t blocks = (n_local + 31) / 32;
-    const TPre pad = (TPre)~(TPre)0;
     for (uint64_t blk = gwarp; blk < blocks; blk += nwarps) {
         const uint64_t base = sell_off[blk];
         const uint64_t width = (sell_off[blk + 1] - base) / 32;
-        const TPre *pp = pre + base + lane;
-        const float *wp = w + base + lane;
+        const uint2 *sp = slots + base + lane;
         float acc = 0.0f;
         uint64_t k = 0;
         for (; k + kPullUnroll <= width; k += kPullUnroll) {
-            TPre p[kPullUnroll];
+            uint2 q[kPullUnroll];
 #pragma unroll
-            for (int j = 0; j < kPullUnroll; ++j) p[j] = __ldcs(pp + (k + j) * 32u);
-            uint32_t bit[kPullUnroll];
-#pragma unroll
-            for (int j = 0; j < kPullUnroll; ++j)
-                bit[j] = p[j] != pad ? (__ldg(bitmap + ((uint64_t)p[j] >> 5)) >> ((uint32_t)p[j] & 31u)) & 1u : 0u;
-            float wv[kPullUnroll];
-#pragma unroll
-            for (int j = 0; j < kPullUnroll; ++j) wv[j] = bit[j] ? __ldcs(wp + (k + j) * 32u) : 0.0f;
+            for (int j = 0; j < kPullUnroll; ++j) q[j] = __ldcs(sp + (k + j) * 32u);
 #pragma unroll
             for (int j = 0; j < kPullUnroll; ++j)
-                if (bit[j]) acc = __fadd_rn(acc, wv[j]);
+                if (q[j].x != 0xffffffffu && ((__ldg(bitmap + (q[j].x >> 5)) >> (q[j].x & 31u)) & 1u))
+                    acc = __fadd_rn(acc, __uint_as_float(q[j].y));
         }
         for (; k < width; ++k) {
-            const TPre q = pp[k * 32u];
-            if (q != pad && ((__ldg(bitmap + ((uint64_t)q >> 5)) >> ((uint32_t)q & 31u)) & 1u))
-                acc = __fadd_rn(acc, wp[k * 32u]);
+            const uint2 q = sp[k * 32u];
+            if (q.x != 0xffffffffu && ((__ldg(bitmap + (q.x >> 5)) >> (q.x & 31u)) & 1u))
+                acc = __fadd_rn(acc, __uint_as_float(q.y));
         }
         const uint64_t t = blk * 32u + lane;
         if (t < n_local) next[t] = acc;
@@ -591,20 +585,19 @@ __global__ void __launch_bounds__(256) propagate_pull_kernel(uint64_t n_local, c
 // takes sweeps of 32 warps x 4 blocks; each lane keeps its 4 targets' sums
 // in registers across the chunks, which are visited in ascending order, so
 // the fold order is still ascending presynaptic row, ascending edge.
-constexpr uint32_t kPullChunkWords = 56320;  // 220 KB of shared memory
+constexpr uint32_t kPullChunkWords = 56320;  // 220 KB of shared memory (+1 zero word)
 constexpr int kPullSmemThreads = 1024;
 constexpr int kPullBlocksPerWarp = 4;
 constexpr int kPullSmemUnroll = 8;  // slot loads in flight per lane
 
-template <typename TPre, typename TIdx>
+template <typename TIdx>
 __global__ void __launch_bounds__(kPullSmemThreads, 1)
     propagate_pull_smem_kernel(uint64_t n_local, uint32_t chunks, uint64_t chunk_words,
-                               const uint64_t *__restrict__ sell_off,
-                               const TPre *__restrict__ pre, const float *__restrict__ w,
+                               const uint64_t *__restrict__ sell_off, const uint2 *__restrict__ slots,
                                const uint32_t *__restrict__ bitmap, uint64_t words, float *__restrict__ next,
                                const TIdx *__restrict__ list, const uint32_t *__restrict__ out_degree,
                                DevCounters *ctr, int parity, int count_spikes, uint32_t pull_above) {
-    extern __shared__ __align__(16) uint32_t s_bits[];
+    extern __shared__ __align__(16) uint32_t s_bits[];  // chunk_words + 1 (the last word: zero, for padding)
     const uint32_t count = *(volatile uint32_t *)&ctr->list_count[parity];
     if (pull_above && count <= pull_above) return;  // sparse step: the push kernel runs
     const unsigned lane = lane_id();
@@ -612,7 +605,6 @@ __global__ void __launch_bounds__(kPullSmemThreads, 1)
     const uint64_t blocks = (n_local + 31) / 32;
     constexpr uint64_t kSweep = (kPullSmemThreads / 32) * kPullBlocksPerWarp;
     const uint64_t sweeps = (blocks + kSweep - 1) / kSweep;
-    const TPre pad = (TPre)~(TPre)0;
     for (uint64_t sw = blockIdx.x; sw < sweeps; sw += gridDim.x) {
         const uint64_t b0 = sw * kSweep + (uint64_t)warp * kPullBlocksPerWarp;
         float acc[kPullBlocksPerWarp];
@@ -631,47 +623,36 @@ __global__ void __launch_bounds__(kPullSmemThreads, 1)
             } else {
                 for (uint64_t i = threadIdx.x; i < cw; i += blockDim.x) s_bits[i] = __ldcg(src + i);
             }
+            if (threadIdx.x == 0) s_bits[chunk_words] = 0u;
             __syncthreads();
-            const uint64_t id0 = w0 * 32u;
 #pragma unroll
             for (int j = 0; j < kPullBlocksPerWarp; ++j) {
                 const uint64_t b = b0 + j;
                 if (b >= blocks) break;
                 const uint64_t base = sell_off[b * chunks + c];
                 const uint64_t width = (sell_off[b * chunks + c + 1] - base) / 32;
-                const TPre *pp = pre + base + lane;
-                const float *wp = w + base + lane;
+                const uint2 *sp = slots + base + lane;
                 float a = acc[j];
                 uint64_t k = 0;
-                // Software-pipelined: the next group's ids are in flight
-                // while this group's bits are looked up and weights folded.
-                TPre q[kPullSmemUnroll];
+                // Software-pipelined: the next group's slots are in flight
+                // while this group's bits are looked up and folded.
+                uint2 q[kPullSmemUnroll];
                 bool have = kPullSmemUnroll <= width;
                 if (have) {
 #pragma unroll
-                    for (int u = 0; u < kPullSmemUnroll; ++u) q[u] = __ldcs(pp + (uint64_t)u * 32u);
+                    for (int u = 0; u < kPullSmemUnroll; ++u) q[u] = __ldcs(sp + (uint64_t)u * 32u);
                 }
                 while (have) {
                     const uint64_t kn = k + kPullSmemUnroll;
                     const bool more = kn + kPullSmemUnroll <= width;
-                    TPre qn[kPullSmemUnroll];
+                    uint2 qn[kPullSmemUnroll];
                     if (more) {
 #pragma unroll
-                        for (int u = 0; u < kPullSmemUnroll; ++u) qn[u] = __ldcs(pp + (kn + u) * 32u);
+                        for (int u = 0; u < kPullSmemUnroll; ++u) qn[u] = __ldcs(sp + (kn + u) * 32u);
                     }
-                    uint32_t bits = 0;
-#pragma unroll
-                    for (int u = 0; u < kPullSmemUnroll; ++u) {
-                        const uint64_t r = (uint64_t)q[u] - id0;
-                        bits |= (q[u] != pad ? (s_bits[r >> 5] >> (r & 31u)) & 1u : 0u) << u;
-                    }
-                    float wv[kPullSmemUnroll];
 #pragma unroll
                     for (int u = 0; u < kPullSmemUnroll; ++u)
-                        wv[u] = (bits >> u) & 1u ? __ldcs(wp + (k + u) * 32u) : 0.0f;
-#pragma unroll
-                    for (int u = 0; u < kPullSmemUnroll; ++u)
-                        if ((bits >> u) & 1u) a = __fadd_rn(a, wv[u]);
+                        if ((s_bits[q[u].x >> 5] >> (q[u].x & 31u)) & 1u) a = __fadd_rn(a, __uint_as_float(q[u].y));
                     if (more) {
 #pragma unroll
                         for (int u = 0; u < kPullSmemUnroll; ++u) q[u] = qn[u];
@@ -680,11 +661,8 @@ __global__ void __launch_bounds__(kPullSmemThreads, 1)
                     have = more;
                 }
                 for (; k < width; ++k) {
-                    const TPre q = pp[k * 32u];
-                    if (q != pad) {
-                        const uint64_t r = (uint64_t)q - id0;
-                        if ((s_bits[r >> 5] >> (r & 31u)) & 1u) a = __fadd_rn(a, wp[k * 32u]);
-                    }
+                    const uint2 q1 = sp[k * 32u];
+                    if ((s_bits[q1.x >> 5] >> (q1.x & 31u)) & 1u) a = __fadd_rn(a, __uint_as_float(q1.y));
                 }
                 acc[j] = a;
             }
@@ -987,13 +965,11 @@ __global__ void __launch_bounds__(256) gen_fill_keys_kernel(GenParams g, uint64_
 // k = q0 + q - col_ptr[t]. In the chunked sliced-ELL layout it goes to the
 // slots of (block t / 32, chunk c = pre / chunk_neurons) at rank k minus the
 // target's in-edges from earlier chunks.
-template <typename TPre>
 __global__ void gather_generated_sell_kernel(GenParams g, const uint32_t *__restrict__ keys,
                                              const uint64_t *__restrict__ eids, uint64_t e, uint64_t t0, uint64_t q0,
                                              const uint64_t *__restrict__ col_ptr, const uint32_t *__restrict__ cnt,
-                                             uint32_t chunks, uint64_t chunk_neurons,
-                                             const uint64_t *__restrict__ sell_off, TPre *__restrict__ pre,
-                                             float *__restrict__ w_out) {
+                                             uint32_t chunks, uint64_t chunk_neurons, int relative,
+                                             const uint64_t *__restrict__ sell_off, uint2 *__restrict__ slots) {
     const uint64_t stride = (uint64_t)blockDim.x * gridDim.x;
     for (uint64_t q = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; q < e; q += stride) {
         const uint64_t ed = eids[q];
@@ -1003,8 +979,8 @@ __global__ void gather_generated_sell_kernel(GenParams g, const uint32_t *__rest
         uint64_t k = q0 + q - col_ptr[t];
         for (uint32_t c2 = 0; c2 < c; ++c2) k -= cnt[t * chunks + c2];
         const uint64_t dst = sell_off[(t >> 5) * chunks + c] + k * 32u + (t & 31u);
-        pre[dst] = (TPre)p;
-        w_out[dst] = gen_weight(g, ed);
+        const uint32_t id = (uint32_t)(relative ? p - (uint64_t)c * chunk_neurons : p);
+        slots[dst] = make_uint2(id, __float_as_uint(gen_weight(g, ed)));
     }
 }
 
@@ -1127,47 +1103,52 @@ uint32_t pull_chunks(uint64_t words) { return (uint32_t)((words + pull_chunk_wor
 uint64_t pull_chunk_neurons() { return pull_chunk_words() * 32u; }
 
 void launch_propagate_pull(cudaStream_t s, int device, uint64_t n_local, uint32_t chunks, uint64_t chunk_words,
-                           const uint64_t *sell_off, const void *pre, int pre_bits, const float *w,
-                           const uint32_t *bitmap, uint64_t words, float *next, const void *list, int idx_bits,
-                           const uint32_t *out_degree, DevCounters *ctr, int parity, int count_spikes,
-                           uint32_t pull_above) {
+                           const uint64_t *sell_off, const uint2 *slots, const uint32_t *bitmap, uint64_t words,
+                           float *next, const void *list, int idx_bits, const uint32_t *out_degree, DevCounters *ctr,
+                           int parity, int count_spikes, uint32_t pull_above) {
     if ((uint64_t)chunks * chunk_words >= words) {
         // Chunked layout: shared-memory spike bits.
         const uint64_t blocks = (n_local + 31) / 32;
         const uint64_t sweeps = (blocks + (kPullSmemThreads / 32) * kPullBlocksPerWarp - 1) /
                                 ((kPullSmemThreads / 32) * kPullBlocksPerWarp);
         const int grid = (int)std::max<uint64_t>(1, std::min<uint64_t>(sweeps, (uint64_t)sm_count(device)));
-        const size_t smem = (size_t)std::min<uint64_t>(std::max<uint64_t>(words, 1), chunk_words) * 4;
-#define B200_PULLS(TP, TI)                                                                                        \
-    do {                                                                                                          \
-        static bool attr[64] = {};                                                                                \
-        if (device >= 0 && device < 64 && !attr[device]) {                                                        \
-            cudaFuncSetAttribute(propagate_pull_smem_kernel<TP, TI>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
-                                 (int)(kPullChunkWords * 4));                                                     \
-            attr[device] = true;                                                                                  \
-        }                                                                                                         \
-        propagate_pull_smem_kernel<TP, TI><<<grid, kPullSmemThreads, smem, s>>>(                                  \
-            n_local, chunks, chunk_words, sell_off, (const TP *)pre, w, bitmap, words, next, (const TI *)list, out_degree,     \
-            ctr, parity, count_spikes, pull_above);                                                               \
+        const size_t smem = (size_t)(chunk_words + 1) * 4;
+#define B200_PULLS(TI)                                                                                          \
+    do {                                                                                                        \
+        static bool attr[64] = {};                                                                              \
+        if (device >= 0 && device < 64 && !attr[device]) {                                                      \
+            cudaFuncSetAttribute(propagate_pull_smem_kernel<TI>, cudaFuncAttributeMaxDynamicSharedMemorySize,   \
+                                 (int)((kPullChunkWords + 1) * 4));                                             \
+            attr[device] = true;                                                                                \
+        }                                                                                                       \
+        propagate_pull_smem_kernel<TI><<<grid, kPullSmemThreads, smem, s>>>(                                    \
+            n_local, chunks, chunk_words, sell_off, slots, bitmap, words, next, (const TI *)list, out_degree,   \
+            ctr, parity, count_spikes, pull_above);                                                             \
     } while (0)
-        if (pre_bits == 32 && idx_bits == 32) B200_PULLS(uint32_t, uint32_t);
-        else if (pre_bits == 32) B200_PULLS(uint32_t, uint64_t);
-        else if (idx_bits == 32) B200_PULLS(uint64_t, uint32_t);
-        else B200_PULLS(uint64_t, uint64_t);
+        if (idx_bits == 32) B200_PULLS(uint32_t);
+        else B200_PULLS(uint64_t);
 #undef B200_PULLS
         return;
     }
     // One chunk over a bitmap larger than shared memory: lookups through L1/L2.
     const int grid = sm_count(device) * 8;
-#define B200_PULL(TP, TI)                                                                                    \
-    propagate_pull_kernel<TP, TI><<<grid, 256, 0, s>>>(n_local, sell_off, (const TP *)pre, w, bitmap, next,   \
-                                                       (const TI *)list, out_degree, ctr, parity, count_spikes, \
-                                                       pull_above)
-    if (pre_bits == 32 && idx_bits == 32) B200_PULL(uint32_t, uint32_t);
-    else if (pre_bits == 32) B200_PULL(uint32_t, uint64_t);
-    else if (idx_bits == 32) B200_PULL(uint64_t, uint32_t);
-    else B200_PULL(uint64_t, uint64_t);
-#undef B200_PULL
+    if (idx_bits == 32)
+        propagate_pull_kernel<uint32_t><<<grid, 256, 0, s>>>(n_local, sell_off, slots, bitmap, next,
+                                                             (const uint32_t *)list, out_degree, ctr, parity,
+                                                             count_spikes, pull_above);
+    else
+        propagate_pull_kernel<uint64_t><<<grid, 256, 0, s>>>(n_local, sell_off, slots, bitmap, next,
+                                                             (const uint64_t *)list, out_degree, ctr, parity,
+                                                             count_spikes, pull_above);
+}
+
+__global__ void fill_u2_kernel(uint2 *__restrict__ p, uint64_t n, uint2 v) {
+    const uint64_t stride = (uint64_t)blockDim.x * gridDim.x;
+    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) p[i] = v;
+}
+
+void launch_fill_u2(cudaStream_t s, int device, uint2 *p, uint64_t n, uint32_t x, uint32_t y) {
+    fill_u2_kernel<<<grid_for(device, 8, n, 256), 256, 0, s>>>(p, n, make_uint2(x, y));
 }
 
 void launch_propagate_chunk(cudaStream_t s, int device, uint64_t row0, uint64_t rows, uint64_t edge_base,
@@ -1263,15 +1244,11 @@ cudaError_t sort_pairs_u32_u64(cudaStream_t s, uint32_t *keys, uint32_t *keys_al
 
 void launch_gather_generated_sell(cudaStream_t s, int device, const GenParams &g, const uint32_t *keys,
                                   const uint64_t *eids, uint64_t e, uint64_t t0, uint64_t q0, const uint64_t *col_ptr,
-                                  const uint32_t *cnt, uint32_t chunks, uint64_t chunk_neurons,
-                                  const uint64_t *sell_off, void *pre, int pre_bits, float *w_out) {
-    const int grid = grid_for(device, 8, e, 256);
-    if (pre_bits == 32)
-        gather_generated_sell_kernel<uint32_t><<<grid, 256, 0, s>>>(g, keys, eids, e, t0, q0, col_ptr, cnt, chunks,
-                                                                     chunk_neurons, sell_off, (uint32_t *)pre, w_out);
-    else
-        gather_generated_sell_kernel<uint64_t><<<grid, 256, 0, s>>>(g, keys, eids, e, t0, q0, col_ptr, cnt, chunks,
-                                                                     chunk_neurons, sell_off, (uint64_t *)pre, w_out);
+                                  const uint32_t *cnt, uint32_t chunks, uint64_t chunk_neurons, int relative,
+                                  const uint64_t *sell_off, uint2 *slots) {
+    gather_generated_sell_kernel<<<grid_for(device, 8, e, 256), 256, 0, s>>>(g, keys, eids, e, t0, q0, col_ptr, cnt,
+                                                                              chunks, chunk_neurons, relative,
+                                                                              sell_off, slots);
 }
 
 void launch_gen_chunk_counts(cudaStream_t s, int device, const GenParams &g, uint64_t lo, uint64_t hi,

@@ -129,25 +129,25 @@ void launch_propagate_push(cudaStream_t s, int device, const void *list, int idx
                            int parity, int count_spikes, uint64_t batch_rows = 0, uint32_t pull_above = 0);
 
 // Ordered pull over a sliced-ELL CSC: local targets in blocks of 32,
-// presynaptic ids cut into `chunks` chunks of pull_chunk_neurons() ids; the
-// slots of (block b, chunk c) start at sell_off[b * chunks + c] (32 per
-// rank: slot k of target t at + 32k + t%32; padding ids all ones) and each
-// target's ids in a chunk keep CSR order. For every local target, folds the
-// weights of its spiking presynaptic rows in (row, edge) order from 0.0f.
-// chunks == pull_chunks(words): shared-memory spike bits; chunks == 1 over a
-// larger bitmap: lookups through L1/L2. pull_above != 0: a push kernel
-// launched with the same gate handles steps of at most pull_above spikes;
-// the pull runs only above it.
-// The layout's chunk size (bitmap words) is fixed when it is built:
-// pull_chunk_words() then, passed back to every launch.
+// presynaptic ids cut into `chunks` chunks of chunk_words * 32 ids; the slots
+// of (block b, chunk c) start at sell_off[b * chunks + c] (32 per rank: slot
+// k of target t at + 32k + t%32), each a (presynaptic id, weight bits) pair;
+// each target's slots in a chunk keep CSR order. For every local target,
+// folds the weights of its spiking presynaptic rows in (row, edge) order
+// from 0.0f. chunks * chunk_words >= words: ids are chunk-relative, padding
+// id chunk_words * 32, spike bits staged in shared memory; otherwise (one
+// chunk over a larger bitmap) ids are global, padding id all ones, lookups
+// through L1/L2. pull_above != 0: a push kernel launched with the same gate
+// handles steps of at most pull_above spikes; the pull runs only above it.
+// The layout's chunk size is fixed when it is built: pull_chunk_words() then.
 uint64_t pull_chunk_words();
 uint32_t pull_chunks(uint64_t words);
 uint64_t pull_chunk_neurons();
 void launch_propagate_pull(cudaStream_t s, int device, uint64_t n_local, uint32_t chunks, uint64_t chunk_words,
-                           const uint64_t *sell_off, const void *pre, int pre_bits, const float *w,
-                           const uint32_t *bitmap, uint64_t words, float *next, const void *list, int idx_bits,
-                           const uint32_t *out_degree, DevCounters *ctr, int parity, int count_spikes,
-                           uint32_t pull_above = 0);
+                           const uint64_t *sell_off, const uint2 *slots, const uint32_t *bitmap, uint64_t words,
+                           float *next, const void *list, int idx_bits, const uint32_t *out_degree, DevCounters *ctr,
+                           int parity, int count_spikes, uint32_t pull_above = 0);
+void launch_fill_u2(cudaStream_t s, int device, uint2 *p, uint64_t n, uint32_t x, uint32_t y);
 
 // STREAMING: one chunk of `rows` rows starting at row0, with the chunk's raw
 // row_ptr slice (rows+1 entries, absolute edge offsets) and its edges starting
@@ -211,8 +211,8 @@ cudaError_t sort_pairs_u32_u64(cudaStream_t s, uint32_t *keys, uint32_t *keys_al
                                bool *result_in_alt);
 void launch_gather_generated_sell(cudaStream_t s, int device, const GenParams &g, const uint32_t *keys,
                                   const uint64_t *eids, uint64_t e, uint64_t t0, uint64_t q0, const uint64_t *col_ptr,
-                                  const uint32_t *cnt, uint32_t chunks, uint64_t chunk_neurons,
-                                  const uint64_t *sell_off, void *pre, int pre_bits, float *w_out);
+                                  const uint32_t *cnt, uint32_t chunks, uint64_t chunk_neurons, int relative,
+                                  const uint64_t *sell_off, uint2 *slots);
 // cnt[t * chunks + c]: in-edges of local target t from presynaptic chunk c.
 void launch_gen_chunk_counts(cudaStream_t s, int device, const GenParams &g, uint64_t lo, uint64_t hi,
                              uint32_t chunks, uint64_t chunk_neurons, uint32_t *cnt);

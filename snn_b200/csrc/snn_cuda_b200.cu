@@ -637,7 +637,7 @@ snn_status_t ordered_push_step(snn_cuda_context_t *c, int parity, float *next, b
         b200::launch_ordered_sdeg(c->stream, c->device, c->d_list, c->idx_bits, c->d_ctr, parity, n, c->d_row_ptr,
                                   c->d_sdeg, 1, brows);
         b200::launch_propagate_pull(c->stream, c->device, c->n_local, c->sell_chunks, c->sell_chunk_words,
-                                    c->d_sell_off, c->d_pre, c->idx_bits, c->d_cw,
+                                    c->d_sell_off, (const uint2 *)c->d_pre, 
                                     bitmap, c->bitmap_words, next, c->d_list, c->idx_bits, c->d_deg, c->d_ctr, parity,
                                     !sharded);
         c->launches += 2;
@@ -705,18 +705,26 @@ uint32_t choose_chunks(snn_cuda_context_t *c) {
 
 // Allocates the SELL slot arrays (padding: all-ones ids, zero weights) and
 // uploads the block offsets.
+// Chunk-relative ids (shared-memory bits) when the chunks cover the bitmap.
+bool sell_relative(const snn_cuda_context_t *c) {
+    return (uint64_t)c->sell_chunks * c->sell_chunk_words >= c->bitmap_words;
+}
+
+uint32_t sell_pad_id(const snn_cuda_context_t *c) {
+    return sell_relative(c) ? (uint32_t)(c->sell_chunk_words * 32u) : 0xffffffffu;
+}
+
+// The slot array: (id, weight bits) pairs, d_pre as uint2[slots].
 snn_status_t alloc_sell_slots(snn_cuda_context_t *c, uint64_t slots) {
-    const int pre_bytes = c->idx_bits / 8;
     c->sell_slots = slots;
-    if (slots && (cudaMalloc(&c->d_pre, slots * pre_bytes) != cudaSuccess ||
-                  cudaMalloc((void **)&c->d_cw, slots * 4) != cudaSuccess)) {
+    if (slots && cudaMalloc(&c->d_pre, slots * 8) != cudaSuccess) {
         cudaGetLastError();
         set_error("pull topology", "out of device memory for the sliced-ELL CSC");
         return SNN_ERR_OUT_OF_MEMORY;
     }
-    snn_status_t st = SNN_OK;
-    if (slots) st = cuda_status(cudaMemsetAsync(c->d_pre, 0xff, slots * pre_bytes, c->stream));
-    if (st == SNN_OK && slots) st = cuda_status(cudaMemsetAsync(c->d_cw, 0, slots * 4, c->stream));
+    // Padding slots: an id whose spike bit is always zero, weight 0.
+    if (slots) b200::launch_fill_u2(c->stream, c->device, (uint2 *)c->d_pre, slots, sell_pad_id(c), 0u);
+    snn_status_t st = cuda_status(cudaGetLastError());
     if (st == SNN_OK) st = cuda_status(cudaStreamSynchronize(c->stream));
     return st;
 }
@@ -754,12 +762,12 @@ snn_status_t upload_full_ordered(snn_cuda_context_t *c, const snn_network_t *net
     const uint64_t nl = c->n_local;
     const uint32_t first_choice = choose_chunks(c);
     const uint64_t chunk_neurons = c->sell_chunk_words * 32u;
-    std::vector<uint64_t> off, pre;
-    std::vector<float> w;
+    std::vector<uint64_t> off, slot;  // slot: weight bits << 32 | id (a little-endian uint2)
     std::vector<uint32_t> deg, cnt;
     uint64_t e = 0;
     size_t free_b = 0, total_b = 0;
     if (cudaMemGetInfo(&free_b, &total_b) != cudaSuccess) return SNN_ERR_CUDA;
+    if (c->idx_bits != 32) return SNN_ERR_UNSUPPORTED;  // 32-bit slot ids
     try {
         deg.assign(n, 0);
         for (uint32_t chunks : {first_choice, 1u}) {
@@ -776,14 +784,14 @@ snn_status_t upload_full_ordered(snn_cuda_context_t *c, const snn_network_t *net
                 }
             }
             off = sell_offsets(cnt, nl, chunks);
-            if (chunks == 1 || off.back() * (c->idx_bits / 8 + 4) + (1ull << 30) < free_b) break;
+            if (chunks == 1 || off.back() * 8 + (1ull << 30) < free_b) break;
         }
         for (uint64_t i = 0; i < n; ++i)
             for (uint64_t q = net->row_ptr[i]; q < net->row_ptr[i + 1]; ++q)
                 deg[i] += (net->col_idx[q] >= c->lo && net->col_idx[q] < c->hi);
-        pre.assign(off.back(), ~0ull);
-        w.assign(off.back(), 0.0f);
         const uint32_t chunks = c->sell_chunks;
+        const bool relative = sell_relative(c);
+        slot.assign(off.back(), (uint64_t)sell_pad_id(c));
         std::vector<uint32_t> fill(nl * chunks, 0);
         for (uint64_t i = 0; i < n; ++i) {
             const uint32_t ch = chunks > 1 ? (uint32_t)(i / chunk_neurons) : 0u;
@@ -792,8 +800,9 @@ snn_status_t upload_full_ordered(snn_cuda_context_t *c, const snn_network_t *net
                 if (t >= c->lo && t < c->hi) {
                     const uint64_t tl = t - c->lo;
                     const uint64_t dst = off[(tl >> 5) * chunks + ch] + (uint64_t)fill[tl * chunks + ch]++ * 32 + (tl & 31);
-                    pre[dst] = i;
-                    w[dst] = net->weights[q];
+                    uint32_t wb;
+                    std::memcpy(&wb, &net->weights[q], 4);
+                    slot[dst] = (uint64_t)wb << 32 | (uint32_t)(relative ? i - (uint64_t)ch * chunk_neurons : i);
                 }
             }
         }
@@ -803,8 +812,7 @@ snn_status_t upload_full_ordered(snn_cuda_context_t *c, const snn_network_t *net
     c->e_local = e;
     snn_status_t st;
     if ((st = alloc_sell(c, off)) != SNN_OK) return st;
-    if ((st = upload_cols(c, c->d_pre, pre.data(), off.back(), 0, c->idx_bits)) != SNN_OK) return st;
-    if ((st = h2d(c, c->d_cw, w.data(), off.back() * 4)) != SNN_OK) return st;
+    if ((st = h2d(c, c->d_pre, slot.data(), off.back() * 8)) != SNN_OK) return st;
     if ((st = dmalloc((void **)&c->d_deg, n, 4)) != SNN_OK) return st;
     if ((st = h2d(c, c->d_deg, deg.data(), n * 4)) != SNN_OK) return st;
     return cuda_status(cudaStreamSynchronize(c->stream));
@@ -1109,8 +1117,8 @@ snn_status_t enqueue_step(snn_cuda_context_t *c, bool has_ext) {
             if ((st = ordered_push_step(c, parity, next, sharded, peer ? xbitmap : c->d_bitmap)) != SNN_OK) return st;
         } else if (c->propagation == SNN_B200_PROPAGATE_ORDERED)
             b200::launch_propagate_pull(c->stream, c->device, c->n_local, c->sell_chunks, c->sell_chunk_words,
-                                    c->d_sell_off, c->d_pre, c->idx_bits,
-                                        c->d_cw, peer ? xbitmap : c->d_bitmap, c->bitmap_words, next, c->d_list, c->idx_bits,
+                                    c->d_sell_off, (const uint2 *)c->d_pre,
+                                         peer ? xbitmap : c->d_bitmap, c->bitmap_words, next, c->d_list, c->idx_bits,
                                         c->d_deg, c->d_ctr, parity, !sharded);
         else if (c->binned) {
             const cudaError_t e = b200::launch_propagate_binned(c->stream, c->d_list, c->idx_bits, next, c->d_ctr,
@@ -1124,8 +1132,8 @@ snn_status_t enqueue_step(snn_cuda_context_t *c, bool has_ext) {
                                         c->batch > 1 ? c->n_rows : 0, c->has_csc ? c->pull_above : 0);
             if (c->has_csc) {
                 b200::launch_propagate_pull(c->stream, c->device, c->n_local, c->sell_chunks, c->sell_chunk_words,
-                                    c->d_sell_off, c->d_pre, c->idx_bits,
-                                            c->d_cw, peer ? xbitmap : c->d_bitmap, c->bitmap_words, next, c->d_list, c->idx_bits,
+                                    c->d_sell_off, (const uint2 *)c->d_pre,
+                                             peer ? xbitmap : c->d_bitmap, c->bitmap_words, next, c->d_list, c->idx_bits,
                                             c->d_deg, c->d_ctr, parity, !sharded, c->pull_above);
                 c->launches++;
             }
@@ -1282,6 +1290,7 @@ snn_status_t generate_full(snn_cuda_context_t *c, const b200::GenParams &g, uint
 snn_status_t build_generated_csc(snn_cuda_context_t *c, const b200::GenParams &g) {
     const uint64_t n = g.n, nl = c->n_local, lo = c->lo;
     snn_status_t st;
+    if (c->idx_bits != 32) return SNN_ERR_UNSUPPORTED;  // 32-bit slot ids
     if ((st = dmalloc((void **)&c->d_col_ptr, nl + 1, 8)) != SNN_OK) return st;
     if ((st = dmalloc((void **)&c->d_deg, n, 4)) != SNN_OK) return st;
     {
@@ -1349,7 +1358,7 @@ snn_status_t build_generated_csc(snn_cuda_context_t *c, const b200::GenParams &g
         cudaFree(slots);
         size_t free_b = 0, total_b = 0;
         if (st == SNN_OK) st = cuda_status(cudaMemGetInfo(&free_b, &total_b));
-        const bool fits = total * (c->idx_bits / 8 + 4) + (8ull << 30) < free_b;
+        const bool fits = total * 8 + (8ull << 30) < free_b;
         if (st == SNN_OK && (fits || chunks == 1)) {
             st = alloc_sell_slots(c, total);
             break;
@@ -1431,7 +1440,7 @@ snn_status_t build_generated_csc(snn_cuda_context_t *c, const b200::GenParams &g
         b200::launch_gather_generated_sell(c->stream, c->device, g, alt ? keys_alt : keys, alt ? ids_alt : ids, ep,
                                            a, col_ptr[a], c->d_col_ptr, cnt, c->sell_chunks,
                                            c->sell_chunks > 1 ? c->sell_chunk_words * 32u : UINT64_MAX,
-                                           c->d_sell_off, c->d_pre, c->idx_bits, c->d_cw);
+                                           sell_relative(c) ? 1 : 0, c->d_sell_off, (uint2 *)c->d_pre);
         st = cuda_status(cudaGetLastError());
     }
     if (st == SNN_OK) st = cuda_status(cudaStreamSynchronize(c->stream));
@@ -1452,25 +1461,25 @@ snn_status_t build_generated_csc(snn_cuda_context_t *c, const b200::GenParams &g
 // sorted event (ORDERED) per event. ORDERED decides per step from the exact
 // event count (events > local synapses / SNN_B200_ORDERED_PULL_DIV, default
 // 10); PUSH decides on the device from the spike count (spikes > rows /
-// SNN_B200_PUSH_PULL_DIV, default 2), launching both kernels behind the same
+// SNN_B200_PUSH_PULL_DIV, default 4), launching both kernels behind the same
 // gate so no host round trip is added. A divisor of 0 disables the pull.
 snn_status_t add_pull_topology(snn_cuda_context_t *c, const snn_network_t *net, const b200::GenParams *g) {
     const bool ordered = c->propagation == SNN_B200_PROPAGATE_ORDERED;
     if (!ordered && (c->propagation != SNN_B200_PROPAGATE_PUSH || c->binned || c->mode != SNN_CUDA_MODE_FULL))
         return SNN_OK;
-    // Measured at config 2 on B200: the pull takes ~33 ms whatever the
-    // firing; the ordered push costs about as much at ~1.5e9 events, the
-    // atomic push at ~5.6e9 (56% firing at fanout 1000).
-    uint64_t div = ordered ? 10 : 2;
+    // Measured at config 2 on B200: the pull takes ~16 ms whatever the
+    // firing; the ordered push costs about as much at ~1e9 events, the
+    // atomic push at ~2.5e9 (25% firing at fanout 1000).
+    uint64_t div = ordered ? 10 : 4;
     if (const char *env = std::getenv(ordered ? "SNN_B200_ORDERED_PULL_DIV" : "SNN_B200_PUSH_PULL_DIV"))
         div = std::strtoull(env, nullptr, 10);
     c->pull_div = div;
-    if (div == 0 || c->e_local == 0 || c->batch > 1) return SNN_OK;
+    if (div == 0 || c->e_local == 0 || c->batch > 1 || c->idx_bits != 32) return SNN_OK;
     if (!ordered && c->n_rows / div > 0xffffffffull) return SNN_OK;
     size_t free_b = 0, total_b = 0;
     if (cudaMemGetInfo(&free_b, &total_b) != cudaSuccess) return SNN_ERR_CUDA;
     // Padding of the sliced ELL: about 1.07x at fan-in 1000; budget 1.15x.
-    const uint64_t sell = (uint64_t)((double)c->e_local * 1.15) * (c->idx_bits / 8 + 4) + (c->n_local + 1) * 8 +
+    const uint64_t sell = (uint64_t)((double)c->e_local * 1.15) * 8 + (c->n_local + 1) * 8 +
                           c->n_global * 4;
     const uint64_t reserve = (2 * (c->n_rows + 1) * 8) + (4ull << 30);  // build scratch + working margin
     if (sell + reserve > free_b) return SNN_OK;  // no room: every step takes the push
@@ -1974,7 +1983,7 @@ snn_status_t snn_b200_get_layout(const snn_cuda_context_t *c, snn_b200_layout_t 
         out->device_topology_bytes = 2 * ((c->slot_rows + 1) * 8 + c->slot_edges * 12);
     else if (c->opull || c->has_csc)
         out->device_topology_bytes = (c->has_csc ? (c->n_rows + 1) * 8 + c->e_local * (c->col_bits / 8 + 4) : 0) +
-                                     ((c->n_local + 31) / 32 + 1) * 8 + c->sell_slots * (c->idx_bits / 8 + 4) +
+                                     ((c->n_local + 31) / 32 * c->sell_chunks + 1) * 8 + c->sell_slots * 8 +
                                      c->n_rows * 4;
     else
         out->device_topology_bytes = (c->n_rows + 1) * 8 + c->e_local * (c->col_bits / 8 + 4);
