@@ -1040,7 +1040,12 @@ void launch_lif(cudaStream_t s, int device, uint64_t n, const LifArgs &p, float 
     PeerArgs peer{};
     if (peer_in) peer = *peer_in;
     if (n == 0 && peer.npeers == 0) return;
-    if (idx_bits == 32) {
+    // Small populations: 1024-neuron tiles, so the grid still covers the SMs.
+    const bool small = n < (uint64_t)sm_count(device) * 2u * kLifThreads * 4u * 8u;
+    if (idx_bits == 32 && small) {
+        if (ext) lif_dispatch<true, uint32_t, 1>(s, device, n, p, v, cur, ext, refr, spikes, bitmap, list, off, ctr, parity, peer);
+        else lif_dispatch<false, uint32_t, 1>(s, device, n, p, v, cur, ext, refr, spikes, bitmap, list, off, ctr, parity, peer);
+    } else if (idx_bits == 32) {
         if (ext) lif_dispatch<true, uint32_t, 8>(s, device, n, p, v, cur, ext, refr, spikes, bitmap, list, off, ctr, parity, peer);
         else lif_dispatch<false, uint32_t, 8>(s, device, n, p, v, cur, ext, refr, spikes, bitmap, list, off, ctr, parity, peer);
     } else {

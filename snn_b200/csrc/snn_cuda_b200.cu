@@ -1475,6 +1475,13 @@ snn_status_t add_pull_topology(snn_cuda_context_t *c, const snn_network_t *net, 
         div = std::strtoull(env, nullptr, 10);
     c->pull_div = div;
     if (div == 0 || c->e_local == 0 || c->batch > 1 || c->idx_bits != 32) return SNN_OK;
+    // PUSH launches the gated pull kernel every step (a few microseconds even
+    // when it exits at once): small networks, where that is a visible share
+    // of a step and a dense step is cheap anyway, keep the plain push.
+    // SNN_B200_PUSH_PULL_MIN_SYNAPSES (environment) moves the bound (tests).
+    uint64_t min_syn = 1ull << 26;
+    if (const char *env = std::getenv("SNN_B200_PUSH_PULL_MIN_SYNAPSES")) min_syn = std::strtoull(env, nullptr, 10);
+    if (!ordered && c->e_local < min_syn) return SNN_OK;
     if (!ordered && c->n_rows / div > 0xffffffffull) return SNN_OK;
     size_t free_b = 0, total_b = 0;
     if (cudaMemGetInfo(&free_b, &total_b) != cudaSuccess) return SNN_ERR_CUDA;

@@ -586,6 +586,7 @@ def test_push_with_pull_gate_dyadic_bit_exact(generated, chunk_words, monkeypatc
     With SNN_B200_PULL_CHUNK_WORDS=32 the pull's layout is cut into 3
     presynaptic chunks (shared-memory spike bits staged chunk by chunk)."""
     monkeypatch.setenv("SNN_B200_PUSH_PULL_DIV", "4")
+    monkeypatch.setenv("SNN_B200_PUSH_PULL_MIN_SYNAPSES", "0")
     if chunk_words:
         monkeypatch.setenv("SNN_B200_PULL_CHUNK_WORDS", chunk_words)
     lif = default_lif(v_rest=0.0, v_reset=0.0, v_threshold=1.0, input_scale=1.0, refractory_steps=1)
@@ -608,8 +609,11 @@ def test_push_with_pull_gate_dyadic_bit_exact(generated, chunk_words, monkeypatc
 
 
 def test_push_pull_gate_disabled_keeps_plain_push(monkeypatch):
-    monkeypatch.setenv("SNN_B200_PUSH_PULL_DIV", "0")
     net = ORC.random_pool(2000, 50, 0.1, 0.2, 3)
+    # Below the synapse bound (2^26 by default) PUSH keeps the plain push.
+    assert sb.CudaContext.create(net, None, opts()).layout["ordered_csc"] == 0
+    monkeypatch.setenv("SNN_B200_PUSH_PULL_MIN_SYNAPSES", "0")
+    monkeypatch.setenv("SNN_B200_PUSH_PULL_DIV", "0")
     ctx = sb.CudaContext.create(net, None, opts())
     assert ctx.layout["ordered_csc"] == 0
     ref = sb.CudaContext.create(net, None)  # the reference entry point never adds it
