@@ -20,7 +20,7 @@ import torch  # noqa: E402
 import torch.distributed as dist  # noqa: E402
 
 import snn_b200 as sb  # noqa: E402
-from oracle.oracle import Oracle, State, baseline_lif, stream_indices_np  # noqa: E402
+from oracle.oracle import Oracle, State, baseline_lif, default_lif, stream_indices_np  # noqa: E402
 from tests._helpers import lif_to_sb  # noqa: E402
 
 
@@ -123,6 +123,39 @@ def main():
                     np.array_equal(w.view(np.uint32), hw[keep].view(np.uint32))):
                 failures.append(f"device shard {lo} topology mismatch")
     ctx.free()
+    # Dense steps on sharded contexts: the gated pull (PUSH, one dyadic weight so
+    # every sum is exact) and the ORDERED pull, over 3-chunk layouts, against
+    # the CPU step. Frames alternate between sparse and dense drive.
+    os.environ["SNN_B200_PUSH_PULL_MIN_SYNAPSES"] = "0"
+    os.environ["SNN_B200_PULL_CHUNK_WORDS"] = "64"
+    dlif = default_lif(v_rest=0.0, v_reset=0.0, v_threshold=1.0, input_scale=1.0, refractory_steps=1)
+    dn = 6001
+    for prop, wlo, whi in ((sb.PROPAGATE_PUSH, 0.0009765625, 0.0009765625), (sb.PROPAGATE_ORDERED, -0.0005, 0.002)):
+        dnet = orc.random_pool(dn, 600, wlo, whi, 21, lif=dlif)
+        ctx = sb.CudaContext.create(dnet, None, options(prop, sb.EXCHANGE_PEER))
+        connect(ctx, sb.EXCHANGE_PEER)
+        if ctx.layout["ordered_csc"] != 1:
+            failures.append(f"rank {rank}: no pull topology for {prop}")
+        lo, cnt = ctx.local_begin, ctx.local_count
+        rng = np.random.default_rng(8)
+        frames = [(rng.random(dn) < (0.6 if t % 3 == 0 else 0.02)).astype(np.float32) * np.float32(1.5)
+                  for t in range(9)]
+        raster = np.zeros((9, cnt), np.uint8)
+        for t in range(9):
+            raster[t] = ctx.step(frames[t][lo:lo + cnt])
+        parts = [None] * world
+        dist.all_gather_object(parts, (lo, raster, ctx.download_voltage()))
+        if rank == 0:
+            st = State(dnet)
+            ras = np.array([st.step(frames[t]) for t in range(9)])
+            parts.sort(key=lambda p: p[0])
+            g_r = np.concatenate([p[1] for p in parts], axis=1)
+            g_v = np.concatenate([p[2] for p in parts])
+            if not (np.array_equal(g_r, ras) and np.array_equal(g_v.view(np.uint32), st.voltage().view(np.uint32))):
+                failures.append(f"dense sharded {prop} differs from the CPU step")
+            if not (0 < int((ras.sum(axis=1) > dn // 4).sum()) < 9):
+                failures.append("dense sharded case lacks a mix of sparse and dense steps")
+        ctx.free()
     dist.barrier()
     if rank == 0:
         print("FAILURES:" if failures else "MGPU PARITY OK", failures)
