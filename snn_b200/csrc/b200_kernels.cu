@@ -140,6 +140,9 @@ __global__ void __launch_bounds__(kLifThreads) lif_kernel(uint64_t n, LifArgs p,
                                                           uint64_t global_offset, DevCounters *ctr, int parity,
                                                           PeerArgs peer) {
     constexpr uint64_t kTile = (uint64_t)ITERS * kLifThreads * 4u;
+    // The step's injection (stream order: already complete) has read the
+    // index; advance it for the next step.
+    if (p.stream_step != nullptr && blockIdx.x == 0 && threadIdx.x == 0) *p.stream_step += 1ull;
     __shared__ TIdx sbuf[WRITE_LIST ? kTile : 1];
     __shared__ uint32_t warp_tot[kLifThreads / 32];
     __shared__ uint32_t s_base;
@@ -753,7 +756,9 @@ __global__ void inject_ordered_kernel(uint64_t count, const uint64_t *__restrict
 }
 
 __global__ void inject_stream_kernel(uint64_t seed, uint64_t first_draw, uint64_t count, uint64_t n, float addend,
-                                     float *__restrict__ cur, uint64_t lo, uint64_t hi) {
+                                     float *__restrict__ cur, uint64_t lo, uint64_t hi,
+                                     const unsigned long long *__restrict__ step_dev) {
+    if (step_dev != nullptr) first_draw = (uint64_t)*step_dev * count;
     const uint64_t stride = (uint64_t)blockDim.x * gridDim.x;
     for (uint64_t k = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; k < count; k += stride) {
         const uint64_t i = draw_at(seed, first_draw + k + 1u) % n;
@@ -1147,6 +1152,10 @@ void launch_propagate_pull(cudaStream_t s, int device, uint64_t n_local, uint32_
                                                              count_spikes, pull_above);
 }
 
+__global__ void set_u64_kernel(unsigned long long *p, unsigned long long v) { *p = v; }
+
+void launch_set_u64(cudaStream_t s, unsigned long long *p, unsigned long long v) { set_u64_kernel<<<1, 1, 0, s>>>(p, v); }
+
 __global__ void fill_u2_kernel(uint2 *__restrict__ p, uint64_t n, uint2 v) {
     const uint64_t stride = (uint64_t)blockDim.x * gridDim.x;
     for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) p[i] = v;
@@ -1179,9 +1188,9 @@ void launch_inject_ordered(cudaStream_t s, int device, uint64_t count, const uin
 }
 
 void launch_inject_stream(cudaStream_t s, int device, uint64_t seed, uint64_t step, uint64_t count, uint64_t n,
-                          float addend, float *cur, uint64_t lo, uint64_t hi) {
+                          float addend, float *cur, uint64_t lo, uint64_t hi, const unsigned long long *step_dev) {
     inject_stream_kernel<<<grid_for(device, 8, count, 256), 256, 0, s>>>(seed, step * count, count, n, addend, cur,
-                                                                        lo, hi);
+                                                                        lo, hi, step_dev);
 }
 
 void launch_convert_cols(cudaStream_t s, int device, const uint64_t *src, void *dst, int col_bits, uint64_t count,

@@ -16,6 +16,9 @@ struct LifArgs {
     float v_threshold;
     float input_scale;
     uint32_t refractory_steps;
+    // When set (graph-replayed runs), block 0 of the LIF kernel advances this
+    // device-side injection-stream step index once per step.
+    unsigned long long *stream_step;
 };
 
 // Small device-side bookkeeping block, one per context.
@@ -29,6 +32,7 @@ struct DevCounters {
     uint32_t pad;
     unsigned long long spikes;
     unsigned long long events;
+    unsigned long long stream_step;  // injection-stream step of graph-replayed runs
 };
 
 // Peer (NVLink, CUDA IPC) spike-bitmap exchange fused into the LIF kernel:
@@ -148,6 +152,8 @@ void launch_propagate_pull(cudaStream_t s, int device, uint64_t n_local, uint32_
                            float *next, const void *list, int idx_bits, const uint32_t *out_degree, DevCounters *ctr,
                            int parity, int count_spikes, uint32_t pull_above = 0);
 void launch_fill_u2(cudaStream_t s, int device, uint2 *p, uint64_t n, uint32_t x, uint32_t y);
+// *p = v, in stream order.
+void launch_set_u64(cudaStream_t s, unsigned long long *p, unsigned long long v);
 
 // STREAMING: one chunk of `rows` rows starting at row0, with the chunk's raw
 // row_ptr slice (rows+1 entries, absolute edge offsets) and its edges starting
@@ -168,8 +174,11 @@ void launch_inject_atomic(cudaStream_t s, int device, uint64_t count, const uint
 void launch_inject_ordered(cudaStream_t s, int device, uint64_t count, const uint64_t *idx, const float *val,
                            float scale, float *cur, uint64_t lo, uint64_t hi);
 // The seeded injection stream (see snn_b200_inject_stream_async).
+// step_dev != nullptr: the step index is read on the device from *step_dev
+// (graph-replayed runs; `step` is then ignored).
 void launch_inject_stream(cudaStream_t s, int device, uint64_t seed, uint64_t step, uint64_t count, uint64_t n,
-                          float addend, float *cur, uint64_t lo, uint64_t hi);
+                          float addend, float *cur, uint64_t lo, uint64_t hi,
+                          const unsigned long long *step_dev = nullptr);
 
 // u64 global column ids -> local ids of the chosen width (subtracting lo).
 void launch_convert_cols(cudaStream_t s, int device, const uint64_t *src, void *dst, int col_bits, uint64_t count,

@@ -104,6 +104,14 @@ struct snn_cuda_context {
     int cur = 0;
     float *d_ext = nullptr;
     bool ext_held = false;  // snn_b200_set_external: d_ext applies to every step without its own
+    // run_stream_async on unsharded push contexts replays a captured CUDA
+    // graph of two steps (one per parity); the injection step index then
+    // lives on the device (DevCounters::stream_step, advanced by LIF).
+    bool dev_stream_step = false;
+    cudaGraphExec_t graph = nullptr;
+    uint64_t graph_seed = 0, graph_count = 0, graph_launches = 0;
+    float graph_value = 0.0f;
+    bool graph_ext = false;
     uint32_t *d_refr = nullptr;
     uint8_t *d_spikes = nullptr;
     void *d_ws = nullptr;
@@ -285,6 +293,7 @@ void free_context(snn_cuda_context_t *c) {
     if (c->ev_lif) cudaEventDestroy(c->ev_lif);
     if (c->ev_spk) cudaEventDestroy(c->ev_spk);
     if (c->spk_stream) cudaStreamDestroy(c->spk_stream);
+    if (c->graph) cudaGraphExecDestroy(c->graph);
     for (auto *v : {&c->pending, &c->pool})
         for (auto &g : *v)
             for (auto e : g.ev) cudaEventDestroy(e);
@@ -1073,7 +1082,9 @@ snn_status_t enqueue_step(snn_cuda_context_t *c, bool has_ext) {
         pa.ticket = (uint32_t *)((char *)c->d_xbuf + xflags_offset(c) + c->world * 8);
         xbitmap = (uint32_t *)c->d_xbuf + par * c->bitmap_words;
     }
-    b200::launch_lif(c->stream, c->device, c->n_local, c->args, c->d_v, cur, has_ext ? c->d_ext : nullptr, c->d_refr,
+    b200::LifArgs lif_args = c->args;
+    if (c->dev_stream_step) lif_args.stream_step = &c->d_ctr->stream_step;
+    b200::launch_lif(c->stream, c->device, c->n_local, lif_args, c->d_v, cur, has_ext ? c->d_ext : nullptr, c->d_refr,
                      c->d_spikes, own_bitmap, sharded ? nullptr : c->d_list, c->idx_bits, c->lo, c->d_ctr, parity,
                      peer ? &pa : nullptr);
     snn_status_t st = check_launch(c);
@@ -1531,6 +1542,79 @@ snn_status_t finish_generated(snn_cuda_context_t *c, const b200::GenParams &g, u
     return SNN_OK;
 }
 
+// Launch-bound loops (small networks, quiet steps) pay a launch gap per
+// kernel; unsharded push contexts without device timing replay a captured
+// graph of two steps instead. SNN_B200_NO_GRAPHS (environment) disables it.
+bool graph_eligible(const snn_cuda_context_t *c) {
+    return c->world == 1 && c->mode == SNN_CUDA_MODE_FULL && c->propagation != SNN_B200_PROPAGATE_ORDERED &&
+           !c->binned && !c->timing && std::getenv("SNN_B200_NO_GRAPHS") == nullptr;
+}
+
+// One step of the injection stream with the step index read on the device.
+snn_status_t stream_step_dev(snn_cuda_context_t *c, uint64_t seed, snn_size_t count, float value) {
+    if (count) {
+        b200::launch_inject_stream(c->stream, c->device, seed, 0, count, c->n_global, value * c->lif.input_scale,
+                                   c->d_cur[c->cur], c->lo, c->hi, &c->d_ctr->stream_step);
+        c->launches++;
+    }
+    return enqueue_step(c, c->ext_held);
+}
+
+snn_status_t run_stream_graph(snn_cuda_context_t *c, uint64_t seed, uint64_t first_step, uint64_t steps,
+                              snn_size_t count, float value) {
+    snn_status_t st = SNN_OK;
+    b200::launch_set_u64(c->stream, &c->d_ctr->stream_step, first_step);
+    c->launches++;
+    c->dev_stream_step = true;
+    uint64_t t = 0;
+    // The graph starts on an even step (current buffer 0, list parity 0).
+    if (c->step & 1u) {
+        st = stream_step_dev(c, seed, count, value);
+        ++t;
+    }
+    if (st == SNN_OK && (c->graph == nullptr || c->graph_seed != seed || c->graph_count != count ||
+                         c->graph_value != value || c->graph_ext != c->ext_held)) {
+        if (c->graph) cudaGraphExecDestroy(c->graph);
+        c->graph = nullptr;
+        const uint64_t step0 = c->step, launches0 = c->launches;
+        const int cur0 = c->cur;
+        cudaGraph_t g = nullptr;
+        if (cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeRelaxed) == cudaSuccess) {
+            snn_status_t cs = stream_step_dev(c, seed, count, value);
+            if (cs == SNN_OK) cs = stream_step_dev(c, seed, count, value);
+            const cudaError_t ce = cudaStreamEndCapture(c->stream, &g);
+            if (cs == SNN_OK && ce == cudaSuccess && g != nullptr &&
+                cudaGraphInstantiate(&c->graph, g, 0) == cudaSuccess) {
+                c->graph_seed = seed;
+                c->graph_count = count;
+                c->graph_value = value;
+                c->graph_ext = c->ext_held;
+                c->graph_launches = c->launches - launches0;
+            } else {
+                c->graph = nullptr;
+            }
+            if (g) cudaGraphDestroy(g);
+        }
+        cudaGetLastError();
+        // Capture recorded the work without running it: undo its host state.
+        c->step = step0;
+        c->cur = cur0;
+        c->launches = launches0;
+    }
+    while (st == SNN_OK && c->graph != nullptr && steps - t >= 2) {
+        st = cuda_status(cudaGraphLaunch(c->graph, c->stream));
+        c->step += 2;
+        c->launches += c->graph_launches;
+        t += 2;
+    }
+    while (st == SNN_OK && t < steps) {  // odd remainder, or no graph could be made
+        st = stream_step_dev(c, seed, count, value);
+        ++t;
+    }
+    c->dev_stream_step = false;
+    return st == SNN_OK ? cuda_status(cudaGetLastError()) : st;
+}
+
 }  // namespace
 
 // ======================================================================
@@ -1921,6 +2005,7 @@ snn_status_t snn_b200_run_stream_async(snn_cuda_context_t *c, uint64_t seed, uin
     if (c == nullptr) return SNN_ERR_INVALID_ARGUMENT;
     snn_status_t st = set_device(c);
     if (st != SNN_OK) return st;
+    if (graph_eligible(c) && steps >= 8) return run_stream_graph(c, seed, first_step, steps, count, value);
     for (uint64_t t = 0; t < steps; ++t) {
         if (count) {
             b200::launch_inject_stream(c->stream, c->device, seed, first_step + t, count, c->n_global,

@@ -618,3 +618,28 @@ def test_push_pull_gate_disabled_keeps_plain_push(monkeypatch):
     assert ctx.layout["ordered_csc"] == 0
     ref = sb.CudaContext.create(net, None)  # the reference entry point never adds it
     assert ref.layout["ordered_csc"] == 0
+
+
+def test_run_stream_graph_replay_dyadic_exact():
+    """Unsharded push contexts replay run_stream_async as a captured CUDA
+    graph of two steps (the injection step index kept on the device). Starting
+    on an odd step, with an odd count of steps, then again with another seed
+    (a new graph): spikes, events and voltages equal the CPU step (one shared
+    dyadic weight makes every sum exact), and equal an eager run."""
+    lif = baseline_lif()
+    n, f = 30011, 64
+    net = ORC.random_pool(n, f, 0.25, 0.25, 5, lif=lif)
+    st = State(net)
+    sc1, ev1, _, _ = ORC.run_inject_stream(net, st, 3, 0, 1, 600, 20.0)
+    sc2, ev2, _, _ = ORC.run_inject_stream(net, st, 3, 1, 37, 600, 20.0)
+    sc3, ev3, _, _ = ORC.run_inject_stream(net, st, 9, 38, 20, 600, 20.0)
+    ctx = sb.CudaContext.create(net, None, opts())
+    ctx.run_stream_async(3, 0, 1, 600, 20.0)   # step 0 (fewer than 8 steps: launched one by one)
+    ctx.run_stream_async(3, 1, 37, 600, 20.0)  # starts on an odd step
+    ctx.run_stream_async(9, 38, 20, 600, 20.0)  # another seed: a new graph
+    ctx.synchronize()
+    s = ctx.stats()
+    assert s["steps"] == 58
+    assert s["spikes"] == int(sc1.sum() + sc2.sum() + sc3.sum())
+    assert s["events"] == int(ev1.sum() + ev2.sum() + ev3.sum())
+    np.testing.assert_array_equal(bits(st.voltage()), bits(ctx.download_voltage()))
