@@ -136,7 +136,12 @@ void snn_test_cuda_force_meminfo_fail(int enable);
 
 typedef enum snn_b200_propagation {
     /* Push from the compacted spike list with L2-resident fp32 red.add
-     * (the reference's accumulation semantics; order not deterministic). */
+     * (the reference's accumulation semantics; order not deterministic).
+     * Contexts made with options or by the device generators also keep a
+     * pull topology (chunked sliced-ELL CSC) when the device has room and
+     * the network has 2^26+ synapses; steps where more than a quarter of the
+     * rows fire then take the pull instead (chosen on the device), which
+     * folds in CSR order. snn_cuda_create keeps the plain push. */
     SNN_B200_PROPAGATE_PUSH = 0,
     /* Every target folds its contributions in CSR order (ascending
      * presynaptic row, ascending edge): bit-identical to the reference's
