@@ -6,9 +6,12 @@ fixed fanout 1,000 (10B synapses), weights U[-0.2, 0.5] mV, FULL policy;
 every step injects 0.5% of the neurons (seeded uniform indices) with 25.0.
 The network is generated on the device, bit-identical to the reference's
 snn_build_random_pool for the same seed (a host build would need ~120 GB and
-minutes). At N GPUs the pool is sharded by postsynaptic neuron (strong
-scaling: the total network is fixed) and the spike bitmap is all-gathered
-with NCCL every step.
+minutes). Propagation is the atomic push, with the chunked sliced-ELL pull
+taking the steps where more than a quarter of the rows fire (chosen on the
+device). At N GPUs the pool is sharded by postsynaptic neuron (strong
+scaling: the total network is fixed) and every step's spike bitmap is
+exchanged over NVLink by the LIF kernel itself (--exchange peer; --exchange
+nccl all-gathers it with NCCL).
 
     python bench.py [--gpus N --steps K --warmup W]          # snn_b200 arm
     python bench.py --impl reference [--steps K --warmup W]  # reference CPU arm
