@@ -136,6 +136,7 @@ def measured_peak_gbs():
 # dram__bytes_read.sum + dram__bytes_write.sum / events of one ncu capture
 # (profiles/propagate_push_config2.md); scaled by this run's events.
 NCU_DRAM_BYTES_PER_EVENT = 8.68
+NCU_PULL_BYTES_PER_SLOT = 8.0
 
 
 # ------------------------------------------------------------ CPU side ----
@@ -527,8 +528,13 @@ def run_b200(args):
     prop_s = s["propagate_ms"] / 1e3
     achieved = prop_bytes / prop_s / 1e9 if prop_s > 0 else 0.0
     traffic = None
-    if args.propagation not in ("binned", "ordered") and not gated and int(lay["index_bits"]) == 32 and timed:
-        traffic = NCU_DRAM_BYTES_PER_EVENT * s["events"] / timed
+    if args.propagation not in ("binned", "ordered") and int(lay["index_bits"]) == 32 and timed:
+        # ncu-measured DRAM bytes: the push kernel 8.68 B per event, the pull
+        # kernel 8 B per slot of its layout (profiles/); pull steps counted
+        # on the device.
+        push_events = s["events"] - s.get("pull_events", 0)
+        traffic = (NCU_DRAM_BYTES_PER_EVENT * push_events
+                   + NCU_PULL_BYTES_PER_SLOT * int(lay.get("pull_slots", 0)) * s.get("pull_steps", 0)) / timed
     step_bytes = (prop_bytes + 25.0 * ctx.local_count * timed
                   + 12.0 * count * timed)
     launches = int(s["kernel_launches"])
@@ -585,6 +591,7 @@ def run_b200(args):
             "spike_rate": spikes_total / (args.steps * n), "events_per_step": events_total / args.steps,
             "kernel_ms": {"lif": s["lif_ms"] / args.steps, "exchange": s["exchange_ms"] / args.steps,
                           "propagate": s["propagate_ms"] / args.steps},
+            "pull_steps": int(s.get("pull_steps", 0)),
             "gpu_launches": launches, "generate_s": gen_s, "clocks": clk.summary(), "e2e": e2e,
             "cpu_baseline": cpu,
         }

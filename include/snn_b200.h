@@ -207,7 +207,8 @@ typedef struct snn_b200_stats {
     double propagate_ms;       /* device time of the propagation kernels (timing = 1) */
     double lif_ms;             /* device time of the LIF kernels (timing = 1) */
     double exchange_ms;        /* device time of the spike all-gather + compaction (timing = 1) */
-    uint64_t pull_steps;       /* ORDERED: steps that took the pull over the CSC (dense steps) */
+    uint64_t pull_steps;       /* steps whose propagation ran the pull kernel (dense steps) */
+    uint64_t pull_events;      /* synaptic events of those steps */
 } snn_b200_stats_t;
 
 typedef struct snn_b200_layout {
@@ -224,6 +225,7 @@ typedef struct snn_b200_layout {
     uint32_t ordered_csc;           /* ORDERED: 1 when a CSC is resident (pull for dense steps) */
     uint32_t batch;                 /* states sharing the topology (neuron_count = batch x rows) */
     snn_size_t topology_rows;       /* rows of the shared topology (n of the network) */
+    uint64_t pull_slots;            /* slots (8-byte id/weight pairs) of the pull topology, 0 without */
 } snn_b200_layout_t;
 
 snn_b200_options_t snn_b200_default_options(void);

@@ -86,7 +86,7 @@ class Options(C.Structure):
 class Stats(C.Structure):
     _fields_ = [("steps", u64), ("spikes", u64), ("events", u64), ("kernel_launches", u64),
                 ("step_ms", C.c_double), ("propagate_ms", C.c_double), ("lif_ms", C.c_double),
-                ("exchange_ms", C.c_double), ("pull_steps", u64)]
+                ("exchange_ms", C.c_double), ("pull_steps", u64), ("pull_events", u64)]
 
     def as_dict(self):
         return {k: getattr(self, k) for k, _ in self._fields_}
@@ -96,7 +96,7 @@ class Layout(C.Structure):
     _fields_ = [("neuron_count", u64), ("local_begin", u64), ("local_count", u64), ("local_synapses", u64),
                 ("index_bits", C.c_uint32), ("propagation", C.c_int), ("device_state_bytes", u64),
                 ("device_topology_bytes", u64), ("binned", C.c_uint32), ("binned_passes", C.c_uint32),
-                ("ordered_csc", C.c_uint32), ("batch", C.c_uint32), ("topology_rows", u64)]
+                ("ordered_csc", C.c_uint32), ("batch", C.c_uint32), ("topology_rows", u64), ("pull_slots", u64)]
 
     def as_dict(self):
         return {k: getattr(self, k) for k, _ in self._fields_}

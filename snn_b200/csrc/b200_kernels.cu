@@ -107,6 +107,9 @@ __global__ void init_state_kernel(uint64_t n, float v_rest, float *v, float *cur
         ctr->error = 0u;
         ctr->spikes = 0ull;
         ctr->events = 0ull;
+        ctr->stream_step = 0ull;
+        ctr->pull_runs = 0ull;
+        ctr->pull_events = 0ull;
     }
 }
 
@@ -577,6 +580,8 @@ __global__ void __launch_bounds__(256) propagate_pull_kernel(uint64_t n_local, c
     unsigned long long events = 0;
     for (uint64_t s = gthread; s < count; s += nthreads) events += out_degree[(uint64_t)list[s]];
     block_add_u64(events, &ctr->events);
+    block_add_u64(events, &ctr->pull_events);
+    if (blockIdx.x == 0 && threadIdx.x == 0) ctr->pull_runs += 1ull;
     step_epilogue(ctr, parity, count_spikes, count);
 }
 
@@ -682,6 +687,8 @@ __global__ void __launch_bounds__(kPullSmemThreads, 1)
     unsigned long long events = 0;
     for (uint64_t s = gthread; s < count; s += nthreads) events += out_degree[(uint64_t)list[s]];
     block_add_u64(events, &ctr->events);
+    block_add_u64(events, &ctr->pull_events);
+    if (blockIdx.x == 0 && threadIdx.x == 0) ctr->pull_runs += 1ull;
     step_epilogue(ctr, parity, count_spikes, count);
 }
 

@@ -33,6 +33,8 @@ struct DevCounters {
     unsigned long long spikes;
     unsigned long long events;
     unsigned long long stream_step;  // injection-stream step of graph-replayed runs
+    unsigned long long pull_runs;    // steps whose propagation ran a pull kernel
+    unsigned long long pull_events;  // synaptic events of those steps
 };
 
 // Peer (NVLink, CUDA IPC) spike-bitmap exchange fused into the LIF kernel:

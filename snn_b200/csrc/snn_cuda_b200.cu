@@ -150,7 +150,6 @@ struct snn_cuda_context {
     uint64_t sell_chunk_words = 0;  // bitmap words per chunk, fixed when the layout is built
     uint32_t pull_above = 0;  // PUSH with a SELL CSC: steps with more spikes than this pull
     uint64_t pull_div = 10;  // pull when a step's events exceed local synapses / pull_div
-    uint64_t pull_steps = 0;
     uint32_t *d_sdeg = nullptr;
     unsigned long long *d_eoff = nullptr;
     uint32_t *d_okeys[2] = {nullptr, nullptr};
@@ -650,7 +649,6 @@ snn_status_t ordered_push_step(snn_cuda_context_t *c, int parity, float *next, b
                                     bitmap, c->bitmap_words, next, c->d_list, c->idx_bits, c->d_deg, c->d_ctr, parity,
                                     !sharded);
         c->launches += 2;
-        c->pull_steps++;
         return SNN_OK;
     }
     // Row ranges of at most ocap events each (one range unless the step is huge).
@@ -2041,7 +2039,8 @@ snn_status_t snn_b200_get_stats(snn_cuda_context_t *c, snn_b200_stats_t *out) {
     out->propagate_ms = c->t_prop;
     out->lif_ms = c->t_lif;
     out->exchange_ms = c->t_exchange;
-    out->pull_steps = c->pull_steps;
+    out->pull_steps = d.pull_runs;
+    out->pull_events = d.pull_events;
     return SNN_OK;
 }
 
@@ -2053,9 +2052,10 @@ snn_status_t snn_b200_reset_stats(snn_cuda_context_t *c) {
     if (cudaMemcpy(&d, c->d_ctr, sizeof(d), cudaMemcpyDeviceToHost) != cudaSuccess) return SNN_ERR_CUDA;
     d.spikes = 0;
     d.events = 0;
+    d.pull_runs = 0;
+    d.pull_events = 0;
     if (cudaMemcpy(c->d_ctr, &d, sizeof(d), cudaMemcpyHostToDevice) != cudaSuccess) return SNN_ERR_CUDA;
     c->launches = 0;
-    c->pull_steps = 0;
     c->t_step = c->t_lif = c->t_exchange = c->t_prop = 0;
     return SNN_OK;
 }
@@ -2082,6 +2082,7 @@ snn_status_t snn_b200_get_layout(const snn_cuda_context_t *c, snn_b200_layout_t 
     out->binned = c->binned ? 1u : 0u;
     out->binned_passes = c->binned ? c->bin.passes : 0u;
     out->ordered_csc = (c->opull || c->has_csc) ? 1u : 0u;
+    out->pull_slots = c->sell_slots;
     out->batch = (uint32_t)c->batch;
     out->topology_rows = c->n_rows;
     return SNN_OK;

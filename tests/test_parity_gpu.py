@@ -605,7 +605,11 @@ def test_push_with_pull_gate_dyadic_bit_exact(generated, chunk_words, monkeypatc
     dense = (cr.sum(axis=1) > n // 4).sum()
     assert 0 < dense < 12
     np.testing.assert_array_equal(bits(cv), bits(gv))
-    assert ctx.stats()["events"] == int(cr.sum()) * f
+    s = ctx.stats()
+    assert s["events"] == int(cr.sum()) * f
+    assert s["pull_steps"] == dense  # the gate: more spikes than rows / 4
+    assert s["pull_events"] == int(cr[cr.sum(axis=1) > n // 4].sum()) * f
+    assert ctx.layout["pull_slots"] >= n * f
 
 
 def test_push_pull_gate_disabled_keeps_plain_push(monkeypatch):
