@@ -256,6 +256,15 @@ snn_status_t snn_b200_create_layered_random(const snn_size_t *layer_sizes, size_
                                             const snn_b200_options_t *options,
                                             snn_cuda_context_t **out_context);
 
+/* Device build of the reference's snn_build_feedforward (src/snn.c:463-521),
+ * bit-identical: layer l's rows connect to every neuron of layer l+1 in order
+ * when fanout is 0 or >= its size, else to `fanout` targets drawn from one
+ * splitmix64 stream seeded with `seed` (edge order, sparse layers only);
+ * every weight is `weight`. At most 16 layers. */
+snn_status_t snn_b200_create_feedforward(const snn_size_t *layer_sizes, size_t layer_count, snn_size_t fanout,
+                                         float weight, uint64_t seed, const snn_lif_params_t *lif,
+                                         const snn_b200_options_t *options, snn_cuda_context_t **out_context);
+
 /* Human-readable detail of the calling thread's most recent CUDA/NCCL
  * failure inside the library ("" if none); valid until the next failure. */
 const char *snn_b200_last_error(void);

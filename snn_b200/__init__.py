@@ -121,6 +121,7 @@ ENTRY_POINTS = [
     ("snn_b200_create", C.c_int, [P, P, P, P]),
     ("snn_b200_create_random_pool", C.c_int, [P, P, P, P, P]),
     ("snn_b200_create_layered_random", C.c_int, [P, C.c_size_t, u64, f32, f32, u64, P, P, P]),
+    ("snn_b200_create_feedforward", C.c_int, [P, C.c_size_t, u64, f32, u64, P, P, P]),
     ("snn_b200_nccl_unique_id", C.c_int, [P]),
     ("snn_b200_ipc_handle", C.c_int, [P, P]),
     ("snn_b200_ipc_connect", C.c_int, [P, P]),
@@ -301,6 +302,17 @@ class CudaContext:
                                                   C.byref(lif) if lif else None,
                                                   C.byref(options) if options else None, C.byref(h))
         _check(st, "snn_b200_create_layered_random")
+        return cls(h)
+
+    @classmethod
+    def feedforward(cls, layers, fanout, weight, seed, lif=None, options=None):
+        """snn_b200_create_feedforward: snn_build_feedforward on the device."""
+        arr = np.ascontiguousarray(layers, np.uint64)
+        h = P()
+        st = lib().snn_b200_create_feedforward(_ptr(arr), arr.size, fanout, weight, seed,
+                                               C.byref(lif) if lif else None,
+                                               C.byref(options) if options else None, C.byref(h))
+        _check(st, "snn_b200_create_feedforward")
         return cls(h)
 
     # ---- reference entry points ---------------------------------------

@@ -789,49 +789,79 @@ __global__ void row_degrees_kernel(const uint64_t *__restrict__ row_ptr, uint64_
 }
 
 // Target range of presynaptic row `pre`: random pool -> all n neurons;
-// layered -> the next layer (the last layer has no edges).
+// layered and feed-forward -> the next layer (the last layer has no edges).
+// Also the row's edges: [first, first + edges), and for a sparse
+// feed-forward layer the draw index of the row's first edge.
 struct TargetRange {
     uint64_t base;
     uint64_t count;
     bool has_edges;
+    uint64_t first;
+    uint64_t edges;
+    uint64_t draw0;  // feed-forward: ~0 for a dense layer
 };
 
+__device__ __forceinline__ uint64_t rows_with_edges(const GenParams &g) {
+    return g.recurrent ? g.n : g.off[g.layers - 1];
+}
+
 __device__ __forceinline__ TargetRange target_range(const GenParams &g, uint64_t pre) {
-    TargetRange t{0, g.n, true};
+    TargetRange t{0, g.n, true, 0, g.fanout, ~0ull};
     if (!g.recurrent) {
         int l = 0;
         while (l + 1 < g.layers && pre >= g.off[l + 1]) ++l;
         if (l + 1 >= g.layers) {
             t.has_edges = false;
             t.count = 0;
-        } else {
-            t.base = g.off[l + 1];
-            t.count = g.off[l + 2] - g.off[l + 1];
+            t.edges = 0;
+            t.first = g.feedforward ? g.ledge[g.layers - 1] : rows_with_edges(g) * g.fanout;
+            return t;
+        }
+        t.base = g.off[l + 1];
+        t.count = g.off[l + 2] - g.off[l + 1];
+        if (g.feedforward) {
+            t.edges = g.lfan[l];
+            t.first = g.ledge[l] + (pre - g.off[l]) * t.edges;
+            t.draw0 = g.ldraw[l] == ~0ull ? ~0ull : g.ldraw[l] + (pre - g.off[l]) * t.edges;
+            return t;
         }
     }
+    t.first = pre * g.fanout;
     return t;
 }
 
-// Edges of rows in non-last layers: row `pre` owns edges [pre*F, pre*F+F).
+__device__ __forceinline__ uint64_t total_edges(const GenParams &g) {
+    return g.feedforward ? g.ledge[g.layers - 1] : rows_with_edges(g) * g.fanout;
+}
+
+// The presynaptic row that owns edge e.
+__device__ __forceinline__ uint64_t edge_row(const GenParams &g, uint64_t e) {
+    if (!g.feedforward) return e / g.fanout;
+    int l = 0;
+    while (l + 2 < g.layers && e >= g.ledge[l + 1]) ++l;
+    return g.off[l] + (e - g.ledge[l]) / g.lfan[l];
+}
+
+// Edge e of row `pre` (t = target_range(g, pre)).
 __device__ __forceinline__ uint64_t gen_target(const GenParams &g, uint64_t pre, uint64_t e, const TargetRange &t) {
+    if (g.feedforward) {
+        const uint64_t j = e - t.first;  // src/snn.c:507: j when dense, else the next draw % post
+        return t.draw0 == ~0ull ? t.base + j : t.base + draw_at(g.seed, t.draw0 + j + 1u) % t.count;
+    }
     uint64_t post = t.base + draw_at(g.seed, 2u * e + 1u) % t.count;
     if (g.recurrent && !g.allow_self && post == pre) post = (post + 1u) % g.n;  // src/snn.c:563-565
     return post;
 }
 
 __device__ __forceinline__ float gen_weight(const GenParams &g, uint64_t e) {
+    if (g.feedforward) return g.wconst;
     return lerp_weight(g.wmin, g.wmax, unit_float(draw_at(g.seed, 2u * e + 2u)));
-}
-
-__device__ __forceinline__ uint64_t rows_with_edges(const GenParams &g) {
-    return g.recurrent ? g.n : g.off[g.layers - 1];
 }
 
 __global__ void gen_row_ptr_dense_kernel(GenParams g, uint64_t *__restrict__ row_ptr) {
     const uint64_t stride = (uint64_t)blockDim.x * gridDim.x;
-    const uint64_t r = rows_with_edges(g);
     for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i <= g.n; i += stride)
-        row_ptr[i] = (i < r ? i : r) * g.fanout;
+        row_ptr[i] = i < g.n ? target_range(g, i).first : total_edges(g);
 }
 
 template <typename TCol>
@@ -839,7 +869,7 @@ __global__ void __launch_bounds__(256) gen_edges_dense_kernel(GenParams g, uint6
                                                               TCol *__restrict__ col, float *__restrict__ w) {
     const uint64_t stride = (uint64_t)blockDim.x * gridDim.x;
     for (uint64_t e = e0 + (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; e < e1; e += stride) {
-        const uint64_t pre = e / g.fanout;
+        const uint64_t pre = edge_row(g, e);
         const TargetRange t = target_range(g, pre);
         col[e] = (TCol)gen_target(g, pre, e, t);
         w[e] = gen_weight(g, e);
@@ -857,8 +887,8 @@ __global__ void __launch_bounds__(256) gen_count_shard_kernel(GenParams g, uint6
         const TargetRange t = target_range(g, pre);
         uint32_t c = 0;
         if (t.has_edges) {
-            for (uint64_t j = lane; j < g.fanout; j += 32u) {
-                const uint64_t post = gen_target(g, pre, pre * g.fanout + j, t);
+            for (uint64_t j = lane; j < t.edges; j += 32u) {
+                const uint64_t post = gen_target(g, pre, t.first + j, t);
                 c += (post >= lo && post < hi);
             }
         }
@@ -880,12 +910,12 @@ __global__ void __launch_bounds__(256) gen_fill_shard_kernel(GenParams g, uint64
         const TargetRange t = target_range(g, pre);
         if (!t.has_edges) continue;
         uint64_t pos = row_ptr[pre];
-        for (uint64_t j0 = 0; j0 < g.fanout; j0 += 32u) {
+        for (uint64_t j0 = 0; j0 < t.edges; j0 += 32u) {
             const uint64_t j = j0 + lane;
             bool keep = false;
             uint64_t post = 0;
-            const uint64_t e = pre * g.fanout + j;
-            if (j < g.fanout) {
+            const uint64_t e = t.first + j;
+            if (j < t.edges) {
                 post = gen_target(g, pre, e, t);
                 keep = post >= lo && post < hi;
             }
@@ -904,10 +934,10 @@ __global__ void __launch_bounds__(256) gen_fill_shard_kernel(GenParams g, uint64
 // In-degree of the targets in [lo, hi): one relaxed atomic per kept edge.
 __global__ void __launch_bounds__(256) gen_indegree_kernel(GenParams g, uint64_t lo, uint64_t hi,
                                                            unsigned long long *__restrict__ indeg) {
-    const uint64_t total = rows_with_edges(g) * g.fanout;
+    const uint64_t total = total_edges(g);
     const uint64_t stride = (uint64_t)blockDim.x * gridDim.x;
     for (uint64_t e = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += stride) {
-        const uint64_t pre = e / g.fanout;
+        const uint64_t pre = edge_row(g, e);
         const uint64_t post = gen_target(g, pre, e, target_range(g, pre));
         if (post >= lo && post < hi) atomicAdd(indeg + (post - lo), 1ull);
     }
@@ -917,10 +947,10 @@ __global__ void __launch_bounds__(256) gen_indegree_kernel(GenParams g, uint64_t
 // the target's in-edges come from that chunk (chunked sliced-ELL layout).
 __global__ void __launch_bounds__(256) gen_chunk_counts_kernel(GenParams g, uint64_t lo, uint64_t hi, uint32_t chunks,
                                                                uint64_t chunk_neurons, uint32_t *__restrict__ cnt) {
-    const uint64_t total = rows_with_edges(g) * g.fanout;
+    const uint64_t total = total_edges(g);
     const uint64_t stride = (uint64_t)blockDim.x * gridDim.x;
     for (uint64_t e = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += stride) {
-        const uint64_t pre = e / g.fanout;
+        const uint64_t pre = edge_row(g, e);
         const uint64_t post = gen_target(g, pre, e, target_range(g, pre));
         if (post >= lo && post < hi) atomicAdd(cnt + (post - lo) * chunks + pre / chunk_neurons, 1u);
     }
@@ -952,12 +982,12 @@ __global__ void __launch_bounds__(256) gen_fill_keys_kernel(GenParams g, uint64_
         const TargetRange t = target_range(g, pre);
         if (!t.has_edges) continue;
         uint64_t pos = row_off[pre];
-        for (uint64_t j0 = 0; j0 < g.fanout; j0 += 32u) {
+        for (uint64_t j0 = 0; j0 < t.edges; j0 += 32u) {
             const uint64_t j = j0 + lane;
-            const uint64_t e = pre * g.fanout + j;
+            const uint64_t e = t.first + j;
             uint64_t post = 0;
             bool keep = false;
-            if (j < g.fanout) {
+            if (j < t.edges) {
                 post = gen_target(g, pre, e, t);
                 keep = post >= lo && post < hi;
             }
@@ -986,7 +1016,7 @@ __global__ void gather_generated_sell_kernel(GenParams g, const uint32_t *__rest
     for (uint64_t q = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; q < e; q += stride) {
         const uint64_t ed = eids[q];
         const uint64_t t = t0 + keys[q];
-        const uint64_t p = ed / g.fanout;
+        const uint64_t p = edge_row(g, ed);
         const uint32_t c = (uint32_t)(p / chunk_neurons);
         uint64_t k = q0 + q - col_ptr[t];
         for (uint32_t c2 = 0; c2 < c; ++c2) k -= cnt[t * chunks + c2];

@@ -72,6 +72,16 @@ struct GenParams {
     int recurrent;        // 1: random pool (targets in [0,n)), 0: layered
     int layers;           // layered: number of layers (<= 16)
     uint64_t off[17];     // layered: prefix offsets of the layers
+    // Feed-forward (snn_build_feedforward, src/snn.c:463-521): per layer, the
+    // edges of each row (0 for the last layer), the first edge of the layer,
+    // and the first splitmix64 draw of its edges (~0: a dense layer, which
+    // draws nothing); every weight is wconst. fanout then holds the largest
+    // per-row edge count (an upper bound for grid sizing).
+    int feedforward;
+    float wconst;
+    uint64_t lfan[16];
+    uint64_t ledge[17];
+    uint64_t ldraw[16];
 };
 
 // Geometry and buffers of the binned push propagation (b200_binned.cu).

@@ -1881,6 +1881,57 @@ snn_status_t snn_b200_create_layered_random(const snn_size_t *layer_sizes, size_
     return finish_generated(c, g, rows * fanout, out_context);
 }
 
+// Device build of snn_build_feedforward (src/snn.c:463-521), bit-identical:
+// per layer, dense (fanout 0 or >= the next layer: every target in order,
+// no draws) or fanout targets drawn from one splitmix64 stream seeded with
+// `seed` and consumed in edge order across the sparse layers; every weight
+// `weight`. Validation as src/snn.c:184-215 plus isfinite(weight).
+snn_status_t snn_b200_create_feedforward(const snn_size_t *layer_sizes, size_t layer_count, snn_size_t fanout,
+                                         float weight, uint64_t seed, const snn_lif_params_t *lif,
+                                         const snn_b200_options_t *options, snn_cuda_context_t **out_context) {
+    if (out_context == nullptr) return SNN_ERR_INVALID_ARGUMENT;
+    *out_context = nullptr;
+    if (layer_sizes == nullptr || layer_count < 2 || layer_count > 16 || !std::isfinite(weight))
+        return SNN_ERR_INVALID_ARGUMENT;
+    const snn_lif_params_t p = lif ? *lif : snn_lif_params_t{1.0f, 20.0f, 0.0f, 0.0f, 1.0f, 1.0f, 1u};
+    if (!lif_valid(&p)) return SNN_ERR_INVALID_ARGUMENT;
+    b200::GenParams g{};
+    g.off[0] = 0;
+    for (size_t l = 0; l < layer_count; ++l) {
+        if (layer_sizes[l] == 0) return SNN_ERR_INVALID_ARGUMENT;
+        if (g.off[l] > UINT64_MAX - layer_sizes[l]) return SNN_ERR_OVERFLOW;
+        g.off[l + 1] = g.off[l] + layer_sizes[l];
+    }
+    g.n = g.off[layer_count];
+    g.seed = seed;
+    g.wconst = weight;
+    g.recurrent = 0;
+    g.feedforward = 1;
+    g.layers = (int)layer_count;
+    uint64_t edges = 0, draws = 0, widest = 1;
+    for (size_t l = 0; l + 1 < layer_count; ++l) {
+        const uint64_t pre = layer_sizes[l], post = layer_sizes[l + 1];
+        const bool dense = fanout == 0 || fanout >= post;
+        const uint64_t f = dense ? post : fanout;
+        if (f != 0 && pre > UINT64_MAX / f) return SNN_ERR_OVERFLOW;
+        const uint64_t le = pre * f;
+        if (edges > UINT64_MAX - le) return SNN_ERR_OVERFLOW;
+        g.lfan[l] = f;
+        g.ledge[l] = edges;
+        g.ldraw[l] = dense ? ~0ull : draws;
+        if (!dense) draws += le;
+        edges += le;
+        widest = std::max(widest, f);
+    }
+    g.ledge[layer_count - 1] = edges;
+    g.fanout = widest;
+    snn_cuda_context_t *c = nullptr;
+    CreateEnv env;
+    snn_status_t st = begin_create(g.n, p, expf(-p.dt_ms / p.membrane_tau_ms), nullptr, options, &c, &env);
+    if (st != SNN_OK) return st;
+    return finish_generated(c, g, edges, out_context);
+}
+
 const char *snn_b200_last_error(void) { return g_last_error; }
 
 snn_status_t snn_test_b200_peer_loopback(snn_cuda_context_t *c, uint32_t spin_limit) {
