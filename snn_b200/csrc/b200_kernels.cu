@@ -700,7 +700,8 @@ __global__ void __launch_bounds__(256) propagate_chunk_kernel(uint64_t row0, uin
                                                               const uint64_t *__restrict__ row_ptr,
                                                               const uint64_t *__restrict__ col,
                                                               const float *__restrict__ w, float *__restrict__ next,
-                                                              DevCounters *ctr, int parity, int first_chunk) {
+                                                              DevCounters *ctr, int parity, int first_chunk,
+                                                              int count_spikes) {
     const unsigned lane = lane_id();
     const uint64_t gwarp = ((uint64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const uint64_t nwarps = ((uint64_t)gridDim.x * blockDim.x) >> 5;
@@ -726,7 +727,7 @@ __global__ void __launch_bounds__(256) propagate_chunk_kernel(uint64_t row0, uin
     block_add_u64(lane == 0 ? events : 0ull, &ctr->events);
     if (first_chunk) {
         const uint32_t count = *(volatile uint32_t *)&ctr->list_count[parity];
-        step_epilogue(ctr, parity, 1, count);
+        step_epilogue(ctr, parity, count_spikes, count);
     }
 }
 
@@ -1204,10 +1205,10 @@ void launch_fill_u2(cudaStream_t s, int device, uint2 *p, uint64_t n, uint32_t x
 
 void launch_propagate_chunk(cudaStream_t s, int device, uint64_t row0, uint64_t rows, uint64_t edge_base,
                             const uint32_t *bitmap, const uint64_t *row_ptr, const uint64_t *col, const float *w,
-                            float *next, DevCounters *ctr, int parity, int first_chunk) {
+                            float *next, DevCounters *ctr, int parity, int first_chunk, int count_spikes) {
     const int grid = grid_for(device, 8, rows, 256);
     propagate_chunk_kernel<<<grid, 256, 0, s>>>(row0, rows, edge_base, bitmap, row_ptr, col, w, next, ctr, parity,
-                                                first_chunk);
+                                                first_chunk, count_spikes);
 }
 
 void launch_step_epilogue(cudaStream_t s, DevCounters *ctr, int parity, int count_spikes) {

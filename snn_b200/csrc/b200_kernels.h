@@ -172,7 +172,7 @@ void launch_set_u64(cudaStream_t s, unsigned long long *p, unsigned long long v)
 // at edge_base; col holds 64-bit global target ids.
 void launch_propagate_chunk(cudaStream_t s, int device, uint64_t row0, uint64_t rows, uint64_t edge_base,
                             const uint32_t *bitmap, const uint64_t *row_ptr, const uint64_t *col, const float *w,
-                            float *next, DevCounters *ctr, int parity, int first_chunk);
+                            float *next, DevCounters *ctr, int parity, int first_chunk, int count_spikes = 1);
 
 // Step epilogue for STREAMING contexts with no chunk (never happens) or for
 // steps without a propagation launch: zeroes the next list slot, adds stats.

@@ -160,6 +160,11 @@ struct snn_cuda_context {
     unsigned long long *h_ototal = nullptr;
 
     std::vector<StreamChunk> chunks;
+    // Sharded STREAMING: the rank's slice of the host CSR (local target ids),
+    // viewed as a network by the streaming code.
+    snn_network_t slice_net{};
+    uint64_t *h_slice_rp = nullptr, *h_slice_col = nullptr;
+    float *h_slice_w = nullptr;
     uint64_t slot_rows = 0, slot_edges = 0, slot_stride = 0;
     uint64_t *d_chunk_row = nullptr;
     uint64_t *d_chunk_col = nullptr;
@@ -284,6 +289,9 @@ void free_context(snn_cuda_context_t *c) {
     if (c->h_inj_val) cudaFreeHost(c->h_inj_val);
     for (const void *p : c->registered)
         if (p) cudaHostUnregister(const_cast<void *>(p));
+    std::free(c->h_slice_rp);
+    std::free(c->h_slice_col);
+    std::free(c->h_slice_w);
     for (int i = 0; i < 2; ++i) {
         if (c->ev_copied[i]) cudaEventDestroy(c->ev_copied[i]);
         if (c->ev_free[i]) cudaEventDestroy(c->ev_free[i]);
@@ -831,6 +839,41 @@ uint64_t max_degree(const snn_network_t *net) {
     return m;
 }
 
+// Sharded STREAMING: copies the edges into [lo, hi) to host buffers (every
+// row kept, CSR order, targets relative to lo) that the streaming code reads
+// in place of the borrowed network.
+snn_status_t make_stream_slice(snn_cuda_context_t *c, const snn_network_t *net) {
+    const uint64_t n = net->neuron_count;
+    uint64_t e = 0;
+    for (uint64_t q = 0; q < net->synapse_count; ++q) e += (net->col_idx[q] >= c->lo && net->col_idx[q] < c->hi);
+    auto alloc = [](uint64_t bytes) { return std::aligned_alloc(64, (bytes + 63) / 64 * 64 + 64); };
+    c->h_slice_rp = (uint64_t *)alloc((n + 1) * 8);
+    c->h_slice_col = (uint64_t *)alloc(e * 8);
+    c->h_slice_w = (float *)alloc(e * 4);
+    if (!c->h_slice_rp || !c->h_slice_col || !c->h_slice_w) return SNN_ERR_OUT_OF_MEMORY;
+    uint64_t pos = 0;
+    for (uint64_t i = 0; i < n; ++i) {
+        c->h_slice_rp[i] = pos;
+        for (uint64_t q = net->row_ptr[i]; q < net->row_ptr[i + 1]; ++q) {
+            const uint64_t t = net->col_idx[q];
+            if (t >= c->lo && t < c->hi) {
+                c->h_slice_col[pos] = t - c->lo;
+                c->h_slice_w[pos] = net->weights[q];
+                ++pos;
+            }
+        }
+    }
+    c->h_slice_rp[n] = pos;
+    c->slice_net = *net;
+    c->slice_net.synapse_count = e;
+    c->slice_net.row_ptr = c->h_slice_rp;
+    c->slice_net.col_idx = c->h_slice_col;
+    c->slice_net.weights = c->h_slice_w;
+    c->network = &c->slice_net;
+    c->e_local = e;
+    return SNN_OK;
+}
+
 // STREAMING: chunk sizing follows the reference's rules
 // (src/snn_cuda.cu:327-401): rows <= 65536 and <= n; auto rows take at most
 // half of the budget left after the resident state; an explicit synapse cap
@@ -1151,7 +1194,7 @@ snn_status_t enqueue_step(snn_cuda_context_t *c, bool has_ext) {
     } else if (c->streaming == SNN_B200_STREAMING_SPARSE) {
         // Sparse STREAMING: spiking rows read straight from mapped host memory.
         b200::launch_propagate_push(c->stream, c->device, c->d_list, c->idx_bits, c->d_row_ptr, c->h_col_dev, 64,
-                                    c->h_w_dev, next, c->d_ctr, parity, 1);
+                                    c->h_w_dev, next, c->d_ctr, parity, !sharded);
         if ((st = check_launch(c)) != SNN_OK) return st;
     } else {
         // STREAMING: chunk i uses copy slot i&1; its copies wait until the
@@ -1181,8 +1224,9 @@ snn_status_t enqueue_step(snn_cuda_context_t *c, bool has_ext) {
             }
             cudaEventRecord(c->ev_copied[s], c->copy_stream);
             cudaStreamWaitEvent(c->stream, c->ev_copied[s], 0);
-            b200::launch_propagate_chunk(c->stream, c->device, ch.row_begin, ch.rows, ch.edge_begin, c->d_bitmap,
-                                         drow, dcol, dw, next, c->d_ctr, parity, i == 0);
+            b200::launch_propagate_chunk(c->stream, c->device, ch.row_begin, ch.rows, ch.edge_begin,
+                                         peer ? xbitmap : c->d_bitmap, drow, dcol, dw, next, c->d_ctr, parity,
+                                         i == 0, !sharded);
             if ((st = check_launch(c)) != SNN_OK) return st;
             cudaEventRecord(c->ev_free[s], c->stream);
         }
@@ -1657,14 +1701,14 @@ snn_status_t snn_b200_create(const snn_network_t *network, const snn_cuda_config
     if (network == nullptr) return SNN_ERR_INVALID_ARGUMENT;
     const snn_cuda_config_t cfg = config ? *config : snn_cuda_default_config();
     const snn_b200_options_t o = options ? *options : snn_b200_default_options();
-    if ((o.world_size > 1 || o.propagation == SNN_B200_PROPAGATE_ORDERED || o.batch > 1) && cfg.prefer_streaming)
+    if ((o.propagation == SNN_B200_PROPAGATE_ORDERED || o.batch > 1) && cfg.prefer_streaming)
         return SNN_ERR_UNSUPPORTED;
     snn_cuda_context_t *c = nullptr;
     CreateEnv env;
     snn_status_t st = begin_create(network->neuron_count, network->lif, network->decay, &cfg, &o, &c, &env);
     if (st != SNN_OK) return st;
     c->network = network;
-    const bool full_only = c->world > 1 || c->propagation == SNN_B200_PROPAGATE_ORDERED || c->batch > 1;
+    const bool full_only = c->propagation == SNN_B200_PROPAGATE_ORDERED || c->batch > 1;
     if (full_only || (!cfg.prefer_streaming && full_push_bytes(c, network->synapse_count) <= env.budget)) {
         c->mode = SNN_CUDA_MODE_FULL;
         if (c->propagation != SNN_B200_PROPAGATE_ORDERED) {
@@ -1679,8 +1723,11 @@ snn_status_t snn_b200_create(const snn_network_t *network, const snn_cuda_config
     } else {
         c->mode = SNN_CUDA_MODE_STREAMING;
         c->e_local = network->synapse_count;
+        // A shard streams only the edges into its own neurons: a host copy of
+        // them, with local target ids, stands in for the network.
+        if (c->world > 1) st = make_stream_slice(c, network);
         bool fallback = true;
-        if (c->streaming == SNN_B200_STREAMING_SPARSE) st = allocate_sparse_streaming(c, &fallback);
+        if (st == SNN_OK && c->streaming == SNN_B200_STREAMING_SPARSE) st = allocate_sparse_streaming(c, &fallback);
         if (st == SNN_OK && fallback) {
             c->streaming = SNN_B200_STREAMING_CHUNKED;
             st = allocate_streaming(c, cfg, env.budget);

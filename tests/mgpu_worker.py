@@ -31,8 +31,9 @@ def main():
     dist.init_process_group("gloo")
     keep = []
 
-    def options(prop, exchange=sb.EXCHANGE_NCCL):
-        o = sb.default_options(device=local, rank=rank, world_size=world, propagation=prop, exchange=exchange)
+    def options(prop, exchange=sb.EXCHANGE_NCCL, streaming=sb.STREAMING_CHUNKED):
+        o = sb.default_options(device=local, rank=rank, world_size=world, propagation=prop, exchange=exchange,
+                               streaming=streaming)
         if exchange == sb.EXCHANGE_NCCL:
             # A fresh NCCL unique id per context (one communicator each).
             obj = [sb.nccl_unique_id() if rank == 0 else None]
@@ -116,11 +117,11 @@ def main():
     if rank == 0:
         hrp, hci, hw = net.row_ptr(), net.col_idx(), net.weights()
         for lo, cnt, rp, ci, w in parts:
-            keep = (hci >= lo) & (hci < lo + cnt)
-            deg = np.add.reduceat(keep.astype(np.int64), hrp[:-1].astype(np.int64)) if hci.size else None
+            mask = (hci >= lo) & (hci < lo + cnt)
+            deg = np.add.reduceat(mask.astype(np.int64), hrp[:-1].astype(np.int64)) if hci.size else None
             exp_rp = np.concatenate([[0], np.cumsum(deg)]).astype(np.uint64)
-            if not (np.array_equal(rp, exp_rp) and np.array_equal(ci, hci[keep]) and
-                    np.array_equal(w.view(np.uint32), hw[keep].view(np.uint32))):
+            if not (np.array_equal(rp, exp_rp) and np.array_equal(ci, hci[mask]) and
+                    np.array_equal(w.view(np.uint32), hw[mask].view(np.uint32))):
                 failures.append(f"device shard {lo} topology mismatch")
     ctx.free()
     # Dense steps on sharded contexts: the gated pull (PUSH, one dyadic weight so
@@ -155,6 +156,36 @@ def main():
                 failures.append(f"dense sharded {prop} differs from the CPU step")
             if not (0 < int((ras.sum(axis=1) > dn // 4).sum()) < 9):
                 failures.append("dense sharded case lacks a mix of sparse and dense steps")
+        ctx.free()
+    # Sharded STREAMING: each rank streams only the edges into its neurons
+    # (chunked copies, or sparse reads of its mapped slice). One dyadic
+    # weight: exact against the CPU step.
+    snet = orc.random_pool(20011, 48, 0.046875, 0.046875, 4242, lif=default_lif(refractory_steps=2))
+    for smode, exchange in ((sb.STREAMING_CHUNKED, sb.EXCHANGE_PEER), (sb.STREAMING_SPARSE, sb.EXCHANGE_NCCL)):
+        cfg = sb.default_config(prefer_streaming=1, max_stream_rows=700)
+        ctx = sb.CudaContext.create(snet, cfg, options(sb.PROPAGATE_PUSH, exchange, smode))
+        connect(ctx, exchange)
+        if ctx.mode != sb.MODE_STREAMING:
+            failures.append(f"rank {rank}: sharded context is not STREAMING")
+        lo, cnt = ctx.local_begin, ctx.local_count
+        rng = np.random.default_rng(11)
+        frames = [(rng.random(20011) < 0.08).astype(np.float32) * np.float32(1.5) for _ in range(8)]
+        raster = np.zeros((8, cnt), np.uint8)
+        for t in range(8):
+            raster[t] = ctx.step(frames[t][lo:lo + cnt])
+        stats = ctx.stats()
+        parts = [None] * world
+        dist.all_gather_object(parts, (lo, raster, ctx.download_voltage(), stats["events"], stats["spikes"]))
+        if rank == 0:
+            st = State(snet)
+            ras = np.array([st.step(frames[t]) for t in range(8)])
+            parts.sort(key=lambda p: p[0])
+            g_r = np.concatenate([p[1] for p in parts], axis=1)
+            g_v = np.concatenate([p[2] for p in parts])
+            if not (np.array_equal(g_r, ras) and np.array_equal(g_v.view(np.uint32), st.voltage().view(np.uint32))):
+                failures.append(f"sharded streaming {smode} differs from the CPU step")
+            if sum(p[3] for p in parts) != int(ras.sum()) * 48 or sum(p[4] for p in parts) != int(ras.sum()):
+                failures.append(f"sharded streaming {smode} stats differ")
         ctx.free()
     dist.barrier()
     if rank == 0:
