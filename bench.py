@@ -65,9 +65,12 @@ def parse():
     ap.add_argument("--stream-mode", choices=["chunked", "sparse"], default="sparse")
     ap.add_argument("--stream-budget-frac", type=float, default=0.25,
                     help="VRAM budget as a fraction of the host CSR bytes (config 3 streams ~15x its budget)")
-    ap.add_argument("--workload", choices=["config2", "config1"], default="config2",
+    ap.add_argument("--workload", choices=["config2", "config1", "config4"], default="config2",
                     help="config1: BASELINE config 1 (784-1000-10 dense, 25 steps per static frame) run as "
-                         "--batch samples at once over one shared topology")
+                         "--batch samples at once over one shared topology; config4: 8 layers x "
+                         "--layer-size, fanout 500 to the next layer, w ~ U[0,1], 5%% of layer 0 injected "
+                         "with 30.0 per step")
+    ap.add_argument("--layer-size", type=int, default=1_000_000, help="config4: neurons per layer")
     ap.add_argument("--batch", type=int, default=2000, help="config1: samples per batched context")
     ap.add_argument("--propagation", choices=["auto", "binned", "atomic", "ordered"], default="auto",
                     help="push kernel: auto (library default), binned (shared-memory tiles), atomic (L2 red); "
@@ -201,6 +204,16 @@ def reference_arm(args):
 
 
 def workload_config(args, world):
+    if args.workload == "config4":
+        ls = args.layer_size
+        return {"workload": "config4_layered", "layers": [ls] * 8, "fanout": 500, "synapses": 7 * ls * 500,
+                "weights": "U[0,1] mV", "seed": args.seed,
+                "inject": f"5% of layer 0 ({int(round(0.05 * ls))}) x 30 per step",
+                "lif": "dt 1 ms, tau 20 ms, rest=reset -65 mV, thr -50 mV, refractory 2", "policy": "FULL",
+                "propagation": "ordered (bit-exact push)" if args.propagation == "ordered"
+                else f"push ({args.propagation})",
+                "parallelism": f"postsynaptic shards x{world}" + (f", {args.exchange} spike exchange" if world > 1 else ""),
+                "l2": L2_NOTE}
     return {"workload": "config2_resident_random_pool", "neurons": args.neurons, "fanout": args.fanout,
             "synapses": args.neurons * args.fanout, "weights": "U[-0.2,0.5] mV", "seed": args.seed,
             "inject": f"{args.inject_frac * 100:g}% of neurons x {args.inject_value:g} per step",
@@ -456,10 +469,22 @@ def run_b200(args):
         id_buf = ctypes.create_string_buffer(nccl_id, 128)
         opts.nccl_id = ctypes.cast(id_buf, ctypes.c_void_p)
     lif = sb.LifParams(1.0, 20.0, -65.0, -65.0, -50.0, 1.0, 2)
-    n, f = args.neurons, args.fanout
-    count = max(1, int(round(args.inject_frac * n)))
     t0 = time.time()
-    ctx = sb.CudaContext.random_pool(n, f, -0.2, 0.5, args.seed, lif=lif, options=opts)
+    if args.workload == "config4":
+        # 8 layers, fanout 500 to the next layer, w ~ U[0, 1]; the seeded
+        # injection stream restricted to layer 0 (5% of it, 30.0 each).
+        layers = [args.layer_size] * 8
+        n, f = sum(layers), 500
+        inj_range = args.layer_size
+        count = max(1, int(round(0.05 * inj_range)))
+        args.inject_value = 30.0
+        ctx = sb.CudaContext.layered_random(layers, f, 0.0, 1.0, args.seed, lif=lif, options=opts)
+        ctx.set_stream_range(inj_range)
+    else:
+        n, f = args.neurons, args.fanout
+        inj_range = n
+        count = max(1, int(round(args.inject_frac * n)))
+        ctx = sb.CudaContext.random_pool(n, f, -0.2, 0.5, args.seed, lif=lif, options=opts)
     gen_s = time.time() - t0
     if world > 1 and args.exchange == "peer":
         handles = [None] * world
@@ -542,7 +567,7 @@ def run_b200(args):
     e2e = None
     if not args.no_e2e:
         pinned_idx = torch.empty((args.steps, count), dtype=torch.int64).pin_memory()
-        from_stream = _stream_indices(args.seed, args.warmup + args.steps, args.steps, count, n)
+        from_stream = _stream_indices(args.seed, args.warmup + args.steps, args.steps, count, inj_range)
         pinned_idx.numpy()[:] = from_stream.view(np.int64)
         pinned_val = torch.full((count,), args.inject_value, dtype=torch.float32).pin_memory()
         spikes_out = torch.empty((ctx.local_count,), dtype=torch.uint8).pin_memory()
@@ -565,7 +590,9 @@ def run_b200(args):
                "api": "snn_cuda_inject_current + snn_cuda_step (host buffers, synchronous)"}
 
     cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+    if rank == 0 and world == 1 and not args.no_cpu_baseline and args.workload == "config4":
+        cpu = {"value": None, "unavailable": "no CPU sample for config 4 (the CPU baseline is measured on config 2)"}
+    elif rank == 0 and world == 1 and not args.no_cpu_baseline:
         try:
             r = cpu_sample(args, seconds=args.cpu_seconds)
             cpu = {k: r[k] for k in ("value", "unit", "cores", "kind", "sample")}

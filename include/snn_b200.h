@@ -310,6 +310,11 @@ snn_status_t snn_b200_run_stream_async(snn_cuda_context_t *context, uint64_t see
 /* One step without host input or output and without a final synchronisation. */
 snn_status_t snn_b200_step_async(snn_cuda_context_t *context);
 
+/* Restricts the seeded injection stream's indices to [0, range) (mix64(...)
+ * % range instead of % n; range 0 restores all neurons), e.g. to drive only
+ * the input layer of a layered network. */
+snn_status_t snn_b200_set_stream_range(snn_cuda_context_t *context, snn_size_t range);
+
 /* Holds an external current frame on the device (local-count floats, scaled
  * by input_scale like snn_cuda_step's): every later step that does not pass
  * its own external current adds it (snn_cuda_step with NULL, step_async,

@@ -134,6 +134,7 @@ ENTRY_POINTS = [
     ("snn_b200_run_stream_async", C.c_int, [P, u64, u64, u64, u64, f32]),
     ("snn_b200_step_async", C.c_int, [P]),
     ("snn_b200_set_external", C.c_int, [P, P]),
+    ("snn_b200_set_stream_range", C.c_int, [P, u64]),
     ("snn_b200_synchronize", C.c_int, [P]),
     ("snn_b200_get_stats", C.c_int, [P, P]),
     ("snn_b200_reset_stats", C.c_int, [P]),
@@ -349,6 +350,10 @@ class CudaContext:
 
     def step_async(self):
         _check(lib().snn_b200_step_async(self.handle), "snn_b200_step_async")
+
+    def set_stream_range(self, n: int):
+        """Injection-stream indices in [0, n) (0: all neurons)."""
+        _check(lib().snn_b200_set_stream_range(self.handle, n), "snn_b200_set_stream_range")
 
     def set_external(self, external):
         """Holds an external frame on the device for every later step without its own (None clears)."""

@@ -104,12 +104,13 @@ struct snn_cuda_context {
     int cur = 0;
     float *d_ext = nullptr;
     bool ext_held = false;  // snn_b200_set_external: d_ext applies to every step without its own
+    uint64_t inject_range = 0;  // snn_b200_set_stream_range: stream indices drawn in [0, range); 0 = all
     // run_stream_async on unsharded push contexts replays a captured CUDA
     // graph of two steps (one per parity); the injection step index then
     // lives on the device (DevCounters::stream_step, advanced by LIF).
     bool dev_stream_step = false;
     cudaGraphExec_t graph = nullptr;
-    uint64_t graph_seed = 0, graph_count = 0, graph_launches = 0;
+    uint64_t graph_seed = 0, graph_count = 0, graph_launches = 0, graph_range = 0;
     float graph_value = 0.0f;
     bool graph_ext = false;
     uint32_t *d_refr = nullptr;
@@ -1584,6 +1585,8 @@ snn_status_t finish_generated(snn_cuda_context_t *c, const b200::GenParams &g, u
     return SNN_OK;
 }
 
+uint64_t stream_range(const snn_cuda_context_t *c) { return c->inject_range ? c->inject_range : c->n_global; }
+
 // Launch-bound loops (small networks, quiet steps) pay a launch gap per
 // kernel; unsharded push contexts without device timing replay a captured
 // graph of two steps instead. SNN_B200_NO_GRAPHS (environment) disables it.
@@ -1595,7 +1598,7 @@ bool graph_eligible(const snn_cuda_context_t *c) {
 // One step of the injection stream with the step index read on the device.
 snn_status_t stream_step_dev(snn_cuda_context_t *c, uint64_t seed, snn_size_t count, float value) {
     if (count) {
-        b200::launch_inject_stream(c->stream, c->device, seed, 0, count, c->n_global, value * c->lif.input_scale,
+        b200::launch_inject_stream(c->stream, c->device, seed, 0, count, stream_range(c), value * c->lif.input_scale,
                                    c->d_cur[c->cur], c->lo, c->hi, &c->d_ctr->stream_step);
         c->launches++;
     }
@@ -1615,7 +1618,8 @@ snn_status_t run_stream_graph(snn_cuda_context_t *c, uint64_t seed, uint64_t fir
         ++t;
     }
     if (st == SNN_OK && (c->graph == nullptr || c->graph_seed != seed || c->graph_count != count ||
-                         c->graph_value != value || c->graph_ext != c->ext_held)) {
+                         c->graph_value != value || c->graph_ext != c->ext_held ||
+                         c->graph_range != stream_range(c))) {
         if (c->graph) cudaGraphExecDestroy(c->graph);
         c->graph = nullptr;
         const uint64_t step0 = c->step, launches0 = c->launches;
@@ -1631,6 +1635,7 @@ snn_status_t run_stream_graph(snn_cuda_context_t *c, uint64_t seed, uint64_t fir
                 c->graph_count = count;
                 c->graph_value = value;
                 c->graph_ext = c->ext_held;
+                c->graph_range = stream_range(c);
                 c->graph_launches = c->launches - launches0;
             } else {
                 c->graph = nullptr;
@@ -2066,7 +2071,7 @@ snn_status_t snn_b200_inject_stream_async(snn_cuda_context_t *c, uint64_t seed, 
     snn_status_t st = set_device(c);
     if (st != SNN_OK) return st;
     // Uniform value: the atomic scatter is order-exact (see inject_current).
-    b200::launch_inject_stream(c->stream, c->device, seed, step, count, c->n_global,
+    b200::launch_inject_stream(c->stream, c->device, seed, step, count, stream_range(c),
                                value * c->lif.input_scale, c->d_cur[c->cur], c->lo, c->hi);
     c->launches++;
     return cuda_status(cudaGetLastError());
@@ -2077,6 +2082,12 @@ snn_status_t snn_b200_step_async(snn_cuda_context_t *c) {
     snn_status_t st = set_device(c);
     if (st != SNN_OK) return st;
     return enqueue_step(c, c->ext_held);
+}
+
+snn_status_t snn_b200_set_stream_range(snn_cuda_context_t *c, snn_size_t range) {
+    if (c == nullptr || range > c->n_global) return SNN_ERR_INVALID_ARGUMENT;
+    c->inject_range = range;
+    return SNN_OK;
 }
 
 snn_status_t snn_b200_set_external(snn_cuda_context_t *c, const float *host_external_current) {
@@ -2104,7 +2115,7 @@ snn_status_t snn_b200_run_stream_async(snn_cuda_context_t *c, uint64_t seed, uin
     if (graph_eligible(c) && steps >= 8) return run_stream_graph(c, seed, first_step, steps, count, value);
     for (uint64_t t = 0; t < steps; ++t) {
         if (count) {
-            b200::launch_inject_stream(c->stream, c->device, seed, first_step + t, count, c->n_global,
+            b200::launch_inject_stream(c->stream, c->device, seed, first_step + t, count, stream_range(c),
                                        value * c->lif.input_scale, c->d_cur[c->cur], c->lo, c->hi);
             c->launches++;
         }

@@ -686,3 +686,28 @@ def test_device_feedforward_steps_exact(mode, monkeypatch):
     assert first_divergence(cr, gr) is None
     assert cr[:, 2700:].sum() > 0  # activity reaches the last layers
     np.testing.assert_array_equal(bits(cv), bits(gv))
+
+
+@pytest.mark.parametrize("prop", [sb.PROPAGATE_ORDERED, sb.PROPAGATE_PUSH])
+def test_stream_range_drives_input_layer(prop):
+    """snn_b200_set_stream_range: the seeded injection stream drawn in
+    [0, range) drives only the first layer of a layered network (BASELINE
+    config 4 scaled). ORDERED with general weights, or PUSH (the two-step
+    graph replay) with one dyadic weight: equal to host injection of the same
+    indices into the CPU step, bit for bit."""
+    lif = baseline_lif()
+    layers, f = [2000, 2000, 2000, 2000], 100
+    w = (0.0, 1.0) if prop == sb.PROPAGATE_ORDERED else (0.5, 0.5)
+    net = ORC.layered_random(layers, f, *w, 4, lif=lif)
+    ctx = sb.CudaContext.layered_random(layers, f, *w, 4, lif=lif_to_sb(lif), options=opts(propagation=prop))
+    ctx.set_stream_range(2000)
+    st = State(net)
+    for t in range(24):
+        assert st.inject(stream_indices_np(6, t, 100, 2000), np.full(100, 30.0, np.float32)) == 0
+        st.step()
+    ctx.run_stream_async(6, 0, 24, 100, 30.0)
+    ctx.synchronize()
+    np.testing.assert_array_equal(bits(st.voltage()), bits(ctx.download_voltage()))
+    assert ctx.stats()["spikes"] > 0
+    with pytest.raises(sb.SnnError):
+        ctx.set_stream_range(8001)
