@@ -56,6 +56,9 @@ def parse():
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-parity", action="store_true", help="skip the ORDERED raster-hash check")
+    ap.add_argument("--parity-neurons", type=int, default=200_000)
+    ap.add_argument("--parity-steps", type=int, default=40)
     ap.add_argument("--exchange", choices=["nccl", "peer"], default="peer",
                     help="N>1: spike exchange by ncclAllGather or fused into the LIF kernel over NVLink")
     ap.add_argument("--policy", choices=["full", "streaming"], default="full",
@@ -143,17 +146,55 @@ NCU_PULL_BYTES_PER_SLOT = 8.0
 
 
 # ------------------------------------------------------------ CPU side ----
-def cpu_sample(args, kind_pref=("ref_omp", "port"), steps=None, warmup=None, seconds=None):
-    """Times the reference CPU step (OpenMP build when present) on a bounded
-    sample: the same pool scaled to --cpu-neurons neurons."""
+def host_threads() -> int:
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+def pin_cpu_threads():
+    """Give the reference's OpenMP step every host core, whatever a launcher
+    (torchrun sets OMP_NUM_THREADS=1) left in the environment. Must run before
+    the OpenMP runtime is loaded."""
+    os.environ["OMP_NUM_THREADS"] = str(host_threads())
+
+
+def omp_threads() -> int:
+    """Threads the loaded OpenMP runtime will use."""
+    import ctypes
+    try:
+        return int(ctypes.CDLL("libgomp.so.1").omp_get_max_threads())
+    except OSError:
+        return 1
+
+
+def full_pool_fits(n, fanout) -> bool:
+    """Whether the host can hold the full pool (12 B/edge + 8 B/row) with the
+    reference's per-thread partial buffers and a margin."""
+    try:
+        import psutil
+        avail = psutil.virtual_memory().available
+    except Exception:
+        return False
+    need = 12 * n * fanout + 8 * (n + 1) + 4 * n * (host_threads() + 8)
+    return need < 0.85 * avail
+
+
+def cpu_sample(args, kind_pref=("ref_omp", "port"), steps=None, warmup=None, seconds=None, neurons=None):
+    """Times the reference CPU step (OpenMP build when present) on the pool of
+    `neurons` neurons (default --cpu-neurons, a bounded sample of the same
+    pool). The network is built by the oracle's multi-threaded builder,
+    bit-identical to the reference's snn_build_random_pool, and stepped by
+    the reference's own library."""
     import numpy as np
 
     from oracle.oracle import Oracle, State, baseline_lif, ref_available, stream_indices_np
     kind = next(k for k in kind_pref if k == "port" or ref_available(k))
     orc = Oracle(kind)
-    n = args.cpu_neurons
-    net = orc.random_pool(n, args.fanout, -0.2, 0.5, args.seed, lif=baseline_lif())
-    st = State(net)
+    n = neurons or args.cpu_neurons
+    net = Oracle("port").random_pool_parallel(n, args.fanout, -0.2, 0.5, args.seed, lif=baseline_lif())
+    st = State(net, lib=orc)
     rp = net.row_ptr()
     deg = (rp[1:] - rp[:-1]).astype(np.int64)
     count = max(1, int(round(args.inject_frac * n)))
@@ -176,12 +217,13 @@ def cpu_sample(args, kind_pref=("ref_omp", "port"), steps=None, warmup=None, sec
         elapsed += time.perf_counter() - t0
         events += int(deg[s.astype(bool)].sum())
         done += 1
-    threads = int(os.environ.get("OMP_NUM_THREADS", os.cpu_count() or 1)) if kind == "ref_omp" else 1
+    threads = omp_threads() if kind == "ref_omp" else 1
+    scope = "the full pool" if n == args.neurons else f"the same pool scaled to {n} neurons"
     return {"value": events / elapsed if elapsed > 0 else 0.0, "unit": "events/s", "cores": threads,
             "kind": "reference" if kind.startswith("ref") else "port",
-            "sample": f"same pool scaled to {n} neurons x fanout {args.fanout}, {done} steps after {warm} warm-up "
-                      f"steps, {kind} build ({'OpenMP' if kind == 'ref_omp' else 'serial'})",
-            "steps": done, "seconds": elapsed}
+            "sample": f"{scope} x fanout {args.fanout}, {done} steps after {warm} warm-up steps, reference "
+                      f"src/snn.c snn_step_cpu ({'OpenMP, ' + str(threads) + ' threads' if kind == 'ref_omp' else 'serial'})",
+            "steps": done, "seconds": elapsed, "neurons": n}
 
 
 def reference_arm(args):
@@ -191,8 +233,19 @@ def reference_arm(args):
     if not os.path.exists(os.path.join(ROOT, "oracle", "liboracle.so")):
         print(json.dumps({"impl": "reference", "unavailable": "oracle/liboracle.so not built"}))
         return
+    if args.workload != "config2":
+        print(json.dumps({"impl": "reference", "unavailable": "the reference arm times config 2 only"}))
+        return
+    pin_cpu_threads()
     warm = max(args.warmup, 0)
-    r = cpu_sample(args, steps=args.steps, warmup=warm, seconds=None)
+    # The full pool when the host can hold it (the reference's own step on
+    # the same 10M x 1000 network the GPU arm runs); else the largest
+    # bounded sample, and the config says which.
+    full = full_pool_fits(args.neurons, args.fanout)
+    n = args.neurons if full else args.cpu_neurons
+    r = cpu_sample(args, steps=args.steps, warmup=warm, seconds=None, neurons=n)
+    if not full:
+        args.neurons = n
     cfg = workload_config(args, args.gpus)
     line = {"impl": "reference", "metric": "synaptic_events_per_sec", "value": r["value"], "unit": "events/s",
             "n_gpus": args.gpus, "steps": r["steps"], "warmup": warm,
@@ -512,12 +565,22 @@ def run_b200(args):
     # Warm-up (untimed) then exactly K timed steps.
     ctx.run_stream_async(args.seed, 0, args.warmup, count, args.inject_value)
     ctx.synchronize()
+    # The state at the start of the timed window, so that the e2e pass below
+    # replays the same steps from the same state.
+    v0, c0, r0 = ctx.download_state()
     ctx.reset_stats()
     stream = torch.cuda.ExternalStream(ctx.stream())
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    rendezvous = torch.zeros(1, dtype=torch.float32, device="cuda") if dist is not None else None
     barrier()
     torch.cuda.synchronize()
     with ClockSampler(local) as clk:
+        if rendezvous is not None:
+            # The ranks meet on the device right before the timed window (an
+            # all-reduce on the library's stream), so that the host launch
+            # skew between processes is not charged to the first exchange.
+            with torch.cuda.stream(stream):
+                dist.all_reduce(rendezvous)
         ev0.record(stream)
         ctx.run_stream_async(args.seed, args.warmup, args.steps, count, args.inject_value)
         ev1.record(stream)
@@ -530,44 +593,70 @@ def run_b200(args):
     events_total = sum_over_ranks(float(s["events"]))
     spikes_total = sum_over_ranks(float(s["spikes"]))
     value = events_total / (ms / 1e3)
-    # Roofline of the dominant kernel (push propagation) on this rank:
-    # algorithmic bytes = 12 per event (8 B col_idx + 4 B weight, the
-    # reference's CSR format) + 16 per spiking row (row_ptr pair).
+    # Roofline of the dominant kernels (propagation) on this rank: the
+    # algorithmic bytes are 12 per event (8 B col_idx + 4 B weight, the
+    # reference's CSR format) + 16 per spiking row (row_ptr pair). Push steps
+    # and pull steps (device-chosen) are reported apart and blended.
     peak, peak_kind = measured_peak_gbs()
-    # Stats count steps since creation; the timed region ran args.steps.
     timed = args.steps
-    prop_bytes = 12.0 * s["events"] + 16.0 * spikes_total
-    kernel_name = "propagate_push_kernel"
     lay = ctx.layout
+    # Every rank reads the row_ptr pair of every spiking row (the global list).
+    spikes_rows = spikes_total
+    prop_bytes = 12.0 * s["events"] + 16.0 * spikes_rows
+    kernel_name = "propagate_push_kernel"
     if args.propagation == "ordered":
-        # Ordered push: the same algorithmic bytes as the push (the spiking
-        # rows' CSR slices); its kernels (histogram, placement, segmented
-        # sort, fold) are timed together as the propagation.
-        kernel_name = "ordered push (hist + scatter + segmented sort + fold)"
+        kernel_name = "ordered propagation (bin-fold push; pull on dense steps)"
     gated = int(lay.get("ordered_csc", 0)) == 1 and args.propagation == "auto"
     if gated:
-        # A sliced-ELL CSC sits beside the CSR: steps where more than half the
-        # rows fire take propagate_pull_kernel (device-side gate), the rest
-        # propagate_push_kernel; both are timed as the propagation.
-        kernel_name = "propagate_push_kernel + propagate_pull_kernel (dense steps)"
+        kernel_name = "propagate_push_kernel (sparse steps) + propagate_pull_smem_kernel (dense steps)"
     prop_s = s["propagate_ms"] / 1e3
     achieved = prop_bytes / prop_s / 1e9 if prop_s > 0 else 0.0
+    pull_steps = int(s.get("pull_steps", 0))
+    pull_ms = s.get("propagate_pull_ms", 0.0)
+    push_ms = s["propagate_ms"] - pull_ms
+    push_events = s["events"] - s.get("pull_events", 0)
+    push_spikes = spikes_rows - s.get("pull_spikes", 0)
+    split = {"push_steps": timed - pull_steps, "pull_steps": pull_steps}
+    if push_ms > 0:
+        b = 12.0 * push_events + 16.0 * push_spikes
+        split["push"] = {"achieved": b / (push_ms / 1e3) / 1e9, "frac": b / (push_ms / 1e3) / 1e9 / peak,
+                         "ms_per_step": push_ms / max(1, timed - pull_steps),
+                         "events_per_s": push_events / (push_ms / 1e3)}
+    if pull_ms > 0:
+        b = 12.0 * s.get("pull_events", 0) + 16.0 * s.get("pull_spikes", 0)
+        slot_bytes = 8.0 * int(lay.get("pull_slots", 0)) * pull_steps
+        split["pull"] = {"achieved": b / (pull_ms / 1e3) / 1e9, "frac": b / (pull_ms / 1e3) / 1e9 / peak,
+                         "device_bytes_gbs": slot_bytes / (pull_ms / 1e3) / 1e9,
+                         "device_frac": slot_bytes / (pull_ms / 1e3) / 1e9 / peak,
+                         "ms_per_step": pull_ms / max(1, pull_steps)}
     traffic = None
     if args.propagation not in ("binned", "ordered") and int(lay["index_bits"]) == 32 and timed:
-        # ncu-measured DRAM bytes: the push kernel 8.68 B per event, the pull
-        # kernel 8 B per slot of its layout (profiles/); pull steps counted
-        # on the device.
-        push_events = s["events"] - s.get("pull_events", 0)
+        # DRAM bytes from one ncu capture per kernel: the push kernel moves
+        # 8.68 B per event (32-bit columns), the pull kernel 8 B per slot of
+        # its layout; scaled by this run's events and pull steps.
         traffic = (NCU_DRAM_BYTES_PER_EVENT * push_events
-                   + NCU_PULL_BYTES_PER_SLOT * int(lay.get("pull_slots", 0)) * s.get("pull_steps", 0)) / timed
+                   + NCU_PULL_BYTES_PER_SLOT * int(lay.get("pull_slots", 0)) * pull_steps) / timed
     step_bytes = (prop_bytes + 25.0 * ctx.local_count * timed
                   + 12.0 * count * timed)
     launches = int(s["kernel_launches"])
+    exchange = None
+    if world > 1:
+        waits = [max_over_ranks(s.get("exchange_wait_ms", 0.0) / timed),
+                 max_over_ranks(s.get("exchange_wait_max_ms", 0.0))]
+        exchange = {"kind": args.exchange, "ms_per_step": max_over_ranks(s["exchange_ms"] / timed),
+                    "flag_wait_ms_per_step_max_rank": waits[0] if args.exchange == "peer" else None,
+                    "longest_flag_wait_ms": waits[1] if args.exchange == "peer" else None,
+                    "lif_with_peer_stores_ms_per_step": max_over_ranks(s["lif_ms"] / timed),
+                    "propagate_ms_per_step_max_rank": max_over_ranks(s["propagate_ms"] / timed)}
 
     e2e = None
     if not args.no_e2e:
+        # The same K steps as the device window: the state saved at its start
+        # is restored, and the seeded stream's indices of those steps are fed
+        # from pinned host memory through the reference-facing entry points.
+        ctx.upload_state(v0, c0, r0)
         pinned_idx = torch.empty((args.steps, count), dtype=torch.int64).pin_memory()
-        from_stream = _stream_indices(args.seed, args.warmup + args.steps, args.steps, count, inj_range)
+        from_stream = _stream_indices(args.seed, args.warmup, args.steps, count, inj_range)
         pinned_idx.numpy()[:] = from_stream.view(np.int64)
         pinned_val = torch.full((count,), args.inject_value, dtype=torch.float32).pin_memory()
         spikes_out = torch.empty((ctx.local_count,), dtype=torch.uint8).pin_memory()
@@ -587,7 +676,22 @@ def run_b200(args):
         e2e_events = sum_over_ranks(float(s2["events"]))
         e2e = {"value": e2e_events / e2e_s, "unit": "events/s", "h2d_bytes_per_step": count * 12,
                "d2h_bytes_per_step": int(ctx.local_count), "ms_per_step": 1e3 * e2e_s / args.steps,
+               "events_per_step": e2e_events / args.steps, "device_events_per_step": events_total / args.steps,
+               "window": f"steps {args.warmup}..{args.warmup + args.steps - 1} from the saved state",
                "api": "snn_cuda_inject_current + snn_cuda_step (host buffers, synchronous)"}
+    ctx.free()
+
+    parity = None
+    if not args.no_parity:
+        pid_buf = None
+        if world > 1 and args.exchange == "nccl":
+            import ctypes
+            obj = [sb.nccl_unique_id() if rank == 0 else None]  # a fresh id: one per communicator
+            dist.broadcast_object_list(obj, src=0)
+            pid_buf = ctypes.create_string_buffer(obj[0], 128)
+        parity = raster_check(args, world, rank, local, dist, opts_base=dict(
+            device=local, world_size=world, rank=rank,
+            exchange=sb.EXCHANGE_PEER if args.exchange == "peer" else sb.EXCHANGE_NCCL), nccl_id_buf=pid_buf)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline and args.workload == "config4":
@@ -606,26 +710,106 @@ def run_b200(args):
             "scaling": "strong", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic: seeded random pool generated on device (bit-identical to snn_build_random_pool), "
                     "seeded injection stream",
-            "config": dict(workload_config(args, world), index_bits=int(lay["index_bits"])),
+            "config": workload_config(args, world),
+            "index_bits": int(lay["index_bits"]),
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": traffic, "peak_kind": peak_kind,
                          "kernel": kernel_name,
                          "algorithmic_bytes_per_launch": prop_bytes / timed,
-                         "kernel_ms_per_launch": s["propagate_ms"] / timed},
+                         "kernel_ms_per_launch": s["propagate_ms"] / timed,
+                         "by_step_kind": split},
             "step_roofline": {"achieved": step_bytes / (ms / 1e3) / 1e9 if world == 1 else None,
                               "frac": (step_bytes / (ms / 1e3) / 1e9) / peak if world == 1 else None,
                               "bytes_per_step": step_bytes / timed},
             "spike_rate": spikes_total / (args.steps * n), "events_per_step": events_total / args.steps,
             "kernel_ms": {"lif": s["lif_ms"] / args.steps, "exchange": s["exchange_ms"] / args.steps,
                           "propagate": s["propagate_ms"] / args.steps},
-            "pull_steps": int(s.get("pull_steps", 0)),
+            "pull_steps": pull_steps, "exchange": exchange,
             "gpu_launches": launches, "generate_s": gen_s, "clocks": clk.summary(), "e2e": e2e,
-            "cpu_baseline": cpu,
+            "cpu_baseline": cpu, "parity": parity,
         }
         print(json.dumps(line), flush=True)
-    ctx.free()
     if dist is not None:
         dist.destroy_process_group()
+
+
+def raster_check(args, world, rank, local, dist, opts_base, nccl_id_buf):
+    """Bit-exactness check printed with every bench line: ORDERED propagation
+    on a seeded pool of --parity-neurons neurons (fanout and weights as the
+    timed workload), sharded over the same ranks, for --parity-steps steps of
+    the same injection stream. Rank 0 hashes the whole spike raster (SHA-256
+    over the per-step spike vectors); the hash is the same at every GPU count
+    and equals the reference's serial CPU step's (computed here when the
+    reference library is present)."""
+    import hashlib
+
+    import numpy as np
+    import torch
+
+    import snn_b200 as sb
+
+    n, steps = args.parity_neurons, args.parity_steps
+    count = max(1, int(round(args.inject_frac * n)))
+    lif = sb.LifParams(1.0, 20.0, -65.0, -65.0, -50.0, 1.0, 2)
+    opts = sb.default_options(propagation=sb.PROPAGATE_ORDERED, **opts_base)
+    if nccl_id_buf is not None:
+        import ctypes
+        opts.nccl_id = ctypes.cast(nccl_id_buf, ctypes.c_void_p)
+    ctx = sb.CudaContext.random_pool(n, args.fanout, -0.2, 0.5, args.seed + 1, lif=lif, options=opts)
+    if world > 1 and args.exchange == "peer":
+        handles = [None] * world
+        dist.all_gather_object(handles, ctx.ipc_handle())
+        ctx.ipc_connect(handles)
+    slot = ctx.local_count if world == 1 else -(-(-(-n // world)) // 32) * 32
+    sha = hashlib.sha256()
+    spikes = 0
+    buf = np.zeros(ctx.local_count, np.uint8)
+    for t in range(steps):
+        idx = _stream_indices(args.seed, t, 1, count, n)[0]
+        ctx.inject_current(idx, np.full(count, args.inject_value, np.float32))
+        ctx.step(out=buf)
+        if world > 1:
+            mine = torch.zeros(slot, dtype=torch.uint8, device="cuda")
+            mine[:ctx.local_count] = torch.from_numpy(buf).cuda()
+            parts = [torch.empty_like(mine) for _ in range(world)]
+            dist.all_gather(parts, mine)
+            full = np.concatenate([parts[r].cpu().numpy()[:sb.shard_range(n, world, r)[1]] for r in range(world)])
+        else:
+            full = buf
+        if rank == 0:
+            sha.update(full.tobytes())
+            spikes += int(full.sum())
+    ctx.free()
+    if rank != 0:
+        return None
+    out = {"check": "ORDERED spike raster, SHA-256 over all steps", "neurons": n, "fanout": args.fanout,
+           "steps": steps, "seed": args.seed + 1, "raster_sha256": sha.hexdigest(), "spikes": spikes}
+    ref = reference_raster_sha(args, n, steps, count)
+    if ref is not None:
+        out["reference_raster_sha256"] = ref
+        out["match"] = ref == out["raster_sha256"]
+    return out
+
+
+def reference_raster_sha(args, n, steps, count):
+    """The reference's serial CPU step (oracle/_ref, CSR-order scatter) on the
+    same network and inputs: the SHA-256 of its raster, or None when the
+    reference library is absent."""
+    import hashlib
+
+    import numpy as np
+
+    from oracle.oracle import Oracle, State, baseline_lif, ref_available
+    if not ref_available("ref"):
+        return None
+    net = Oracle("port").random_pool_parallel(n, args.fanout, -0.2, 0.5, args.seed + 1, lif=baseline_lif())
+    st = State(net, lib=Oracle("ref"))
+    sha = hashlib.sha256()
+    val = np.full(count, args.inject_value, np.float32)
+    for t in range(steps):
+        st.inject(_stream_indices(args.seed, t, 1, count, n)[0], val)
+        sha.update(st.step().tobytes())
+    return sha.hexdigest()
 
 
 def _stream_indices(seed, first_step, steps, count, n):

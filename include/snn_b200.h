@@ -209,6 +209,11 @@ typedef struct snn_b200_stats {
     double exchange_ms;        /* device time of the spike all-gather + compaction (timing = 1) */
     uint64_t pull_steps;       /* steps whose propagation ran the pull kernel (dense steps) */
     uint64_t pull_events;      /* synaptic events of those steps */
+    uint64_t pull_spikes;      /* spiking rows of those steps */
+    double propagate_pull_ms;  /* share of propagate_ms spent in those steps (timing = 1) */
+    double exchange_wait_ms;   /* peer exchange: device time this rank waited for the other
+                                * ranks' spike slices (flag waits, summed over steps) */
+    double exchange_wait_max_ms;  /* the longest single flag wait */
 } snn_b200_stats_t;
 
 typedef struct snn_b200_layout {

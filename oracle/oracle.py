@@ -129,9 +129,14 @@ class Network:
 
 
 class State:
-    def __init__(self, net: Network):
+    """A simulation state. `lib` selects the back end that steps it (default:
+    the one that built the network); networks of every back end share the
+    reference's struct layout, so a port-built network can be stepped by the
+    reference's own library."""
+
+    def __init__(self, net: Network, lib: "Oracle | None" = None):
         self.net = net
-        self.lib = net.lib
+        self.lib = lib if lib is not None else net.lib
         h = P()
         st = self.lib._state_create(net.handle, C.byref(h))
         if st != 0:
@@ -236,6 +241,7 @@ class Oracle:
         self._plan_net = fn("network_memory_plan", C.c_int, P, P)
         if kind == "port":
             self._pool = fn("build_random_pool", C.c_int, u64, u64, f32, f32, u64, C.c_int, P, P)
+            self._pool_par = fn("build_random_pool_parallel", C.c_int, u64, u64, f32, f32, u64, C.c_int, P, P)
             self._ff = fn("build_feedforward", C.c_int, P, C.c_size_t, u64, f32, u64, P, P)
             self._layered = fn("build_layered_random", C.c_int, P, C.c_size_t, u64, f32, f32, u64, P, P)
             self._dense_gauss = fn("build_dense_gaussian", C.c_int, P, C.c_size_t, u64, P, P)
@@ -261,6 +267,14 @@ class Oracle:
         else:
             cfg = RandomPoolConfig(n, fanout, wmin, wmax, seed, int(allow_self))
             st = self._pool(C.byref(cfg), lp, C.byref(h))
+        return self._wrap(st, h)
+
+    def random_pool_parallel(self, n, fanout, wmin, wmax, seed, allow_self=False, lif=None) -> Network:
+        """random_pool built by all host threads (port only), bit-identical."""
+        assert self.kind == "port"
+        h = P()
+        st = self._pool_par(n, fanout, wmin, wmax, seed, int(allow_self),
+                            C.byref(lif) if lif is not None else None, C.byref(h))
         return self._wrap(st, h)
 
     def feedforward(self, layers, fanout, weight, seed, lif=None) -> Network:

@@ -302,6 +302,53 @@ int orc_build_random_pool(orc_size_t n, orc_size_t fanout, float wmin, float wma
     return ORC_OK;
 }
 
+/* The same network as orc_build_random_pool, built by all host threads.
+ * Draw d of the stream is mix64(seed + d * gamma) (src/snn.c:94-99), so edge
+ * e = pre * fanout + j reads draws 2e+1 (target) and 2e+2 (weight) in any
+ * order: the rows are filled in parallel and the result is bit-identical to
+ * the serial builder (src/snn.c:523-574). Used to give the reference's own
+ * CPU step a full-size (10M x 1000) pool in seconds instead of minutes. */
+int orc_build_random_pool_parallel(orc_size_t n, orc_size_t fanout, float wmin, float wmax, uint64_t seed,
+                                   int allow_self, const orc_lif_params_t *params, orc_network_t **out) {
+    uint64_t e = 0;
+    orc_network_t *net = NULL;
+    int64_t pre;
+    int st;
+    if (out == NULL) {
+        return ORC_ERR_INVALID_ARGUMENT;
+    }
+    *out = NULL;
+    if (n == 0 || (!allow_self && n == 1u && fanout != 0u) || !isfinite(wmin) || !isfinite(wmax) || wmax < wmin ||
+        !isfinite(wmax - wmin)) {
+        return ORC_ERR_INVALID_ARGUMENT;
+    }
+    if (!mul_u64(n, fanout, &e) || n > (orc_size_t)INT64_MAX) {
+        return ORC_ERR_OVERFLOW;
+    }
+    st = alloc_network(n, e, 2, params, &net);
+    if (st != ORC_OK) {
+        return st;
+    }
+#pragma omp parallel for schedule(static)
+    for (pre = 0; pre < (int64_t)n; ++pre) {
+        orc_size_t j;
+        orc_size_t edge = (orc_size_t)pre * fanout;
+        net->row_ptr[pre] = edge;
+        for (j = 0; j < fanout; ++j, ++edge) {
+            orc_size_t post = mix64(seed + (2u * edge + 1u) * ORC_GAMMA) % n;
+            const float u = unit_from_bits(mix64(seed + (2u * edge + 2u) * ORC_GAMMA));
+            if (!allow_self && post == (orc_size_t)pre) {
+                post = (post + 1u) % n;
+            }
+            net->col_idx[edge] = post;
+            net->weights[edge] = lerp_weight(wmin, wmax, u);
+        }
+    }
+    net->row_ptr[n] = e;
+    *out = net;
+    return ORC_OK;
+}
+
 /* BASELINE config 4 generator (no reference builder exists for it): edge e in
  * CSR order takes draws 2e+1 (target) and 2e+2 (weight) of the stream seeded
  * `seed`, exactly like the random-pool builder's per-edge pair. */

@@ -106,6 +106,10 @@ int orc_build_feedforward(const orc_size_t *layer_sizes, size_t layer_count, orc
                           uint64_t seed, const orc_lif_params_t *params, orc_network_t **out);
 int orc_build_random_pool(orc_size_t neuron_count, orc_size_t fanout, float weight_min, float weight_max,
                           uint64_t seed, int allow_self, const orc_lif_params_t *params, orc_network_t **out);
+/* orc_build_random_pool filled by all host threads (OpenMP), bit-identical. */
+int orc_build_random_pool_parallel(orc_size_t neuron_count, orc_size_t fanout, float weight_min,
+                                   float weight_max, uint64_t seed, int allow_self,
+                                   const orc_lif_params_t *params, orc_network_t **out);
 /* Deep fixed-fanout layered net: every neuron of layer l < L-1
  * sends `fanout` edges to uniform targets (with replacement) in layer l+1, weights
  * U[wmin, wmax] with the random-pool interpolation; the last layer has no edges. */

@@ -86,7 +86,9 @@ class Options(C.Structure):
 class Stats(C.Structure):
     _fields_ = [("steps", u64), ("spikes", u64), ("events", u64), ("kernel_launches", u64),
                 ("step_ms", C.c_double), ("propagate_ms", C.c_double), ("lif_ms", C.c_double),
-                ("exchange_ms", C.c_double), ("pull_steps", u64), ("pull_events", u64)]
+                ("exchange_ms", C.c_double), ("pull_steps", u64), ("pull_events", u64),
+                ("pull_spikes", u64), ("propagate_pull_ms", C.c_double), ("exchange_wait_ms", C.c_double),
+                ("exchange_wait_max_ms", C.c_double)]
 
     def as_dict(self):
         return {k: getattr(self, k) for k, _ in self._fields_}

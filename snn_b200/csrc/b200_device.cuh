@@ -29,11 +29,23 @@ __device__ __forceinline__ void block_add_u64(unsigned long long v, unsigned lon
 
 // Per step bookkeeping done by block 0 of the (last) propagation kernel:
 // zero the list slot the next step appends to, and count this step's spikes.
-__device__ __forceinline__ void step_epilogue(DevCounters *ctr, int parity, int count_spikes, uint32_t count) {
+// pulled: this step's propagation was a pull kernel (recorded in the step
+// kind log and the pull statistics).
+__device__ __forceinline__ void step_epilogue(DevCounters *ctr, int parity, int count_spikes, uint32_t count,
+                                              int pulled = 0) {
     if (blockIdx.x == 0 && threadIdx.x == 0) {
         ctr->list_count[parity ^ 1] = 0u;
         if (count_spikes) ctr->spikes += count;
+        if (pulled) ctr->pull_spikes += count;
+        if (ctr->kind_log) ctr->kind_log[ctr->step_seq % kStepLog] = (uint8_t)(pulled != 0);
+        ctr->step_seq += 1ull;
     }
+}
+
+__device__ __forceinline__ unsigned long long global_ns() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
 }
 
 }  // namespace dev

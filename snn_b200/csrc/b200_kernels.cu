@@ -89,7 +89,7 @@ __device__ __forceinline__ float fget(const float2 &v, int i) { return i == 0 ? 
 // ---------------------------------------------------------------- init ----
 __global__ void init_state_kernel(uint64_t n, float v_rest, float *v, float *cur0, float *cur1, float *ext,
                                   uint32_t *refr, uint8_t *spikes, uint64_t words, uint32_t *bitmap,
-                                  DevCounters *ctr) {
+                                  DevCounters *ctr, uint8_t *kind_log) {
     const uint64_t stride = (uint64_t)blockDim.x * gridDim.x;
     const uint64_t t0 = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
     for (uint64_t i = t0; i < n; i += stride) {
@@ -110,6 +110,11 @@ __global__ void init_state_kernel(uint64_t n, float v_rest, float *v, float *cur
         ctr->stream_step = 0ull;
         ctr->pull_runs = 0ull;
         ctr->pull_events = 0ull;
+        ctr->pull_spikes = 0ull;
+        ctr->step_seq = 0ull;
+        ctr->wait_ns = 0ull;
+        ctr->wait_max_ns = 0ull;
+        ctr->kind_log = kind_log;
     }
 }
 
@@ -278,6 +283,7 @@ __global__ void __launch_bounds__(256) compact_kernel(const uint32_t *__restrict
         __shared__ uint32_t s_ok;
         if (threadIdx.x == 0) {
             uint32_t ok = 1u;
+            const unsigned long long t0 = blockIdx.x == 0 ? global_ns() : 0ull;
             for (uint32_t r = 0; r < pw.nflags && ok; ++r) {
                 for (uint32_t it = 0;; ++it) {
                     unsigned long long v;
@@ -292,6 +298,11 @@ __global__ void __launch_bounds__(256) compact_kernel(const uint32_t *__restrict
                 }
             }
             s_ok = ok;
+            if (blockIdx.x == 0) {
+                const unsigned long long dt = global_ns() - t0;
+                ctr->wait_ns += dt;
+                if (dt > ctr->wait_max_ns) ctr->wait_max_ns = dt;
+            }
         }
         __syncthreads();
         if (!s_ok) return;
@@ -582,7 +593,7 @@ __global__ void __launch_bounds__(256) propagate_pull_kernel(uint64_t n_local, c
     block_add_u64(events, &ctr->events);
     block_add_u64(events, &ctr->pull_events);
     if (blockIdx.x == 0 && threadIdx.x == 0) ctr->pull_runs += 1ull;
-    step_epilogue(ctr, parity, count_spikes, count);
+    step_epilogue(ctr, parity, count_spikes, count, 1);
 }
 
 // Chunked variant (the default when the layout was built chunked): the
@@ -689,7 +700,7 @@ __global__ void __launch_bounds__(kPullSmemThreads, 1)
     block_add_u64(events, &ctr->events);
     block_add_u64(events, &ctr->pull_events);
     if (blockIdx.x == 0 && threadIdx.x == 0) ctr->pull_runs += 1ull;
-    step_epilogue(ctr, parity, count_spikes, count);
+    step_epilogue(ctr, parity, count_spikes, count, 1);
 }
 
 // ----------------------------------------------------------- streaming ----
@@ -1055,12 +1066,14 @@ int sm_count(int device) {
 }
 
 void launch_init_state(cudaStream_t s, uint64_t n, float v_rest, float *v, float *cur0, float *cur1, float *ext,
-                       uint32_t *refr, uint8_t *spikes, uint64_t words, uint32_t *bitmap, DevCounters *ctr) {
+                       uint32_t *refr, uint8_t *spikes, uint64_t words, uint32_t *bitmap, DevCounters *ctr,
+                       uint8_t *kind_log) {
     const uint64_t work = n > words ? n : words;
     uint64_t blocks = (work + 255) / 256;
     if (blocks > 65535) blocks = 65535;
     if (blocks == 0) blocks = 1;
-    init_state_kernel<<<(unsigned)blocks, 256, 0, s>>>(n, v_rest, v, cur0, cur1, ext, refr, spikes, words, bitmap, ctr);
+    init_state_kernel<<<(unsigned)blocks, 256, 0, s>>>(n, v_rest, v, cur0, cur1, ext, refr, spikes, words, bitmap, ctr,
+                                                       kind_log);
 }
 
 template <bool EXT, typename TIdx, int ITERS>

@@ -26,6 +26,13 @@ struct LifArgs {
 //                 (ping-pong: the propagation of step t zeroes slot (t+1)&1).
 //  spikes/events  cumulative statistics (this rank's neurons / targets).
 //  error          first error code raised by a bounded device wait (0 = none).
+//  step_seq       steps completed since the context was created (never reset).
+//  kind_log       optional ring of kStepLog bytes: entry step_seq % kStepLog
+//                 is 1 when that step's propagation ran a pull kernel.
+//  wait_ns        nanoseconds the peer-exchange compaction spent waiting for
+//                 the other ranks' flags (summed over steps), wait_max_ns the
+//                 longest single wait.
+constexpr uint32_t kStepLog = 8192;
 struct DevCounters {
     uint32_t list_count[2];
     uint32_t error;
@@ -35,7 +42,13 @@ struct DevCounters {
     unsigned long long stream_step;  // injection-stream step of graph-replayed runs
     unsigned long long pull_runs;    // steps whose propagation ran a pull kernel
     unsigned long long pull_events;  // synaptic events of those steps
+    unsigned long long pull_spikes;  // spiking rows of those steps
+    unsigned long long step_seq;
+    unsigned long long wait_ns;
+    unsigned long long wait_max_ns;
+    uint8_t *kind_log;
 };
+static_assert(sizeof(DevCounters) <= 256, "DevCounters must fit its 256-byte block");
 
 // Peer (NVLink, CUDA IPC) spike-bitmap exchange fused into the LIF kernel:
 // every bitmap word a rank computes is also stored into each rank's exchange
@@ -120,9 +133,10 @@ cudaError_t launch_propagate_binned(cudaStream_t s, const void *list, int idx_bi
 // Number of SMs of the current device (cached per device).
 int sm_count(int device);
 
+// ctr != nullptr: the counters are zeroed and ctr->kind_log set to kind_log.
 void launch_init_state(cudaStream_t s, uint64_t n, float v_rest, float *v, float *cur0, float *cur1, float *ext,
                        uint32_t *refr, uint8_t *spikes, uint64_t bitmap_words, uint32_t *bitmap,
-                       DevCounters *ctr);
+                       DevCounters *ctr, uint8_t *kind_log = nullptr);
 
 // LIF update of n local neurons; writes spikes (u8), the local bitmap words
 // and, when list != nullptr, appends the spiking ids (+ global_offset) to the

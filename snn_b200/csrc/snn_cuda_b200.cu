@@ -74,6 +74,7 @@ struct StreamChunk {
 
 struct TimingGroup {
     cudaEvent_t ev[4];  // start, after LIF, after exchange, after propagation
+    uint64_t seq = 0;   // the step's index since create (DevCounters::step_seq)
 };
 
 }  // namespace
@@ -205,8 +206,10 @@ struct snn_cuda_context {
     uint64_t step = 0;
     uint64_t launches = 0;
     int timing = 0;
+    uint64_t seq = 0;  // steps enqueued since create (mirrors DevCounters::step_seq)
+    uint8_t *d_kind_log = nullptr;  // inside d_ws: b200::kStepLog bytes
     std::vector<TimingGroup> pending, pool;
-    double t_step = 0, t_lif = 0, t_exchange = 0, t_prop = 0;
+    double t_step = 0, t_lif = 0, t_exchange = 0, t_prop = 0, t_prop_pull = 0;
 };
 
 namespace {
@@ -368,7 +371,8 @@ snn_status_t apply_options(snn_cuda_context_t *c, uint64_t n, const snn_b200_opt
 }
 
 uint64_t state_bytes(const snn_cuda_context_t *c) {
-    return c->n_local * (4u + 8u + 4u + 4u + 1u) + c->bitmap_words * 4u + c->n_global * (c->idx_bits / 8) + 256u;
+    return c->n_local * (4u + 8u + 4u + 4u + 1u) + c->bitmap_words * 4u + c->n_global * (c->idx_bits / 8) + 256u +
+           b200::kStepLog;
 }
 
 // Device state: seams #1-#6 (six allocations) and #7 (init launch), matching
@@ -383,17 +387,19 @@ snn_status_t allocate_state(snn_cuda_context_t *c) {
     if ((st = dmalloc((void **)&c->d_ext, n, 4)) != SNN_OK) return st;
     if ((st = dmalloc((void **)&c->d_refr, n, 4)) != SNN_OK) return st;
     if ((st = dmalloc((void **)&c->d_spikes, n, 1)) != SNN_OK) return st;
-    // Workspace: [counters | bitmap (global, padded) | spike list (global)].
+    // Workspace: [counters | step kind log | bitmap (global, padded) | spike list (global)].
     const uint64_t list_bytes = c->n_global * (c->idx_bits / 8);
-    const uint64_t ws = 256 + ((c->bitmap_words * 4 + 255) / 256) * 256 + list_bytes;
+    const uint64_t head = 256 + b200::kStepLog;
+    const uint64_t ws = head + ((c->bitmap_words * 4 + 255) / 256) * 256 + list_bytes;
     if ((st = dmalloc(&c->d_ws, ws, 1)) != SNN_OK) return st;
     c->d_ctr = (b200::DevCounters *)c->d_ws;
-    c->d_bitmap = (uint32_t *)((char *)c->d_ws + 256);
-    c->d_list = (char *)c->d_ws + 256 + ((c->bitmap_words * 4 + 255) / 256) * 256;
+    c->d_kind_log = (uint8_t *)c->d_ws + 256;
+    c->d_bitmap = (uint32_t *)((char *)c->d_ws + head);
+    c->d_list = (char *)c->d_ws + head + ((c->bitmap_words * 4 + 255) / 256) * 256;
     c->d_cur[0] = c->d_cur_pair;
     c->d_cur[1] = c->d_cur_pair ? c->d_cur_pair + cur_stride : nullptr;
     b200::launch_init_state(c->stream, n, c->lif.v_rest, c->d_v, c->d_cur[0], c->d_cur[1], c->d_ext, c->d_refr,
-                            c->d_spikes, c->bitmap_words, c->d_bitmap, c->d_ctr);
+                            c->d_spikes, c->bitmap_words, c->d_bitmap, c->d_ctr, c->d_kind_log);
     return check_launch(c);
 }
 
@@ -1067,6 +1073,7 @@ TimingGroup *timing_begin(snn_cuda_context_t *c) {
     c->pending.push_back(c->pool.back());
     c->pool.pop_back();
     TimingGroup *g = &c->pending.back();
+    g->seq = c->seq;
     cudaEventRecord(g->ev[0], c->stream);
     return g;
 }
@@ -1076,6 +1083,14 @@ void timing_mark(snn_cuda_context_t *c, TimingGroup *g, int k) {
 }
 
 void timing_fold(snn_cuda_context_t *c) {
+    // Which steps ran a pull kernel (device-chosen): the step kind log, for
+    // the steps still inside its ring.
+    std::vector<uint8_t> kinds;
+    if (!c->pending.empty() && c->d_kind_log) {
+        kinds.resize(b200::kStepLog);
+        if (cudaMemcpy(kinds.data(), c->d_kind_log, b200::kStepLog, cudaMemcpyDeviceToHost) != cudaSuccess)
+            kinds.clear();
+    }
     for (auto &g : c->pending) {
         float a = 0, b = 0, d = 0, t = 0;
         if (cudaEventElapsedTime(&a, g.ev[0], g.ev[1]) == cudaSuccess &&
@@ -1086,6 +1101,7 @@ void timing_fold(snn_cuda_context_t *c) {
             c->t_exchange += b;
             c->t_prop += d;
             c->t_step += t;
+            if (!kinds.empty() && c->seq - g.seq <= b200::kStepLog && kinds[g.seq % b200::kStepLog]) c->t_prop_pull += d;
         }
         c->pool.push_back(g);
     }
@@ -1236,6 +1252,7 @@ snn_status_t enqueue_step(snn_cuda_context_t *c, bool has_ext) {
     timing_mark(c, tg, 3);
     c->cur ^= 1;
     c->step++;
+    c->seq++;
     return SNN_OK;
 }
 
@@ -2053,7 +2070,7 @@ snn_status_t snn_b200_reset(snn_cuda_context_t *c) {
     if (cudaMemcpy(&saved, c->d_ctr, sizeof(saved), cudaMemcpyDeviceToHost) != cudaSuccess) return SNN_ERR_CUDA;
     b200::launch_init_state(c->stream, c->n_local, c->lif.v_rest, c->d_v, c->d_cur[0], c->d_cur[1],
                             c->ext_held ? nullptr : c->d_ext, c->d_refr, c->d_spikes, c->bitmap_words, c->d_bitmap,
-                            c->d_ctr);
+                            c->d_ctr, c->d_kind_log);
     c->launches++;
     if ((st = cuda_status(cudaGetLastError())) != SNN_OK) return st;
     saved.list_count[0] = saved.list_count[1] = 0;
@@ -2150,6 +2167,10 @@ snn_status_t snn_b200_get_stats(snn_cuda_context_t *c, snn_b200_stats_t *out) {
     out->exchange_ms = c->t_exchange;
     out->pull_steps = d.pull_runs;
     out->pull_events = d.pull_events;
+    out->pull_spikes = d.pull_spikes;
+    out->propagate_pull_ms = c->t_prop_pull;
+    out->exchange_wait_ms = (double)d.wait_ns * 1e-6;
+    out->exchange_wait_max_ms = (double)d.wait_max_ns * 1e-6;
     return SNN_OK;
 }
 
@@ -2163,9 +2184,12 @@ snn_status_t snn_b200_reset_stats(snn_cuda_context_t *c) {
     d.events = 0;
     d.pull_runs = 0;
     d.pull_events = 0;
+    d.pull_spikes = 0;
+    d.wait_ns = 0;
+    d.wait_max_ns = 0;
     if (cudaMemcpy(c->d_ctr, &d, sizeof(d), cudaMemcpyHostToDevice) != cudaSuccess) return SNN_ERR_CUDA;
     c->launches = 0;
-    c->t_step = c->t_lif = c->t_exchange = c->t_prop = 0;
+    c->t_step = c->t_lif = c->t_exchange = c->t_prop = c->t_prop_pull = 0;
     return SNN_OK;
 }
 

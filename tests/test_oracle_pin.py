@@ -201,3 +201,39 @@ def test_port_equals_reference_randomized(seed):
         a, b = sts[0].step(ext if t % 2 else None), sts[1].step(ext if t % 2 else None)
         assert np.array_equal(a, b)
     assert np.array_equal(sts[0].voltage().view(np.uint32), sts[1].voltage().view(np.uint32))
+
+
+@pytest.mark.parametrize("n,fanout,allow_self,seed", [(1, 0, False, 3), (2, 5, False, 0), (97, 13, False, 9),
+                                                      (1000, 64, True, 123456789), (4096, 100, False, 0)])
+def test_parallel_pool_builder_bit_identical(n, fanout, allow_self, seed):
+    """The multi-threaded random-pool builder (used to give the reference's
+    CPU step a full-size pool) equals the serial builder and, when present,
+    the reference's own snn_build_random_pool bit for bit."""
+    lif = baseline_lif()
+    a = PORT.random_pool(n, fanout, -0.2, 0.5, seed, allow_self=allow_self, lif=lif)
+    b = PORT.random_pool_parallel(n, fanout, -0.2, 0.5, seed, allow_self=allow_self, lif=lif)
+    for x, y in ((a.row_ptr(), b.row_ptr()), (a.col_idx(), b.col_idx()),
+                 (a.weights().view(np.uint32), b.weights().view(np.uint32))):
+        np.testing.assert_array_equal(x, y)
+    assert a.decay == b.decay
+    if ref_available("ref"):
+        r = Oracle("ref").random_pool(n, fanout, -0.2, 0.5, seed, allow_self=allow_self, lif=lif)
+        np.testing.assert_array_equal(r.col_idx(), b.col_idx())
+        np.testing.assert_array_equal(r.weights().view(np.uint32), b.weights().view(np.uint32))
+
+
+@pytest.mark.skipif(not ref_available("ref"), reason="reference library not built")
+def test_port_network_stepped_by_reference_library():
+    """A port-built network has the reference's struct layout: the
+    reference's own snn_step_cpu steps it exactly as it steps its own build."""
+    lif = baseline_lif()
+    ref = Oracle("ref")
+    mine = PORT.random_pool_parallel(3000, 50, 0.0, 0.6, 7, lif=lif)
+    theirs = ref.random_pool(3000, 50, 0.0, 0.6, 7, lif=lif)
+    s1, s2 = State(mine, lib=ref), State(theirs)
+    for t in range(30):
+        idx = np.arange(t * 37, t * 37 + 60, dtype=np.uint64) % 3000
+        val = np.full(60, 20.0, np.float32)
+        assert s1.inject(idx, val) == 0 and s2.inject(idx, val) == 0
+        np.testing.assert_array_equal(s1.step(), s2.step())
+    np.testing.assert_array_equal(s1.voltage().view(np.uint32), s2.voltage().view(np.uint32))
