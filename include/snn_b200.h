@@ -146,18 +146,17 @@ typedef enum snn_b200_propagation {
     /* Every target folds its contributions in CSR order (ascending
      * presynaptic row, ascending edge): bit-identical to the reference's
      * serial CPU step (src/snn.c:898-906) for any weights. FULL mode only.
-     * Each step either sorts its events by target (stable radix sort of the
-     * spiking rows' CSR slices; cost ~ events) or, on dense steps when a CSC
-     * fits beside the CSR, pulls over the CSC (cost ~ synapses). */
+     * Each step either bins its events by target tile in CSR order and
+     * folds every tile in shared memory (the bin-fold; cost ~ events), or,
+     * on dense steps when a CSC fits beside the CSR, pulls over the CSC
+     * (cost ~ synapses); the choice is made on the device from the step's
+     * event count, with no host round trip. */
     SNN_B200_PROPAGATE_ORDERED = 1,
     /* The plain push kernel: one red.global.add.f32 per event. */
     SNN_B200_PROPAGATE_PUSH_ATOMIC = 2,
-    /* The binned push kernel: target tiles in shared memory, events routed
-     * through L2 bins by TMA-fed producer/consumer warps (at most 4 target
-     * passes of < 2^24 targets each, 32-bit columns; falls back to the
-     * atomic kernel otherwise). SNN_B200_PROPAGATE_PUSH picks whichever of
-     * the two is faster on this device. Both equal ORDERED up to fp32
-     * reassociation. */
+    /* The binned push: each step's events are binned by target tile and
+     * folded tile by tile in shared memory. It keeps CSR order, so it is the
+     * same propagation as ORDERED (the context reports ORDERED). */
     SNN_B200_PROPAGATE_PUSH_BINNED = 3
 } snn_b200_propagation_t;
 
@@ -225,8 +224,8 @@ typedef struct snn_b200_layout {
     int propagation;                /* snn_b200_propagation_t */
     uint64_t device_state_bytes;    /* resident per-neuron state + spike workspace */
     uint64_t device_topology_bytes; /* resident topology (FULL) or chunk buffers (STREAMING) */
-    uint32_t binned;                /* 1: push runs the binned shared-memory kernel */
-    uint32_t binned_passes;         /* binned: target passes (each with its own CSR slice) */
+    uint32_t binned;                /* 1: ORDERED runs the bin-fold (events binned per target tile) */
+    uint32_t binned_passes;         /* bin-fold: number of target tiles */
     uint32_t ordered_csc;           /* ORDERED: 1 when a CSC is resident (pull for dense steps) */
     uint32_t batch;                 /* states sharing the topology (neuron_count = batch x rows) */
     snn_size_t topology_rows;       /* rows of the shared topology (n of the network) */

@@ -1,0 +1,463 @@
+// Bin-fold propagation: bit-exact (CSR-order) synaptic propagation whose cost
+// follows the step's events, with no sort library and no host round trip.
+//
+// The serial CPU step adds, for every target, the weights of its spiking
+// presynaptic rows in ascending (row, edge) order, starting from +0.0f
+// (src/snn.c:898-906). Per step, on the device:
+//  1. ordered compaction: the spike bitmap becomes the ascending spike list
+//     (per-chunk popcounts, then every chunk writes its ids at its prefix),
+//     and the step's event total (sum of the spiking rows' degrees) is added
+//     to DevCounters::step_events[parity];
+//  2. count: the spike list is cut into G contiguous slices, one per CTA;
+//     each CTA counts its events per target tile (2^tile_bits consecutive
+//     local targets) into hist[tile][cta];
+//  3. an exclusive scan of hist (tile-major) gives every (tile, CTA) its
+//     first slot in the event array;
+//  4. scatter: every CTA walks its slice again, eight rows at a time (one per
+//     warp), and writes each event (target within the tile, weight) to its
+//     tile's slots; ranks inside a warp come from __match_any_sync, ranks
+//     across warps from a per-(warp, tile) prefix, so every tile's events
+//     keep the global (row, edge) order;
+//  5. fold: one CTA per tile keeps the tile's sums in shared memory and folds
+//     the tile's events window by window in order (each warp owns an eighth
+//     of the tile; same-target events inside one round of 32 are applied in
+//     lane order), then writes the tile's currents.
+// A step whose events exceed `gate_events` is a dense step: 2-5 do nothing
+// and the pull kernel (launched behind the same device-side gate) runs.
+// HBM per event: 4 B (count) + 8 B (scatter reads) + 8 B (scatter writes) +
+// 8 B (fold reads), with 32-bit columns.
+#include "b200_binfold.h"
+#include "b200_device.cuh"
+
+#include <cub/device/device_scan.cuh>
+
+#include <algorithm>
+#include <mutex>
+#include <vector>
+
+namespace b200 {
+
+namespace {
+
+using namespace dev;
+
+constexpr int kBfThreads = 256;
+constexpr int kBfWarps = kBfThreads / 32;
+constexpr uint32_t kChunkWords = 2048;  // bitmap words per compaction chunk (65,536 neurons)
+constexpr int kWordsPerThread = kChunkWords / kBfThreads;
+constexpr uint32_t kFoldWindow = 2048;  // events staged in shared memory per fold round
+
+__device__ __forceinline__ uint32_t lanemask_lt() {
+    uint32_t m;
+    asm("mov.u32 %0, %%lanemask_lt;" : "=r"(m));
+    return m;
+}
+
+__device__ __forceinline__ bool dense_step(const DevCounters *ctr, int parity, unsigned long long gate) {
+    return *(volatile const unsigned long long *)&ctr->step_events[parity] > gate;
+}
+
+// Block-wide exclusive scan of one u32 per thread; returns the thread's
+// exclusive prefix, *total the block's sum. Every thread must call it.
+__device__ __forceinline__ uint32_t block_exclusive_scan(uint32_t v, uint32_t *total) {
+    __shared__ uint32_t s_warp[kBfWarps];
+    const unsigned lane = lane_id(), warp = threadIdx.x >> 5;
+    uint32_t incl = v;
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+        const uint32_t y = __shfl_up_sync(kFull, incl, d);
+        if (lane >= (unsigned)d) incl += y;
+    }
+    if (lane == 31u) s_warp[warp] = incl;
+    __syncthreads();
+    uint32_t base = 0, tot = 0;
+#pragma unroll
+    for (int w = 0; w < kBfWarps; ++w) {
+        const uint32_t t = s_warp[w];
+        base += (w < (int)warp) ? t : 0u;
+        tot += t;
+    }
+    __syncthreads();  // s_warp may be reused by the next call
+    *total = tot;
+    return base + incl - v;
+}
+
+__device__ __forceinline__ unsigned long long block_sum_u64(unsigned long long v) {
+    __shared__ unsigned long long s_part[kBfWarps];
+#pragma unroll
+    for (int d = 16; d > 0; d >>= 1) v += __shfl_xor_sync(kFull, v, d);
+    if (lane_id() == 0) s_part[threadIdx.x >> 5] = v;
+    __syncthreads();
+    unsigned long long t = 0;
+#pragma unroll
+    for (int w = 0; w < kBfWarps; ++w) t += s_part[w];
+    __syncthreads();
+    return t;
+}
+
+// ------------------------------------------------- ordered compaction ----
+// Per-chunk popcounts of the (global) bitmap; also the popcount of this
+// rank's own words [own_begin, own_end) into ctr->spikes. With a peer wait
+// (the exchange fused into LIF), every CTA first waits (bounded) for all
+// ranks' flags of this step.
+__global__ void __launch_bounds__(kBfThreads) chunk_counts_kernel(const uint32_t *__restrict__ bitmap, uint64_t words,
+                                                                  uint32_t *__restrict__ ccnt, DevCounters *ctr,
+                                                                  uint64_t own_begin, uint64_t own_end, PeerWait pw) {
+    if (pw.nflags) {
+        __shared__ uint32_t s_ok;
+        if (threadIdx.x == 0) {
+            uint32_t ok = 1u;
+            const unsigned long long t0 = blockIdx.x == 0 ? global_ns() : 0ull;
+            for (uint32_t r = 0; r < pw.nflags && ok; ++r) {
+                for (uint32_t it = 0;; ++it) {
+                    unsigned long long v;
+                    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(pw.flags + r) : "memory");
+                    if (v >= pw.tag) break;
+                    if (*(volatile uint32_t *)&ctr->error != 0u || it >= pw.spin_limit) {
+                        atomicExch(&ctr->error, 3u);
+                        ok = 0u;
+                        break;
+                    }
+                    __nanosleep(64);
+                }
+            }
+            s_ok = ok;
+            if (blockIdx.x == 0) {
+                const unsigned long long dt = global_ns() - t0;
+                ctr->wait_ns += dt;
+                if (dt > ctr->wait_max_ns) ctr->wait_max_ns = dt;
+            }
+        }
+        __syncthreads();
+        if (!s_ok) return;
+    }
+    const uint64_t chunks = (words + kChunkWords - 1) / kChunkWords;
+    unsigned long long own = 0;
+    for (uint64_t c = blockIdx.x; c < chunks; c += gridDim.x) {
+        const uint64_t w0 = c * kChunkWords;
+        uint32_t cnt = 0;
+        for (uint32_t k = threadIdx.x; k < kChunkWords; k += kBfThreads) {
+            const uint64_t wi = w0 + k;
+            if (wi < words) {
+                const uint32_t p = __popc(__ldcg(bitmap + wi));
+                cnt += p;
+                if (wi >= own_begin && wi < own_end) own += p;
+            }
+        }
+        uint32_t tot;
+        block_exclusive_scan(cnt, &tot);
+        if (threadIdx.x == 0) ccnt[c] = tot;
+    }
+    own = block_sum_u64(own);
+    if (threadIdx.x == 0 && own) atomicAdd(&ctr->spikes, own);
+}
+
+// Each chunk writes its spiking ids ascending at the prefix of the chunks
+// before it, so the list is globally ascending. The degrees of the written
+// rows (batched states: row = id % batch_rows) are summed into
+// step_events[parity]; the last chunk sets list_count[parity].
+template <typename TIdx>
+__global__ void __launch_bounds__(kBfThreads) compact_ordered_kernel(const uint32_t *__restrict__ bitmap,
+                                                                     uint64_t words,
+                                                                     const uint32_t *__restrict__ ccnt,
+                                                                     TIdx *__restrict__ list, DevCounters *ctr,
+                                                                     int parity, const uint64_t *__restrict__ row_ptr,
+                                                                     uint64_t batch_rows) {
+    if (*(volatile uint32_t *)&ctr->error != 0u) return;  // a peer wait expired: nothing to compact
+    const uint64_t chunks = (words + kChunkWords - 1) / kChunkWords;
+    unsigned long long events = 0;
+    for (uint64_t c = blockIdx.x; c < chunks; c += gridDim.x) {
+        uint32_t before = 0;
+        for (uint64_t k = threadIdx.x; k < c; k += kBfThreads) before += ccnt[k];
+        uint32_t prefix;
+        block_exclusive_scan(before, &prefix);
+        const uint64_t w0 = c * kChunkWords + (uint64_t)threadIdx.x * kWordsPerThread;
+        uint32_t wv[kWordsPerThread];
+        uint32_t cnt = 0;
+#pragma unroll
+        for (int j = 0; j < kWordsPerThread; ++j) {
+            wv[j] = w0 + j < words ? __ldcg(bitmap + w0 + j) : 0u;
+            cnt += __popc(wv[j]);
+        }
+        uint32_t tot;
+        uint32_t pos = prefix + block_exclusive_scan(cnt, &tot);
+#pragma unroll
+        for (int j = 0; j < kWordsPerThread; ++j) {
+            uint32_t m = wv[j];
+            while (m) {
+                const int b = __ffs(m) - 1;
+                m &= m - 1u;
+                const uint64_t id = (w0 + j) * 32u + (uint64_t)b;
+                list[pos++] = (TIdx)id;
+                const uint64_t row = batch_rows ? id % batch_rows : id;
+                events += row_ptr[row + 1] - row_ptr[row];
+            }
+        }
+        if (c == chunks - 1 && threadIdx.x == 0) ctr->list_count[parity] = prefix + tot;
+    }
+    events = block_sum_u64(events);
+    if (threadIdx.x == 0 && events) atomicAdd(&ctr->step_events[parity], events);
+}
+
+// --------------------------------------------------------------- count ----
+// CTA c owns list positions [count*c/G, count*(c+1)/G); hist[tile*G + c] =
+// its events into each tile.
+template <typename TIdx, typename TCol>
+__global__ void __launch_bounds__(kBfThreads) binfold_count_kernel(const TIdx *__restrict__ list, DevCounters *ctr,
+                                                                   int parity, const uint64_t *__restrict__ row_ptr,
+                                                                   const TCol *__restrict__ col, uint64_t batch_rows,
+                                                                   uint32_t tile_bits, uint32_t tiles,
+                                                                   uint32_t *__restrict__ hist,
+                                                                   unsigned long long gate) {
+    extern __shared__ uint32_t s_cnt[];  // [tiles]
+    if (dense_step(ctr, parity, gate)) return;
+    const uint32_t count = *(volatile uint32_t *)&ctr->list_count[parity];
+    const unsigned lane = lane_id(), warp = threadIdx.x >> 5;
+    for (uint32_t b = threadIdx.x; b < tiles; b += kBfThreads) s_cnt[b] = 0u;
+    __syncthreads();
+    const uint64_t G = gridDim.x;
+    const uint64_t s0 = (uint64_t)count * blockIdx.x / G, s1 = (uint64_t)count * (blockIdx.x + 1) / G;
+    for (uint64_t s = s0 + warp; s < s1; s += kBfWarps) {
+        const uint64_t id = (uint64_t)list[s];
+        const uint64_t row = batch_rows ? id % batch_rows : id;
+        const uint64_t base = id - row;
+        const uint64_t b = row_ptr[row], e = row_ptr[row + 1];
+        for (uint64_t k0 = b; k0 < e; k0 += 32u) {
+            const uint64_t k = k0 + lane;
+            const bool act = k < e;
+            const uint32_t tile = act ? (uint32_t)((base + (uint64_t)__ldg(col + k)) >> tile_bits) : 0u;
+            const uint32_t peers = __match_any_sync(kFull, act ? tile : (0x80000000u | lane));
+            if (act && lane == (unsigned)(__ffs(peers) - 1)) atomicAdd(&s_cnt[tile], (uint32_t)__popc(peers));
+        }
+    }
+    __syncthreads();
+    for (uint32_t b = threadIdx.x; b < tiles; b += kBfThreads) hist[(uint64_t)b * G + blockIdx.x] = s_cnt[b];
+}
+
+// ------------------------------------------------------------- scatter ----
+// Same slices as the count. Rows go eight at a time, warp w taking row
+// s + w: pass 1 counts each warp's events per tile, a prefix over the warps
+// (in row order) turns the counts into slot positions, pass 2 writes the
+// events, pass 3 clears the touched counters. The rows' columns are re-read
+// from L1 by passes 2 and 3.
+template <typename TIdx, typename TCol>
+__global__ void __launch_bounds__(kBfThreads) binfold_scatter_kernel(const TIdx *__restrict__ list, DevCounters *ctr,
+                                                                     int parity, const uint64_t *__restrict__ row_ptr,
+                                                                     const TCol *__restrict__ col,
+                                                                     const float *__restrict__ w, uint64_t batch_rows,
+                                                                     uint32_t tile_bits, uint32_t tiles,
+                                                                     const uint32_t *__restrict__ offs,
+                                                                     uint2 *__restrict__ bins,
+                                                                     unsigned long long gate) {
+    extern __shared__ uint32_t s_mem[];
+    uint32_t *s_cur = s_mem;           // [tiles] next slot of each tile (this CTA)
+    uint32_t *s_w = s_mem + tiles;     // [warps][tiles] per-warp counts, then positions
+    if (dense_step(ctr, parity, gate)) return;
+    const uint32_t count = *(volatile uint32_t *)&ctr->list_count[parity];
+    const unsigned lane = lane_id(), warp = threadIdx.x >> 5;
+    const uint64_t G = gridDim.x;
+    for (uint32_t b = threadIdx.x; b < tiles; b += kBfThreads) s_cur[b] = offs[(uint64_t)b * G + blockIdx.x];
+    for (uint32_t b = threadIdx.x; b < tiles * kBfWarps; b += kBfThreads) s_w[b] = 0u;
+    __syncthreads();
+    const uint64_t s0 = (uint64_t)count * blockIdx.x / G, s1 = (uint64_t)count * (blockIdx.x + 1) / G;
+    const uint32_t tmask = (1u << tile_bits) - 1u;
+    uint32_t *my = s_w + (uint64_t)warp * tiles;
+    for (uint64_t g0 = s0; g0 < s1; g0 += kBfWarps) {
+        const uint64_t s = g0 + warp;
+        uint64_t b = 0, e = 0, base = 0;
+        if (s < s1) {
+            const uint64_t id = (uint64_t)list[s];
+            const uint64_t row = batch_rows ? id % batch_rows : id;
+            base = id - row;
+            b = row_ptr[row];
+            e = row_ptr[row + 1];
+        }
+        for (uint64_t k0 = b; k0 < e; k0 += 32u) {
+            const uint64_t k = k0 + lane;
+            const bool act = k < e;
+            const uint32_t tile = act ? (uint32_t)((base + (uint64_t)__ldg(col + k)) >> tile_bits) : 0u;
+            const uint32_t peers = __match_any_sync(kFull, act ? tile : (0x80000000u | lane));
+            if (act && lane == (unsigned)(__ffs(peers) - 1)) my[tile] += (uint32_t)__popc(peers);
+        }
+        __syncthreads();
+        for (uint32_t t = threadIdx.x; t < tiles; t += kBfThreads) {
+            uint32_t run = s_cur[t];
+#pragma unroll
+            for (int q = 0; q < kBfWarps; ++q) {
+                // Only a warp with events in the tile reads its position (and
+                // clears it afterwards); the others' counters stay zero.
+                const uint32_t x = s_w[(uint64_t)q * tiles + t];
+                if (x) s_w[(uint64_t)q * tiles + t] = run;
+                run += x;
+            }
+            s_cur[t] = run;
+        }
+        __syncthreads();
+        for (uint64_t k0 = b; k0 < e; k0 += 32u) {
+            const uint64_t k = k0 + lane;
+            const bool act = k < e;
+            const uint32_t t = act ? (uint32_t)(base + (uint64_t)__ldg(col + k)) : 0u;
+            const uint32_t tile = t >> tile_bits;
+            const uint32_t peers = __match_any_sync(kFull, act ? tile : (0x80000000u | lane));
+            const int leader = __ffs(peers) - 1;
+            uint32_t pos = 0;
+            if (act && lane == (unsigned)leader) pos = my[tile];
+            pos = __shfl_sync(kFull, pos, leader);
+            __syncwarp();
+            if (act && lane == (unsigned)leader) my[tile] = pos + (uint32_t)__popc(peers);
+            if (act) bins[pos + __popc(peers & lanemask_lt())] = make_uint2(t & tmask, __float_as_uint(__ldcs(w + k)));
+        }
+        __syncwarp();
+        for (uint64_t k0 = b; k0 < e; k0 += 32u) {
+            const uint64_t k = k0 + lane;
+            if (k < e) my[(uint32_t)((base + (uint64_t)__ldg(col + k)) >> tile_bits)] = 0u;
+        }
+        __syncthreads();
+    }
+}
+
+// ---------------------------------------------------------------- fold ----
+// CTA per tile (grid-stride over tiles). Warp w owns the tile's targets
+// [w*T/8, (w+1)*T/8); every warp reads each window of events and applies
+// its own targets' events in order.
+__global__ void __launch_bounds__(kBfThreads) binfold_fold_kernel(const uint2 *__restrict__ bins,
+                                                                  const uint32_t *__restrict__ offs, uint32_t tiles,
+                                                                  uint32_t grid_count, uint32_t tile_bits,
+                                                                  uint64_t n_local, float *__restrict__ next,
+                                                                  DevCounters *ctr, int parity,
+                                                                  unsigned long long gate) {
+    extern __shared__ __align__(16) unsigned char s_raw[];
+    const uint32_t T = 1u << tile_bits;
+    float *acc = reinterpret_cast<float *>(s_raw);
+    uint2 *win = reinterpret_cast<uint2 *>(s_raw + (size_t)T * 4);
+    if (dense_step(ctr, parity, gate)) return;
+    const unsigned lane = lane_id(), warp = threadIdx.x >> 5;
+    const uint32_t owner_shift = tile_bits - 3;
+    const uint64_t G = grid_count;
+    for (uint32_t tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
+        for (uint32_t t = threadIdx.x; t < T; t += kBfThreads) acc[t] = 0.0f;
+        const uint64_t lo = offs[(uint64_t)tile * G];
+        const uint64_t hi = offs[(uint64_t)(tile + 1) * G];
+        __syncthreads();
+        for (uint64_t w0 = lo; w0 < hi; w0 += kFoldWindow) {
+            const uint32_t nwin = (uint32_t)min((uint64_t)kFoldWindow, hi - w0);
+            for (uint32_t i = threadIdx.x; i < nwin; i += kBfThreads) win[i] = __ldcs(bins + w0 + i);
+            __syncthreads();
+            for (uint32_t i0 = 0; i0 < nwin; i0 += 32u) {
+                const uint32_t i = i0 + lane;
+                const uint2 ev = i < nwin ? win[i] : make_uint2(0u, 0u);
+                const bool own = i < nwin && (ev.x >> owner_shift) == warp;
+                if (!__any_sync(kFull, own)) continue;
+                const uint32_t peers = __match_any_sync(kFull, own ? ev.x : (0x80000000u | lane));
+                const int rank = __popc(peers & lanemask_lt());
+                const int rounds = (int)__reduce_max_sync(kFull, own ? (uint32_t)__popc(peers) : 0u);
+                for (int r = 0; r < rounds; ++r) {
+                    if (own && rank == r) acc[ev.x] = __fadd_rn(acc[ev.x], __uint_as_float(ev.y));
+                    __syncwarp();
+                }
+            }
+            __syncthreads();
+        }
+        const uint64_t t0 = (uint64_t)tile << tile_bits;
+        const uint32_t nt = (uint32_t)min((uint64_t)T, n_local - t0);
+        for (uint32_t t = threadIdx.x; t < nt; t += kBfThreads) next[t0 + t] = acc[t];
+        __syncthreads();
+    }
+    if (blockIdx.x == 0 && threadIdx.x == 0) ctr->events += ctr->step_events[parity];
+    step_epilogue(ctr, parity, 0, *(volatile uint32_t *)&ctr->list_count[parity]);
+}
+
+int fold_smem(uint32_t tile_bits) { return (int)(((size_t)4 << tile_bits) + (size_t)kFoldWindow * 8); }
+int scatter_smem(uint32_t tiles) { return (int)((size_t)tiles * (kBfWarps + 1) * 4); }
+
+template <typename K>
+void allow_smem(K kernel, int bytes) {
+    cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+}
+
+}  // namespace
+
+bool binfold_plan(int device, uint64_t n_local, BinFoldPlan *plan) {
+    // Tiles of 2^tile_bits targets, at most kBinFoldMaxTiles of them; a tile's
+    // sums (4 B each) plus a fold window must fit one CTA's shared memory.
+    uint32_t tb = 10;
+    while (tb < 15 && ((n_local + (1ull << tb) - 1) >> tb) > kBinFoldMaxTiles) ++tb;
+    const uint64_t tiles = (n_local + (1ull << tb) - 1) >> tb;
+    if (tiles > kBinFoldMaxTiles || tiles == 0) return false;
+    plan->tile_bits = tb;
+    plan->tiles = (uint32_t)tiles;
+    plan->grid = (uint32_t)sm_count(device) * 2u;
+    plan->hist_entries = (uint64_t)plan->tiles * plan->grid + 1;
+    plan->chunks = 0;
+    return true;
+}
+
+uint32_t binfold_chunks(uint64_t words) { return (uint32_t)((words + kChunkWords - 1) / kChunkWords); }
+
+cudaError_t binfold_scan(cudaStream_t s, const uint32_t *hist, uint32_t *offs, uint64_t n, void *temp,
+                         size_t *temp_bytes) {
+    return cub::DeviceScan::ExclusiveSum(temp, *temp_bytes, hist, offs, (int64_t)n, s);
+}
+
+void launch_compact_ordered(cudaStream_t s, int device, const uint32_t *bitmap, uint64_t words, uint32_t *ccnt,
+                            void *list, int idx_bits, DevCounters *ctr, int parity, uint64_t own_begin,
+                            uint64_t own_end, const uint64_t *row_ptr, uint64_t batch_rows, const PeerWait *wait) {
+    PeerWait pw{};
+    if (wait) pw = *wait;
+    const uint64_t chunks = binfold_chunks(words);
+    const int grid = (int)std::max<uint64_t>(1, std::min<uint64_t>(chunks, (uint64_t)sm_count(device) * 8));
+    chunk_counts_kernel<<<grid, kBfThreads, 0, s>>>(bitmap, words, ccnt, ctr, own_begin, own_end, pw);
+    if (idx_bits == 32)
+        compact_ordered_kernel<uint32_t><<<grid, kBfThreads, 0, s>>>(bitmap, words, ccnt, (uint32_t *)list, ctr,
+                                                                     parity, row_ptr, batch_rows);
+    else
+        compact_ordered_kernel<uint64_t><<<grid, kBfThreads, 0, s>>>(bitmap, words, ccnt, (uint64_t *)list, ctr,
+                                                                     parity, row_ptr, batch_rows);
+}
+
+cudaError_t launch_binfold(cudaStream_t s, int device, const BinFoldPlan &p, const BinFoldBuffers &buf,
+                           const void *list, int idx_bits, const uint64_t *row_ptr, const void *col, int col_bits,
+                           const float *w, uint64_t batch_rows, uint64_t n_local, float *next, DevCounters *ctr,
+                           int parity, unsigned long long gate) {
+    static std::mutex mu;
+    static bool attr_done[64] = {};
+    const int ssm = scatter_smem(p.tiles), fsm = fold_smem(p.tile_bits);
+#define B200_BF(TI, TC)                                                                                          \
+    do {                                                                                                         \
+        {                                                                                                        \
+            std::lock_guard<std::mutex> lock(mu);                                                                \
+            if (device >= 0 && device < 64 && !attr_done[device]) {                                             \
+                allow_smem(binfold_scatter_kernel<uint32_t, uint32_t>, scatter_smem(kBinFoldMaxTiles));           \
+                allow_smem(binfold_scatter_kernel<uint32_t, uint64_t>, scatter_smem(kBinFoldMaxTiles));           \
+                allow_smem(binfold_scatter_kernel<uint64_t, uint32_t>, scatter_smem(kBinFoldMaxTiles));           \
+                allow_smem(binfold_scatter_kernel<uint64_t, uint64_t>, scatter_smem(kBinFoldMaxTiles));           \
+                allow_smem(binfold_fold_kernel, fold_smem(15));                                                  \
+                attr_done[device] = true;                                                                        \
+            }                                                                                                    \
+        }                                                                                                        \
+        binfold_count_kernel<TI, TC><<<p.grid, kBfThreads, (size_t)p.tiles * 4, s>>>(                            \
+            (const TI *)list, ctr, parity, row_ptr, (const TC *)col, batch_rows, p.tile_bits, p.tiles, buf.hist, \
+            gate);                                                                                               \
+        size_t tb = buf.scan_bytes;                                                                              \
+        const cudaError_t e = binfold_scan(s, buf.hist, buf.offs, p.hist_entries, buf.scan_temp, &tb);           \
+        if (e != cudaSuccess) return e;                                                                          \
+        binfold_scatter_kernel<TI, TC><<<p.grid, kBfThreads, ssm, s>>>(                                          \
+            (const TI *)list, ctr, parity, row_ptr, (const TC *)col, w, batch_rows, p.tile_bits, p.tiles,        \
+            buf.offs, buf.bins, gate);                                                                           \
+    } while (0)
+    if (idx_bits == 32 && col_bits == 32) B200_BF(uint32_t, uint32_t);
+    else if (idx_bits == 32) B200_BF(uint32_t, uint64_t);
+    else if (col_bits == 32) B200_BF(uint64_t, uint32_t);
+    else B200_BF(uint64_t, uint64_t);
+#undef B200_BF
+    int per_sm = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, binfold_fold_kernel, kBfThreads, fsm) != cudaSuccess ||
+        per_sm <= 0)
+        per_sm = 1;
+    const int grid = (int)std::min<uint64_t>(p.tiles, (uint64_t)sm_count(device) * per_sm);
+    binfold_fold_kernel<<<grid, kBfThreads, fsm, s>>>(buf.bins, buf.offs, p.tiles, p.grid, p.tile_bits, n_local,
+                                                       next, ctr, parity, gate);
+    return cudaGetLastError();
+}
+
+}  // namespace b200

@@ -35,6 +35,7 @@ __device__ __forceinline__ void step_epilogue(DevCounters *ctr, int parity, int 
                                               int pulled = 0) {
     if (blockIdx.x == 0 && threadIdx.x == 0) {
         ctr->list_count[parity ^ 1] = 0u;
+        ctr->step_events[parity ^ 1] = 0ull;
         if (count_spikes) ctr->spikes += count;
         if (pulled) ctr->pull_spikes += count;
         if (ctr->kind_log) ctr->kind_log[ctr->step_seq % kStepLog] = (uint8_t)(pulled != 0);

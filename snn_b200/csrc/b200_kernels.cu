@@ -115,6 +115,8 @@ __global__ void init_state_kernel(uint64_t n, float v_rest, float *v, float *cur
         ctr->wait_ns = 0ull;
         ctr->wait_max_ns = 0ull;
         ctr->kind_log = kind_log;
+        ctr->step_events[0] = 0ull;
+        ctr->step_events[1] = 0ull;
     }
 }
 
@@ -555,9 +557,11 @@ __global__ void __launch_bounds__(256) propagate_pull_kernel(uint64_t n_local, c
                                                              float *__restrict__ next, const TIdx *__restrict__ list,
                                                              const uint32_t *__restrict__ out_degree,
                                                              DevCounters *ctr, int parity, int count_spikes,
-                                                             uint32_t pull_above) {
+                                                             uint32_t pull_above, int events_gate,
+                                                             unsigned long long events_above) {
     const uint32_t count = *(volatile uint32_t *)&ctr->list_count[parity];
     if (pull_above && count <= pull_above) return;  // sparse step: the push kernel runs
+    if (events_gate && *(volatile unsigned long long *)&ctr->step_events[parity] <= events_above) return;
     const unsigned lane = lane_id();
     const uint64_t gwarp = ((uint64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const uint64_t nwarps = ((uint64_t)gridDim.x * blockDim.x) >> 5;
@@ -615,10 +619,12 @@ __global__ void __launch_bounds__(kPullSmemThreads, 1)
                                const uint64_t *__restrict__ sell_off, const uint2 *__restrict__ slots,
                                const uint32_t *__restrict__ bitmap, uint64_t words, float *__restrict__ next,
                                const TIdx *__restrict__ list, const uint32_t *__restrict__ out_degree,
-                               DevCounters *ctr, int parity, int count_spikes, uint32_t pull_above) {
+                               DevCounters *ctr, int parity, int count_spikes, uint32_t pull_above,
+                               int events_gate, unsigned long long events_above) {
     extern __shared__ __align__(16) uint32_t s_bits[];  // chunk_words + 1 (the last word: zero, for padding)
     const uint32_t count = *(volatile uint32_t *)&ctr->list_count[parity];
     if (pull_above && count <= pull_above) return;  // sparse step: the push kernel runs
+    if (events_gate && *(volatile unsigned long long *)&ctr->step_events[parity] <= events_above) return;
     const unsigned lane = lane_id();
     const unsigned warp = threadIdx.x >> 5;
     const uint64_t blocks = (n_local + 31) / 32;
@@ -1166,7 +1172,8 @@ uint64_t pull_chunk_neurons() { return pull_chunk_words() * 32u; }
 void launch_propagate_pull(cudaStream_t s, int device, uint64_t n_local, uint32_t chunks, uint64_t chunk_words,
                            const uint64_t *sell_off, const uint2 *slots, const uint32_t *bitmap, uint64_t words,
                            float *next, const void *list, int idx_bits, const uint32_t *out_degree, DevCounters *ctr,
-                           int parity, int count_spikes, uint32_t pull_above) {
+                           int parity, int count_spikes, uint32_t pull_above, int events_gate,
+                           unsigned long long events_above) {
     if ((uint64_t)chunks * chunk_words >= words) {
         // Chunked layout: shared-memory spike bits.
         const uint64_t blocks = (n_local + 31) / 32;
@@ -1184,7 +1191,7 @@ void launch_propagate_pull(cudaStream_t s, int device, uint64_t n_local, uint32_
         }                                                                                                       \
         propagate_pull_smem_kernel<TI><<<grid, kPullSmemThreads, smem, s>>>(                                    \
             n_local, chunks, chunk_words, sell_off, slots, bitmap, words, next, (const TI *)list, out_degree,   \
-            ctr, parity, count_spikes, pull_above);                                                             \
+            ctr, parity, count_spikes, pull_above, events_gate, events_above);                                  \
     } while (0)
         if (idx_bits == 32) B200_PULLS(uint32_t);
         else B200_PULLS(uint64_t);
@@ -1196,11 +1203,11 @@ void launch_propagate_pull(cudaStream_t s, int device, uint64_t n_local, uint32_
     if (idx_bits == 32)
         propagate_pull_kernel<uint32_t><<<grid, 256, 0, s>>>(n_local, sell_off, slots, bitmap, next,
                                                              (const uint32_t *)list, out_degree, ctr, parity,
-                                                             count_spikes, pull_above);
+                                                             count_spikes, pull_above, events_gate, events_above);
     else
         propagate_pull_kernel<uint64_t><<<grid, 256, 0, s>>>(n_local, sell_off, slots, bitmap, next,
                                                              (const uint64_t *)list, out_degree, ctr, parity,
-                                                             count_spikes, pull_above);
+                                                             count_spikes, pull_above, events_gate, events_above);
 }
 
 __global__ void set_u64_kernel(unsigned long long *p, unsigned long long v) { *p = v; }

@@ -47,6 +47,7 @@ struct DevCounters {
     unsigned long long wait_ns;
     unsigned long long wait_max_ns;
     uint8_t *kind_log;
+    unsigned long long step_events[2];  // ordered compaction: events of the step of each parity
 };
 static_assert(sizeof(DevCounters) <= 256, "DevCounters must fit its 256-byte block");
 
@@ -97,39 +98,6 @@ struct GenParams {
     uint64_t ldraw[16];
 };
 
-// Geometry and buffers of the binned push propagation (b200_binned.cu).
-constexpr uint32_t kMaxBinPasses = 4;
-struct BinLayout {
-    uint2 *bins;              // [nb][grid dest][grid src][cap] (offset in tile, weight bits)
-    uint32_t *counts;         // [nb][grid dest][grid src] entries per sub-bin, published per round
-    unsigned long long *sync; // [0] router rounds finished, [1] drain rounds finished (x grid)
-    const uint64_t *row_ptr[kMaxBinPasses];  // per pass: CSR over all rows, edges into the pass only
-    const uint32_t *col[kMaxBinPasses];      // per pass: target ids relative to pass_lo
-    const float *w[kMaxBinPasses];
-    uint64_t pass_lo[kMaxBinPasses];         // first local target of each pass
-    uint64_t pass_len[kMaxBinPasses];        // targets of each pass
-    uint32_t passes;
-    uint32_t grid;            // persistent CTAs = target tiles (one per SM)
-    uint32_t nb;              // bin buffers (routers run up to nb-1 rounds ahead)
-    uint32_t tile;            // targets per tile
-    uint64_t div_magic;       // ceil(2^40 / tile): t / tile == (t * div_magic) >> 40 for t < 2^24
-    uint32_t rows_per_cta;    // spiking rows each CTA routes per round
-    uint32_t cap;             // capacity of one sub-bin; overflow falls back to red.global
-    uint32_t smem_bytes;      // dynamic shared memory per CTA
-    uint32_t spin_limit;      // polls before a cross-CTA wait is declared failed
-    unsigned long long *prof; // optional [grid][16] clock64 totals per role/section (diagnostics)
-};
-
-// Fills the geometry for n_local targets (buffers and CSR pointers left
-// unset); false when the device cannot run it. force_passes > 0 asks for at
-// least that many passes.
-bool binned_layout(int device, uint64_t n_local, uint64_t e_local, uint64_t n_rows, uint32_t force_passes,
-                   BinLayout *layout);
-// True when the cooperative grid of this layout is resident on the device.
-bool binned_fits(int device, const BinLayout &layout);
-cudaError_t launch_propagate_binned(cudaStream_t s, const void *list, int idx_bits, float *next, DevCounters *ctr,
-                                    int parity, int count_spikes, const BinLayout &layout);
-
 // Number of SMs of the current device (cached per device).
 int sm_count(int device);
 
@@ -169,6 +137,8 @@ void launch_propagate_push(cudaStream_t s, int device, const void *list, int idx
 // chunk over a larger bitmap) ids are global, padding id all ones, lookups
 // through L1/L2. pull_above != 0: a push kernel launched with the same gate
 // handles steps of at most pull_above spikes; the pull runs only above it.
+// events_gate != 0: the kernel runs only if ctr->step_events[parity] (the
+// ordered compaction's event total) exceeds events_above.
 // The layout's chunk size is fixed when it is built: pull_chunk_words() then.
 uint64_t pull_chunk_words();
 uint32_t pull_chunks(uint64_t words);
@@ -176,7 +146,8 @@ uint64_t pull_chunk_neurons();
 void launch_propagate_pull(cudaStream_t s, int device, uint64_t n_local, uint32_t chunks, uint64_t chunk_words,
                            const uint64_t *sell_off, const uint2 *slots, const uint32_t *bitmap, uint64_t words,
                            float *next, const void *list, int idx_bits, const uint32_t *out_degree, DevCounters *ctr,
-                           int parity, int count_spikes, uint32_t pull_above = 0);
+                           int parity, int count_spikes, uint32_t pull_above = 0, int events_gate = 0,
+                           unsigned long long events_above = 0);
 void launch_fill_u2(cudaStream_t s, int device, uint2 *p, uint64_t n, uint32_t x, uint32_t y);
 // *p = v, in stream order.
 void launch_set_u64(cudaStream_t s, unsigned long long *p, unsigned long long v);

@@ -18,6 +18,7 @@
 //  * sharded contexts (extension) own a contiguous range of postsynaptic
 //    neurons and all-gather the spike bitmap with NCCL every step.
 #include "snn_b200.h"
+#include "b200_binfold.h"
 #include "b200_kernels.h"
 #include "b200_network.h"
 
@@ -106,7 +107,7 @@ struct snn_cuda_context {
     float *d_ext = nullptr;
     bool ext_held = false;  // snn_b200_set_external: d_ext applies to every step without its own
     uint64_t inject_range = 0;  // snn_b200_set_stream_range: stream indices drawn in [0, range); 0 = all
-    // run_stream_async on unsharded push contexts replays a captured CUDA
+    // run_stream_async on unsharded push and bin-fold contexts replays a captured CUDA
     // graph of two steps (one per parity); the injection step index then
     // lives on the device (DevCounters::stream_step, advanced by LIF).
     bool dev_stream_step = false;
@@ -126,15 +127,6 @@ struct snn_cuda_context {
     void *d_col = nullptr;
     float *d_w = nullptr;
 
-    bool binned = false;
-    b200::BinLayout bin{};
-    void *d_bin_mem = nullptr;
-    // Binned push with more than one target pass keeps one CSR slice per
-    // pass (edges into the pass only, columns relative to the pass start).
-    uint32_t passes = 1;
-    uint64_t *d_prow[b200::kMaxBinPasses] = {};
-    void *d_pcol[b200::kMaxBinPasses] = {};
-    float *d_pw[b200::kMaxBinPasses] = {};
     uint32_t *h_err = nullptr;  // pinned copy of DevCounters::error
 
     uint64_t *d_col_ptr = nullptr;
@@ -160,6 +152,14 @@ struct snn_cuda_context {
     void *d_otemp = nullptr;
     size_t otemp_bytes = 0;
     unsigned long long *h_ototal = nullptr;
+    // ORDERED through the bin-fold (the default ORDERED propagation): ordered
+    // compaction, per-tile counts, stable scatter and shared-memory fold, all
+    // gated on the device against the pull for steps above bf_gate events.
+    bool binfold = false;
+    b200::BinFoldPlan bf{};
+    b200::BinFoldBuffers bfb{};
+    uint64_t bf_cap = 0;
+    unsigned long long bf_gate = 0;
 
     std::vector<StreamChunk> chunks;
     // Sharded STREAMING: the rank's slice of the host CSR (local target ids),
@@ -243,35 +243,12 @@ uint64_t ceil_div(uint64_t a, uint64_t b) { return (a + b - 1) / b; }
 using b200host::lif_valid;
 using b200host::validate_csr;
 
-// SNN_B200_BINNED_PROFILE: print the binned kernel's per-role cycle totals
-// (summed over CTAs, in ms at the current SM clock) when a context is freed.
-void report_binned_profile(snn_cuda_context_t *c) {
-    if (!c->bin.prof) return;
-    std::vector<unsigned long long> h((size_t)c->bin.grid * 16);
-    cudaStreamSynchronize(c->stream);
-    if (cudaMemcpy(h.data(), c->bin.prof, h.size() * 8, cudaMemcpyDeviceToHost) != cudaSuccess) return;
-    int khz = 0;
-    cudaDeviceGetAttribute(&khz, cudaDevAttrClockRate, c->device);
-    const char *names[11] = {"rprod_wait_empty", "rprod_total", "rcons_wait_drained", "rcons_wait_full",
-                             "rcons_route", "rcons_flush", "dprod_wait_routed", "dprod_issue",
-                             "dcons_wait_full", "dcons_fold", "kernel"};
-    std::fprintf(stderr, "[snn_b200 binned profile] mean per CTA over %llu steps (ms):", (unsigned long long)c->step);
-    for (int k = 0; k < 11; ++k) {
-        double sum = 0;
-        for (uint32_t b = 0; b < c->bin.grid; ++b) sum += (double)h[(size_t)b * 16 + k];
-        std::fprintf(stderr, " %s=%.3f", names[k], khz ? sum / c->bin.grid / khz : 0.0);
-    }
-    std::fprintf(stderr, "\n");
-    cudaFree(c->bin.prof);
-}
-
 void free_context(snn_cuda_context_t *c) {
     if (c == nullptr) return;
     if (c->device >= 0) cudaSetDevice(c->device);
     if (c->stream) cudaStreamSynchronize(c->stream);
     if (c->copy_stream) cudaStreamSynchronize(c->copy_stream);
     if (c->spk_stream) cudaStreamSynchronize(c->spk_stream);
-    report_binned_profile(c);
     if (c->comm) ncclCommDestroy(c->comm);
     for (uint32_t r = 0; r < b200::kMaxPeers; ++r)
         if (c->peer_ipc[r]) cudaIpcCloseMemHandle(c->peer_x[r]);
@@ -279,14 +256,10 @@ void free_context(snn_cuda_context_t *c) {
     void *dev[] = {c->d_v, c->d_cur_pair, c->d_ext, c->d_refr, c->d_spikes, c->d_ws, c->d_row_ptr, c->d_col,
                    c->d_w, c->d_col_ptr, c->d_pre, c->d_cw, c->d_deg, c->d_sell_off, c->d_sdeg, c->d_eoff, c->d_okeys[0], c->d_okeys[1], c->d_ovals[0], c->d_ovals[1], c->d_otemp,
                    c->d_chunk_row, c->d_chunk_col,
-                   c->d_chunk_w, c->d_inj_idx, c->d_inj_val, c->d_bin_mem};
+                   c->d_chunk_w, c->d_inj_idx, c->d_inj_val, c->bfb.hist, c->bfb.offs,
+                   c->bfb.bins, c->bfb.ccnt, c->bfb.scan_temp};
     for (void *p : dev)
         if (p) cudaFree(p);
-    for (uint32_t p = 1; p < b200::kMaxBinPasses; ++p) {
-        if (c->d_prow[p]) cudaFree(c->d_prow[p]);
-        if (c->d_pcol[p]) cudaFree(c->d_pcol[p]);
-        if (c->d_pw[p]) cudaFree(c->d_pw[p]);
-    }
     if (c->h_err) cudaFreeHost(c->h_err);
     if (c->h_ototal) cudaFreeHost(c->h_ototal);
     if (c->h_inj_idx) cudaFreeHost(c->h_inj_idx);
@@ -338,7 +311,8 @@ snn_status_t apply_options(snn_cuda_context_t *c, uint64_t n, const snn_b200_opt
     if (o.streaming != SNN_B200_STREAMING_CHUNKED && o.streaming != SNN_B200_STREAMING_SPARSE)
         return SNN_ERR_INVALID_ARGUMENT;
     c->streaming = o.streaming;
-    c->propagation = o.propagation;
+    // The binned push is the bin-fold, which keeps CSR order: ORDERED.
+    c->propagation = o.propagation == SNN_B200_PROPAGATE_PUSH_BINNED ? SNN_B200_PROPAGATE_ORDERED : o.propagation;
     c->opull = o.propagation == SNN_B200_PROPAGATE_ORDERED && std::getenv("SNN_B200_ORDERED_PULL") != nullptr;
     c->world = o.world_size;
     c->rank = o.rank;
@@ -349,9 +323,9 @@ snn_status_t apply_options(snn_cuda_context_t *c, uint64_t n, const snn_b200_opt
     const uint64_t batch = o.batch ? o.batch : 1;
     if (batch > 1) {
         if (o.world_size != 1 || o.streaming != SNN_B200_STREAMING_CHUNKED ||
-            (o.propagation != SNN_B200_PROPAGATE_PUSH && o.propagation != SNN_B200_PROPAGATE_PUSH_ATOMIC &&
-             o.propagation != SNN_B200_PROPAGATE_ORDERED) ||
-            (o.propagation == SNN_B200_PROPAGATE_ORDERED && c->opull))
+            (c->propagation != SNN_B200_PROPAGATE_PUSH && c->propagation != SNN_B200_PROPAGATE_PUSH_ATOMIC &&
+             c->propagation != SNN_B200_PROPAGATE_ORDERED) ||
+            (c->propagation == SNN_B200_PROPAGATE_ORDERED && c->opull))
             return SNN_ERR_UNSUPPORTED;
         if (n > UINT64_MAX / batch) return SNN_ERR_OVERFLOW;
     }
@@ -409,54 +383,6 @@ snn_status_t create_streams(snn_cuda_context_t *c) {
     if (cudaMallocHost(&c->h_err, sizeof(uint32_t)) != cudaSuccess) return SNN_ERR_OUT_OF_MEMORY;
     *c->h_err = 0;
     return SNN_OK;
-}
-
-// Whether SNN_B200_PROPAGATE_PUSH picks the binned kernel (when it can run)
-// rather than the atomic one; set from the measured step times on B200.
-constexpr bool kAutoBinned = false;
-
-// Binned push (b200_binned.cu) for FULL push contexts with 32-bit columns.
-// plan_binned decides, before the topology is built, whether the binned
-// kernel runs and with how many target passes (each pass then gets its own
-// CSR slice); finish_binned allocates the bins once the slices exist.
-// SNN_B200_BINNED_PASSES (environment) forces a minimum pass count, for tests.
-void plan_binned(snn_cuda_context_t *c, uint64_t e_estimate) {
-    c->binned = false;
-    c->passes = 1;
-    const bool want = c->propagation == SNN_B200_PROPAGATE_PUSH_BINNED ||
-                      (c->propagation == SNN_B200_PROPAGATE_PUSH && kAutoBinned);
-    if (!want || c->mode != SNN_CUDA_MODE_FULL || c->col_bits != 32) return;
-    uint32_t force = 0;
-    if (const char *env = std::getenv("SNN_B200_BINNED_PASSES")) force = (uint32_t)std::atoi(env);
-    if (!b200::binned_layout(c->device, c->n_local, e_estimate, c->n_global, force, &c->bin) ||
-        !b200::binned_fits(c->device, c->bin))
-        return;
-    c->binned = true;
-    c->passes = c->bin.passes;
-}
-
-snn_status_t finish_binned(snn_cuda_context_t *c) {
-    if (!c->binned) return SNN_OK;
-    b200::BinLayout &L = c->bin;
-    for (uint32_t p = 0; p < L.passes; ++p) {
-        L.row_ptr[p] = p == 0 ? c->d_row_ptr : c->d_prow[p];
-        L.col[p] = (const uint32_t *)(p == 0 ? c->d_col : c->d_pcol[p]);
-        L.w[p] = p == 0 ? c->d_w : c->d_pw[p];
-    }
-    const uint64_t subs = (uint64_t)L.nb * L.grid * L.grid;
-    const uint64_t counts_bytes = ((subs * 4 + 255) / 256) * 256;
-    const uint64_t bytes = 256 + counts_bytes + subs * L.cap * 8ull;
-    snn_status_t st = dmalloc(&c->d_bin_mem, bytes, 1);
-    if (st != SNN_OK) return st;
-    L.sync = (unsigned long long *)c->d_bin_mem;
-    L.counts = (uint32_t *)((char *)c->d_bin_mem + 256);
-    L.bins = (uint2 *)((char *)c->d_bin_mem + 256 + counts_bytes);
-    if ((st = cuda_status(cudaMemsetAsync(c->d_bin_mem, 0, 256 + counts_bytes, c->stream))) != SNN_OK) return st;
-    if (std::getenv("SNN_B200_BINNED_PROFILE")) {
-        if (cudaMalloc(&L.prof, (size_t)L.grid * 16 * 8) != cudaSuccess) return SNN_ERR_CUDA;
-        cudaMemsetAsync(L.prof, 0, (size_t)L.grid * 16 * 8, c->stream);
-    }
-    return cuda_status(cudaStreamSynchronize(c->stream));
 }
 
 // Offsets inside the peer exchange buffer.
@@ -559,22 +485,12 @@ snn_status_t upload_push_range(snn_cuda_context_t *c, const snn_network_t *net, 
     return cuda_status(cudaStreamSynchronize(c->stream));
 }
 
-// FULL push topology from a host network: the rank's range, or one slice per
-// binned target pass.
+// FULL push topology from a host network: the edges into the rank's range.
 snn_status_t upload_full_push(snn_cuda_context_t *c, const snn_network_t *net) {
-    const uint64_t e_est = (uint64_t)((double)net->synapse_count * ((double)c->n_local / (double)c->n_global));
-    plan_binned(c, e_est);
-    snn_status_t st = SNN_OK;
-    c->e_local = 0;
-    for (uint32_t p = 0; p < c->passes && st == SNN_OK; ++p) {
-        const uint64_t rlo = c->passes > 1 ? c->lo + c->bin.pass_lo[p] : c->lo;
-        const uint64_t rhi = c->passes > 1 ? rlo + c->bin.pass_len[p] : std::min(c->hi, c->n_rows);
-        uint64_t e = 0;
-        st = p == 0 ? upload_push_range(c, net, rlo, rhi, &c->d_row_ptr, &c->d_col, &c->d_w, &e)
-                    : upload_push_range(c, net, rlo, rhi, &c->d_prow[p], &c->d_pcol[p], &c->d_pw[p], &e);
-        c->e_local += e;
-    }
-    if (st == SNN_OK) st = finish_binned(c);
+    uint64_t e = 0;
+    const snn_status_t st =
+        upload_push_range(c, net, c->lo, std::min(c->hi, c->n_rows), &c->d_row_ptr, &c->d_col, &c->d_w, &e);
+    c->e_local = e;
     return st;
 }
 
@@ -635,6 +551,65 @@ snn_status_t setup_ordered_push(snn_cuda_context_t *c) {
     c->otemp_bytes = std::max({a, b, (size_t)256});
     if (cudaMalloc(&c->d_otemp, c->otemp_bytes) != cudaSuccess) return fail("out of device memory for sort scratch");
     return cuda_status(cudaStreamSynchronize(c->stream));
+}
+
+// Bin-fold buffers (b200_binfold.cu). Returns false (nothing allocated)
+// when the bin-fold cannot serve this context: too many local targets for its
+// tiles, or, without a pull topology for dense steps, too little memory for
+// an event array as large as the local synapses. SNN_B200_ORDERED_SORT
+// (environment) keeps the event-sort propagation, for tests.
+bool setup_binfold(snn_cuda_context_t *c) {
+    if (std::getenv("SNN_B200_ORDERED_SORT") != nullptr) return false;
+    b200::BinFoldPlan plan{};
+    if (!b200::binfold_plan(c->device, c->n_local, &plan)) return false;
+    plan.chunks = b200::binfold_chunks(c->bitmap_words);
+    size_t free_b = 0, total_b = 0;
+    if (cudaMemGetInfo(&free_b, &total_b) != cudaSuccess) return false;
+    const uint64_t fixed = plan.hist_entries * 8 + (uint64_t)plan.chunks * 4 + (64ull << 20);
+    const uint64_t margin = 512ull << 20;
+    if (free_b < fixed + margin) return false;
+    const uint64_t all = c->e_local * c->batch;
+    uint64_t cap = std::min<uint64_t>(all, (free_b - fixed - margin) / 8);
+    cap = std::min<uint64_t>(cap, 0xffffffffull);  // 32-bit slot offsets
+    if (const char *env = std::getenv("SNN_B200_ORDERED_CAP")) {  // tests: dense steps at a low count
+        const uint64_t v = std::strtoull(env, nullptr, 10);
+        if (v) cap = std::min(cap, v);
+    }
+    if (!c->has_csc && cap < all) return false;
+    uint64_t gate = cap;
+    if (c->has_csc && c->pull_div) gate = std::min<uint64_t>(cap, all / c->pull_div);
+    b200::BinFoldBuffers b{};
+    size_t scan_bytes = 0;
+    b200::binfold_scan(c->stream, nullptr, nullptr, plan.hist_entries, nullptr, &scan_bytes);
+    if (cudaMalloc(&b.hist, plan.hist_entries * 4) != cudaSuccess ||
+        cudaMalloc(&b.offs, plan.hist_entries * 4) != cudaSuccess ||
+        cudaMalloc(&b.ccnt, (uint64_t)plan.chunks * 4 + 4) != cudaSuccess ||
+        cudaMalloc(&b.scan_temp, std::max<size_t>(scan_bytes, 256)) != cudaSuccess ||
+        (cap && cudaMalloc(&b.bins, cap * 8) != cudaSuccess)) {
+        cudaGetLastError();
+        for (void *p : {(void *)b.hist, (void *)b.offs, (void *)b.ccnt, b.scan_temp, (void *)b.bins})
+            if (p) cudaFree(p);
+        return false;
+    }
+    b.scan_bytes = std::max<size_t>(scan_bytes, 256);
+    // The last hist entry is never written: the scan's total lands in offs.
+    cudaMemsetAsync(b.hist, 0, plan.hist_entries * 4, c->stream);
+    if (cudaStreamSynchronize(c->stream) != cudaSuccess) return false;
+    c->bf = plan;
+    c->bfb = b;
+    c->bf_cap = cap;
+    c->bf_gate = gate;
+    c->binfold = true;
+    return true;
+}
+
+// ORDERED propagation set-up after the push CSR (and the pull topology, when
+// there is room) exist: the bin-fold, else the event sort.
+snn_status_t setup_ordered(snn_cuda_context_t *c) {
+    if (setup_binfold(c)) return SNN_OK;
+    // The event sort costs more per event: its dense-step bound is lower.
+    if (std::getenv("SNN_B200_ORDERED_PULL_DIV") == nullptr && c->pull_div) c->pull_div = 10;
+    return setup_ordered_push(c);
 }
 
 // One ordered push propagation (b200_kernels.cu describes the steps); one
@@ -1142,9 +1117,12 @@ snn_status_t enqueue_step(snn_cuda_context_t *c, bool has_ext) {
     }
     b200::LifArgs lif_args = c->args;
     if (c->dev_stream_step) lif_args.stream_step = &c->d_ctr->stream_step;
+    // The bin-fold needs an ascending spike list: the ordered compaction
+    // below builds it from the bitmap, so LIF writes no list then.
+    const bool ordered_list = c->binfold && c->mode == SNN_CUDA_MODE_FULL;
     b200::launch_lif(c->stream, c->device, c->n_local, lif_args, c->d_v, cur, has_ext ? c->d_ext : nullptr, c->d_refr,
-                     c->d_spikes, own_bitmap, sharded ? nullptr : c->d_list, c->idx_bits, c->lo, c->d_ctr, parity,
-                     peer ? &pa : nullptr);
+                     c->d_spikes, own_bitmap, (sharded || ordered_list) ? nullptr : c->d_list, c->idx_bits, c->lo,
+                     c->d_ctr, parity, peer ? &pa : nullptr);
     snn_status_t st = check_launch(c);
     if (st != SNN_OK) return st;
     timing_mark(c, tg, 1);
@@ -1159,7 +1137,27 @@ snn_status_t enqueue_step(snn_cuda_context_t *c, bool has_ext) {
             return SNN_ERR_CUDA;
         cudaEventRecord(c->ev_spk, c->spk_stream);
     }
-    if (peer) {
+    const uint64_t brows = c->batch > 1 ? c->n_rows : 0;
+    if (ordered_list) {
+        // Ascending spike list (and the step's event total) from the bitmap:
+        // assembled by the peer stores (after the flag waits), by the NCCL
+        // all-gather, or this rank's own.
+        const b200::PeerWait pw{peer ? (const unsigned long long *)((char *)c->d_xbuf + xflags_offset(c)) : nullptr,
+                                c->xstep, peer ? c->world : 0u, c->peer_spin_limit};
+        if (sharded && !peer) {
+            const ncclResult_t r =
+                ncclAllGather(own_bitmap, c->d_bitmap, c->slot / 32, ncclUint32, c->comm, c->stream);
+            if (r != ncclSuccess) {
+                set_error("ncclAllGather", ncclGetErrorString(r));
+                return SNN_ERR_CUDA;
+            }
+        }
+        b200::launch_compact_ordered(c->stream, c->device, peer ? xbitmap : c->d_bitmap, c->bitmap_words,
+                                     c->bfb.ccnt, c->d_list, c->idx_bits, c->d_ctr, parity, c->lo / 32,
+                                     ceil_div(c->hi, 32), c->d_row_ptr, brows, peer ? &pw : nullptr);
+        c->launches += 2;
+        if ((st = cuda_status(cudaGetLastError())) != SNN_OK) return st;
+    } else if (peer) {
         // LIF already stored this rank's words into every rank's buffer and
         // raised its flag; the compaction waits for all flags of this step.
         const b200::PeerWait pw{(const unsigned long long *)((char *)c->d_xbuf + xflags_offset(c)), c->xstep,
@@ -1182,18 +1180,28 @@ snn_status_t enqueue_step(snn_cuda_context_t *c, bool has_ext) {
     }
     timing_mark(c, tg, 2);
     if (c->mode == SNN_CUDA_MODE_FULL) {
-        if (c->propagation == SNN_B200_PROPAGATE_ORDERED && !c->opull) {
+        if (c->binfold) {
+            const cudaError_t e = b200::launch_binfold(c->stream, c->device, c->bf, c->bfb, c->d_list, c->idx_bits,
+                                                       c->d_row_ptr, c->d_col, c->col_bits, c->d_w, brows,
+                                                       c->n_local, next, c->d_ctr, parity, c->bf_gate);
+            c->launches += 5;  // count, scan (two), scatter, fold
+            if (e != cudaSuccess) return cuda_status(e);
+            if (c->has_csc) {
+                // Dense steps (more than bf_gate events) take the pull instead.
+                b200::launch_propagate_pull(c->stream, c->device, c->n_local, c->sell_chunks, c->sell_chunk_words,
+                                            c->d_sell_off, (const uint2 *)c->d_pre, peer ? xbitmap : c->d_bitmap,
+                                            c->bitmap_words, next, c->d_list, c->idx_bits, c->d_deg, c->d_ctr,
+                                            parity, 0, 0, 1, c->bf_gate);
+                c->launches++;
+            }
+        } else if (c->propagation == SNN_B200_PROPAGATE_ORDERED && !c->opull) {
             if ((st = ordered_push_step(c, parity, next, sharded, peer ? xbitmap : c->d_bitmap)) != SNN_OK) return st;
         } else if (c->propagation == SNN_B200_PROPAGATE_ORDERED)
             b200::launch_propagate_pull(c->stream, c->device, c->n_local, c->sell_chunks, c->sell_chunk_words,
                                     c->d_sell_off, (const uint2 *)c->d_pre,
                                          peer ? xbitmap : c->d_bitmap, c->bitmap_words, next, c->d_list, c->idx_bits,
                                         c->d_deg, c->d_ctr, parity, !sharded);
-        else if (c->binned) {
-            const cudaError_t e = b200::launch_propagate_binned(c->stream, c->d_list, c->idx_bits, next, c->d_ctr,
-                                                                parity, !sharded, c->bin);
-            if (e != cudaSuccess) return cuda_status(e);
-        } else {
+        else {
             // With a SELL CSC both kernels are launched behind the same
             // device-side gate on this step's spike count: one of them runs.
             b200::launch_propagate_push(c->stream, c->device, c->d_list, c->idx_bits, c->d_row_ptr, c->d_col,
@@ -1334,18 +1342,10 @@ snn_status_t generate_range(snn_cuda_context_t *c, const b200::GenParams &g, uin
 }
 
 snn_status_t generate_full(snn_cuda_context_t *c, const b200::GenParams &g, uint64_t e_total) {
-    plan_binned(c, (uint64_t)((double)e_total * ((double)c->n_local / (double)c->n_global)));
-    snn_status_t st = SNN_OK;
-    c->e_local = 0;
-    for (uint32_t p = 0; p < c->passes && st == SNN_OK; ++p) {
-        const uint64_t rlo = c->passes > 1 ? c->lo + c->bin.pass_lo[p] : c->lo;
-        const uint64_t rhi = c->passes > 1 ? rlo + c->bin.pass_len[p] : std::min(c->hi, c->n_rows);
-        uint64_t e = 0;
-        st = p == 0 ? generate_range(c, g, e_total, rlo, rhi, &c->d_row_ptr, &c->d_col, &c->d_w, &e)
-                    : generate_range(c, g, e_total, rlo, rhi, &c->d_prow[p], &c->d_pcol[p], &c->d_pw[p], &e);
-        c->e_local += e;
-    }
-    if (st == SNN_OK) st = finish_binned(c);
+    uint64_t e = 0;
+    const snn_status_t st =
+        generate_range(c, g, e_total, c->lo, std::min(c->hi, c->n_rows), &c->d_row_ptr, &c->d_col, &c->d_w, &e);
+    c->e_local = e;
     return st;
 }
 
@@ -1536,12 +1536,12 @@ snn_status_t build_generated_csc(snn_cuda_context_t *c, const b200::GenParams &g
 // gate so no host round trip is added. A divisor of 0 disables the pull.
 snn_status_t add_pull_topology(snn_cuda_context_t *c, const snn_network_t *net, const b200::GenParams *g) {
     const bool ordered = c->propagation == SNN_B200_PROPAGATE_ORDERED;
-    if (!ordered && (c->propagation != SNN_B200_PROPAGATE_PUSH || c->binned || c->mode != SNN_CUDA_MODE_FULL))
+    if (!ordered && (c->propagation != SNN_B200_PROPAGATE_PUSH || c->mode != SNN_CUDA_MODE_FULL))
         return SNN_OK;
     // Measured at config 2 on B200: the pull takes ~16 ms whatever the
     // firing; the ordered push costs about as much at ~1e9 events, the
     // atomic push at ~2.5e9 (25% firing at fanout 1000).
-    uint64_t div = ordered ? 10 : 4;
+    uint64_t div = ordered ? 3 : 4;
     if (const char *env = std::getenv(ordered ? "SNN_B200_ORDERED_PULL_DIV" : "SNN_B200_PUSH_PULL_DIV"))
         div = std::strtoull(env, nullptr, 10);
     c->pull_div = div;
@@ -1591,7 +1591,7 @@ snn_status_t finish_generated(snn_cuda_context_t *c, const b200::GenParams &g, u
     }
     else if (!c->opull) {
         if ((st = generate_full(c, g, e_total)) == SNN_OK && (st = add_pull_topology(c, nullptr, &g)) == SNN_OK)
-            st = setup_ordered_push(c);
+            st = setup_ordered(c);
     } else if (c->n_local > 0xffffffffull) st = SNN_ERR_UNSUPPORTED;  // 32-bit sort keys
     else st = build_generated_csc(c, g);
     if (st != SNN_OK) {
@@ -1605,11 +1605,12 @@ snn_status_t finish_generated(snn_cuda_context_t *c, const b200::GenParams &g, u
 uint64_t stream_range(const snn_cuda_context_t *c) { return c->inject_range ? c->inject_range : c->n_global; }
 
 // Launch-bound loops (small networks, quiet steps) pay a launch gap per
-// kernel; unsharded push contexts without device timing replay a captured
+// kernel; unsharded push and bin-fold contexts without device timing replay a captured
 // graph of two steps instead. SNN_B200_NO_GRAPHS (environment) disables it.
 bool graph_eligible(const snn_cuda_context_t *c) {
-    return c->world == 1 && c->mode == SNN_CUDA_MODE_FULL && c->propagation != SNN_B200_PROPAGATE_ORDERED &&
-           !c->binned && !c->timing && std::getenv("SNN_B200_NO_GRAPHS") == nullptr;
+    return c->world == 1 && c->mode == SNN_CUDA_MODE_FULL &&
+           (c->propagation != SNN_B200_PROPAGATE_ORDERED || c->binfold) && !c->timing &&
+           std::getenv("SNN_B200_NO_GRAPHS") == nullptr;
 }
 
 // One step of the injection stream with the step index read on the device.
@@ -1723,7 +1724,8 @@ snn_status_t snn_b200_create(const snn_network_t *network, const snn_cuda_config
     if (network == nullptr) return SNN_ERR_INVALID_ARGUMENT;
     const snn_cuda_config_t cfg = config ? *config : snn_cuda_default_config();
     const snn_b200_options_t o = options ? *options : snn_b200_default_options();
-    if ((o.propagation == SNN_B200_PROPAGATE_ORDERED || o.batch > 1) && cfg.prefer_streaming)
+    if ((o.propagation == SNN_B200_PROPAGATE_ORDERED || o.propagation == SNN_B200_PROPAGATE_PUSH_BINNED ||
+         o.batch > 1) && cfg.prefer_streaming)
         return SNN_ERR_UNSUPPORTED;
     snn_cuda_context_t *c = nullptr;
     CreateEnv env;
@@ -1741,7 +1743,7 @@ snn_status_t snn_b200_create(const snn_network_t *network, const snn_cuda_config
                 st = add_pull_topology(c, network, nullptr);
         } else if (c->opull) st = upload_full_ordered(c, network);
         else if ((st = upload_full_push(c, network)) == SNN_OK && (st = add_pull_topology(c, network, nullptr)) == SNN_OK)
-            st = setup_ordered_push(c);
+            st = setup_ordered(c);
     } else {
         c->mode = SNN_CUDA_MODE_STREAMING;
         c->e_local = network->synapse_count;
@@ -1852,7 +1854,7 @@ snn_status_t snn_cuda_step(snn_cuda_context_t *c, const float *host_external_cur
         if (early) cudaStreamSynchronize(c->spk_stream);  // no copy lands after the return
         return st;
     }
-    if (c->binned || c->exchange == SNN_B200_EXCHANGE_PEER) queue_error_check(c);
+    if (c->exchange == SNN_B200_EXCHANGE_PEER) queue_error_check(c);
     if (host_out_spikes != nullptr && c->n_local != 0) {
         if (seam_fail()) {
             cudaStreamSynchronize(c->stream);
@@ -2074,6 +2076,7 @@ snn_status_t snn_b200_reset(snn_cuda_context_t *c) {
     c->launches++;
     if ((st = cuda_status(cudaGetLastError())) != SNN_OK) return st;
     saved.list_count[0] = saved.list_count[1] = 0;
+    saved.step_events[0] = saved.step_events[1] = 0;
     if (cudaMemcpyAsync(c->d_ctr, &saved, sizeof(saved), cudaMemcpyHostToDevice, c->stream) != cudaSuccess)
         return SNN_ERR_CUDA;
     c->cur = 0;
@@ -2212,8 +2215,8 @@ snn_status_t snn_b200_get_layout(const snn_cuda_context_t *c, snn_b200_layout_t 
                                      c->n_rows * 4;
     else
         out->device_topology_bytes = (c->n_rows + 1) * 8 + c->e_local * (c->col_bits / 8 + 4);
-    out->binned = c->binned ? 1u : 0u;
-    out->binned_passes = c->binned ? c->bin.passes : 0u;
+    out->binned = c->binfold ? 1u : 0u;
+    out->binned_passes = c->binfold ? c->bf.tiles : 0u;
     out->ordered_csc = (c->opull || c->has_csc) ? 1u : 0u;
     out->pull_slots = c->sell_slots;
     out->batch = (uint32_t)c->batch;
@@ -2273,7 +2276,6 @@ snn_status_t snn_b200_download_topology(const snn_cuda_context_t *c, snn_size_t 
                                         snn_size_t *col_idx, float *weights, snn_size_t edge_capacity) {
     if (c == nullptr || c->mode != SNN_CUDA_MODE_FULL || c->propagation == SNN_B200_PROPAGATE_ORDERED)
         return SNN_ERR_INVALID_ARGUMENT;
-    if (c->passes > 1) return SNN_ERR_UNSUPPORTED;  // topology split into target-pass slices
     if ((row_ptr && row_capacity < c->n_rows + 1) || ((col_idx || weights) && edge_capacity < c->e_local))
         return SNN_ERR_INVALID_ARGUMENT;
     if (set_device(c) != SNN_OK) return SNN_ERR_CUDA;

@@ -86,19 +86,15 @@ def test_push_dyadic_bit_exact(prop):
     np.testing.assert_array_equal(bits(cv), bits(gv))
 
 
-@pytest.mark.parametrize("width,prop,passes", [(32, sb.PROPAGATE_PUSH_BINNED, "0"), (32, sb.PROPAGATE_PUSH_BINNED, "3"),
-                                                (32, sb.PROPAGATE_PUSH_ATOMIC, "0"), (64, sb.PROPAGATE_PUSH, "0")])
-def test_push_general_weights_tolerance(width, prop, passes, monkeypatch):
+@pytest.mark.parametrize("width,prop", [(32, sb.PROPAGATE_PUSH_ATOMIC), (64, sb.PROPAGATE_PUSH)])
+def test_push_general_weights_tolerance(width, prop):
     """Push with fp32 atomics: from the SAME state each step (teacher forcing
     through snn_b200_upload_state), voltages agree within 1e-5 relative and
     the divergent spikes (threshold ties) are counted and must be rare."""
     lif = baseline_lif()
     n = 20000
     net = ORC.random_pool(n, 100, 0.0, 0.6, 0, lif=lif)
-    monkeypatch.setenv("SNN_B200_BINNED_PASSES", passes)  # force several target passes (CSR slices)
     ctx = sb.CudaContext.create(net, None, opts(index_width=width, propagation=prop))
-    if prop == sb.PROPAGATE_PUSH_BINNED and width == 32:
-        assert ctx.layout["binned"] == 1 and ctx.layout["binned_passes"] == max(1, int(passes))
     st = State(net)
     inj = stream_inject(1, 200, 20.0, n)
     divergent = 0
@@ -309,45 +305,57 @@ def test_dense_gaussian_config1_samples_with_reset():
         ctx.reset()
 
 
-def test_binned_push_overflow_fallback_exact():
-    """A hub row whose 70k edges hit 7 targets overflows the shared-memory
-    staging and the L2 bin capacity of one tile; the overflow falls back to
-    direct L2 atomics. Dyadic weights keep every sum exact, so the binned
-    push must equal the ordered CPU fold bit for bit."""
+@pytest.mark.parametrize("prop", [sb.PROPAGATE_ORDERED, sb.PROPAGATE_PUSH_ATOMIC])
+def test_hub_row_collisions_exact(prop):
+    """A hub row whose 70k edges hit 7 targets: in the bin-fold every round of
+    32 events is all collisions (ten thousand events per target, applied in
+    lane order). ORDERED with general weights, and the atomic push with one
+    dyadic weight: bit-identical to the serial CPU fold."""
     n = 70001
     rp = np.zeros(n + 1, np.uint64)
     rp[1:] = 70000
     col = (np.arange(70000, dtype=np.uint64) % 7) + 1
-    w = np.full(70000, 0.0625, np.float32)
+    if prop == sb.PROPAGATE_ORDERED:
+        w = np.random.default_rng(3).random(70000, dtype=np.float32)
+    else:
+        w = np.full(70000, 0.0625, np.float32)
     net = ORC.custom_csr(rp, col, w, lif=default_lif(v_threshold=1e6))
     ext = np.zeros(n, np.float32)
     ext[0] = 2e6
-    for prop in (sb.PROPAGATE_PUSH_BINNED, sb.PROPAGATE_PUSH_ATOMIC):
-        ctx = sb.CudaContext.create(net, None, opts(propagation=prop))
-        cr, gr, cv, gv = run_pair(net, ctx, 3, ext=lambda t: ext if t == 0 else None)
-        assert first_divergence(cr, gr) is None
-        np.testing.assert_array_equal(bits(cv), bits(gv))
-        ctx.free()
+    ctx = sb.CudaContext.create(net, None, opts(propagation=prop))
+    cr, gr, cv, gv = run_pair(net, ctx, 3, ext=lambda t: ext if t == 0 else None)
+    assert first_divergence(cr, gr) is None
+    np.testing.assert_array_equal(bits(cv), bits(gv))
+    ctx.free()
 
 
-@pytest.mark.parametrize("passes", ["0", "2"])
-def test_generated_pool_binned_passes_exact(passes, monkeypatch):
-    """Device-generated pool on the binned push path, with one and with two
-    target passes (per-pass CSR slices generated on the device): dyadic weights
-    make every sum exact, so spikes, events and voltages equal the oracle's."""
-    monkeypatch.setenv("SNN_B200_BINNED_PASSES", passes)
+@pytest.mark.parametrize("prop,env", [(sb.PROPAGATE_ORDERED, {}), (sb.PROPAGATE_PUSH_BINNED, {}),
+                                      (sb.PROPAGATE_ORDERED, {"SNN_B200_ORDERED_SORT": "1"}),
+                                      (sb.PROPAGATE_ORDERED, {"SNN_B200_ORDERED_CAP": "4000"})])
+def test_generated_pool_binfold_exact(prop, env, monkeypatch):
+    """Device-generated pool, general weights, ORDERED through the bin-fold
+    (PUSH_BINNED is the same propagation), through the event-sort fallback,
+    and with an event capacity so small that busy steps go to the pull:
+    spikes, events and voltages equal the serial CPU step's."""
+    for k, v in env.items():
+        monkeypatch.setenv(k, v)
     lif = baseline_lif()
     n, f = 30011, 64
-    net = ORC.random_pool(n, f, 0.25, 0.25, 21, lif=lif)
+    net = ORC.random_pool(n, f, -0.1, 0.55, 21, lif=lif)
     st = State(net)
     sc, ev, hs, _ = ORC.run_inject_stream(net, st, 5, 0, 30, 600, 20.0)
-    ctx = sb.CudaContext.random_pool(n, f, 0.25, 0.25, 21, lif=lif_to_sb(lif),
-                                     options=opts(propagation=sb.PROPAGATE_PUSH_BINNED))
-    assert ctx.layout["binned"] == 1 and ctx.layout["binned_passes"] == max(1, int(passes))
+    ctx = sb.CudaContext.random_pool(n, f, -0.1, 0.55, 21, lif=lif_to_sb(lif), options=opts(propagation=prop))
+    lay = ctx.layout
+    assert lay["propagation"] == sb.PROPAGATE_ORDERED
+    assert lay["binned"] == (0 if "SNN_B200_ORDERED_SORT" in env else 1)
+    if lay["binned"]:
+        assert lay["binned_passes"] == -(-n // 1024)  # tiles of 1024 targets
     ctx.run_stream_async(5, 0, 30, 600, 20.0)
     s = ctx.stats()
     assert s["spikes"] == int(sc.sum()) and s["events"] == int(ev.sum())
     np.testing.assert_array_equal(bits(st.voltage()), bits(ctx.download_voltage()))
+    if "SNN_B200_ORDERED_CAP" in env:
+        assert s["pull_steps"] > 0
 
 
 def test_peer_exchange_wait_expires_without_fault():
@@ -503,9 +511,9 @@ def test_batched_states_equal_independent_runs(prop, weights):
         np.testing.assert_array_equal(bits(v[b * n:(b + 1) * n]), bits(states[b].voltage()))
     assert sum(int(st.voltage().size) for st in states) == B * n
     assert ctx.stats()["spikes"] > 100
-    # Batched contexts are FULL, unsharded, and not for the CSC pull / binned push.
+    # Batched contexts are FULL only.
     with pytest.raises(sb.SnnError):
-        sb.CudaContext.create(net, None, sb.default_options(propagation=sb.PROPAGATE_PUSH_BINNED, batch=B))
+        sb.CudaContext.create(net, sb.default_config(prefer_streaming=1), sb.default_options(batch=B))
 
 
 def test_batched_config1_samples_with_held_frames():
@@ -662,21 +670,19 @@ def test_device_feedforward_matches_host_builder(layers, fanout, seed):
     np.testing.assert_array_equal(bits(w), bits(net.weights()))
 
 
-@pytest.mark.parametrize("mode", ["ordered", "binned2"])
+@pytest.mark.parametrize("mode", ["ordered", "sort"])
 def test_device_feedforward_steps_exact(mode, monkeypatch):
     """A device-built feed-forward network (one dense and two sparse layers)
-    stepped against the CPU step of the host-built one: ORDERED (CSC built on
-    the device from the generator), and the binned push with two target
-    passes (per-pass slices generated on the device) with a dyadic weight."""
+    stepped against the CPU step of the host-built one: ORDERED through the
+    bin-fold and through the event-sort fallback (CSC built on the device
+    from the generator for the dense steps)."""
     layers, fanout = [1500, 1200, 40, 900], 60
-    weight = 0.75 if mode == "ordered" else 0.5
+    weight = 0.75
     lif = default_lif(refractory_steps=1)
     net = ORC.feedforward(layers, fanout, weight, 11, lif=lif)
-    if mode == "ordered":
-        o = ordered()
-    else:
-        monkeypatch.setenv("SNN_B200_BINNED_PASSES", "2")
-        o = opts(propagation=sb.PROPAGATE_PUSH_BINNED)
+    if mode == "sort":
+        monkeypatch.setenv("SNN_B200_ORDERED_SORT", "1")
+    o = ordered()
     ctx = sb.CudaContext.feedforward(layers, fanout, weight, 11, lif=lif_to_sb(lif), options=o)
     rng = np.random.default_rng(4)
     n = net.neuron_count
