@@ -37,6 +37,8 @@ import time
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
+PROPAGATION_LABEL = {"auto": "push (auto)", "atomic": "push (atomic)", "ordered": "ordered (bit-exact, event sort)",
+                     "binned": "ordered (bit-exact, bin-fold)"}
 L2_NOTE = "inputs larger than L2 (FULL CSR of the shard read sparsely each step; target currents L2-resident by design)"
 
 
@@ -76,8 +78,9 @@ def parse():
     ap.add_argument("--layer-size", type=int, default=1_000_000, help="config4: neurons per layer")
     ap.add_argument("--batch", type=int, default=2000, help="config1: samples per batched context")
     ap.add_argument("--propagation", choices=["auto", "binned", "atomic", "ordered"], default="auto",
-                    help="push kernel: auto (library default), binned (shared-memory tiles), atomic (L2 red); "
-                         "ordered: the bit-exact pull over a device-built CSC")
+                    help="auto: the library's push (atomic push, pull on dense steps); atomic: the push alone; "
+                         "ordered: bit-exact CSR-order propagation (event sort, pull on dense steps); "
+                         "binned: bit-exact bin-fold (no host round trip, pull on dense steps)")
     return ap.parse_args()
 
 
@@ -138,9 +141,10 @@ def measured_peak_gbs():
         return 6650.0, "fallback"
 
 
-# DRAM bytes per synaptic event of propagate_push_kernel (32-bit columns),
-# dram__bytes_read.sum + dram__bytes_write.sum / events of one ncu capture
-# (profiles/propagate_push_config2.md); scaled by this run's events.
+# DRAM bytes per synaptic event of propagate_push_kernel (32-bit columns):
+# dram__bytes_read.sum + dram__bytes_write.sum over the events of one ncu
+# capture of the kernel (500k-neuron pool, fanout 1000); scaled by this
+# run's events. The pull kernel reads 8 B per slot of its layout.
 NCU_DRAM_BYTES_PER_EVENT = 8.68
 NCU_PULL_BYTES_PER_SLOT = 8.0
 
@@ -263,15 +267,14 @@ def workload_config(args, world):
                 "weights": "U[0,1] mV", "seed": args.seed,
                 "inject": f"5% of layer 0 ({int(round(0.05 * ls))}) x 30 per step",
                 "lif": "dt 1 ms, tau 20 ms, rest=reset -65 mV, thr -50 mV, refractory 2", "policy": "FULL",
-                "propagation": "ordered (bit-exact push)" if args.propagation == "ordered"
-                else f"push ({args.propagation})",
+                "propagation": PROPAGATION_LABEL[args.propagation],
                 "parallelism": f"postsynaptic shards x{world}" + (f", {args.exchange} spike exchange" if world > 1 else ""),
                 "l2": L2_NOTE}
     return {"workload": "config2_resident_random_pool", "neurons": args.neurons, "fanout": args.fanout,
             "synapses": args.neurons * args.fanout, "weights": "U[-0.2,0.5] mV", "seed": args.seed,
             "inject": f"{args.inject_frac * 100:g}% of neurons x {args.inject_value:g} per step",
             "lif": "dt 1 ms, tau 20 ms, rest=reset -65 mV, thr -50 mV, refractory 2", "policy": "FULL",
-            "propagation": "ordered (bit-exact push)" if args.propagation == "ordered" else f"push ({args.propagation})", "parallelism": f"postsynaptic shards x{world}" + (f", {args.exchange} spike exchange" if world > 1 else ""), "l2": L2_NOTE}
+            "propagation": PROPAGATION_LABEL[args.propagation], "parallelism": f"postsynaptic shards x{world}" + (f", {args.exchange} spike exchange" if world > 1 else ""), "l2": L2_NOTE}
 
 
 # ------------------------------------------------------------ GPU side ----
@@ -605,7 +608,9 @@ def run_b200(args):
     prop_bytes = 12.0 * s["events"] + 16.0 * spikes_rows
     kernel_name = "propagate_push_kernel"
     if args.propagation == "ordered":
-        kernel_name = "ordered propagation (bin-fold push; pull on dense steps)"
+        kernel_name = "ordered propagation (event sort + in-order fold; pull on dense steps)"
+    elif args.propagation == "binned":
+        kernel_name = "ordered propagation (bin-fold; pull on dense steps)"
     gated = int(lay.get("ordered_csc", 0)) == 1 and args.propagation == "auto"
     if gated:
         kernel_name = "propagate_push_kernel (sparse steps) + propagate_pull_smem_kernel (dense steps)"

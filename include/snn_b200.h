@@ -146,17 +146,18 @@ typedef enum snn_b200_propagation {
     /* Every target folds its contributions in CSR order (ascending
      * presynaptic row, ascending edge): bit-identical to the reference's
      * serial CPU step (src/snn.c:898-906) for any weights. FULL mode only.
-     * Each step either bins its events by target tile in CSR order and
-     * folds every tile in shared memory (the bin-fold; cost ~ events), or,
-     * on dense steps when a CSC fits beside the CSR, pulls over the CSC
-     * (cost ~ synapses); the choice is made on the device from the step's
-     * event count, with no host round trip. */
+     * Each step either sorts its events by target (a stable radix sort of
+     * the spiking rows' CSR slices, then an in-order fold; cost ~ events;
+     * one host read of the event count per step), or, on dense steps when a
+     * CSC fits beside the CSR, pulls over the CSC (cost ~ synapses). */
     SNN_B200_PROPAGATE_ORDERED = 1,
     /* The plain push kernel: one red.global.add.f32 per event. */
     SNN_B200_PROPAGATE_PUSH_ATOMIC = 2,
-    /* The binned push: each step's events are binned by target tile and
-     * folded tile by tile in shared memory. It keeps CSR order, so it is the
-     * same propagation as ORDERED (the context reports ORDERED). */
+    /* ORDERED through the bin-fold: each step's events are binned by target
+     * tile in CSR order and every tile is folded in shared memory, gated on
+     * the device against the pull for dense steps: no host round trip, so
+     * multi-step runs replay as CUDA graphs. Bit-identical to ORDERED (the
+     * context reports ORDERED and layout.binned = 1). */
     SNN_B200_PROPAGATE_PUSH_BINNED = 3
 } snn_b200_propagation_t;
 

@@ -53,6 +53,41 @@ __device__ __forceinline__ uint32_t lanemask_lt() {
     return m;
 }
 
+// Lanes of `active` whose `key` (its low `nbits` bits) equals this lane's:
+// one ballot per key bit. Cheaper than __match_any_sync when most lanes hold
+// distinct keys (its cost grows with the number of distinct values).
+template <int NB>
+__device__ __forceinline__ uint32_t match_bits_n(uint32_t key, uint32_t active) {
+    uint32_t peers = active;
+#pragma unroll
+    for (int b = 0; b < NB; ++b) {
+        const uint32_t bit = (key >> b) & 1u;
+        peers &= ~(__ballot_sync(kFull, bit) ^ (0u - bit));  // equal bit b
+    }
+    return peers;
+}
+
+// Groups the active lanes by key through a scratch array over the key range
+// (this warp's): every active lane writes its lane id into tag[key] and reads
+// back one writer per key, the group's id (5 bits). Returns the lanes of this
+// lane's group, in lane order: rank = popc(peers & lanemask_lt). When no two
+// lanes share a key (the common case) no ballot beyond the first is needed.
+// Stale scratch entries are harmless: each active lane writes before it reads.
+__device__ __forceinline__ uint32_t group_by_key(uint8_t *tag, uint32_t key, bool act, unsigned lane) {
+    if (act) tag[key] = (uint8_t)lane;
+    __syncwarp();
+    const uint32_t g = act ? tag[key] : lane;
+    const uint32_t active = __ballot_sync(kFull, act);
+    uint32_t peers;
+    if (__ballot_sync(kFull, g != lane) == 0u)
+        peers = 1u << lane;  // all keys distinct
+    else
+        peers = match_bits_n<5>(g, active);
+    __syncwarp();
+    return act ? peers : (1u << lane);
+}
+
+
 __device__ __forceinline__ bool dense_step(const DevCounters *ctr, int parity, unsigned long long gate) {
     return *(volatile const unsigned long long *)&ctr->step_events[parity] > gate;
 }
@@ -222,12 +257,13 @@ __global__ void __launch_bounds__(kBfThreads) binfold_count_kernel(const TIdx *_
         const uint64_t row = batch_rows ? id % batch_rows : id;
         const uint64_t base = id - row;
         const uint64_t b = row_ptr[row], e = row_ptr[row + 1];
-        for (uint64_t k0 = b; k0 < e; k0 += 32u) {
-            const uint64_t k = k0 + lane;
-            const bool act = k < e;
-            const uint32_t tile = act ? (uint32_t)((base + (uint64_t)__ldg(col + k)) >> tile_bits) : 0u;
-            const uint32_t peers = __match_any_sync(kFull, act ? tile : (0x80000000u | lane));
-            if (act && lane == (unsigned)(__ffs(peers) - 1)) atomicAdd(&s_cnt[tile], (uint32_t)__popc(peers));
+        for (uint64_t k0 = b + lane; k0 < e; k0 += 256u) {
+            uint64_t c[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) c[u] = k0 + 32u * u < e ? (uint64_t)__ldg(col + k0 + 32u * u) : ~0ull;
+#pragma unroll
+            for (int u = 0; u < 8; ++u)
+                if (c[u] != ~0ull) atomicAdd(&s_cnt[(uint32_t)((base + c[u]) >> tile_bits)], 1u);
         }
     }
     __syncthreads();
@@ -235,11 +271,16 @@ __global__ void __launch_bounds__(kBfThreads) binfold_count_kernel(const TIdx *_
 }
 
 // ------------------------------------------------------------- scatter ----
-// Same slices as the count. Rows go eight at a time, warp w taking row
-// s + w: pass 1 counts each warp's events per tile, a prefix over the warps
-// (in row order) turns the counts into slot positions, pass 2 writes the
-// events, pass 3 clears the touched counters. The rows' columns are re-read
-// from L1 by passes 2 and 3.
+// Same CTA slices as the count. The slice goes in groups of kScatterRows
+// rows per warp, warp w taking the w-th run of consecutive rows of the group
+// (so the warps are in row order): pass 1 counts each warp's events per tile,
+// a prefix over the warps places them behind the CTA's cursor of each tile,
+// pass 2 writes the events (equal tiles inside a round of 32 events ranked
+// in lane = edge order), then the counters are cleared. All warps of a CTA
+// append to one region per tile, so the partly written sectors waiting in L2
+// number about CTAs x tiles.
+constexpr uint32_t kScatterRows = 8;
+
 template <typename TIdx, typename TCol>
 __global__ void __launch_bounds__(kBfThreads) binfold_scatter_kernel(const TIdx *__restrict__ list, DevCounters *ctr,
                                                                      int parity, const uint64_t *__restrict__ row_ptr,
@@ -250,8 +291,9 @@ __global__ void __launch_bounds__(kBfThreads) binfold_scatter_kernel(const TIdx 
                                                                      uint2 *__restrict__ bins,
                                                                      unsigned long long gate) {
     extern __shared__ uint32_t s_mem[];
-    uint32_t *s_cur = s_mem;           // [tiles] next slot of each tile (this CTA)
-    uint32_t *s_w = s_mem + tiles;     // [warps][tiles] per-warp counts, then positions
+    uint32_t *s_cur = s_mem;            // [tiles] this CTA's next slot of each tile
+    uint32_t *s_w = s_mem + tiles;      // [warps][tiles] per-warp counts, then positions
+    uint8_t *s_tag = reinterpret_cast<uint8_t *>(s_mem + (uint64_t)tiles * (kBfWarps + 1));  // [warps][tiles]
     if (dense_step(ctr, parity, gate)) return;
     const uint32_t count = *(volatile uint32_t *)&ctr->list_count[parity];
     const unsigned lane = lane_id(), warp = threadIdx.x >> 5;
@@ -262,64 +304,82 @@ __global__ void __launch_bounds__(kBfThreads) binfold_scatter_kernel(const TIdx 
     const uint64_t s0 = (uint64_t)count * blockIdx.x / G, s1 = (uint64_t)count * (blockIdx.x + 1) / G;
     const uint32_t tmask = (1u << tile_bits) - 1u;
     uint32_t *my = s_w + (uint64_t)warp * tiles;
-    for (uint64_t g0 = s0; g0 < s1; g0 += kBfWarps) {
-        const uint64_t s = g0 + warp;
-        uint64_t b = 0, e = 0, base = 0;
-        if (s < s1) {
+    uint8_t *tag = s_tag + (uint64_t)warp * tiles;
+    for (uint64_t g0 = s0; g0 < s1; g0 += (uint64_t)kScatterRows * kBfWarps) {
+        const uint64_t r0 = min(s1, g0 + (uint64_t)warp * kScatterRows);
+        const uint64_t r1 = min(s1, r0 + kScatterRows);
+        for (uint64_t s = r0; s < r1; ++s) {
             const uint64_t id = (uint64_t)list[s];
             const uint64_t row = batch_rows ? id % batch_rows : id;
-            base = id - row;
-            b = row_ptr[row];
-            e = row_ptr[row + 1];
-        }
-        for (uint64_t k0 = b; k0 < e; k0 += 32u) {
-            const uint64_t k = k0 + lane;
-            const bool act = k < e;
-            const uint32_t tile = act ? (uint32_t)((base + (uint64_t)__ldg(col + k)) >> tile_bits) : 0u;
-            const uint32_t peers = __match_any_sync(kFull, act ? tile : (0x80000000u | lane));
-            if (act && lane == (unsigned)(__ffs(peers) - 1)) my[tile] += (uint32_t)__popc(peers);
+            const uint64_t base = id - row;
+            const uint64_t b = row_ptr[row], e = row_ptr[row + 1];
+            for (uint64_t k0 = b + lane; k0 < e; k0 += 256u) {
+                uint64_t c[8];
+#pragma unroll
+                for (int u = 0; u < 8; ++u) c[u] = k0 + 32u * u < e ? (uint64_t)__ldg(col + k0 + 32u * u) : ~0ull;
+#pragma unroll
+                for (int u = 0; u < 8; ++u)
+                    if (c[u] != ~0ull) atomicAdd(&my[(uint32_t)((base + c[u]) >> tile_bits)], 1u);
+            }
         }
         __syncthreads();
         for (uint32_t t = threadIdx.x; t < tiles; t += kBfThreads) {
             uint32_t run = s_cur[t];
 #pragma unroll
             for (int q = 0; q < kBfWarps; ++q) {
-                // Only a warp with events in the tile reads its position (and
-                // clears it afterwards); the others' counters stay zero.
                 const uint32_t x = s_w[(uint64_t)q * tiles + t];
-                if (x) s_w[(uint64_t)q * tiles + t] = run;
+                s_w[(uint64_t)q * tiles + t] = run;
                 run += x;
             }
             s_cur[t] = run;
         }
         __syncthreads();
-        for (uint64_t k0 = b; k0 < e; k0 += 32u) {
-            const uint64_t k = k0 + lane;
-            const bool act = k < e;
-            const uint32_t t = act ? (uint32_t)(base + (uint64_t)__ldg(col + k)) : 0u;
-            const uint32_t tile = t >> tile_bits;
-            const uint32_t peers = __match_any_sync(kFull, act ? tile : (0x80000000u | lane));
-            const int leader = __ffs(peers) - 1;
-            uint32_t pos = 0;
-            if (act && lane == (unsigned)leader) pos = my[tile];
-            pos = __shfl_sync(kFull, pos, leader);
-            __syncwarp();
-            if (act && lane == (unsigned)leader) my[tile] = pos + (uint32_t)__popc(peers);
-            if (act) bins[pos + __popc(peers & lanemask_lt())] = make_uint2(t & tmask, __float_as_uint(__ldcs(w + k)));
+        for (uint64_t s = r0; s < r1; ++s) {
+            const uint64_t id = (uint64_t)list[s];
+            const uint64_t row = batch_rows ? id % batch_rows : id;
+            const uint64_t base = id - row;
+            const uint64_t b = row_ptr[row], e = row_ptr[row + 1];
+            // Eight rounds of columns and weights in flight per lane, then the
+            // eight rounds are ranked and written in order.
+            for (uint64_t k0 = b; k0 < e; k0 += 256u) {
+                uint32_t tv[8];
+                float wv[8];
+#pragma unroll
+                for (int u = 0; u < 8; ++u) {
+                    const uint64_t k = k0 + 32u * u + lane;
+                    tv[u] = k < e ? (uint32_t)(base + (uint64_t)__ldg(col + k)) : 0u;
+                    wv[u] = k < e ? __ldcs(w + k) : 0.0f;
+                }
+#pragma unroll
+                for (int u = 0; u < 8; ++u) {
+                    if (k0 + 32u * u >= e) break;  // warp-uniform
+                    const bool act = k0 + 32u * u + lane < e;
+                    const uint32_t t = tv[u];
+                    const uint32_t tile = t >> tile_bits;
+                    const uint32_t peers = group_by_key(tag, tile, act, lane);
+                    const int leader = __ffs(peers) - 1;
+                    uint32_t pos = 0;
+                    if (act && lane == (unsigned)leader) pos = my[tile];
+                    pos = __shfl_sync(kFull, pos, leader);
+                    __syncwarp();
+                    if (act && lane == (unsigned)leader) my[tile] = pos + (uint32_t)__popc(peers);
+                    if (act) bins[pos + __popc(peers & lanemask_lt())] = make_uint2(t & tmask, __float_as_uint(wv[u]));
+                }
+            }
         }
-        __syncwarp();
-        for (uint64_t k0 = b; k0 < e; k0 += 32u) {
-            const uint64_t k = k0 + lane;
-            if (k < e) my[(uint32_t)((base + (uint64_t)__ldg(col + k)) >> tile_bits)] = 0u;
-        }
+        __syncthreads();
+        for (uint32_t b = threadIdx.x; b < tiles * kBfWarps; b += kBfThreads) s_w[b] = 0u;
         __syncthreads();
     }
 }
 
 // ---------------------------------------------------------------- fold ----
-// CTA per tile (grid-stride over tiles). Warp w owns the tile's targets
-// [w*T/8, (w+1)*T/8); every warp reads each window of events and applies
-// its own targets' events in order.
+// CTA per tile (grid-stride over tiles); warp w owns the tile's targets
+// [w*T/8, (w+1)*T/8). Each window of events is first partitioned by owner,
+// stably (warp w reads window positions [w*W/8, (w+1)*W/8) in rounds of 32;
+// eight ballots rank every event among the equal-owner events before it),
+// then every warp folds its own bucket in order: inside a round of 32, events
+// for the same target are applied one after the other in lane order.
 __global__ void __launch_bounds__(kBfThreads) binfold_fold_kernel(const uint2 *__restrict__ bins,
                                                                   const uint32_t *__restrict__ offs, uint32_t tiles,
                                                                   uint32_t grid_count, uint32_t tile_bits,
@@ -327,32 +387,81 @@ __global__ void __launch_bounds__(kBfThreads) binfold_fold_kernel(const uint2 *_
                                                                   DevCounters *ctr, int parity,
                                                                   unsigned long long gate) {
     extern __shared__ __align__(16) unsigned char s_raw[];
+    constexpr int kRounds = kFoldWindow / kBfWarps / 32;  // rounds of 32 events per warp per window
     const uint32_t T = 1u << tile_bits;
     float *acc = reinterpret_cast<float *>(s_raw);
-    uint2 *win = reinterpret_cast<uint2 *>(s_raw + (size_t)T * 4);
+    uint2 *sorted = reinterpret_cast<uint2 *>(s_raw + (size_t)T * 4);
+    uint8_t *tag = reinterpret_cast<uint8_t *>(s_raw + (size_t)T * 4 + (size_t)kFoldWindow * 8);  // [T]
+    __shared__ uint32_t s_cnt[kBfWarps][kBfWarps];  // [warp][owner] events in the warp's part
+    __shared__ uint32_t s_pos[kBfWarps][kBfWarps];  // [warp][owner] first sorted position
+    __shared__ uint32_t s_bucket[kBfWarps + 1];     // owner buckets in the sorted window
     if (dense_step(ctr, parity, gate)) return;
     const unsigned lane = lane_id(), warp = threadIdx.x >> 5;
     const uint32_t owner_shift = tile_bits - 3;
     const uint64_t G = grid_count;
+    const uint32_t lt = lanemask_lt();
     for (uint32_t tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
-        for (uint32_t t = threadIdx.x; t < T; t += kBfThreads) acc[t] = 0.0f;
         const uint64_t lo = offs[(uint64_t)tile * G];
         const uint64_t hi = offs[(uint64_t)(tile + 1) * G];
-        __syncthreads();
+        if (lo == hi) continue;  // no events: the tile's currents stay zero
+        for (uint32_t t = threadIdx.x; t < T; t += kBfThreads) acc[t] = 0.0f;
         for (uint64_t w0 = lo; w0 < hi; w0 += kFoldWindow) {
             const uint32_t nwin = (uint32_t)min((uint64_t)kFoldWindow, hi - w0);
-            for (uint32_t i = threadIdx.x; i < nwin; i += kBfThreads) win[i] = __ldcs(bins + w0 + i);
+            // Partition: events of this warp's part, their owners and ranks.
+            uint2 ev[kRounds];
+            uint32_t rk[kRounds];
+            if (lane < kBfWarps) s_cnt[warp][lane] = 0u;
+            // Warp w partitions window positions [p0, p1), in order.
+            const uint32_t p0 = nwin * warp / kBfWarps, p1 = nwin * (warp + 1) / kBfWarps;
+#pragma unroll
+            for (int j = 0; j < kRounds; ++j) {
+                const uint32_t i = p0 + j * 32u + lane;
+                ev[j] = i < p1 ? __ldcs(bins + w0 + i) : make_uint2(0u, 0u);
+            }
+            __syncwarp();
+#pragma unroll
+            for (int j = 0; j < kRounds; ++j) {
+                if (p0 + j * 32u >= p1) break;  // warp-uniform
+                const uint32_t i = p0 + j * 32u + lane;
+                const bool act = i < p1;
+                const uint32_t o = ev[j].x >> owner_shift;
+                uint32_t peers = match_bits_n<3>(o, __ballot_sync(kFull, act));
+                if (!act) peers = 1u << lane;
+                const int leader = __ffs(peers) - 1;
+                uint32_t base = 0;
+                if (act && lane == (unsigned)leader) base = atomicAdd(&s_cnt[warp][o], (uint32_t)__popc(peers));
+                base = __shfl_sync(kFull, base, leader);
+                rk[j] = base + __popc(peers & lt);
+            }
             __syncthreads();
-            for (uint32_t i0 = 0; i0 < nwin; i0 += 32u) {
+            if (threadIdx.x < kBfWarps * kBfWarps) {
+                const uint32_t o = threadIdx.x / kBfWarps, wq = threadIdx.x % kBfWarps;
+                uint32_t p = 0;
+                for (uint32_t o2 = 0; o2 < o; ++o2)
+                    for (uint32_t w2 = 0; w2 < kBfWarps; ++w2) p += s_cnt[w2][o2];
+                for (uint32_t w2 = 0; w2 < wq; ++w2) p += s_cnt[w2][o];
+                s_pos[wq][o] = p;
+                if (wq == 0) s_bucket[o] = p;
+                if (threadIdx.x == 0) s_bucket[kBfWarps] = nwin;
+            }
+            __syncthreads();
+#pragma unroll
+            for (int j = 0; j < kRounds; ++j) {
+                const uint32_t i = p0 + j * 32u + lane;
+                if (i < p1) sorted[s_pos[warp][ev[j].x >> owner_shift] + rk[j]] = ev[j];
+            }
+            __syncthreads();
+            // Fold this warp's bucket in order.
+            const uint32_t b0 = s_bucket[warp], b1 = s_bucket[warp + 1];
+            for (uint32_t i0 = b0; i0 < b1; i0 += 32u) {
                 const uint32_t i = i0 + lane;
-                const uint2 ev = i < nwin ? win[i] : make_uint2(0u, 0u);
-                const bool own = i < nwin && (ev.x >> owner_shift) == warp;
-                if (!__any_sync(kFull, own)) continue;
-                const uint32_t peers = __match_any_sync(kFull, own ? ev.x : (0x80000000u | lane));
-                const int rank = __popc(peers & lanemask_lt());
-                const int rounds = (int)__reduce_max_sync(kFull, own ? (uint32_t)__popc(peers) : 0u);
+                const bool act = i < b1;
+                const uint2 e = act ? sorted[i] : make_uint2(0u, 0u);
+                const uint32_t peers = group_by_key(tag, e.x, act, lane);
+                const int rank = __popc(peers & lt);
+                const int rounds = (int)__reduce_max_sync(kFull, act ? (uint32_t)__popc(peers) : 0u);
                 for (int r = 0; r < rounds; ++r) {
-                    if (own && rank == r) acc[ev.x] = __fadd_rn(acc[ev.x], __uint_as_float(ev.y));
+                    if (act && rank == r) acc[e.x] = __fadd_rn(acc[e.x], __uint_as_float(e.y));
                     __syncwarp();
                 }
             }
@@ -367,8 +476,8 @@ __global__ void __launch_bounds__(kBfThreads) binfold_fold_kernel(const uint2 *_
     step_epilogue(ctr, parity, 0, *(volatile uint32_t *)&ctr->list_count[parity]);
 }
 
-int fold_smem(uint32_t tile_bits) { return (int)(((size_t)4 << tile_bits) + (size_t)kFoldWindow * 8); }
-int scatter_smem(uint32_t tiles) { return (int)((size_t)tiles * (kBfWarps + 1) * 4); }
+int fold_smem(uint32_t tile_bits) { return (int)(((size_t)5 << tile_bits) + (size_t)kFoldWindow * 8); }
+int scatter_smem(uint32_t tiles) { return (int)((size_t)tiles * (kBfWarps + 1) * 4 + (size_t)tiles * kBfWarps); }
 
 template <typename K>
 void allow_smem(K kernel, int bytes) {
@@ -386,7 +495,7 @@ bool binfold_plan(int device, uint64_t n_local, BinFoldPlan *plan) {
     if (tiles > kBinFoldMaxTiles || tiles == 0) return false;
     plan->tile_bits = tb;
     plan->tiles = (uint32_t)tiles;
-    plan->grid = (uint32_t)sm_count(device) * 2u;
+    plan->grid = (uint32_t)sm_count(device) * 4u;
     plan->hist_entries = (uint64_t)plan->tiles * plan->grid + 1;
     plan->chunks = 0;
     return true;

@@ -62,10 +62,12 @@ def _gpu_run(net, n, steps, count, prop):
     return raster, v, lay
 
 
-def test_config0_full_ordered_bit_exact(config0_cpu):
+@pytest.mark.parametrize("prop", [sb.PROPAGATE_ORDERED, sb.PROPAGATE_PUSH_BINNED])
+def test_config0_full_ordered_bit_exact(config0_cpu, prop):
+    """Both bit-exact propagations: the event sort and the bin-fold."""
     net, n, steps, count, cr, cv = config0_cpu
-    gr, gv, lay = _gpu_run(net, n, steps, count, sb.PROPAGATE_ORDERED)
-    assert lay["binned"] == 1  # the bin-fold, not the sort fallback
+    gr, gv, lay = _gpu_run(net, n, steps, count, prop)
+    assert lay["binned"] == (1 if prop == sb.PROPAGATE_PUSH_BINNED else 0)
     bad = np.nonzero((cr != gr).any(axis=1))[0]
     assert bad.size == 0, f"first divergent step {bad[0]}"
     np.testing.assert_array_equal(cv.view(np.uint32), gv.view(np.uint32))
@@ -97,14 +99,15 @@ def test_config0_full_push_free_running_divergence(config0_cpu):
     assert total <= 0.001 * spikes, report
 
 
-def test_config1_real_shape_500_samples_ordered():
+@pytest.mark.parametrize("prop", [sb.PROPAGATE_ORDERED, sb.PROPAGATE_PUSH_BINNED])
+def test_config1_real_shape_500_samples_ordered(prop):
     lif = baseline_lif()
     lif.input_scale = 20.0
     net = ORC.dense_gaussian([784, 1000, 10], 5, lif=lif)
     n, B, T = net.neuron_count, 500, 25
     frames = [ORC.sparse_frame(17, b, 784, 0.8, n) for b in range(B)]
-    ctx = sb.CudaContext.create(net, None, sb.default_options(propagation=sb.PROPAGATE_ORDERED, batch=B))
-    assert ctx.layout["binned"] == 1
+    ctx = sb.CudaContext.create(net, None, sb.default_options(propagation=prop, batch=B))
+    assert ctx.layout["binned"] == (1 if prop == sb.PROPAGATE_PUSH_BINNED else 0)
     ctx.set_external(np.concatenate(frames))
     ctx.reset()
     graster = np.zeros((T, B * n), np.uint8)

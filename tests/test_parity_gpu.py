@@ -305,7 +305,7 @@ def test_dense_gaussian_config1_samples_with_reset():
         ctx.reset()
 
 
-@pytest.mark.parametrize("prop", [sb.PROPAGATE_ORDERED, sb.PROPAGATE_PUSH_ATOMIC])
+@pytest.mark.parametrize("prop", [sb.PROPAGATE_ORDERED, sb.PROPAGATE_PUSH_BINNED, sb.PROPAGATE_PUSH_ATOMIC])
 def test_hub_row_collisions_exact(prop):
     """A hub row whose 70k edges hit 7 targets: in the bin-fold every round of
     32 events is all collisions (ten thousand events per target, applied in
@@ -315,7 +315,7 @@ def test_hub_row_collisions_exact(prop):
     rp = np.zeros(n + 1, np.uint64)
     rp[1:] = 70000
     col = (np.arange(70000, dtype=np.uint64) % 7) + 1
-    if prop == sb.PROPAGATE_ORDERED:
+    if prop != sb.PROPAGATE_PUSH_ATOMIC:
         w = np.random.default_rng(3).random(70000, dtype=np.float32)
     else:
         w = np.full(70000, 0.0625, np.float32)
@@ -330,13 +330,12 @@ def test_hub_row_collisions_exact(prop):
 
 
 @pytest.mark.parametrize("prop,env", [(sb.PROPAGATE_ORDERED, {}), (sb.PROPAGATE_PUSH_BINNED, {}),
-                                      (sb.PROPAGATE_ORDERED, {"SNN_B200_ORDERED_SORT": "1"}),
-                                      (sb.PROPAGATE_ORDERED, {"SNN_B200_ORDERED_CAP": "4000"})])
+                                      (sb.PROPAGATE_PUSH_BINNED, {"SNN_B200_ORDERED_CAP": "4000"})])
 def test_generated_pool_binfold_exact(prop, env, monkeypatch):
-    """Device-generated pool, general weights, ORDERED through the bin-fold
-    (PUSH_BINNED is the same propagation), through the event-sort fallback,
-    and with an event capacity so small that busy steps go to the pull:
-    spikes, events and voltages equal the serial CPU step's."""
+    """Device-generated pool, general weights, ORDERED through the event sort
+    and through the bin-fold (PUSH_BINNED), the latter also with an event
+    capacity so small that busy steps go to the pull: spikes, events and
+    voltages equal the serial CPU step's."""
     for k, v in env.items():
         monkeypatch.setenv(k, v)
     lif = baseline_lif()
@@ -347,7 +346,7 @@ def test_generated_pool_binfold_exact(prop, env, monkeypatch):
     ctx = sb.CudaContext.random_pool(n, f, -0.1, 0.55, 21, lif=lif_to_sb(lif), options=opts(propagation=prop))
     lay = ctx.layout
     assert lay["propagation"] == sb.PROPAGATE_ORDERED
-    assert lay["binned"] == (0 if "SNN_B200_ORDERED_SORT" in env else 1)
+    assert lay["binned"] == (1 if prop == sb.PROPAGATE_PUSH_BINNED else 0)
     if lay["binned"]:
         assert lay["binned_passes"] == -(-n // 1024)  # tiles of 1024 targets
     ctx.run_stream_async(5, 0, 30, 600, 20.0)
@@ -670,19 +669,17 @@ def test_device_feedforward_matches_host_builder(layers, fanout, seed):
     np.testing.assert_array_equal(bits(w), bits(net.weights()))
 
 
-@pytest.mark.parametrize("mode", ["ordered", "sort"])
-def test_device_feedforward_steps_exact(mode, monkeypatch):
+@pytest.mark.parametrize("mode", ["ordered", "binfold"])
+def test_device_feedforward_steps_exact(mode):
     """A device-built feed-forward network (one dense and two sparse layers)
     stepped against the CPU step of the host-built one: ORDERED through the
-    bin-fold and through the event-sort fallback (CSC built on the device
-    from the generator for the dense steps)."""
+    event sort and through the bin-fold (CSC built on the device from the
+    generator for the dense steps)."""
     layers, fanout = [1500, 1200, 40, 900], 60
     weight = 0.75
     lif = default_lif(refractory_steps=1)
     net = ORC.feedforward(layers, fanout, weight, 11, lif=lif)
-    if mode == "sort":
-        monkeypatch.setenv("SNN_B200_ORDERED_SORT", "1")
-    o = ordered()
+    o = ordered() if mode == "ordered" else opts(propagation=sb.PROPAGATE_PUSH_BINNED)
     ctx = sb.CudaContext.feedforward(layers, fanout, weight, 11, lif=lif_to_sb(lif), options=o)
     rng = np.random.default_rng(4)
     n = net.neuron_count
