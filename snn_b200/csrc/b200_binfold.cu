@@ -132,37 +132,15 @@ __device__ __forceinline__ unsigned long long block_sum_u64(unsigned long long v
 
 // ------------------------------------------------- ordered compaction ----
 // Per-chunk popcounts of the (global) bitmap; also the popcount of this
-// rank's own words [own_begin, own_end) into ctr->spikes. With a peer wait
-// (the exchange fused into LIF), every CTA first waits (bounded) for all
-// ranks' flags of this step.
-__global__ void __launch_bounds__(kBfThreads) chunk_counts_kernel(const uint32_t *__restrict__ bitmap, uint64_t words,
+// rank's own words [own_begin, own_end) into ctr->spikes. With a peer wait,
+// every CTA first waits (bounded) for all ranks' flags of this step and
+// gathers the other ranks' words into `bitmap` as it counts them.
+__global__ void __launch_bounds__(kBfThreads) chunk_counts_kernel(uint32_t *__restrict__ bitmap, uint64_t words,
                                                                   uint32_t *__restrict__ ccnt, DevCounters *ctr,
                                                                   uint64_t own_begin, uint64_t own_end, PeerWait pw) {
     if (pw.nflags) {
         __shared__ uint32_t s_ok;
-        if (threadIdx.x == 0) {
-            uint32_t ok = 1u;
-            const unsigned long long t0 = blockIdx.x == 0 ? global_ns() : 0ull;
-            for (uint32_t r = 0; r < pw.nflags && ok; ++r) {
-                for (uint32_t it = 0;; ++it) {
-                    unsigned long long v;
-                    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(pw.flags + r) : "memory");
-                    if (v >= pw.tag) break;
-                    if (*(volatile uint32_t *)&ctr->error != 0u || it >= pw.spin_limit) {
-                        atomicExch(&ctr->error, 3u);
-                        ok = 0u;
-                        break;
-                    }
-                    __nanosleep(64);
-                }
-            }
-            s_ok = ok;
-            if (blockIdx.x == 0) {
-                const unsigned long long dt = global_ns() - t0;
-                ctr->wait_ns += dt;
-                if (dt > ctr->wait_max_ns) ctr->wait_max_ns = dt;
-            }
-        }
+        if (threadIdx.x == 0) s_ok = wait_peer_flags(pw, ctr, blockIdx.x == 0) ? 1u : 0u;
         __syncthreads();
         if (!s_ok) return;
     }
@@ -174,7 +152,7 @@ __global__ void __launch_bounds__(kBfThreads) chunk_counts_kernel(const uint32_t
         for (uint32_t k = threadIdx.x; k < kChunkWords; k += kBfThreads) {
             const uint64_t wi = w0 + k;
             if (wi < words) {
-                const uint32_t p = __popc(__ldcg(bitmap + wi));
+                const uint32_t p = __popc(pw.nflags ? gather_word(pw, bitmap, wi) : __ldcg(bitmap + wi));
                 cnt += p;
                 if (wi >= own_begin && wi < own_end) own += p;
             }
@@ -508,7 +486,7 @@ cudaError_t binfold_scan(cudaStream_t s, const uint32_t *hist, uint32_t *offs, u
     return cub::DeviceScan::ExclusiveSum(temp, *temp_bytes, hist, offs, (int64_t)n, s);
 }
 
-void launch_compact_ordered(cudaStream_t s, int device, const uint32_t *bitmap, uint64_t words, uint32_t *ccnt,
+void launch_compact_ordered(cudaStream_t s, int device, uint32_t *bitmap, uint64_t words, uint32_t *ccnt,
                             void *list, int idx_bits, DevCounters *ctr, int parity, uint64_t own_begin,
                             uint64_t own_end, const uint64_t *row_ptr, uint64_t batch_rows, const PeerWait *wait) {
     PeerWait pw{};

@@ -36,7 +36,7 @@ cudaError_t binfold_scan(cudaStream_t s, const uint32_t *hist, uint32_t *offs, u
 // ascending spike list of parity `parity`; adds the own-range popcount to
 // ctr->spikes and the spiking rows' degrees to ctr->step_events[parity].
 // With a peer wait, first waits (bounded) for every rank's flag.
-void launch_compact_ordered(cudaStream_t s, int device, const uint32_t *bitmap, uint64_t words, uint32_t *ccnt,
+void launch_compact_ordered(cudaStream_t s, int device, uint32_t *bitmap, uint64_t words, uint32_t *ccnt,
                             void *list, int idx_bits, DevCounters *ctr, int parity, uint64_t own_begin,
                             uint64_t own_end, const uint64_t *row_ptr, uint64_t batch_rows,
                             const PeerWait *wait = nullptr);

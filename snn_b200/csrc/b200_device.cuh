@@ -49,5 +49,45 @@ __device__ __forceinline__ unsigned long long global_ns() {
     return t;
 }
 
+// One thread waits (bounded) until every flag of pw reaches pw.tag; false
+// when the wait expired or another wait already failed (ctr->error is set).
+// timed: add the wait to ctr->wait_ns / wait_max_ns.
+__device__ __forceinline__ bool wait_peer_flags(const PeerWait &pw, DevCounters *ctr, bool timed) {
+    bool ok = true;
+    const unsigned long long t0 = timed ? global_ns() : 0ull;
+    for (uint32_t r = 0; r < pw.nflags && ok; ++r) {
+        for (uint32_t it = 0;; ++it) {
+            unsigned long long v;
+            asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(pw.flags + r) : "memory");
+            if (v >= pw.tag) break;
+            if (*(volatile uint32_t *)&ctr->error != 0u || it >= pw.spin_limit) {
+                atomicExch(&ctr->error, 3u);
+                ok = false;
+                break;
+            }
+            __nanosleep(64);
+        }
+    }
+    if (timed) {
+        const unsigned long long dt = global_ns() - t0;
+        ctr->wait_ns += dt;
+        if (dt > ctr->wait_max_ns) ctr->wait_max_ns = dt;
+    }
+    return ok;
+}
+
+// Word wi of the global bitmap after the peer wait: this rank's words from
+// the local buffer, the others read from their owner over NVLink (relaxed,
+// system scope: ordered after the flag acquire by the CTA barrier) and
+// stored into the local buffer.
+__device__ __forceinline__ uint32_t gather_word(const PeerWait &pw, uint32_t *local, uint64_t wi) {
+    const uint32_t r = (uint32_t)(wi / pw.slot_words);
+    if (r == pw.rank) return __ldcg(local + wi);
+    uint32_t v;
+    asm volatile("ld.relaxed.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(pw.src[r] + wi) : "memory");
+    local[wi] = v;
+    return v;
+}
+
 }  // namespace dev
 }  // namespace b200

@@ -147,8 +147,7 @@ __global__ void __launch_bounds__(kLifThreads) lif_kernel(uint64_t n, LifArgs p,
                                                           const float *__restrict__ ext,
                                                           uint32_t *__restrict__ refr, uint8_t *__restrict__ spikes,
                                                           uint32_t *__restrict__ bitmap, TIdx *__restrict__ list,
-                                                          uint64_t global_offset, DevCounters *ctr, int parity,
-                                                          PeerArgs peer) {
+                                                          uint64_t global_offset, DevCounters *ctr, int parity) {
     constexpr uint64_t kTile = (uint64_t)ITERS * kLifThreads * 4u;
     // The step's injection (stream order: already complete) has read the
     // index; advance it for the next step.
@@ -156,7 +155,6 @@ __global__ void __launch_bounds__(kLifThreads) lif_kernel(uint64_t n, LifArgs p,
     __shared__ TIdx sbuf[WRITE_LIST ? kTile : 1];
     __shared__ uint32_t warp_tot[kLifThreads / 32];
     __shared__ uint32_t s_base;
-    __shared__ uint32_t s_words[kTile / 32];  // this tile's bitmap words, for the peer stores
     const unsigned lane = lane_id();
     const unsigned warp = threadIdx.x >> 5;
     const uint64_t tiles = (n + kTile - 1) / kTile;
@@ -207,10 +205,7 @@ __global__ void __launch_bounds__(kLifThreads) lif_kernel(uint64_t n, LifArgs p,
             word |= __shfl_xor_sync(kFull, word, 1);
             word |= __shfl_xor_sync(kFull, word, 2);
             word |= __shfl_xor_sync(kFull, word, 4);
-            if ((lane & 7u) == 0u && i0 < n) {
-                bitmap[i0 >> 5] = word;
-                if (peer.npeers) s_words[it * (kLifThreads / 8) + (threadIdx.x >> 3)] = word;
-            }
+            if ((lane & 7u) == 0u && i0 < n) bitmap[i0 >> 5] = word;
             if (WRITE_LIST) {
                 const uint32_t cnt = __popc(nib);
                 uint32_t incl = cnt;
@@ -237,17 +232,6 @@ __global__ void __launch_bounds__(kLifThreads) lif_kernel(uint64_t n, LifArgs p,
                 block_off += total;
             }
         }
-        if (peer.npeers) {
-            // Fused all-gather: the tile's words go to every rank's exchange
-            // buffer over NVLink as coalesced runs of plain peer stores.
-            __syncthreads();
-            const uint64_t w0 = tile * (kTile / 32);
-            const uint64_t nw = min((uint64_t)(kTile / 32), (n + 31) / 32 - w0);
-            for (uint32_t q = 0; q < peer.npeers; ++q)
-                for (uint32_t k = threadIdx.x; k < nw; k += kLifThreads)
-                    peer.dst[q][peer.word_offset + w0 + k] = s_words[k];
-            __syncthreads();
-        }
         if (WRITE_LIST) {
             if (threadIdx.x == 0) s_base = block_off ? atomicAdd(&ctr->list_count[parity], block_off) : 0u;
             __syncthreads();
@@ -257,55 +241,27 @@ __global__ void __launch_bounds__(kLifThreads) lif_kernel(uint64_t n, LifArgs p,
             __syncthreads();
         }
     }
-    if (peer.npeers) {
-        // Publish: every CTA's peer stores become visible system-wide before
-        // its ticket; the last CTA then raises this rank's flag everywhere.
-        __syncthreads();
-        if (threadIdx.x == 0) {
-            __threadfence_system();
-            const uint32_t t = atomicAdd(peer.ticket, 1u);
-            if (t == gridDim.x - 1) {
-                __threadfence_system();
-                for (uint32_t q = 0; q < peer.npeers; ++q)
-                    asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(peer.flag[q]), "l"(peer.tag) : "memory");
-                *peer.ticket = 0u;
-            }
-        }
-    }
+}
+
+// Peer exchange publication, launched right after the LIF kernel on the same
+// stream: the LIF kernel's words are complete and visible when it starts, and
+// its release store of the step tag into this rank's flag slot of every rank
+// lets the others read them after an acquire.
+__global__ void publish_flags_kernel(PeerArgs peer) {
+    if (threadIdx.x < peer.npeers)
+        asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(peer.flag[threadIdx.x]), "l"(peer.tag) : "memory");
 }
 
 // ---------------------------------------------------------- compaction ----
 template <typename TIdx>
-__global__ void __launch_bounds__(256) compact_kernel(const uint32_t *__restrict__ bitmap, uint64_t words,
+__global__ void __launch_bounds__(256) compact_kernel(uint32_t *__restrict__ bitmap, uint64_t words,
                                                       TIdx *__restrict__ list, DevCounters *ctr, int parity,
                                                       uint64_t own_begin, uint64_t own_end, PeerWait pw) {
     const unsigned lane = lane_id();
     if (pw.nflags) {
         // Wait (bounded) until every rank has published this step's slice.
         __shared__ uint32_t s_ok;
-        if (threadIdx.x == 0) {
-            uint32_t ok = 1u;
-            const unsigned long long t0 = blockIdx.x == 0 ? global_ns() : 0ull;
-            for (uint32_t r = 0; r < pw.nflags && ok; ++r) {
-                for (uint32_t it = 0;; ++it) {
-                    unsigned long long v;
-                    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(pw.flags + r) : "memory");
-                    if (v >= pw.tag) break;
-                    if (*(volatile uint32_t *)&ctr->error != 0u || it >= pw.spin_limit) {
-                        atomicExch(&ctr->error, 3u);
-                        ok = 0u;
-                        break;
-                    }
-                    __nanosleep(64);
-                }
-            }
-            s_ok = ok;
-            if (blockIdx.x == 0) {
-                const unsigned long long dt = global_ns() - t0;
-                ctr->wait_ns += dt;
-                if (dt > ctr->wait_max_ns) ctr->wait_max_ns = dt;
-            }
-        }
+        if (threadIdx.x == 0) s_ok = wait_peer_flags(pw, ctr, blockIdx.x == 0) ? 1u : 0u;
         __syncthreads();
         if (!s_ok) return;
     }
@@ -313,7 +269,7 @@ __global__ void __launch_bounds__(256) compact_kernel(const uint32_t *__restrict
     uint32_t own = 0;
     for (uint64_t base = (uint64_t)blockIdx.x * blockDim.x; base < words; base += stride) {
         const uint64_t wi = base + threadIdx.x;
-        const uint32_t word = wi < words ? __ldcg(bitmap + wi) : 0u;
+        const uint32_t word = wi >= words ? 0u : pw.nflags ? gather_word(pw, bitmap, wi) : __ldcg(bitmap + wi);
         const uint32_t cnt = __popc(word);
         if (wi >= own_begin && wi < own_end) own += cnt;
         uint32_t incl = cnt;
@@ -345,7 +301,7 @@ __global__ void __launch_bounds__(256) compact_kernel(const uint32_t *__restrict
 // once per step and must not push the L2-resident target currents out),
 // software-pipelined one vector deep, and every edge issues a fire-and-forget
 // red.global.add.f32 into next_current, which stays L2-resident.
-template <typename TCol>
+template <typename TCol, int LANES = 32>
 __device__ __forceinline__ void push_row(uint64_t b, uint64_t e, const TCol *__restrict__ col,
                                          const float *__restrict__ w, float *__restrict__ next, unsigned lane) {
     using V = typename Vec16<TCol>::type;
@@ -365,7 +321,7 @@ __device__ __forceinline__ void push_row(uint64_t b, uint64_t e, const TCol *__r
         x0 = __ldcs(wv + k);
     }
     while (k < nvec) {
-        const uint64_t k1 = k + 32u;
+        const uint64_t k1 = k + (uint64_t)LANES;
         V c1;
         FV x1;
         if (k1 < nvec) {
@@ -382,7 +338,9 @@ __device__ __forceinline__ void push_row(uint64_t b, uint64_t e, const TCol *__r
     if (lane < e - t0) red_add(next + col[t0 + lane], w[t0 + lane]);
 }
 
-template <typename TIdx, typename TCol>
+// LANES lanes per spiking row (32: a warp; 16 or 8 for short rows, such as
+// a shard's slice of a row, so that a warp has several rows in flight).
+template <typename TIdx, typename TCol, int LANES>
 __global__ void __launch_bounds__(256) propagate_push_kernel(const TIdx *__restrict__ list,
                                                              const uint64_t *__restrict__ row_ptr,
                                                              const TCol *__restrict__ col,
@@ -391,9 +349,9 @@ __global__ void __launch_bounds__(256) propagate_push_kernel(const TIdx *__restr
                                                              uint64_t batch_rows, uint32_t pull_above) {
     const uint32_t count = *(volatile uint32_t *)&ctr->list_count[parity];
     if (pull_above && count > pull_above) return;  // dense step: the pull kernel runs
-    const unsigned lane = lane_id();
-    const uint64_t gwarp = ((uint64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-    const uint64_t nwarps = ((uint64_t)gridDim.x * blockDim.x) >> 5;
+    const unsigned lane = lane_id() % LANES;
+    const uint64_t gwarp = ((uint64_t)blockIdx.x * blockDim.x + threadIdx.x) / LANES;
+    const uint64_t nwarps = ((uint64_t)gridDim.x * blockDim.x) / LANES;
     unsigned long long events = 0;
     for (uint64_t s = gwarp; s < count; s += nwarps) {
         uint64_t row = (uint64_t)list[s];
@@ -406,7 +364,7 @@ __global__ void __launch_bounds__(256) propagate_push_kernel(const TIdx *__restr
         const uint64_t b = row_ptr[row];
         const uint64_t e = row_ptr[row + 1];
         events += e - b;
-        push_row<TCol>(b, e, col, w, dst, lane);
+        push_row<TCol, LANES>(b, e, col, w, dst, lane);
     }
     block_add_u64(lane == 0 ? events : 0ull, &ctr->events);
     step_epilogue(ctr, parity, count_spikes, count);
@@ -628,10 +586,14 @@ __global__ void __launch_bounds__(kPullSmemThreads, 1)
     const unsigned lane = lane_id();
     const unsigned warp = threadIdx.x >> 5;
     const uint64_t blocks = (n_local + 31) / 32;
-    constexpr uint64_t kSweep = (kPullSmemThreads / 32) * kPullBlocksPerWarp;
-    const uint64_t sweeps = (blocks + kSweep - 1) / kSweep;
-    for (uint64_t sw = blockIdx.x; sw < sweeps; sw += gridDim.x) {
-        const uint64_t b0 = sw * kSweep + (uint64_t)warp * kPullBlocksPerWarp;
+    constexpr uint64_t kWarps = kPullSmemThreads / 32;
+    constexpr uint64_t kSweep = kWarps * kPullBlocksPerWarp;
+    // Each CTA owns an equal contiguous range of target blocks, visited in
+    // sweeps of up to kSweep blocks; inside a sweep block j of warp w is
+    // sweep_base + j * kWarps + w, so a short last sweep still spreads over
+    // the warps.
+    const uint64_t c_lo = blocks * blockIdx.x / gridDim.x, c_hi = blocks * (blockIdx.x + 1) / gridDim.x;
+    for (uint64_t sb = c_lo; sb < c_hi; sb += kSweep) {
         float acc[kPullBlocksPerWarp];
 #pragma unroll
         for (int j = 0; j < kPullBlocksPerWarp; ++j) acc[j] = 0.0f;
@@ -652,8 +614,8 @@ __global__ void __launch_bounds__(kPullSmemThreads, 1)
             __syncthreads();
 #pragma unroll
             for (int j = 0; j < kPullBlocksPerWarp; ++j) {
-                const uint64_t b = b0 + j;
-                if (b >= blocks) break;
+                const uint64_t b = sb + (uint64_t)j * kWarps + warp;
+                if (b >= c_hi) break;
                 const uint64_t base = sell_off[b * chunks + c];
                 const uint64_t width = (sell_off[b * chunks + c + 1] - base) / 32;
                 const uint2 *sp = slots + base + lane;
@@ -694,8 +656,9 @@ __global__ void __launch_bounds__(kPullSmemThreads, 1)
         }
 #pragma unroll
         for (int j = 0; j < kPullBlocksPerWarp; ++j) {
-            const uint64_t t = (b0 + j) * 32u + lane;
-            if (b0 + j < blocks && t < n_local) next[t] = acc[j];
+            const uint64_t b = sb + (uint64_t)j * kWarps + warp;
+            const uint64_t t = b * 32u + lane;
+            if (b < c_hi && t < n_local) next[t] = acc[j];
         }
     }
     // Event statistics: out-degree (towards this rank) of every spiking row.
@@ -1085,38 +1048,40 @@ void launch_init_state(cudaStream_t s, uint64_t n, float v_rest, float *v, float
 template <bool EXT, typename TIdx, int ITERS>
 static void lif_dispatch(cudaStream_t s, int device, uint64_t n, const LifArgs &p, float *v, float *cur,
                          const float *ext, uint32_t *refr, uint8_t *spikes, uint32_t *bitmap, void *list,
-                         uint64_t off, DevCounters *ctr, int parity, const PeerArgs &peer) {
+                         uint64_t off, DevCounters *ctr, int parity) {
     constexpr uint64_t tile = (uint64_t)ITERS * kLifThreads * 4u;
     const int grid = grid_for(device, 6, n, tile);
     if (list != nullptr)
         lif_kernel<EXT, true, TIdx, ITERS><<<grid, kLifThreads, 0, s>>>(n, p, v, cur, ext, refr, spikes, bitmap,
-                                                                        (TIdx *)list, off, ctr, parity, peer);
+                                                                        (TIdx *)list, off, ctr, parity);
     else
         lif_kernel<EXT, false, TIdx, ITERS><<<grid, kLifThreads, 0, s>>>(n, p, v, cur, ext, refr, spikes, bitmap,
-                                                                         (TIdx *)list, off, ctr, parity, peer);
+                                                                         (TIdx *)list, off, ctr, parity);
 }
 
 void launch_lif(cudaStream_t s, int device, uint64_t n, const LifArgs &p, float *v, float *cur, const float *ext,
                 uint32_t *refr, uint8_t *spikes, uint32_t *bitmap, void *list, int idx_bits, uint64_t off,
                 DevCounters *ctr, int parity, const PeerArgs *peer_in) {
-    PeerArgs peer{};
-    if (peer_in) peer = *peer_in;
-    if (n == 0 && peer.npeers == 0) return;
+    if (n == 0) {
+        if (peer_in && peer_in->npeers) publish_flags_kernel<<<1, 32, 0, s>>>(*peer_in);
+        return;
+    }
     // Small populations: 1024-neuron tiles, so the grid still covers the SMs.
     const bool small = n < (uint64_t)sm_count(device) * 2u * kLifThreads * 4u * 8u;
     if (idx_bits == 32 && small) {
-        if (ext) lif_dispatch<true, uint32_t, 1>(s, device, n, p, v, cur, ext, refr, spikes, bitmap, list, off, ctr, parity, peer);
-        else lif_dispatch<false, uint32_t, 1>(s, device, n, p, v, cur, ext, refr, spikes, bitmap, list, off, ctr, parity, peer);
+        if (ext) lif_dispatch<true, uint32_t, 1>(s, device, n, p, v, cur, ext, refr, spikes, bitmap, list, off, ctr, parity);
+        else lif_dispatch<false, uint32_t, 1>(s, device, n, p, v, cur, ext, refr, spikes, bitmap, list, off, ctr, parity);
     } else if (idx_bits == 32) {
-        if (ext) lif_dispatch<true, uint32_t, 8>(s, device, n, p, v, cur, ext, refr, spikes, bitmap, list, off, ctr, parity, peer);
-        else lif_dispatch<false, uint32_t, 8>(s, device, n, p, v, cur, ext, refr, spikes, bitmap, list, off, ctr, parity, peer);
+        if (ext) lif_dispatch<true, uint32_t, 8>(s, device, n, p, v, cur, ext, refr, spikes, bitmap, list, off, ctr, parity);
+        else lif_dispatch<false, uint32_t, 8>(s, device, n, p, v, cur, ext, refr, spikes, bitmap, list, off, ctr, parity);
     } else {
-        if (ext) lif_dispatch<true, uint64_t, 4>(s, device, n, p, v, cur, ext, refr, spikes, bitmap, list, off, ctr, parity, peer);
-        else lif_dispatch<false, uint64_t, 4>(s, device, n, p, v, cur, ext, refr, spikes, bitmap, list, off, ctr, parity, peer);
+        if (ext) lif_dispatch<true, uint64_t, 4>(s, device, n, p, v, cur, ext, refr, spikes, bitmap, list, off, ctr, parity);
+        else lif_dispatch<false, uint64_t, 4>(s, device, n, p, v, cur, ext, refr, spikes, bitmap, list, off, ctr, parity);
     }
+    if (peer_in && peer_in->npeers) publish_flags_kernel<<<1, 32, 0, s>>>(*peer_in);
 }
 
-void launch_compact(cudaStream_t s, int device, const uint32_t *bitmap, uint64_t words, void *list, int idx_bits,
+void launch_compact(cudaStream_t s, int device, uint32_t *bitmap, uint64_t words, void *list, int idx_bits,
                     DevCounters *ctr, int parity, uint64_t own_begin, uint64_t own_end, const PeerWait *wait) {
     PeerWait pw{};
     if (wait) pw = *wait;
@@ -1127,34 +1092,55 @@ void launch_compact(cudaStream_t s, int device, const uint32_t *bitmap, uint64_t
         compact_kernel<uint64_t><<<grid, 256, 0, s>>>(bitmap, words, (uint64_t *)list, ctr, parity, own_begin, own_end, pw);
 }
 
-template <typename TIdx, typename TCol>
+template <typename TIdx, typename TCol, int LANES>
 static int push_grid(int device) {
-    static int blocks_per_sm[2] = {0, 0};
-    int &b = blocks_per_sm[sizeof(TCol) == 8];
-    if (b == 0) {
+    static int blocks_per_sm = 0;
+    if (blocks_per_sm == 0) {
         int v = 0;
-        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&v, propagate_push_kernel<TIdx, TCol>, 256, 0) !=
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&v, propagate_push_kernel<TIdx, TCol, LANES>, 256, 0) !=
                 cudaSuccess ||
             v <= 0)
             v = 4;
-        b = v;
+        blocks_per_sm = v;
     }
-    return sm_count(device) * b;
+    return sm_count(device) * blocks_per_sm;
+}
+
+template <typename TI, typename TC>
+static void push_dispatch(cudaStream_t s, int device, const void *list, const uint64_t *row_ptr, const void *col,
+                          const float *w, float *next, DevCounters *ctr, int parity, int count_spikes,
+                          uint64_t batch_rows, uint32_t pull_above, uint32_t lanes) {
+#define B200_PUSH(L)                                                                                            \
+    propagate_push_kernel<TI, TC, L><<<push_grid<TI, TC, L>(device), 256, 0, s>>>(                              \
+        (const TI *)list, row_ptr, (const TC *)col, w, next, ctr, parity, count_spikes, batch_rows, pull_above)
+    if (lanes <= 8) B200_PUSH(8);
+    else if (lanes <= 16) B200_PUSH(16);
+    else B200_PUSH(32);
+#undef B200_PUSH
 }
 
 void launch_propagate_push(cudaStream_t s, int device, const void *list, int idx_bits, const uint64_t *row_ptr,
                            const void *col, int col_bits, const float *w, float *next, DevCounters *ctr, int parity,
-                           int count_spikes, uint64_t batch_rows, uint32_t pull_above) {
-#define B200_PUSH(TI, TC)                                                                                      \
-    propagate_push_kernel<TI, TC><<<push_grid<TI, TC>(device), 256, 0, s>>>((const TI *)list, row_ptr,         \
-                                                                            (const TC *)col, w, next, ctr,     \
-                                                                            parity, count_spikes, batch_rows,  \
-                                                                            pull_above)
-    if (idx_bits == 32 && col_bits == 32) B200_PUSH(uint32_t, uint32_t);
-    else if (idx_bits == 32) B200_PUSH(uint32_t, uint64_t);
-    else if (col_bits == 32) B200_PUSH(uint64_t, uint32_t);
-    else B200_PUSH(uint64_t, uint64_t);
-#undef B200_PUSH
+                           int count_spikes, uint64_t batch_rows, uint32_t pull_above, uint32_t lanes) {
+    if (idx_bits == 32 && col_bits == 32)
+        push_dispatch<uint32_t, uint32_t>(s, device, list, row_ptr, col, w, next, ctr, parity, count_spikes,
+                                          batch_rows, pull_above, lanes);
+    else if (idx_bits == 32)
+        push_dispatch<uint32_t, uint64_t>(s, device, list, row_ptr, col, w, next, ctr, parity, count_spikes,
+                                          batch_rows, pull_above, lanes);
+    else if (col_bits == 32)
+        push_dispatch<uint64_t, uint32_t>(s, device, list, row_ptr, col, w, next, ctr, parity, count_spikes,
+                                          batch_rows, pull_above, lanes);
+    else
+        push_dispatch<uint64_t, uint64_t>(s, device, list, row_ptr, col, w, next, ctr, parity, count_spikes,
+                                          batch_rows, pull_above, lanes);
+}
+
+uint32_t push_lanes(uint64_t synapses, uint64_t rows) {
+    // About two 16-byte vectors per lane per row: rows of up to ~256 edges
+    // share a warp between several rows.
+    const uint64_t avg = rows ? synapses / rows : 0;
+    return avg >= 512 ? 32u : avg >= 160 ? 16u : 8u;
 }
 
 // SNN_B200_PULL_CHUNK_WORDS (environment, read when a layout is built)
@@ -1179,6 +1165,8 @@ void launch_propagate_pull(cudaStream_t s, int device, uint64_t n_local, uint32_
         const uint64_t blocks = (n_local + 31) / 32;
         const uint64_t sweeps = (blocks + (kPullSmemThreads / 32) * kPullBlocksPerWarp - 1) /
                                 ((kPullSmemThreads / 32) * kPullBlocksPerWarp);
+        // One CTA per SM (a chunk of spike bits fills its shared memory);
+        // fewer when there are fewer sweeps than SMs.
         const int grid = (int)std::max<uint64_t>(1, std::min<uint64_t>(sweeps, (uint64_t)sm_count(device)));
         const size_t smem = (size_t)(chunk_words + 1) * 4;
 #define B200_PULLS(TI)                                                                                          \

@@ -51,26 +51,31 @@ struct DevCounters {
 };
 static_assert(sizeof(DevCounters) <= 256, "DevCounters must fit its 256-byte block");
 
-// Peer (NVLink, CUDA IPC) spike-bitmap exchange fused into the LIF kernel:
-// every bitmap word a rank computes is also stored into each rank's exchange
-// buffer; the LIF grid's last CTA then publishes `tag` into every rank's
-// flag slot for this rank. npeers == 0 disables it.
+// Peer (NVLink, CUDA IPC) spike-bitmap exchange, pull style. The LIF kernel
+// writes this rank's bitmap words into its own exchange buffer (passed as its
+// bitmap); a one-CTA kernel launched behind it on the same stream then
+// releases `tag` into this rank's flag slot of every rank (st.release.sys).
+// npeers == 0 disables it.
 constexpr uint32_t kMaxPeers = 8;
 struct PeerArgs {
-    uint32_t *dst[kMaxPeers];             // exchange bitmap (this step's parity) of each rank
     unsigned long long *flag[kMaxPeers];  // this rank's flag slot in each rank's exchange buffer
-    uint32_t *ticket;                     // local CTA-completion counter (returns to 0)
-    uint64_t word_offset;                 // first word of this rank's slice
     unsigned long long tag;               // monotonic exchange step, published when done
     uint32_t npeers;
 };
-// Wait side of the exchange, done by the compaction kernel before it reads
-// the assembled bitmap: all `nflags` flags must reach `tag` (bounded wait).
+// Wait side, done by the compaction before it reads the global bitmap: all
+// `nflags` flags (in the local buffer) must reach `tag` (bounded wait); then
+// the words of every other rank r are read from src[r] (that rank's exchange
+// buffer of this parity, over NVLink) and stored into the local buffer, so
+// the local buffer holds the whole global bitmap afterwards. Rank r owns
+// words [r * slot_words, (r + 1) * slot_words).
 struct PeerWait {
     const unsigned long long *flags;
     unsigned long long tag;
     uint32_t nflags;
     uint32_t spin_limit;
+    const uint32_t *src[kMaxPeers];
+    uint64_t slot_words;
+    uint32_t rank;
 };
 
 // Network generator description shared by the random-pool and the layered
@@ -113,18 +118,23 @@ void launch_lif(cudaStream_t s, int device, uint64_t n, const LifArgs &p, float 
                 uint32_t *refr, uint8_t *spikes, uint32_t *bitmap, void *list, int idx_bits, uint64_t global_offset,
                 DevCounters *ctr, int parity, const PeerArgs *peer = nullptr);
 
-// Global bitmap -> spike list (sharded contexts, after the all-gather).
+// Global bitmap -> spike list (sharded contexts, after the all-gather; with a
+// peer wait, the other ranks' words are first gathered into `bitmap`).
 // Also adds the popcount of words [own_begin, own_end) to ctr->spikes.
-void launch_compact(cudaStream_t s, int device, const uint32_t *bitmap, uint64_t words, void *list, int idx_bits,
+void launch_compact(cudaStream_t s, int device, uint32_t *bitmap, uint64_t words, void *list, int idx_bits,
                     DevCounters *ctr, int parity, uint64_t own_begin, uint64_t own_end, const PeerWait *wait = nullptr);
 
 // Push propagation from the spike list over a resident CSR.
 // col_bits = 32 or 64 (local target ids), idx_bits = spike list width.
 // batch_rows != 0: batched states; list id g is row g % batch_rows of the
 // topology adding into the current slice starting at g - g % batch_rows.
+// lanes: 32, 16 or 8 lanes per spiking row (push_lanes picks it from the
+// average row length).
 void launch_propagate_push(cudaStream_t s, int device, const void *list, int idx_bits, const uint64_t *row_ptr,
                            const void *col, int col_bits, const float *w, float *next, DevCounters *ctr,
-                           int parity, int count_spikes, uint64_t batch_rows = 0, uint32_t pull_above = 0);
+                           int parity, int count_spikes, uint64_t batch_rows = 0, uint32_t pull_above = 0,
+                           uint32_t lanes = 32);
+uint32_t push_lanes(uint64_t synapses, uint64_t rows);
 
 // Ordered pull over a sliced-ELL CSC: local targets in blocks of 32,
 // presynaptic ids cut into `chunks` chunks of chunk_words * 32 ids; the slots

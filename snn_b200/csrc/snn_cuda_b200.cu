@@ -156,7 +156,8 @@ struct snn_cuda_context {
     // compaction, per-tile counts, stable scatter and shared-memory fold, all
     // gated on the device against the pull for steps above bf_gate events.
     bool binfold = false;
-    bool want_binfold = false;  // SNN_B200_PROPAGATE_PUSH_BINNED: the bin-fold rather than the event sort
+    bool want_binfold = false;
+    uint32_t push_lanes = 0;  // lanes per spiking row of the push kernel (0: not chosen yet)  // SNN_B200_PROPAGATE_PUSH_BINNED: the bin-fold rather than the event sort
     b200::BinFoldPlan bf{};
     b200::BinFoldBuffers bfb{};
     uint64_t bf_cap = 0;
@@ -1105,19 +1106,28 @@ snn_status_t enqueue_step(snn_cuda_context_t *c, bool has_ext) {
         return SNN_ERR_INVALID_ARGUMENT;
     }
     b200::PeerArgs pa{};
-    uint32_t *xbitmap = nullptr;  // this step's assembled global bitmap (peer exchange)
+    b200::PeerWait pw{};
+    uint32_t *xbitmap = nullptr;  // this step's global bitmap in the local exchange buffer (peer exchange)
     if (peer) {
+        // Pull exchange: LIF writes this rank's words into its own buffer of
+        // this parity and releases its flag at every rank; the compaction
+        // waits for every flag and reads the other ranks' words over NVLink.
         ++c->xstep;
         const uint64_t par = c->xstep & 1u;
         for (uint32_t r = 0; r < c->world; ++r) {
-            pa.dst[r] = c->peer_x[r] + par * c->bitmap_words;
             pa.flag[r] = (unsigned long long *)((char *)c->peer_x[r] + xflags_offset(c)) + c->rank;
+            pw.src[r] = c->peer_x[r] + par * c->bitmap_words;
         }
         pa.npeers = c->world;
-        pa.word_offset = (uint64_t)c->rank * (c->slot / 32);
         pa.tag = c->xstep;
-        pa.ticket = (uint32_t *)((char *)c->d_xbuf + xflags_offset(c) + c->world * 8);
         xbitmap = (uint32_t *)c->d_xbuf + par * c->bitmap_words;
+        own_bitmap = xbitmap + (uint64_t)c->rank * (c->slot / 32);
+        pw.flags = (const unsigned long long *)((char *)c->d_xbuf + xflags_offset(c));
+        pw.tag = c->xstep;
+        pw.nflags = c->world;
+        pw.spin_limit = c->peer_spin_limit;
+        pw.slot_words = c->slot / 32;
+        pw.rank = c->rank;
     }
     b200::LifArgs lif_args = c->args;
     if (c->dev_stream_step) lif_args.stream_step = &c->d_ctr->stream_step;
@@ -1129,6 +1139,7 @@ snn_status_t enqueue_step(snn_cuda_context_t *c, bool has_ext) {
                      c->d_ctr, parity, peer ? &pa : nullptr);
     snn_status_t st = check_launch(c);
     if (st != SNN_OK) return st;
+    if (peer) c->launches++;  // the flag publication behind the LIF kernel
     timing_mark(c, tg, 1);
     if (c->spk_dst != nullptr) {
         // The spikes are final once LIF is done; download them while the
@@ -1144,10 +1155,8 @@ snn_status_t enqueue_step(snn_cuda_context_t *c, bool has_ext) {
     const uint64_t brows = c->batch > 1 ? c->n_rows : 0;
     if (ordered_list) {
         // Ascending spike list (and the step's event total) from the bitmap:
-        // assembled by the peer stores (after the flag waits), by the NCCL
-        // all-gather, or this rank's own.
-        const b200::PeerWait pw{peer ? (const unsigned long long *)((char *)c->d_xbuf + xflags_offset(c)) : nullptr,
-                                c->xstep, peer ? c->world : 0u, c->peer_spin_limit};
+        // gathered from the peers (after the flag waits), assembled by the
+        // NCCL all-gather, or this rank's own.
         if (sharded && !peer) {
             const ncclResult_t r =
                 ncclAllGather(own_bitmap, c->d_bitmap, c->slot / 32, ncclUint32, c->comm, c->stream);
@@ -1162,10 +1171,8 @@ snn_status_t enqueue_step(snn_cuda_context_t *c, bool has_ext) {
         c->launches += 2;
         if ((st = cuda_status(cudaGetLastError())) != SNN_OK) return st;
     } else if (peer) {
-        // LIF already stored this rank's words into every rank's buffer and
-        // raised its flag; the compaction waits for all flags of this step.
-        const b200::PeerWait pw{(const unsigned long long *)((char *)c->d_xbuf + xflags_offset(c)), c->xstep,
-                                c->world, c->peer_spin_limit};
+        // The compaction waits for all flags of this step and gathers the
+        // other ranks' words into the local buffer as it compacts.
         b200::launch_compact(c->stream, c->device, xbitmap, c->bitmap_words, c->d_list, c->idx_bits, c->d_ctr,
                              parity, c->lo / 32, ceil_div(c->hi, 32), &pw);
         c->launches++;
@@ -1206,11 +1213,18 @@ snn_status_t enqueue_step(snn_cuda_context_t *c, bool has_ext) {
                                          peer ? xbitmap : c->d_bitmap, c->bitmap_words, next, c->d_list, c->idx_bits,
                                         c->d_deg, c->d_ctr, parity, !sharded);
         else {
+            if (c->push_lanes == 0) {
+                // From the average row length of this rank's topology;
+                // SNN_B200_PUSH_LANES (environment: 8, 16 or 32) overrides it.
+                c->push_lanes = b200::push_lanes(c->e_local, c->n_rows);
+                if (const char *env = std::getenv("SNN_B200_PUSH_LANES")) c->push_lanes = (uint32_t)std::atoi(env);
+            }
             // With a SELL CSC both kernels are launched behind the same
             // device-side gate on this step's spike count: one of them runs.
             b200::launch_propagate_push(c->stream, c->device, c->d_list, c->idx_bits, c->d_row_ptr, c->d_col,
                                         c->col_bits, c->d_w, next, c->d_ctr, parity, !sharded,
-                                        c->batch > 1 ? c->n_rows : 0, c->has_csc ? c->pull_above : 0);
+                                        c->batch > 1 ? c->n_rows : 0, c->has_csc ? c->pull_above : 0,
+                                        c->push_lanes);
             if (c->has_csc) {
                 b200::launch_propagate_pull(c->stream, c->device, c->n_local, c->sell_chunks, c->sell_chunk_words,
                                     c->d_sell_off, (const uint2 *)c->d_pre,
