@@ -684,7 +684,19 @@ def run_b200(args):
                "events_per_step": e2e_events / args.steps, "device_events_per_step": events_total / args.steps,
                "window": f"steps {args.warmup}..{args.warmup + args.steps - 1} from the saved state",
                "api": "snn_cuda_inject_current + snn_cuda_step (host buffers, synchronous)"}
+    local_count = ctx.local_count
     ctx.free()
+
+    # The atomic push is bound by L2 reduction requests (one per event), not
+    # by HBM bytes: measure that ceiling on this device (same target count)
+    # and report the push steps against it.
+    if "push" in split and args.propagation in ("auto", "atomic"):
+        try:
+            red = sb.probe_red_rate(local, targets=local_count, events=1 << 28, repeats=5)
+            split["push"]["red_ceiling_per_s"] = red
+            split["push"]["frac_of_red_ceiling"] = split["push"]["events_per_s"] / red
+        except sb.SnnError as exc:  # reported, never required
+            split["push"]["red_ceiling_per_s"] = repr(exc)
 
     parity = None
     if not args.no_parity:
@@ -765,7 +777,7 @@ def raster_check(args, world, rank, local, dist, opts_base, nccl_id_buf):
         handles = [None] * world
         dist.all_gather_object(handles, ctx.ipc_handle())
         ctx.ipc_connect(handles)
-    slot = ctx.local_count if world == 1 else -(-(-(-n // world)) // 32) * 32
+    slot = max(sb.shard_range(n, world, r)[1] for r in range(world))
     sha = hashlib.sha256()
     spikes = 0
     buf = np.zeros(ctx.local_count, np.uint8)

@@ -381,6 +381,13 @@ void snn_b200_network_unwrap(snn_network_t *network);
 snn_status_t snn_b200_network_save(const snn_network_t *network, const char *path);
 snn_status_t snn_b200_network_map(const char *path, snn_network_t **out_network);
 
+/* Diagnostic, no counterpart in the reference: the rate (per second) at which
+ * this device's L2 serves red.global.add.f32 to uniformly random slots of a
+ * `targets`-float array (the push propagation's access pattern), measured
+ * over `repeats` launches of `events` reductions. Allocates its own buffers. */
+snn_status_t snn_b200_probe_red_rate(int device, uint64_t targets, uint64_t events, uint32_t repeats,
+                                     double *out_reds_per_s);
+
 /* Largest network snn_b200_step_noalloc accepts: its scratch is a fixed
  * array of this many spike-list entries (plus bitmap and counters, ~4.2 MB)
  * compiled into the library and resident on every GPU that loads it. */
@@ -396,16 +403,19 @@ snn_status_t snn_b200_network_map(const char *path, snn_network_t **out_network)
  * library array above. Same arithmetic as snn_cuda_step on a FULL push
  * context: `current` (the input this step consumes) is zeroed, `next_current`
  * must be all zero on entry and receives the propagated input; swap the two
- * before the next call. `external` may be NULL; row_ptr holds n+1 edge
- * offsets, col_idx 32-bit target ids. Neuron, external, col_idx and weight
+ * before the next call. `external` may be NULL (every other array is
+ * required; a network without edges still passes aligned col_idx and weights
+ * buffers); row_ptr holds n+1 edge offsets, col_idx 32-bit target ids. Neuron, external, col_idx and weight
  * arrays must be 16-byte aligned, spikes 4-byte aligned.
  *
  * Work is enqueued on `stream` (a cudaStream_t, NULL = legacy default) of
  * `device`; the call does not synchronise. neuron_count of 0 or above
  * SNN_B200_NOALLOC_MAX_NEURONS, NULL or misaligned arrays return
  * SNN_ERR_INVALID_ARGUMENT. The first call on a device looks up the scratch
- * array's device address (make it before any stream capture). All calls on a
- * device share the scratch: calls that overlap on the GPU race. */
+ * array's device address (make it before any stream capture) and keeps it for
+ * the lifetime of the device's primary context: do not call it again on a
+ * device after cudaDeviceReset. All calls on a device share the scratch:
+ * calls that overlap on the GPU race. */
 snn_status_t snn_b200_step_noalloc(int device, void *stream, snn_size_t neuron_count, const snn_lif_params_t *lif,
                                    float decay, float *voltage, float *current, const float *external,
                                    uint32_t *refractory, uint8_t *spikes, const snn_size_t *row_ptr,

@@ -131,6 +131,7 @@ ENTRY_POINTS = [
     ("snn_b200_shard_range", C.c_int, [u64, C.c_uint32, C.c_uint32, P, P]),
     ("snn_b200_last_error", C.c_char_p, []),
     ("snn_b200_step_noalloc", C.c_int, [C.c_int, P, u64, P, f32, P, P, P, P, P, P, P, P, P]),
+    ("snn_b200_probe_red_rate", C.c_int, [C.c_int, u64, u64, C.c_uint32, P]),
     ("snn_b200_reset", C.c_int, [P]),
     ("snn_b200_inject_stream_async", C.c_int, [P, u64, u64, u64, f32]),
     ("snn_b200_run_stream_async", C.c_int, [P, u64, u64, u64, u64, f32]),
@@ -209,6 +210,14 @@ def shard_range(n: int, world: int, rank: int) -> tuple[int, int]:
     b, c = u64(), u64()
     _check(lib().snn_b200_shard_range(n, world, rank, C.byref(b), C.byref(c)), "snn_b200_shard_range")
     return int(b.value), int(c.value)
+
+
+def probe_red_rate(device: int = 0, targets: int = 10_000_000, events: int = 1 << 28, repeats: int = 5) -> float:
+    """Reductions per second the device's L2 serves to random float slots
+    (snn_b200_probe_red_rate): the ceiling of the atomic push."""
+    out = C.c_double()
+    _check(lib().snn_b200_probe_red_rate(device, targets, events, repeats, C.byref(out)), "snn_b200_probe_red_rate")
+    return out.value
 
 
 def nccl_unique_id() -> bytes:

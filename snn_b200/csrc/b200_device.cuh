@@ -89,5 +89,20 @@ __device__ __forceinline__ uint32_t gather_word(const PeerWait &pw, uint32_t *lo
     return v;
 }
 
+// Four words [wi, wi + 4) (wi a multiple of 4, inside one rank's slice),
+// gathered like gather_word with one 16-byte load.
+__device__ __forceinline__ uint4 gather_vec(const PeerWait &pw, uint32_t *local, uint64_t wi) {
+    const uint32_t r = (uint32_t)(wi / pw.slot_words);
+    uint4 *dst = reinterpret_cast<uint4 *>(local + wi);
+    if (r == pw.rank) return __ldcg(dst);
+    uint4 v;
+    asm volatile("ld.volatile.global.v4.u32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(pw.src[r] + wi)
+                 : "memory");
+    *dst = v;
+    return v;
+}
+
 }  // namespace dev
 }  // namespace b200

@@ -265,12 +265,18 @@ __global__ void __launch_bounds__(256) compact_kernel(uint32_t *__restrict__ bit
         __syncthreads();
         if (!s_ok) return;
     }
+    // Four words (16 bytes) per thread: the bitmap (words a multiple of 4)
+    // and every rank's slice (slot_words a multiple of 4) are 16-byte
+    // aligned, so a vector never straddles two owners.
     const uint64_t stride = (uint64_t)blockDim.x * gridDim.x;
+    const uint64_t vecs = words / 4;
     uint32_t own = 0;
-    for (uint64_t base = (uint64_t)blockIdx.x * blockDim.x; base < words; base += stride) {
-        const uint64_t wi = base + threadIdx.x;
-        const uint32_t word = wi >= words ? 0u : pw.nflags ? gather_word(pw, bitmap, wi) : __ldcg(bitmap + wi);
-        const uint32_t cnt = __popc(word);
+    for (uint64_t base = (uint64_t)blockIdx.x * blockDim.x; base < vecs; base += stride) {
+        const uint64_t vi = base + threadIdx.x;
+        const uint64_t wi = vi * 4;
+        uint4 q = make_uint4(0u, 0u, 0u, 0u);
+        if (vi < vecs) q = pw.nflags ? gather_vec(pw, bitmap, wi) : __ldcg(reinterpret_cast<const uint4 *>(bitmap) + vi);
+        const uint32_t cnt = __popc(q.x) + __popc(q.y) + __popc(q.z) + __popc(q.w);
         if (wi >= own_begin && wi < own_end) own += cnt;
         uint32_t incl = cnt;
 #pragma unroll
@@ -283,11 +289,14 @@ __global__ void __launch_bounds__(256) compact_kernel(uint32_t *__restrict__ bit
         if (lane == 31u && total) off = atomicAdd(&ctr->list_count[parity], total);
         off = __shfl_sync(kFull, off, 31);
         uint32_t pos = off + incl - cnt;
-        uint32_t m = word;
-        while (m) {
-            const int b = __ffs(m) - 1;
-            m &= m - 1u;
-            list[pos++] = (TIdx)(wi * 32u + (uint64_t)b);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            uint32_t m = j == 0 ? q.x : j == 1 ? q.y : j == 2 ? q.z : q.w;
+            while (m) {
+                const int b = __ffs(m) - 1;
+                m &= m - 1u;
+                list[pos++] = (TIdx)((wi + j) * 32u + (uint64_t)b);
+            }
         }
     }
 #pragma unroll
@@ -1085,7 +1094,7 @@ void launch_compact(cudaStream_t s, int device, uint32_t *bitmap, uint64_t words
                     DevCounters *ctr, int parity, uint64_t own_begin, uint64_t own_end, const PeerWait *wait) {
     PeerWait pw{};
     if (wait) pw = *wait;
-    const int grid = grid_for(device, 8, words, 256);
+    const int grid = grid_for(device, 8, words / 4, 256);
     if (idx_bits == 32)
         compact_kernel<uint32_t><<<grid, 256, 0, s>>>(bitmap, words, (uint32_t *)list, ctr, parity, own_begin, own_end, pw);
     else

@@ -37,7 +37,8 @@ static __device__ __align__(256) unsigned char g_noalloc_scratch[kScratchBytes];
 
 // In host code g_noalloc_scratch names a host-side stand-in, not device
 // memory: its device address is looked up once per device (with that device
-// current) and cached here.
+// current) and cached here, for the lifetime of the device's primary context
+// (a caller that resets the device must not call this entry point again).
 constexpr int kMaxDevices = 64;
 std::mutex g_mu;
 void *g_scratch_addr[kMaxDevices] = {};
@@ -52,14 +53,15 @@ extern "C" snn_status_t snn_b200_step_noalloc(int device, void *stream, snn_size
                                               uint8_t *spikes, const snn_size_t *row_ptr, const uint32_t *col_idx,
                                               const float *weights, float *next_current) {
     if (lif == nullptr || voltage == nullptr || current == nullptr || refractory == nullptr ||
-        spikes == nullptr || row_ptr == nullptr || next_current == nullptr || device < 0 || device >= kMaxDevices)
+        spikes == nullptr || row_ptr == nullptr || col_idx == nullptr || weights == nullptr ||
+        next_current == nullptr || device < 0 || device >= kMaxDevices)
         return SNN_ERR_INVALID_ARGUMENT;
     if (neuron_count == 0 || neuron_count > kMaxNeurons)
         return SNN_ERR_INVALID_ARGUMENT;  // beyond the fixed scratch: use a context instead
     // 16-byte vector loads/stores on the neuron arrays and the edge arrays.
     if (!aligned(voltage, 16) || !aligned(current, 16) || !aligned(refractory, 16) || !aligned(spikes, 4) ||
-        (external && !aligned(external, 16)) || (col_idx && !aligned(col_idx, 16)) ||
-        (weights && !aligned(weights, 16)) || !aligned(row_ptr, 8))
+        (external && !aligned(external, 16)) || !aligned(col_idx, 16) || !aligned(weights, 16) ||
+        !aligned(row_ptr, 8))
         return SNN_ERR_INVALID_ARGUMENT;
 
     int prev = -1;

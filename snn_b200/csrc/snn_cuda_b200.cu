@@ -289,11 +289,12 @@ void free_context(snn_cuda_context_t *c) {
     cudaGetLastError();  // leave no non-sticky error behind for the next launch check
 }
 
-// Rank r owns [r*S, min((r+1)*S, n)) with S = ceil(n / world / 32) * 32: equal
-// 32-aligned slots keep every rank's bitmap slice whole words of equal size
-// (the in-place all-gather needs equal counts).
+// Rank r owns [r*S, min((r+1)*S, n)) with S = ceil(n / world / 128) * 128:
+// equal 128-aligned slots keep every rank's bitmap slice whole 16-byte
+// vectors of words, all of equal size (the in-place all-gather needs equal
+// counts; the compaction reads the bitmap 4 words at a time).
 void shard_geometry(uint64_t n, uint32_t world, uint32_t rank, uint64_t *slot, uint64_t *lo, uint64_t *hi) {
-    *slot = ceil_div(ceil_div(n, world), 32) * 32;
+    *slot = ceil_div(ceil_div(n, world), 128) * 128;
     *lo = std::min<uint64_t>(n, (uint64_t)rank * *slot);
     *hi = std::min<uint64_t>(n, *lo + *slot);
 }

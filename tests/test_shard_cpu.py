@@ -43,7 +43,7 @@ def _worker(rank, world, port, n, steps, count, out):
     lif = baseline_lif()
     net = orc.random_pool(n, 60, -0.2, 0.5, 3, lif=lif)
     lo, cnt = sb.shard_range(n, world, rank)
-    slot_words = -(-(-(-n // world)) // 32)  # ceil(ceil(n/world)/32)
+    slot_words = -(-(-(-n // world)) // 128) * 4  # ceil(ceil(n/world)/128) * 4 words
     rp, ci, w = net.row_ptr(), net.col_idx(), net.weights()
     rows = np.repeat(np.arange(n, dtype=np.int64), np.diff(rp).astype(np.int64))
     keep = (ci >= lo) & (ci < lo + cnt)
@@ -112,7 +112,7 @@ def test_shard_geometry_tiles_the_network():
             for b, c in ranges:
                 assert b == pos or c == 0
                 pos = max(pos, b + c)
-                assert b % 32 == 0 or c == 0
+                assert b % 128 == 0 or c == 0
             assert pos == n
             assert sum(c for _, c in ranges) == n
     with pytest.raises(sb.SnnError):

@@ -80,7 +80,29 @@ def test_noalloc_step_matches_context_step(weights):
         np.testing.assert_allclose(gv, ref_v, rtol=1e-5, atol=0)
         np.testing.assert_allclose(gc, ref_c, rtol=1e-5, atol=1e-5)
 
-    # Limits: beyond the fixed scratch, or misaligned, is rejected up front.
+    # The entry point allocates nothing: after the first call (which looks up
+    # the scratch address), further calls leave the device's free memory and
+    # torch's allocator exactly where they were.
+    torch.cuda.synchronize(dev)
+    free0, _ = torch.cuda.mem_get_info(dev)
+    alloc0 = torch.cuda.memory_stats(dev).get("allocation.all.allocated", 0)
+    for _ in range(3):
+        assert L.snn_b200_step_noalloc(0, stream, n, C.byref(lp), net.decay, _ptr(v), _ptr(cur), None, _ptr(refr),
+                                       _ptr(spikes), _ptr(row_ptr), _ptr(col), _ptr(w), _ptr(nxt)) == sb.SNN_OK
+        cur, nxt = nxt, cur
+    torch.cuda.synchronize(dev)
+    free1, _ = torch.cuda.mem_get_info(dev)
+    assert free1 == free0
+    assert torch.cuda.memory_stats(dev).get("allocation.all.allocated", 0) == alloc0
+
+    # Limits: beyond the fixed scratch, misaligned or missing arrays are
+    # rejected up front.
+    assert L.snn_b200_step_noalloc(0, stream, n, C.byref(lp), net.decay, _ptr(v), _ptr(cur), None, _ptr(refr),
+                                   _ptr(spikes), _ptr(row_ptr), None, _ptr(w),
+                                   _ptr(nxt)) == sb.SNN_ERR_INVALID_ARGUMENT
+    assert L.snn_b200_step_noalloc(0, stream, n, C.byref(lp), net.decay, _ptr(v), _ptr(cur), None, _ptr(refr),
+                                   _ptr(spikes), _ptr(row_ptr), _ptr(col), None,
+                                   _ptr(nxt)) == sb.SNN_ERR_INVALID_ARGUMENT
     too_big = sb.NOALLOC_MAX_NEURONS + 1
     assert L.snn_b200_step_noalloc(0, stream, too_big, C.byref(lp), net.decay, _ptr(v), _ptr(cur), None,
                                    _ptr(refr), _ptr(spikes), _ptr(row_ptr), _ptr(col), _ptr(w),
