@@ -59,6 +59,8 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-parity", action="store_true", help="skip the ORDERED raster-hash check")
+    ap.add_argument("--no-secondary", action="store_true",
+                    help="N=1: skip the other workloads (config 0, ORDERED config 2, config 4, STREAMING)")
     ap.add_argument("--parity-neurons", type=int, default=200_000)
     ap.add_argument("--parity-steps", type=int, default=40)
     ap.add_argument("--exchange", choices=["nccl", "peer"], default="peer",
@@ -710,6 +712,10 @@ def run_b200(args):
             device=local, world_size=world, rank=rank,
             exchange=sb.EXCHANGE_PEER if args.exchange == "peer" else sb.EXCHANGE_NCCL), nccl_id_buf=pid_buf)
 
+    secondary = None
+    if world == 1 and not args.no_secondary and args.workload == "config2":
+        secondary = secondary_workloads(args, local)
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline and args.workload == "config4":
         cpu = {"value": None, "unavailable": "no CPU sample for config 4 (the CPU baseline is measured on config 2)"}
@@ -743,11 +749,155 @@ def run_b200(args):
                           "propagate": s["propagate_ms"] / args.steps},
             "pull_steps": pull_steps, "exchange": exchange,
             "gpu_launches": launches, "generate_s": gen_s, "clocks": clk.summary(), "e2e": e2e,
-            "cpu_baseline": cpu, "parity": parity,
+            "cpu_baseline": cpu, "parity": parity, "secondary": secondary,
         }
         print(json.dumps(line), flush=True)
     if dist is not None:
         dist.destroy_process_group()
+
+
+def timed_run(ctx, seed, first, steps, count, value, device=0):
+    """Device time (CUDA events on the library's stream) of `steps` steps of
+    the seeded injection stream through snn_b200_run_stream_async, with the
+    SM clocks sampled meanwhile; stats cover exactly those steps."""
+    import torch
+    ctx.synchronize()
+    ctx.reset_stats()
+    stream = torch.cuda.ExternalStream(ctx.stream())
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    with ClockSampler(device) as clk:
+        e0.record(stream)
+        ctx.run_stream_async(seed, first, steps, count, value)
+        e1.record(stream)
+        ctx.synchronize()
+    return e0.elapsed_time(e1), ctx.stats(), clk.summary()
+
+
+def secondary_workloads(args, local):
+    """The other workloads, measured in the same N=1 run (each bounded to a
+    few seconds of device time): config 0 through graph replay, ORDERED
+    config 2, config 4, and the STREAMING policy (chunked and sparse) on a
+    host-resident pool, each with its own roofline and clock record."""
+    import numpy as np
+    import torch
+
+    import snn_b200 as sb
+
+    peak, peak_kind = measured_peak_gbs()
+    lif = sb.LifParams(1.0, 20.0, -65.0, -65.0, -50.0, 1.0, 2)
+    out = {}
+
+    def roof(bytes_, ms):
+        a = bytes_ / (ms / 1e3) / 1e9
+        return {"bound": "hbm", "achieved": a, "peak": peak, "unit": "GB/s", "frac": a / peak,
+                "peak_kind": peak_kind, "algorithmic_bytes_per_step": bytes_}
+
+    def record(name, fn):
+        t0 = time.time()
+        try:
+            out[name] = fn()
+        except Exception as exc:  # a secondary workload never fails the bench
+            out[name] = {"unavailable": repr(exc)}
+        out[name]["wall_s"] = round(time.time() - t0, 1)
+
+    # Config 0: 100k x fanout 100, w ~ U[0, 0.6], 1% injection of 20.0 per
+    # step, 1,000 steps; launch-bound, so timed through the graph-replayed
+    # multi-step run (device timing off). PUSH, and the bit-exact bin-fold.
+    def config0(prop):
+        n, f, steps, count = 100_000, 100, 1000, 1000
+        ctx = sb.CudaContext.random_pool(n, f, 0.0, 0.6, 0, lif=lif,
+                                         options=sb.default_options(device=local, propagation=prop))
+        ctx.run_stream_async(0, 0, 20, count, 20.0)
+        ms, s, clk = timed_run(ctx, 0, 20, steps, count, 20.0, local)
+        ctx.free()
+        b = 12.0 * s["events"] + 16.0 * s["spikes"] + (25.0 * n + 12.0 * count) * steps
+        return {"workload": "config0: 100k x 100, 1% x 20.0 per step, graph replay", "value": s["events"] / (ms / 1e3),
+                "unit": "events/s", "us_per_step": 1e3 * ms / steps, "steps": steps,
+                "gpu_launches": int(s["kernel_launches"]), "spike_rate": s["spikes"] / (steps * n),
+                "roofline": roof(b / steps, ms / steps), "clocks": clk}
+    record("config0_push_graph", lambda: config0(sb.PROPAGATE_PUSH))
+    record("config0_ordered_binfold_graph", lambda: config0(sb.PROPAGATE_PUSH_BINNED))
+
+    # ORDERED (bit-exact) on the headline workload: the same 10M x 1000 pool
+    # and window as the main line.
+    def config2_ordered():
+        n, f = args.neurons, args.fanout
+        count = max(1, int(round(args.inject_frac * n)))
+        ctx = sb.CudaContext.random_pool(n, f, -0.2, 0.5, args.seed, lif=lif, options=sb.default_options(
+            device=local, timing=1, propagation=sb.PROPAGATE_ORDERED))
+        ctx.run_stream_async(args.seed, 0, args.warmup, count, args.inject_value)
+        ms, s, clk = timed_run(ctx, args.seed, args.warmup, args.steps, count, args.inject_value, local)
+        ctx.free()
+        b = 12.0 * s["events"] + 16.0 * s["spikes"]
+        return {"workload": "config2 ORDERED (event sort + in-order fold; pull on dense steps), same window",
+                "value": s["events"] / (ms / 1e3), "unit": "events/s", "ms_per_step": ms / args.steps,
+                "steps": args.steps, "pull_steps": int(s["pull_steps"]), "gpu_launches": int(s["kernel_launches"]),
+                "roofline": roof(b / args.steps, s["propagate_ms"] / args.steps), "clocks": clk}
+    record("config2_ordered", config2_ordered)
+
+    # Config 4: 8 layers x 1M, fanout 500 to the next layer, w ~ U[0, 1], 5%
+    # of layer 0 injected with 30.0 per step.
+    def config4():
+        ls, f = args.layer_size, 500
+        layers = [ls] * 8
+        count = max(1, int(round(0.05 * ls)))
+        ctx = sb.CudaContext.layered_random(layers, f, 0.0, 1.0, args.seed, lif=lif,
+                                            options=sb.default_options(device=local, timing=1))
+        ctx.set_stream_range(ls)
+        ctx.run_stream_async(args.seed, 0, args.warmup, count, 30.0)
+        ms, s, clk = timed_run(ctx, args.seed, args.warmup, args.steps, count, 30.0, local)
+        ctx.free()
+        b = 12.0 * s["events"] + 16.0 * s["spikes"]
+        return {"workload": "config4: 8 x 1M layers, fanout 500, 5% of layer 0 x 30.0", "value": s["events"] / (ms / 1e3),
+                "unit": "events/s", "ms_per_step": ms / args.steps, "steps": args.steps,
+                "spike_rate": s["spikes"] / (args.steps * 8 * ls), "pull_steps": int(s["pull_steps"]),
+                "gpu_launches": int(s["kernel_launches"]),
+                "roofline": roof(b / args.steps, s["propagate_ms"] / args.steps), "clocks": clk}
+    record("config4", config4)
+
+    # STREAMING (config 3's policy, scaled to a host pool of 1M x 1000, 12 GB
+    # of CSR in host memory, VRAM budget a quarter of it): chunked streams
+    # the whole CSR every step, sparse reads only the spiking rows.
+    n, f = args.stream_neurons, args.fanout
+    e = n * f
+    rng = np.random.default_rng(args.seed)
+    row_ptr = np.arange(0, e + 1, f, dtype=np.uint64)
+    col = rng.integers(0, n, size=e, dtype=np.uint64)
+    w = (rng.random(e, dtype=np.float32) * np.float32(0.7) - np.float32(0.2)).astype(np.float32)
+    net = sb.Network.from_csr(row_ptr, col, w, lif)
+    csr_bytes = 12 * e + 8 * (n + 1)
+    h = torch.empty(1 << 30, dtype=torch.uint8).pin_memory()
+    d = torch.empty(1 << 30, dtype=torch.uint8, device="cuda")
+    h2d = 0.0
+    for _ in range(5):
+        a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a0.record()
+        d.copy_(h, non_blocking=True)
+        a1.record()
+        torch.cuda.synchronize()
+        h2d = max(h2d, (1 << 30) / (a0.elapsed_time(a1) / 1e3) / 1e9)
+    del h, d
+
+    def streaming(mode, steps):
+        count = max(1, int(round(args.inject_frac * n)))
+        cfg = sb.default_config(prefer_streaming=1, max_vram_bytes=int(0.25 * csr_bytes))
+        ctx = sb.CudaContext.create(net, cfg, sb.default_options(
+            device=local, timing=1, streaming=sb.STREAMING_SPARSE if mode == "sparse" else sb.STREAMING_CHUNKED))
+        ctx.run_stream_async(args.seed, 0, 3, count, args.inject_value)
+        ms, s, clk = timed_run(ctx, args.seed, 3, steps, count, args.inject_value, local)
+        ctx.free()
+        streamed = csr_bytes * steps if mode == "chunked" else 12 * s["events"] + 16 * s["spikes"]
+        gbs = streamed / (ms / 1e3) / 1e9
+        return {"workload": f"STREAMING {mode}: host pool {n} x {f} ({csr_bytes / 1e9:.1f} GB CSR), VRAM budget 25%",
+                "value": s["events"] / (ms / 1e3), "unit": "events/s", "ms_per_step": ms / steps, "steps": steps,
+                "roofline": {"bound": "host_link", "achieved": gbs, "peak": h2d, "unit": "GB/s", "frac": gbs / h2d,
+                             "peak_kind": "measured pinned H2D (1 GiB, best of 5)"},
+                "clocks": clk}
+    record("streaming_chunked", lambda: streaming("chunked", 4))
+    record("streaming_sparse", lambda: streaming("sparse", 20))
+    net.free()
+    return out
 
 
 def raster_check(args, world, rank, local, dist, opts_base, nccl_id_buf):
