@@ -238,9 +238,31 @@ snn_b200_options_t snn_b200_default_options(void);
 /* snn_cuda_create with options: propagation mode, device, index width and
  * postsynaptic sharding. With world_size > 1 every rank passes the same
  * host network and the same NCCL id; rank r owns neurons
- * [r*S, min((r+1)*S, n)) with S = ceil(n / world_size / 32) * 32. */
+ * [r*S, min((r+1)*S, n)) with S = ceil(n / world_size / 128) * 128. */
 snn_status_t snn_b200_create(const snn_network_t *network, const snn_cuda_config_t *config,
                              const snn_b200_options_t *options, snn_cuda_context_t **out_context);
+
+/* One context driving device_count GPUs of this process (no counterpart in
+ * the reference, whose CUDA backend uses one device): the network is sharded
+ * by postsynaptic neuron, rank r on devices[r] (distinct devices), and the
+ * spike bitmap is exchanged every step over NVLink peer memory when every
+ * pair of devices can reach the other's, else with NCCL (ncclCommInitAll).
+ * The returned context works with the reference's snn_cuda_inject_current,
+ * snn_cuda_step (external current and spikes cover all n neurons),
+ * snn_cuda_download_voltage, snn_cuda_context_mode and snn_cuda_free, and
+ * with snn_b200_reset, _get_stats, _get_layout, _run_stream_async,
+ * _step_async, _inject_stream_async, _set_external, _set_stream_range and
+ * _synchronize; the per-member state calls return SNN_ERR_UNSUPPORTED. With
+ * ORDERED propagation the result is bit-identical to the serial CPU step at
+ * any device count. device_count 1 returns a plain context on devices[0]. */
+snn_status_t snn_cuda_create_sharded(const snn_network_t *network, const snn_cuda_config_t *config,
+                                     int device_count, const int *devices, snn_cuda_context_t **out_context);
+/* The same with options (propagation, index width, streaming mode, timing;
+ * exchange: SNN_B200_EXCHANGE_PEER falls back to NCCL when a pair of devices
+ * has no peer access). rank, world_size, device and nccl_id are ignored. */
+snn_status_t snn_b200_create_sharded(const snn_network_t *network, const snn_cuda_config_t *config,
+                                     const snn_b200_options_t *options, int device_count, const int *devices,
+                                     snn_cuda_context_t **out_context);
 
 /* Generates the network of snn_build_random_pool (src/snn.c:523-574) directly
  * on the device, bit-identical to the host builder, without a host copy:

@@ -132,6 +132,8 @@ ENTRY_POINTS = [
     ("snn_b200_last_error", C.c_char_p, []),
     ("snn_b200_step_noalloc", C.c_int, [C.c_int, P, u64, P, f32, P, P, P, P, P, P, P, P, P]),
     ("snn_b200_probe_red_rate", C.c_int, [C.c_int, u64, u64, C.c_uint32, P]),
+    ("snn_cuda_create_sharded", C.c_int, [P, P, C.c_int, P, P]),
+    ("snn_b200_create_sharded", C.c_int, [P, P, P, C.c_int, P, P]),
     ("snn_b200_reset", C.c_int, [P]),
     ("snn_b200_inject_stream_async", C.c_int, [P, u64, u64, u64, f32]),
     ("snn_b200_run_stream_async", C.c_int, [P, u64, u64, u64, u64, f32]),
@@ -294,6 +296,21 @@ class CudaContext:
         else:
             st = lib().snn_b200_create(handle, C.byref(config) if config else None, C.byref(options), C.byref(h))
         _check(st, "snn_cuda_create")
+        return cls(h, keep=network)
+
+    @classmethod
+    def create_sharded(cls, network, devices, config: CudaConfig | None = None, options: Options | None = None):
+        """One context over several GPUs of this process (snn_cuda_create_sharded)."""
+        h = P()
+        handle = network.handle if hasattr(network, "handle") else network
+        devs = (C.c_int * len(devices))(*devices)
+        if options is None:
+            st = lib().snn_cuda_create_sharded(handle, C.byref(config) if config else None, len(devices), devs,
+                                               C.byref(h))
+        else:
+            st = lib().snn_b200_create_sharded(handle, C.byref(config) if config else None, C.byref(options),
+                                               len(devices), devs, C.byref(h))
+        _check(st, "snn_cuda_create_sharded")
         return cls(h, keep=network)
 
     @classmethod

@@ -53,6 +53,9 @@ int seam_fail() {
 }
 
 thread_local char g_last_error[512] = "";
+// Set while snn_b200_create_sharded creates its member contexts: their NCCL
+// communicator is made afterwards for all of them at once (ncclCommInitAll).
+thread_local bool t_group_member = false;
 
 void set_error(const char *what, const char *detail) {
     std::snprintf(g_last_error, sizeof(g_last_error), "%s: %s", what, detail ? detail : "");
@@ -76,6 +79,18 @@ struct StreamChunk {
 struct TimingGroup {
     cudaEvent_t ev[4];  // start, after LIF, after exchange, after propagation
     uint64_t seq = 0;   // the step's index since create (DevCounters::step_seq)
+};
+
+// What the three phases of one step (LIF, exchange, propagation) share.
+struct StepState {
+    int parity = 0;
+    float *next = nullptr;
+    TimingGroup *tg = nullptr;
+    bool sharded = false, peer = false, ordered_list = false;
+    uint32_t *own_bitmap = nullptr;
+    uint32_t *xbitmap = nullptr;
+    b200::PeerWait pw{};
+    uint64_t brows = 0;
 };
 
 }  // namespace
@@ -212,6 +227,11 @@ struct snn_cuda_context {
     uint8_t *d_kind_log = nullptr;  // inside d_ws: b200::kStepLog bytes
     std::vector<TimingGroup> pending, pool;
     double t_step = 0, t_lif = 0, t_exchange = 0, t_prop = 0, t_prop_pull = 0;
+    StepState ps;  // the step in progress between its phases
+    // A context made by snn_cuda_create_sharded drives one member context per
+    // device (ranks 0..G-1 of the postsynaptic sharding); the public calls on
+    // it act on every member.
+    std::vector<snn_cuda_context *> group;
 };
 
 namespace {
@@ -247,6 +267,11 @@ using b200host::validate_csr;
 
 void free_context(snn_cuda_context_t *c) {
     if (c == nullptr) return;
+    if (!c->group.empty()) {
+        for (snn_cuda_context_t *m : c->group) free_context(m);
+        delete c;
+        return;
+    }
     if (c->device >= 0) cudaSetDevice(c->device);
     if (c->stream) cudaStreamSynchronize(c->stream);
     if (c->copy_stream) cudaStreamSynchronize(c->copy_stream);
@@ -307,7 +332,7 @@ snn_status_t apply_options(snn_cuda_context_t *c, uint64_t n, const snn_b200_opt
         return SNN_ERR_INVALID_ARGUMENT;
     if (o.index_width != 0 && o.index_width != 32 && o.index_width != 64) return SNN_ERR_INVALID_ARGUMENT;
     if (o.exchange != SNN_B200_EXCHANGE_NCCL && o.exchange != SNN_B200_EXCHANGE_PEER) return SNN_ERR_INVALID_ARGUMENT;
-    if (o.world_size > 1 && o.exchange == SNN_B200_EXCHANGE_NCCL && o.nccl_id == nullptr)
+    if (o.world_size > 1 && o.exchange == SNN_B200_EXCHANGE_NCCL && o.nccl_id == nullptr && !t_group_member)
         return SNN_ERR_INVALID_ARGUMENT;
     if (o.exchange == SNN_B200_EXCHANGE_PEER && o.world_size > b200::kMaxPeers) return SNN_ERR_UNSUPPORTED;
     c->exchange = o.exchange;
@@ -401,7 +426,7 @@ snn_status_t init_peer_exchange(snn_cuda_context_t *c) {
 }
 
 snn_status_t init_nccl(snn_cuda_context_t *c, const void *id) {
-    if (c->world <= 1 || c->exchange != SNN_B200_EXCHANGE_NCCL) return SNN_OK;
+    if (c->world <= 1 || c->exchange != SNN_B200_EXCHANGE_NCCL || t_group_member) return SNN_OK;
     ncclUniqueId uid;
     std::memcpy(&uid, id, sizeof(uid));
     const ncclResult_t r = ncclCommInitRank(&c->comm, (int)c->world, uid, (int)c->rank);
@@ -1091,24 +1116,26 @@ void timing_fold(snn_cuda_context_t *c) {
 }
 
 // --------------------------------------------------------------- step ----
-// The device part of one step: LIF (+ exchange) + propagation, then the
-// current-buffer swap. Seams: #1 integrate launch, #2 propagate launch (or
-// the per-chunk copies and launches in STREAMING). Enqueued on c->stream.
-snn_status_t enqueue_step(snn_cuda_context_t *c, bool has_ext) {
-    const int parity = (int)(c->step & 1u);
+// Phase 1 of a step: LIF (writing this rank's bitmap words; with the peer
+// exchange, followed by the flag publication) and the early spike download.
+snn_status_t step_lif(snn_cuda_context_t *c, bool has_ext) {
+    StepState &ps = c->ps;
+    ps = StepState{};
+    ps.parity = (int)(c->step & 1u);
+    const int parity = ps.parity;
     float *cur = c->d_cur[c->cur];
-    float *next = c->d_cur[c->cur ^ 1];
-    TimingGroup *tg = timing_begin(c);
-    const bool sharded = c->world > 1;
-    uint32_t *own_bitmap = c->d_bitmap + (uint64_t)c->rank * (c->slot / 32);
-    const bool peer = sharded && c->exchange == SNN_B200_EXCHANGE_PEER;
+    ps.next = c->d_cur[c->cur ^ 1];
+    ps.tg = timing_begin(c);
+    TimingGroup *tg = ps.tg;
+    const bool sharded = ps.sharded = c->world > 1;
+    ps.own_bitmap = c->d_bitmap + (uint64_t)c->rank * (c->slot / 32);
+    const bool peer = ps.peer = sharded && c->exchange == SNN_B200_EXCHANGE_PEER;
     if (peer && !c->peers_connected) {
         set_error("snn_b200", "peer exchange used before snn_b200_ipc_connect");
         return SNN_ERR_INVALID_ARGUMENT;
     }
     b200::PeerArgs pa{};
-    b200::PeerWait pw{};
-    uint32_t *xbitmap = nullptr;  // this step's global bitmap in the local exchange buffer (peer exchange)
+    b200::PeerWait &pw = ps.pw;
     if (peer) {
         // Pull exchange: LIF writes this rank's words into its own buffer of
         // this parity and releases its flag at every rank; the compaction
@@ -1121,8 +1148,8 @@ snn_status_t enqueue_step(snn_cuda_context_t *c, bool has_ext) {
         }
         pa.npeers = c->world;
         pa.tag = c->xstep;
-        xbitmap = (uint32_t *)c->d_xbuf + par * c->bitmap_words;
-        own_bitmap = xbitmap + (uint64_t)c->rank * (c->slot / 32);
+        ps.xbitmap = (uint32_t *)c->d_xbuf + par * c->bitmap_words;
+        ps.own_bitmap = ps.xbitmap + (uint64_t)c->rank * (c->slot / 32);
         pw.flags = (const unsigned long long *)((char *)c->d_xbuf + xflags_offset(c));
         pw.tag = c->xstep;
         pw.nflags = c->world;
@@ -1134,9 +1161,9 @@ snn_status_t enqueue_step(snn_cuda_context_t *c, bool has_ext) {
     if (c->dev_stream_step) lif_args.stream_step = &c->d_ctr->stream_step;
     // The bin-fold needs an ascending spike list: the ordered compaction
     // below builds it from the bitmap, so LIF writes no list then.
-    const bool ordered_list = c->binfold && c->mode == SNN_CUDA_MODE_FULL;
+    const bool ordered_list = ps.ordered_list = c->binfold && c->mode == SNN_CUDA_MODE_FULL;
     b200::launch_lif(c->stream, c->device, c->n_local, lif_args, c->d_v, cur, has_ext ? c->d_ext : nullptr, c->d_refr,
-                     c->d_spikes, own_bitmap, (sharded || ordered_list) ? nullptr : c->d_list, c->idx_bits, c->lo,
+                     c->d_spikes, ps.own_bitmap, (sharded || ordered_list) ? nullptr : c->d_list, c->idx_bits, c->lo,
                      c->d_ctr, parity, peer ? &pa : nullptr);
     snn_status_t st = check_launch(c);
     if (st != SNN_OK) return st;
@@ -1153,19 +1180,39 @@ snn_status_t enqueue_step(snn_cuda_context_t *c, bool has_ext) {
             return SNN_ERR_CUDA;
         cudaEventRecord(c->ev_spk, c->spk_stream);
     }
-    const uint64_t brows = c->batch > 1 ? c->n_rows : 0;
+    ps.brows = c->batch > 1 ? c->n_rows : 0;
+    return SNN_OK;
+}
+
+// Phase 2: the NCCL all-gather of the bitmap (NCCL exchange only). Several
+// ranks driven from one thread issue theirs inside one NCCL group.
+snn_status_t step_exchange(snn_cuda_context_t *c) {
+    const StepState &ps = c->ps;
+    if (!ps.sharded || ps.peer) return SNN_OK;
+    const ncclResult_t r = ncclAllGather(ps.own_bitmap, c->d_bitmap, c->slot / 32, ncclUint32, c->comm, c->stream);
+    if (r != ncclSuccess) {
+        set_error("ncclAllGather", ncclGetErrorString(r));
+        return SNN_ERR_CUDA;
+    }
+    return SNN_OK;
+}
+
+// Phase 3: compaction (the global spike list; with the peer exchange after
+// the flag waits and the NVLink gather), propagation, buffer swap.
+snn_status_t step_propagate(snn_cuda_context_t *c) {
+    StepState &ps = c->ps;
+    const int parity = ps.parity;
+    float *next = ps.next;
+    TimingGroup *tg = ps.tg;
+    const bool sharded = ps.sharded, peer = ps.peer, ordered_list = ps.ordered_list;
+    uint32_t *xbitmap = ps.xbitmap;
+    const b200::PeerWait &pw = ps.pw;
+    const uint64_t brows = ps.brows;
+    snn_status_t st = SNN_OK;
     if (ordered_list) {
         // Ascending spike list (and the step's event total) from the bitmap:
         // gathered from the peers (after the flag waits), assembled by the
         // NCCL all-gather, or this rank's own.
-        if (sharded && !peer) {
-            const ncclResult_t r =
-                ncclAllGather(own_bitmap, c->d_bitmap, c->slot / 32, ncclUint32, c->comm, c->stream);
-            if (r != ncclSuccess) {
-                set_error("ncclAllGather", ncclGetErrorString(r));
-                return SNN_ERR_CUDA;
-            }
-        }
         b200::launch_compact_ordered(c->stream, c->device, peer ? xbitmap : c->d_bitmap, c->bitmap_words,
                                      c->bfb.ccnt, c->d_list, c->idx_bits, c->d_ctr, parity, c->lo / 32,
                                      ceil_div(c->hi, 32), c->d_row_ptr, brows, peer ? &pw : nullptr);
@@ -1179,12 +1226,6 @@ snn_status_t enqueue_step(snn_cuda_context_t *c, bool has_ext) {
         c->launches++;
         if ((st = cuda_status(cudaGetLastError())) != SNN_OK) return st;
     } else if (sharded) {
-        const size_t words = c->slot / 32;
-        const ncclResult_t r = ncclAllGather(own_bitmap, c->d_bitmap, words, ncclUint32, c->comm, c->stream);
-        if (r != ncclSuccess) {
-            set_error("ncclAllGather", ncclGetErrorString(r));
-            return SNN_ERR_CUDA;
-        }
         b200::launch_compact(c->stream, c->device, c->d_bitmap, c->bitmap_words, c->d_list, c->idx_bits, c->d_ctr,
                              parity, c->lo / 32, ceil_div(c->hi, 32));
         c->launches++;
@@ -1281,6 +1322,16 @@ snn_status_t enqueue_step(snn_cuda_context_t *c, bool has_ext) {
     c->step++;
     c->seq++;
     return SNN_OK;
+}
+
+// The device part of one step (the three phases in a row), enqueued on
+// c->stream. Seams: #1 integrate launch, #2 propagate launch (or the
+// per-chunk copies and launches in STREAMING).
+snn_status_t enqueue_step(snn_cuda_context_t *c, bool has_ext) {
+    snn_status_t st = step_lif(c, has_ext);
+    if (st == SNN_OK) st = step_exchange(c);
+    if (st == SNN_OK) st = step_propagate(c);
+    return st;
 }
 
 snn_status_t ensure_inject_capacity(snn_cuda_context_t *c, uint64_t count) {
@@ -1699,6 +1750,94 @@ snn_status_t run_stream_graph(snn_cuda_context_t *c, uint64_t seed, uint64_t fir
     return st == SNN_OK ? cuda_status(cudaGetLastError()) : st;
 }
 
+bool is_group(const snn_cuda_context_t *c) { return c != nullptr && !c->group.empty(); }
+
+// The early spike download of snn_cuda_step (FULL contexts): a side stream
+// copies the spikes as soon as the LIF kernel is done.
+snn_status_t prepare_spike_stream(snn_cuda_context_t *c) {
+    if (c->spk_stream != nullptr) return SNN_OK;
+    if (cudaStreamCreateWithFlags(&c->spk_stream, cudaStreamNonBlocking) != cudaSuccess ||
+        cudaEventCreateWithFlags(&c->ev_lif, cudaEventDisableTiming) != cudaSuccess ||
+        cudaEventCreateWithFlags(&c->ev_spk, cudaEventDisableTiming) != cudaSuccess)
+        return SNN_ERR_CUDA;
+    return SNN_OK;
+}
+
+// Runs one phase on every member, each with its device current.
+template <typename F>
+snn_status_t for_members(snn_cuda_context_t *g, F &&f) {
+    snn_status_t st = SNN_OK;
+    for (snn_cuda_context_t *m : g->group) {
+        snn_status_t s2 = set_device(m);
+        if (s2 == SNN_OK) s2 = f(m);
+        if (st == SNN_OK) st = s2;
+    }
+    return st;
+}
+
+// The NCCL all-gathers of all members, issued from this thread as one group.
+snn_status_t group_exchange(snn_cuda_context_t *g) {
+    if (g->group[0]->exchange != SNN_B200_EXCHANGE_NCCL) return SNN_OK;
+    if (ncclGroupStart() != ncclSuccess) return SNN_ERR_CUDA;
+    const snn_status_t st = for_members(g, [](snn_cuda_context_t *m) { return step_exchange(m); });
+    const ncclResult_t r = ncclGroupEnd();
+    if (r != ncclSuccess) {
+        set_error("ncclGroupEnd", ncclGetErrorString(r));
+        return SNN_ERR_CUDA;
+    }
+    return st;
+}
+
+// One step of every member: all LIF phases first (with the peer exchange a
+// member's compaction waits for every member's flag), the all-gathers as
+// one NCCL group, then the propagations.
+snn_status_t group_step_async(snn_cuda_context_t *g, const float *ext, uint8_t *spikes) {
+    snn_status_t st = for_members(g, [&](snn_cuda_context_t *m) {
+        if (ext != nullptr && m->n_local) {
+            if (cudaMemcpyAsync(m->d_ext, ext + m->lo, m->n_local * 4, cudaMemcpyHostToDevice, m->stream) !=
+                cudaSuccess)
+                return SNN_ERR_CUDA;
+            m->ext_held = false;
+        }
+        m->spk_dst = nullptr;
+        if (spikes != nullptr && m->n_local && m->mode == SNN_CUDA_MODE_FULL) {
+            const snn_status_t s2 = prepare_spike_stream(m);
+            if (s2 != SNN_OK) return s2;
+            m->spk_dst = spikes + m->lo;
+        }
+        return step_lif(m, ext != nullptr || m->ext_held);
+    });
+    if (st == SNN_OK) st = group_exchange(g);
+    const snn_status_t s3 = for_members(g, [&](snn_cuda_context_t *m) {
+        const snn_status_t s2 = st == SNN_OK ? step_propagate(m) : SNN_OK;
+        m->spk_dst = nullptr;
+        return s2;
+    });
+    return st == SNN_OK ? s3 : st;
+}
+
+snn_status_t group_synchronize(snn_cuda_context_t *g) {
+    return for_members(g, [](snn_cuda_context_t *m) {
+        if (m->exchange == SNN_B200_EXCHANGE_PEER) queue_error_check(m);
+        return error_after_sync(m, cuda_status(cudaStreamSynchronize(m->stream)));
+    });
+}
+
+snn_status_t group_step(snn_cuda_context_t *g, const float *ext, uint8_t *spikes) {
+    snn_status_t st = group_step_async(g, ext, spikes);
+    // STREAMING members download their spikes after the step.
+    const snn_status_t s2 = for_members(g, [&](snn_cuda_context_t *m) {
+        if (spikes == nullptr || m->n_local == 0 || m->mode == SNN_CUDA_MODE_FULL) return SNN_OK;
+        return cudaMemcpyAsync(spikes + m->lo, m->d_spikes, m->n_local, cudaMemcpyDeviceToHost, m->stream) ==
+                       cudaSuccess
+                   ? SNN_OK
+                   : SNN_ERR_CUDA;
+    });
+    const snn_status_t s3 = group_synchronize(g);
+    if (st == SNN_OK) st = s2;
+    return st == SNN_OK ? s3 : st;
+}
+
 }  // namespace
 
 // ======================================================================
@@ -1789,6 +1928,112 @@ snn_status_t snn_cuda_create(const snn_network_t *network, const snn_cuda_config
     return snn_b200_create(network, config, nullptr, out_context);
 }
 
+snn_status_t snn_b200_create_sharded(const snn_network_t *network, const snn_cuda_config_t *config,
+                                     const snn_b200_options_t *options, int device_count, const int *devices,
+                                     snn_cuda_context_t **out_context) {
+    if (out_context == nullptr) return SNN_ERR_INVALID_ARGUMENT;
+    *out_context = nullptr;
+    if (network == nullptr || devices == nullptr || device_count < 1 || device_count > (int)b200::kMaxPeers)
+        return SNN_ERR_INVALID_ARGUMENT;
+    if (!snn_cuda_available()) return SNN_ERR_CUDA;
+    int have = 0;
+    if (cudaGetDeviceCount(&have) != cudaSuccess) return SNN_ERR_CUDA;
+    for (int r = 0; r < device_count; ++r) {
+        if (devices[r] < 0 || devices[r] >= have) return SNN_ERR_INVALID_ARGUMENT;
+        for (int q = 0; q < r; ++q)
+            if (devices[q] == devices[r]) return SNN_ERR_INVALID_ARGUMENT;  // one rank per device
+    }
+    snn_b200_options_t o = options ? *options : snn_b200_default_options();
+    if (o.batch > 1) return SNN_ERR_UNSUPPORTED;
+    if (device_count == 1) {
+        o.world_size = 1;
+        o.rank = 0;
+        o.device = devices[0];
+        return snn_b200_create(network, config, &o, out_context);
+    }
+    // Peer exchange when every pair of devices can reach the other's memory
+    // (without options: whenever it can), else NCCL.
+    bool peer_ok = true;
+    for (int a = 0; a < device_count && peer_ok; ++a)
+        for (int b = 0; b < device_count && peer_ok; ++b) {
+            int can = 0;
+            if (a != b && (cudaDeviceCanAccessPeer(&can, devices[a], devices[b]) != cudaSuccess || !can))
+                peer_ok = false;
+        }
+    cudaGetLastError();
+    int exchange = options ? o.exchange : SNN_B200_EXCHANGE_PEER;
+    if (exchange == SNN_B200_EXCHANGE_PEER && !peer_ok) exchange = SNN_B200_EXCHANGE_NCCL;
+    if (exchange == SNN_B200_EXCHANGE_PEER) {
+        for (int a = 0; a < device_count; ++a) {
+            if (cudaSetDevice(devices[a]) != cudaSuccess) return SNN_ERR_CUDA;
+            for (int b = 0; b < device_count; ++b) {
+                if (a == b) continue;
+                const cudaError_t e = cudaDeviceEnablePeerAccess(devices[b], 0);
+                if (e != cudaSuccess && e != cudaErrorPeerAccessAlreadyEnabled) return cuda_status(e);
+                cudaGetLastError();
+            }
+        }
+    }
+    snn_cuda_context_t *g = new (std::nothrow) snn_cuda_context();
+    if (g == nullptr) return SNN_ERR_OUT_OF_MEMORY;
+    g->group.assign((size_t)device_count, nullptr);
+    snn_status_t st = SNN_OK;
+    t_group_member = true;
+    for (int r = 0; r < device_count && st == SNN_OK; ++r) {
+        snn_b200_options_t m = o;
+        m.rank = (uint32_t)r;
+        m.world_size = (uint32_t)device_count;
+        m.device = devices[r];
+        m.nccl_id = nullptr;
+        m.exchange = exchange;
+        st = snn_b200_create(network, config, &m, &g->group[r]);
+    }
+    t_group_member = false;
+    if (st == SNN_OK && exchange == SNN_B200_EXCHANGE_NCCL) {
+        std::vector<ncclComm_t> comms((size_t)device_count);
+        const ncclResult_t r = ncclCommInitAll(comms.data(), device_count, devices);
+        if (r != ncclSuccess) {
+            set_error("ncclCommInitAll", ncclGetErrorString(r));
+            st = SNN_ERR_CUDA;
+        } else {
+            for (int q = 0; q < device_count; ++q) g->group[q]->comm = comms[q];
+        }
+    }
+    if (st == SNN_OK && exchange == SNN_B200_EXCHANGE_PEER) {
+        // In-process peer mappings: every member reaches the others'
+        // exchange buffers directly (unified addressing, peer access on).
+        for (snn_cuda_context_t *m : g->group) {
+            for (int q = 0; q < device_count; ++q) m->peer_x[q] = (uint32_t *)g->group[q]->d_xbuf;
+            m->peers_connected = true;
+        }
+    }
+    if (st != SNN_OK) {
+        g->group.erase(std::remove(g->group.begin(), g->group.end(), nullptr), g->group.end());
+        if (g->group.empty())
+            delete g;
+        else
+            free_context(g);
+        return st;
+    }
+    snn_cuda_context_t *m0 = g->group[0];
+    g->network = network;
+    g->mode = m0->mode;
+    g->device = devices[0];
+    g->propagation = m0->propagation;
+    g->exchange = exchange;
+    g->world = (uint32_t)device_count;
+    g->n_global = g->n_rows = g->n_local = g->hi = network->neuron_count;
+    g->col_bits = m0->col_bits;
+    for (snn_cuda_context_t *m : g->group) g->e_local += m->e_local;
+    *out_context = g;
+    return SNN_OK;
+}
+
+snn_status_t snn_cuda_create_sharded(const snn_network_t *network, const snn_cuda_config_t *config,
+                                     int device_count, const int *devices, snn_cuda_context_t **out_context) {
+    return snn_b200_create_sharded(network, config, nullptr, device_count, devices, out_context);
+}
+
 void snn_cuda_free(snn_cuda_context_t *context) { free_context(context); }
 
 snn_cuda_mode_t snn_cuda_context_mode(const snn_cuda_context_t *context) {
@@ -1800,6 +2045,16 @@ snn_status_t snn_cuda_inject_current(snn_cuda_context_t *c, const snn_size_t *ho
     if (c == nullptr || (count != 0 && (host_indices == nullptr || host_values == nullptr)))
         return SNN_ERR_INVALID_ARGUMENT;
     if (count == 0) return SNN_OK;
+    if (is_group(c)) {
+        // All-or-nothing validation first, then every member takes the
+        // indices of its own range.
+        for (uint64_t k = 0; k < count; ++k)
+            if (host_indices[k] >= c->n_global) return SNN_ERR_INVALID_ARGUMENT;
+        snn_status_t st = SNN_OK;
+        for (snn_cuda_context_t *m : c->group)
+            if (st == SNN_OK) st = snn_cuda_inject_current(m, host_indices, host_values, count);
+        return st;
+    }
     if (count > UINT64_MAX / sizeof(snn_size_t)) return SNN_ERR_INVALID_ARGUMENT;
     for (uint64_t k = 0; k < count; ++k)
         if (host_indices[k] >= c->n_global) return SNN_ERR_INVALID_ARGUMENT;
@@ -1848,6 +2103,7 @@ snn_status_t snn_cuda_inject_current(snn_cuda_context_t *c, const snn_size_t *ho
 
 snn_status_t snn_cuda_step(snn_cuda_context_t *c, const float *host_external_current, uint8_t *host_out_spikes) {
     if (c == nullptr) return SNN_ERR_INVALID_ARGUMENT;
+    if (is_group(c)) return group_step(c, host_external_current, host_out_spikes);
     snn_status_t st = set_device(c);
     if (st != SNN_OK) return st;
     if (host_external_current != nullptr) {
@@ -1888,6 +2144,12 @@ snn_status_t snn_cuda_step(snn_cuda_context_t *c, const float *host_external_cur
 
 snn_status_t snn_cuda_download_voltage(const snn_cuda_context_t *c, float *host_voltage, snn_size_t count) {
     if (c == nullptr || host_voltage == nullptr || count < c->n_local) return SNN_ERR_INVALID_ARGUMENT;
+    if (is_group(c)) {
+        snn_status_t st = SNN_OK;
+        for (const snn_cuda_context_t *m : c->group)
+            if (st == SNN_OK) st = snn_cuda_download_voltage(m, host_voltage + m->lo, m->n_local);
+        return st;
+    }
     if (c->n_local == 0) return SNN_OK;
     if (set_device(c) != SNN_OK) return SNN_ERR_CUDA;
     if (seam_fail()) return SNN_ERR_CUDA;
@@ -2033,7 +2295,7 @@ snn_status_t snn_test_b200_peer_loopback(snn_cuda_context_t *c, uint32_t spin_li
 }
 
 snn_status_t snn_b200_ipc_handle(const snn_cuda_context_t *c, void *out_handle64) {
-    if (c == nullptr || out_handle64 == nullptr || c->d_xbuf == nullptr) return SNN_ERR_INVALID_ARGUMENT;
+    if (c == nullptr || out_handle64 == nullptr || c->d_xbuf == nullptr || is_group(c)) return SNN_ERR_INVALID_ARGUMENT;
     if (set_device(c) != SNN_OK) return SNN_ERR_CUDA;
     cudaIpcMemHandle_t h;
     const snn_status_t st = cuda_status(cudaIpcGetMemHandle(&h, c->d_xbuf));
@@ -2083,6 +2345,12 @@ snn_status_t snn_b200_nccl_unique_id(void *out_id128) {
 
 snn_status_t snn_b200_reset(snn_cuda_context_t *c) {
     if (c == nullptr) return SNN_ERR_INVALID_ARGUMENT;
+    if (is_group(c)) {
+        snn_status_t st = SNN_OK;
+        for (snn_cuda_context_t *m : c->group)
+            if (st == SNN_OK) st = snn_b200_reset(m);
+        return st;
+    }
     snn_status_t st = set_device(c);
     if (st != SNN_OK) return st;
     cudaStreamSynchronize(c->stream);
@@ -2106,6 +2374,12 @@ snn_status_t snn_b200_reset(snn_cuda_context_t *c) {
 snn_status_t snn_b200_inject_stream_async(snn_cuda_context_t *c, uint64_t seed, uint64_t step, snn_size_t count,
                                           float value) {
     if (c == nullptr) return SNN_ERR_INVALID_ARGUMENT;
+    if (is_group(c)) {
+        snn_status_t st = SNN_OK;
+        for (snn_cuda_context_t *m : c->group)
+            if (st == SNN_OK) st = snn_b200_inject_stream_async(m, seed, step, count, value);
+        return st;
+    }
     if (count == 0) return SNN_OK;
     snn_status_t st = set_device(c);
     if (st != SNN_OK) return st;
@@ -2118,6 +2392,7 @@ snn_status_t snn_b200_inject_stream_async(snn_cuda_context_t *c, uint64_t seed, 
 
 snn_status_t snn_b200_step_async(snn_cuda_context_t *c) {
     if (c == nullptr) return SNN_ERR_INVALID_ARGUMENT;
+    if (is_group(c)) return group_step_async(c, nullptr, nullptr);
     snn_status_t st = set_device(c);
     if (st != SNN_OK) return st;
     return enqueue_step(c, c->ext_held);
@@ -2125,12 +2400,19 @@ snn_status_t snn_b200_step_async(snn_cuda_context_t *c) {
 
 snn_status_t snn_b200_set_stream_range(snn_cuda_context_t *c, snn_size_t range) {
     if (c == nullptr || range > c->n_global) return SNN_ERR_INVALID_ARGUMENT;
+    for (snn_cuda_context_t *m : c->group) m->inject_range = range;
     c->inject_range = range;
     return SNN_OK;
 }
 
 snn_status_t snn_b200_set_external(snn_cuda_context_t *c, const float *host_external_current) {
     if (c == nullptr) return SNN_ERR_INVALID_ARGUMENT;
+    if (is_group(c)) {
+        snn_status_t st = SNN_OK;
+        for (snn_cuda_context_t *m : c->group)
+            if (st == SNN_OK) st = snn_b200_set_external(m, host_external_current ? host_external_current + m->lo : nullptr);
+        return st;
+    }
     snn_status_t st = set_device(c);
     if (st != SNN_OK) return st;
     if (host_external_current == nullptr) {
@@ -2149,6 +2431,14 @@ snn_status_t snn_b200_set_external(snn_cuda_context_t *c, const float *host_exte
 snn_status_t snn_b200_run_stream_async(snn_cuda_context_t *c, uint64_t seed, uint64_t first_step, uint64_t steps,
                                        snn_size_t count, float value) {
     if (c == nullptr) return SNN_ERR_INVALID_ARGUMENT;
+    if (is_group(c)) {
+        snn_status_t st = SNN_OK;
+        for (uint64_t t = 0; t < steps && st == SNN_OK; ++t) {
+            st = snn_b200_inject_stream_async(c, seed, first_step + t, count, value);
+            if (st == SNN_OK) st = group_step_async(c, nullptr, nullptr);
+        }
+        return st;
+    }
     snn_status_t st = set_device(c);
     if (st != SNN_OK) return st;
     if (graph_eligible(c) && steps >= 8) return run_stream_graph(c, seed, first_step, steps, count, value);
@@ -2165,6 +2455,11 @@ snn_status_t snn_b200_run_stream_async(snn_cuda_context_t *c, uint64_t seed, uin
 
 snn_status_t snn_b200_synchronize(snn_cuda_context_t *c) {
     if (c == nullptr) return SNN_ERR_INVALID_ARGUMENT;
+    if (is_group(c)) {
+        const snn_status_t st = group_synchronize(c);
+        for (snn_cuda_context_t *m : c->group) timing_fold(m);
+        return st;
+    }
     snn_status_t st = set_device(c);
     if (st != SNN_OK) return st;
     queue_error_check(c);
@@ -2175,6 +2470,32 @@ snn_status_t snn_b200_synchronize(snn_cuda_context_t *c) {
 
 snn_status_t snn_b200_get_stats(snn_cuda_context_t *c, snn_b200_stats_t *out) {
     if (c == nullptr || out == nullptr) return SNN_ERR_INVALID_ARGUMENT;
+    if (is_group(c)) {
+        // Counts summed over the members (events are per target, spikes per
+        // own neuron), device times the slowest member's.
+        snn_b200_stats_t acc{};
+        for (snn_cuda_context_t *m : c->group) {
+            snn_b200_stats_t s1{};
+            const snn_status_t st = snn_b200_get_stats(m, &s1);
+            if (st != SNN_OK) return st;
+            acc.steps = s1.steps;
+            acc.spikes += s1.spikes;
+            acc.events += s1.events;
+            acc.kernel_launches += s1.kernel_launches;
+            acc.step_ms = std::max(acc.step_ms, s1.step_ms);
+            acc.propagate_ms = std::max(acc.propagate_ms, s1.propagate_ms);
+            acc.lif_ms = std::max(acc.lif_ms, s1.lif_ms);
+            acc.exchange_ms = std::max(acc.exchange_ms, s1.exchange_ms);
+            acc.pull_steps = std::max(acc.pull_steps, s1.pull_steps);
+            acc.pull_events += s1.pull_events;
+            acc.pull_spikes = std::max(acc.pull_spikes, s1.pull_spikes);
+            acc.propagate_pull_ms = std::max(acc.propagate_pull_ms, s1.propagate_pull_ms);
+            acc.exchange_wait_ms = std::max(acc.exchange_wait_ms, s1.exchange_wait_ms);
+            acc.exchange_wait_max_ms = std::max(acc.exchange_wait_max_ms, s1.exchange_wait_max_ms);
+        }
+        *out = acc;
+        return SNN_OK;
+    }
     snn_status_t st = snn_b200_synchronize(c);
     if (st != SNN_OK) return st;
     b200::DevCounters d{};
@@ -2198,6 +2519,12 @@ snn_status_t snn_b200_get_stats(snn_cuda_context_t *c, snn_b200_stats_t *out) {
 
 snn_status_t snn_b200_reset_stats(snn_cuda_context_t *c) {
     if (c == nullptr) return SNN_ERR_INVALID_ARGUMENT;
+    if (is_group(c)) {
+        snn_status_t st = SNN_OK;
+        for (snn_cuda_context_t *m : c->group)
+            if (st == SNN_OK) st = snn_b200_reset_stats(m);
+        return st;
+    }
     snn_status_t st = snn_b200_synchronize(c);
     if (st != SNN_OK) return st;
     b200::DevCounters d{};
@@ -2217,6 +2544,22 @@ snn_status_t snn_b200_reset_stats(snn_cuda_context_t *c) {
 
 snn_status_t snn_b200_get_layout(const snn_cuda_context_t *c, snn_b200_layout_t *out) {
     if (c == nullptr || out == nullptr) return SNN_ERR_INVALID_ARGUMENT;
+    if (is_group(c)) {
+        // The whole network over all members (device bytes summed).
+        snn_status_t st = snn_b200_get_layout(c->group[0], out);
+        if (st != SNN_OK) return st;
+        out->local_begin = 0;
+        out->local_count = c->n_global;
+        out->local_synapses = c->e_local;
+        for (size_t r = 1; r < c->group.size(); ++r) {
+            snn_b200_layout_t l{};
+            if ((st = snn_b200_get_layout(c->group[r], &l)) != SNN_OK) return st;
+            out->device_state_bytes += l.device_state_bytes;
+            out->device_topology_bytes += l.device_topology_bytes;
+            out->pull_slots += l.pull_slots;
+        }
+        return SNN_OK;
+    }
     out->neuron_count = c->n_global;
     out->local_begin = c->lo;
     out->local_count = c->n_local;
@@ -2243,10 +2586,14 @@ snn_status_t snn_b200_get_layout(const snn_cuda_context_t *c, snn_b200_layout_t 
     return SNN_OK;
 }
 
-void *snn_b200_stream(const snn_cuda_context_t *c) { return c ? (void *)c->stream : nullptr; }
+void *snn_b200_stream(const snn_cuda_context_t *c) {
+    if (is_group(c)) return (void *)c->group[0]->stream;  // the first member's (device devices[0])
+    return c ? (void *)c->stream : nullptr;
+}
 
 snn_status_t snn_b200_download_spikes(const snn_cuda_context_t *c, uint8_t *host, snn_size_t count) {
     if (c == nullptr || host == nullptr || count < c->n_local) return SNN_ERR_INVALID_ARGUMENT;
+    if (is_group(c)) return SNN_ERR_UNSUPPORTED;  // per member state: use one context per device
     if (c->n_local == 0) return SNN_OK;
     if (set_device(c) != SNN_OK) return SNN_ERR_CUDA;
     if (cudaMemcpyAsync(host, c->d_spikes, c->n_local, cudaMemcpyDeviceToHost, c->stream) != cudaSuccess)
@@ -2256,6 +2603,7 @@ snn_status_t snn_b200_download_spikes(const snn_cuda_context_t *c, uint8_t *host
 
 snn_status_t snn_b200_download_current(const snn_cuda_context_t *c, float *host, snn_size_t count) {
     if (c == nullptr || host == nullptr || count < c->n_local) return SNN_ERR_INVALID_ARGUMENT;
+    if (is_group(c)) return SNN_ERR_UNSUPPORTED;  // per member state: use one context per device
     if (c->n_local == 0) return SNN_OK;
     if (set_device(c) != SNN_OK) return SNN_ERR_CUDA;
     if (cudaMemcpyAsync(host, c->d_cur[c->cur], c->n_local * 4, cudaMemcpyDeviceToHost, c->stream) != cudaSuccess)
@@ -2266,6 +2614,7 @@ snn_status_t snn_b200_download_current(const snn_cuda_context_t *c, float *host,
 snn_status_t snn_b200_upload_state(snn_cuda_context_t *c, const float *v, const float *cur, const uint32_t *refr,
                                    snn_size_t count) {
     if (c == nullptr || count < c->n_local) return SNN_ERR_INVALID_ARGUMENT;
+    if (is_group(c)) return SNN_ERR_UNSUPPORTED;  // per member state: use one context per device
     if (c->n_local == 0) return SNN_OK;
     if (set_device(c) != SNN_OK) return SNN_ERR_CUDA;
     const uint64_t n = c->n_local;
@@ -2280,6 +2629,7 @@ snn_status_t snn_b200_upload_state(snn_cuda_context_t *c, const float *v, const 
 snn_status_t snn_b200_download_state(const snn_cuda_context_t *c, float *v, float *cur, uint32_t *refr,
                                      snn_size_t count) {
     if (c == nullptr || count < c->n_local) return SNN_ERR_INVALID_ARGUMENT;
+    if (is_group(c)) return SNN_ERR_UNSUPPORTED;  // per member state: use one context per device
     if (c->n_local == 0) return SNN_OK;
     if (set_device(c) != SNN_OK) return SNN_ERR_CUDA;
     const uint64_t n = c->n_local;
@@ -2293,7 +2643,7 @@ snn_status_t snn_b200_download_state(const snn_cuda_context_t *c, float *v, floa
 
 snn_status_t snn_b200_download_topology(const snn_cuda_context_t *c, snn_size_t *row_ptr, snn_size_t row_capacity,
                                         snn_size_t *col_idx, float *weights, snn_size_t edge_capacity) {
-    if (c == nullptr || c->mode != SNN_CUDA_MODE_FULL || c->propagation == SNN_B200_PROPAGATE_ORDERED)
+    if (c == nullptr || is_group(c) || c->mode != SNN_CUDA_MODE_FULL || c->propagation == SNN_B200_PROPAGATE_ORDERED)
         return SNN_ERR_INVALID_ARGUMENT;
     if ((row_ptr && row_capacity < c->n_rows + 1) || ((col_idx || weights) && edge_capacity < c->e_local))
         return SNN_ERR_INVALID_ARGUMENT;
