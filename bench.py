@@ -70,6 +70,9 @@ def parse():
                          "measured against the host-link roofline")
     ap.add_argument("--stream-neurons", type=int, default=1_000_000)
     ap.add_argument("--stream-mode", choices=["chunked", "sparse"], default="sparse")
+    ap.add_argument("--stream-source", choices=["host", "generated"], default="host",
+                    help="host: a numpy-built pool in host memory (1 GPU); generated: each rank's slice of a "
+                         "seeded pool generated on its device and moved to host memory (any GPU count)")
     ap.add_argument("--stream-budget-frac", type=float, default=0.25,
                     help="VRAM budget as a fraction of the host CSR bytes (config 3 streams ~15x its budget)")
     ap.add_argument("--workload", choices=["config2", "config1", "config4"], default="config2",
@@ -287,6 +290,9 @@ def main():
     if args.impl == "reference":
         reference_arm(args)
         return
+    if args.policy == "streaming" and args.stream_source == "generated":
+        run_streaming_generated(args)
+        return
     if args.policy == "streaming":
         run_streaming(args)
         return
@@ -495,6 +501,115 @@ def run_streaming(args):
         "spike_rate": s["spikes"] / (args.steps * n), "clocks": clk.summary(),
     }), flush=True)
     ctx.free()
+
+
+def run_streaming_generated(args):
+    """STREAMING at N GPUs (config 3's policy at the largest scale the host
+    holds): a seeded pool of --stream-neurons x --fanout, sharded by
+    postsynaptic neuron; every rank generates its own slice on its device,
+    moves it to host memory and streams it every step over its own host link
+    (chunked, or sparse reads of the spiking rows), with a VRAM budget of
+    --stream-budget-frac of its slice. Reported per GPU against the host-link
+    roofline (pinned H2D measured on each rank)."""
+    import torch
+
+    import snn_b200 as sb
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+    n, f = args.stream_neurons, args.fanout
+    lo, cnt = sb.shard_range(n, world, rank)
+    slice_bytes = 12 * n * f // world + 8 * (n + 1)
+    budget = int(args.stream_budget_frac * slice_bytes)
+    sparse = args.stream_mode == "sparse"
+    opts = sb.default_options(device=local, world_size=world, rank=rank, timing=1,
+                              exchange=sb.EXCHANGE_PEER if args.exchange == "peer" else sb.EXCHANGE_NCCL,
+                              streaming=sb.STREAMING_SPARSE if sparse else sb.STREAMING_CHUNKED)
+    id_buf = None
+    if world > 1 and args.exchange == "nccl":
+        import ctypes
+        obj = [sb.nccl_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(obj, src=0)
+        id_buf = ctypes.create_string_buffer(obj[0], 128)
+        opts.nccl_id = ctypes.cast(id_buf, ctypes.c_void_p)
+    lif = sb.LifParams(1.0, 20.0, -65.0, -65.0, -50.0, 1.0, 2)
+    t0 = time.time()
+    ctx = sb.CudaContext.random_pool(n, f, -0.2, 0.5, args.seed, lif=lif,
+                                     config=sb.default_config(prefer_streaming=1, max_vram_bytes=budget),
+                                     options=opts)
+    gen_s = time.time() - t0
+    assert ctx.mode == sb.MODE_STREAMING
+    if world > 1 and args.exchange == "peer":
+        handles = [None] * world
+        dist.all_gather_object(handles, ctx.ipc_handle())
+        ctx.ipc_connect(handles)
+    h = torch.empty(1 << 30, dtype=torch.uint8).pin_memory()
+    d = torch.empty(1 << 30, dtype=torch.uint8, device="cuda")
+    h2d = 0.0
+    for _ in range(3):
+        a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a0.record()
+        d.copy_(h, non_blocking=True)
+        a1.record()
+        torch.cuda.synchronize()
+        h2d = max(h2d, (1 << 30) / (a0.elapsed_time(a1) / 1e3) / 1e9)
+    del h, d
+    count = max(1, int(round(args.inject_frac * n)))
+    ctx.run_stream_async(args.seed, 0, args.warmup, count, args.inject_value)
+    ctx.synchronize()
+    ctx.reset_stats()
+    stream = torch.cuda.ExternalStream(ctx.stream())
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clk:
+        if dist is not None:
+            z = torch.zeros(1, device="cuda")
+            with torch.cuda.stream(stream):
+                dist.all_reduce(z)
+        e0.record(stream)
+        ctx.run_stream_async(args.seed, args.warmup, args.steps, count, args.inject_value)
+        e1.record(stream)
+        ctx.synchronize()
+        torch.cuda.synchronize()
+    ms_local = e0.elapsed_time(e1)
+    s = ctx.stats()
+    lay = ctx.layout
+    streamed = (12 * lay["local_synapses"] + 8 * (n + 1)) * args.steps if not sparse else \
+        12 * s["events"] + 16 * s["spikes"]
+    mine = {"rank": rank, "ms": ms_local, "host_link_gbs": streamed / (ms_local / 1e3) / 1e9, "h2d_peak_gbs": h2d,
+            "events": s["events"], "local_synapses": lay["local_synapses"]}
+    allr = [mine]
+    if dist is not None:
+        allr = [None] * world
+        dist.all_gather_object(allr, mine)
+    ctx.free()
+    if rank == 0:
+        ms = max(r["ms"] for r in allr)
+        events = sum(r["events"] for r in allr)
+        fr = [r["host_link_gbs"] / r["h2d_peak_gbs"] for r in allr]
+        print(json.dumps({
+            "metric": "synaptic_events_per_sec", "value": events / (ms / 1e3), "unit": "events/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic: seeded pool generated on each rank's device (bit-identical to snn_build_random_pool)",
+            "config": {"workload": "config3_streaming_policy_scaled", "neurons": n, "fanout": f,
+                       "synapses": n * f, "host_csr_bytes_total": 12 * n * f + 8 * (n + 1) * world,
+                       "vram_budget_bytes_per_gpu": budget, "policy": f"STREAMING ({args.stream_mode})",
+                       "parallelism": f"postsynaptic shards x{world}, {args.exchange} spike exchange"},
+            "roofline": {"bound": "host_link", "per_gpu_gbs": [r["host_link_gbs"] for r in allr],
+                         "per_gpu_peak_gbs": [r["h2d_peak_gbs"] for r in allr], "frac_min": min(fr),
+                         "frac_mean": sum(fr) / len(fr), "aggregate_gbs": sum(r["host_link_gbs"] for r in allr)},
+            "generate_s": gen_s, "clocks": clk.summary()}), flush=True)
+    if dist is not None:
+        dist.destroy_process_group()
 
 
 def run_b200(args):

@@ -1652,11 +1652,68 @@ snn_status_t add_pull_topology(snn_cuda_context_t *c, const snn_network_t *net, 
     return SNN_OK;
 }
 
+// STREAMING for a device-generated network (config prefer_streaming, or a
+// topology larger than the VRAM budget): the rank's slice (targets relative
+// to its first neuron, 64-bit) is generated on the device in scratch memory,
+// copied into host memory owned by the context, released on the device, and
+// then streamed every step like a host network's slice. Each rank of a
+// sharded run thus holds and streams only its own slice.
+snn_status_t generate_streaming(snn_cuda_context_t *c, const b200::GenParams &g, uint64_t e_total,
+                                const snn_cuda_config_t &cfg, uint64_t budget) {
+    const uint64_t n = g.n;
+    c->col_bits = 64;
+    uint64_t *d_row = nullptr;
+    void *d_col = nullptr;
+    float *d_w = nullptr;
+    uint64_t e = 0;
+    snn_status_t st = generate_range(c, g, e_total, c->lo, std::min(c->hi, c->n_rows), &d_row, &d_col, &d_w, &e);
+    auto alloc = [](uint64_t bytes) { return std::aligned_alloc(64, (bytes + 63) / 64 * 64 + 64); };
+    if (st == SNN_OK) {
+        c->h_slice_rp = (uint64_t *)alloc((n + 1) * 8);
+        c->h_slice_col = (uint64_t *)alloc(e * 8);
+        c->h_slice_w = (float *)alloc(e * 4);
+        if (!c->h_slice_rp || !c->h_slice_col || !c->h_slice_w) st = SNN_ERR_OUT_OF_MEMORY;
+    }
+    if (st == SNN_OK) st = cuda_status(cudaMemcpy(c->h_slice_rp, d_row, (n + 1) * 8, cudaMemcpyDeviceToHost));
+    if (st == SNN_OK && e) st = cuda_status(cudaMemcpy(c->h_slice_col, d_col, e * 8, cudaMemcpyDeviceToHost));
+    if (st == SNN_OK && e) st = cuda_status(cudaMemcpy(c->h_slice_w, d_w, e * 4, cudaMemcpyDeviceToHost));
+    cudaFree(d_row);
+    cudaFree(d_col);
+    cudaFree(d_w);
+    if (st != SNN_OK) return st;
+    snn_network_t &sn = c->slice_net;
+    sn.neuron_count = n;
+    sn.synapse_count = e;
+    sn.architecture = g.recurrent ? SNN_ARCH_RANDOM_POOL : SNN_ARCH_CUSTOM_CSR;
+    sn.lif = c->lif;
+    sn.decay = c->args.decay;
+    sn.row_ptr = c->h_slice_rp;
+    sn.col_idx = c->h_slice_col;
+    sn.weights = c->h_slice_w;
+    c->network = &sn;
+    c->e_local = e;
+    c->mode = SNN_CUDA_MODE_STREAMING;
+    bool fallback = true;
+    if (c->streaming == SNN_B200_STREAMING_SPARSE && (st = allocate_sparse_streaming(c, &fallback)) != SNN_OK)
+        return st;
+    if (fallback) {
+        c->streaming = SNN_B200_STREAMING_CHUNKED;
+        st = allocate_streaming(c, cfg, budget);
+    }
+    return st;
+}
+
 snn_status_t finish_generated(snn_cuda_context_t *c, const b200::GenParams &g, uint64_t e_total,
-                              snn_cuda_context_t **out) {
+                              snn_cuda_context_t **out, const snn_cuda_config_t *config = nullptr,
+                              uint64_t budget = 0) {
     snn_status_t st = SNN_OK;
     c->mode = SNN_CUDA_MODE_FULL;
-    if (c->propagation != SNN_B200_PROPAGATE_ORDERED) {
+    const snn_cuda_config_t cfg = config ? *config : snn_cuda_default_config();
+    const uint64_t e_est = (uint64_t)((double)e_total * ((double)c->n_local / (double)c->n_global));
+    const bool full_only = c->propagation == SNN_B200_PROPAGATE_ORDERED || c->batch > 1;
+    if (!full_only && budget && (cfg.prefer_streaming || full_push_bytes(c, e_est) > budget)) {
+        st = generate_streaming(c, g, e_total, cfg, budget);
+    } else if (c->propagation != SNN_B200_PROPAGATE_ORDERED) {
         if ((st = generate_full(c, g, e_total)) == SNN_OK) st = add_pull_topology(c, nullptr, &g);
     }
     else if (!c->opull) {
@@ -2197,7 +2254,7 @@ snn_status_t snn_b200_create_random_pool(const snn_random_pool_config_t *pool, c
     CreateEnv env;
     snn_status_t st = begin_create(n, p, expf(-p.dt_ms / p.membrane_tau_ms), config, options, &c, &env);
     if (st != SNN_OK) return st;
-    return finish_generated(c, g, n * f, out_context);
+    return finish_generated(c, g, n * f, out_context, config, env.budget);
 }
 
 snn_status_t snn_b200_create_layered_random(const snn_size_t *layer_sizes, size_t layer_count, snn_size_t fanout,

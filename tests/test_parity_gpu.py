@@ -714,3 +714,25 @@ def test_stream_range_drives_input_layer(prop):
     assert ctx.stats()["spikes"] > 0
     with pytest.raises(sb.SnnError):
         ctx.set_stream_range(8001)
+
+
+@pytest.mark.parametrize("mode", [sb.STREAMING_CHUNKED, sb.STREAMING_SPARSE])
+def test_generated_pool_streaming_exact(mode):
+    """A device-generated pool under the STREAMING policy: the topology is
+    generated on the device, moved to host memory and streamed from there
+    every step (chunked, or sparse reads of the spiking rows). One dyadic
+    weight (the atomic scatter is then exact): spikes, events and voltages
+    equal the serial CPU step's on the host-built pool."""
+    lif = baseline_lif()
+    n, f = 20011, 80
+    net = ORC.random_pool(n, f, 0.25, 0.25, 44, lif=lif)
+    st = State(net)
+    sc, ev, _, _ = ORC.run_inject_stream(net, st, 2, 0, 30, 300, 25.0)
+    cfg = sb.default_config(prefer_streaming=1, max_vram_bytes=8 << 20)
+    ctx = sb.CudaContext.random_pool(n, f, 0.25, 0.25, 44, lif=lif_to_sb(lif), config=cfg,
+                                     options=opts(streaming=mode))
+    assert ctx.mode == sb.MODE_STREAMING
+    ctx.run_stream_async(2, 0, 30, 300, 25.0)
+    s = ctx.stats()
+    assert s["spikes"] == int(sc.sum()) and s["events"] == int(ev.sum())
+    np.testing.assert_array_equal(bits(st.voltage()), bits(ctx.download_voltage()))
