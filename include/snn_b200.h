@@ -145,7 +145,8 @@ typedef enum snn_b200_propagation {
     SNN_B200_PROPAGATE_PUSH = 0,
     /* Every target folds its contributions in CSR order (ascending
      * presynaptic row, ascending edge): bit-identical to the reference's
-     * serial CPU step (src/snn.c:898-906) for any weights. FULL mode only.
+     * serial CPU step (src/snn.c:898-906) for any weights. FULL and STREAMING
+     * (STREAMING: each streamed chunk sorts and folds its own events, in row order).
      * Each step either sorts its events by target (a stable radix sort of
      * the spiking rows' CSR slices, then an in-order fold; cost ~ events;
      * one host read of the event count per step), or, on dense steps when a

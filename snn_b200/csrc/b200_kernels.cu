@@ -1207,6 +1207,17 @@ void launch_propagate_pull(cudaStream_t s, int device, uint64_t n_local, uint32_
                                                              count_spikes, pull_above, events_gate, events_above);
 }
 
+__global__ void gather_u64_kernel(const unsigned long long *src, const uint64_t *idx, uint64_t count,
+                                  unsigned long long *dst) {
+    const uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < count) dst[i] = src[idx[i]];
+}
+
+void launch_gather_u64(cudaStream_t s, const unsigned long long *src, const uint64_t *idx, uint64_t count,
+                       unsigned long long *dst) {
+    if (count) gather_u64_kernel<<<(unsigned)((count + 255) / 256), 256, 0, s>>>(src, idx, count, dst);
+}
+
 __global__ void set_u64_kernel(unsigned long long *p, unsigned long long v) { *p = v; }
 
 void launch_set_u64(cudaStream_t s, unsigned long long *p, unsigned long long v) { set_u64_kernel<<<1, 1, 0, s>>>(p, v); }

@@ -159,6 +159,9 @@ void launch_propagate_pull(cudaStream_t s, int device, uint64_t n_local, uint32_
                            int parity, int count_spikes, uint32_t pull_above = 0, int events_gate = 0,
                            unsigned long long events_above = 0);
 void launch_fill_u2(cudaStream_t s, int device, uint2 *p, uint64_t n, uint32_t x, uint32_t y);
+// dst[i] = src[idx[i]] for i < count.
+void launch_gather_u64(cudaStream_t s, const unsigned long long *src, const uint64_t *idx, uint64_t count,
+                       unsigned long long *dst);
 // *p = v, in stream order.
 void launch_set_u64(cudaStream_t s, unsigned long long *p, unsigned long long v);
 

@@ -186,6 +186,10 @@ struct snn_cuda_context {
     float *h_slice_w = nullptr;
     uint64_t slot_rows = 0, slot_edges = 0, slot_stride = 0;
     uint64_t *d_chunk_row = nullptr;
+    // ORDERED over chunked STREAMING: each chunk's first row (device), and
+    // the step's event offsets at the chunk boundaries (pinned host).
+    uint64_t *d_chunk_rb = nullptr;
+    unsigned long long *d_bounds = nullptr, *h_bounds = nullptr;
     uint64_t *d_chunk_col = nullptr;
     float *d_chunk_w = nullptr;
     cudaEvent_t ev_copied[2] = {nullptr, nullptr};
@@ -282,13 +286,14 @@ void free_context(snn_cuda_context_t *c) {
     if (c->d_xbuf) cudaFree(c->d_xbuf);
     void *dev[] = {c->d_v, c->d_cur_pair, c->d_ext, c->d_refr, c->d_spikes, c->d_ws, c->d_row_ptr, c->d_col,
                    c->d_w, c->d_col_ptr, c->d_pre, c->d_cw, c->d_deg, c->d_sell_off, c->d_sdeg, c->d_eoff, c->d_okeys[0], c->d_okeys[1], c->d_ovals[0], c->d_ovals[1], c->d_otemp,
-                   c->d_chunk_row, c->d_chunk_col,
+                   c->d_chunk_row, c->d_chunk_col, c->d_chunk_rb, c->d_bounds,
                    c->d_chunk_w, c->d_inj_idx, c->d_inj_val, c->bfb.hist, c->bfb.offs,
                    c->bfb.bins, c->bfb.ccnt, c->bfb.scan_temp};
     for (void *p : dev)
         if (p) cudaFree(p);
     if (c->h_err) cudaFreeHost(c->h_err);
     if (c->h_ototal) cudaFreeHost(c->h_ototal);
+    if (c->h_bounds) cudaFreeHost(c->h_bounds);
     if (c->h_inj_idx) cudaFreeHost(c->h_inj_idx);
     if (c->h_inj_val) cudaFreeHost(c->h_inj_val);
     for (const void *p : c->registered)
@@ -533,7 +538,7 @@ int target_bits(const snn_cuda_context_t *c) {
 // Ordered push buffers, after the push CSR exists. The event capacity (events
 // per sort) is bounded by half of the free device memory at 16 B per event
 // (keys and weights, double-buffered) and by the local synapse count.
-snn_status_t setup_ordered_push(snn_cuda_context_t *c) {
+snn_status_t setup_ordered_push(snn_cuda_context_t *c, uint64_t cap_limit = UINT64_MAX) {
     const uint64_t n = c->n_global, nl = c->n_local;
     auto fail = [&](const char *what) {
         set_error("ordered push setup", what);
@@ -558,7 +563,7 @@ snn_status_t setup_ordered_push(snn_cuda_context_t *c) {
     for (uint64_t i = 0; i < rows; ++i) max_deg = std::max(max_deg, rp[i + 1] - rp[i]);
     size_t free_b = 0, total_b = 0;
     if (cudaMemGetInfo(&free_b, &total_b) != cudaSuccess) return SNN_ERR_CUDA;
-    uint64_t cap = std::min<uint64_t>(c->e_local * c->batch, (uint64_t)(free_b / 2) / 16);
+    uint64_t cap = std::min<uint64_t>({c->e_local * c->batch, (uint64_t)(free_b / 2) / 16, cap_limit});
     if (const char *env = std::getenv("SNN_B200_ORDERED_CAP")) {  // tests: force the multi-range path
         const uint64_t v = std::strtoull(env, nullptr, 10);
         if (v) cap = std::min(cap, v);
@@ -645,12 +650,15 @@ snn_status_t setup_ordered(snn_cuda_context_t *c) {
 
 // One ordered push propagation (b200_kernels.cu describes the steps); one
 // host round trip reads the step's event count to size the sort.
+// The CSR comes in explicitly: the resident one (FULL) or the mapped host
+// CSR (sparse STREAMING; col is then 64-bit).
 snn_status_t ordered_push_step(snn_cuda_context_t *c, int parity, float *next, bool sharded,
-                               const uint32_t *bitmap) {
+                               const uint32_t *bitmap, const uint64_t *row_ptr, const void *col, int col_bits,
+                               const float *w) {
     const uint64_t n = c->n_global;
     snn_status_t st;
     const uint64_t brows = c->batch > 1 ? c->n_rows : 0;
-    b200::launch_ordered_sdeg(c->stream, c->device, c->d_list, c->idx_bits, c->d_ctr, parity, n, c->d_row_ptr,
+    b200::launch_ordered_sdeg(c->stream, c->device, c->d_list, c->idx_bits, c->d_ctr, parity, n, row_ptr,
                               c->d_sdeg, 0, brows);
     size_t tb = c->otemp_bytes;
     if ((st = cuda_status(b200::scan_degrees_u64(c->stream, c->d_sdeg, c->d_eoff, n + 1, c->d_otemp, &tb))) != SNN_OK)
@@ -663,7 +671,7 @@ snn_status_t ordered_push_step(snn_cuda_context_t *c, int parity, float *next, b
     if (c->has_csc && c->pull_div && total > c->e_local / c->pull_div) {
         // Most rows spike: the pull over the CSC reads every synapse once,
         // cheaper than sorting this many events.
-        b200::launch_ordered_sdeg(c->stream, c->device, c->d_list, c->idx_bits, c->d_ctr, parity, n, c->d_row_ptr,
+        b200::launch_ordered_sdeg(c->stream, c->device, c->d_list, c->idx_bits, c->d_ctr, parity, n, row_ptr,
                                   c->d_sdeg, 1, brows);
         b200::launch_propagate_pull(c->stream, c->device, c->n_local, c->sell_chunks, c->sell_chunk_words,
                                     c->d_sell_off, (const uint2 *)c->d_pre, 
@@ -691,8 +699,8 @@ snn_status_t ordered_push_step(snn_cuda_context_t *c, int parity, float *next, b
     for (size_t i = 0; i < ranges.size(); ++i) {
         const uint64_t r0 = ranges[i][0], r1 = ranges[i][1], base = ranges[i][2];
         const uint64_t events = (i + 1 < ranges.size() ? ranges[i + 1][2] : total) - base;
-        b200::launch_ordered_gen(c->stream, c->device, c->d_list, c->idx_bits, c->d_ctr, parity, r0, r1, c->d_row_ptr,
-                                 c->d_col, c->col_bits, c->d_w, c->d_eoff, n, base, c->d_sdeg, c->d_okeys[0],
+        b200::launch_ordered_gen(c->stream, c->device, c->d_list, c->idx_bits, c->d_ctr, parity, r0, r1, row_ptr,
+                                 col, col_bits, w, c->d_eoff, n, base, c->d_sdeg, c->d_okeys[0],
                                  c->d_ovals[0], i + 1 == ranges.size(), !sharded, brows);
         c->launches++;
         if (!events) continue;
@@ -705,6 +713,103 @@ snn_status_t ordered_push_step(snn_cuda_context_t *c, int parity, float *next, b
         b200::launch_ordered_fold(c->stream, c->device, events, c->d_okeys[alt ? 1 : 0], c->d_ovals[alt ? 1 : 0],
                                   next);
         c->launches++;
+    }
+    return SNN_OK;
+}
+
+// ORDERED over chunked STREAMING. The step's events are numbered in CSR
+// order once (spiking degrees over the resident row_ptr, scanned); one host
+// read fetches the event offsets at the chunk boundaries. Then each chunk, as
+// its copy lands, copies its spiking rows' events, sorts them stably by
+// target and folds them onto the currents the earlier chunks left. Chunks are
+// in ascending row order, so every target's fold is the serial CPU order
+// (src/snn.c:898-906): bit-identical for any weights.
+snn_status_t ordered_stream_chunked(snn_cuda_context_t *c, int parity, float *next, bool sharded) {
+    const uint64_t n = c->n_global;
+    const snn_network_t *net = c->network;
+    snn_status_t st;
+    b200::launch_ordered_sdeg(c->stream, c->device, c->d_list, c->idx_bits, c->d_ctr, parity, n, c->d_row_ptr,
+                              c->d_sdeg, 0, 0);
+    size_t tb = c->otemp_bytes;
+    if ((st = cuda_status(b200::scan_degrees_u64(c->stream, c->d_sdeg, c->d_eoff, n + 1, c->d_otemp, &tb))) != SNN_OK)
+        return st;
+    const uint64_t K = c->chunks.size();
+    b200::launch_gather_u64(c->stream, c->d_eoff, c->d_chunk_rb, K + 1, c->d_bounds);
+    if ((st = cuda_status(cudaMemcpyAsync(c->h_bounds, c->d_bounds, (K + 1) * 8, cudaMemcpyDeviceToHost,
+                                          c->stream))) != SNN_OK)
+        return st;
+    if ((st = cuda_status(cudaStreamSynchronize(c->stream))) != SNN_OK) return st;
+    c->launches += 3;
+    for (size_t i = 0; i < K; ++i) {
+        const StreamChunk &ch = c->chunks[i];
+        const uint64_t events = c->h_bounds[i + 1] - c->h_bounds[i];
+        if (events == 0) continue;  // no spiking row in this chunk: nothing to copy
+        const int s = (int)(i & 1u);
+        uint64_t *drow = c->d_chunk_row + (uint64_t)s * (c->slot_rows + 1);
+        uint64_t *dcol = c->d_chunk_col + (uint64_t)s * c->slot_stride;
+        float *dw = c->d_chunk_w + (uint64_t)s * c->slot_stride;
+        cudaStreamWaitEvent(c->copy_stream, c->ev_free[s], 0);
+        if (cudaMemcpyAsync(drow, net->row_ptr + ch.row_begin, (ch.rows + 1) * 8, cudaMemcpyHostToDevice,
+                            c->copy_stream) != cudaSuccess ||
+            cudaMemcpyAsync(dcol, net->col_idx + ch.edge_begin, ch.edge_count * 8, cudaMemcpyHostToDevice,
+                            c->copy_stream) != cudaSuccess ||
+            cudaMemcpyAsync(dw, net->weights + ch.edge_begin, ch.edge_count * 4, cudaMemcpyHostToDevice,
+                            c->copy_stream) != cudaSuccess)
+            return SNN_ERR_CUDA;
+        cudaEventRecord(c->ev_copied[s], c->copy_stream);
+        cudaStreamWaitEvent(c->stream, c->ev_copied[s], 0);
+        // The chunk arrays hold rows [row_begin, row_begin + rows) and edges
+        // from edge_begin: index them with absolute row and edge numbers.
+        b200::launch_ordered_gen(c->stream, c->device, c->d_list, c->idx_bits, c->d_ctr, parity, ch.row_begin,
+                                 ch.row_begin + ch.rows, drow - ch.row_begin, dcol - ch.edge_begin, 64,
+                                 dw - ch.edge_begin, c->d_eoff, n, c->h_bounds[i], c->d_sdeg, c->d_okeys[0],
+                                 c->d_ovals[0], 0, 0, 0);
+        tb = c->otemp_bytes;
+        bool alt = false;
+        if ((st = cuda_status(b200::sort_pairs_u32_f32(c->stream, c->d_okeys[0], c->d_okeys[1], c->d_ovals[0],
+                                                       c->d_ovals[1], events, target_bits(c), c->d_otemp, &tb,
+                                                       &alt))) != SNN_OK)
+            return st;
+        b200::launch_ordered_fold(c->stream, c->device, events, c->d_okeys[alt ? 1 : 0], c->d_ovals[alt ? 1 : 0],
+                                  next);
+        cudaEventRecord(c->ev_free[s], c->stream);
+        c->launches += 3;
+    }
+    // Statistics and the step epilogue (an empty row range).
+    b200::launch_ordered_gen(c->stream, c->device, c->d_list, c->idx_bits, c->d_ctr, parity, 0, 0, c->d_row_ptr,
+                             nullptr, 64, nullptr, c->d_eoff, n, 0, c->d_sdeg, c->d_okeys[0], c->d_ovals[0], 1,
+                             !sharded, 0);
+    c->launches++;
+    return cuda_status(cudaGetLastError());
+}
+
+// ORDERED set-up of a STREAMING context: row_ptr resident (8 B per row), the
+// event sort's buffers (chunked: as large as a chunk's synapses), and the
+// chunk boundary tables.
+snn_status_t setup_ordered_streaming(snn_cuda_context_t *c) {
+    const snn_network_t *net = c->network;
+    const uint64_t n = net->neuron_count;
+    snn_status_t st;
+    if (c->d_row_ptr == nullptr) {
+        if (cudaMalloc(&c->d_row_ptr, (n + 1) * 8) != cudaSuccess) return SNN_ERR_OUT_OF_MEMORY;
+        if ((st = cuda_status(cudaMemcpy(c->d_row_ptr, net->row_ptr, (n + 1) * 8, cudaMemcpyHostToDevice))) !=
+            SNN_OK)
+            return st;
+    }
+    const bool chunked = c->streaming == SNN_B200_STREAMING_CHUNKED;
+    if ((st = setup_ordered_push(c, chunked ? std::max<uint64_t>(c->slot_edges, 1) : UINT64_MAX)) != SNN_OK)
+        return st;
+    if (chunked) {
+        const uint64_t K = c->chunks.size();
+        std::vector<uint64_t> rb(K + 1);
+        for (uint64_t i = 0; i < K; ++i) rb[i] = c->chunks[i].row_begin;
+        rb[K] = n;
+        if (cudaMalloc(&c->d_chunk_rb, (K + 1) * 8) != cudaSuccess ||
+            cudaMalloc(&c->d_bounds, (K + 1) * 8) != cudaSuccess ||
+            cudaMallocHost(&c->h_bounds, (K + 1) * 8) != cudaSuccess)
+            return SNN_ERR_OUT_OF_MEMORY;
+        if ((st = cuda_status(cudaMemcpy(c->d_chunk_rb, rb.data(), (K + 1) * 8, cudaMemcpyHostToDevice))) != SNN_OK)
+            return st;
     }
     return SNN_OK;
 }
@@ -1248,7 +1353,9 @@ snn_status_t step_propagate(snn_cuda_context_t *c) {
                 c->launches++;
             }
         } else if (c->propagation == SNN_B200_PROPAGATE_ORDERED && !c->opull) {
-            if ((st = ordered_push_step(c, parity, next, sharded, peer ? xbitmap : c->d_bitmap)) != SNN_OK) return st;
+            if ((st = ordered_push_step(c, parity, next, sharded, peer ? xbitmap : c->d_bitmap, c->d_row_ptr, c->d_col,
+                                        c->col_bits, c->d_w)) != SNN_OK)
+                return st;
         } else if (c->propagation == SNN_B200_PROPAGATE_ORDERED)
             b200::launch_propagate_pull(c->stream, c->device, c->n_local, c->sell_chunks, c->sell_chunk_words,
                                     c->d_sell_off, (const uint2 *)c->d_pre,
@@ -1276,6 +1383,13 @@ snn_status_t step_propagate(snn_cuda_context_t *c) {
             }
         }
         if ((st = check_launch(c)) != SNN_OK) return st;
+    } else if (c->propagation == SNN_B200_PROPAGATE_ORDERED && c->streaming == SNN_B200_STREAMING_SPARSE) {
+        // Bit-exact sparse STREAMING: the event sort over the mapped host CSR.
+        if ((st = ordered_push_step(c, parity, next, sharded, peer ? xbitmap : c->d_bitmap, c->d_row_ptr,
+                                    c->h_col_dev, 64, c->h_w_dev)) != SNN_OK)
+            return st;
+    } else if (c->propagation == SNN_B200_PROPAGATE_ORDERED) {
+        if ((st = ordered_stream_chunked(c, parity, next, sharded)) != SNN_OK) return st;
     } else if (c->streaming == SNN_B200_STREAMING_SPARSE) {
         // Sparse STREAMING: spiking rows read straight from mapped host memory.
         b200::launch_propagate_push(c->stream, c->device, c->d_list, c->idx_bits, c->d_row_ptr, c->h_col_dev, 64,
@@ -1939,15 +2053,14 @@ snn_status_t snn_b200_create(const snn_network_t *network, const snn_cuda_config
     if (network == nullptr) return SNN_ERR_INVALID_ARGUMENT;
     const snn_cuda_config_t cfg = config ? *config : snn_cuda_default_config();
     const snn_b200_options_t o = options ? *options : snn_b200_default_options();
-    if ((o.propagation == SNN_B200_PROPAGATE_ORDERED || o.propagation == SNN_B200_PROPAGATE_PUSH_BINNED ||
-         o.batch > 1) && cfg.prefer_streaming)
+    if ((o.propagation == SNN_B200_PROPAGATE_PUSH_BINNED || o.batch > 1) && cfg.prefer_streaming)
         return SNN_ERR_UNSUPPORTED;
     snn_cuda_context_t *c = nullptr;
     CreateEnv env;
     snn_status_t st = begin_create(network->neuron_count, network->lif, network->decay, &cfg, &o, &c, &env);
     if (st != SNN_OK) return st;
     c->network = network;
-    const bool full_only = c->propagation == SNN_B200_PROPAGATE_ORDERED || c->batch > 1;
+    const bool full_only = c->want_binfold || c->batch > 1;
     if (full_only || (!cfg.prefer_streaming && full_push_bytes(c, network->synapse_count) <= env.budget)) {
         c->mode = SNN_CUDA_MODE_FULL;
         if (c->propagation != SNN_B200_PROPAGATE_ORDERED) {
@@ -1971,6 +2084,7 @@ snn_status_t snn_b200_create(const snn_network_t *network, const snn_cuda_config
             c->streaming = SNN_B200_STREAMING_CHUNKED;
             st = allocate_streaming(c, cfg, env.budget);
         }
+        if (st == SNN_OK && c->propagation == SNN_B200_PROPAGATE_ORDERED) st = setup_ordered_streaming(c);
     }
     if (st != SNN_OK) {
         free_context(c);

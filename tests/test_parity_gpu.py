@@ -736,3 +736,53 @@ def test_generated_pool_streaming_exact(mode):
     s = ctx.stats()
     assert s["spikes"] == int(sc.sum()) and s["events"] == int(ev.sum())
     np.testing.assert_array_equal(bits(st.voltage()), bits(ctx.download_voltage()))
+
+
+@pytest.mark.parametrize("mode,rows,syn", [(sb.STREAMING_CHUNKED, 700, 40000), (sb.STREAMING_CHUNKED, 0, 0),
+                                           (sb.STREAMING_SPARSE, 0, 0)])
+def test_streaming_ordered_general_weights_bit_exact(mode, rows, syn):
+    """STREAMING with ORDERED propagation and general (non-dyadic, mixed-sign)
+    weights: chunked (every chunk folds its own events onto the earlier
+    chunks' sums; with small chunks a step spans dozens of them) and sparse
+    (the event sort over the mapped host CSR). Rasters and voltages equal the
+    serial CPU step bit for bit."""
+    lif = baseline_lif()
+    n = 20011
+    net = ORC.random_pool(n, 100, -0.2, 0.5, 61, lif=lif)
+    cfg = sb.default_config(prefer_streaming=1, max_stream_rows=rows, max_stream_synapses=syn)
+    ctx = sb.CudaContext.create(net, cfg, opts(propagation=sb.PROPAGATE_ORDERED, streaming=mode))
+    assert ctx.mode == sb.MODE_STREAMING
+    cr, gr, cv, gv = run_pair(net, ctx, 40, inject=stream_inject(8, 200, 25.0, n))
+    assert first_divergence(cr, gr) is None
+    assert cr.sum() > 1000
+    np.testing.assert_array_equal(bits(cv), bits(gv))
+
+
+@pytest.mark.parametrize("mode", [sb.STREAMING_CHUNKED, sb.STREAMING_SPARSE])
+def test_streaming_push_general_weights_tolerance(mode):
+    """STREAMING with the atomic push and general weights: from the same state
+    every step (teacher forcing), voltages and propagated currents within
+    1e-5 relative of the serial CPU step, divergent spikes counted (rare)."""
+    lif = baseline_lif()
+    n = 20011
+    net = ORC.random_pool(n, 100, -0.2, 0.5, 62, lif=lif)
+    cfg = sb.default_config(prefer_streaming=1, max_stream_rows=900)
+    ctx = sb.CudaContext.create(net, cfg, opts(streaming=mode))
+    assert ctx.mode == sb.MODE_STREAMING
+    st = State(net)
+    inj = stream_inject(9, 200, 25.0, n)
+    divergent, max_rel = 0, 0.0
+    for t in range(40):
+        ctx.upload_state(st.voltage(), st.current(), st.refractory())
+        idx, val = inj(t)
+        st.inject(idx, val)
+        ctx.inject_current(idx, val)
+        cs, gs = st.step(), ctx.step()
+        divergent += int((cs != gs).sum())
+        same = cs == gs
+        cv, gv = st.voltage(), ctx.download_voltage()
+        rel = np.abs(cv[same] - gv[same]) / np.maximum(np.abs(cv[same]), 1e-30)
+        max_rel = max(max_rel, float(rel.max()))
+        assert np.allclose(st.current(), ctx.download_current(), rtol=1e-5, atol=1e-5)
+    assert max_rel <= 1e-5, max_rel
+    assert divergent <= 5, divergent
