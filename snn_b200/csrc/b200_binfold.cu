@@ -139,10 +139,7 @@ __global__ void __launch_bounds__(kBfThreads) chunk_counts_kernel(uint32_t *__re
                                                                   uint32_t *__restrict__ ccnt, DevCounters *ctr,
                                                                   uint64_t own_begin, uint64_t own_end, PeerWait pw) {
     if (pw.nflags) {
-        __shared__ uint32_t s_ok;
-        if (threadIdx.x == 0) s_ok = wait_peer_flags(pw, ctr, blockIdx.x == 0) ? 1u : 0u;
-        __syncthreads();
-        if (!s_ok) return;
+        if (!block_peer_sync(pw, ctr)) return;
     }
     const uint64_t chunks = (words + kChunkWords - 1) / kChunkWords;
     unsigned long long own = 0;

@@ -49,31 +49,44 @@ __device__ __forceinline__ unsigned long long global_ns() {
     return t;
 }
 
-// One thread waits (bounded) until every flag of pw reaches pw.tag; false
-// when the wait expired or another wait already failed (ctr->error is set).
-// timed: add the wait to ctr->wait_ns / wait_max_ns.
-__device__ __forceinline__ bool wait_peer_flags(const PeerWait &pw, DevCounters *ctr, bool timed) {
-    bool ok = true;
-    const unsigned long long t0 = timed ? global_ns() : 0ull;
-    for (uint32_t r = 0; r < pw.nflags && ok; ++r) {
+// The peer exchange's publish-then-wait, by every thread of a CTA (the
+// kernel right after LIF on the stream). Thread r < nflags releases this
+// step's tag into this rank's slot at rank r, then waits (bounded) for rank
+// r's flag here. Every CTA publishes (idempotently), so no CTA depends on
+// another one having been scheduled. False when a wait expired or another
+// wait already failed (ctr->error is set). timed: block 0 adds its wait to
+// ctr->wait_ns / wait_max_ns.
+__device__ __forceinline__ bool block_peer_sync(const PeerWait &pw, DevCounters *ctr) {
+    __shared__ uint32_t s_fail;
+    __shared__ unsigned long long s_t0;
+    if (threadIdx.x == 0) {
+        s_fail = 0u;
+        s_t0 = global_ns();
+    }
+    __syncthreads();
+    if (threadIdx.x < pw.nflags) {
+        const uint32_t r = threadIdx.x;
+        if (pw.publish[r] != nullptr)
+            asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(pw.publish[r]), "l"(pw.tag) : "memory");
         for (uint32_t it = 0;; ++it) {
             unsigned long long v;
             asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(pw.flags + r) : "memory");
             if (v >= pw.tag) break;
             if (*(volatile uint32_t *)&ctr->error != 0u || it >= pw.spin_limit) {
                 atomicExch(&ctr->error, 3u);
-                ok = false;
+                s_fail = 1u;
                 break;
             }
             __nanosleep(64);
         }
     }
-    if (timed) {
-        const unsigned long long dt = global_ns() - t0;
+    __syncthreads();
+    if (blockIdx.x == 0 && threadIdx.x == 0) {
+        const unsigned long long dt = global_ns() - s_t0;
         ctr->wait_ns += dt;
         if (dt > ctr->wait_max_ns) ctr->wait_max_ns = dt;
     }
-    return ok;
+    return s_fail == 0u;
 }
 
 // Word wi of the global bitmap after the peer wait: this rank's words from

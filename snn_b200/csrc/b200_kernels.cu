@@ -243,15 +243,6 @@ __global__ void __launch_bounds__(kLifThreads) lif_kernel(uint64_t n, LifArgs p,
     }
 }
 
-// Peer exchange publication, launched right after the LIF kernel on the same
-// stream: the LIF kernel's words are complete and visible when it starts, and
-// its release store of the step tag into this rank's flag slot of every rank
-// lets the others read them after an acquire.
-__global__ void publish_flags_kernel(PeerArgs peer) {
-    if (threadIdx.x < peer.npeers)
-        asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(peer.flag[threadIdx.x]), "l"(peer.tag) : "memory");
-}
-
 // ---------------------------------------------------------- compaction ----
 template <typename TIdx>
 __global__ void __launch_bounds__(256) compact_kernel(uint32_t *__restrict__ bitmap, uint64_t words,
@@ -260,10 +251,7 @@ __global__ void __launch_bounds__(256) compact_kernel(uint32_t *__restrict__ bit
     const unsigned lane = lane_id();
     if (pw.nflags) {
         // Wait (bounded) until every rank has published this step's slice.
-        __shared__ uint32_t s_ok;
-        if (threadIdx.x == 0) s_ok = wait_peer_flags(pw, ctr, blockIdx.x == 0) ? 1u : 0u;
-        __syncthreads();
-        if (!s_ok) return;
+        if (!block_peer_sync(pw, ctr)) return;
     }
     // Four words (16 bytes) per thread: the bitmap (words a multiple of 4)
     // and every rank's slice (slot_words a multiple of 4) are 16-byte
@@ -1070,11 +1058,8 @@ static void lif_dispatch(cudaStream_t s, int device, uint64_t n, const LifArgs &
 
 void launch_lif(cudaStream_t s, int device, uint64_t n, const LifArgs &p, float *v, float *cur, const float *ext,
                 uint32_t *refr, uint8_t *spikes, uint32_t *bitmap, void *list, int idx_bits, uint64_t off,
-                DevCounters *ctr, int parity, const PeerArgs *peer_in) {
-    if (n == 0) {
-        if (peer_in && peer_in->npeers) publish_flags_kernel<<<1, 32, 0, s>>>(*peer_in);
-        return;
-    }
+                DevCounters *ctr, int parity) {
+    if (n == 0) return;
     // Small populations: 1024-neuron tiles, so the grid still covers the SMs.
     const bool small = n < (uint64_t)sm_count(device) * 2u * kLifThreads * 4u * 8u;
     if (idx_bits == 32 && small) {
@@ -1087,7 +1072,6 @@ void launch_lif(cudaStream_t s, int device, uint64_t n, const LifArgs &p, float 
         if (ext) lif_dispatch<true, uint64_t, 4>(s, device, n, p, v, cur, ext, refr, spikes, bitmap, list, off, ctr, parity);
         else lif_dispatch<false, uint64_t, 4>(s, device, n, p, v, cur, ext, refr, spikes, bitmap, list, off, ctr, parity);
     }
-    if (peer_in && peer_in->npeers) publish_flags_kernel<<<1, 32, 0, s>>>(*peer_in);
 }
 
 void launch_compact(cudaStream_t s, int device, uint32_t *bitmap, uint64_t words, void *list, int idx_bits,

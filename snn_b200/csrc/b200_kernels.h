@@ -51,24 +51,21 @@ struct DevCounters {
 };
 static_assert(sizeof(DevCounters) <= 256, "DevCounters must fit its 256-byte block");
 
-// Peer (NVLink, CUDA IPC) spike-bitmap exchange, pull style. The LIF kernel
-// writes this rank's bitmap words into its own exchange buffer (passed as its
-// bitmap); a one-CTA kernel launched behind it on the same stream then
-// releases `tag` into this rank's flag slot of every rank (st.release.sys).
-// npeers == 0 disables it.
+// Peer (NVLink, CUDA IPC) spike-bitmap exchange, pull style: the LIF kernel
+// writes this rank's bitmap words into its own exchange buffer (passed as
+// its bitmap); the compaction publishes and gathers (PeerWait).
 constexpr uint32_t kMaxPeers = 8;
-struct PeerArgs {
-    unsigned long long *flag[kMaxPeers];  // this rank's flag slot in each rank's exchange buffer
-    unsigned long long tag;               // monotonic exchange step, published when done
-    uint32_t npeers;
-};
-// Wait side, done by the compaction before it reads the global bitmap: all
-// `nflags` flags (in the local buffer) must reach `tag` (bounded wait); then
+// Wait side, done by the compaction (the kernel after LIF) before it reads
+// the global bitmap: every CTA first releases `tag` into this rank's flag
+// slot at every rank (publish[r]; LIF's words are complete when the kernel
+// starts), then all `nflags` flags (in the local buffer) must reach `tag`
+// (bounded wait, one thread per flag); then
 // the words of every other rank r are read from src[r] (that rank's exchange
 // buffer of this parity, over NVLink) and stored into the local buffer, so
 // the local buffer holds the whole global bitmap afterwards. Rank r owns
 // words [r * slot_words, (r + 1) * slot_words).
 struct PeerWait {
+    unsigned long long *publish[kMaxPeers];  // this rank's flag slot at each rank (released first)
     const unsigned long long *flags;
     unsigned long long tag;
     uint32_t nflags;
@@ -116,7 +113,7 @@ void launch_init_state(cudaStream_t s, uint64_t n, float v_rest, float *v, float
 // spike list of parity `parity`. idx_bits selects a 32- or 64-bit list.
 void launch_lif(cudaStream_t s, int device, uint64_t n, const LifArgs &p, float *v, float *cur, const float *ext,
                 uint32_t *refr, uint8_t *spikes, uint32_t *bitmap, void *list, int idx_bits, uint64_t global_offset,
-                DevCounters *ctr, int parity, const PeerArgs *peer = nullptr);
+                DevCounters *ctr, int parity);
 
 // Global bitmap -> spike list (sharded contexts, after the all-gather; with a
 // peer wait, the other ranks' words are first gathered into `bitmap`).

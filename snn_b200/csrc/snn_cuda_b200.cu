@@ -1239,20 +1239,18 @@ snn_status_t step_lif(snn_cuda_context_t *c, bool has_ext) {
         set_error("snn_b200", "peer exchange used before snn_b200_ipc_connect");
         return SNN_ERR_INVALID_ARGUMENT;
     }
-    b200::PeerArgs pa{};
     b200::PeerWait &pw = ps.pw;
     if (peer) {
         // Pull exchange: LIF writes this rank's words into its own buffer of
-        // this parity and releases its flag at every rank; the compaction
-        // waits for every flag and reads the other ranks' words over NVLink.
+        // this parity; the compaction (the next kernel) releases this rank's
+        // flag at every rank, waits for every flag and reads the other ranks'
+        // words over NVLink.
         ++c->xstep;
         const uint64_t par = c->xstep & 1u;
         for (uint32_t r = 0; r < c->world; ++r) {
-            pa.flag[r] = (unsigned long long *)((char *)c->peer_x[r] + xflags_offset(c)) + c->rank;
+            pw.publish[r] = (unsigned long long *)((char *)c->peer_x[r] + xflags_offset(c)) + c->rank;
             pw.src[r] = c->peer_x[r] + par * c->bitmap_words;
         }
-        pa.npeers = c->world;
-        pa.tag = c->xstep;
         ps.xbitmap = (uint32_t *)c->d_xbuf + par * c->bitmap_words;
         ps.own_bitmap = ps.xbitmap + (uint64_t)c->rank * (c->slot / 32);
         pw.flags = (const unsigned long long *)((char *)c->d_xbuf + xflags_offset(c));
@@ -1269,10 +1267,9 @@ snn_status_t step_lif(snn_cuda_context_t *c, bool has_ext) {
     const bool ordered_list = ps.ordered_list = c->binfold && c->mode == SNN_CUDA_MODE_FULL;
     b200::launch_lif(c->stream, c->device, c->n_local, lif_args, c->d_v, cur, has_ext ? c->d_ext : nullptr, c->d_refr,
                      c->d_spikes, ps.own_bitmap, (sharded || ordered_list) ? nullptr : c->d_list, c->idx_bits, c->lo,
-                     c->d_ctr, parity, peer ? &pa : nullptr);
+                     c->d_ctr, parity);
     snn_status_t st = check_launch(c);
     if (st != SNN_OK) return st;
-    if (peer) c->launches++;  // the flag publication behind the LIF kernel
     timing_mark(c, tg, 1);
     if (c->spk_dst != nullptr) {
         // The spikes are final once LIF is done; download them while the
