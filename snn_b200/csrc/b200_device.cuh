@@ -49,12 +49,9 @@ __device__ __forceinline__ unsigned long long global_ns() {
     return t;
 }
 
-// The peer exchange's publish-then-wait, by every thread of a CTA (the
-// kernel right after LIF on the stream). Thread r < nflags releases this
-// step's tag into this rank's slot at rank r, then waits (bounded) for rank
-// r's flag here. Every CTA publishes (idempotently), so no CTA depends on
-// another one having been scheduled. False when a wait expired or another
-// wait already failed (ctr->error is set). timed: block 0 adds its wait to
+// The peer exchange's wait, by every thread of a CTA: thread r < nflags
+// waits (bounded) for rank r's flag. False when a wait expired or another
+// wait already failed (ctr->error is set). Block 0 adds its wait to
 // ctr->wait_ns / wait_max_ns.
 __device__ __forceinline__ bool block_peer_sync(const PeerWait &pw, DevCounters *ctr) {
     __shared__ uint32_t s_fail;
@@ -66,8 +63,6 @@ __device__ __forceinline__ bool block_peer_sync(const PeerWait &pw, DevCounters 
     __syncthreads();
     if (threadIdx.x < pw.nflags) {
         const uint32_t r = threadIdx.x;
-        if (pw.publish[r] != nullptr)
-            asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(pw.publish[r]), "l"(pw.tag) : "memory");
         for (uint32_t it = 0;; ++it) {
             unsigned long long v;
             asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(pw.flags + r) : "memory");

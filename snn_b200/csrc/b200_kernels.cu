@@ -243,6 +243,15 @@ __global__ void __launch_bounds__(kLifThreads) lif_kernel(uint64_t n, LifArgs p,
     }
 }
 
+// Peer exchange publication, launched right after the LIF kernel on the same
+// stream: the LIF kernel's words are complete and visible when it starts, and
+// its release store of the step tag into this rank's flag slot of every rank
+// lets the others read them after an acquire.
+__global__ void publish_flags_kernel(PeerWait pw) {
+    if (threadIdx.x < pw.nflags && pw.publish[threadIdx.x] != nullptr)
+        asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(pw.publish[threadIdx.x]), "l"(pw.tag) : "memory");
+}
+
 // ---------------------------------------------------------- compaction ----
 template <typename TIdx>
 __global__ void __launch_bounds__(256) compact_kernel(uint32_t *__restrict__ bitmap, uint64_t words,
@@ -1196,6 +1205,8 @@ __global__ void gather_u64_kernel(const unsigned long long *src, const uint64_t 
     const uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (i < count) dst[i] = src[idx[i]];
 }
+
+void launch_publish_flags(cudaStream_t s, const PeerWait &pw) { publish_flags_kernel<<<1, 32, 0, s>>>(pw); }
 
 void launch_gather_u64(cudaStream_t s, const unsigned long long *src, const uint64_t *idx, uint64_t count,
                        unsigned long long *dst) {

@@ -53,19 +53,19 @@ static_assert(sizeof(DevCounters) <= 256, "DevCounters must fit its 256-byte blo
 
 // Peer (NVLink, CUDA IPC) spike-bitmap exchange, pull style: the LIF kernel
 // writes this rank's bitmap words into its own exchange buffer (passed as
-// its bitmap); the compaction publishes and gathers (PeerWait).
+// its bitmap); launch_publish_flags then releases this rank's flag and the
+// compaction waits and gathers (PeerWait).
 constexpr uint32_t kMaxPeers = 8;
-// Wait side, done by the compaction (the kernel after LIF) before it reads
-// the global bitmap: every CTA first releases `tag` into this rank's flag
-// slot at every rank (publish[r]; LIF's words are complete when the kernel
-// starts), then all `nflags` flags (in the local buffer) must reach `tag`
-// (bounded wait, one thread per flag); then
+// A one-CTA kernel behind LIF releases `tag` into this rank's flag slot at
+// every rank (publish[r]). The compaction then waits (bounded, one thread
+// per flag) until all `nflags` flags (in the local buffer) reach `tag`;
+// then
 // the words of every other rank r are read from src[r] (that rank's exchange
 // buffer of this parity, over NVLink) and stored into the local buffer, so
 // the local buffer holds the whole global bitmap afterwards. Rank r owns
 // words [r * slot_words, (r + 1) * slot_words).
 struct PeerWait {
-    unsigned long long *publish[kMaxPeers];  // this rank's flag slot at each rank (released first)
+    unsigned long long *publish[kMaxPeers];  // this rank's flag slot at each rank (publication kernel)
     const unsigned long long *flags;
     unsigned long long tag;
     uint32_t nflags;
@@ -114,6 +114,9 @@ void launch_init_state(cudaStream_t s, uint64_t n, float v_rest, float *v, float
 void launch_lif(cudaStream_t s, int device, uint64_t n, const LifArgs &p, float *v, float *cur, const float *ext,
                 uint32_t *refr, uint8_t *spikes, uint32_t *bitmap, void *list, int idx_bits, uint64_t global_offset,
                 DevCounters *ctr, int parity);
+
+// The flag release of the peer exchange (behind the LIF kernel).
+void launch_publish_flags(cudaStream_t s, const PeerWait &pw);
 
 // Global bitmap -> spike list (sharded contexts, after the all-gather; with a
 // peer wait, the other ranks' words are first gathered into `bitmap`).

@@ -1242,9 +1242,9 @@ snn_status_t step_lif(snn_cuda_context_t *c, bool has_ext) {
     b200::PeerWait &pw = ps.pw;
     if (peer) {
         // Pull exchange: LIF writes this rank's words into its own buffer of
-        // this parity; the compaction (the next kernel) releases this rank's
-        // flag at every rank, waits for every flag and reads the other ranks'
-        // words over NVLink.
+        // this parity, a one-CTA kernel behind it releases this rank's flag
+        // at every rank; the compaction waits for every flag and reads the
+        // other ranks' words over NVLink.
         ++c->xstep;
         const uint64_t par = c->xstep & 1u;
         for (uint32_t r = 0; r < c->world; ++r) {
@@ -1270,6 +1270,10 @@ snn_status_t step_lif(snn_cuda_context_t *c, bool has_ext) {
                      c->d_ctr, parity);
     snn_status_t st = check_launch(c);
     if (st != SNN_OK) return st;
+    if (peer) {
+        b200::launch_publish_flags(c->stream, pw);
+        c->launches++;
+    }
     timing_mark(c, tg, 1);
     if (c->spk_dst != nullptr) {
         // The spikes are final once LIF is done; download them while the
@@ -1300,11 +1304,12 @@ snn_status_t step_exchange(snn_cuda_context_t *c) {
 }
 
 // Phase 3: compaction (the global spike list; with the peer exchange after
-// the flag waits and the NVLink gather), propagation, buffer swap.
-snn_status_t step_propagate(snn_cuda_context_t *c) {
+// the flag waits and the NVLink gather). Ranks driven from one thread
+// enqueue every compaction before any propagation: a propagation may wait on
+// the host (ORDERED's event count).
+snn_status_t step_compact(snn_cuda_context_t *c) {
     StepState &ps = c->ps;
     const int parity = ps.parity;
-    float *next = ps.next;
     TimingGroup *tg = ps.tg;
     const bool sharded = ps.sharded, peer = ps.peer, ordered_list = ps.ordered_list;
     uint32_t *xbitmap = ps.xbitmap;
@@ -1334,6 +1339,19 @@ snn_status_t step_propagate(snn_cuda_context_t *c) {
         if ((st = cuda_status(cudaGetLastError())) != SNN_OK) return st;
     }
     timing_mark(c, tg, 2);
+    return SNN_OK;
+}
+
+// Phase 4: propagation and buffer swap.
+snn_status_t step_propagate(snn_cuda_context_t *c) {
+    StepState &ps = c->ps;
+    const int parity = ps.parity;
+    float *next = ps.next;
+    TimingGroup *tg = ps.tg;
+    const bool sharded = ps.sharded, peer = ps.peer;
+    uint32_t *xbitmap = ps.xbitmap;
+    const uint64_t brows = ps.brows;
+    snn_status_t st = SNN_OK;
     if (c->mode == SNN_CUDA_MODE_FULL) {
         if (c->binfold) {
             const cudaError_t e = b200::launch_binfold(c->stream, c->device, c->bf, c->bfb, c->d_list, c->idx_bits,
@@ -1441,6 +1459,7 @@ snn_status_t step_propagate(snn_cuda_context_t *c) {
 snn_status_t enqueue_step(snn_cuda_context_t *c, bool has_ext) {
     snn_status_t st = step_lif(c, has_ext);
     if (st == SNN_OK) st = step_exchange(c);
+    if (st == SNN_OK) st = step_compact(c);
     if (st == SNN_OK) st = step_propagate(c);
     return st;
 }
@@ -1956,9 +1975,9 @@ snn_status_t group_exchange(snn_cuda_context_t *g) {
     return st;
 }
 
-// One step of every member: all LIF phases first (with the peer exchange a
-// member's compaction waits for every member's flag), the all-gathers as
-// one NCCL group, then the propagations.
+// One step of every member: all LIF phases first, the all-gathers as one
+// NCCL group, all compactions (with the peer exchange each releases its
+// member's flag and waits for every other's), then the propagations.
 snn_status_t group_step_async(snn_cuda_context_t *g, const float *ext, uint8_t *spikes) {
     snn_status_t st = for_members(g, [&](snn_cuda_context_t *m) {
         if (ext != nullptr && m->n_local) {
@@ -1976,6 +1995,7 @@ snn_status_t group_step_async(snn_cuda_context_t *g, const float *ext, uint8_t *
         return step_lif(m, ext != nullptr || m->ext_held);
     });
     if (st == SNN_OK) st = group_exchange(g);
+    if (st == SNN_OK) st = for_members(g, [](snn_cuda_context_t *m) { return step_compact(m); });
     const snn_status_t s3 = for_members(g, [&](snn_cuda_context_t *m) {
         const snn_status_t s2 = st == SNN_OK ? step_propagate(m) : SNN_OK;
         m->spk_dst = nullptr;
