@@ -13,16 +13,19 @@
 //     local targets) into hist[tile][cta];
 //  3. an exclusive scan of hist (tile-major) gives every (tile, CTA) its
 //     first slot in the event array;
-//  4. scatter: every CTA walks its slice again, eight rows at a time (one per
-//     warp), and writes each event (target within the tile, weight) to its
-//     tile's slots; ranks inside a warp come from __match_any_sync, ranks
-//     across warps from a per-(warp, tile) prefix, so every tile's events
-//     keep the global (row, edge) order;
-//  5. fold: one CTA per tile keeps the tile's sums in shared memory and folds
-//     the tile's events window by window in order (each warp owns an eighth
-//     of the tile; same-target events inside one round of 32 are applied in
-//     lane order), then writes the tile's currents.
-// A step whose events exceed `gate_events` is a dense step: 2-5 do nothing
+//  4. scatter: every CTA walks its slice again in groups of rows (each warp
+//     a run of consecutive rows, the warps in row order): per-warp counts per
+//     tile, a prefix over the warps behind the CTA's cursor of each tile, then
+//     every event (target within the tile, weight) is written to its slot;
+//     equal tiles inside one round of 32 events are ranked in lane (= edge)
+//     order (a shared-memory tag finds collisions, a ballot match over the
+//     5-bit group id ranks them), so every tile keeps the global order;
+//  5. fold: one CTA per tile keeps the tile's sums in shared memory; each
+//     window of events is partitioned stably by owner warp (an eighth of the
+//     tile each), then every warp applies its events in order, same-target
+//     events of a round one after the other in lane order; last, the tile's
+//     currents are written.
+// A step whose events exceed the gate is a dense step: 2-5 do nothing
 // and the pull kernel (launched behind the same device-side gate) runs.
 // HBM per event: 4 B (count) + 8 B (scatter reads) + 8 B (scatter writes) +
 // 8 B (fold reads), with 32-bit columns.

@@ -211,7 +211,7 @@ struct snn_cuda_context {
 
     ncclComm_t comm = nullptr;
     // Peer exchange (SNN_B200_EXCHANGE_PEER): [2 parities][bitmap_words] u32,
-    // then world u64 flags, then a u32 ticket; peers' buffers mapped by IPC.
+    // then world u64 flags (slot r: rank r's step tag); peers' buffers mapped by IPC.
     int exchange = SNN_B200_EXCHANGE_NCCL;
     int streaming = SNN_B200_STREAMING_CHUNKED;
     // Sparse streaming: device pointers of the page-locked, mapped host CSR.
