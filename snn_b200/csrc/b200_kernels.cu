@@ -723,13 +723,14 @@ __global__ void step_epilogue_kernel(DevCounters *ctr, int parity, int count_spi
 }
 
 // ------------------------------------------------------------- inject ----
-__global__ void inject_atomic_kernel(uint64_t count, const uint64_t *__restrict__ idx,
-                                     const float *__restrict__ val, float scale, float *__restrict__ cur,
-                                     uint64_t lo, uint64_t hi) {
+// Equal values: one value for every index (any order gives the same bits).
+__global__ void inject_uniform_kernel(uint64_t count, const uint64_t *__restrict__ idx, float value, float scale,
+                                      float *__restrict__ cur, uint64_t lo, uint64_t hi) {
+    const float add = __fmul_rn(value, scale);
     const uint64_t stride = (uint64_t)blockDim.x * gridDim.x;
     for (uint64_t k = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; k < count; k += stride) {
         const uint64_t i = idx[k];
-        if (i >= lo && i < hi) red_add(cur + (i - lo), __fmul_rn(val[k], scale));
+        if (i >= lo && i < hi) red_add(cur + (i - lo), add);
     }
 }
 
@@ -1238,9 +1239,9 @@ void launch_step_epilogue(cudaStream_t s, DevCounters *ctr, int parity, int coun
     step_epilogue_kernel<<<1, 32, 0, s>>>(ctr, parity, count_spikes);
 }
 
-void launch_inject_atomic(cudaStream_t s, int device, uint64_t count, const uint64_t *idx, const float *val,
-                          float scale, float *cur, uint64_t lo, uint64_t hi) {
-    inject_atomic_kernel<<<grid_for(device, 8, count, 256), 256, 0, s>>>(count, idx, val, scale, cur, lo, hi);
+void launch_inject_uniform(cudaStream_t s, int device, uint64_t count, const uint64_t *idx, float value,
+                           float scale, float *cur, uint64_t lo, uint64_t hi) {
+    inject_uniform_kernel<<<grid_for(device, 8, count, 256), 256, 0, s>>>(count, idx, value, scale, cur, lo, hi);
 }
 
 void launch_inject_ordered(cudaStream_t s, int device, uint64_t count, const uint64_t *idx, const float *val,

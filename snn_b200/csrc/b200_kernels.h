@@ -177,8 +177,9 @@ void launch_propagate_chunk(cudaStream_t s, int device, uint64_t row0, uint64_t 
 void launch_step_epilogue(cudaStream_t s, DevCounters *ctr, int parity, int count_spikes);
 
 // Sparse injection. Indices outside [lo, hi) are skipped (other shards).
-void launch_inject_atomic(cudaStream_t s, int device, uint64_t count, const uint64_t *idx, const float *val,
-                          float scale, float *cur, uint64_t lo, uint64_t hi);
+// Every index receives value * scale (equal values: order-free).
+void launch_inject_uniform(cudaStream_t s, int device, uint64_t count, const uint64_t *idx, float value,
+                           float scale, float *cur, uint64_t lo, uint64_t hi);
 // Indices sorted ascending with a stable sort: every run of equal indices is
 // folded sequentially in its (original k) order.
 void launch_inject_ordered(cudaStream_t s, int device, uint64_t count, const uint64_t *idx, const float *val,

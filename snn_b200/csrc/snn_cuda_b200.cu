@@ -203,6 +203,11 @@ struct snn_cuda_context {
     float *h_inj_val = nullptr;
     uint64_t h_inj_cap = 0;
     cudaEvent_t ev_inj = nullptr;
+    // Equal-value injections copy the caller's indices straight to the device
+    // on their own stream (the host waits for that copy only); ev_inj_used
+    // marks the last injection kernel, after which the index buffer is free.
+    cudaStream_t inj_stream = nullptr;
+    cudaEvent_t ev_inj_copy = nullptr, ev_inj_used = nullptr;
     // snn_cuda_step on FULL contexts: the spike download runs on its own
     // stream as soon as the LIF kernel is done, overlapping propagation.
     cudaStream_t spk_stream = nullptr;
@@ -306,6 +311,9 @@ void free_context(snn_cuda_context_t *c) {
         if (c->ev_free[i]) cudaEventDestroy(c->ev_free[i]);
     }
     if (c->ev_inj) cudaEventDestroy(c->ev_inj);
+    if (c->ev_inj_copy) cudaEventDestroy(c->ev_inj_copy);
+    if (c->ev_inj_used) cudaEventDestroy(c->ev_inj_used);
+    if (c->inj_stream) cudaStreamDestroy(c->inj_stream);
     if (c->ev_lif) cudaEventDestroy(c->ev_lif);
     if (c->ev_spk) cudaEventDestroy(c->ev_spk);
     if (c->spk_stream) cudaStreamDestroy(c->spk_stream);
@@ -2244,27 +2252,55 @@ snn_status_t snn_cuda_inject_current(snn_cuda_context_t *c, const snn_size_t *ho
         return st;
     }
     if (count > UINT64_MAX / sizeof(snn_size_t)) return SNN_ERR_INVALID_ARGUMENT;
-    for (uint64_t k = 0; k < count; ++k)
-        if (host_indices[k] >= c->n_global) return SNN_ERR_INVALID_ARGUMENT;
-    bool uniform = true;
+    // One pass: every index in range, and whether all values are equal.
     uint32_t v0;
     std::memcpy(&v0, host_values, 4);
-    for (uint64_t k = 1; k < count && uniform; ++k) {
+    uint64_t bad = 0;
+    uint32_t differ = 0;
+    for (uint64_t k = 0; k < count; ++k) {
         uint32_t vk;
         std::memcpy(&vk, host_values + k, 4);
-        uniform = vk == v0;
+        bad |= (uint64_t)(host_indices[k] >= c->n_global);
+        differ |= vk ^ v0;
     }
+    if (bad) return SNN_ERR_INVALID_ARGUMENT;
+    const bool uniform = differ == 0;
     snn_status_t st = set_device(c);
     if (st != SNN_OK) return st;
     if ((st = ensure_inject_capacity(c, count)) != SNN_OK) return st;
-    // The pinned staging is reused: wait until the previous batch's copy is done.
-    if (cudaEventSynchronize(c->ev_inj) != cudaSuccess) return SNN_ERR_CUDA;
     if (uniform) {
         // Equal values: any accumulation order gives the same bits, so a
-        // plain atomic scatter is exact.
-        std::memcpy(c->h_inj_idx, host_indices, count * 8);
-        std::memcpy(c->h_inj_val, host_values, count * 4);
-    } else {
+        // plain atomic scatter is exact, and the value travels as a kernel
+        // argument. The indices go straight from the caller's buffer; the
+        // call returns once that copy is done (the caller may reuse it).
+        // Fault seams as the staged path: index copy, value copy, launch.
+        if (c->inj_stream == nullptr) {
+            if (cudaStreamCreateWithFlags(&c->inj_stream, cudaStreamNonBlocking) != cudaSuccess ||
+                cudaEventCreateWithFlags(&c->ev_inj_copy, cudaEventDisableTiming) != cudaSuccess ||
+                cudaEventCreateWithFlags(&c->ev_inj_used, cudaEventDisableTiming) != cudaSuccess)
+                return SNN_ERR_CUDA;
+            cudaEventRecord(c->ev_inj_used, c->stream);  // covers earlier (staged) injections
+        }
+        if (seam_fail()) return SNN_ERR_CUDA;
+        cudaStreamWaitEvent(c->inj_stream, c->ev_inj_used, 0);  // the previous injection has read the buffer
+        if (cudaMemcpyAsync(c->d_inj_idx, host_indices, count * 8, cudaMemcpyHostToDevice, c->inj_stream) !=
+            cudaSuccess)
+            return cuda_status(cudaGetLastError());
+        if (seam_fail()) return SNN_ERR_CUDA;
+        cudaEventRecord(c->ev_inj_copy, c->inj_stream);
+        cudaStreamWaitEvent(c->stream, c->ev_inj_copy, 0);
+        if ((st = cuda_status(cudaEventSynchronize(c->ev_inj_copy))) != SNN_OK) return st;
+        float vf;
+        std::memcpy(&vf, &v0, 4);
+        b200::launch_inject_uniform(c->stream, c->device, count, c->d_inj_idx, vf, c->lif.input_scale,
+                                    c->d_cur[c->cur], c->lo, c->hi);
+        st = check_launch(c);
+        cudaEventRecord(c->ev_inj_used, c->stream);
+        return st;
+    }
+    // The pinned staging is reused: wait until the previous batch's copy is done.
+    if (cudaEventSynchronize(c->ev_inj) != cudaSuccess) return SNN_ERR_CUDA;
+    {
         // Unequal values: stable sort by index so each index's values fold
         // in their original order (src/snn.c:737-739).
         std::vector<uint64_t> perm(count);
@@ -2279,14 +2315,11 @@ snn_status_t snn_cuda_inject_current(snn_cuda_context_t *c, const snn_size_t *ho
     if ((st = h2d(c, c->d_inj_idx, c->h_inj_idx, count * 8)) != SNN_OK) return st;
     if ((st = h2d(c, c->d_inj_val, c->h_inj_val, count * 4)) != SNN_OK) return st;
     cudaEventRecord(c->ev_inj, c->stream);
-    float *cur = c->d_cur[c->cur];
-    if (uniform)
-        b200::launch_inject_atomic(c->stream, c->device, count, c->d_inj_idx, c->d_inj_val, c->lif.input_scale, cur,
-                                   c->lo, c->hi);
-    else
-        b200::launch_inject_ordered(c->stream, c->device, count, c->d_inj_idx, c->d_inj_val, c->lif.input_scale, cur,
-                                    c->lo, c->hi);
-    return check_launch(c);
+    b200::launch_inject_ordered(c->stream, c->device, count, c->d_inj_idx, c->d_inj_val, c->lif.input_scale,
+                                c->d_cur[c->cur], c->lo, c->hi);
+    st = check_launch(c);
+    if (c->ev_inj_used) cudaEventRecord(c->ev_inj_used, c->stream);
+    return st;
 }
 
 snn_status_t snn_cuda_step(snn_cuda_context_t *c, const float *host_external_current, uint8_t *host_out_spikes) {
