@@ -1377,6 +1377,15 @@ cudaError_t sort_pairs_u32_f32(cudaStream_t s, uint32_t *keys, uint32_t *keys_al
     return e;
 }
 
+cudaError_t sort_pairs_u64_f32(cudaStream_t s, uint64_t *keys, uint64_t *keys_alt, float *vals, float *vals_alt,
+                               uint64_t n, int end_bit, void *temp, size_t *temp_bytes, bool *result_in_alt) {
+    cub::DoubleBuffer<uint64_t> k(keys, keys_alt);
+    cub::DoubleBuffer<float> v(vals, vals_alt);
+    const cudaError_t e = cub::DeviceRadixSort::SortPairs(temp, *temp_bytes, k, v, (int64_t)n, 0, end_bit, s);
+    if (temp != nullptr) *result_in_alt = k.Current() != keys;
+    return e;
+}
+
 void launch_ordered_fold(cudaStream_t s, int device, uint64_t events, const uint32_t *keys, const float *vals,
                          float *next) {
     ordered_fold_kernel<<<grid_for(device, 8, events, 256), 256, 0, s>>>(events, keys, vals, next);

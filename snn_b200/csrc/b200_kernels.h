@@ -180,6 +180,9 @@ void launch_step_epilogue(cudaStream_t s, DevCounters *ctr, int parity, int coun
 // Every index receives value * scale (equal values: order-free).
 void launch_inject_uniform(cudaStream_t s, int device, uint64_t count, const uint64_t *idx, float value,
                            float scale, float *cur, uint64_t lo, uint64_t hi);
+// Stable radix sort of injection (index, value) pairs by index (low end_bit bits).
+cudaError_t sort_pairs_u64_f32(cudaStream_t s, uint64_t *keys, uint64_t *keys_alt, float *vals, float *vals_alt,
+                               uint64_t n, int end_bit, void *temp, size_t *temp_bytes, bool *result_in_alt);
 // Indices sorted ascending with a stable sort: every run of equal indices is
 // folded sequentially in its (original k) order.
 void launch_inject_ordered(cudaStream_t s, int device, uint64_t count, const uint64_t *idx, const float *val,

@@ -199,13 +199,12 @@ struct snn_cuda_context {
     uint64_t *d_inj_idx = nullptr;
     float *d_inj_val = nullptr;
     uint64_t inj_cap = 0;
-    uint64_t *h_inj_idx = nullptr;
-    float *h_inj_val = nullptr;
-    uint64_t h_inj_cap = 0;
-    cudaEvent_t ev_inj = nullptr;
-    // Equal-value injections copy the caller's indices straight to the device
-    // on their own stream (the host waits for that copy only); ev_inj_used
-    // marks the last injection kernel, after which the index buffer is free.
+    // Injections copy the caller's arrays straight to the device on their own
+    // stream (the host waits for that copy only); ev_inj_used marks the last
+    // injection kernel, after which the buffers are free. d_inj_idx holds the
+    // indices and their sort's alternate buffer (2 x inj_cap); d_inj_val the
+    // values, their alternate and the sort's scratch (inj_tmp_bytes).
+    size_t inj_tmp_bytes = 0;
     cudaStream_t inj_stream = nullptr;
     cudaEvent_t ev_inj_copy = nullptr, ev_inj_used = nullptr;
     // snn_cuda_step on FULL contexts: the spike download runs on its own
@@ -299,8 +298,6 @@ void free_context(snn_cuda_context_t *c) {
     if (c->h_err) cudaFreeHost(c->h_err);
     if (c->h_ototal) cudaFreeHost(c->h_ototal);
     if (c->h_bounds) cudaFreeHost(c->h_bounds);
-    if (c->h_inj_idx) cudaFreeHost(c->h_inj_idx);
-    if (c->h_inj_val) cudaFreeHost(c->h_inj_val);
     for (const void *p : c->registered)
         if (p) cudaHostUnregister(const_cast<void *>(p));
     std::free(c->h_slice_rp);
@@ -310,7 +307,6 @@ void free_context(snn_cuda_context_t *c) {
         if (c->ev_copied[i]) cudaEventDestroy(c->ev_copied[i]);
         if (c->ev_free[i]) cudaEventDestroy(c->ev_free[i]);
     }
-    if (c->ev_inj) cudaEventDestroy(c->ev_inj);
     if (c->ev_inj_copy) cudaEventDestroy(c->ev_inj_copy);
     if (c->ev_inj_used) cudaEventDestroy(c->ev_inj_used);
     if (c->inj_stream) cudaStreamDestroy(c->inj_stream);
@@ -421,7 +417,10 @@ snn_status_t allocate_state(snn_cuda_context_t *c) {
 
 snn_status_t create_streams(snn_cuda_context_t *c) {
     if (cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) != cudaSuccess) return SNN_ERR_CUDA;
-    if (cudaEventCreateWithFlags(&c->ev_inj, cudaEventDisableTiming) != cudaSuccess) return SNN_ERR_CUDA;
+    if (cudaStreamCreateWithFlags(&c->inj_stream, cudaStreamNonBlocking) != cudaSuccess ||
+        cudaEventCreateWithFlags(&c->ev_inj_copy, cudaEventDisableTiming) != cudaSuccess ||
+        cudaEventCreateWithFlags(&c->ev_inj_used, cudaEventDisableTiming) != cudaSuccess)
+        return SNN_ERR_CUDA;
     if (cudaMallocHost(&c->h_err, sizeof(uint32_t)) != cudaSuccess) return SNN_ERR_OUT_OF_MEMORY;
     *c->h_err = 0;
     return SNN_OK;
@@ -1472,31 +1471,33 @@ snn_status_t enqueue_step(snn_cuda_context_t *c, bool has_ext) {
     return st;
 }
 
+// Bits that cover every global index (the injection sort's key width).
+int inject_key_bits(const snn_cuda_context_t *c) {
+    int bits = 1;
+    while (bits < 64 && (1ull << bits) < c->n_global) ++bits;
+    return bits;
+}
+
 snn_status_t ensure_inject_capacity(snn_cuda_context_t *c, uint64_t count) {
-    if (count > c->inj_cap) {
-        cudaStreamSynchronize(c->stream);
-        cudaFree(c->d_inj_idx);
-        cudaFree(c->d_inj_val);
-        c->d_inj_idx = nullptr;
-        c->d_inj_val = nullptr;
-        c->inj_cap = 0;
-        snn_status_t st;
-        if ((st = dmalloc((void **)&c->d_inj_idx, count, 8)) != SNN_OK) return st;
-        if ((st = dmalloc((void **)&c->d_inj_val, count, 4)) != SNN_OK) return st;
-        c->inj_cap = count;
-    }
-    if (count > c->h_inj_cap) {
-        cudaEventSynchronize(c->ev_inj);
-        if (c->h_inj_idx) cudaFreeHost(c->h_inj_idx);
-        if (c->h_inj_val) cudaFreeHost(c->h_inj_val);
-        c->h_inj_idx = nullptr;
-        c->h_inj_val = nullptr;
-        c->h_inj_cap = 0;
-        if (cudaMallocHost(&c->h_inj_idx, count * 8) != cudaSuccess ||
-            cudaMallocHost(&c->h_inj_val, count * 4) != cudaSuccess)
-            return SNN_ERR_OUT_OF_MEMORY;
-        c->h_inj_cap = count;
-    }
+    if (count <= c->inj_cap) return SNN_OK;
+    cudaStreamSynchronize(c->stream);
+    cudaFree(c->d_inj_idx);
+    cudaFree(c->d_inj_val);
+    c->d_inj_idx = nullptr;
+    c->d_inj_val = nullptr;
+    c->inj_cap = 0;
+    size_t tmp = 0;
+    if (b200::sort_pairs_u64_f32(c->stream, nullptr, nullptr, nullptr, nullptr, count, inject_key_bits(c), nullptr,
+                                 &tmp, nullptr) != cudaSuccess)
+        return SNN_ERR_CUDA;
+    // Values and their alternate (2 x count floats), the scratch from the
+    // next 256-byte boundary.
+    const uint64_t val_bytes = (count * 8 + 255) & ~255ull;
+    snn_status_t st;
+    if ((st = dmalloc((void **)&c->d_inj_idx, count * 2, 8)) != SNN_OK) return st;
+    if ((st = dmalloc((void **)&c->d_inj_val, val_bytes + tmp, 1)) != SNN_OK) return st;
+    c->inj_tmp_bytes = tmp;
+    c->inj_cap = count;
     return SNN_OK;
 }
 
@@ -2268,57 +2269,44 @@ snn_status_t snn_cuda_inject_current(snn_cuda_context_t *c, const snn_size_t *ho
     snn_status_t st = set_device(c);
     if (st != SNN_OK) return st;
     if ((st = ensure_inject_capacity(c, count)) != SNN_OK) return st;
+    // The arrays go straight from the caller's buffers; the call returns once
+    // those copies are done (the caller may reuse them). Fault seams as the
+    // reference's staging: index copy, value copy, launch.
+    if (seam_fail()) return SNN_ERR_CUDA;
+    cudaStreamWaitEvent(c->inj_stream, c->ev_inj_used, 0);  // the previous injection has read the buffers
+    if (cudaMemcpyAsync(c->d_inj_idx, host_indices, count * 8, cudaMemcpyHostToDevice, c->inj_stream) != cudaSuccess)
+        return cuda_status(cudaGetLastError());
+    if (seam_fail()) return SNN_ERR_CUDA;
+    if (!uniform &&
+        cudaMemcpyAsync(c->d_inj_val, host_values, count * 4, cudaMemcpyHostToDevice, c->inj_stream) != cudaSuccess)
+        return cuda_status(cudaGetLastError());
+    cudaEventRecord(c->ev_inj_copy, c->inj_stream);
+    cudaStreamWaitEvent(c->stream, c->ev_inj_copy, 0);
+    if ((st = cuda_status(cudaEventSynchronize(c->ev_inj_copy))) != SNN_OK) return st;
     if (uniform) {
         // Equal values: any accumulation order gives the same bits, so a
-        // plain atomic scatter is exact, and the value travels as a kernel
-        // argument. The indices go straight from the caller's buffer; the
-        // call returns once that copy is done (the caller may reuse it).
-        // Fault seams as the staged path: index copy, value copy, launch.
-        if (c->inj_stream == nullptr) {
-            if (cudaStreamCreateWithFlags(&c->inj_stream, cudaStreamNonBlocking) != cudaSuccess ||
-                cudaEventCreateWithFlags(&c->ev_inj_copy, cudaEventDisableTiming) != cudaSuccess ||
-                cudaEventCreateWithFlags(&c->ev_inj_used, cudaEventDisableTiming) != cudaSuccess)
-                return SNN_ERR_CUDA;
-            cudaEventRecord(c->ev_inj_used, c->stream);  // covers earlier (staged) injections
-        }
-        if (seam_fail()) return SNN_ERR_CUDA;
-        cudaStreamWaitEvent(c->inj_stream, c->ev_inj_used, 0);  // the previous injection has read the buffer
-        if (cudaMemcpyAsync(c->d_inj_idx, host_indices, count * 8, cudaMemcpyHostToDevice, c->inj_stream) !=
-            cudaSuccess)
-            return cuda_status(cudaGetLastError());
-        if (seam_fail()) return SNN_ERR_CUDA;
-        cudaEventRecord(c->ev_inj_copy, c->inj_stream);
-        cudaStreamWaitEvent(c->stream, c->ev_inj_copy, 0);
-        if ((st = cuda_status(cudaEventSynchronize(c->ev_inj_copy))) != SNN_OK) return st;
+        // plain atomic scatter is exact; the value is a kernel argument.
         float vf;
         std::memcpy(&vf, &v0, 4);
         b200::launch_inject_uniform(c->stream, c->device, count, c->d_inj_idx, vf, c->lif.input_scale,
                                     c->d_cur[c->cur], c->lo, c->hi);
-        st = check_launch(c);
-        cudaEventRecord(c->ev_inj_used, c->stream);
-        return st;
+    } else {
+        // Unequal values: a stable radix sort by index, so each index's
+        // values fold in their original order (src/snn.c:737-739).
+        uint64_t *idx_alt = c->d_inj_idx + c->inj_cap;
+        float *val_alt = c->d_inj_val + c->inj_cap;
+        void *tmp = (char *)c->d_inj_val + ((c->inj_cap * 8 + 255) & ~255ull);
+        size_t tmp_bytes = c->inj_tmp_bytes;
+        bool in_alt = false;
+        if ((st = cuda_status(b200::sort_pairs_u64_f32(c->stream, c->d_inj_idx, idx_alt, c->d_inj_val, val_alt, count,
+                                                       inject_key_bits(c), tmp, &tmp_bytes, &in_alt))) != SNN_OK)
+            return st;
+        b200::launch_inject_ordered(c->stream, c->device, count, in_alt ? idx_alt : c->d_inj_idx,
+                                    in_alt ? val_alt : c->d_inj_val, c->lif.input_scale, c->d_cur[c->cur], c->lo,
+                                    c->hi);
     }
-    // The pinned staging is reused: wait until the previous batch's copy is done.
-    if (cudaEventSynchronize(c->ev_inj) != cudaSuccess) return SNN_ERR_CUDA;
-    {
-        // Unequal values: stable sort by index so each index's values fold
-        // in their original order (src/snn.c:737-739).
-        std::vector<uint64_t> perm(count);
-        std::iota(perm.begin(), perm.end(), 0ull);
-        std::stable_sort(perm.begin(), perm.end(),
-                         [&](uint64_t a, uint64_t b) { return host_indices[a] < host_indices[b]; });
-        for (uint64_t k = 0; k < count; ++k) {
-            c->h_inj_idx[k] = host_indices[perm[k]];
-            c->h_inj_val[k] = host_values[perm[k]];
-        }
-    }
-    if ((st = h2d(c, c->d_inj_idx, c->h_inj_idx, count * 8)) != SNN_OK) return st;
-    if ((st = h2d(c, c->d_inj_val, c->h_inj_val, count * 4)) != SNN_OK) return st;
-    cudaEventRecord(c->ev_inj, c->stream);
-    b200::launch_inject_ordered(c->stream, c->device, count, c->d_inj_idx, c->d_inj_val, c->lif.input_scale,
-                                c->d_cur[c->cur], c->lo, c->hi);
     st = check_launch(c);
-    if (c->ev_inj_used) cudaEventRecord(c->ev_inj_used, c->stream);
+    cudaEventRecord(c->ev_inj_used, c->stream);
     return st;
 }
 
