@@ -50,47 +50,6 @@ constexpr uint32_t kChunkWords = 2048;  // bitmap words per compaction chunk (65
 constexpr int kWordsPerThread = kChunkWords / kBfThreads;
 constexpr uint32_t kFoldWindow = 2048;  // events staged in shared memory per fold round
 
-__device__ __forceinline__ uint32_t lanemask_lt() {
-    uint32_t m;
-    asm("mov.u32 %0, %%lanemask_lt;" : "=r"(m));
-    return m;
-}
-
-// Lanes of `active` whose `key` (its low `nbits` bits) equals this lane's:
-// one ballot per key bit. Cheaper than __match_any_sync when most lanes hold
-// distinct keys (its cost grows with the number of distinct values).
-template <int NB>
-__device__ __forceinline__ uint32_t match_bits_n(uint32_t key, uint32_t active) {
-    uint32_t peers = active;
-#pragma unroll
-    for (int b = 0; b < NB; ++b) {
-        const uint32_t bit = (key >> b) & 1u;
-        peers &= ~(__ballot_sync(kFull, bit) ^ (0u - bit));  // equal bit b
-    }
-    return peers;
-}
-
-// Groups the active lanes by key through a scratch array over the key range
-// (this warp's): every active lane writes its lane id into tag[key] and reads
-// back one writer per key, the group's id (5 bits). Returns the lanes of this
-// lane's group, in lane order: rank = popc(peers & lanemask_lt). When no two
-// lanes share a key (the common case) no ballot beyond the first is needed.
-// Stale scratch entries are harmless: each active lane writes before it reads.
-__device__ __forceinline__ uint32_t group_by_key(uint8_t *tag, uint32_t key, bool act, unsigned lane) {
-    if (act) tag[key] = (uint8_t)lane;
-    __syncwarp();
-    const uint32_t g = act ? tag[key] : lane;
-    const uint32_t active = __ballot_sync(kFull, act);
-    uint32_t peers;
-    if (__ballot_sync(kFull, g != lane) == 0u)
-        peers = 1u << lane;  // all keys distinct
-    else
-        peers = match_bits_n<5>(g, active);
-    __syncwarp();
-    return act ? peers : (1u << lane);
-}
-
-
 __device__ __forceinline__ bool dense_step(const DevCounters *ctr, int parity, unsigned long long gate) {
     return *(volatile const unsigned long long *)&ctr->step_events[parity] > gate;
 }

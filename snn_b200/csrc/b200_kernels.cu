@@ -440,6 +440,86 @@ __global__ void __launch_bounds__(256) ordered_gen_kernel(const TIdx *__restrict
     }
 }
 
+// First position in [lo, hi) whose key is >= x (hi if none), for keys
+// sorted in their bits above kFoldGroupBits and x a multiple of the group
+// size: a 33-way search, one load per lane per round.
+__device__ __forceinline__ uint64_t warp_lower_bound(const uint32_t *__restrict__ keys, uint64_t lo, uint64_t hi,
+                                                     uint32_t x, unsigned lane) {
+    while (hi - lo > 32u) {
+        const uint64_t span = hi - lo;
+        const uint64_t p = lo + span * (lane + 1u) / 33u;
+        const uint32_t ge = __ballot_sync(kFull, keys[p] >= x);
+        if (ge == 0u) {
+            lo = __shfl_sync(kFull, p, 31) + 1u;
+        } else {
+            const int f = __ffs(ge) - 1;
+            const uint64_t pf = __shfl_sync(kFull, p, f);
+            const uint64_t pb = __shfl_sync(kFull, p, f > 0 ? f - 1 : 0);
+            if (f > 0) lo = pb + 1u;
+            hi = pf;
+        }
+    }
+    const uint64_t q = lo + lane;
+    const uint32_t ge = __ballot_sync(kFull, q < hi && keys[q] >= x);
+    return ge ? lo + (uint64_t)(__ffs(ge) - 1) : hi;
+}
+
+// Group fold: the events are sorted stably by target >> kFoldGroupBits only,
+// so every group of 2^kFoldGroupBits consecutive targets has its events
+// contiguous and still in CSR order (one radix pass fewer than a full sort
+// by target). A warp per group keeps the group's currents in shared memory
+// (loaded from next, so successive row ranges accumulate) and applies the
+// events 32 at a time in order: events of one round that hit the same target
+// are applied one after the other in lane (= CSR) order.
+__global__ void __launch_bounds__(256) ordered_group_fold_kernel(uint64_t events, const uint32_t *__restrict__ keys,
+                                                                 const float *__restrict__ vals,
+                                                                 float *__restrict__ next, uint64_t n_targets) {
+    constexpr uint32_t G = 1u << kFoldGroupBits;
+    constexpr int kAhead = 4;  // rounds of 32 events loaded ahead
+    __shared__ float s_acc[8][G];
+    __shared__ uint8_t s_tag[8][G];
+    const unsigned lane = lane_id(), warp = threadIdx.x >> 5;
+    float *acc = s_acc[warp];
+    uint8_t *tag = s_tag[warp];
+    const uint32_t lt = lanemask_lt();
+    const uint64_t groups = (n_targets + G - 1) / G;
+    const uint64_t gwarp = ((uint64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const uint64_t nwarps = ((uint64_t)gridDim.x * blockDim.x) >> 5;
+    for (uint64_t g = gwarp; g < groups; g += nwarps) {
+        const uint32_t t0 = (uint32_t)(g * G);
+        const uint64_t lo = warp_lower_bound(keys, 0, events, t0, lane);
+        const uint64_t hi = g + 1 < groups ? warp_lower_bound(keys, lo, events, t0 + G, lane) : events;
+        if (lo == hi) continue;  // warp-uniform: no events, currents untouched
+        const uint32_t nt = (uint32_t)min((uint64_t)G, n_targets - t0);
+        for (uint32_t t = lane; t < nt; t += 32u) acc[t] = next[t0 + t];
+        __syncwarp();
+        for (uint64_t i0 = lo; i0 < hi; i0 += 32u * kAhead) {
+            uint32_t key[kAhead];
+            float v[kAhead];
+#pragma unroll
+            for (int j = 0; j < kAhead; ++j) {
+                const uint64_t i = i0 + 32u * j + lane;
+                key[j] = i < hi ? __ldcs(keys + i) - t0 : 0u;
+                v[j] = i < hi ? __ldcs(vals + i) : 0.0f;
+            }
+#pragma unroll
+            for (int j = 0; j < kAhead; ++j) {
+                if (i0 + 32u * j >= hi) break;  // warp-uniform
+                const bool act = i0 + 32u * j + lane < hi;
+                const uint32_t peers = group_by_key(tag, key[j], act, lane);
+                const int rank = __popc(peers & lt);
+                const int rounds = (int)__reduce_max_sync(kFull, act ? (uint32_t)__popc(peers) : 0u);
+                for (int r = 0; r < rounds; ++r) {
+                    if (act && rank == r) acc[key[j]] = __fadd_rn(acc[key[j]], v[j]);
+                    __syncwarp();
+                }
+            }
+        }
+        for (uint32_t t = lane; t < nt; t += 32u) next[t0 + t] = acc[t];
+        __syncwarp();
+    }
+}
+
 // Warp per 32-event chunk of the target-sorted array; every run (one
 // target's events) is folded in order onto next[target] by the chunk where
 // it starts. A run shorter than 32 events is walked by the lane at its start
@@ -1369,10 +1449,12 @@ void launch_ordered_gen(cudaStream_t s, int device, const void *list, int idx_bi
 }
 
 cudaError_t sort_pairs_u32_f32(cudaStream_t s, uint32_t *keys, uint32_t *keys_alt, float *vals, float *vals_alt,
-                               uint64_t n, int end_bit, void *temp, size_t *temp_bytes, bool *result_in_alt) {
+                               uint64_t n, int begin_bit, int end_bit, void *temp, size_t *temp_bytes,
+                               bool *result_in_alt) {
     cub::DoubleBuffer<uint32_t> k(keys, keys_alt);
     cub::DoubleBuffer<float> v(vals, vals_alt);
-    const cudaError_t e = cub::DeviceRadixSort::SortPairs(temp, *temp_bytes, k, v, (int64_t)n, 0, end_bit, s);
+    const cudaError_t e =
+        cub::DeviceRadixSort::SortPairs(temp, *temp_bytes, k, v, (int64_t)n, begin_bit, end_bit, s);
     if (temp != nullptr) *result_in_alt = k.Current() != keys;
     return e;
 }
@@ -1389,6 +1471,13 @@ cudaError_t sort_pairs_u64_f32(cudaStream_t s, uint64_t *keys, uint64_t *keys_al
 void launch_ordered_fold(cudaStream_t s, int device, uint64_t events, const uint32_t *keys, const float *vals,
                          float *next) {
     ordered_fold_kernel<<<grid_for(device, 8, events, 256), 256, 0, s>>>(events, keys, vals, next);
+}
+
+void launch_ordered_group_fold(cudaStream_t s, int device, uint64_t events, const uint32_t *keys, const float *vals,
+                               float *next, uint64_t n_targets) {
+    const uint64_t groups = (n_targets + (1u << kFoldGroupBits) - 1) >> kFoldGroupBits;
+    ordered_group_fold_kernel<<<grid_for(device, 8, groups * 32u, 256), 256, 0, s>>>(events, keys, vals, next,
+                                                                                     n_targets);
 }
 
 cudaError_t scan_degrees_u64(cudaStream_t s, const uint32_t *in, unsigned long long *out, uint64_t n, void *temp,

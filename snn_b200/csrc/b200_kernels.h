@@ -245,8 +245,8 @@ void launch_sell_slots(cudaStream_t s, int device, const uint32_t *cnt, uint64_t
 
 // Ordered push (bit-exact, event-driven), in step order: sdeg of the
 // spiking rows -> scan_degrees_u64 (eoff, rows+1 entries) -> per row range:
-// gen (events in CSR order) -> sort_pairs_u32_f32 (stable, by target) ->
-// fold.
+// gen (events in CSR order) -> sort_pairs_u32_f32 (stable, by target, or by
+// target group) -> fold (or group fold).
 void launch_ordered_sdeg(cudaStream_t s, int device, const void *list, int idx_bits, DevCounters *ctr, int parity,
                          uint64_t max_rows, const uint64_t *row_ptr, uint32_t *sdeg, int clear,
                          uint64_t batch_rows);
@@ -257,10 +257,18 @@ void launch_ordered_gen(cudaStream_t s, int device, const void *list, int idx_bi
                         const float *w, const unsigned long long *eoff, uint64_t rows, uint64_t id_base,
                         uint32_t *sdeg, uint32_t *keys, float *vals, int epilogue, int count_spikes,
                         uint64_t batch_rows);
+// Sorts by key bits [begin_bit, end_bit), stably.
 cudaError_t sort_pairs_u32_f32(cudaStream_t s, uint32_t *keys, uint32_t *keys_alt, float *vals, float *vals_alt,
-                               uint64_t n, int end_bit, void *temp, size_t *temp_bytes, bool *result_in_alt);
+                               uint64_t n, int begin_bit, int end_bit, void *temp, size_t *temp_bytes,
+                               bool *result_in_alt);
+// Fold of events sorted fully by target (begin_bit 0).
 void launch_ordered_fold(cudaStream_t s, int device, uint64_t events, const uint32_t *keys, const float *vals,
                          float *next);
+// Fold of events sorted by target >> kFoldGroupBits (begin_bit kFoldGroupBits);
+// keys below n_targets.
+constexpr int kFoldGroupBits = 8;
+void launch_ordered_group_fold(cudaStream_t s, int device, uint64_t events, const uint32_t *keys, const float *vals,
+                               float *next, uint64_t n_targets);
 
 // Per-row out-degrees (u32) from a row_ptr, for event statistics in ordered mode.
 void launch_row_degrees(cudaStream_t s, int device, const uint64_t *row_ptr, uint64_t rows, uint32_t *deg);

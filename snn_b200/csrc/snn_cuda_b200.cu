@@ -587,8 +587,8 @@ snn_status_t setup_ordered_push(snn_cuda_context_t *c, uint64_t cap_limit = UINT
     bool alt = false;
     b200::scan_degrees_u64(c->stream, nullptr, nullptr, n + 1, nullptr, &a);
     if (c->ocap)
-        b200::sort_pairs_u32_f32(c->stream, nullptr, nullptr, nullptr, nullptr, c->ocap, target_bits(c), nullptr, &b,
-                                 &alt);
+        b200::sort_pairs_u32_f32(c->stream, nullptr, nullptr, nullptr, nullptr, c->ocap, 0, target_bits(c), nullptr,
+                                 &b, &alt);
     c->otemp_bytes = std::max({a, b, (size_t)256});
     if (cudaMalloc(&c->d_otemp, c->otemp_bytes) != cudaSuccess) return fail("out of device memory for sort scratch");
     return cuda_status(cudaStreamSynchronize(c->stream));
@@ -640,6 +640,34 @@ bool setup_binfold(snn_cuda_context_t *c) {
     c->bf_gate = gate;
     c->binfold = true;
     return true;
+}
+
+// Sorts a range's events (in CSR order in d_okeys[0] / d_ovals[0]) and folds
+// them onto next. By default the sort orders only the target-group bits and
+// the group fold finishes (one radix pass fewer); SNN_B200_ORDERED_FOLD=full
+// sorts by the whole target and folds runs. With one group, no sort at all.
+snn_status_t sort_and_fold(snn_cuda_context_t *c, uint64_t events, float *next) {
+    static const bool full = [] {
+        const char *e = std::getenv("SNN_B200_ORDERED_FOLD");
+        return e != nullptr && std::strcmp(e, "full") == 0;
+    }();
+    const int end_bit = target_bits(c);
+    const int begin_bit = full ? 0 : b200::kFoldGroupBits;
+    bool alt = false;
+    if (end_bit > begin_bit) {
+        size_t tb = c->otemp_bytes;
+        const snn_status_t st = cuda_status(b200::sort_pairs_u32_f32(c->stream, c->d_okeys[0], c->d_okeys[1],
+                                                                     c->d_ovals[0], c->d_ovals[1], events, begin_bit,
+                                                                     end_bit, c->d_otemp, &tb, &alt));
+        if (st != SNN_OK) return st;
+    }
+    const uint32_t *keys = c->d_okeys[alt ? 1 : 0];
+    const float *vals = c->d_ovals[alt ? 1 : 0];
+    if (full)
+        b200::launch_ordered_fold(c->stream, c->device, events, keys, vals, next);
+    else
+        b200::launch_ordered_group_fold(c->stream, c->device, events, keys, vals, next, c->n_local);
+    return SNN_OK;
 }
 
 // ORDERED propagation set-up after the push CSR (and the pull topology, when
@@ -711,14 +739,7 @@ snn_status_t ordered_push_step(snn_cuda_context_t *c, int parity, float *next, b
                                  c->d_ovals[0], i + 1 == ranges.size(), !sharded, brows);
         c->launches++;
         if (!events) continue;
-        tb = c->otemp_bytes;
-        bool alt = false;
-        if ((st = cuda_status(b200::sort_pairs_u32_f32(c->stream, c->d_okeys[0], c->d_okeys[1], c->d_ovals[0],
-                                                       c->d_ovals[1], events, target_bits(c), c->d_otemp, &tb,
-                                                       &alt))) != SNN_OK)
-            return st;
-        b200::launch_ordered_fold(c->stream, c->device, events, c->d_okeys[alt ? 1 : 0], c->d_ovals[alt ? 1 : 0],
-                                  next);
+        if ((st = sort_and_fold(c, events, next)) != SNN_OK) return st;
         c->launches++;
     }
     return SNN_OK;
@@ -771,14 +792,7 @@ snn_status_t ordered_stream_chunked(snn_cuda_context_t *c, int parity, float *ne
                                  ch.row_begin + ch.rows, drow - ch.row_begin, dcol - ch.edge_begin, 64,
                                  dw - ch.edge_begin, c->d_eoff, n, c->h_bounds[i], c->d_sdeg, c->d_okeys[0],
                                  c->d_ovals[0], 0, 0, 0);
-        tb = c->otemp_bytes;
-        bool alt = false;
-        if ((st = cuda_status(b200::sort_pairs_u32_f32(c->stream, c->d_okeys[0], c->d_okeys[1], c->d_ovals[0],
-                                                       c->d_ovals[1], events, target_bits(c), c->d_otemp, &tb,
-                                                       &alt))) != SNN_OK)
-            return st;
-        b200::launch_ordered_fold(c->stream, c->device, events, c->d_okeys[alt ? 1 : 0], c->d_ovals[alt ? 1 : 0],
-                                  next);
+        if ((st = sort_and_fold(c, events, next)) != SNN_OK) return st;
         cudaEventRecord(c->ev_free[s], c->stream);
         c->launches += 3;
     }
