@@ -441,7 +441,7 @@ __global__ void __launch_bounds__(256) ordered_gen_kernel(const TIdx *__restrict
 }
 
 // First position in [lo, hi) whose key is >= x (hi if none), for keys
-// sorted in their bits above kFoldGroupBits and x a multiple of the group
+// sorted in their bits above the fold group's and x a multiple of the group
 // size: a 33-way search, one load per lane per round.
 __device__ __forceinline__ uint64_t warp_lower_bound(const uint32_t *__restrict__ keys, uint64_t lo, uint64_t hi,
                                                      uint32_t x, unsigned lane) {
@@ -464,24 +464,29 @@ __device__ __forceinline__ uint64_t warp_lower_bound(const uint32_t *__restrict_
     return ge ? lo + (uint64_t)(__ffs(ge) - 1) : hi;
 }
 
-// Group fold: the events are sorted stably by target >> kFoldGroupBits only,
-// so every group of 2^kFoldGroupBits consecutive targets has its events
-// contiguous and still in CSR order (one radix pass fewer than a full sort
-// by target). A warp per group keeps the group's currents in shared memory
-// (loaded from next, so successive row ranges accumulate) and applies the
-// events 32 at a time in order: events of one round that hit the same target
-// are applied one after the other in lane (= CSR) order.
+// Group fold: the events are sorted stably by target >> GB only, so every
+// group of 2^GB consecutive targets has its events contiguous and still in
+// CSR order (one radix pass fewer than a full sort by target). A warp per
+// group keeps the group's currents in shared memory (loaded from next, so
+// successive row ranges accumulate) and applies the events 32 at a time in
+// order: within a round of 32, the lowest pending lane of every target (a
+// shared-memory atomicMin on a per-target tag) applies its event, then the
+// next, so same-target events go in lane (= CSR) order. The next rounds'
+// events are loaded while the current ones are applied.
+template <int GB>
 __global__ void __launch_bounds__(256) ordered_group_fold_kernel(uint64_t events, const uint32_t *__restrict__ keys,
                                                                  const float *__restrict__ vals,
                                                                  float *__restrict__ next, uint64_t n_targets) {
-    constexpr uint32_t G = 1u << kFoldGroupBits;
-    constexpr int kAhead = 4;  // rounds of 32 events loaded ahead
+    constexpr uint32_t G = 1u << GB;
+    constexpr int kAhead = 4;  // rounds of 32 events per load batch
+    constexpr uint32_t kFree = 0xffffffffu;
     __shared__ float s_acc[8][G];
-    __shared__ uint8_t s_tag[8][G];
+    __shared__ uint32_t s_tag[8][G];
     const unsigned lane = lane_id(), warp = threadIdx.x >> 5;
     float *acc = s_acc[warp];
-    uint8_t *tag = s_tag[warp];
-    const uint32_t lt = lanemask_lt();
+    uint32_t *tag = s_tag[warp];
+    for (uint32_t t = lane; t < G; t += 32u) tag[t] = kFree;
+    __syncwarp();
     const uint64_t groups = (n_targets + G - 1) / G;
     const uint64_t gwarp = ((uint64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const uint64_t nwarps = ((uint64_t)gridDim.x * blockDim.x) >> 5;
@@ -492,29 +497,46 @@ __global__ void __launch_bounds__(256) ordered_group_fold_kernel(uint64_t events
         if (lo == hi) continue;  // warp-uniform: no events, currents untouched
         const uint32_t nt = (uint32_t)min((uint64_t)G, n_targets - t0);
         for (uint32_t t = lane; t < nt; t += 32u) acc[t] = next[t0 + t];
+        uint32_t key[kAhead], nkey[kAhead];
+        float v[kAhead], nv[kAhead];
+#pragma unroll
+        for (int j = 0; j < kAhead; ++j) {
+            const uint64_t i = lo + 32u * j + lane;
+            key[j] = i < hi ? __ldcs(keys + i) - t0 : 0u;
+            v[j] = i < hi ? __ldcs(vals + i) : 0.0f;
+        }
         __syncwarp();
         for (uint64_t i0 = lo; i0 < hi; i0 += 32u * kAhead) {
-            uint32_t key[kAhead];
-            float v[kAhead];
+            const uint64_t n0 = i0 + 32u * kAhead;
 #pragma unroll
             for (int j = 0; j < kAhead; ++j) {
-                const uint64_t i = i0 + 32u * j + lane;
-                key[j] = i < hi ? __ldcs(keys + i) - t0 : 0u;
-                v[j] = i < hi ? __ldcs(vals + i) : 0.0f;
+                const uint64_t i = n0 + 32u * j + lane;
+                nkey[j] = i < hi ? __ldcs(keys + i) - t0 : 0u;
+                nv[j] = i < hi ? __ldcs(vals + i) : 0.0f;
             }
 #pragma unroll
             for (int j = 0; j < kAhead; ++j) {
-                if (i0 + 32u * j >= hi) break;  // warp-uniform
-                const bool act = i0 + 32u * j + lane < hi;
-                const uint32_t peers = group_by_key(tag, key[j], act, lane);
-                const int rank = __popc(peers & lt);
-                const int rounds = (int)__reduce_max_sync(kFull, act ? (uint32_t)__popc(peers) : 0u);
-                for (int r = 0; r < rounds; ++r) {
-                    if (act && rank == r) acc[key[j]] = __fadd_rn(acc[key[j]], v[j]);
+                uint32_t pending = __ballot_sync(kFull, i0 + 32u * j + lane < hi);
+                while (pending) {  // warp-uniform
+                    const bool mine = (pending >> lane) & 1u;
+                    if (mine) atomicMin(&tag[key[j]], lane);
                     __syncwarp();
+                    const bool win = mine && tag[key[j]] == lane;
+                    if (win) {  // a loser reading the freed tag sees no match
+                        acc[key[j]] = __fadd_rn(acc[key[j]], v[j]);
+                        tag[key[j]] = kFree;
+                    }
+                    __syncwarp();
+                    pending &= ~__ballot_sync(kFull, win);
                 }
             }
+#pragma unroll
+            for (int j = 0; j < kAhead; ++j) {
+                key[j] = nkey[j];
+                v[j] = nv[j];
+            }
         }
+        __syncwarp();
         for (uint32_t t = lane; t < nt; t += 32u) next[t0 + t] = acc[t];
         __syncwarp();
     }
@@ -1473,11 +1495,24 @@ void launch_ordered_fold(cudaStream_t s, int device, uint64_t events, const uint
     ordered_fold_kernel<<<grid_for(device, 8, events, 256), 256, 0, s>>>(events, keys, vals, next);
 }
 
+int fold_group_bits() {
+    static const int bits = [] {
+        const char *e = std::getenv("SNN_B200_FOLD_GROUP_BITS");
+        const int v = e ? std::atoi(e) : 0;
+        return v == 8 ? 8 : 9;
+    }();
+    return bits;
+}
+
 void launch_ordered_group_fold(cudaStream_t s, int device, uint64_t events, const uint32_t *keys, const float *vals,
                                float *next, uint64_t n_targets) {
-    const uint64_t groups = (n_targets + (1u << kFoldGroupBits) - 1) >> kFoldGroupBits;
-    ordered_group_fold_kernel<<<grid_for(device, 8, groups * 32u, 256), 256, 0, s>>>(events, keys, vals, next,
-                                                                                     n_targets);
+    const int gb = fold_group_bits();
+    const uint64_t groups = (n_targets + (1ull << gb) - 1) >> gb;
+    const int grid = grid_for(device, 8, groups * 32u, 256);
+    if (gb == 8)
+        ordered_group_fold_kernel<8><<<grid, 256, 0, s>>>(events, keys, vals, next, n_targets);
+    else
+        ordered_group_fold_kernel<9><<<grid, 256, 0, s>>>(events, keys, vals, next, n_targets);
 }
 
 cudaError_t scan_degrees_u64(cudaStream_t s, const uint32_t *in, unsigned long long *out, uint64_t n, void *temp,

@@ -652,7 +652,7 @@ snn_status_t sort_and_fold(snn_cuda_context_t *c, uint64_t events, float *next) 
         return e != nullptr && std::strcmp(e, "full") == 0;
     }();
     const int end_bit = target_bits(c);
-    const int begin_bit = full ? 0 : b200::kFoldGroupBits;
+    const int begin_bit = full ? 0 : b200::fold_group_bits();
     bool alt = false;
     if (end_bit > begin_bit) {
         size_t tb = c->otemp_bytes;
