@@ -672,8 +672,9 @@ snn_status_t sort_and_fold(snn_cuda_context_t *c, uint64_t events, float *next) 
 
 // ORDERED propagation set-up after the push CSR (and the pull topology, when
 // there is room) exist. The event sort by default: per event it costs less
-// than the bin-fold on B200 (config 2 quiet steps, 1.7e8 events: 2.35 ms
-// against 8.2 ms), at the price of one host read per step. PUSH_BINNED asks
+// than the bin-fold on B200 (the same config 2 quiet steps: 2.35 ms with a
+// full sort by target, less with the group sort, against 8.2 ms), at the
+// price of one host read per step. PUSH_BINNED asks
 // for the bin-fold (no host round trip, graph-replayable); it falls back to
 // the event sort when it cannot be set up.
 snn_status_t setup_ordered(snn_cuda_context_t *c) {
