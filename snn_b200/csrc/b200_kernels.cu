@@ -428,7 +428,23 @@ __global__ void __launch_bounds__(256) ordered_gen_kernel(const TIdx *__restrict
         const uint32_t base = (uint32_t)(id - row);  // batched: the sample's first neuron
         const uint64_t b = row_ptr[row], e = row_ptr[row + 1];
         const uint64_t d = eoff[id] - id_base - b;
-        for (uint64_t k = b + lane; k < e; k += 32u) {
+        uint64_t k = b + lane;
+        // Four rounds of loads in flight per lane, then their stores.
+        for (; k + 96u < e; k += 128u) {
+            uint32_t cv[4];
+            float wv[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                cv[u] = (uint32_t)__ldcs(col + k + 32u * u);
+                wv[u] = __ldcs(w + k + 32u * u);
+            }
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                keys[d + k + 32u * u] = base + cv[u];
+                vals[d + k + 32u * u] = wv[u];
+            }
+        }
+        for (; k < e; k += 32u) {
             keys[d + k] = base + (uint32_t)col[k];
             vals[d + k] = __ldcs(w + k);
         }
