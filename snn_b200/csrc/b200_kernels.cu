@@ -1511,24 +1511,11 @@ void launch_ordered_fold(cudaStream_t s, int device, uint64_t events, const uint
     ordered_fold_kernel<<<grid_for(device, 8, events, 256), 256, 0, s>>>(events, keys, vals, next);
 }
 
-int fold_group_bits() {
-    static const int bits = [] {
-        const char *e = std::getenv("SNN_B200_FOLD_GROUP_BITS");
-        const int v = e ? std::atoi(e) : 0;
-        return v == 8 ? 8 : 9;
-    }();
-    return bits;
-}
-
 void launch_ordered_group_fold(cudaStream_t s, int device, uint64_t events, const uint32_t *keys, const float *vals,
                                float *next, uint64_t n_targets) {
-    const int gb = fold_group_bits();
-    const uint64_t groups = (n_targets + (1ull << gb) - 1) >> gb;
-    const int grid = grid_for(device, 8, groups * 32u, 256);
-    if (gb == 8)
-        ordered_group_fold_kernel<8><<<grid, 256, 0, s>>>(events, keys, vals, next, n_targets);
-    else
-        ordered_group_fold_kernel<9><<<grid, 256, 0, s>>>(events, keys, vals, next, n_targets);
+    const uint64_t groups = (n_targets + (1ull << kFoldGroupBits) - 1) >> kFoldGroupBits;
+    ordered_group_fold_kernel<kFoldGroupBits><<<grid_for(device, 8, groups * 32u, 256), 256, 0, s>>>(
+        events, keys, vals, next, n_targets);
 }
 
 cudaError_t scan_degrees_u64(cudaStream_t s, const uint32_t *in, unsigned long long *out, uint64_t n, void *temp,

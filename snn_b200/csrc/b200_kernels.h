@@ -264,10 +264,9 @@ cudaError_t sort_pairs_u32_f32(cudaStream_t s, uint32_t *keys, uint32_t *keys_al
 // Fold of events sorted fully by target (begin_bit 0).
 void launch_ordered_fold(cudaStream_t s, int device, uint64_t events, const uint32_t *keys, const float *vals,
                          float *next);
-// Fold of events sorted by target >> fold_group_bits() (the sort's
-// begin_bit); keys below n_targets. Group bits: 9, or 8 from
-// SNN_B200_FOLD_GROUP_BITS=8.
-int fold_group_bits();
+// Fold of events sorted by target >> kFoldGroupBits (the sort's begin_bit);
+// keys below n_targets. (512-target groups measured the same as 256.)
+constexpr int kFoldGroupBits = 9;
 void launch_ordered_group_fold(cudaStream_t s, int device, uint64_t events, const uint32_t *keys, const float *vals,
                                float *next, uint64_t n_targets);
 

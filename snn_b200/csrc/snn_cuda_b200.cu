@@ -647,12 +647,10 @@ bool setup_binfold(snn_cuda_context_t *c) {
 // the group fold finishes (one radix pass fewer); SNN_B200_ORDERED_FOLD=full
 // sorts by the whole target and folds runs. With one group, no sort at all.
 snn_status_t sort_and_fold(snn_cuda_context_t *c, uint64_t events, float *next) {
-    static const bool full = [] {
-        const char *e = std::getenv("SNN_B200_ORDERED_FOLD");
-        return e != nullptr && std::strcmp(e, "full") == 0;
-    }();
+    const char *fold_env = std::getenv("SNN_B200_ORDERED_FOLD");
+    const bool full = fold_env != nullptr && std::strcmp(fold_env, "full") == 0;
     const int end_bit = target_bits(c);
-    const int begin_bit = full ? 0 : b200::fold_group_bits();
+    const int begin_bit = full ? 0 : b200::kFoldGroupBits;
     bool alt = false;
     if (end_bit > begin_bit) {
         size_t tb = c->otemp_bytes;

@@ -399,7 +399,8 @@ def test_sparse_streaming_dyadic_bit_exact():
 
 
 @pytest.mark.parametrize("allow_self,env", [
-    (0, {}),                                   # ordered push, one bucket pass per step
+    (0, {}),                                   # ordered push, one row range per step
+    (0, {"SNN_B200_ORDERED_FOLD": "full"}),    # full sort by target + run fold
     (1, {"SNN_B200_ORDERED_CAP": "3000"}),     # ordered push, several row ranges per step
     (0, {"SNN_B200_ORDERED_PULL": "1"}),       # pull over a device-built CSC
     (1, {"SNN_B200_ORDERED_PULL": "1", "SNN_B200_CSC_PASS_EDGES": "150000"}),  # CSC built in several passes
@@ -407,8 +408,9 @@ def test_sparse_streaming_dyadic_bit_exact():
 ])
 def test_generated_pool_ordered_bit_exact(allow_self, env, monkeypatch):
     """snn_b200_create_random_pool with ORDERED propagation, through both
-    bit-exact kernels: the event-driven ordered push (bucket by target, sort
-    by edge index, sequential fold) and the pull over a CSC built on the
+    bit-exact kernels: the event-driven ordered push (events copied in CSR
+    order, sorted stably by target group, folded in order per group; or the
+    full sort by target and a run fold) and the pull over a CSC built on the
     device. General weights: spikes, events and voltages bit-identical to the
     serial CPU step."""
     for k, v in env.items():
