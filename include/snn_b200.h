@@ -124,7 +124,8 @@ snn_status_t snn_cuda_download_voltage(const snn_cuda_context_t *context, float 
  * and #11-#13 uploads, or STREAMING #8 host chunk table and #9-#11 chunk
  * buffers; step #0 external upload, #1 integrate launch, #2 propagate launch
  * (STREAMING: per chunk row_ptr, col_idx, weights copy then launch), #3 spike
- * download; inject #0-#1 staging growth, then uploads and the launch. */
+ * download; inject #0-#1 device buffer growth, then the index and value
+ * copies and the launch. */
 snn_cuda_context_t *snn_test_nonnull_cuda_context(void);
 void snn_test_cuda_set_fail_after(int64_t calls_before_failure);
 void snn_test_cuda_disable_failure(void);
